@@ -1,0 +1,784 @@
+/*
+ * emel_oracle.c -- CPU restatement of the emel-kernels elementwise, broadcast
+ * and reduction hot path.  TEST INFRASTRUCTURE ONLY (parity checker and timed
+ * CPU baseline); see emel_oracle.h.
+ *
+ * Citations are paths inside stateforward/emel.rs.  Build flags matter:
+ * -O2 -ffp-contract=off -fno-fast-math -fno-math-errno, x86-64 SSE scalar
+ * arithmetic, glibc libm for expf/tanhf/expm1f/log1pf/logf/sinf/cosf (the
+ * functions Rust's f32::{exp,tanh,exp_m1,ln_1p,ln,sin,cos} call on Linux).
+ */
+#include "emel_oracle.h"
+
+#include <math.h>
+#include <stdint.h>
+#include <string.h>
+
+typedef unsigned __int128 u128;
+
+enum { DT_F32 = 0, DT_F16 = 1, DT_I32 = 26, DT_I64 = 27 };
+
+/* ---------------------------------------------------------------------- */
+/* Layout rules: crates/emel-kernels/src/any/tensor_view.rs                */
+/* ---------------------------------------------------------------------- */
+
+static uint64_t dtype_size(uint32_t dtype) {
+    switch (dtype) {
+    case DT_F32: return 4;
+    case DT_F16: return 2;
+    case DT_I32: return 4;
+    case DT_I64: return 8;
+    default: return 0;
+    }
+}
+
+/* Layout::element_count (tensor_view.rs:346-358): zero extent or overflow -> none. */
+static int element_count(const oracle_view* v, uint64_t* out) {
+    uint64_t count = 1;
+    for (int d = 0; d < 4; ++d) {
+        if (v->ne[d] == 0) return 0;
+        if (__builtin_mul_overflow(count, v->ne[d], &count)) return 0;
+    }
+    *out = count;
+    return 1;
+}
+
+/* Layout::effective_f32_strides (tensor_view.rs:262-277), generalised to the
+ * element size of the view's dtype: nb[0]==0 means implicit row-major. */
+static int effective_strides(const oracle_view* v, uint64_t elem, uint64_t s[4]) {
+    if (v->nb[0] != 0) {
+        memcpy(s, v->nb, sizeof(uint64_t) * 4);
+        return 1;
+    }
+    s[0] = elem;
+    for (int d = 1; d < 4; ++d)
+        if (__builtin_mul_overflow(s[d - 1], v->ne[d - 1], &s[d])) return 0;
+    return 1;
+}
+
+/* Layout::validate_element_storage (tensor_view.rs:392-447).  Returns 1 when
+ * the view is valid for `dtype`; strides must be >= and a multiple of the
+ * element size (an explicit zero stride on a singleton dimension is allowed
+ * only under the binary contract), and the whole byte span must fit. */
+static int validate_as(const oracle_view* v, uint32_t dtype, int allow_singleton_zero, uint64_t* count_out) {
+    if (v == NULL || v->dtype != dtype) return 0;
+    uint64_t elem = dtype_size(dtype);
+    uint64_t count;
+    if (!element_count(v, &count)) return 0;
+    uint64_t s[4];
+    if (!effective_strides(v, elem, s)) return 0;
+    for (int d = 0; d < 4; ++d) {
+        int singleton_zero = allow_singleton_zero && v->ne[d] == 1 && s[d] == 0;
+        if (!singleton_zero && (s[d] < elem || s[d] % elem != 0)) return 0;
+    }
+    u128 max_offset = 0;
+    for (int d = 0; d < 4; ++d) max_offset += (u128)(v->ne[d] - 1) * (u128)s[d];
+    u128 end = max_offset + elem;
+    if (end > (u128)v->storage_bytes) return 0;
+    if (count_out) *count_out = count;
+    return 1;
+}
+
+/* Float views: F32 always; F16 as this build's extension of the same rule. */
+static int validate_float(const oracle_view* v, int allow_singleton_zero, uint64_t* count) {
+    if (v == NULL) return 0;
+    if (v->dtype != DT_F32 && v->dtype != DT_F16) return 0;
+    return validate_as(v, v->dtype, allow_singleton_zero, count);
+}
+
+/* normalization_view_valid (normalization.rs:237-287). */
+static int normalization_view_valid(const oracle_view* v) {
+    if (v == NULL || v->dtype != DT_F32 || v->ne[0] == 0) return 0;
+    if (v->nb[0] != 0) {
+        if (v->nb[0] < 4 || v->nb[0] % 4 != 0) return 0;
+        for (int d = 0; d < 4; ++d)
+            if (v->ne[d] > 1 && v->nb[d] == 0) return 0;
+    }
+    for (int d = 0; d < 4; ++d)
+        if (v->ne[d] == 0) return 0;
+    uint64_t s[4];
+    if (!effective_strides(v, 4, s)) return 0;
+    for (int d = 0; d < 4; ++d)
+        if (s[d] < 4 || s[d] % 4 != 0) return 0;
+    u128 max_offset = 0;
+    for (int d = 0; d < 4; ++d) max_offset += (u128)(v->ne[d] - 1) * (u128)s[d];
+    return max_offset + 4 <= (u128)v->storage_bytes;
+}
+
+static int same_ne(const oracle_view* a, const oracle_view* b) {
+    return memcmp(a->ne, b->ne, sizeof(uint64_t) * 4) == 0;
+}
+
+/* Layout::is_dense_contiguous_for (tensor_view.rs:297-314). */
+static int is_dense(const oracle_view* v, uint64_t elem) {
+    uint64_t expected = elem;
+    for (int d = 0; d < 4; ++d) {
+        if (v->nb[d] != expected) return 0;
+        if (__builtin_mul_overflow(expected, v->ne[d], &expected)) return 0;
+    }
+    return 1;
+}
+
+/* TensorView::element_index (tensor_view.rs:778-789): logical ordinal ->
+ * byte offset through each dimension's extent and effective stride. */
+static uint64_t ordinal_offset(const oracle_view* v, const uint64_t s[4], uint64_t ordinal) {
+    uint64_t off = 0;
+    for (int d = 0; d < 4; ++d) {
+        off += (ordinal % v->ne[d]) * s[d];
+        ordinal /= v->ne[d];
+    }
+    return off;
+}
+
+/* Reference binary16 helpers (unary.rs:546-586), kept step for step because
+ * the GELU path rounds through them and their results are part of parity. */
+static inline uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
+static inline float u2f(uint32_t u) { float f; memcpy(&f, &u, 4); return f; }
+
+uint16_t oracle_fp32_to_fp16(float value) {
+    const float scale_to_inf = u2f(0x77800000u);
+    const float scale_to_zero = u2f(0x08800000u);
+    float base = (fabsf(value) * scale_to_inf) * scale_to_zero;
+    uint32_t word = f2u(value);
+    uint32_t doubled = word + word;
+    uint32_t sign = word & 0x80000000u;
+    uint32_t bias = doubled & 0xff000000u;
+    if (bias < 0x71000000u) bias = 0x71000000u;
+    base += u2f((bias >> 1) + 0x07800000u);
+    uint32_t base_bits = f2u(base);
+    uint32_t exponent = (base_bits >> 13) & 0x00007c00u;
+    uint32_t mantissa = base_bits & 0x00000fffu;
+    uint32_t nonsign = exponent + mantissa;
+    return (uint16_t)((sign >> 16) | (doubled > 0xff000000u ? 0x7e00u : nonsign));
+}
+
+float oracle_fp16_to_fp32(uint16_t bits16) {
+    uint32_t word = (uint32_t)bits16 << 16;
+    uint32_t sign = word & 0x80000000u;
+    uint32_t doubled = word + word;
+    uint32_t exp_offset = 0xe0u << 23;
+    float normalized = u2f((doubled >> 4) + exp_offset) * u2f(0x07800000u);
+    float denormalized = u2f((doubled >> 17) | (126u << 23)) - 0.5f;
+    uint32_t result = doubled < (1u << 27) ? (sign | f2u(denormalized)) : (sign | f2u(normalized));
+    return u2f(result);
+}
+
+/* Element accessors for F32/F16 storage. */
+static inline float load_f(const oracle_view* v, uint64_t off) {
+    const unsigned char* p = (const unsigned char*)v->data + off;
+    if (v->dtype == DT_F16) {
+        uint16_t h;
+        memcpy(&h, p, 2);
+        return oracle_fp16_to_fp32(h);
+    }
+    float f;
+    memcpy(&f, p, 4);
+    return f;
+}
+
+static inline void store_f(const oracle_view* v, uint64_t off, float value) {
+    unsigned char* p = (unsigned char*)v->data + off;
+    if (v->dtype == DT_F16) {
+        uint16_t h = oracle_fp32_to_fp16(value);
+        memcpy(p, &h, 2);
+        return;
+    }
+    memcpy(p, &value, 4);
+}
+
+/* ---------------------------------------------------------------------- */
+/* Binary family                                                          */
+/* ---------------------------------------------------------------------- */
+
+/* Formulas: binary.rs:386-409. */
+static inline float binary_apply(int op, float a, float b) {
+    switch (op) {
+    case ORACLE_ADD: return a + b;
+    case ORACLE_SUB: return a - b;
+    case ORACLE_MUL: return a * b;
+    default: return a / b;
+    }
+}
+
+static int all_same_float_dtype(const oracle_view* a, const oracle_view* b, const oracle_view* c) {
+    return a->dtype == b->dtype && a->dtype == c->dtype;
+}
+
+/* binary.rs:336-354 guards, 411-424 loop: every output ordinal reads the
+ * same ordinal of each operand through its own layout. */
+int oracle_binary(int op, const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst) {
+    if (op < ORACLE_ADD || op > ORACLE_DIV) return ORACLE_UNEXPECTED_EVENT;
+    uint64_t nl, nr, nd;
+    if (!validate_float(lhs, 1, &nl) || !validate_float(rhs, 1, &nr) || !validate_float(dst, 1, &nd) ||
+        !all_same_float_dtype(lhs, rhs, dst))
+        return ORACLE_INVALID_VIEW;
+    if (nl != nr || nl != nd) return ORACLE_SHAPE_MISMATCH;
+    uint64_t sl[4], sr[4], sd[4];
+    effective_strides(lhs, dtype_size(lhs->dtype), sl);
+    effective_strides(rhs, dtype_size(rhs->dtype), sr);
+    effective_strides(dst, dtype_size(dst->dtype), sd);
+    for (uint64_t i = 0; i < nd; ++i) {
+        float a = load_f(lhs, ordinal_offset(lhs, sl, i));
+        float b = load_f(rhs, ordinal_offset(rhs, sr, i));
+        store_f(dst, ordinal_offset(dst, sd, i), binary_apply(op, a, b));
+    }
+    return ORACLE_OK;
+}
+
+/* broadcast.rs:323-350 guards, 352-390 loops (add/mul; sub/div use the
+ * same loop with the binary.rs formula). */
+int oracle_broadcast_row(int op, const oracle_view* src0, const oracle_view* src1, const oracle_view* dst) {
+    if (op < ORACLE_ADD || op > ORACLE_DIV) return ORACLE_UNEXPECTED_EVENT;
+    uint64_t n0, n1, nd;
+    if (!validate_float(src0, 1, &n0) || !validate_float(src1, 1, &n1) || !validate_float(dst, 1, &nd) ||
+        !all_same_float_dtype(src0, src1, dst))
+        return ORACLE_INVALID_VIEW;
+    if (!(same_ne(src0, dst) && dst->ne[0] > 0 && src1->ne[0] == dst->ne[0] && src1->ne[1] == 1 &&
+          src1->ne[2] == 1 && src1->ne[3] == 1 && dst->ne[1] > 0 && nd > n1))
+        return ORACLE_SHAPE_MISMATCH;
+    uint64_t s0[4], s1[4], sd[4];
+    effective_strides(src0, dtype_size(src0->dtype), s0);
+    effective_strides(src1, dtype_size(src1->dtype), s1);
+    effective_strides(dst, dtype_size(dst->dtype), sd);
+    uint64_t columns = n1, rows = nd / columns;
+    for (uint64_t r = 0; r < rows; ++r)
+        for (uint64_t c = 0; c < columns; ++c) {
+            uint64_t ordinal = r * columns + c;
+            float a = load_f(src0, ordinal_offset(src0, s0, ordinal));
+            float b = load_f(src1, ordinal_offset(src1, s1, c));
+            store_f(dst, ordinal_offset(dst, sd, ordinal), binary_apply(op, a, b));
+        }
+    return ORACLE_OK;
+}
+
+/* generic.rs:1641-1665 (repeat: dst coordinate % source extent) composed
+ * with binary.rs:386-424.  src0 and dst share extents; every src1 extent
+ * divides the dst extent (the ggml repeat contract). */
+int oracle_binary_repeat(int op, const oracle_view* src0, const oracle_view* src1, const oracle_view* dst) {
+    if (op < ORACLE_ADD || op > ORACLE_DIV) return ORACLE_UNEXPECTED_EVENT;
+    uint64_t n0, n1, nd;
+    if (!validate_float(src0, 1, &n0) || !validate_float(src1, 1, &n1) || !validate_float(dst, 1, &nd) ||
+        !all_same_float_dtype(src0, src1, dst))
+        return ORACLE_INVALID_VIEW;
+    if (!same_ne(src0, dst)) return ORACLE_SHAPE_MISMATCH;
+    for (int d = 0; d < 4; ++d)
+        if (dst->ne[d] % src1->ne[d] != 0) return ORACLE_SHAPE_MISMATCH;
+    uint64_t s0[4], s1[4], sd[4];
+    effective_strides(src0, dtype_size(src0->dtype), s0);
+    effective_strides(src1, dtype_size(src1->dtype), s1);
+    effective_strides(dst, dtype_size(dst->dtype), sd);
+    for (uint64_t i = 0; i < nd; ++i) {
+        uint64_t rem = i, off1 = 0;
+        for (int d = 0; d < 4; ++d) {
+            uint64_t c = rem % dst->ne[d];
+            rem /= dst->ne[d];
+            off1 += (c % src1->ne[d]) * s1[d];
+        }
+        float a = load_f(src0, ordinal_offset(src0, s0, i));
+        float b = load_f(src1, off1);
+        store_f(dst, ordinal_offset(dst, sd, i), binary_apply(op, a, b));
+    }
+    return ORACLE_OK;
+}
+
+/* ---------------------------------------------------------------------- */
+/* Unary family                                                            */
+/* ---------------------------------------------------------------------- */
+
+enum {
+    U_ABS = 0, U_SGN = 1, U_NEG = 2, U_STEP = 3, U_TANH = 4, U_ELU = 5, U_RELU = 6, U_SIGMOID = 7,
+    U_GELU = 8, U_GELU_QUICK = 9, U_SILU = 10, U_HARDSWISH = 11, U_HARDSIGMOID = 12, U_EXP = 13,
+    U_EXPM1 = 14, U_SOFTPLUS = 15, U_GELU_ERF = 16, U_XIELU = 17, U_FLOOR = 18, U_CEIL = 19,
+    U_ROUND = 20, U_TRUNC = 21,
+    U_SQR = 64, U_SQRT = 65, U_LOG = 66, U_SIN = 67, U_COS = 68
+};
+
+/* Rust's f32::clamp keeps NaN; both comparisons are false for it. */
+static inline float clampf_rs(float v, float lo, float hi) {
+    if (v < lo) return lo;
+    if (v > hi) return hi;
+    return v;
+}
+
+/* Formulas: unary.rs:474-672, power.rs:315 and 397-412, reductions.rs:640-668. */
+static inline float unary_apply(int op, float v) {
+    switch (op) {
+    case U_ABS: return fabsf(v);
+    case U_SGN: return isnan(v) ? NAN : copysignf(1.0f, v); /* f32::signum: NaN -> f32::NAN */
+    case U_NEG: return -v;
+    case U_STEP: return v > 0.0f ? 1.0f : 0.0f;
+    case U_TANH: return tanhf(v);
+    case U_ELU: return v >= 0.0f ? v : expm1f(v);
+    case U_RELU: return isnan(v) ? 0.0f : (v > 0.0f ? v : 0.0f); /* f32::max(0.0) */
+    case U_SIGMOID: return 1.0f / (1.0f + expf(-v));
+    case U_GELU: {
+        if (v <= -10.0f) return 0.0f;
+        if (v >= 10.0f) return v;
+        float q = oracle_fp16_to_fp32(oracle_fp32_to_fp16(v));
+        float inner = 0.7978846f * (q + 0.044715f * q * q * q);
+        float approximation = 0.5f * q * (1.0f + tanhf(inner));
+        return oracle_fp16_to_fp32(oracle_fp32_to_fp16(approximation));
+    }
+    case U_GELU_QUICK: return 0.5f * v * (1.0f + tanhf(0.7978846f * v * (1.0f + 0.044715f * v * v)));
+    case U_SILU: return v / (1.0f + expf(-v));
+    case U_HARDSWISH: return v * clampf_rs(v + 3.0f, 0.0f, 6.0f) / 6.0f;
+    case U_HARDSIGMOID: return clampf_rs(v + 3.0f, 0.0f, 6.0f) / 6.0f;
+    case U_EXP: return expf(v);
+    case U_EXPM1: return expm1f(v);
+    case U_SOFTPLUS: return log1pf(expf(v));
+    case U_GELU_ERF: {
+        float sign = v < 0.0f ? -1.0f : 1.0f;
+        float x = fabsf(v) / 1.41421356237309504880f;
+        float t = 1.0f / (1.0f + 0.3275911f * x);
+        float polynomial = (((((1.0614054f * t - 1.4531521f) * t) + 1.4214138f) * t - 0.28449672f) * t + 0.2548296f) * t;
+        float erf = sign * (1.0f - polynomial * expf(-x * x));
+        return 0.5f * v * (1.0f + erf);
+    }
+    case U_FLOOR: return floorf(v);
+    case U_CEIL: return ceilf(v);
+    case U_ROUND: return roundf(v);
+    case U_TRUNC: return truncf(v);
+    case U_SQR: return v * v;
+    case U_SQRT: return sqrtf(v);
+    case U_LOG: return logf(v);
+    case U_SIN: return sinf(v);
+    case U_COS: return cosf(v);
+    default: return v;
+    }
+}
+
+static int unary_op_known(int op) {
+    return (op >= U_ABS && op <= U_TRUNC && op != U_XIELU) || (op >= U_SQR && op <= U_COS);
+}
+
+/* unary.rs:455-461 guards (both views valid, equal element counts) and the
+ * ordinal loop of unary.rs:674-685.  The same guard shape is used by
+ * power.rs:266-272 and reductions.rs:448-466. */
+static int unary_views(const oracle_view* src, const oracle_view* dst, uint64_t* count) {
+    uint64_t ns, nd;
+    if (!validate_float(src, 0, &ns) || !validate_float(dst, 0, &nd) || src->dtype != dst->dtype)
+        return ORACLE_INVALID_VIEW;
+    if (ns != nd) return ORACLE_SHAPE_MISMATCH;
+    *count = ns;
+    return ORACLE_OK;
+}
+
+void oracle_unary_range(int op, const oracle_view* src, const oracle_view* dst, uint64_t begin, uint64_t end) {
+    uint64_t ss[4], sd[4];
+    effective_strides(src, dtype_size(src->dtype), ss);
+    effective_strides(dst, dtype_size(dst->dtype), sd);
+    for (uint64_t i = begin; i < end; ++i)
+        store_f(dst, ordinal_offset(dst, sd, i), unary_apply(op, load_f(src, ordinal_offset(src, ss, i))));
+}
+
+int oracle_unary(int op, const oracle_view* src, const oracle_view* dst) {
+    if (!unary_op_known(op)) return ORACLE_UNEXPECTED_EVENT;
+    uint64_t count;
+    int st = unary_views(src, dst, &count);
+    if (st != ORACLE_OK) return st;
+    oracle_unary_range(op, src, dst, 0, count);
+    return ORACLE_OK;
+}
+
+/* Generic OpUnary (unary.rs:276-292, 942-1027): eight accepted subops; any
+ * other subop, invalid view or count mismatch reports UnexpectedEvent. */
+int oracle_op_unary(int subop, const oracle_view* src, const oracle_view* dst) {
+    int accepted = subop == U_ABS || subop == U_NEG || subop == U_TANH || subop == U_ELU ||
+                   subop == U_RELU || subop == U_GELU || subop == U_SILU || subop == U_EXP;
+    uint64_t ns, nd;
+    if (!accepted || !validate_as(src, DT_F32, 0, &ns) || !validate_as(dst, DT_F32, 0, &nd) || ns != nd)
+        return ORACLE_UNEXPECTED_EVENT;
+    oracle_unary_range(subop, src, dst, 0, ns);
+    return ORACLE_OK;
+}
+
+/* activation.rs:327-333 guards (valid views, identical extents). */
+static int same_shape_views(const oracle_view* src, const oracle_view* dst, uint64_t* count) {
+    uint64_t ns, nd;
+    if (!validate_as(src, DT_F32, 0, &ns) || !validate_as(dst, DT_F32, 0, &nd)) return ORACLE_INVALID_VIEW;
+    if (!same_ne(src, dst)) return ORACLE_SHAPE_MISMATCH;
+    *count = ns;
+    return ORACLE_OK;
+}
+
+#define ORACLE_MAP(src, dst, count, expr)                                                  \
+    do {                                                                                   \
+        uint64_t ss_[4], sd_[4];                                                           \
+        effective_strides(src, 4, ss_);                                                    \
+        effective_strides(dst, 4, sd_);                                                    \
+        for (uint64_t i_ = 0; i_ < (count); ++i_) {                                        \
+            float v = load_f(src, ordinal_offset(src, ss_, i_));                           \
+            store_f(dst, ordinal_offset(dst, sd_, i_), (expr));                            \
+        }                                                                                  \
+    } while (0)
+
+/* activation.rs:366-377 */
+int oracle_scale(const oracle_view* src, const oracle_view* dst, float scale) {
+    uint64_t n;
+    int st = same_shape_views(src, dst, &n);
+    if (st != ORACLE_OK) return st;
+    ORACLE_MAP(src, dst, n, v * scale);
+    return ORACLE_OK;
+}
+
+/* activation.rs:403-423 (std::clamp comparison contract; NaN passes). */
+int oracle_clamp(const oracle_view* src, const oracle_view* dst, float lo, float hi) {
+    uint64_t n;
+    int st = same_shape_views(src, dst, &n);
+    if (st != ORACLE_OK) return st;
+    ORACLE_MAP(src, dst, n, (v < lo ? lo : (v > hi ? hi : v)));
+    return ORACLE_OK;
+}
+
+/* activation.rs:507-521 */
+int oracle_leaky_relu(const oracle_view* src, const oracle_view* dst, float slope) {
+    uint64_t n;
+    int st = same_shape_views(src, dst, &n);
+    if (st != ORACLE_OK) return st;
+    ORACLE_MAP(src, dst, n, (v < 0.0f ? v * slope : v));
+    return ORACLE_OK;
+}
+
+/* activation.rs:335-349 guards (three valid views, identical extents),
+ * 467-481 loop. */
+int oracle_silu_back(const oracle_view* src, const oracle_view* grad, const oracle_view* dst) {
+    uint64_t n, ng;
+    if (!validate_as(src, DT_F32, 0, &n) || !validate_as(grad, DT_F32, 0, &ng) || !validate_as(dst, DT_F32, 0, NULL))
+        return ORACLE_INVALID_VIEW;
+    if (!same_ne(src, grad) || !same_ne(src, dst)) return ORACLE_SHAPE_MISMATCH;
+    uint64_t ss[4], sg[4], sd[4];
+    effective_strides(src, 4, ss);
+    effective_strides(grad, 4, sg);
+    effective_strides(dst, 4, sd);
+    for (uint64_t i = 0; i < n; ++i) {
+        float v = load_f(src, ordinal_offset(src, ss, i));
+        float sigmoid = 1.0f / (1.0f + expf(-v));
+        float derivative = sigmoid * (1.0f + v * (1.0f - sigmoid));
+        store_f(dst, ordinal_offset(dst, sd, i), load_f(grad, ordinal_offset(grad, sg, i)) * derivative);
+    }
+    return ORACLE_OK;
+}
+
+/* elementwise.rs:219-225 guards, 280-291 loop. */
+int oracle_add1(const oracle_view* src, const oracle_view* dst, float scalar) {
+    uint64_t n;
+    int st = same_shape_views(src, dst, &n);
+    if (st != ORACLE_OK) return st;
+    ORACLE_MAP(src, dst, n, v + scalar);
+    return ORACLE_OK;
+}
+
+/* tensor_view.rs:1096-1122 (CopyTensor: valid views, identical extents). */
+int oracle_copy(const oracle_view* src, const oracle_view* dst) {
+    uint64_t n;
+    int st = same_shape_views(src, dst, &n);
+    if (st != ORACLE_OK) return st;
+    ORACLE_MAP(src, dst, n, v);
+    return ORACLE_OK;
+}
+
+/* ---------------------------------------------------------------------- */
+/* Row normalisation: normalization.rs                                     */
+/* ---------------------------------------------------------------------- */
+
+static int norm_guards(const oracle_view* src, const oracle_view* dst, float eps) {
+    if (!normalization_view_valid(src) || !normalization_view_valid(dst)) return ORACLE_INVALID_VIEW;
+    if (!same_ne(src, dst)) return ORACLE_SHAPE_MISMATCH;
+    if (!(isfinite(eps) && eps >= 0.0f)) return ORACLE_INVALID_PARAMETERS;
+    return ORACLE_OK;
+}
+
+/* normalization.rs:316-341 */
+int oracle_norm(const oracle_view* src, const oracle_view* dst, float eps) {
+    int st = norm_guards(src, dst, eps);
+    if (st != ORACLE_OK) return st;
+    uint64_t ss[4], sd[4], count = 0;
+    effective_strides(src, 4, ss);
+    effective_strides(dst, 4, sd);
+    element_count(src, &count);
+    uint64_t columns = src->ne[0], rows = count / columns;
+    for (uint64_t r = 0; r < rows; ++r) {
+        uint64_t start = r * columns, end = start + columns;
+        double sum = 0.0;
+        for (uint64_t o = start; o < end; ++o) sum += (double)load_f(src, ordinal_offset(src, ss, o));
+        float mean = (float)(sum / (double)columns);
+        double variance_sum = 0.0;
+        for (uint64_t o = start; o < end; ++o) {
+            float centered = load_f(src, ordinal_offset(src, ss, o)) - mean;
+            variance_sum += (double)centered * (double)centered;
+        }
+        float variance = (float)(variance_sum / (double)columns);
+        float scale = 1.0f / sqrtf(variance + eps);
+        for (uint64_t o = start; o < end; ++o)
+            store_f(dst, ordinal_offset(dst, sd, o), (load_f(src, ordinal_offset(src, ss, o)) - mean) * scale);
+    }
+    return ORACLE_OK;
+}
+
+/* normalization.rs:343-362, optionally followed by the broadcast.rs:372-390
+ * row multiply (weight ne == [ne0,1,1,1]). */
+static void rms_rows(const oracle_view* src, const oracle_view* weight, const oracle_view* dst, float eps,
+                     uint64_t row_begin, uint64_t row_end) {
+    uint64_t ss[4], sd[4], sw[4] = {0, 0, 0, 0};
+    effective_strides(src, 4, ss);
+    effective_strides(dst, 4, sd);
+    if (weight) effective_strides(weight, 4, sw);
+    uint64_t columns = src->ne[0];
+    for (uint64_t r = row_begin; r < row_end; ++r) {
+        uint64_t start = r * columns, end = start + columns;
+        double sum = 0.0;
+        for (uint64_t o = start; o < end; ++o) {
+            float v = load_f(src, ordinal_offset(src, ss, o));
+            sum += (double)(v * v);
+        }
+        float mean = (float)(sum / (double)columns);
+        float scale = 1.0f / sqrtf(mean + eps);
+        for (uint64_t o = start; o < end; ++o) {
+            float y = load_f(src, ordinal_offset(src, ss, o)) * scale;
+            if (weight) y = y * load_f(weight, ordinal_offset(weight, sw, o - start));
+            store_f(dst, ordinal_offset(dst, sd, o), y);
+        }
+    }
+}
+
+void oracle_rms_norm_rows(const oracle_view* src, const oracle_view* dst, float eps, uint64_t row_begin,
+                          uint64_t row_end) {
+    rms_rows(src, NULL, dst, eps, row_begin, row_end);
+}
+
+int oracle_rms_norm(const oracle_view* src, const oracle_view* dst, float eps) {
+    int st = norm_guards(src, dst, eps);
+    if (st != ORACLE_OK) return st;
+    uint64_t count = 0;
+    element_count(src, &count);
+    rms_rows(src, NULL, dst, eps, 0, count / src->ne[0]);
+    return ORACLE_OK;
+}
+
+int oracle_rms_norm_mul(const oracle_view* src, const oracle_view* weight, const oracle_view* dst, float eps) {
+    uint64_t count = 0;
+    if (!normalization_view_valid(src) || !normalization_view_valid(dst) || !validate_as(weight, DT_F32, 1, NULL))
+        return ORACLE_INVALID_VIEW;
+    if (!same_ne(src, dst) || weight->ne[0] != src->ne[0] || weight->ne[1] != 1 || weight->ne[2] != 1 ||
+        weight->ne[3] != 1)
+        return ORACLE_SHAPE_MISMATCH;
+    if (!(isfinite(eps) && eps >= 0.0f)) return ORACLE_INVALID_PARAMETERS;
+    element_count(src, &count);
+    rms_rows(src, weight, dst, eps, 0, count / src->ne[0]);
+    return ORACLE_OK;
+}
+
+/* ---------------------------------------------------------------------- */
+/* Softmax: reductions.rs:473-495 guards, 565-638 loops                   */
+/* ---------------------------------------------------------------------- */
+
+static int soft_max_dense_layout(const oracle_view* v) {
+    if (v->nb[0] == 0) {
+        uint64_t s[4];
+        return effective_strides(v, 4, s);
+    }
+    return is_dense(v, 4);
+}
+
+/* mask (optional): F16 or F32, ne0 == src ne0, ne1 >= src ne1, ne2/ne3
+ * divide the source extents; row (i1,i2,i3) reads mask row (i1, i2 % m2, i3 % m3). */
+static int soft_max_core(const oracle_view* src, const oracle_view* mask, const oracle_view* dst, float scale,
+                         int apply_scale) {
+    uint64_t ns, nd;
+    if (!validate_as(src, DT_F32, 0, &ns) || !validate_as(dst, DT_F32, 0, &nd)) return ORACLE_INVALID_VIEW;
+    if (mask && !validate_float(mask, 0, NULL)) return ORACLE_INVALID_VIEW;
+    uint64_t width = src->ne[0];
+    if (!(width > 0 && ns > 0 && ns % width == 0 && ns == nd)) return ORACLE_SHAPE_MISMATCH;
+    if (mask && !(mask->ne[0] == width && mask->ne[1] >= src->ne[1] && src->ne[2] % mask->ne[2] == 0 &&
+                  src->ne[3] % mask->ne[3] == 0))
+        return ORACLE_SHAPE_MISMATCH;
+    int dense = soft_max_dense_layout(src) && soft_max_dense_layout(dst);
+    uint64_t ss[4], sd[4], sm[4] = {0, 0, 0, 0};
+    effective_strides(src, 4, ss);
+    effective_strides(dst, 4, sd);
+    if (mask) effective_strides(mask, dtype_size(mask->dtype), sm);
+    uint64_t rows = ns / width;
+    for (uint64_t r = 0; r < rows; ++r) {
+        uint64_t offset = r * width;
+        uint64_t mask_row = 0;
+        if (mask) {
+            uint64_t i1 = r % src->ne[1], i2 = (r / src->ne[1]) % src->ne[2], i3 = r / (src->ne[1] * src->ne[2]);
+            mask_row = i1 * sm[1] + (i2 % mask->ne[2]) * sm[2] + (i3 % mask->ne[3]) * sm[3];
+        }
+#define SM_VALUE(c)                                                                                   \
+    (!apply_scale ? load_f(src, ordinal_offset(src, ss, offset + (c)))                               \
+     : mask ? load_f(src, ordinal_offset(src, ss, offset + (c))) * scale + load_f(mask, mask_row + (c) * sm[0]) \
+            : load_f(src, ordinal_offset(src, ss, offset + (c))) * scale)
+        float max_value = SM_VALUE(0);
+        for (uint64_t c = 1; c < width; ++c) {
+            float v = SM_VALUE(c);
+            if (v > max_value) max_value = v;
+        }
+        if (dense) {
+            double sum = 0.0;
+            for (uint64_t c = 0; c < width; ++c) {
+                float e = expf(SM_VALUE(c) - max_value);
+                store_f(dst, ordinal_offset(dst, sd, offset + c), e);
+                sum += (double)e;
+            }
+            float denominator = (float)sum;
+            for (uint64_t c = 0; c < width; ++c) {
+                uint64_t o = ordinal_offset(dst, sd, offset + c);
+                store_f(dst, o, load_f(dst, o) / denominator);
+            }
+        } else {
+            float sum = 0.0f;
+            for (uint64_t c = 0; c < width; ++c) {
+                float e = expf(SM_VALUE(c) - max_value);
+                store_f(dst, ordinal_offset(dst, sd, offset + c), e);
+                sum += e;
+            }
+            for (uint64_t c = 0; c < width; ++c) {
+                uint64_t o = ordinal_offset(dst, sd, offset + c);
+                store_f(dst, o, load_f(dst, o) / sum);
+            }
+        }
+#undef SM_VALUE
+    }
+    return ORACLE_OK;
+}
+
+int oracle_soft_max(const oracle_view* src, const oracle_view* dst) { return soft_max_core(src, NULL, dst, 1.0f, 0); }
+
+int oracle_soft_max_ext(const oracle_view* src, const oracle_view* mask, const oracle_view* dst, float scale) {
+    return soft_max_core(src, mask, dst, scale, 1);
+}
+
+/* ---------------------------------------------------------------------- */
+/* Reductions: reductions.rs:448-463 guards, 671-730 loops                */
+/* ---------------------------------------------------------------------- */
+
+static int scalar_output(const oracle_view* dst) {
+    return dst->ne[0] == 1 && dst->ne[1] == 1 && dst->ne[2] == 1 && dst->ne[3] == 1;
+}
+
+static int rows_output(const oracle_view* src, const oracle_view* dst) {
+    return dst->ne[0] == 1 && dst->ne[1] == src->ne[1] && dst->ne[2] == src->ne[2] && dst->ne[3] == src->ne[3];
+}
+
+int oracle_sum_f64(const oracle_view* src, double* out) {
+    uint64_t n;
+    if (!validate_as(src, DT_F32, 0, &n)) return ORACLE_INVALID_VIEW;
+    uint64_t ss[4];
+    effective_strides(src, 4, ss);
+    double sum = 0.0;
+    for (uint64_t i = 0; i < n; ++i) sum += (double)load_f(src, ordinal_offset(src, ss, i));
+    *out = sum;
+    return ORACLE_OK;
+}
+
+int oracle_sum(const oracle_view* src, const oracle_view* dst) {
+    if (!validate_as(src, DT_F32, 0, NULL) || !validate_as(dst, DT_F32, 0, NULL)) return ORACLE_INVALID_VIEW;
+    if (!scalar_output(dst)) return ORACLE_SHAPE_MISMATCH;
+    double sum;
+    oracle_sum_f64(src, &sum);
+    store_f(dst, 0, (float)sum);
+    return ORACLE_OK;
+}
+
+int oracle_mean(const oracle_view* src, const oracle_view* dst) {
+    uint64_t n;
+    if (!validate_as(src, DT_F32, 0, &n) || !validate_as(dst, DT_F32, 0, NULL)) return ORACLE_INVALID_VIEW;
+    if (!scalar_output(dst)) return ORACLE_SHAPE_MISMATCH;
+    double sum;
+    oracle_sum_f64(src, &sum);
+    store_f(dst, 0, (float)(sum / (double)n));
+    return ORACLE_OK;
+}
+
+int oracle_sum_rows(const oracle_view* src, const oracle_view* dst) {
+    uint64_t n;
+    if (!validate_as(src, DT_F32, 0, &n) || !validate_as(dst, DT_F32, 0, NULL)) return ORACLE_INVALID_VIEW;
+    if (!rows_output(src, dst)) return ORACLE_SHAPE_MISMATCH;
+    uint64_t ss[4], sd[4];
+    effective_strides(src, 4, ss);
+    effective_strides(dst, 4, sd);
+    uint64_t width = src->ne[0], rows = n / width;
+    for (uint64_t r = 0; r < rows; ++r) {
+        double sum = 0.0;
+        for (uint64_t c = 0; c < width; ++c) sum += (double)load_f(src, ordinal_offset(src, ss, r * width + c));
+        store_f(dst, ordinal_offset(dst, sd, r), (float)sum);
+    }
+    return ORACLE_OK;
+}
+
+/* reductions.rs:715-730: first index of the strict running maximum. */
+static uint64_t argmax_scan(const oracle_view* src, const uint64_t ss[4], uint64_t begin, uint64_t end,
+                            float* best_out) {
+    uint64_t best_index = begin;
+    float best_value = load_f(src, ordinal_offset(src, ss, begin));
+    for (uint64_t i = begin + 1; i < end; ++i) {
+        float v = load_f(src, ordinal_offset(src, ss, i));
+        if (v > best_value) {
+            best_value = v;
+            best_index = i;
+        }
+    }
+    if (best_out) *best_out = best_value;
+    return best_index;
+}
+
+int oracle_argmax_index(const oracle_view* src, int64_t* index, float* value) {
+    uint64_t n;
+    if (!validate_as(src, DT_F32, 0, &n)) return ORACLE_INVALID_VIEW;
+    uint64_t ss[4];
+    effective_strides(src, 4, ss);
+    float best;
+    uint64_t i = argmax_scan(src, ss, 0, n, &best);
+    if (index) *index = (int64_t)i;
+    if (value) *value = best;
+    return ORACLE_OK;
+}
+
+/* Scalar destination: F32 (the reference's index-as-f32, exact below 2^24)
+ * or I64 (exact index, this build's extension). */
+static int index_output_valid(const oracle_view* dst) {
+    return validate_as(dst, DT_F32, 0, NULL) || validate_as(dst, DT_I64, 0, NULL) ||
+           validate_as(dst, DT_I32, 0, NULL);
+}
+
+static void store_index(const oracle_view* dst, uint64_t off, uint64_t index) {
+    unsigned char* p = (unsigned char*)dst->data + off;
+    if (dst->dtype == DT_F32) {
+        float f = (float)index;
+        memcpy(p, &f, 4);
+    } else if (dst->dtype == DT_I64) {
+        int64_t v = (int64_t)index;
+        memcpy(p, &v, 8);
+    } else {
+        int32_t v = (int32_t)index;
+        memcpy(p, &v, 4);
+    }
+}
+
+int oracle_argmax(const oracle_view* src, const oracle_view* dst) {
+    uint64_t n;
+    if (!validate_as(src, DT_F32, 0, &n) || !index_output_valid(dst)) return ORACLE_INVALID_VIEW;
+    if (!scalar_output(dst)) return ORACLE_SHAPE_MISMATCH;
+    uint64_t ss[4];
+    effective_strides(src, 4, ss);
+    store_index(dst, 0, argmax_scan(src, ss, 0, n, NULL));
+    return ORACLE_OK;
+}
+
+/* Per-row argmax: the reductions.rs:715-730 scan applied to each ne0 row;
+ * index is the column within the row. */
+int oracle_argmax_rows(const oracle_view* src, const oracle_view* dst) {
+    uint64_t n;
+    if (!validate_as(src, DT_F32, 0, &n) || !index_output_valid(dst)) return ORACLE_INVALID_VIEW;
+    if (!rows_output(src, dst)) return ORACLE_SHAPE_MISMATCH;
+    uint64_t ss[4], sd[4];
+    effective_strides(src, 4, ss);
+    effective_strides(dst, dtype_size(dst->dtype), sd);
+    uint64_t width = src->ne[0], rows = n / width;
+    for (uint64_t r = 0; r < rows; ++r) {
+        uint64_t i = argmax_scan(src, ss, r * width, r * width + width, NULL);
+        store_index(dst, ordinal_offset(dst, sd, r), i - r * width);
+    }
+    return ORACLE_OK;
+}

@@ -1,0 +1,95 @@
+/*
+ * emel_oracle.h -- CPU restatement of the emel-kernels elementwise, broadcast
+ * and reduction loops (stateforward/emel.rs, crates/emel-kernels/src/any/).
+ *
+ * TEST INFRASTRUCTURE ONLY.  This library is the parity checker and the timed
+ * CPU baseline.  Only tests/, __graft_entry__.smoke() and bench.py's CPU legs
+ * may load it; the device library never links or calls it.
+ *
+ * Parity pinning: the restatement is checked against the reference's golden
+ * parity manifests (snapshots/parity/kernel-{binary,broadcast,elementwise,
+ * power,unary,softmax,normalization,activation,...}/manifest.txt) and the
+ * known-answer unit tests (crates/emel-kernels/tests/any/) through
+ * tests/golden/.  Operators the reference does not have (sub/div row
+ * broadcast, modulo broadcast, f16 elementwise, softmax scale+mask, per-row
+ * argmax, exact i64 argmax) are defined here as the cited loop extended with
+ * the new operand; their parity is "unpinned" by any reference vector.
+ *
+ * Every entry point validates exactly as the reference guards do and never
+ * writes the destination of a rejected request.
+ */
+#ifndef EMEL_ORACLE_H
+#define EMEL_ORACLE_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Same field layout as emel_tensor_view in include/emel_cuda.h so one host
+ * struct can describe a buffer to both libraries. `data` is a HOST pointer. */
+typedef struct oracle_view {
+    void* data;
+    uint64_t storage_bytes;
+    uint64_t ne[4];
+    uint64_t nb[4];
+    uint32_t dtype;
+    uint32_t reserved;
+} oracle_view;
+
+/* Status codes (numerically equal to emel_cuda_status). */
+enum {
+    ORACLE_OK = 0,
+    ORACLE_INVALID_VIEW = 1,
+    ORACLE_SHAPE_MISMATCH = 2,
+    ORACLE_INVALID_PARAMETERS = 3,
+    ORACLE_UNEXPECTED_EVENT = 4,
+    ORACLE_INVALID_ARGUMENT = 18
+};
+
+/* Shared op codes (numerically equal to the device library's enums). */
+enum { ORACLE_ADD = 0, ORACLE_SUB = 1, ORACLE_MUL = 2, ORACLE_DIV = 3 };
+
+int oracle_binary(int op, const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst);
+int oracle_broadcast_row(int op, const oracle_view* src0, const oracle_view* src1, const oracle_view* dst);
+int oracle_binary_repeat(int op, const oracle_view* src0, const oracle_view* src1, const oracle_view* dst);
+
+int oracle_unary(int op, const oracle_view* src, const oracle_view* dst);
+int oracle_op_unary(int subop, const oracle_view* src, const oracle_view* dst);
+int oracle_scale(const oracle_view* src, const oracle_view* dst, float scale);
+int oracle_clamp(const oracle_view* src, const oracle_view* dst, float lo, float hi);
+int oracle_leaky_relu(const oracle_view* src, const oracle_view* dst, float slope);
+int oracle_silu_back(const oracle_view* src, const oracle_view* grad, const oracle_view* dst);
+int oracle_add1(const oracle_view* src, const oracle_view* dst, float scalar);
+int oracle_copy(const oracle_view* src, const oracle_view* dst);
+
+int oracle_norm(const oracle_view* src, const oracle_view* dst, float eps);
+int oracle_rms_norm(const oracle_view* src, const oracle_view* dst, float eps);
+int oracle_rms_norm_mul(const oracle_view* src, const oracle_view* weight, const oracle_view* dst, float eps);
+
+int oracle_soft_max(const oracle_view* src, const oracle_view* dst);
+int oracle_soft_max_ext(const oracle_view* src, const oracle_view* mask, const oracle_view* dst, float scale);
+
+int oracle_sum(const oracle_view* src, const oracle_view* dst);
+int oracle_sum_f64(const oracle_view* src, double* out);
+int oracle_mean(const oracle_view* src, const oracle_view* dst);
+int oracle_sum_rows(const oracle_view* src, const oracle_view* dst);
+int oracle_argmax(const oracle_view* src, const oracle_view* dst);
+int oracle_argmax_index(const oracle_view* src, int64_t* index, float* value);
+int oracle_argmax_rows(const oracle_view* src, const oracle_view* dst);
+
+/* Row-range variants used by the multi-threaded CPU baseline: identical
+ * arithmetic, restricted to rows [row_begin, row_end) of a validated request
+ * (no validation; the caller validated the whole request first). */
+void oracle_unary_range(int op, const oracle_view* src, const oracle_view* dst, uint64_t begin, uint64_t end);
+void oracle_rms_norm_rows(const oracle_view* src, const oracle_view* dst, float eps, uint64_t row_begin, uint64_t row_end);
+
+/* The reference's own binary16 conversions (crates/emel-kernels/src/any/unary.rs:546-586). */
+uint16_t oracle_fp32_to_fp16(float value);
+float oracle_fp16_to_fp32(uint16_t bits);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

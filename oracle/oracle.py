@@ -1,0 +1,108 @@
+"""ctypes binding for the CPU oracle (liboracle.so).
+
+TEST INFRASTRUCTURE ONLY: the parity checker for tests/ and __graft_entry__,
+and the timed CPU baseline for bench.py.  The product library never imports
+this module.
+"""
+
+import ctypes
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "liboracle.so"
+
+DTYPE_CODE = {np.dtype(np.float32): 0, np.dtype(np.float16): 1, np.dtype(np.int32): 26, np.dtype(np.int64): 27}
+
+STATUS = {0: "ok", 1: "invalid_view", 2: "shape_mismatch", 3: "invalid_parameters", 4: "unexpected_event",
+          18: "invalid_argument"}
+
+
+class View(ctypes.Structure):
+    """Field-for-field the same layout as emel_tensor_view (include/emel_cuda.h)."""
+
+    _fields_ = [("data", ctypes.c_void_p), ("storage_bytes", ctypes.c_uint64), ("ne", ctypes.c_uint64 * 4),
+                ("nb", ctypes.c_uint64 * 4), ("dtype", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
+
+
+def make_view(ptr, storage_bytes, ne, nb, dtype_code):
+    v = View()
+    v.data = ptr
+    v.storage_bytes = storage_bytes
+    for d in range(4):
+        v.ne[d] = int(ne[d])
+        v.nb[d] = int(nb[d])
+    v.dtype = dtype_code
+    return v
+
+
+def host_view(array, ne=None, nb=None):
+    """View of a host numpy array; by default a dense row-major view whose ne[0]
+    is the last numpy axis (ggml order)."""
+    code = DTYPE_CODE[array.dtype]
+    if ne is None:
+        shape = list(array.shape)[::-1] + [1] * (4 - array.ndim)
+        ne = shape[:4]
+    if nb is None:
+        nb = [array.itemsize]
+        for d in range(1, 4):
+            nb.append(nb[-1] * ne[d - 1])
+    return make_view(array.ctypes.data, array.nbytes, ne, nb, code)
+
+
+_lib = None
+
+
+def build():
+    subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
+
+
+def load():
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        build()
+    lib = ctypes.CDLL(str(LIB_PATH))
+    P = ctypes.POINTER(View)
+    sigs = {
+        "oracle_binary": [ctypes.c_int, P, P, P],
+        "oracle_broadcast_row": [ctypes.c_int, P, P, P],
+        "oracle_binary_repeat": [ctypes.c_int, P, P, P],
+        "oracle_unary": [ctypes.c_int, P, P],
+        "oracle_op_unary": [ctypes.c_int, P, P],
+        "oracle_scale": [P, P, ctypes.c_float],
+        "oracle_clamp": [P, P, ctypes.c_float, ctypes.c_float],
+        "oracle_leaky_relu": [P, P, ctypes.c_float],
+        "oracle_silu_back": [P, P, P],
+        "oracle_add1": [P, P, ctypes.c_float],
+        "oracle_copy": [P, P],
+        "oracle_norm": [P, P, ctypes.c_float],
+        "oracle_rms_norm": [P, P, ctypes.c_float],
+        "oracle_rms_norm_mul": [P, P, P, ctypes.c_float],
+        "oracle_soft_max": [P, P],
+        "oracle_soft_max_ext": [P, P, P, ctypes.c_float],
+        "oracle_sum": [P, P],
+        "oracle_sum_f64": [P, ctypes.POINTER(ctypes.c_double)],
+        "oracle_mean": [P, P],
+        "oracle_sum_rows": [P, P],
+        "oracle_argmax": [P, P],
+        "oracle_argmax_index": [P, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_float)],
+        "oracle_argmax_rows": [P, P],
+    }
+    for name, args in sigs.items():
+        fn = getattr(lib, name)
+        fn.argtypes = args
+        fn.restype = ctypes.c_int
+    lib.oracle_unary_range.argtypes = [ctypes.c_int, P, P, ctypes.c_uint64, ctypes.c_uint64]
+    lib.oracle_unary_range.restype = None
+    lib.oracle_rms_norm_rows.argtypes = [P, P, ctypes.c_float, ctypes.c_uint64, ctypes.c_uint64]
+    lib.oracle_rms_norm_rows.restype = None
+    lib.oracle_fp32_to_fp16.argtypes = [ctypes.c_float]
+    lib.oracle_fp32_to_fp16.restype = ctypes.c_uint16
+    lib.oracle_fp16_to_fp32.argtypes = [ctypes.c_uint16]
+    lib.oracle_fp16_to_fp32.restype = ctypes.c_float
+    _lib = lib
+    return lib
