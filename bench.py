@@ -1,0 +1,467 @@
+"""Benchmark of the emel-kernels hot path on B200.
+
+Default workload (configuration 2 of the benchmark set): the unary /
+activation sweep -- silu, gelu (tanh approximation), relu, exp, neg, sqr,
+sqrt and pow(x, 2) -- over f32 and f16 tensors of ne = [14336, 512].  One
+step = those 16 ops once.  Metric: achieved HBM GB/s (algorithmic bytes:
+every input element read once, every output element written once).
+
+    python bench.py [--gpus N --steps K --warmup W]       # B200 device table
+    python bench.py --impl reference ...                   # CPU reference lane
+    python bench.py --suite                                # per-op lines, all configs
+
+Multi-GPU (torchrun, one process per GPU): every rank runs the same
+per-GPU workload on its own seeded data (weak scaling, no collective on the
+data path); the timed region is bracketed by barriers and the max over
+ranks is reported.
+"""
+
+import argparse
+import ctypes
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from __graft_entry__ import load_package  # noqa: E402
+
+METRIC = "per-op achieved HBM GB/s (fraction of ~8 TB/s) at 1/2/4/8 B200 vs host CPU"
+UNIT = "GB/s"
+OPS = [("silu", 10), ("gelu", 8), ("relu", 6), ("exp", 13), ("neg", 2), ("sqr", 64), ("sqrt", 65), ("pow2", 64)]
+FALLBACK_HBM_GBS = 6650.0
+
+
+# ---------------------------------------------------------------------------
+# environment
+# ---------------------------------------------------------------------------
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def profile_traffic(name):
+    """Per-launch DRAM bytes of the dominant kernel from a committed ncu
+    summary (a line `dram_bytes_per_launch: <int>`), or None."""
+    p = ROOT / "profiles" / name
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.strip().startswith("dram_bytes_per_launch:"):
+            return int(line.split(":", 1)[1].strip().split()[0])
+    return None
+
+
+class ClockSampler:
+    """Samples SM clock and throttle reasons through NVML while the timed
+    region runs."""
+
+    REASONS = {0x8: "hw_slowdown", 0x40: "hw_thermal_slowdown", 0x20: "sw_thermal_slowdown", 0x4: "sw_power_cap"}
+
+    def __init__(self, device):
+        self.device = device
+        self.samples = []
+        self.reasons = set()
+        self.stop = threading.Event()
+        self.max_mhz = None
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(self._physical_index(device))
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception:
+            self.nv = None
+
+    @staticmethod
+    def _physical_index(device):
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+        if vis:
+            ids = [v.strip() for v in vis.split(",") if v.strip()]
+            if device < len(ids) and ids[device].isdigit():
+                return int(ids[device])
+        return device
+
+    def _run(self):
+        while not self.stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                get = getattr(self.nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+                    self.nv.nvmlDeviceGetCurrentClocksThrottleReasons
+                r = get(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit:
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            self.stop.wait(0.01)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *exc):
+        if self.ok:
+            self.stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": sorted(self.reasons), "samples": 0}
+        return {"sm_mhz": statistics.median(self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# B200 arm
+# ---------------------------------------------------------------------------
+class Cfg2Step:
+    """The 16-op sweep over device buffers.  Each op reads its own copy of
+    its input so one step touches ~705 MB (5.6x the 126 MB L2): no input is
+    still in L2 when it is read again a step later."""
+
+    def __init__(self, pkg, ctx, torch, device, seed):
+        from emel_rs_b200 import workloads
+        self.pkg, self.ctx = pkg, ctx
+        x, xa = workloads.cfg2(seed)
+        self.host = {"f32": (x, xa), "f16": (x.astype(np.float16), xa.astype(np.float16))}
+        self.ne = [workloads.CFG2_NE[0], workloads.CFG2_NE[1], 1, 1]
+        self.n = x.size
+        self.tensors = []
+        self.launches = []  # (name, bytes, fn, args)
+        lib = pkg.lib()
+        for dt_name, code, tdt in (("f32", 0, torch.float32), ("f16", 1, torch.float16)):
+            base, base_abs = (torch.from_numpy(a).to(device) for a in self.host[dt_name])
+            for name, op in OPS:
+                src = (base_abs if name in ("sqrt", "pow2") else base).clone()
+                dst = torch.empty_like(src)
+                self.tensors += [src, dst]
+                sv = self._view(src, code)
+                dv = self._view(dst, code)
+                nbytes = 2 * self.n * src.element_size()
+                self.launches.append((f"{name}_{dt_name}", nbytes, lib.emel_cuda_unary,
+                                      [op, ctypes.byref(sv), ctypes.byref(dv)], (sv, dv)))
+        self.step_bytes = sum(l[1] for l in self.launches)
+
+    def _view(self, t, code):
+        v = self.pkg.CView()
+        v.data = t.data_ptr()
+        v.storage_bytes = t.numel() * t.element_size()
+        nb = self.pkg.contiguous_nb(self.ne, code)
+        for d in range(4):
+            v.ne[d] = self.ne[d]
+            v.nb[d] = nb[d]
+        v.dtype = code
+        return v
+
+    def run(self, stream, events=None):
+        h = self.ctx.handle
+        for i, (_, _, fn, args, _) in enumerate(self.launches):
+            if events is not None:
+                events[i][0].record()
+            st = fn(h, stream, *args)
+            if events is not None:
+                events[i][1].record()
+            if st != 0:
+                raise RuntimeError(f"launch {self.launches[i][0]} failed: {st} {self.ctx.last_error}")
+
+
+def run_b200(args, world, rank, local):
+    import torch
+    import torch.distributed as dist
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    pkg = load_package()
+    ctx = pkg.Context(local)
+    step = Cfg2Step(pkg, ctx, torch, device, seed=2 + 1000 * rank)
+    stream = torch.cuda.current_stream(device)
+    sh = ctypes.c_void_p(stream.cuda_stream)
+
+    for _ in range(args.warmup):
+        step.run(sh)
+    torch.cuda.synchronize()
+
+    # per-op events on a spread-out subset of the timed steps
+    sample_every = max(1, args.steps // 64)
+    sampled = list(range(0, args.steps, sample_every))
+    ev = {s: [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+              for _ in step.launches] for s in sampled}
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    launches_before = ctx.launches
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        t0.record()
+        for s in range(args.steps):
+            step.run(sh, ev.get(s))
+        t1.record()
+        torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    gpu_launches = ctx.launches - launches_before
+    ms = t0.elapsed_time(t1)
+    ms_t = torch.tensor([ms], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms_max = float(ms_t.item())
+
+    # per-op average durations over the sampled steps
+    per_op = {}
+    for i, (name, nbytes, *_rest) in enumerate(step.launches):
+        d = [ev[s][i][0].elapsed_time(ev[s][i][1]) for s in sampled]
+        per_op[name] = (nbytes, statistics.mean(d))
+    dom = max(per_op.items(), key=lambda kv: kv[1][1])
+    dom_name, (dom_bytes, dom_ms) = dom
+
+    e2e = run_e2e(args, pkg, ctx, torch, step, stream, sh, world)
+
+    if rank != 0:
+        if world > 1:
+            dist.destroy_process_group()
+        return
+    peak, peak_kind = peaks()
+    value = world * args.steps * step.step_bytes / (ms_max / 1e3) / 1e9
+    achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+    traffic = profile_traffic("unary_cfg2_ncu.md")
+    line = {
+        "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(ms_max / args.steps, 5), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32+f16", "data": "synthetic (seeded, per rank)",
+        "config": {
+            "workload": "cfg2 unary/activation sweep: silu, gelu(tanh), relu, exp, neg, sqr, sqrt, pow(x,2) "
+                        "on f32 and f16 ne=[14336,512]; N(0,2) clamped to [-10,10]; sqrt/pow on |x|+1e-3",
+            "ops_per_step": len(step.launches), "bytes_per_step": step.step_bytes,
+            "l2": "inputs larger than L2: 16 distinct input/output buffer pairs, 705 MB touched per step",
+            "parallelism": f"dp{world} (independent per-GPU batches)",
+        },
+        "roofline": {"bound": "hbm", "kernel": f"ew_flat ({dom_name})", "achieved": round(achieved, 1),
+                     "peak": peak, "peak_source": f"{peak_kind} hbm_gbs", "unit": "GB/s",
+                     "frac": round(achieved / peak, 4), "traffic": traffic,
+                     "algorithmic_bytes_per_launch": dom_bytes},
+        "per_op_gbs": {k: round(b / (t / 1e3) / 1e9, 1) for k, (b, t) in per_op.items()},
+        "e2e": e2e,
+        "gpu_launches": gpu_launches,
+        "clocks": clocks.summary(),
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_single(args)
+    print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.destroy_process_group()
+
+
+def run_e2e(args, pkg, ctx, torch, step, stream, sh, world):
+    """The same metric through the C ABI with host buffers: every step copies
+    the four source tensors from pinned host memory, runs the 16 ops and
+    reads all 16 outputs back."""
+    lib = pkg.lib()
+    srcs = []  # (pinned host, device tensor)
+    for dt_name in ("f32", "f16"):
+        for arr in step.host[dt_name]:
+            h = torch.from_numpy(arr.copy()).pin_memory()
+            d = torch.empty_like(h, device=stream.device)
+            srcs.append((h, d))
+    f32x, f32a, f16x, f16a = (d for _, d in srcs)
+    outs = []
+    launches = []
+    for dt_name, code, (x, xa) in (("f32", 0, (f32x, f32a)), ("f16", 1, (f16x, f16a))):
+        for name, op in OPS:
+            src = xa if name in ("sqrt", "pow2") else x
+            dst = torch.empty_like(src)
+            hout = torch.empty(dst.shape, dtype=dst.dtype, pin_memory=True)
+            outs.append((hout, dst))
+            sv, dv = step._view(src, code), step._view(dst, code)
+            launches.append((op, sv, dv))
+    h2d = sum(h.numel() * h.element_size() for h, _ in srcs)
+    d2h = sum(h.numel() * h.element_size() for h, _ in outs)
+
+    def one():
+        for h, d in srcs:
+            lib.emel_cuda_memcpy_h2d(ctx.handle, sh, d.data_ptr(), h.data_ptr(), h.numel() * h.element_size())
+        for op, sv, dv in launches:
+            st = lib.emel_cuda_unary(ctx.handle, sh, op, ctypes.byref(sv), ctypes.byref(dv))
+            if st != 0:
+                raise RuntimeError(ctx.last_error)
+        for h, d in outs:
+            lib.emel_cuda_memcpy_d2h(ctx.handle, sh, h.data_ptr(), d.data_ptr(), h.numel() * h.element_size())
+
+    steps = max(3, min(args.steps, 20))
+    for _ in range(2):
+        one()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record()
+    for _ in range(steps):
+        one()
+    t1.record()
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1)
+    if world > 1:
+        import torch.distributed as dist
+        m = torch.tensor([ms], dtype=torch.float64, device=stream.device)
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        ms = float(m.item())
+    value = world * steps * step.step_bytes / (ms / 1e3) / 1e9
+    return {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "steps": steps, "path": "emel_cuda_memcpy_h2d + emel_cuda_unary x16 + emel_cuda_memcpy_d2h (pinned host)"}
+
+
+# ---------------------------------------------------------------------------
+# CPU lanes (the oracle: C restatement of the reference loops)
+# ---------------------------------------------------------------------------
+def cpu_workload():
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+    pkg = load_package()
+    from emel_rs_b200 import workloads
+    x, xa = workloads.cfg2(2)
+    bufs = []
+    items = []
+    ne = [workloads.CFG2_NE[0], workloads.CFG2_NE[1], 1, 1]
+    for dt, code in ((np.float32, 0), (np.float16, 1)):
+        xs, xas = x.astype(dt), xa.astype(dt)
+        for name, op in OPS:
+            src = xas if name in ("sqrt", "pow2") else xs
+            dst = np.empty_like(src)
+            bufs += [src, dst]
+            nb = pkg.contiguous_nb(ne, code)
+            sv = oracle.make_view(src.ctypes.data, src.nbytes, ne, nb, code)
+            dv = oracle.make_view(dst.ctypes.data, dst.nbytes, ne, nb, code)
+            items.append((op, sv, dv, 2 * src.nbytes))
+    return oracle.load(), items, bufs, x.size
+
+
+def cpu_baseline_single(args):
+    """Single-thread oracle (the reference's kernels are single-threaded) on a
+    time-bounded sample: whole 16-op passes over the cfg2 tensors."""
+    lib, items, bufs, n = cpu_workload()
+    done_bytes, t0 = 0, time.perf_counter()
+    passes = 0
+    while True:
+        for op, sv, dv, nbytes in items:
+            lib.oracle_unary_range(op, ctypes.byref(sv), ctypes.byref(dv), 0, n)
+            done_bytes += nbytes
+        passes += 1
+        if time.perf_counter() - t0 >= args.cpu_seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(done_bytes / dt / 1e9, 3), "unit": UNIT, "cores": 1, "kind": "port",
+            "sample": f"{passes} full cfg2 step(s) (16 ops x 7340032 elements) in {dt:.1f} s, single thread, "
+                      f"C restatement of the emel-kernels loops (reference Rust not buildable offline)",
+            "cpu_model": cpu_model()}
+
+
+def cpu_model():
+    try:
+        for line in Path("/proc/cpuinfo").read_text().splitlines():
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except Exception:
+        pass
+    return "unknown"
+
+
+def host_threads():
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def run_reference(args, world, rank):
+    """CPU reference lane: the oracle on all host threads (rows split across
+    threads; ctypes releases the GIL), same metric and workload."""
+    if rank != 0:
+        return
+    from concurrent.futures import ThreadPoolExecutor
+    lib, items, bufs, n = cpu_workload()
+    threads = host_threads()
+    pool = ThreadPoolExecutor(max_workers=threads)
+
+    def step(frac):
+        count = max(threads, int(n * frac))
+        chunk = (count + threads - 1) // threads
+        done = 0
+        for op, sv, dv, nbytes in items:
+            futs = [pool.submit(lib.oracle_unary_range, op, ctypes.byref(sv), ctypes.byref(dv), b,
+                                min(b + chunk, count)) for b in range(0, count, chunk)]
+            for f in futs:
+                f.result()
+            done += nbytes * count // n
+        return done
+
+    t = time.perf_counter()
+    step(1.0)
+    full = time.perf_counter() - t
+    # size each step so warmup + steps stay within the time budget
+    frac = min(1.0, args.ref_seconds / max(1e-9, full * (args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        step(frac)
+    t = time.perf_counter()
+    done = 0
+    for _ in range(args.steps):
+        done += step(frac)
+    dt = time.perf_counter() - t
+    value = done / dt / 1e9
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32+f16",
+        "data": "synthetic (seeded)",
+        "config": {"workload": "cfg2 unary/activation sweep (same ops and tensors as the B200 arm)",
+                   "sample_fraction_per_step": round(frac, 5)},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{frac:.4f} of the cfg2 elements per op per step, {threads} threads",
+                         "cpu_model": cpu_model()},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=2000)
+    ap.add_argument("--warmup", type=int, default=20)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--ref-seconds", type=float, default=60.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    world, rank, local = dist_env()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args, world, rank)
+        return
+    run_b200(args, world, rank, local)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,592 @@
+"""emel.rs_b200 -- B200 (sm_100a) device op table for the emel-kernels
+elementwise, broadcast and reduction operators.
+
+This module is the host-side mirror of the reference operator contract
+(stateforward/emel.rs, crates/emel-kernels/src/any/): the same event names,
+argument meaning and error behaviour, dispatched through the C ABI of
+libemel_cuda.so (include/emel_cuda.h) to hand-written sm_100a kernels.
+
+    k = Kernel(device=0)
+    status = k.process_event(OpAdd(lhs, rhs, out))      # binary.rs:47-81
+    assert status == Status.OK
+
+Views bind device memory: either a DeviceBuffer allocated through the
+library, or any device pointer (e.g. a torch tensor's data_ptr()).  There is
+no CPU fallback: without the compiled library or a CUDA device every call
+raises.
+"""
+
+import ctypes
+import enum
+from dataclasses import dataclass
+from pathlib import Path
+from typing import Optional, Sequence
+
+PACKAGE_DIR = Path(__file__).resolve().parent
+LIB_PATH = PACKAGE_DIR / "libemel_cuda.so"
+
+
+class DType(enum.IntEnum):
+    """DType::code() wire values (tensor_view.rs:160-209)."""
+    F32 = 0
+    F16 = 1
+    I32 = 26
+    I64 = 27
+
+
+DTYPE_SIZE = {DType.F32: 4, DType.F16: 2, DType.I32: 4, DType.I64: 8}
+
+
+class Status(enum.IntEnum):
+    OK = 0
+    INVALID_VIEW = 1
+    SHAPE_MISMATCH = 2
+    INVALID_PARAMETERS = 3
+    UNEXPECTED_EVENT = 4
+    INTERNAL = 5
+    DEVICE_ERROR = 16
+    TIMEOUT = 17
+    INVALID_ARGUMENT = 18
+    OUT_OF_MEMORY = 19
+
+
+class BinaryOp(enum.IntEnum):
+    ADD = 0
+    SUB = 1
+    MUL = 2
+    DIV = 3
+
+
+class UnaryOp(enum.IntEnum):
+    """UnarySubOp wire codes (unary.rs:101-146) plus the other one-input events."""
+    ABS = 0
+    SGN = 1
+    NEG = 2
+    STEP = 3
+    TANH = 4
+    ELU = 5
+    RELU = 6
+    SIGMOID = 7
+    GELU = 8
+    GELU_QUICK = 9
+    SILU = 10
+    HARDSWISH = 11
+    HARDSIGMOID = 12
+    EXP = 13
+    EXPM1 = 14
+    SOFTPLUS = 15
+    GELU_ERF = 16
+    XIELU = 17
+    FLOOR = 18
+    CEIL = 19
+    ROUND = 20
+    TRUNC = 21
+    SQR = 64
+    SQRT = 65
+    LOG = 66
+    SIN = 67
+    COS = 68
+
+
+class CView(ctypes.Structure):
+    """emel_tensor_view."""
+    _fields_ = [("data", ctypes.c_void_p), ("storage_bytes", ctypes.c_uint64), ("ne", ctypes.c_uint64 * 4),
+                ("nb", ctypes.c_uint64 * 4), ("dtype", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
+
+
+class CArgmaxPartial(ctypes.Structure):
+    """emel_cuda_argmax_partial."""
+    _fields_ = [("value", ctypes.c_float), ("has_value", ctypes.c_uint32), ("index", ctypes.c_int64),
+                ("first_is_nan", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
+
+
+# Every symbol include/emel_cuda.h declares, with its ctypes signature.
+_P = ctypes.POINTER(CView)
+_V = ctypes.c_void_p
+_CTX = ctypes.c_void_p
+_I = ctypes.c_int
+_F = ctypes.c_float
+SIGNATURES = {
+    "emel_cuda_context_create": (_I, [_I, ctypes.POINTER(_CTX)]),
+    "emel_cuda_context_destroy": (_I, [_CTX]),
+    "emel_cuda_context_last_error": (ctypes.c_char_p, [_CTX]),
+    "emel_cuda_malloc": (_I, [_CTX, ctypes.c_uint64, ctypes.POINTER(_V)]),
+    "emel_cuda_free": (_I, [_CTX, _V]),
+    "emel_cuda_memcpy_h2d": (_I, [_CTX, _V, _V, _V, ctypes.c_uint64]),
+    "emel_cuda_memcpy_d2h": (_I, [_CTX, _V, _V, _V, ctypes.c_uint64]),
+    "emel_cuda_memset": (_I, [_CTX, _V, _V, _I, ctypes.c_uint64]),
+    "emel_cuda_stream_create": (_I, [_CTX, ctypes.POINTER(_V)]),
+    "emel_cuda_stream_destroy": (_I, [_CTX, _V]),
+    "emel_cuda_stream_synchronize": (_I, [_CTX, _V]),
+    "emel_cuda_launch_count": (ctypes.c_uint64, [_CTX]),
+    "emel_cuda_binary": (_I, [_CTX, _V, _I, _P, _P, _P]),
+    "emel_cuda_broadcast_row": (_I, [_CTX, _V, _I, _P, _P, _P]),
+    "emel_cuda_binary_repeat": (_I, [_CTX, _V, _I, _P, _P, _P]),
+    "emel_cuda_unary": (_I, [_CTX, _V, _I, _P, _P]),
+    "emel_cuda_op_unary": (_I, [_CTX, _V, _I, _P, _P]),
+    "emel_cuda_scale": (_I, [_CTX, _V, _P, _P, _F]),
+    "emel_cuda_clamp": (_I, [_CTX, _V, _P, _P, _F, _F]),
+    "emel_cuda_leaky_relu": (_I, [_CTX, _V, _P, _P, _F]),
+    "emel_cuda_silu_back": (_I, [_CTX, _V, _P, _P, _P]),
+    "emel_cuda_add1": (_I, [_CTX, _V, _P, _P, _F]),
+    "emel_cuda_copy": (_I, [_CTX, _V, _P, _P]),
+    "emel_cuda_norm": (_I, [_CTX, _V, _P, _P, _F]),
+    "emel_cuda_rms_norm": (_I, [_CTX, _V, _P, _P, _F]),
+    "emel_cuda_rms_norm_mul": (_I, [_CTX, _V, _P, _P, _P, _F]),
+    "emel_cuda_soft_max": (_I, [_CTX, _V, _P, _P]),
+    "emel_cuda_soft_max_ext": (_I, [_CTX, _V, _P, _P, _P, _F]),
+    "emel_cuda_sum": (_I, [_CTX, _V, _P, _P]),
+    "emel_cuda_sum_f64": (_I, [_CTX, _V, _P, _V]),
+    "emel_cuda_mean": (_I, [_CTX, _V, _P, _P]),
+    "emel_cuda_sum_rows": (_I, [_CTX, _V, _P, _P]),
+    "emel_cuda_argmax": (_I, [_CTX, _V, _P, _P]),
+    "emel_cuda_argmax_partial_compute": (_I, [_CTX, _V, _P, ctypes.c_int64, _V]),
+    "emel_cuda_argmax_combine": (_I, [ctypes.POINTER(CArgmaxPartial), _I, ctypes.POINTER(ctypes.c_int64),
+                                      ctypes.POINTER(ctypes.c_float)]),
+    "emel_cuda_argmax_rows": (_I, [_CTX, _V, _P, _P]),
+}
+
+_lib = None
+
+
+def lib():
+    """The loaded device library.  Raises when it has not been built: the
+    operators have no CPU path."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB_PATH.exists():
+        raise RuntimeError(f"{LIB_PATH} is missing: build it with `make -C emel.rs_b200/csrc` "
+                           "(the device op table has no CPU fallback)")
+    handle = ctypes.CDLL(str(LIB_PATH))
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(handle, name)
+        fn.restype = res
+        fn.argtypes = args
+    _lib = handle
+    return handle
+
+
+# ---------------------------------------------------------------------------
+# Layouts and views (tensor_view.rs:215-448, 537-898)
+# ---------------------------------------------------------------------------
+
+def contiguous_nb(ne: Sequence[int], dtype: DType = DType.F32):
+    nb = [DTYPE_SIZE[DType(dtype)]]
+    for d in range(1, 4):
+        nb.append(nb[-1] * int(ne[d - 1]))
+    return nb
+
+
+@dataclass(frozen=True)
+class Layout:
+    """Layout { dtype, ne[4], nb[4] } (tensor_view.rs:215-219); nb in bytes,
+    nb[0] == 0 means implicit row-major."""
+    dtype: DType
+    ne: tuple
+    nb: tuple
+
+    @staticmethod
+    def contiguous(dtype, ne):
+        ne = tuple(int(x) for x in ne)
+        return Layout(DType(dtype), ne, tuple(contiguous_nb(ne, dtype)))
+
+    @staticmethod
+    def new(dtype, ne, nb):
+        return Layout(DType(dtype), tuple(int(x) for x in ne), tuple(int(x) for x in nb))
+
+    def permuted(self, axes):
+        """Layout::permuted (tensor_view.rs:318-332)."""
+        return Layout(self.dtype, tuple(self.ne[a] for a in axes), tuple(self.nb[a] for a in axes))
+
+
+@dataclass
+class TensorView:
+    """A layout bound to device storage: `ptr` is a device address and
+    `storage_bytes` how far the view may reach (the slice length)."""
+    ptr: int
+    storage_bytes: int
+    layout: Layout
+
+    def c(self) -> CView:
+        v = CView()
+        v.data = self.ptr
+        v.storage_bytes = self.storage_bytes
+        for d in range(4):
+            v.ne[d] = self.layout.ne[d]
+            v.nb[d] = self.layout.nb[d]
+        v.dtype = int(self.layout.dtype)
+        v.reserved = 0
+        return v
+
+
+TensorViewMut = TensorView
+
+
+def _check(status, what="call"):
+    st = Status(status)
+    if st != Status.OK:
+        raise RuntimeError(f"{what} failed with {st.name}")
+    return st
+
+
+class Context:
+    """emel_cuda_context: device selection, reduction workspace, handles."""
+
+    def __init__(self, device: int = 0):
+        self._lib = lib()
+        h = ctypes.c_void_p()
+        st = self._lib.emel_cuda_context_create(device, ctypes.byref(h))
+        if st != 0:
+            raise RuntimeError(f"emel_cuda_context_create(device={device}) failed: {Status(st).name}")
+        self.handle = h
+        self.device = device
+
+    def close(self):
+        if self.handle:
+            self._lib.emel_cuda_context_destroy(self.handle)
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def last_error(self):
+        return self._lib.emel_cuda_context_last_error(self.handle).decode()
+
+    @property
+    def launches(self):
+        return int(self._lib.emel_cuda_launch_count(self.handle))
+
+    def synchronize(self, stream=None):
+        _check(self._lib.emel_cuda_stream_synchronize(self.handle, stream), "stream synchronize")
+
+
+class DeviceBuffer:
+    """Device memory owned through the library (emel_cuda_malloc)."""
+
+    def __init__(self, ctx: Context, nbytes: int):
+        self.ctx = ctx
+        self.nbytes = int(nbytes)
+        p = ctypes.c_void_p()
+        _check(ctx._lib.emel_cuda_malloc(ctx.handle, max(self.nbytes, 1), ctypes.byref(p)), "malloc")
+        self.ptr = p.value
+
+    def upload(self, array, stream=None):
+        """Copies a host numpy array into the start of the buffer and waits."""
+        _check(self.ctx._lib.emel_cuda_memcpy_h2d(self.ctx.handle, stream, self.ptr, array.ctypes.data, array.nbytes), "h2d")
+        self.ctx.synchronize(stream)
+
+    def download(self, array, stream=None):
+        _check(self.ctx._lib.emel_cuda_memcpy_d2h(self.ctx.handle, stream, array.ctypes.data, self.ptr, array.nbytes), "d2h")
+        self.ctx.synchronize(stream)
+        return array
+
+    def view(self, layout: Layout, storage_bytes: Optional[int] = None) -> TensorView:
+        return TensorView(self.ptr, self.nbytes if storage_bytes is None else storage_bytes, layout)
+
+    def free(self):
+        if self.ptr:
+            self.ctx._lib.emel_cuda_free(self.ctx.handle, self.ptr)
+            self.ptr = None
+
+    def __del__(self):
+        try:
+            self.free()
+        except Exception:
+            pass
+
+
+# ---------------------------------------------------------------------------
+# Events (crates/emel-kernels/src/any/event.rs and the per-family modules)
+# ---------------------------------------------------------------------------
+
+class Event:
+    def dispatch(self, ctx: Context, stream) -> int:
+        raise NotImplementedError
+
+
+def _r(view):
+    return ctypes.byref(view.c()) if view is not None else None
+
+
+@dataclass
+class _Binary(Event):
+    lhs: TensorView
+    rhs: TensorView
+    output: TensorView
+    OP = BinaryOp.ADD
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_binary(ctx.handle, stream, int(self.OP), _r(self.lhs), _r(self.rhs), _r(self.output))
+
+
+class OpAdd(_Binary):
+    """binary::OpAdd (binary.rs:78)."""
+    OP = BinaryOp.ADD
+
+
+class OpSub(_Binary):
+    OP = BinaryOp.SUB
+
+
+class OpMul(_Binary):
+    OP = BinaryOp.MUL
+
+
+class OpDiv(_Binary):
+    OP = BinaryOp.DIV
+
+
+@dataclass
+class _BroadcastRow(Event):
+    src0: TensorView
+    src1: TensorView
+    dst: TensorView
+    OP = BinaryOp.ADD
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_broadcast_row(ctx.handle, stream, int(self.OP), _r(self.src0), _r(self.src1), _r(self.dst))
+
+
+class OpAddBroadcastRow(_BroadcastRow):
+    """broadcast::OpAddBroadcastRow (broadcast.rs:53-67)."""
+    OP = BinaryOp.ADD
+
+
+class OpSubBroadcastRow(_BroadcastRow):
+    OP = BinaryOp.SUB
+
+
+class OpMulBroadcastRow(_BroadcastRow):
+    """broadcast::OpMulBroadcastRow (broadcast.rs:69-84)."""
+    OP = BinaryOp.MUL
+
+
+class OpDivBroadcastRow(_BroadcastRow):
+    OP = BinaryOp.DIV
+
+
+@dataclass
+class OpBinaryRepeat(Event):
+    """Repeat src1 to dst's extents (generic.rs:1641-1665), then op."""
+    op: BinaryOp
+    src0: TensorView
+    src1: TensorView
+    dst: TensorView
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_binary_repeat(ctx.handle, stream, int(self.op), _r(self.src0), _r(self.src1), _r(self.dst))
+
+
+@dataclass
+class OpUnaryTyped(Event):
+    """The typed unary events OpAbs..OpTrunc, OpSqr, OpSqrt, OpLog, OpSin, OpCos."""
+    op: UnaryOp
+    input: TensorView
+    output: TensorView
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_unary(ctx.handle, stream, int(self.op), _r(self.input), _r(self.output))
+
+
+def _typed(op):
+    def make(input, output):
+        return OpUnaryTyped(op, input, output)
+    return make
+
+
+OpAbs, OpSgn, OpNeg, OpStep = _typed(UnaryOp.ABS), _typed(UnaryOp.SGN), _typed(UnaryOp.NEG), _typed(UnaryOp.STEP)
+OpTanh, OpElu, OpRelu, OpSigmoid = _typed(UnaryOp.TANH), _typed(UnaryOp.ELU), _typed(UnaryOp.RELU), _typed(UnaryOp.SIGMOID)
+OpGelu, OpGeluQuick, OpSilu = _typed(UnaryOp.GELU), _typed(UnaryOp.GELU_QUICK), _typed(UnaryOp.SILU)
+OpHardswish, OpHardsigmoid = _typed(UnaryOp.HARDSWISH), _typed(UnaryOp.HARDSIGMOID)
+OpExp, OpExpm1, OpSoftplus, OpGeluErf = _typed(UnaryOp.EXP), _typed(UnaryOp.EXPM1), _typed(UnaryOp.SOFTPLUS), _typed(UnaryOp.GELU_ERF)
+OpFloor, OpCeil, OpRound, OpTrunc = _typed(UnaryOp.FLOOR), _typed(UnaryOp.CEIL), _typed(UnaryOp.ROUND), _typed(UnaryOp.TRUNC)
+OpSqr, OpSqrt = _typed(UnaryOp.SQR), _typed(UnaryOp.SQRT)
+OpLog, OpSin, OpCos = _typed(UnaryOp.LOG), _typed(UnaryOp.SIN), _typed(UnaryOp.COS)
+
+
+@dataclass
+class OpUnary(Event):
+    """Generic unary::OpUnary (unary.rs:148-172): eight accepted subops."""
+    subop: UnaryOp
+    input: TensorView
+    output: TensorView
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_op_unary(ctx.handle, stream, int(self.subop), _r(self.input), _r(self.output))
+
+
+@dataclass
+class OpScale(Event):
+    """activation::OpScale (activation.rs:58)."""
+    input: TensorView
+    output: TensorView
+    scale: float
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_scale(ctx.handle, stream, _r(self.input), _r(self.output), self.scale)
+
+
+@dataclass
+class OpClamp(Event):
+    input: TensorView
+    output: TensorView
+    min: float
+    max: float
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_clamp(ctx.handle, stream, _r(self.input), _r(self.output), self.min, self.max)
+
+
+@dataclass
+class OpLeakyRelu(Event):
+    input: TensorView
+    output: TensorView
+    negative_slope: float
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_leaky_relu(ctx.handle, stream, _r(self.input), _r(self.output), self.negative_slope)
+
+
+@dataclass
+class OpSiluBack(Event):
+    input: TensorView
+    gradient: TensorView
+    output: TensorView
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_silu_back(ctx.handle, stream, _r(self.input), _r(self.gradient), _r(self.output))
+
+
+@dataclass
+class OpAdd1(Event):
+    src: TensorView
+    dst: TensorView
+    scalar: float
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_add1(ctx.handle, stream, _r(self.src), _r(self.dst), self.scalar)
+
+
+@dataclass
+class CopyTensor(Event):
+    """tensor_view::CopyTensor (tensor_view.rs:954-967)."""
+    src: TensorView
+    dst: TensorView
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_copy(ctx.handle, stream, _r(self.src), _r(self.dst))
+
+
+@dataclass
+class OpNorm(Event):
+    """normalization::OpNorm (normalization.rs:58-76)."""
+    input: TensorView
+    output: TensorView
+    epsilon: float
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_norm(ctx.handle, stream, _r(self.input), _r(self.output), self.epsilon)
+
+
+@dataclass
+class OpRmsNorm(Event):
+    """normalization::OpRmsNorm (normalization.rs:78-96)."""
+    input: TensorView
+    output: TensorView
+    epsilon: float
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_rms_norm(ctx.handle, stream, _r(self.input), _r(self.output), self.epsilon)
+
+
+@dataclass
+class OpRmsNormMul(Event):
+    """OpRmsNorm then OpMulBroadcastRow by `weight`, fused."""
+    input: TensorView
+    weight: TensorView
+    output: TensorView
+    epsilon: float
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_rms_norm_mul(ctx.handle, stream, _r(self.input), _r(self.weight), _r(self.output),
+                                               self.epsilon)
+
+
+@dataclass
+class OpSoftMax(Event):
+    """reductions::OpSoftMax (reductions.rs:150-163)."""
+    src: TensorView
+    dst: TensorView
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_soft_max(ctx.handle, stream, _r(self.src), _r(self.dst))
+
+
+@dataclass
+class OpSoftMaxExt(Event):
+    """Softmax of src * scale + mask (mask optional, F16 or F32)."""
+    src: TensorView
+    mask: Optional[TensorView]
+    dst: TensorView
+    scale: float
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_soft_max_ext(ctx.handle, stream, _r(self.src), _r(self.mask), _r(self.dst), self.scale)
+
+
+def _reduce(name, doc):
+    @dataclass
+    class R(Event):
+        src: TensorView
+        dst: TensorView
+
+        def dispatch(self, ctx, stream):
+            return getattr(ctx._lib, name)(ctx.handle, stream, _r(self.src), _r(self.dst))
+    R.__doc__ = doc
+    return R
+
+
+OpSum = _reduce("emel_cuda_sum", "reductions::OpSum (reductions.rs:90-103).")
+OpMean = _reduce("emel_cuda_mean", "reductions::OpMean (reductions.rs:120-133).")
+OpSumRows = _reduce("emel_cuda_sum_rows", "reductions::OpSumRows (reductions.rs:105-118).")
+OpArgmax = _reduce("emel_cuda_argmax", "reductions::OpArgmax (reductions.rs:135-148).")
+OpArgmaxRows = _reduce("emel_cuda_argmax_rows", "Per-row argmax (reductions.rs:715-730 per row).")
+
+
+class Kernel:
+    """Mirror of emel_kernels::Kernel (actor.rs:905-949): single-writer,
+    dispatches one typed event per call.  Device work is enqueued on
+    `stream` (None = legacy default stream); process_event returns the
+    reference-style status without waiting for the device unless
+    `synchronize` is set."""
+
+    def __init__(self, device: int = 0, ctx: Optional[Context] = None, stream=None, synchronize: bool = False):
+        self.ctx = ctx or Context(device)
+        self.stream = stream
+        self.synchronize = synchronize
+
+    def process_event(self, event: Event) -> Status:
+        st = Status(event.dispatch(self.ctx, self.stream))
+        if st == Status.OK and self.synchronize:
+            self.ctx.synchronize(self.stream)
+        return st
+
+
+def argmax_combine(partials):
+    """Combines per-shard (value, has_value, index, first_is_nan) tuples in
+    shard order through emel_cuda_argmax_combine."""
+    arr = (CArgmaxPartial * len(partials))()
+    for k, (value, has, index, first_nan) in enumerate(partials):
+        arr[k].value = value
+        arr[k].has_value = has
+        arr[k].index = index
+        arr[k].first_is_nan = first_nan
+    idx = ctypes.c_int64()
+    val = ctypes.c_float()
+    _check(lib().emel_cuda_argmax_combine(arr, len(partials), ctypes.byref(idx), ctypes.byref(val)), "argmax_combine")
+    return idx.value, val.value

@@ -1,0 +1,250 @@
+// Device-side numeric helpers shared by every kernel of the device op table.
+//
+// Bit-exactness contract: results must equal the reference's x86-64 CPU
+// loops (IEEE binary32, round-to-nearest-even, no FMA contraction, subnormals
+// kept).  The translation units are compiled with -fmad=false -ftz=false
+// -prec-div=true -prec-sqrt=true, and every formula spells out the
+// reference's operation order.  Two things differ between SSE and the GPU
+// and are handled here explicitly:
+//   * NaN results: SSE returns the first NaN operand, quietened, or the
+//     "indefinite" QNaN 0xFFC00000 for an invalid operation; the GPU returns
+//     a canonical NaN.  `x86_nan2`/`x86_nan1` rebuild the SSE bits.
+//   * sign/abs: PTX neg/abs leave NaN payloads unspecified, so they are
+//     done on the integer bits.
+// Transcendentals are evaluated in binary64 and rounded once to binary32,
+// which stays within 1 ulp of glibc's expf/expm1f/logf/sinf/cosf and within
+// 2 ulp of its tanhf over the inputs the parity tests sweep.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cstdint>
+
+#include "plan.hpp"
+
+namespace emel {
+
+constexpr uint32_t kIndefiniteNaN = 0xFFC00000u;
+
+__device__ __forceinline__ uint32_t fbits(float f) { return __float_as_uint(f); }
+__device__ __forceinline__ float bitsf(uint32_t u) { return __uint_as_float(u); }
+__device__ __forceinline__ bool is_nan(float f) { return (fbits(f) & 0x7fffffffu) > 0x7f800000u; }
+__device__ __forceinline__ float quiet(float f) { return bitsf(fbits(f) | 0x00400000u); }
+
+// Result of an SSE binary operation whose GPU result `r` was computed from
+// operands (a, b) in that source order.
+__device__ __forceinline__ float x86_nan2(float r, float a, float b) {
+    if (!is_nan(r)) return r;
+    if (is_nan(a)) return quiet(a);
+    if (is_nan(b)) return quiet(b);
+    return bitsf(kIndefiniteNaN);
+}
+
+// Result of a one-input libm/SSE operation: a NaN input comes back quietened,
+// a NaN produced from a number is the invalid-operation QNaN.
+__device__ __forceinline__ float x86_nan1(float r, float a) {
+    if (!is_nan(r)) return r;
+    if (is_nan(a)) return quiet(a);
+    return bitsf(kIndefiniteNaN);
+}
+
+__device__ __forceinline__ float f_add(float a, float b) { return x86_nan2(__fadd_rn(a, b), a, b); }
+__device__ __forceinline__ float f_sub(float a, float b) { return x86_nan2(__fsub_rn(a, b), a, b); }
+__device__ __forceinline__ float f_mul(float a, float b) { return x86_nan2(__fmul_rn(a, b), a, b); }
+__device__ __forceinline__ float f_div(float a, float b) { return x86_nan2(__fdiv_rn(a, b), a, b); }
+__device__ __forceinline__ float f_neg(float a) { return bitsf(fbits(a) ^ 0x80000000u); }
+__device__ __forceinline__ float f_abs(float a) { return bitsf(fbits(a) & 0x7fffffffu); }
+__device__ __forceinline__ float f_sqrt(float a) { return x86_nan1(__fsqrt_rn(a), a); }
+
+// binary32 <-> binary16 with the reference's NaN behaviour: a NaN becomes the
+// quiet half 0x7E00 with the input's sign (unary.rs:546-570); a half NaN
+// widens with its payload shifted up and quietened (unary.rs:572-586).  For
+// every other value both directions are exact IEEE conversions (RNE when
+// narrowing), which the hardware cvt instructions implement.
+__device__ __forceinline__ uint16_t f32_to_f16_bits(float v) {
+    if (is_nan(v)) return (uint16_t)(((fbits(v) >> 16) & 0x8000u) | 0x7e00u);
+    return __half_as_ushort(__float2half_rn(v));
+}
+
+__device__ __forceinline__ float f16_bits_to_f32(uint16_t h) {
+    if ((h & 0x7fffu) > 0x7c00u) return bitsf(((uint32_t)(h & 0x8000u) << 16) | 0x7fc00000u | ((uint32_t)(h & 0x3ffu) << 13));
+    return __half2float(__ushort_as_half(h));
+}
+
+// ---------------------------------------------------------------------------
+// Binary formulas (binary.rs:386-409).
+// ---------------------------------------------------------------------------
+
+template <int OP>
+__device__ __forceinline__ float binary_apply(float a, float b) {
+    if constexpr (OP == kAdd) return f_add(a, b);
+    if constexpr (OP == kSub) return f_sub(a, b);
+    if constexpr (OP == kMul) return f_mul(a, b);
+    return f_div(a, b);
+}
+
+// ---------------------------------------------------------------------------
+// Unary formulas (unary.rs:474-672, power.rs:315/397-412,
+// reductions.rs:640-668, activation.rs:366-521, elementwise.rs:280-291).
+// Codes match emel_cuda_unary_op; parameterised ops use codes >= 128.
+// ---------------------------------------------------------------------------
+
+struct UnaryParams {
+    float a;
+    float b;
+};
+
+// One libm call of the reference evaluated as binary64 and rounded once.
+__device__ __forceinline__ float lm_exp(float x) { return x86_nan1((float)exp((double)x), x); }
+__device__ __forceinline__ float lm_expm1(float x) { return x86_nan1((float)expm1((double)x), x); }
+__device__ __forceinline__ float lm_tanh(float x) { return x86_nan1((float)tanh((double)x), x); }
+__device__ __forceinline__ float lm_log(float x) { return x86_nan1((float)log((double)x), x); }
+__device__ __forceinline__ float lm_log1p(float x) { return x86_nan1((float)log1p((double)x), x); }
+__device__ __forceinline__ float lm_sin(float x) { return x86_nan1((float)sin((double)x), x); }
+__device__ __forceinline__ float lm_cos(float x) { return x86_nan1((float)cos((double)x), x); }
+
+// f32::clamp: both comparisons false for NaN, which passes through.
+__device__ __forceinline__ float clamp_rs(float v, float lo, float hi) {
+    if (v < lo) return lo;
+    if (v > hi) return hi;
+    return v;
+}
+
+template <int OP>
+__device__ __forceinline__ float unary_apply(float v, UnaryParams p) {
+    if constexpr (OP == kAbs) return f_abs(v);
+    if constexpr (OP == kSgn) return is_nan(v) ? bitsf(0x7fc00000u) : bitsf((fbits(v) & 0x80000000u) | 0x3f800000u);
+    if constexpr (OP == kNeg) return f_neg(v);
+    if constexpr (OP == kStep) return v > 0.0f ? 1.0f : 0.0f;
+    if constexpr (OP == kTanh) return lm_tanh(v);
+    if constexpr (OP == kElu) return v >= 0.0f ? v : lm_expm1(v);
+    if constexpr (OP == kRelu) return v > 0.0f ? v : 0.0f;
+    if constexpr (OP == kSigmoid) return f_div(1.0f, f_add(1.0f, lm_exp(f_neg(v))));
+    if constexpr (OP == kGelu) {
+        if (v <= -10.0f) return 0.0f;
+        if (v >= 10.0f) return v;
+        const float q = f16_bits_to_f32(f32_to_f16_bits(v));
+        const float cube = f_mul(f_mul(f_mul(0.044715f, q), q), q);
+        const float inner = f_mul(0.7978846f, f_add(q, cube));
+        const float approx = f_mul(f_mul(0.5f, q), f_add(1.0f, lm_tanh(inner)));
+        return f16_bits_to_f32(f32_to_f16_bits(approx));
+    }
+    if constexpr (OP == kGeluQuick) {
+        const float inner = f_mul(f_mul(0.7978846f, v), f_add(1.0f, f_mul(f_mul(0.044715f, v), v)));
+        return f_mul(f_mul(0.5f, v), f_add(1.0f, lm_tanh(inner)));
+    }
+    if constexpr (OP == kSilu) return f_div(v, f_add(1.0f, lm_exp(f_neg(v))));
+    if constexpr (OP == kHardswish) return f_div(f_mul(v, clamp_rs(f_add(v, 3.0f), 0.0f, 6.0f)), 6.0f);
+    if constexpr (OP == kHardsigmoid) return f_div(clamp_rs(f_add(v, 3.0f), 0.0f, 6.0f), 6.0f);
+    if constexpr (OP == kExp) return lm_exp(v);
+    if constexpr (OP == kExpm1) return lm_expm1(v);
+    if constexpr (OP == kSoftplus) return lm_log1p(lm_exp(v));
+    if constexpr (OP == kGeluErf) {
+        const float sign = v < 0.0f ? -1.0f : 1.0f;
+        const float x = f_div(f_abs(v), 1.41421356237309504880f);
+        const float t = f_div(1.0f, f_add(1.0f, f_mul(0.3275911f, x)));
+        float poly = f_sub(f_mul(1.0614054f, t), 1.4531521f);
+        poly = f_add(f_mul(poly, t), 1.4214138f);
+        poly = f_sub(f_mul(poly, t), 0.28449672f);
+        poly = f_add(f_mul(poly, t), 0.2548296f);
+        poly = f_mul(poly, t);
+        const float erf = f_mul(sign, f_sub(1.0f, f_mul(poly, lm_exp(f_mul(f_neg(x), x)))));
+        return f_mul(f_mul(0.5f, v), f_add(1.0f, erf));
+    }
+    if constexpr (OP == kFloor) return x86_nan1(floorf(v), v);
+    if constexpr (OP == kCeil) return x86_nan1(ceilf(v), v);
+    if constexpr (OP == kRound) return x86_nan1(roundf(v), v);
+    if constexpr (OP == kTrunc) return x86_nan1(truncf(v), v);
+    if constexpr (OP == kSqr) return f_mul(v, v);
+    if constexpr (OP == kSqrt) return f_sqrt(v);
+    if constexpr (OP == kLog) return lm_log(v);
+    if constexpr (OP == kSin) return lm_sin(v);
+    if constexpr (OP == kCos) return lm_cos(v);
+    if constexpr (OP == kScale) return f_mul(v, p.a);
+    if constexpr (OP == kClamp) return v < p.a ? p.a : (v > p.b ? p.b : v);
+    if constexpr (OP == kLeakyRelu) return v < 0.0f ? f_mul(v, p.a) : v;
+    if constexpr (OP == kAdd1) return f_add(v, p.a);
+    if constexpr (OP == kCopy) return v;
+    return v;
+}
+
+// ---------------------------------------------------------------------------
+// Element access for the two floating storage types.
+// ---------------------------------------------------------------------------
+template <typename T>
+struct Elem;
+
+template <>
+struct Elem<float> {
+    static __device__ __forceinline__ float load(const float* p) { return *p; }
+    static __device__ __forceinline__ void store(float* p, float v) { *p = v; }
+};
+
+template <>
+struct Elem<uint16_t> {
+    static __device__ __forceinline__ float load(const uint16_t* p) { return f16_bits_to_f32(*p); }
+    static __device__ __forceinline__ void store(uint16_t* p, float v) { *p = f32_to_f16_bits(v); }
+};
+
+// 16-byte vector of T.
+template <typename T>
+struct alignas(16) Vec16 {
+    static constexpr int N = 16 / sizeof(T);
+    T v[N];
+};
+
+template <typename T>
+__device__ __forceinline__ Vec16<T> ld_stream(const T* p) {
+    Vec16<T> r;
+    uint4 u;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(u.x), "=r"(u.y), "=r"(u.z), "=r"(u.w)
+                 : "l"(p));
+    *reinterpret_cast<uint4*>(&r) = u;
+    return r;
+}
+
+template <typename T>
+__device__ __forceinline__ Vec16<T> ld_keep(const T* p) {
+    Vec16<T> r;
+    *reinterpret_cast<uint4*>(&r) = __ldg(reinterpret_cast<const uint4*>(p));
+    return r;
+}
+
+template <typename T>
+__device__ __forceinline__ void st_stream(T* p, const Vec16<T>& v) {
+    const uint4 u = *reinterpret_cast<const uint4*>(&v);
+    asm volatile("st.global.L1::no_allocate.v4.u32 [%0], {%1,%2,%3,%4};" ::"l"(p), "r"(u.x), "r"(u.y), "r"(u.z),
+                 "r"(u.w)
+                 : "memory");
+}
+
+__device__ __forceinline__ float vget(const Vec16<float>& v, int i) { return v.v[i]; }
+__device__ __forceinline__ float vget(const Vec16<uint16_t>& v, int i) { return f16_bits_to_f32(v.v[i]); }
+__device__ __forceinline__ void vset(Vec16<float>& v, int i, float x) { v.v[i] = x; }
+__device__ __forceinline__ void vset(Vec16<uint16_t>& v, int i, float x) { v.v[i] = f32_to_f16_bits(x); }
+
+// 32-bit unsigned division by a run-time constant (round-up multiply-shift,
+// Granlund-Montgomery), used to decode logical ordinals into coordinates.
+struct FastDiv {
+    uint32_t d;
+    uint32_t mul;
+    uint32_t shift;
+};
+
+__host__ __device__ inline FastDiv make_fastdiv(uint32_t d) {
+    FastDiv f{d, 0, 0};
+    if (d <= 1) return f;
+    uint32_t s = 0;
+    while ((1ull << s) < d) ++s;
+    f.shift = s;
+    f.mul = (uint32_t)(((1ull << 32) * ((1ull << s) - d)) / d + 1);
+    return f;
+}
+
+__device__ __forceinline__ uint32_t fdiv(uint32_t n, const FastDiv& f) {
+    if (f.d == 1) return n;
+    const uint32_t t = __umulhi(n, f.mul);
+    return (t + ((n - t) >> 1)) >> (f.shift - 1);
+}
+
+}  // namespace emel

@@ -1,0 +1,277 @@
+// Elementwise kernels: unary, binary, row broadcast and repeat broadcast.
+//
+// All of them are HBM-streaming: one read of each input element, one write
+// of each output element.  Four shapes of the same loop body:
+//   ew_flat    dense operands with identical extents: a grid-stride stream
+//              of 16-byte vectors (4 x f32 / 8 x f16), two in flight per
+//              thread, loads marked no-allocate in L1;
+//   ew_rows    every operand has unit stride in dim0: "row workers" of G
+//              threads (a warp for short rows, a whole CTA for long ones)
+//              walk rows of the iteration space, 16-byte vectors within a
+//              row.  This covers row broadcast (src1 = one row), the ggml
+//              repeat broadcast and permuted / padded views whose rows are
+//              contiguous (e.g. dims 1 and 2 swapped);
+//   ew_generic arbitrary strides: one element per thread, coordinates
+//              decoded from the ordinal with 32-bit fast division;
+//   ew_ordinal equal element counts with different extents: every operand
+//              decodes the ordinal with its own extents (binary.rs:411-424).
+// Grids are sized in multiples of the SM count (148 on B200).
+#include "common.cuh"
+#include "launch.hpp"
+
+namespace emel {
+
+namespace {
+
+constexpr int kThreads = 256;
+
+template <int OP>
+struct UnaryFn {
+    UnaryParams p;
+    static constexpr bool kBinary = false;
+    __device__ __forceinline__ float operator()(float a, float) const { return unary_apply<OP>(a, p); }
+};
+
+template <int OP>
+struct BinaryFn {
+    static constexpr bool kBinary = true;
+    __device__ __forceinline__ float operator()(float a, float b) const { return binary_apply<OP>(a, b); }
+};
+
+// activation.rs:467-481, silu_back as a two-input formula: grad * silu'(x).
+struct SiluBackFn {
+    static constexpr bool kBinary = true;
+    __device__ __forceinline__ float operator()(float x, float grad) const {
+        const float sigmoid = f_div(1.0f, f_add(1.0f, lm_exp(f_neg(x))));
+        const float derivative = f_mul(sigmoid, f_add(1.0f, f_mul(x, f_sub(1.0f, sigmoid))));
+        return f_mul(grad, derivative);
+    }
+};
+
+template <typename T, typename F>
+__device__ __forceinline__ Vec16<T> apply_vec(const F& f, const Vec16<T>& a, const Vec16<T>& b) {
+    Vec16<T> r;
+#pragma unroll
+    for (int k = 0; k < Vec16<T>::N; ++k) vset(r, k, f(vget(a, k), F::kBinary ? vget(b, k) : 0.0f));
+    return r;
+}
+
+template <typename T, typename F>
+__global__ void __launch_bounds__(kThreads) ew_flat(T* __restrict__ dst, const T* __restrict__ a,
+                                                    const T* __restrict__ b, uint64_t n, F f) {
+    constexpr int N = Vec16<T>::N;
+    const uint64_t nvec = n / N;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    uint64_t i = gid;
+    for (; i + stride < nvec; i += 2 * stride) {
+        const Vec16<T> a0 = ld_stream(a + i * N);
+        const Vec16<T> a1 = ld_stream(a + (i + stride) * N);
+        Vec16<T> b0{}, b1{};
+        if constexpr (F::kBinary) {
+            b0 = ld_stream(b + i * N);
+            b1 = ld_stream(b + (i + stride) * N);
+        }
+        st_stream(dst + i * N, apply_vec<T>(f, a0, b0));
+        st_stream(dst + (i + stride) * N, apply_vec<T>(f, a1, b1));
+    }
+    if (i < nvec) {
+        const Vec16<T> a0 = ld_stream(a + i * N);
+        Vec16<T> b0{};
+        if constexpr (F::kBinary) b0 = ld_stream(b + i * N);
+        st_stream(dst + i * N, apply_vec<T>(f, a0, b0));
+    }
+    const uint64_t t = nvec * N + gid;
+    if (t < n) {
+        const float x = Elem<T>::load(a + t);
+        const float y = F::kBinary ? Elem<T>::load(b + t) : 0.0f;
+        Elem<T>::store(dst + t, f(x, y));
+    }
+}
+
+template <typename T>
+__device__ __forceinline__ T* at(const Operand& o, int64_t elems) {
+    return reinterpret_cast<T*>(o.ptr) + elems;
+}
+
+// Row workers: G = 1 << gshift threads per row.
+template <typename T, typename F>
+__global__ void __launch_bounds__(kThreads) ew_rows(EwPlan p, F f, int gshift) {
+    constexpr int N = Vec16<T>::N;
+    const uint32_t G = 1u << gshift;
+    const uint32_t lane = threadIdx.x & (G - 1);
+    const uint64_t group = ((uint64_t)blockIdx.x * blockDim.x + threadIdx.x) >> gshift;
+    const uint64_t ngroups = ((uint64_t)gridDim.x * blockDim.x) >> gshift;
+    const uint64_t ne0 = p.ne[0], ne1 = p.ne[1], ne2 = p.ne[2];
+    const uint64_t rows = p.count / ne0;
+    const bool col_bcast = F::kBinary && p.src1.ne[0] == 1;
+    for (uint64_t r = group; r < rows; r += ngroups) {
+        const uint64_t i1 = r % ne1, q = r / ne1, i2 = q % ne2, i3 = q / ne2;
+        T* drow = at<T>(p.dst, i1 * p.dst.st[1] + i2 * p.dst.st[2] + i3 * p.dst.st[3]);
+        const T* arow = at<T>(p.src0, i1 * p.src0.st[1] + i2 * p.src0.st[2] + i3 * p.src0.st[3]);
+        const T* brow = nullptr;
+        if constexpr (F::kBinary) {
+            const uint64_t j1 = p.src1_bcast ? i1 % p.src1.ne[1] : i1;
+            const uint64_t j2 = p.src1_bcast ? i2 % p.src1.ne[2] : i2;
+            const uint64_t j3 = p.src1_bcast ? i3 % p.src1.ne[3] : i3;
+            brow = at<T>(p.src1, j1 * p.src1.st[1] + j2 * p.src1.st[2] + j3 * p.src1.st[3]);
+        }
+        if (p.vec && !col_bcast) {
+            const uint64_t nv = ne0 / N;
+            for (uint64_t c = lane; c < nv; c += G) {
+                const Vec16<T> a0 = ld_stream(arow + c * N);
+                Vec16<T> b0{};
+                if constexpr (F::kBinary) b0 = ld_keep(brow + c * N);
+                st_stream(drow + c * N, apply_vec<T>(f, a0, b0));
+            }
+        } else {
+            for (uint64_t c = lane; c < ne0; c += G) {
+                const float x = Elem<T>::load(arow + c);
+                float y = 0.0f;
+                if constexpr (F::kBinary) y = Elem<T>::load(brow + (col_bcast ? 0 : (int64_t)(c % p.src1.ne[0]) * p.src1.st[0]));
+                Elem<T>::store(drow + c, f(x, y));
+            }
+        }
+    }
+}
+
+template <typename T, typename F>
+__global__ void __launch_bounds__(kThreads) ew_generic(EwPlan p, F f, FastDiv d0, FastDiv d1, FastDiv d2) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < p.count; i += stride) {
+        const uint32_t o = (uint32_t)i;
+        const uint32_t q0 = fdiv(o, d0), c0 = o - q0 * d0.d;
+        const uint32_t q1 = fdiv(q0, d1), c1 = q0 - q1 * d1.d;
+        const uint32_t c3 = fdiv(q1, d2), c2 = q1 - c3 * d2.d;
+        const uint32_t c[4] = {c0, c1, c2, c3};
+        int64_t od = 0, oa = 0, ob = 0;
+#pragma unroll
+        for (int d = 0; d < 4; ++d) {
+            od += (int64_t)c[d] * p.dst.st[d];
+            oa += (int64_t)c[d] * p.src0.st[d];
+            if constexpr (F::kBinary) ob += (int64_t)(p.src1_bcast ? c[d] % p.src1.ne[d] : c[d]) * p.src1.st[d];
+        }
+        const float x = Elem<T>::load(at<T>(p.src0, oa));
+        const float y = F::kBinary ? Elem<T>::load(at<T>(p.src1, ob)) : 0.0f;
+        Elem<T>::store(at<T>(p.dst, od), f(x, y));
+    }
+}
+
+__device__ __forceinline__ int64_t ordinal_elems(const Operand& o, uint64_t ordinal) {
+    int64_t off = 0;
+#pragma unroll
+    for (int d = 0; d < 4; ++d) {
+        off += (int64_t)(ordinal % o.ne[d]) * o.st[d];
+        ordinal /= o.ne[d];
+    }
+    return off;
+}
+
+// src1 of a repeat broadcast: decode with the iteration extents, wrap each
+// coordinate into src1's extents (generic.rs:1652-1660).
+__device__ __forceinline__ int64_t repeat_elems(const EwPlan& p, uint64_t ordinal) {
+    int64_t off = 0;
+#pragma unroll
+    for (int d = 0; d < 4; ++d) {
+        off += (int64_t)((ordinal % p.ne[d]) % p.src1.ne[d]) * p.src1.st[d];
+        ordinal /= p.ne[d];
+    }
+    return off;
+}
+
+template <typename T, typename F>
+__global__ void __launch_bounds__(kThreads) ew_ordinal(EwPlan p, F f) {
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < p.count; i += stride) {
+        const float x = Elem<T>::load(at<T>(p.src0, ordinal_elems(p.src0, i)));
+        float y = 0.0f;
+        if constexpr (F::kBinary)
+            y = Elem<T>::load(at<T>(p.src1, p.src1_bcast ? repeat_elems(p, i) : ordinal_elems(p.src1, i)));
+        Elem<T>::store(at<T>(p.dst, ordinal_elems(p.dst, i)), f(x, y));
+    }
+}
+
+uint32_t grid_for(const LaunchEnv& env, uint64_t work_items, int per_thread) {
+    const uint64_t want = (work_items + (uint64_t)kThreads * per_thread - 1) / ((uint64_t)kThreads * per_thread);
+    const uint64_t cap = (uint64_t)env.sm_count * 8;  // 8 x 256 threads = 2048 resident threads per SM
+    uint64_t g = want < cap ? want : cap;
+    return (uint32_t)(g == 0 ? 1 : g);
+}
+
+template <typename T, typename F>
+cudaError_t launch_ew(const LaunchEnv& env, const EwPlan& p, const F& f) {
+    switch (p.kind) {
+    case EwKind::Flat: {
+        const uint64_t nvec = p.count / Vec16<T>::N;
+        ew_flat<T, F><<<grid_for(env, nvec, 2), kThreads, 0, env.stream>>>(
+            reinterpret_cast<T*>(p.dst.ptr), reinterpret_cast<const T*>(p.src0.ptr),
+            reinterpret_cast<const T*>(p.src1.ptr), p.count, f);
+        break;
+    }
+    case EwKind::Rows: {
+        const uint64_t per_row = p.vec ? p.ne[0] / Vec16<T>::N : p.ne[0];
+        int gshift = 5;
+        while (gshift < 8 && (1ull << gshift) < per_row) ++gshift;
+        const uint64_t rows = p.count / p.ne[0];
+        const uint64_t threads = rows << gshift;
+        ew_rows<T, F><<<grid_for(env, threads, 1), kThreads, 0, env.stream>>>(p, f, gshift);
+        break;
+    }
+    case EwKind::Generic: {
+        ew_generic<T, F><<<grid_for(env, p.count, 1), kThreads, 0, env.stream>>>(
+            p, f, make_fastdiv((uint32_t)p.ne[0]), make_fastdiv((uint32_t)p.ne[1]), make_fastdiv((uint32_t)p.ne[2]));
+        break;
+    }
+    case EwKind::Ordinal:
+        ew_ordinal<T, F><<<grid_for(env, p.count, 1), kThreads, 0, env.stream>>>(p, f);
+        break;
+    }
+    ++*env.launches;
+    return cudaGetLastError();
+}
+
+template <int OP>
+cudaError_t unary_typed(const LaunchEnv& env, const EwPlan& p, float pa, float pb) {
+    UnaryFn<OP> f{UnaryParams{pa, pb}};
+    if (p.dtype == DType::F16) return launch_ew<uint16_t>(env, p, f);
+    return launch_ew<float>(env, p, f);
+}
+
+template <int OP>
+cudaError_t binary_typed(const LaunchEnv& env, const EwPlan& p) {
+    BinaryFn<OP> f;
+    if (p.dtype == DType::F16) return launch_ew<uint16_t>(env, p, f);
+    return launch_ew<float>(env, p, f);
+}
+
+}  // namespace
+
+cudaError_t launch_unary(const LaunchEnv& env, const EwPlan& p, int op, float pa, float pb) {
+    switch (op) {
+#define EMEL_UNARY_CASE(code) \
+    case code: return unary_typed<code>(env, p, pa, pb);
+        EMEL_UNARY_CASE(kAbs) EMEL_UNARY_CASE(kSgn) EMEL_UNARY_CASE(kNeg) EMEL_UNARY_CASE(kStep)
+        EMEL_UNARY_CASE(kTanh) EMEL_UNARY_CASE(kElu) EMEL_UNARY_CASE(kRelu) EMEL_UNARY_CASE(kSigmoid)
+        EMEL_UNARY_CASE(kGelu) EMEL_UNARY_CASE(kGeluQuick) EMEL_UNARY_CASE(kSilu) EMEL_UNARY_CASE(kHardswish)
+        EMEL_UNARY_CASE(kHardsigmoid) EMEL_UNARY_CASE(kExp) EMEL_UNARY_CASE(kExpm1) EMEL_UNARY_CASE(kSoftplus)
+        EMEL_UNARY_CASE(kGeluErf) EMEL_UNARY_CASE(kFloor) EMEL_UNARY_CASE(kCeil) EMEL_UNARY_CASE(kRound)
+        EMEL_UNARY_CASE(kTrunc) EMEL_UNARY_CASE(kSqr) EMEL_UNARY_CASE(kSqrt) EMEL_UNARY_CASE(kLog)
+        EMEL_UNARY_CASE(kSin) EMEL_UNARY_CASE(kCos) EMEL_UNARY_CASE(kScale) EMEL_UNARY_CASE(kClamp)
+        EMEL_UNARY_CASE(kLeakyRelu) EMEL_UNARY_CASE(kAdd1) EMEL_UNARY_CASE(kCopy)
+#undef EMEL_UNARY_CASE
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+cudaError_t launch_binary(const LaunchEnv& env, const EwPlan& p, int op) {
+    switch (op) {
+    case kAdd: return binary_typed<kAdd>(env, p);
+    case kSub: return binary_typed<kSub>(env, p);
+    case kMul: return binary_typed<kMul>(env, p);
+    case kDiv: return binary_typed<kDiv>(env, p);
+    case kSiluBack: return launch_ew<float>(env, p, SiluBackFn{});
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+}  // namespace emel

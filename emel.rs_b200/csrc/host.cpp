@@ -1,0 +1,815 @@
+// Host side of the device op table: context, memory and stream handles,
+// view validation in the reference's guard order, dimension
+// canonicalisation and launch planning, and the extern "C" entry points
+// declared in include/emel_cuda.h.
+//
+// Validation mirrors crates/emel-kernels/src/any/tensor_view.rs:259-447 and
+// the per-family guards it cites.  It touches no device memory and makes no
+// CUDA call, so a rejected request returns before the context or stream is
+// even looked at and never writes its destination.
+#include <cmath>
+#include <cstdio>
+#include <cstring>
+#include <new>
+
+#include <cuda_runtime.h>
+
+#include "emel_cuda.h"
+#include "launch.hpp"
+
+struct emel_cuda_context {
+    int device;
+    int sm_count;
+    void* workspace;
+    uint64_t workspace_bytes;
+    uint64_t launches;
+    char last_error[256];
+};
+
+namespace {
+
+using emel::DType;
+using u128 = unsigned __int128;
+
+uint64_t dtype_size(uint32_t dtype) {
+    switch (dtype) {
+    case EMEL_DTYPE_F32: return 4;
+    case EMEL_DTYPE_F16: return 2;
+    case EMEL_DTYPE_I32: return 4;
+    case EMEL_DTYPE_I64: return 8;
+    default: return 0;
+    }
+}
+
+// A validated view: element count and effective byte strides.
+struct Checked {
+    uint64_t count = 0;
+    uint64_t nb[4] = {0, 0, 0, 0};
+    uint64_t elem = 0;
+};
+
+// Layout::element_count (tensor_view.rs:346-358).
+bool count_of(const emel_tensor_view& v, uint64_t* out) {
+    uint64_t n = 1;
+    for (int d = 0; d < 4; ++d) {
+        if (v.ne[d] == 0 || __builtin_mul_overflow(n, v.ne[d], &n)) return false;
+    }
+    *out = n;
+    return true;
+}
+
+// Layout::effective_f32_strides (tensor_view.rs:262-277) for any element size.
+bool strides_of(const emel_tensor_view& v, uint64_t elem, uint64_t out[4]) {
+    if (v.nb[0] != 0) {
+        for (int d = 0; d < 4; ++d) out[d] = v.nb[d];
+        return true;
+    }
+    out[0] = elem;
+    for (int d = 1; d < 4; ++d)
+        if (__builtin_mul_overflow(out[d - 1], v.ne[d - 1], &out[d])) return false;
+    return true;
+}
+
+// The device pointer must be able to stand in for the reference's slice:
+// non-null and aligned to the element type.
+bool addressable(const emel_tensor_view& v, uint64_t elem) {
+    return v.data != nullptr && reinterpret_cast<uintptr_t>(v.data) % elem == 0;
+}
+
+// Layout::validate_element_storage (tensor_view.rs:392-447).
+bool validate_as(const emel_tensor_view* v, uint32_t dtype, bool singleton_zero_ok, Checked* out) {
+    if (v == nullptr || v->dtype != dtype) return false;
+    const uint64_t elem = dtype_size(dtype);
+    Checked c;
+    c.elem = elem;
+    if (!count_of(*v, &c.count) || !strides_of(*v, elem, c.nb)) return false;
+    for (int d = 0; d < 4; ++d) {
+        const bool zero_ok = singleton_zero_ok && v->ne[d] == 1 && c.nb[d] == 0;
+        if (!zero_ok && (c.nb[d] < elem || c.nb[d] % elem != 0)) return false;
+    }
+    u128 span = 0;
+    for (int d = 0; d < 4; ++d) span += (u128)(v->ne[d] - 1) * (u128)c.nb[d];
+    if (span + elem > (u128)v->storage_bytes) return false;
+    if (!addressable(*v, elem)) return false;
+    if (out) *out = c;
+    return true;
+}
+
+// F32 views always; F16 views as this device table's extension.
+bool validate_float(const emel_tensor_view* v, bool singleton_zero_ok, Checked* out) {
+    if (v == nullptr || (v->dtype != EMEL_DTYPE_F32 && v->dtype != EMEL_DTYPE_F16)) return false;
+    return validate_as(v, v->dtype, singleton_zero_ok, out);
+}
+
+// normalization_view_valid (normalization.rs:237-287).
+bool normalization_valid(const emel_tensor_view* v, Checked* out) {
+    if (v == nullptr || v->dtype != EMEL_DTYPE_F32 || v->ne[0] == 0) return false;
+    if (v->nb[0] != 0) {
+        if (v->nb[0] < 4 || v->nb[0] % 4 != 0) return false;
+        for (int d = 0; d < 4; ++d)
+            if (v->ne[d] > 1 && v->nb[d] == 0) return false;
+    }
+    return validate_as(v, EMEL_DTYPE_F32, false, out);
+}
+
+bool same_ne(const emel_tensor_view* a, const emel_tensor_view* b) {
+    return std::memcmp(a->ne, b->ne, sizeof(a->ne)) == 0;
+}
+
+// Layout::is_dense_contiguous_for (tensor_view.rs:297-314) on effective strides.
+bool dense(const emel_tensor_view& v, const Checked& c) {
+    uint64_t expect = c.elem;
+    for (int d = 0; d < 4; ++d) {
+        if (c.nb[d] != expect) return false;
+        expect *= v.ne[d];
+    }
+    return true;
+}
+
+bool aligned16(const void* p) { return reinterpret_cast<uintptr_t>(p) % 16 == 0; }
+
+emel::Operand operand(const emel_tensor_view* v, const Checked& c) {
+    emel::Operand o{};
+    o.ptr = static_cast<char*>(v->data);
+    for (int d = 0; d < 4; ++d) {
+        o.st[d] = (int64_t)(c.nb[d] / c.elem);
+        o.ne[d] = v->ne[d];
+    }
+    return o;
+}
+
+// ---------------------------------------------------------------------------
+// Elementwise planning.
+// ---------------------------------------------------------------------------
+
+// Shared-extent plan: drop singleton dimensions, merge neighbours that every
+// operand stores contiguously, then pick the kernel shape.
+emel::EwPlan plan_shared(DType dt, const uint64_t ne_in[4], emel::Operand* ops[3], int nops, bool src1_bcast) {
+    emel::EwPlan p{};
+    p.dtype = dt;
+    uint64_t ne[4];
+    int64_t st[3][4];
+    uint64_t bne[4];  // src1 extents along the kept dims (broadcast plans)
+    int k = 0;
+    for (int d = 0; d < 4; ++d) {
+        if (ne_in[d] == 1) continue;
+        ne[k] = ne_in[d];
+        bne[k] = src1_bcast ? ops[2]->ne[d] : ne_in[d];
+        for (int o = 0; o < nops; ++o) st[o][k] = ops[o]->st[d];
+        ++k;
+    }
+    if (k == 0) {
+        ne[0] = 1;
+        bne[0] = 1;
+        for (int o = 0; o < nops; ++o) st[o][0] = 1;
+        k = 1;
+    }
+    // merge d+1 into d when every operand (and the broadcast pattern) allows it
+    int m = 0;
+    for (int d = 1; d < k; ++d) {
+        bool ok = true;
+        for (int o = 0; o < nops; ++o)
+            if (st[o][d] != st[o][m] * (int64_t)ne[m]) ok = false;
+        if (src1_bcast && !(bne[m] == ne[m] && bne[d] == ne[d])) ok = false;
+        if (ok) {
+            ne[m] *= ne[d];
+            bne[m] *= bne[d];
+        } else {
+            ++m;
+            ne[m] = ne[d];
+            bne[m] = bne[d];
+            for (int o = 0; o < nops; ++o) st[o][m] = st[o][d];
+        }
+    }
+    k = m + 1;
+    for (int d = k; d < 4; ++d) {
+        ne[d] = 1;
+        bne[d] = 1;
+        for (int o = 0; o < nops; ++o) st[o][d] = 0;
+    }
+    p.ndim = k;
+    p.count = 1;
+    for (int d = 0; d < 4; ++d) {
+        p.ne[d] = ne[d];
+        p.count *= ne[d];
+    }
+    emel::Operand* outs[3] = {&p.dst, &p.src0, &p.src1};
+    for (int o = 0; o < nops; ++o) {
+        outs[o]->ptr = ops[o]->ptr;
+        for (int d = 0; d < 4; ++d) {
+            outs[o]->st[d] = st[o][d];
+            outs[o]->ne[d] = (o == 2) ? bne[d] : ne[d];
+        }
+    }
+    p.src1_bcast = false;
+    if (nops == 3 && src1_bcast)
+        for (int d = 0; d < 4; ++d)
+            if (bne[d] != ne[d]) p.src1_bcast = true;
+    const int N = dt == DType::F16 ? 8 : 4;
+    // dim0 unit stride for dst and src0, and for src1 unless it repeats one
+    // column across the row
+    bool unit0 = st[0][0] == 1 && st[1][0] == 1;
+    if (nops == 3 && !(p.src1_bcast && bne[0] == 1) && st[2][0] != 1) unit0 = false;
+    bool all_aligned = true;
+    for (int o = 0; o < nops; ++o)
+        if (!aligned16(ops[o]->ptr)) all_aligned = false;
+    if (k == 1 && unit0 && !p.src1_bcast) {
+        p.kind = emel::EwKind::Flat;
+        p.vec = all_aligned;
+        if (!all_aligned) p.kind = emel::EwKind::Generic;
+    } else if (unit0) {
+        p.kind = emel::EwKind::Rows;
+        bool v = all_aligned && ne[0] % N == 0 && (!p.src1_bcast || bne[0] == ne[0]);
+        for (int o = 0; o < nops; ++o)
+            for (int d = 1; d < 4; ++d)
+                if (st[o][d] % N != 0) v = false;
+        p.vec = v;
+    } else {
+        p.kind = emel::EwKind::Generic;
+    }
+    if (p.kind == emel::EwKind::Generic) {
+        bool small = p.count < (1ull << 32);
+        for (int d = 0; d < 4; ++d)
+            if (ne[d] > (1ull << 31)) small = false;
+        if (!small) {
+            // 64-bit ordinal decode: give every operand the iteration extents
+            p.kind = emel::EwKind::Ordinal;
+        }
+    }
+    return p;
+}
+
+// Equal-count plan where operands may have different extents.
+emel::EwPlan plan_equal_count(DType dt, const emel_tensor_view* views[3], const Checked* cs[3], int nops) {
+    emel::Operand ops[3];
+    emel::Operand* pops[3];
+    for (int o = 0; o < nops; ++o) {
+        ops[o] = operand(views[o], *cs[o]);
+        pops[o] = &ops[o];
+    }
+    bool shared = true;
+    for (int o = 1; o < nops; ++o)
+        if (!same_ne(views[0], views[o])) shared = false;
+    if (shared) return plan_shared(dt, views[0]->ne, pops, nops, false);
+    bool all_dense = true;
+    for (int o = 0; o < nops; ++o)
+        if (!dense(*views[o], *cs[o])) all_dense = false;
+    if (all_dense) {
+        // identical ordinal -> offset maps: stream them as one run
+        uint64_t flat_ne[4] = {cs[0]->count, 1, 1, 1};
+        for (int o = 0; o < nops; ++o) {
+            ops[o].st[0] = 1;
+            ops[o].st[1] = ops[o].st[2] = ops[o].st[3] = 0;
+            ops[o].ne[0] = cs[0]->count;
+            ops[o].ne[1] = ops[o].ne[2] = ops[o].ne[3] = 1;
+        }
+        return plan_shared(dt, flat_ne, pops, nops, false);
+    }
+    emel::EwPlan p{};
+    p.dtype = dt;
+    p.kind = emel::EwKind::Ordinal;
+    p.count = cs[0]->count;
+    p.ndim = 4;
+    for (int d = 0; d < 4; ++d) p.ne[d] = views[0]->ne[d];
+    emel::Operand* outs[3] = {&p.dst, &p.src0, &p.src1};
+    for (int o = 0; o < nops; ++o) *outs[o] = ops[o];
+    return p;
+}
+
+// ---------------------------------------------------------------------------
+// Row planning.
+// ---------------------------------------------------------------------------
+emel::RowOperand row_operand(const emel_tensor_view* v, const Checked& c) {
+    emel::RowOperand o{};
+    o.ptr = static_cast<char*>(v->data);
+    for (int d = 0; d < 4; ++d) {
+        o.st[d] = (int64_t)(c.nb[d] / c.elem);
+        o.ne[d] = v->ne[d];
+    }
+    return o;
+}
+
+bool row_vec_ok(const emel::RowOperand& o) {
+    return o.st[0] == 1 && aligned16(o.ptr) && o.st[1] % 4 == 0 && o.st[2] % 4 == 0 && o.st[3] % 4 == 0;
+}
+
+emel::RowPlan plan_rows(const emel_tensor_view* src, const Checked& cs, const emel_tensor_view* dst,
+                        const Checked* cd) {
+    emel::RowPlan p{};
+    for (int d = 0; d < 4; ++d) p.ne[d] = src->ne[d];
+    p.rows = cs.count / src->ne[0];
+    p.src = row_operand(src, cs);
+    if (dst) p.dst = row_operand(dst, *cd);
+    p.contiguous_rows = p.src.st[0] == 1 && (!dst || p.dst.st[0] == 1);
+    p.vec = p.ne[0] % 4 == 0 && row_vec_ok(p.src) && (!dst || row_vec_ok(p.dst));
+    p.flat = dense(*src, cs) && aligned16(src->data);
+    p.dense = false;
+    p.dst_ordinal = false;
+    return p;
+}
+
+// ---------------------------------------------------------------------------
+// Status helpers.
+// ---------------------------------------------------------------------------
+emel_cuda_status device_status(emel_cuda_context* ctx, cudaError_t err) {
+    if (err == cudaSuccess) return EMEL_CUDA_OK;
+    std::snprintf(ctx->last_error, sizeof(ctx->last_error), "%s: %s", cudaGetErrorName(err), cudaGetErrorString(err));
+    return err == cudaErrorMemoryAllocation ? EMEL_CUDA_OUT_OF_MEMORY : EMEL_CUDA_DEVICE_ERROR;
+}
+
+emel::LaunchEnv env_of(emel_cuda_context* ctx, void* stream) {
+    emel::LaunchEnv e{};
+    e.stream = static_cast<cudaStream_t>(stream);
+    e.sm_count = ctx->sm_count;
+    e.device = ctx->device;
+    e.launches = &ctx->launches;
+    e.workspace = ctx->workspace;
+    e.workspace_bytes = ctx->workspace_bytes;
+    return e;
+}
+
+// Every launch targets the context's device.
+cudaError_t select_device(emel_cuda_context* ctx) {
+    int cur = -1;
+    cudaError_t err = cudaGetDevice(&cur);
+    if (err != cudaSuccess) return err;
+    return cur == ctx->device ? cudaSuccess : cudaSetDevice(ctx->device);
+}
+
+emel_cuda_status run_unary_plan(emel_cuda_context* ctx, void* stream, const emel::EwPlan& plan, int op, float a,
+                                float b) {
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = emel::launch_unary(env_of(ctx, stream), plan, op, a, b);
+    return device_status(ctx, err);
+}
+
+bool unary_op_known(int op) {
+    return (op >= EMEL_UNARY_ABS && op <= EMEL_UNARY_TRUNC && op != EMEL_UNARY_XIELU) ||
+           (op >= EMEL_UNARY_SQR && op <= EMEL_UNARY_COS);
+}
+
+DType dt_of(uint32_t code) { return code == EMEL_DTYPE_F16 ? DType::F16 : DType::F32; }
+
+// Single-input, same-extent ops over F32 views (activation.rs:327-333,
+// elementwise.rs:219-225, tensor_view.rs:1096-1110).
+emel_cuda_status same_shape_unary(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                  const emel_tensor_view* dst, int op, float a, float b) {
+    Checked cs, cd;
+    if (!validate_as(src, EMEL_DTYPE_F32, false, &cs) || !validate_as(dst, EMEL_DTYPE_F32, false, &cd))
+        return EMEL_CUDA_INVALID_VIEW;
+    if (!same_ne(src, dst)) return EMEL_CUDA_SHAPE_MISMATCH;
+    const emel_tensor_view* views[3] = {dst, src, nullptr};
+    const Checked* cks[3] = {&cd, &cs, nullptr};
+    return run_unary_plan(ctx, stream, plan_equal_count(DType::F32, views, cks, 2), op, a, b);
+}
+
+}  // namespace
+
+// ===========================================================================
+// extern "C" entry points
+// ===========================================================================
+extern "C" {
+
+emel_cuda_status emel_cuda_context_create(int device, emel_cuda_context** out) {
+    if (out == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    *out = nullptr;
+    auto* ctx = new (std::nothrow) emel_cuda_context();
+    if (ctx == nullptr) return EMEL_CUDA_OUT_OF_MEMORY;
+    ctx->device = device;
+    ctx->last_error[0] = '\0';
+    cudaError_t err = cudaSetDevice(device);
+    if (err == cudaSuccess) err = cudaDeviceGetAttribute(&ctx->sm_count, cudaDevAttrMultiProcessorCount, device);
+    if (err == cudaSuccess) {
+        ctx->workspace_bytes = emel::reduction_workspace_bytes(ctx->sm_count);
+        err = cudaMalloc(&ctx->workspace, ctx->workspace_bytes);
+    }
+    if (err == cudaSuccess) err = cudaMemset(ctx->workspace, 0, ctx->workspace_bytes);
+    if (err == cudaSuccess) err = cudaDeviceSynchronize();
+    if (err != cudaSuccess) {
+        emel_cuda_status st = device_status(ctx, err);
+        if (ctx->workspace) cudaFree(ctx->workspace);
+        delete ctx;
+        return st;
+    }
+    *out = ctx;
+    return EMEL_CUDA_OK;
+}
+
+emel_cuda_status emel_cuda_context_destroy(emel_cuda_context* ctx) {
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess && ctx->workspace) err = cudaFree(ctx->workspace);
+    delete ctx;
+    return err == cudaSuccess ? EMEL_CUDA_OK : EMEL_CUDA_DEVICE_ERROR;
+}
+
+const char* emel_cuda_context_last_error(const emel_cuda_context* ctx) {
+    return ctx ? ctx->last_error : "null context";
+}
+
+uint64_t emel_cuda_launch_count(const emel_cuda_context* ctx) { return ctx ? ctx->launches : 0; }
+
+emel_cuda_status emel_cuda_malloc(emel_cuda_context* ctx, uint64_t bytes, void** out) {
+    if (ctx == nullptr || out == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = cudaMalloc(out, bytes);
+    return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_free(emel_cuda_context* ctx, void* ptr) {
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = cudaFree(ptr);
+    return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_memcpy_h2d(emel_cuda_context* ctx, void* stream, void* dst, const void* src,
+                                      uint64_t bytes) {
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, (cudaStream_t)stream);
+    return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_memcpy_d2h(emel_cuda_context* ctx, void* stream, void* dst, const void* src,
+                                      uint64_t bytes) {
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, (cudaStream_t)stream);
+    return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_memset(emel_cuda_context* ctx, void* stream, void* dst, int value, uint64_t bytes) {
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = cudaMemsetAsync(dst, value, bytes, (cudaStream_t)stream);
+    return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_stream_create(emel_cuda_context* ctx, void** out) {
+    if (ctx == nullptr || out == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    cudaError_t err = select_device(ctx);
+    cudaStream_t s = nullptr;
+    if (err == cudaSuccess) err = cudaStreamCreateWithFlags(&s, cudaStreamNonBlocking);
+    *out = s;
+    return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_stream_destroy(emel_cuda_context* ctx, void* stream) {
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    return device_status(ctx, cudaStreamDestroy((cudaStream_t)stream));
+}
+
+emel_cuda_status emel_cuda_stream_synchronize(emel_cuda_context* ctx, void* stream) {
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    return device_status(ctx, cudaStreamSynchronize((cudaStream_t)stream));
+}
+
+// ---- binary family ---------------------------------------------------------
+
+emel_cuda_status emel_cuda_binary(emel_cuda_context* ctx, void* stream, int op, const emel_tensor_view* lhs,
+                                  const emel_tensor_view* rhs, const emel_tensor_view* dst) {
+    if (op < EMEL_BINARY_ADD || op > EMEL_BINARY_DIV) return EMEL_CUDA_UNEXPECTED_EVENT;
+    Checked cl, cr, cd;
+    // binary.rs:336-345: all three views under the singleton-zero-stride contract
+    if (!validate_float(lhs, true, &cl) || !validate_float(rhs, true, &cr) || !validate_float(dst, true, &cd) ||
+        lhs->dtype != rhs->dtype || lhs->dtype != dst->dtype)
+        return EMEL_CUDA_INVALID_VIEW;
+    // binary.rs:347-354: equal logical element counts
+    if (cl.count != cr.count || cl.count != cd.count) return EMEL_CUDA_SHAPE_MISMATCH;
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    const emel_tensor_view* views[3] = {dst, lhs, rhs};
+    const Checked* cks[3] = {&cd, &cl, &cr};
+    const emel::EwPlan plan = plan_equal_count(dt_of(dst->dtype), views, cks, 3);
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = emel::launch_binary(env_of(ctx, stream), plan, op);
+    return device_status(ctx, err);
+}
+
+static emel_cuda_status broadcast_common(emel_cuda_context* ctx, void* stream, int op, const emel_tensor_view* src0,
+                                         const emel_tensor_view* src1, const emel_tensor_view* dst, bool row_contract) {
+    if (op < EMEL_BINARY_ADD || op > EMEL_BINARY_DIV) return EMEL_CUDA_UNEXPECTED_EVENT;
+    Checked c0, c1, cd;
+    if (!validate_float(src0, true, &c0) || !validate_float(src1, true, &c1) || !validate_float(dst, true, &cd) ||
+        src0->dtype != src1->dtype || src0->dtype != dst->dtype)
+        return EMEL_CUDA_INVALID_VIEW;
+    if (row_contract) {
+        // broadcast.rs:334-350
+        const bool ok = same_ne(src0, dst) && dst->ne[0] > 0 && src1->ne[0] == dst->ne[0] && src1->ne[1] == 1 &&
+                        src1->ne[2] == 1 && src1->ne[3] == 1 && dst->ne[1] > 0 && cd.count > c1.count;
+        if (!ok) return EMEL_CUDA_SHAPE_MISMATCH;
+    } else {
+        // ggml repeat contract: src0 and dst share extents; src1 extents divide them
+        if (!same_ne(src0, dst)) return EMEL_CUDA_SHAPE_MISMATCH;
+        for (int d = 0; d < 4; ++d)
+            if (dst->ne[d] % src1->ne[d] != 0) return EMEL_CUDA_SHAPE_MISMATCH;
+    }
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    emel::Operand ops[3] = {operand(dst, cd), operand(src0, c0), operand(src1, c1)};
+    emel::Operand* pops[3] = {&ops[0], &ops[1], &ops[2]};
+    const bool bcast = !same_ne(src1, dst);
+    const emel::EwPlan plan = plan_shared(dt_of(dst->dtype), dst->ne, pops, 3, bcast);
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = emel::launch_binary(env_of(ctx, stream), plan, op);
+    return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_broadcast_row(emel_cuda_context* ctx, void* stream, int op, const emel_tensor_view* src0,
+                                         const emel_tensor_view* src1, const emel_tensor_view* dst) {
+    return broadcast_common(ctx, stream, op, src0, src1, dst, true);
+}
+
+emel_cuda_status emel_cuda_binary_repeat(emel_cuda_context* ctx, void* stream, int op, const emel_tensor_view* src0,
+                                         const emel_tensor_view* src1, const emel_tensor_view* dst) {
+    return broadcast_common(ctx, stream, op, src0, src1, dst, false);
+}
+
+// ---- unary family ------------------------------------------------------------
+
+emel_cuda_status emel_cuda_unary(emel_cuda_context* ctx, void* stream, int op, const emel_tensor_view* src,
+                                 const emel_tensor_view* dst) {
+    if (!unary_op_known(op)) return EMEL_CUDA_UNEXPECTED_EVENT;
+    Checked cs, cd;
+    // unary.rs:455-461
+    if (!validate_float(src, false, &cs) || !validate_float(dst, false, &cd) || src->dtype != dst->dtype)
+        return EMEL_CUDA_INVALID_VIEW;
+    if (cs.count != cd.count) return EMEL_CUDA_SHAPE_MISMATCH;
+    const emel_tensor_view* views[3] = {dst, src, nullptr};
+    const Checked* cks[3] = {&cd, &cs, nullptr};
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    return run_unary_plan(ctx, stream, plan_equal_count(dt_of(dst->dtype), views, cks, 2), op, 0.0f, 0.0f);
+}
+
+emel_cuda_status emel_cuda_op_unary(emel_cuda_context* ctx, void* stream, int subop, const emel_tensor_view* src,
+                                    const emel_tensor_view* dst) {
+    // unary.rs:942-1027: eight accepted subops; any failure is UnexpectedEvent
+    const bool accepted = subop == EMEL_UNARY_ABS || subop == EMEL_UNARY_NEG || subop == EMEL_UNARY_TANH ||
+                          subop == EMEL_UNARY_ELU || subop == EMEL_UNARY_RELU || subop == EMEL_UNARY_GELU ||
+                          subop == EMEL_UNARY_SILU || subop == EMEL_UNARY_EXP;
+    Checked cs, cd;
+    if (!accepted || !validate_as(src, EMEL_DTYPE_F32, false, &cs) || !validate_as(dst, EMEL_DTYPE_F32, false, &cd) ||
+        cs.count != cd.count)
+        return EMEL_CUDA_UNEXPECTED_EVENT;
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    const emel_tensor_view* views[3] = {dst, src, nullptr};
+    const Checked* cks[3] = {&cd, &cs, nullptr};
+    return run_unary_plan(ctx, stream, plan_equal_count(DType::F32, views, cks, 2), subop, 0.0f, 0.0f);
+}
+
+emel_cuda_status emel_cuda_scale(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                 const emel_tensor_view* dst, float scale) {
+    return same_shape_unary(ctx, stream, src, dst, emel::kScale, scale, 0.0f);
+}
+
+emel_cuda_status emel_cuda_clamp(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                 const emel_tensor_view* dst, float min, float max) {
+    return same_shape_unary(ctx, stream, src, dst, emel::kClamp, min, max);
+}
+
+emel_cuda_status emel_cuda_leaky_relu(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                      const emel_tensor_view* dst, float negative_slope) {
+    return same_shape_unary(ctx, stream, src, dst, emel::kLeakyRelu, negative_slope, 0.0f);
+}
+
+emel_cuda_status emel_cuda_add1(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                const emel_tensor_view* dst, float scalar) {
+    return same_shape_unary(ctx, stream, src, dst, emel::kAdd1, scalar, 0.0f);
+}
+
+emel_cuda_status emel_cuda_copy(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                const emel_tensor_view* dst) {
+    return same_shape_unary(ctx, stream, src, dst, emel::kCopy, 0.0f, 0.0f);
+}
+
+emel_cuda_status emel_cuda_silu_back(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                     const emel_tensor_view* grad, const emel_tensor_view* dst) {
+    Checked cs, cg, cd;
+    // activation.rs:335-349
+    if (!validate_as(src, EMEL_DTYPE_F32, false, &cs) || !validate_as(grad, EMEL_DTYPE_F32, false, &cg) ||
+        !validate_as(dst, EMEL_DTYPE_F32, false, &cd))
+        return EMEL_CUDA_INVALID_VIEW;
+    if (!same_ne(src, grad) || !same_ne(src, dst)) return EMEL_CUDA_SHAPE_MISMATCH;
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    const emel_tensor_view* views[3] = {dst, src, grad};
+    const Checked* cks[3] = {&cd, &cs, &cg};
+    const emel::EwPlan plan = plan_equal_count(DType::F32, views, cks, 3);
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = emel::launch_binary(env_of(ctx, stream), plan, emel::kSiluBack);
+    return device_status(ctx, err);
+}
+
+// ---- row normalisation --------------------------------------------------------
+
+static emel_cuda_status norm_common(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                    const emel_tensor_view* weight, const emel_tensor_view* dst, float eps, int op) {
+    Checked cs, cd, cw;
+    // normalization.rs:364-382: view -> shape -> parameters
+    if (!normalization_valid(src, &cs) || !normalization_valid(dst, &cd)) return EMEL_CUDA_INVALID_VIEW;
+    if (op == 2 && !validate_as(weight, EMEL_DTYPE_F32, true, &cw)) return EMEL_CUDA_INVALID_VIEW;
+    if (!same_ne(src, dst)) return EMEL_CUDA_SHAPE_MISMATCH;
+    if (op == 2 && !(weight->ne[0] == src->ne[0] && weight->ne[1] == 1 && weight->ne[2] == 1 && weight->ne[3] == 1))
+        return EMEL_CUDA_SHAPE_MISMATCH;
+    if (!(std::isfinite(eps) && eps >= 0.0f)) return EMEL_CUDA_INVALID_PARAMETERS;
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    emel::RowPlan p = plan_rows(src, cs, dst, &cd);
+    if (op == 2) {
+        p.aux = row_operand(weight, cw);
+        p.has_aux = true;
+        p.aux_dtype = (int)DType::F32;
+    }
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = emel::launch_norm(env_of(ctx, stream), p, op, eps);
+    return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_norm(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                const emel_tensor_view* dst, float eps) {
+    return norm_common(ctx, stream, src, nullptr, dst, eps, 0);
+}
+
+emel_cuda_status emel_cuda_rms_norm(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                    const emel_tensor_view* dst, float eps) {
+    return norm_common(ctx, stream, src, nullptr, dst, eps, 1);
+}
+
+emel_cuda_status emel_cuda_rms_norm_mul(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                        const emel_tensor_view* weight, const emel_tensor_view* dst, float eps) {
+    return norm_common(ctx, stream, src, weight, dst, eps, 2);
+}
+
+// ---- softmax -------------------------------------------------------------------
+
+static emel_cuda_status soft_max_common(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                        const emel_tensor_view* mask, const emel_tensor_view* dst, float scale,
+                                        bool apply_scale) {
+    Checked cs, cd, cm;
+    if (!validate_as(src, EMEL_DTYPE_F32, false, &cs) || !validate_as(dst, EMEL_DTYPE_F32, false, &cd))
+        return EMEL_CUDA_INVALID_VIEW;
+    if (mask && !validate_float(mask, false, &cm)) return EMEL_CUDA_INVALID_VIEW;
+    // reductions.rs:473-483
+    const uint64_t width = src->ne[0];
+    if (!(width > 0 && cs.count % width == 0 && cs.count == cd.count)) return EMEL_CUDA_SHAPE_MISMATCH;
+    if (mask && !(mask->ne[0] == width && mask->ne[1] >= src->ne[1] && src->ne[2] % mask->ne[2] == 0 &&
+                  src->ne[3] % mask->ne[3] == 0))
+        return EMEL_CUDA_SHAPE_MISMATCH;
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    emel::RowPlan p = plan_rows(src, cs, dst, &cd);
+    // reductions.rs:485-495: dense (f64 sum) when both layouts are dense
+    p.dense = dense(*src, cs) && dense(*dst, cd);
+    if (!same_ne(src, dst)) {
+        if (dense(*dst, cd)) {
+            // same ordinal -> address map as a dense view with src's extents
+            p.dst.st[0] = 1;
+            p.dst.st[1] = (int64_t)src->ne[0];
+            p.dst.st[2] = (int64_t)(src->ne[0] * src->ne[1]);
+            p.dst.st[3] = (int64_t)(src->ne[0] * src->ne[1] * src->ne[2]);
+            p.vec = p.ne[0] % 4 == 0 && row_vec_ok(p.src) && row_vec_ok(p.dst);
+        } else {
+            p.dst_ordinal = true;
+        }
+    }
+    if (mask) {
+        p.aux = row_operand(mask, cm);
+        p.has_aux = true;
+        p.aux_dtype = (int)dt_of(mask->dtype);
+    }
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = emel::launch_soft_max(env_of(ctx, stream), p, apply_scale, scale);
+    return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_soft_max(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                    const emel_tensor_view* dst) {
+    return soft_max_common(ctx, stream, src, nullptr, dst, 1.0f, false);
+}
+
+emel_cuda_status emel_cuda_soft_max_ext(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                        const emel_tensor_view* mask, const emel_tensor_view* dst, float scale) {
+    return soft_max_common(ctx, stream, src, mask, dst, scale, true);
+}
+
+// ---- reductions ------------------------------------------------------------------
+
+static bool scalar_shape(const emel_tensor_view* v) {
+    return v->ne[0] == 1 && v->ne[1] == 1 && v->ne[2] == 1 && v->ne[3] == 1;
+}
+
+static bool rows_shape(const emel_tensor_view* src, const emel_tensor_view* dst) {
+    return dst->ne[0] == 1 && dst->ne[1] == src->ne[1] && dst->ne[2] == src->ne[2] && dst->ne[3] == src->ne[3];
+}
+
+static bool index_view(const emel_tensor_view* v, Checked* c) {
+    return validate_as(v, EMEL_DTYPE_F32, false, c) || validate_as(v, EMEL_DTYPE_I64, false, c) ||
+           validate_as(v, EMEL_DTYPE_I32, false, c);
+}
+
+static emel_cuda_status sum_common(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                   const emel_tensor_view* dst, int mode) {
+    Checked cs, cd;
+    // reductions.rs:452-458, 520-530
+    if (!validate_as(src, EMEL_DTYPE_F32, false, &cs) || !validate_as(dst, EMEL_DTYPE_F32, false, &cd))
+        return EMEL_CUDA_INVALID_VIEW;
+    if (!scalar_shape(dst)) return EMEL_CUDA_SHAPE_MISMATCH;
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    const emel::RowPlan p = plan_rows(src, cs, nullptr, nullptr);
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = emel::launch_sum(env_of(ctx, stream), p, mode, dst->data);
+    return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_sum(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                               const emel_tensor_view* dst) {
+    return sum_common(ctx, stream, src, dst, 0);
+}
+
+emel_cuda_status emel_cuda_mean(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                const emel_tensor_view* dst) {
+    return sum_common(ctx, stream, src, dst, 1);
+}
+
+emel_cuda_status emel_cuda_sum_f64(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src, double* out) {
+    Checked cs;
+    if (!validate_as(src, EMEL_DTYPE_F32, false, &cs)) return EMEL_CUDA_INVALID_VIEW;
+    if (ctx == nullptr || out == nullptr || reinterpret_cast<uintptr_t>(out) % 8 != 0) return EMEL_CUDA_INVALID_ARGUMENT;
+    const emel::RowPlan p = plan_rows(src, cs, nullptr, nullptr);
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = emel::launch_sum(env_of(ctx, stream), p, 2, out);
+    return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_sum_rows(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                    const emel_tensor_view* dst) {
+    Checked cs, cd;
+    // reductions.rs:460-463, 532-542
+    if (!validate_as(src, EMEL_DTYPE_F32, false, &cs) || !validate_as(dst, EMEL_DTYPE_F32, false, &cd))
+        return EMEL_CUDA_INVALID_VIEW;
+    if (!rows_shape(src, dst)) return EMEL_CUDA_SHAPE_MISMATCH;
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    const emel::RowPlan p = plan_rows(src, cs, dst, &cd);
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = emel::launch_sum_rows(env_of(ctx, stream), p);
+    return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_argmax(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                  const emel_tensor_view* dst) {
+    Checked cs, cd;
+    if (!validate_as(src, EMEL_DTYPE_F32, false, &cs) || !index_view(dst, &cd)) return EMEL_CUDA_INVALID_VIEW;
+    if (!scalar_shape(dst)) return EMEL_CUDA_SHAPE_MISMATCH;
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    const emel::RowPlan p = plan_rows(src, cs, nullptr, nullptr);
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = emel::launch_argmax(env_of(ctx, stream), p, 0, (int)dst->dtype, 0, dst->data);
+    return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_argmax_partial_compute(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                                  int64_t index_base, emel_cuda_argmax_partial* out) {
+    Checked cs;
+    if (!validate_as(src, EMEL_DTYPE_F32, false, &cs)) return EMEL_CUDA_INVALID_VIEW;
+    if (ctx == nullptr || out == nullptr || reinterpret_cast<uintptr_t>(out) % 8 != 0) return EMEL_CUDA_INVALID_ARGUMENT;
+    const emel::RowPlan p = plan_rows(src, cs, nullptr, nullptr);
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = emel::launch_argmax(env_of(ctx, stream), p, 1, 0, index_base, out);
+    return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_argmax_combine(const emel_cuda_argmax_partial* partials, int count, int64_t* index_out,
+                                          float* value_out) {
+    if (partials == nullptr || count <= 0 || index_out == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    // shards are in ordinal order; a later shard wins only with a strictly
+    // greater value (reductions.rs:721), so ties keep the earliest index
+    bool has = false;
+    float best = 0.0f;
+    int64_t idx = 0;
+    for (int k = 0; k < count; ++k) {
+        const emel_cuda_argmax_partial& q = partials[k];
+        if (!q.has_value) continue;
+        if (!has || q.value > best || (q.value == best && q.index < idx)) {
+            has = true;
+            best = q.value;
+            idx = q.index;
+        }
+    }
+    if (partials[0].first_is_nan || !has) {
+        idx = 0;
+    }
+    *index_out = idx;
+    if (value_out) *value_out = best;
+    return EMEL_CUDA_OK;
+}
+
+emel_cuda_status emel_cuda_argmax_rows(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                       const emel_tensor_view* dst) {
+    Checked cs, cd;
+    if (!validate_as(src, EMEL_DTYPE_F32, false, &cs) || !index_view(dst, &cd)) return EMEL_CUDA_INVALID_VIEW;
+    if (!rows_shape(src, dst)) return EMEL_CUDA_SHAPE_MISMATCH;
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    emel::RowPlan p = plan_rows(src, cs, dst, &cd);
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = emel::launch_argmax_rows(env_of(ctx, stream), p, (int)dst->dtype);
+    return device_status(ctx, err);
+}
+
+}  // extern "C"

@@ -1,0 +1,34 @@
+// Kernel launchers called by the host API after validation.  Each returns the
+// CUDA error of its launch(es); none allocates memory.
+#pragma once
+
+#include "plan.hpp"
+
+namespace emel {
+
+struct UnaryParams;
+
+cudaError_t launch_unary(const LaunchEnv& env, const EwPlan& plan, int op, float pa, float pb);
+cudaError_t launch_binary(const LaunchEnv& env, const EwPlan& plan, int op);
+
+// op: 0 norm, 1 rms_norm, 2 rms_norm * weight (aux)
+cudaError_t launch_norm(const LaunchEnv& env, const RowPlan& plan, int op, float eps);
+// soft_max (scale applied when apply_scale; aux = optional mask)
+cudaError_t launch_soft_max(const LaunchEnv& env, const RowPlan& plan, bool apply_scale, float scale);
+cudaError_t launch_sum_rows(const LaunchEnv& env, const RowPlan& plan);
+// dst dtype: F32 / I32 / I64, index written as the column
+cudaError_t launch_argmax_rows(const LaunchEnv& env, const RowPlan& plan, int dst_dtype);
+
+// Whole-tensor reductions over a RowPlan (rows of ne0), using the context
+// workspace for per-block partials.
+// mode: 0 -> write f32 sum to out (dst element), 1 -> f32 mean, 2 -> f64 sum
+cudaError_t launch_sum(const LaunchEnv& env, const RowPlan& plan, int mode, void* out);
+// out_kind: 0 -> index as dtype of dst (F32/I32/I64) into out; 1 -> argmax
+// partial struct (value, has_value, index + index_base) into out
+cudaError_t launch_argmax(const LaunchEnv& env, const RowPlan& plan, int out_kind, int dst_dtype, int64_t index_base,
+                          void* out);
+
+// Bytes of workspace the whole-tensor reductions need.
+uint64_t reduction_workspace_bytes(int sm_count);
+
+}  // namespace emel

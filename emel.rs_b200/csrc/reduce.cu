@@ -1,0 +1,267 @@
+// Whole-tensor reductions: sum / mean (reductions.rs:671-681, 703-713) and
+// argmax (reductions.rs:715-730).
+//
+// One launch per reduction.  Every CTA streams a fixed, grid-strided share
+// of the tensor (16-byte loads when the tensor is one dense run), reduces it
+// in f64 (sum) or as (value, index) (argmax), and stores its partial in the
+// context workspace.  The CTA that finishes last (atomic ticket, no waiting)
+// folds the partials in a fixed order and writes the result, then re-arms
+// the ticket.  With the grid fixed per device, the result is deterministic.
+#include "common.cuh"
+#include "launch.hpp"
+
+namespace emel {
+
+namespace {
+
+constexpr int kThreads = 256;
+constexpr int kCtasPerSm = 4;
+
+struct ArgPart {
+    float v;
+    uint32_t has;
+    int64_t i;
+};
+
+__device__ __forceinline__ ArgPart better(ArgPart a, ArgPart b) {
+    if (!b.has) return a;
+    if (!a.has) return b;
+    if (b.v > a.v) return b;
+    if (a.v > b.v) return a;
+    return b.i < a.i ? b : a;
+}
+
+__device__ __forceinline__ void arg_take(ArgPart& b, float v, int64_t i) {
+    if ((!b.has && !is_nan(v)) || v > b.v) {
+        b.v = v;
+        b.i = i;
+        b.has = 1;
+    }
+}
+
+__device__ __forceinline__ double block_sum(double v, double* sh) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x / 32;
+    __syncthreads();
+    if (lane == 0) sh[warp] = v;
+    __syncthreads();
+    double t = 0.0;
+#pragma unroll
+    for (int w = 0; w < kThreads / 32; ++w) t += sh[w];
+    return t;
+}
+
+__device__ __forceinline__ ArgPart block_arg(ArgPart v, ArgPart* sh) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        ArgPart w;
+        w.v = __shfl_xor_sync(0xffffffffu, v.v, o);
+        w.has = __shfl_xor_sync(0xffffffffu, v.has, o);
+        w.i = __shfl_xor_sync(0xffffffffu, v.i, o);
+        v = better(v, w);
+    }
+    const int lane = threadIdx.x & 31, warp = threadIdx.x / 32;
+    __syncthreads();
+    if (lane == 0) sh[warp] = v;
+    __syncthreads();
+    ArgPart t = sh[0];
+#pragma unroll
+    for (int w = 1; w < kThreads / 32; ++w) t = better(t, sh[w]);
+    return t;
+}
+
+// Logical ordinal of (row r, column c) is r * ne0 + c; its address follows
+// the view's strides.
+__device__ __forceinline__ const float* row_ptr(const RowPlan& p, uint64_t r) {
+    const uint64_t i1 = r % p.ne[1], q = r / p.ne[1], i2 = q % p.ne[2], i3 = q / p.ne[2];
+    return reinterpret_cast<const float*>(p.src.ptr) + (int64_t)i1 * p.src.st[1] + (int64_t)i2 * p.src.st[2] +
+           (int64_t)i3 * p.src.st[3];
+}
+
+// Flat = the view is one dense run of p.rows * ne0 floats.
+template <bool FLAT>
+__device__ __forceinline__ double partial_sum(const RowPlan& p) {
+    double acc = 0.0;
+    const uint64_t gthreads = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if constexpr (FLAT) {
+        const float* x = reinterpret_cast<const float*>(p.src.ptr);
+        const uint64_t n = p.rows * p.ne[0];
+        const uint64_t nvec = n / 4;
+        uint64_t i = gid;
+        for (; i + gthreads < nvec; i += 2 * gthreads) {
+            const float4 a = __ldcs(reinterpret_cast<const float4*>(x) + i);
+            const float4 b = __ldcs(reinterpret_cast<const float4*>(x) + i + gthreads);
+            acc += (double)a.x;
+            acc += (double)a.y;
+            acc += (double)a.z;
+            acc += (double)a.w;
+            acc += (double)b.x;
+            acc += (double)b.y;
+            acc += (double)b.z;
+            acc += (double)b.w;
+        }
+        if (i < nvec) {
+            const float4 a = __ldcs(reinterpret_cast<const float4*>(x) + i);
+            acc += (double)a.x;
+            acc += (double)a.y;
+            acc += (double)a.z;
+            acc += (double)a.w;
+        }
+        const uint64_t t = nvec * 4 + gid;
+        if (t < n) acc += (double)x[t];
+    } else {
+        // warps walk rows; lanes walk columns
+        const uint64_t warp = gid / 32, nwarps = gthreads / 32;
+        const uint32_t lane = threadIdx.x & 31;
+        for (uint64_t r = warp; r < p.rows; r += nwarps) {
+            const float* row = row_ptr(p, r);
+            for (uint64_t c = lane; c < p.ne[0]; c += 32) acc += (double)row[(int64_t)c * p.src.st[0]];
+        }
+    }
+    return acc;
+}
+
+template <bool FLAT>
+__device__ __forceinline__ ArgPart partial_arg(const RowPlan& p) {
+    ArgPart b{0.0f, 0, 0};
+    const uint64_t gthreads = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if constexpr (FLAT) {
+        const float* x = reinterpret_cast<const float*>(p.src.ptr);
+        const uint64_t n = p.rows * p.ne[0];
+        const uint64_t nvec = n / 4;
+        for (uint64_t i = gid; i < nvec; i += gthreads) {
+            const float4 a = __ldcs(reinterpret_cast<const float4*>(x) + i);
+            arg_take(b, a.x, (int64_t)(4 * i));
+            arg_take(b, a.y, (int64_t)(4 * i + 1));
+            arg_take(b, a.z, (int64_t)(4 * i + 2));
+            arg_take(b, a.w, (int64_t)(4 * i + 3));
+        }
+        const uint64_t t = nvec * 4 + gid;
+        if (t < n) arg_take(b, x[t], (int64_t)t);
+    } else {
+        const uint64_t warp = gid / 32, nwarps = gthreads / 32;
+        const uint32_t lane = threadIdx.x & 31;
+        for (uint64_t r = warp; r < p.rows; r += nwarps) {
+            const float* row = row_ptr(p, r);
+            for (uint64_t c = lane; c < p.ne[0]; c += 32)
+                arg_take(b, row[(int64_t)c * p.src.st[0]], (int64_t)(r * p.ne[0] + c));
+        }
+    }
+    return b;
+}
+
+// Returns true in exactly one CTA: the last to finish.  The workspace ticket
+// is re-armed by that CTA.
+__device__ __forceinline__ bool last_cta(unsigned* ticket) {
+    __shared__ bool is_last;
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) is_last = atomicAdd(ticket, 1u) == gridDim.x - 1;
+    __syncthreads();
+    return is_last;
+}
+
+template <bool FLAT>
+__global__ void __launch_bounds__(kThreads) sum_all(RowPlan p, double* partials, unsigned* ticket, int mode, void* out) {
+    __shared__ double sh[kThreads / 32];
+    double acc = block_sum(partial_sum<FLAT>(p), sh);
+    if (threadIdx.x == 0) partials[blockIdx.x] = acc;
+    if (!last_cta(ticket)) return;
+    // fixed-order fold: thread t adds partials t, t+256, ... then a fixed tree
+    double t = 0.0;
+    for (unsigned k = threadIdx.x; k < gridDim.x; k += kThreads) t += __ldcg(partials + k);
+    t = block_sum(t, sh);
+    if (threadIdx.x == 0) {
+        const uint64_t n = p.rows * p.ne[0];
+        if (mode == 0) *reinterpret_cast<float*>(out) = __double2float_rn(t);
+        else if (mode == 1) *reinterpret_cast<float*>(out) = __double2float_rn(t / (double)n);
+        else *reinterpret_cast<double*>(out) = t;
+        *ticket = 0u;
+    }
+}
+
+template <bool FLAT>
+__global__ void __launch_bounds__(kThreads) argmax_all(RowPlan p, ArgPart* partials, unsigned* ticket, int out_kind,
+                                                       int dst_dtype, int64_t index_base, void* out) {
+    __shared__ ArgPart sh[kThreads / 32];
+    ArgPart b = block_arg(partial_arg<FLAT>(p), sh);
+    if (threadIdx.x == 0) partials[blockIdx.x] = b;
+    if (!last_cta(ticket)) return;
+    ArgPart t{0.0f, 0, 0};
+    for (unsigned k = threadIdx.x; k < gridDim.x; k += kThreads) {
+        ArgPart q;
+        q.v = __ldcg(&partials[k].v);
+        q.has = __ldcg(&partials[k].has);
+        q.i = __ldcg(&partials[k].i);
+        t = better(t, q);
+    }
+    t = block_arg(t, sh);
+    if (threadIdx.x == 0) {
+        const float first = reinterpret_cast<const float*>(p.src.ptr)[0];
+        if (out_kind == 0) {
+            // reductions.rs:716-727: the scan starts from element 0, so a NaN
+            // there (or no comparable value at all) leaves index 0.
+            const int64_t idx = (is_nan(first) || !t.has) ? 0 : t.i;
+            if (dst_dtype == (int)DType::I64) *reinterpret_cast<int64_t*>(out) = idx;
+            else if (dst_dtype == (int)DType::I32) *reinterpret_cast<int32_t*>(out) = (int32_t)idx;
+            else *reinterpret_cast<float*>(out) = (float)idx;
+        } else {
+            struct Partial {
+                float value;
+                uint32_t has_value;
+                int64_t index;
+                uint32_t first_is_nan;
+                uint32_t reserved;
+            };
+            Partial* o = reinterpret_cast<Partial*>(out);
+            o->value = t.v;
+            o->has_value = t.has;
+            o->index = t.i + index_base;
+            o->first_is_nan = is_nan(first) ? 1u : 0u;
+            o->reserved = 0u;
+        }
+        *ticket = 0u;
+    }
+}
+
+}  // namespace
+
+uint64_t reduction_workspace_bytes(int sm_count) {
+    // ticket (256 B slot) + one partial (16 B) per CTA
+    return 256 + (uint64_t)sm_count * kCtasPerSm * 16;
+}
+
+static uint32_t reduce_grid(const LaunchEnv& env, uint64_t n) {
+    const uint64_t want = (n + (uint64_t)kThreads * 8 - 1) / ((uint64_t)kThreads * 8);
+    const uint64_t cap = (uint64_t)env.sm_count * kCtasPerSm;
+    const uint64_t g = want < cap ? want : cap;
+    return (uint32_t)(g == 0 ? 1 : g);
+}
+
+static bool flat(const RowPlan& p) { return p.flat; }
+
+cudaError_t launch_sum(const LaunchEnv& env, const RowPlan& p, int mode, void* out) {
+    unsigned* ticket = reinterpret_cast<unsigned*>(env.workspace);
+    double* partials = reinterpret_cast<double*>(reinterpret_cast<char*>(env.workspace) + 256);
+    const uint32_t grid = reduce_grid(env, p.rows * p.ne[0]);
+    if (flat(p)) sum_all<true><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, mode, out);
+    else sum_all<false><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, mode, out);
+    ++*env.launches;
+    return cudaGetLastError();
+}
+
+cudaError_t launch_argmax(const LaunchEnv& env, const RowPlan& p, int out_kind, int dst_dtype, int64_t index_base,
+                          void* out) {
+    unsigned* ticket = reinterpret_cast<unsigned*>(env.workspace);
+    ArgPart* partials = reinterpret_cast<ArgPart*>(reinterpret_cast<char*>(env.workspace) + 256);
+    const uint32_t grid = reduce_grid(env, p.rows * p.ne[0]);
+    if (flat(p)) argmax_all<true><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, out_kind, dst_dtype, index_base, out);
+    else argmax_all<false><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, out_kind, dst_dtype, index_base, out);
+    ++*env.launches;
+    return cudaGetLastError();
+}
+
+}  // namespace emel

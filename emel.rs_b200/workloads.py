@@ -1,0 +1,185 @@
+"""Seeded synthetic inputs for the five benchmark configurations.
+
+No public dataset exists for this path; each configuration is generated
+from a fixed seed with the shapes, value distributions and special values
+its description names.  "N(0, v)" is read as a normal distribution with
+variance v.  Arrays are numpy, in ggml order: numpy shape = ne reversed.
+
+Algorithmic bytes per op count every input element read once and every
+output element written once (the HBM roofline's numerator).
+"""
+
+import math
+from dataclasses import dataclass, field
+from typing import Dict, List
+
+import numpy as np
+
+F32, F16 = 4, 2
+
+
+def normal(rng, shape, variance=1.0):
+    x = rng.standard_normal(size=shape, dtype=np.float32)
+    if variance != 1.0:
+        x *= np.float32(math.sqrt(variance))
+    return x
+
+
+@dataclass
+class OpSpec:
+    name: str
+    bytes: int        # algorithmic bytes per launch
+    elements: int     # logical elements processed per launch
+
+
+@dataclass
+class Config:
+    name: str
+    ops: List[OpSpec] = field(default_factory=list)
+
+
+# ---- config 1: row-broadcast binary ops ------------------------------------
+CFG1_NE = (4096, 2048)
+
+
+def cfg1(seed=1):
+    rng = np.random.default_rng(seed)
+    src0 = normal(rng, (CFG1_NE[1], CFG1_NE[0]))
+    src1 = rng.uniform(0.5, 1.5, size=CFG1_NE[0]).astype(np.float32)
+    return src0, src1
+
+
+def cfg1_spec():
+    n = CFG1_NE[0] * CFG1_NE[1]
+    b = 2 * n * F32 + CFG1_NE[0] * F32
+    return Config("cfg1", [OpSpec(f"broadcast_row_{op}", b, n) for op in ("add", "sub", "mul", "div")])
+
+
+# ---- config 2: unary / activation sweep -------------------------------------
+CFG2_NE = (14336, 512)
+CFG2_OPS = ("silu", "gelu", "relu", "exp", "neg", "sqr", "sqrt", "pow2")
+
+
+def cfg2(seed=2):
+    """x ~ N(0, 2) clamped to [-10, 10]; sqrt and pow take |x| + 1e-3."""
+    rng = np.random.default_rng(seed)
+    x = np.clip(normal(rng, (CFG2_NE[1], CFG2_NE[0]), 2.0), -10.0, 10.0).astype(np.float32)
+    xa = (np.abs(x) + np.float32(1e-3)).astype(np.float32)
+    return x, xa
+
+
+def cfg2_spec():
+    n = CFG2_NE[0] * CFG2_NE[1]
+    ops = [OpSpec(f"{op}_f32", 2 * n * F32, n) for op in CFG2_OPS]
+    ops += [OpSpec(f"{op}_f16", 2 * n * F16, n) for op in CFG2_OPS]
+    return Config("cfg2", ops)
+
+
+# ---- config 3: row normalisation -------------------------------------------
+CFG3_NE = (4096, 8192)
+
+
+def cfg3(seed=3):
+    """x ~ N(0, 1) with 1% of entries (a seeded index set) scaled by 20;
+    weight ~ U(0.5, 1.5) over ne0."""
+    rng = np.random.default_rng(seed)
+    n = CFG3_NE[0] * CFG3_NE[1]
+    x = normal(rng, n)
+    idx = rng.choice(n, size=n // 100, replace=False)
+    x[idx] *= np.float32(20.0)
+    w = rng.uniform(0.5, 1.5, size=CFG3_NE[0]).astype(np.float32)
+    return x.reshape(CFG3_NE[1], CFG3_NE[0]), w
+
+
+def cfg3_spec():
+    n = CFG3_NE[0] * CFG3_NE[1]
+    rows = CFG3_NE[1]
+    return Config("cfg3", [
+        OpSpec("rms_norm", 2 * n * F32, n),
+        OpSpec("rms_norm_mul", 2 * n * F32 + CFG3_NE[0] * F32, n),
+        OpSpec("norm", 2 * n * F32, n),
+        OpSpec("sum_rows", n * F32 + rows * F32, n),
+    ])
+
+
+# ---- config 4: softmax and argmax -------------------------------------------
+CFG4A_NE = (4096, 512, 32)   # kv, q, heads
+CFG4A_SCALE = np.float32(1.0 / math.sqrt(128.0))
+CFG4A_QOFF = 3584
+CFG4B_NE = (151936, 64)
+
+
+def cfg4a(seed=4):
+    """scores ~ N(0, 4); f16 causal mask: 0 where kv <= q + 3584, else -inf."""
+    rng = np.random.default_rng(seed)
+    kv, q, h = CFG4A_NE
+    scores = normal(rng, (h, q, kv), 4.0)
+    kvi = np.arange(kv)[None, :]
+    qi = np.arange(q)[:, None]
+    mask = np.where(kvi <= qi + CFG4A_QOFF, 0.0, -np.inf).astype(np.float16)
+    return scores, mask
+
+
+def cfg4b(seed=5):
+    """logits ~ N(0, 3) with one planted maximum per row (seeded column)."""
+    rng = np.random.default_rng(seed)
+    v, rows = CFG4B_NE
+    logits = normal(rng, (rows, v), 3.0)
+    cols = rng.integers(0, v, size=rows)
+    logits[np.arange(rows), cols] = logits.max(axis=1) + np.float32(1.0)
+    return logits, cols
+
+
+def cfg4_spec():
+    kv, q, h = CFG4A_NE
+    na = kv * q * h
+    v, rows = CFG4B_NE
+    nb = v * rows
+    return Config("cfg4", [
+        OpSpec("soft_max_ext", 2 * na * F32 + kv * q * F16, na),
+        OpSpec("soft_max_vocab", 2 * nb * F32, nb),
+        OpSpec("argmax_rows", nb * F32 + rows * 8, nb),
+    ])
+
+
+# ---- config 5: permuted 4-D broadcast, sharded along dim 3 -----------------
+CFG5_NE = (128, 32, 8192, 8)  # logical view of src0
+
+
+def cfg5_src0_view(ne3=CFG5_NE[3]):
+    """ne/nb (bytes) of src0: contiguous storage [128, 8192, 32, ne3] viewed
+    with dimensions 1 and 2 swapped."""
+    ne0, ne1, ne2, _ = CFG5_NE
+    storage_nb = [F32, F32 * ne0, F32 * ne0 * ne2, F32 * ne0 * ne2 * ne1]
+    return [ne0, ne1, ne2, ne3], [storage_nb[0], storage_nb[2], storage_nb[1], storage_nb[3]]
+
+
+def cfg5(seed=6, ne3=CFG5_NE[3], shard=0):
+    """src0 storage (numpy shape (ne3, 32, 8192, 128)) ~ N(0, 1) and src1
+    (shape (1, 8192, 1, 128)) ~ N(0, 1).  A shard holds the dim-3 slices
+    [shard * ne3, (shard + 1) * ne3) of the full tensor; every shard draws
+    its own slices from a per-slice seed so any sharding yields the same
+    global tensor."""
+    ne0, ne1, ne2, _ = CFG5_NE
+    src0 = np.empty((ne3, ne1, ne2, ne0), dtype=np.float32)
+    for k in range(ne3):
+        rng = np.random.default_rng([seed, shard * ne3 + k])
+        src0[k] = normal(rng, (ne1, ne2, ne0))
+    src1 = normal(np.random.default_rng([seed, 1 << 20]), (1, ne2, 1, ne0))
+    return src0, src1
+
+
+def cfg5_spec(ne3=CFG5_NE[3]):
+    ne0, ne1, ne2, _ = CFG5_NE
+    n = ne0 * ne1 * ne2 * ne3
+    b1 = ne0 * ne2 * F32
+    return Config("cfg5", [
+        OpSpec("repeat_mul", 2 * n * F32 + b1, n),
+        OpSpec("repeat_add", 2 * n * F32 + b1, n),
+        OpSpec("sum", n * F32, n),
+        OpSpec("argmax", n * F32, n),
+    ])
+
+
+SPECS: Dict[str, callable] = {"cfg1": cfg1_spec, "cfg2": cfg2_spec, "cfg3": cfg3_spec, "cfg4": cfg4_spec,
+                              "cfg5": cfg5_spec}

@@ -1,0 +1,270 @@
+/*
+ * emel_cuda.h -- C ABI of the B200 (sm_100a) device op table for the
+ * emel-kernels elementwise, broadcast and reduction operators.
+ *
+ * Every entry point replaces one typed event of the reference operator
+ * contract, `emel_kernels::Kernel::process_event<E: Event>` (stateforward/
+ * emel.rs, crates/emel-kernels/src/any/actor.rs:936-943), and keeps its
+ * argument meaning and error behaviour:
+ *
+ *   - views are the reference's 4-D `Layout { dtype, ne[4], nb[4] }`
+ *     (crates/emel-kernels/src/any/tensor_view.rs:215-219) bound to device
+ *     storage instead of a Rust slice; `nb` are byte strides and nb[0] == 0
+ *     means implicit row-major (tensor_view.rs:262-277);
+ *   - validation runs synchronously on the host before anything is launched,
+ *     in the reference's guard order (view -> shape -> parameters), and a
+ *     rejected request never writes its destination;
+ *   - accepted requests are enqueued on `stream` (a cudaStream_t; NULL is the
+ *     legacy default stream) and return EMEL_CUDA_OK without synchronising.
+ *
+ * Plain C: pointers and sizes only.  No entry point allocates device memory
+ * except emel_cuda_context_create and emel_cuda_malloc.
+ */
+#ifndef EMEL_CUDA_H
+#define EMEL_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define EMEL_CUDA_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define EMEL_CUDA_API __attribute__((visibility("default")))
+#else
+#define EMEL_CUDA_API
+#endif
+
+/* DType::code() wire values (tensor_view.rs:160-209). */
+enum emel_cuda_dtype {
+    EMEL_DTYPE_F32 = 0,
+    EMEL_DTYPE_F16 = 1,
+    EMEL_DTYPE_I32 = 26,
+    EMEL_DTYPE_I64 = 27,
+    EMEL_DTYPE_F64 = 28
+};
+
+/* One status per reference error variant: BinaryError (binary.rs:20-29),
+ * BroadcastError (broadcast.rs:29-38), UnaryError (unary.rs:22-31),
+ * NormalizationError (normalization.rs:31-42), ReductionError
+ * (reductions.rs:21-30); plus the device-side outcomes. */
+typedef enum emel_cuda_status {
+    EMEL_CUDA_OK = 0,
+    EMEL_CUDA_INVALID_VIEW = 1,       /* *Error::InvalidView */
+    EMEL_CUDA_SHAPE_MISMATCH = 2,     /* *Error::ShapeMismatch */
+    EMEL_CUDA_INVALID_PARAMETERS = 3, /* NormalizationError::InvalidParameters */
+    EMEL_CUDA_UNEXPECTED_EVENT = 4,   /* *Error::UnexpectedEvent */
+    EMEL_CUDA_INTERNAL = 5,           /* *Error::Internal */
+    EMEL_CUDA_DEVICE_ERROR = 16,      /* a CUDA runtime call failed */
+    EMEL_CUDA_TIMEOUT = 17,           /* a bounded device wait expired */
+    EMEL_CUDA_INVALID_ARGUMENT = 18,  /* null context / output pointer */
+    EMEL_CUDA_OUT_OF_MEMORY = 19
+} emel_cuda_status;
+
+/* A tensor view over device memory.  `data` is the device address of the
+ * first byte of the backing storage; `storage_bytes` is how many bytes of it
+ * the view may reach (the Rust slice length times the element size).  The
+ * same struct describes inputs and outputs. */
+typedef struct emel_tensor_view {
+    void* data;
+    uint64_t storage_bytes;
+    uint64_t ne[4];
+    uint64_t nb[4];
+    uint32_t dtype;
+    uint32_t reserved; /* must be 0 */
+} emel_tensor_view;
+
+typedef struct emel_cuda_context emel_cuda_context;
+
+/* Binary formulas (binary.rs:386-409); codes match the generic envelope's
+ * binary selector (generic.rs:1280-1305). */
+typedef enum emel_cuda_binary_op {
+    EMEL_BINARY_ADD = 0,
+    EMEL_BINARY_SUB = 1,
+    EMEL_BINARY_MUL = 2,
+    EMEL_BINARY_DIV = 3
+} emel_cuda_binary_op;
+
+/* Unary formulas.  Codes 0..21 are the UnarySubOp wire codes
+ * (unary.rs:101-146); 64.. are the other single-input reference events. */
+typedef enum emel_cuda_unary_op {
+    EMEL_UNARY_ABS = 0,
+    EMEL_UNARY_SGN = 1,
+    EMEL_UNARY_NEG = 2,
+    EMEL_UNARY_STEP = 3,
+    EMEL_UNARY_TANH = 4,
+    EMEL_UNARY_ELU = 5,
+    EMEL_UNARY_RELU = 6,
+    EMEL_UNARY_SIGMOID = 7,
+    EMEL_UNARY_GELU = 8,
+    EMEL_UNARY_GELU_QUICK = 9,
+    EMEL_UNARY_SILU = 10,
+    EMEL_UNARY_HARDSWISH = 11,
+    EMEL_UNARY_HARDSIGMOID = 12,
+    EMEL_UNARY_EXP = 13,
+    EMEL_UNARY_EXPM1 = 14,
+    EMEL_UNARY_SOFTPLUS = 15,
+    EMEL_UNARY_GELU_ERF = 16,
+    EMEL_UNARY_XIELU = 17, /* no typed event in the reference: UNEXPECTED_EVENT */
+    EMEL_UNARY_FLOOR = 18,
+    EMEL_UNARY_CEIL = 19,
+    EMEL_UNARY_ROUND = 20,
+    EMEL_UNARY_TRUNC = 21,
+    EMEL_UNARY_SQR = 64,  /* power.rs OpSqr (pow(x, 2.0)) */
+    EMEL_UNARY_SQRT = 65, /* power.rs OpSqrt */
+    EMEL_UNARY_LOG = 66,  /* reductions.rs OpLog */
+    EMEL_UNARY_SIN = 67,  /* reductions.rs OpSin */
+    EMEL_UNARY_COS = 68   /* reductions.rs OpCos */
+} emel_cuda_unary_op;
+
+/* ---- context, memory and streams (the Rust host side owns these) ------ */
+
+/* Creates a context on `device`: selects the device, queries its SM count
+ * and allocates the context's reduction workspace. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_context_create(int device, emel_cuda_context** out);
+EMEL_CUDA_API emel_cuda_status emel_cuda_context_destroy(emel_cuda_context* ctx);
+/* Human-readable text of the last CUDA error seen by this context. */
+EMEL_CUDA_API const char* emel_cuda_context_last_error(const emel_cuda_context* ctx);
+
+EMEL_CUDA_API emel_cuda_status emel_cuda_malloc(emel_cuda_context* ctx, uint64_t bytes, void** out);
+EMEL_CUDA_API emel_cuda_status emel_cuda_free(emel_cuda_context* ctx, void* ptr);
+EMEL_CUDA_API emel_cuda_status emel_cuda_memcpy_h2d(emel_cuda_context* ctx, void* stream, void* dst, const void* src, uint64_t bytes);
+EMEL_CUDA_API emel_cuda_status emel_cuda_memcpy_d2h(emel_cuda_context* ctx, void* stream, void* dst, const void* src, uint64_t bytes);
+EMEL_CUDA_API emel_cuda_status emel_cuda_memset(emel_cuda_context* ctx, void* stream, void* dst, int value, uint64_t bytes);
+EMEL_CUDA_API emel_cuda_status emel_cuda_stream_create(emel_cuda_context* ctx, void** out);
+EMEL_CUDA_API emel_cuda_status emel_cuda_stream_destroy(emel_cuda_context* ctx, void* stream);
+EMEL_CUDA_API emel_cuda_status emel_cuda_stream_synchronize(emel_cuda_context* ctx, void* stream);
+/* Number of kernels this context has launched (all entry points). */
+EMEL_CUDA_API uint64_t emel_cuda_launch_count(const emel_cuda_context* ctx);
+
+/* ---- binary family --------------------------------------------------- */
+
+/* binary::OpAdd/OpSub/OpMul/OpDiv (binary.rs:47-81, guards 336-354, loop
+ * 411-424): equal element counts, each operand read by logical ordinal
+ * through its own layout.  F32, or F16 for all three views. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_binary(emel_cuda_context* ctx, void* stream, int op, const emel_tensor_view* lhs,
+                                  const emel_tensor_view* rhs, const emel_tensor_view* dst);
+
+/* broadcast::OpAddBroadcastRow / OpMulBroadcastRow (broadcast.rs:53-84,
+ * guards 323-350, loops 352-390); SUB and DIV use the same contract. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_broadcast_row(emel_cuda_context* ctx, void* stream, int op, const emel_tensor_view* src0,
+                                         const emel_tensor_view* src1, const emel_tensor_view* dst);
+
+/* Fused ggml-style repeat + binary: generic repeat (generic.rs:1641-1665)
+ * of src1 to dst's extents followed by the binary.rs formula.  src0.ne ==
+ * dst.ne and every src1.ne[d] divides dst.ne[d]. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_binary_repeat(emel_cuda_context* ctx, void* stream, int op, const emel_tensor_view* src0,
+                                         const emel_tensor_view* src1, const emel_tensor_view* dst);
+
+/* ---- unary family ---------------------------------------------------- */
+
+/* Typed unary events OpAbs..OpTrunc (unary.rs:72-92, guards 455-461),
+ * power::OpSqr/OpSqrt (power.rs:48-63, 266-272) and reductions::OpLog/
+ * OpSin/OpCos (reductions.rs:45-88, 448-466): valid views, equal element
+ * counts.  F32, or F16 for both views. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_unary(emel_cuda_context* ctx, void* stream, int op, const emel_tensor_view* src,
+                                 const emel_tensor_view* dst);
+
+/* Generic unary::OpUnary (unary.rs:148-172, rows 276-292): only abs, neg,
+ * tanh, elu, relu, gelu, silu and exp; every other subop, invalid view or
+ * count mismatch reports EMEL_CUDA_UNEXPECTED_EVENT.  F32 only. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_op_unary(emel_cuda_context* ctx, void* stream, int subop, const emel_tensor_view* src,
+                                    const emel_tensor_view* dst);
+
+/* activation::OpScale (activation.rs:58, 366-377): dst = src * scale. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_scale(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                 const emel_tensor_view* dst, float scale);
+/* activation::OpClamp (activation.rs:78, 403-423). */
+EMEL_CUDA_API emel_cuda_status emel_cuda_clamp(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                 const emel_tensor_view* dst, float min, float max);
+/* activation::OpLeakyRelu (activation.rs:507-521). */
+EMEL_CUDA_API emel_cuda_status emel_cuda_leaky_relu(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                      const emel_tensor_view* dst, float negative_slope);
+/* activation::OpSiluBack (activation.rs:467-481): dst = grad * silu'(src). */
+EMEL_CUDA_API emel_cuda_status emel_cuda_silu_back(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                     const emel_tensor_view* grad, const emel_tensor_view* dst);
+/* elementwise::OpAdd1 (elementwise.rs:280-291): dst = src + scalar. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_add1(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                const emel_tensor_view* dst, float scalar);
+/* tensor_view::CopyTensor (tensor_view.rs:954-967, 1096-1122). */
+EMEL_CUDA_API emel_cuda_status emel_cuda_copy(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                const emel_tensor_view* dst);
+
+/* ---- row normalisation ----------------------------------------------- */
+
+/* normalization::OpNorm (normalization.rs:58-76, guards 364-382, loop
+ * 316-341): per ne0-row mean/variance normalisation, f64 accumulation. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_norm(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                const emel_tensor_view* dst, float eps);
+/* normalization::OpRmsNorm (normalization.rs:78-96, loop 343-362). */
+EMEL_CUDA_API emel_cuda_status emel_cuda_rms_norm(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                    const emel_tensor_view* dst, float eps);
+/* OpRmsNorm followed by OpMulBroadcastRow with `weight` ne == [ne0,1,1,1],
+ * in one pass; bit-identical to the two events run back to back. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_rms_norm_mul(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                        const emel_tensor_view* weight, const emel_tensor_view* dst, float eps);
+
+/* ---- softmax --------------------------------------------------------- */
+
+/* reductions::OpSoftMax (reductions.rs:150-163, guards 473-495, loops
+ * 565-638): per ne0-row max, exp, sum (f64 for dense views, f32 otherwise),
+ * divide. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_soft_max(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                    const emel_tensor_view* dst);
+/* OpSoftMax over v = src * scale + mask (ggml soft_max_ext contract).  mask
+ * may be NULL; when present it is F16 or F32 with ne0 == src ne0, ne1 >=
+ * src ne1, and ne2/ne3 dividing the source extents. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_soft_max_ext(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                        const emel_tensor_view* mask, const emel_tensor_view* dst, float scale);
+
+/* ---- reductions ------------------------------------------------------ */
+
+/* reductions::OpSum (reductions.rs:90-103, 671-681): dst ne == [1,1,1,1]. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_sum(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                               const emel_tensor_view* dst);
+/* The f64 accumulator of OpSum, written to device memory `out` (one double):
+ * the per-shard partial of a multi-GPU whole-tensor sum. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_sum_f64(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src, double* out);
+/* reductions::OpMean (reductions.rs:120-133, 703-713). */
+EMEL_CUDA_API emel_cuda_status emel_cuda_mean(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                const emel_tensor_view* dst);
+/* reductions::OpSumRows (reductions.rs:105-118, 684-700): dst ne ==
+ * [1, ne1, ne2, ne3]. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_sum_rows(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                    const emel_tensor_view* dst);
+/* reductions::OpArgmax (reductions.rs:135-148, 715-730): first index of the
+ * maximum over the whole tensor.  dst ne == [1,1,1,1]; dtype F32 (the
+ * reference's index-as-f32, exact below 2^24), I32 or I64 (exact). */
+EMEL_CUDA_API emel_cuda_status emel_cuda_argmax(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                  const emel_tensor_view* dst);
+/* Per-shard argmax partial for multi-GPU combination, written to device
+ * memory: the shard's winning value and its ordinal plus `index_base`
+ * (has_value == 0 when the shard holds no comparable, non-NaN value), and
+ * whether the shard's element 0 is NaN. */
+typedef struct emel_cuda_argmax_partial {
+    float value;
+    uint32_t has_value;
+    int64_t index;
+    uint32_t first_is_nan;
+    uint32_t reserved;
+} emel_cuda_argmax_partial;
+EMEL_CUDA_API emel_cuda_status emel_cuda_argmax_partial_compute(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                                  int64_t index_base, emel_cuda_argmax_partial* out);
+/* Host-side combination of per-shard partials given in shard order: the
+ * reference's tie rule (earliest index wins) and its NaN rule (a NaN at
+ * element 0 of the whole tensor, i.e. of shard 0, pins the answer to 0). */
+EMEL_CUDA_API emel_cuda_status emel_cuda_argmax_combine(const emel_cuda_argmax_partial* partials, int count, int64_t* index_out,
+                                          float* value_out);
+/* Per-row argmax (the reductions.rs:715-730 scan per ne0-row): dst ne ==
+ * [1, ne1, ne2, ne3], dtype F32, I32 or I64; the index is the column. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_argmax_rows(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                       const emel_tensor_view* dst);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* EMEL_CUDA_H */

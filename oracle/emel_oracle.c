@@ -130,6 +130,33 @@ static uint64_t ordinal_offset(const oracle_view* v, const uint64_t s[4], uint64
     return off;
 }
 
+/* Incremental form of ordinal_offset for consecutive ordinals: the same
+ * ordinal -> offset map walked in ordinal order without per-element
+ * division (dimension 0 fastest, carries into 1, 2, 3). */
+typedef struct walker {
+    uint64_t ne[4], s[4], c[4], off;
+} walker;
+
+static void walker_init(walker* w, const oracle_view* v, const uint64_t s[4], uint64_t ordinal) {
+    w->off = 0;
+    for (int d = 0; d < 4; ++d) {
+        w->ne[d] = v->ne[d];
+        w->s[d] = s[d];
+        w->c[d] = ordinal % v->ne[d];
+        ordinal /= v->ne[d];
+        w->off += w->c[d] * s[d];
+    }
+}
+
+static inline void walker_next(walker* w) {
+    for (int d = 0; d < 4; ++d) {
+        w->off += w->s[d];
+        if (++w->c[d] < w->ne[d]) return;
+        w->off -= w->ne[d] * w->s[d];
+        w->c[d] = 0;
+    }
+}
+
 /* Reference binary16 helpers (unary.rs:546-586), kept step for step because
  * the GELU path rounds through them and their results are part of parity. */
 static inline uint32_t f2u(float f) { uint32_t u; memcpy(&u, &f, 4); return u; }
@@ -217,10 +244,17 @@ int oracle_binary(int op, const oracle_view* lhs, const oracle_view* rhs, const 
     effective_strides(lhs, dtype_size(lhs->dtype), sl);
     effective_strides(rhs, dtype_size(rhs->dtype), sr);
     effective_strides(dst, dtype_size(dst->dtype), sd);
+    walker wl, wr, wd;
+    walker_init(&wl, lhs, sl, 0);
+    walker_init(&wr, rhs, sr, 0);
+    walker_init(&wd, dst, sd, 0);
     for (uint64_t i = 0; i < nd; ++i) {
-        float a = load_f(lhs, ordinal_offset(lhs, sl, i));
-        float b = load_f(rhs, ordinal_offset(rhs, sr, i));
-        store_f(dst, ordinal_offset(dst, sd, i), binary_apply(op, a, b));
+        float a = load_f(lhs, wl.off);
+        float b = load_f(rhs, wr.off);
+        store_f(dst, wd.off, binary_apply(op, a, b));
+        walker_next(&wl);
+        walker_next(&wr);
+        walker_next(&wd);
     }
     return ORACLE_OK;
 }
@@ -241,13 +275,20 @@ int oracle_broadcast_row(int op, const oracle_view* src0, const oracle_view* src
     effective_strides(src1, dtype_size(src1->dtype), s1);
     effective_strides(dst, dtype_size(dst->dtype), sd);
     uint64_t columns = n1, rows = nd / columns;
-    for (uint64_t r = 0; r < rows; ++r)
+    walker w0, wd, w1;
+    walker_init(&w0, src0, s0, 0);
+    walker_init(&wd, dst, sd, 0);
+    for (uint64_t r = 0; r < rows; ++r) {
+        walker_init(&w1, src1, s1, 0);
         for (uint64_t c = 0; c < columns; ++c) {
-            uint64_t ordinal = r * columns + c;
-            float a = load_f(src0, ordinal_offset(src0, s0, ordinal));
-            float b = load_f(src1, ordinal_offset(src1, s1, c));
-            store_f(dst, ordinal_offset(dst, sd, ordinal), binary_apply(op, a, b));
+            float a = load_f(src0, w0.off);
+            float b = load_f(src1, w1.off);
+            store_f(dst, wd.off, binary_apply(op, a, b));
+            walker_next(&w0);
+            walker_next(&w1);
+            walker_next(&wd);
         }
+    }
     return ORACLE_OK;
 }
 
@@ -267,16 +308,18 @@ int oracle_binary_repeat(int op, const oracle_view* src0, const oracle_view* src
     effective_strides(src0, dtype_size(src0->dtype), s0);
     effective_strides(src1, dtype_size(src1->dtype), s1);
     effective_strides(dst, dtype_size(dst->dtype), sd);
+    walker w0, wd;
+    walker_init(&w0, src0, s0, 0);
+    walker_init(&wd, dst, sd, 0);
     for (uint64_t i = 0; i < nd; ++i) {
-        uint64_t rem = i, off1 = 0;
-        for (int d = 0; d < 4; ++d) {
-            uint64_t c = rem % dst->ne[d];
-            rem /= dst->ne[d];
-            off1 += (c % src1->ne[d]) * s1[d];
-        }
-        float a = load_f(src0, ordinal_offset(src0, s0, i));
+        /* wd.c holds dst's coordinates of ordinal i */
+        uint64_t off1 = 0;
+        for (int d = 0; d < 4; ++d) off1 += (wd.c[d] % src1->ne[d]) * s1[d];
+        float a = load_f(src0, w0.off);
         float b = load_f(src1, off1);
-        store_f(dst, ordinal_offset(dst, sd, i), binary_apply(op, a, b));
+        store_f(dst, wd.off, binary_apply(op, a, b));
+        walker_next(&w0);
+        walker_next(&wd);
     }
     return ORACLE_OK;
 }
@@ -367,8 +410,14 @@ void oracle_unary_range(int op, const oracle_view* src, const oracle_view* dst, 
     uint64_t ss[4], sd[4];
     effective_strides(src, dtype_size(src->dtype), ss);
     effective_strides(dst, dtype_size(dst->dtype), sd);
-    for (uint64_t i = begin; i < end; ++i)
-        store_f(dst, ordinal_offset(dst, sd, i), unary_apply(op, load_f(src, ordinal_offset(src, ss, i))));
+    walker ws, wd;
+    walker_init(&ws, src, ss, begin);
+    walker_init(&wd, dst, sd, begin);
+    for (uint64_t i = begin; i < end; ++i) {
+        store_f(dst, wd.off, unary_apply(op, load_f(src, ws.off)));
+        walker_next(&ws);
+        walker_next(&wd);
+    }
 }
 
 int oracle_unary(int op, const oracle_view* src, const oracle_view* dst) {
@@ -404,11 +453,16 @@ static int same_shape_views(const oracle_view* src, const oracle_view* dst, uint
 #define ORACLE_MAP(src, dst, count, expr)                                                  \
     do {                                                                                   \
         uint64_t ss_[4], sd_[4];                                                           \
+        walker ws_, wd_;                                                                   \
         effective_strides(src, 4, ss_);                                                    \
         effective_strides(dst, 4, sd_);                                                    \
+        walker_init(&ws_, src, ss_, 0);                                                    \
+        walker_init(&wd_, dst, sd_, 0);                                                    \
         for (uint64_t i_ = 0; i_ < (count); ++i_) {                                        \
-            float v = load_f(src, ordinal_offset(src, ss_, i_));                           \
-            store_f(dst, ordinal_offset(dst, sd_, i_), (expr));                            \
+            float v = load_f(src, ws_.off);                                                \
+            store_f(dst, wd_.off, (expr));                                                 \
+            walker_next(&ws_);                                                             \
+            walker_next(&wd_);                                                             \
         }                                                                                  \
     } while (0)
 
@@ -450,11 +504,18 @@ int oracle_silu_back(const oracle_view* src, const oracle_view* grad, const orac
     effective_strides(src, 4, ss);
     effective_strides(grad, 4, sg);
     effective_strides(dst, 4, sd);
+    walker ws, wg, wd;
+    walker_init(&ws, src, ss, 0);
+    walker_init(&wg, grad, sg, 0);
+    walker_init(&wd, dst, sd, 0);
     for (uint64_t i = 0; i < n; ++i) {
-        float v = load_f(src, ordinal_offset(src, ss, i));
+        float v = load_f(src, ws.off);
         float sigmoid = 1.0f / (1.0f + expf(-v));
         float derivative = sigmoid * (1.0f + v * (1.0f - sigmoid));
-        store_f(dst, ordinal_offset(dst, sd, i), load_f(grad, ordinal_offset(grad, sg, i)) * derivative);
+        store_f(dst, wd.off, load_f(grad, wg.off) * derivative);
+        walker_next(&ws);
+        walker_next(&wg);
+        walker_next(&wd);
     }
     return ORACLE_OK;
 }
@@ -498,19 +559,20 @@ int oracle_norm(const oracle_view* src, const oracle_view* dst, float eps) {
     element_count(src, &count);
     uint64_t columns = src->ne[0], rows = count / columns;
     for (uint64_t r = 0; r < rows; ++r) {
-        uint64_t start = r * columns, end = start + columns;
+        /* a row is dimension 0 at fixed (i1, i2, i3): base + column * stride */
+        uint64_t xb = ordinal_offset(src, ss, r * columns), yb = ordinal_offset(dst, sd, r * columns);
         double sum = 0.0;
-        for (uint64_t o = start; o < end; ++o) sum += (double)load_f(src, ordinal_offset(src, ss, o));
+        for (uint64_t c = 0; c < columns; ++c) sum += (double)load_f(src, xb + c * ss[0]);
         float mean = (float)(sum / (double)columns);
         double variance_sum = 0.0;
-        for (uint64_t o = start; o < end; ++o) {
-            float centered = load_f(src, ordinal_offset(src, ss, o)) - mean;
+        for (uint64_t c = 0; c < columns; ++c) {
+            float centered = load_f(src, xb + c * ss[0]) - mean;
             variance_sum += (double)centered * (double)centered;
         }
         float variance = (float)(variance_sum / (double)columns);
         float scale = 1.0f / sqrtf(variance + eps);
-        for (uint64_t o = start; o < end; ++o)
-            store_f(dst, ordinal_offset(dst, sd, o), (load_f(src, ordinal_offset(src, ss, o)) - mean) * scale);
+        for (uint64_t c = 0; c < columns; ++c)
+            store_f(dst, yb + c * sd[0], (load_f(src, xb + c * ss[0]) - mean) * scale);
     }
     return ORACLE_OK;
 }
@@ -525,18 +587,18 @@ static void rms_rows(const oracle_view* src, const oracle_view* weight, const or
     if (weight) effective_strides(weight, 4, sw);
     uint64_t columns = src->ne[0];
     for (uint64_t r = row_begin; r < row_end; ++r) {
-        uint64_t start = r * columns, end = start + columns;
+        uint64_t xb = ordinal_offset(src, ss, r * columns), yb = ordinal_offset(dst, sd, r * columns);
         double sum = 0.0;
-        for (uint64_t o = start; o < end; ++o) {
-            float v = load_f(src, ordinal_offset(src, ss, o));
+        for (uint64_t c = 0; c < columns; ++c) {
+            float v = load_f(src, xb + c * ss[0]);
             sum += (double)(v * v);
         }
         float mean = (float)(sum / (double)columns);
         float scale = 1.0f / sqrtf(mean + eps);
-        for (uint64_t o = start; o < end; ++o) {
-            float y = load_f(src, ordinal_offset(src, ss, o)) * scale;
-            if (weight) y = y * load_f(weight, ordinal_offset(weight, sw, o - start));
-            store_f(dst, ordinal_offset(dst, sd, o), y);
+        for (uint64_t c = 0; c < columns; ++c) {
+            float y = load_f(src, xb + c * ss[0]) * scale;
+            if (weight) y = y * load_f(weight, c * sw[0]);
+            store_f(dst, yb + c * sd[0], y);
         }
     }
 }
@@ -598,17 +660,21 @@ static int soft_max_core(const oracle_view* src, const oracle_view* mask, const 
     effective_strides(dst, 4, sd);
     if (mask) effective_strides(mask, dtype_size(mask->dtype), sm);
     uint64_t rows = ns / width;
+    int dst_rows = same_ne(src, dst);
     for (uint64_t r = 0; r < rows; ++r) {
         uint64_t offset = r * width;
+        uint64_t xb = ordinal_offset(src, ss, offset);
+        uint64_t yb = dst_rows ? ordinal_offset(dst, sd, offset) : 0;
         uint64_t mask_row = 0;
         if (mask) {
             uint64_t i1 = r % src->ne[1], i2 = (r / src->ne[1]) % src->ne[2], i3 = r / (src->ne[1] * src->ne[2]);
             mask_row = i1 * sm[1] + (i2 % mask->ne[2]) * sm[2] + (i3 % mask->ne[3]) * sm[3];
         }
 #define SM_VALUE(c)                                                                                   \
-    (!apply_scale ? load_f(src, ordinal_offset(src, ss, offset + (c)))                               \
-     : mask ? load_f(src, ordinal_offset(src, ss, offset + (c))) * scale + load_f(mask, mask_row + (c) * sm[0]) \
-            : load_f(src, ordinal_offset(src, ss, offset + (c))) * scale)
+    (!apply_scale ? load_f(src, xb + (c) * ss[0])                                                   \
+     : mask ? load_f(src, xb + (c) * ss[0]) * scale + load_f(mask, mask_row + (c) * sm[0])          \
+            : load_f(src, xb + (c) * ss[0]) * scale)
+#define SM_DST(c) (dst_rows ? yb + (c) * sd[0] : ordinal_offset(dst, sd, offset + (c)))
         float max_value = SM_VALUE(0);
         for (uint64_t c = 1; c < width; ++c) {
             float v = SM_VALUE(c);
@@ -618,27 +684,28 @@ static int soft_max_core(const oracle_view* src, const oracle_view* mask, const 
             double sum = 0.0;
             for (uint64_t c = 0; c < width; ++c) {
                 float e = expf(SM_VALUE(c) - max_value);
-                store_f(dst, ordinal_offset(dst, sd, offset + c), e);
+                store_f(dst, SM_DST(c), e);
                 sum += (double)e;
             }
             float denominator = (float)sum;
             for (uint64_t c = 0; c < width; ++c) {
-                uint64_t o = ordinal_offset(dst, sd, offset + c);
+                uint64_t o = SM_DST(c);
                 store_f(dst, o, load_f(dst, o) / denominator);
             }
         } else {
             float sum = 0.0f;
             for (uint64_t c = 0; c < width; ++c) {
                 float e = expf(SM_VALUE(c) - max_value);
-                store_f(dst, ordinal_offset(dst, sd, offset + c), e);
+                store_f(dst, SM_DST(c), e);
                 sum += e;
             }
             for (uint64_t c = 0; c < width; ++c) {
-                uint64_t o = ordinal_offset(dst, sd, offset + c);
+                uint64_t o = SM_DST(c);
                 store_f(dst, o, load_f(dst, o) / sum);
             }
         }
 #undef SM_VALUE
+#undef SM_DST
     }
     return ORACLE_OK;
 }
@@ -667,7 +734,12 @@ int oracle_sum_f64(const oracle_view* src, double* out) {
     uint64_t ss[4];
     effective_strides(src, 4, ss);
     double sum = 0.0;
-    for (uint64_t i = 0; i < n; ++i) sum += (double)load_f(src, ordinal_offset(src, ss, i));
+    walker w;
+    walker_init(&w, src, ss, 0);
+    for (uint64_t i = 0; i < n; ++i) {
+        sum += (double)load_f(src, w.off);
+        walker_next(&w);
+    }
     *out = sum;
     return ORACLE_OK;
 }
@@ -701,7 +773,8 @@ int oracle_sum_rows(const oracle_view* src, const oracle_view* dst) {
     uint64_t width = src->ne[0], rows = n / width;
     for (uint64_t r = 0; r < rows; ++r) {
         double sum = 0.0;
-        for (uint64_t c = 0; c < width; ++c) sum += (double)load_f(src, ordinal_offset(src, ss, r * width + c));
+        uint64_t xb = ordinal_offset(src, ss, r * width);
+        for (uint64_t c = 0; c < width; ++c) sum += (double)load_f(src, xb + c * ss[0]);
         store_f(dst, ordinal_offset(dst, sd, r), (float)sum);
     }
     return ORACLE_OK;
@@ -711,9 +784,12 @@ int oracle_sum_rows(const oracle_view* src, const oracle_view* dst) {
 static uint64_t argmax_scan(const oracle_view* src, const uint64_t ss[4], uint64_t begin, uint64_t end,
                             float* best_out) {
     uint64_t best_index = begin;
-    float best_value = load_f(src, ordinal_offset(src, ss, begin));
+    walker w;
+    walker_init(&w, src, ss, begin);
+    float best_value = load_f(src, w.off);
     for (uint64_t i = begin + 1; i < end; ++i) {
-        float v = load_f(src, ordinal_offset(src, ss, i));
+        walker_next(&w);
+        float v = load_f(src, w.off);
         if (v > best_value) {
             best_value = v;
             best_index = i;

@@ -1,0 +1,214 @@
+"""Row-operator parity on the GPU: norm, rms_norm (+ fused weight), soft_max
+(+ scale and f16 mask), sum_rows and per-row argmax, across every kernel
+tier (warp / CTA / 1024-thread rows held in registers, cluster rows with
+DSMEM exchange, streaming fallback, non-dense sequential-f32 softmax).
+
+Tolerance: 1e-5 relative (the f64 accumulators only change summation
+order); argmax indices are exact."""
+
+import ctypes
+
+import numpy as np
+import pytest
+
+import gpu_helpers as gh
+
+pytestmark = pytest.mark.gpu
+
+RTOL = 1e-5
+
+
+@pytest.fixture(scope="module")
+def kern(emel):
+    return emel.Kernel(device=0, synchronize=True)
+
+
+def run_row_op(emel, kern, olib, kind, x, ne, nb=None, eps=1e-5, weight=None, mask=None, scale=1.0,
+               out_ne=None, out_nb=None, out_dtype=np.float32):
+    ctx = kern.ctx
+    px = gh.Pair(emel, ctx, x, ne, nb)
+    if kind in ("sum_rows", "argmax_rows"):
+        o_ne = [1] + list(ne[1:])
+        out_host = np.zeros(int(np.prod(o_ne)), dtype=out_dtype)
+        po = gh.Pair(emel, ctx, out_host, o_ne)
+    else:
+        out_host = np.full(x.size, 3.0, dtype=np.float32)
+        po = gh.Pair(emel, ctx, out_host, out_ne or ne, out_nb)
+    pw = gh.Pair(emel, ctx, weight) if weight is not None else None
+    pm = gh.Pair(emel, ctx, mask[0], mask[1], mask[2]) if mask is not None else None
+    B = ctypes.byref
+    want = out_host.copy()
+    wv = gh.oracle.make_view(want.ctypes.data, want.nbytes, po.ne, po.nb, po.code)
+    if kind == "norm":
+        ev = emel.OpNorm(px.dview(), po.dview(), eps)
+        ost = olib.oracle_norm(B(px.oview()), B(wv), eps)
+    elif kind == "rms_norm":
+        ev = emel.OpRmsNorm(px.dview(), po.dview(), eps)
+        ost = olib.oracle_rms_norm(B(px.oview()), B(wv), eps)
+    elif kind == "rms_norm_mul":
+        ev = emel.OpRmsNormMul(px.dview(), pw.dview(), po.dview(), eps)
+        ost = olib.oracle_rms_norm_mul(B(px.oview()), B(pw.oview()), B(wv), eps)
+    elif kind == "soft_max":
+        ev = emel.OpSoftMax(px.dview(), po.dview())
+        ost = olib.oracle_soft_max(B(px.oview()), B(wv))
+    elif kind == "soft_max_ext":
+        ev = emel.OpSoftMaxExt(px.dview(), pm.dview() if pm else None, po.dview(), scale)
+        ost = olib.oracle_soft_max_ext(B(px.oview()), B(pm.oview()) if pm else None, B(wv), scale)
+    elif kind == "sum_rows":
+        ev = emel.OpSumRows(px.dview(), po.dview())
+        ost = olib.oracle_sum_rows(B(px.oview()), B(wv))
+    elif kind == "argmax_rows":
+        ev = emel.OpArgmaxRows(px.dview(), po.dview())
+        ost = olib.oracle_argmax_rows(B(px.oview()), B(wv))
+    else:
+        raise AssertionError(kind)
+    st = kern.process_event(ev)
+    assert st == emel.Status.OK, (kind, st, ctx.last_error)
+    assert ost == 0
+    got = po.download()
+    for p in (px, po, pw, pm):
+        if p is not None:
+            p.free()
+    return got, want
+
+
+def close(got, want, floor, what):
+    err = gh.max_rel_err(got, want, floor)
+    exact = float(np.mean(got.view(np.uint32) == want.view(np.uint32)))
+    assert err <= RTOL, f"{what}: max relative error {err:.3e} (bit-exact fraction {exact:.6f})"
+    return exact
+
+
+# ---- tiers -------------------------------------------------------------------
+WIDTHS = [1, 7, 32, 1000, 1024, 1025, 4096, 8192, 8193, 32768, 40000]
+
+
+@pytest.mark.parametrize("width", WIDTHS)
+@pytest.mark.parametrize("kind", ["norm", "rms_norm", "soft_max"])
+def test_row_tiers(emel, kern, oracle_lib, width, kind):
+    rows = max(1, min(64, 200000 // width))
+    rng = np.random.default_rng(width)
+    x = (rng.standard_normal(width * rows) * 2).astype(np.float32)
+    got, want = run_row_op(emel, kern, oracle_lib, kind, x, [width, rows, 1, 1], eps=1e-5)
+    close(got, want, 1e-6 if kind != "soft_max" else 1e-30, f"{kind} width={width}")
+
+
+@pytest.mark.parametrize("width", [151936, 300000])
+def test_softmax_vocab_width_rows(emel, kern, oracle_lib, width):
+    """151936 wide: cluster of CTAs with DSMEM; 300000: streaming fallback."""
+    rng = np.random.default_rng(width)
+    x = (rng.standard_normal(width * 3) * 3).astype(np.float32)
+    got, want = run_row_op(emel, kern, oracle_lib, "soft_max", x, [width, 3, 1, 1])
+    close(got, want, 1e-30, f"soft_max width={width}")
+
+
+def test_row_ops_on_strided_views(emel, kern, oracle_lib):
+    rng = np.random.default_rng(21)
+    x = rng.standard_normal(2000).astype(np.float32)
+    ne, nb = [64, 9, 1, 1], [8, 640, 5760, 5760]  # every other element, padded rows
+    for kind in ("norm", "rms_norm", "soft_max"):
+        got, want = run_row_op(emel, kern, oracle_lib, kind, x, ne, nb, eps=1e-5, out_ne=ne, out_nb=nb)
+        close(got, want, 1e-30, f"{kind} strided")
+
+
+def test_softmax_non_dense_keeps_sequential_f32_sum(emel, kern, oracle_lib):
+    """reductions.rs:603-638: non-dense views sum in f32, in row order."""
+    rng = np.random.default_rng(22)
+    x = rng.standard_normal(3000 * 2 * 4).astype(np.float32)
+    ne, nb = [3000, 4, 1, 1], [8, 24000, 96000, 96000]
+    got, want = run_row_op(emel, kern, oracle_lib, "soft_max", x, ne, nb, out_ne=ne, out_nb=nb)
+    close(got, want, 1e-30, "softmax sparse")
+
+
+def test_softmax_count_equal_different_destination_extents(emel, kern, oracle_lib):
+    rng = np.random.default_rng(23)
+    x = rng.standard_normal(6 * 40).astype(np.float32)
+    got, want = run_row_op(emel, kern, oracle_lib, "soft_max", x, [6, 40, 1, 1], out_ne=[40, 6, 1, 1])
+    close(got, want, 1e-30, "softmax dense dst other extents")
+    got, want = run_row_op(emel, kern, oracle_lib, "soft_max", x, [6, 40, 1, 1], out_ne=[10, 24, 1, 1],
+                           out_nb=[4, 40, 960, 960])
+    close(got, want, 1e-30, "softmax ordinal dst")
+
+
+# ---- config 3 ----------------------------------------------------------------
+@pytest.fixture(scope="module")
+def cfg3_data(emel):
+    from emel_rs_b200 import workloads
+    return workloads.cfg3()
+
+
+def test_cfg3_rms_norm_then_weight_full_size(emel, kern, oracle_lib, cfg3_data):
+    x, w = cfg3_data
+    ne = [4096, 8192, 1, 1]
+    got, want = run_row_op(emel, kern, oracle_lib, "rms_norm", x, ne, eps=1e-6)
+    exact = close(got, want, 1e-6, "cfg3 rms_norm")
+    assert exact > 0.999
+    got, want = run_row_op(emel, kern, oracle_lib, "rms_norm_mul", x, ne, eps=1e-6, weight=w)
+    close(got, want, 1e-6, "cfg3 rms_norm * weight")
+
+
+def test_cfg3_fused_weight_equals_two_events(emel, kern, oracle_lib, cfg3_data):
+    """emel_cuda_rms_norm_mul is bit-identical to OpRmsNorm then OpMulBroadcastRow."""
+    x, w = cfg3_data
+    x = x[:512]
+    ctx = kern.ctx
+    ne = [4096, 512, 1, 1]
+    px, pw = gh.Pair(emel, ctx, x, ne), gh.Pair(emel, ctx, w)
+    pt, p1, p2 = (gh.Pair(emel, ctx, np.zeros_like(x), ne) for _ in range(3))
+    assert kern.process_event(emel.OpRmsNorm(px.dview(), pt.dview(), 1e-6)) == emel.Status.OK
+    assert kern.process_event(emel.OpMulBroadcastRow(pt.dview(), pw.dview(), p1.dview())) == emel.Status.OK
+    assert kern.process_event(emel.OpRmsNormMul(px.dview(), pw.dview(), p2.dview(), 1e-6)) == emel.Status.OK
+    gh.assert_bits_equal(p2.download(), p1.download(), "fused vs two events")
+
+
+def test_cfg3_norm_and_sum_rows_full_size(emel, kern, oracle_lib, cfg3_data):
+    x, _ = cfg3_data
+    ne = [4096, 8192, 1, 1]
+    got, want = run_row_op(emel, kern, oracle_lib, "norm", x, ne, eps=1e-5)
+    close(got, want, 1e-6, "cfg3 norm")
+    got, want = run_row_op(emel, kern, oracle_lib, "sum_rows", x, ne)
+    close(got, want, 1e-6, "cfg3 sum_rows")
+
+
+# ---- config 4 ----------------------------------------------------------------
+def test_cfg4a_masked_scaled_softmax_full_size(emel, kern, oracle_lib):
+    from emel_rs_b200 import workloads
+    scores, mask = workloads.cfg4a()
+    kv, q, h = workloads.CFG4A_NE
+    got, want = run_row_op(emel, kern, oracle_lib, "soft_max_ext", scores, [kv, q, h, 1],
+                           mask=(mask, [kv, q, 1, 1], None), scale=float(workloads.CFG4A_SCALE))
+    close(got, want, 1e-30, "cfg4a soft_max_ext")
+    # masked positions are exactly zero
+    m = np.broadcast_to(mask[None].astype(np.float32), scores.shape).ravel()
+    assert np.all(got[np.isneginf(m)] == 0.0)
+
+
+def test_cfg4b_vocab_softmax_and_argmax_full_size(emel, kern, oracle_lib):
+    from emel_rs_b200 import workloads
+    logits, cols = workloads.cfg4b()
+    v, rows = workloads.CFG4B_NE
+    got, want = run_row_op(emel, kern, oracle_lib, "soft_max", logits, [v, rows, 1, 1])
+    close(got, want, 1e-30, "cfg4b soft_max")
+    for dt in (np.int64, np.int32, np.float32):
+        got, want = run_row_op(emel, kern, oracle_lib, "argmax_rows", logits, [v, rows, 1, 1], out_dtype=dt)
+        assert np.array_equal(got, want), f"cfg4b argmax_rows {np.dtype(dt).name}"
+        assert np.array_equal(got.astype(np.int64), cols)
+
+
+def test_argmax_rows_ties_and_nans(emel, kern, oracle_lib):
+    x = np.array([1, 5, 5, 2,   # tie -> first
+                  np.nan, 9, 9, 1,  # NaN first -> 0
+                  -np.inf, -np.inf, -np.inf, -np.inf,  # all equal -> 0
+                  0, np.nan, 3, 3], dtype=np.float32)  # NaN skipped
+    got, want = run_row_op(emel, kern, oracle_lib, "argmax_rows", x, [4, 4, 1, 1], out_dtype=np.int64)
+    assert got.tolist() == want.tolist() == [1, 0, 0, 2]
+
+
+def test_mask_broadcast_over_heads_with_f32_mask(emel, kern, oracle_lib):
+    rng = np.random.default_rng(31)
+    kv, q, h = 256, 16, 4
+    x = rng.standard_normal(kv * q * h).astype(np.float32)
+    mask = np.where(rng.random((q + 3) * kv) < 0.2, -np.inf, rng.standard_normal((q + 3) * kv)).astype(np.float32)
+    got, want = run_row_op(emel, kern, oracle_lib, "soft_max_ext", x, [kv, q, h, 1],
+                           mask=(mask, [kv, q + 3, 1, 1], None), scale=0.37)
+    close(got, want, 1e-30, "softmax f32 mask with extra rows")
