@@ -142,7 +142,7 @@ class Cfg2Step:
     its input so one step touches ~705 MB (5.6x the 126 MB L2): no input is
     still in L2 when it is read again a step later."""
 
-    def __init__(self, pkg, ctx, torch, device, seed):
+    def __init__(self, pkg, ctx, torch, device, seed, only=None):
         from emel_rs_b200 import workloads
         self.pkg, self.ctx = pkg, ctx
         x, xa = workloads.cfg2(seed)
@@ -155,6 +155,8 @@ class Cfg2Step:
         for dt_name, code, tdt in (("f32", 0, torch.float32), ("f16", 1, torch.float16)):
             base, base_abs = (torch.from_numpy(a).to(device) for a in self.host[dt_name])
             for name, op in OPS:
+                if only and f"{name}_{dt_name}" not in only:
+                    continue
                 src = (base_abs if name in ("sqrt", "pow2") else base).clone()
                 dst = torch.empty_like(src)
                 self.tensors += [src, dst]
@@ -177,15 +179,23 @@ class Cfg2Step:
         return v
 
     def run(self, stream, events=None):
+        """Issues the 16 launches on `stream`; with `events` (17 of them),
+        an event before each launch and one after the last."""
         h = self.ctx.handle
         for i, (_, _, fn, args, _) in enumerate(self.launches):
             if events is not None:
-                events[i][0].record()
+                events[i].record(stream)
             st = fn(h, stream, *args)
-            if events is not None:
-                events[i][1].record()
             if st != 0:
                 raise RuntimeError(f"launch {self.launches[i][0]} failed: {st} {self.ctx.last_error}")
+        if events is not None:
+            events[-1].record(stream)
+
+    def capture(self, stream, events=None):
+        g = self.pkg.Graph(self.ctx, stream)
+        with g:
+            self.run(stream.handle, events)
+        return g
 
 
 def run_b200(args, world, rank, local):
@@ -199,48 +209,60 @@ def run_b200(args, world, rank, local):
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
     pkg = load_package()
     ctx = pkg.Context(local)
-    step = Cfg2Step(pkg, ctx, torch, device, seed=2 + 1000 * rank)
-    stream = torch.cuda.current_stream(device)
-    sh = ctypes.c_void_p(stream.cuda_stream)
+    only = set(args.only.split(",")) if args.only else None
+    step = Cfg2Step(pkg, ctx, torch, device, seed=2 + 1000 * rank, only=only)
+    torch.cuda.synchronize()
+    stream = pkg.Stream(ctx)
+    sh = stream.handle
+
+    # The step is captured once as a CUDA graph; a few more captures carry
+    # event-record nodes between the kernels and are replayed at spread-out
+    # positions of the timed region to time each kernel in place.
+    plain = step.capture(stream)
+    n_timed = min(8, args.steps)
+    timed = []
+    for _ in range(n_timed):
+        evs = [pkg.CudaEvent(ctx) for _ in range(len(step.launches) + 1)]
+        timed.append((step.capture(stream, evs), evs))
+    at = {int(round(j * args.steps / n_timed)): j for j in range(n_timed)}
 
     for _ in range(args.warmup):
-        step.run(sh)
-    torch.cuda.synchronize()
-
-    # per-op events on a spread-out subset of the timed steps
-    sample_every = max(1, args.steps // 64)
-    sampled = list(range(0, args.steps, sample_every))
-    ev = {s: [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in step.launches] for s in sampled}
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        plain.launch()
+    stream.synchronize()
+    t0, t1 = pkg.CudaEvent(ctx), pkg.CudaEvent(ctx)
     launches_before = ctx.launches
     if world > 1:
         dist.barrier()
-    torch.cuda.synchronize()
+    stream.synchronize()
     with ClockSampler(local) as clocks:
-        t0.record()
+        t0.record(sh)
         for s in range(args.steps):
-            step.run(sh, ev.get(s))
-        t1.record()
-        torch.cuda.synchronize()
+            if s in at:
+                timed[at[s]][0].launch()
+            else:
+                plain.launch()
+        t1.record(sh)
+        stream.synchronize()
     if world > 1:
         dist.barrier()
     gpu_launches = ctx.launches - launches_before
-    ms = t0.elapsed_time(t1)
+    ms = t0.elapsed_ms(t1)
     ms_t = torch.tensor([ms], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms_max = float(ms_t.item())
 
-    # per-op average durations over the sampled steps
+    # per-kernel average durations over the timed replays
     per_op = {}
     for i, (name, nbytes, *_rest) in enumerate(step.launches):
-        d = [ev[s][i][0].elapsed_time(ev[s][i][1]) for s in sampled]
+        d = [evs[i].elapsed_ms(evs[i + 1]) for _, evs in timed]
         per_op[name] = (nbytes, statistics.mean(d))
-    dom = max(per_op.items(), key=lambda kv: kv[1][1])
-    dom_name, (dom_bytes, dom_ms) = dom
+    # the dominant kernel: the unary instantiation with the largest share of
+    # step time (all 16 launches are the same ew_flat streaming kernel)
+    dom_name, (dom_bytes, dom_ms) = max(per_op.items(), key=lambda kv: kv[1][1])
+    kernel_ms = sum(t for _, t in per_op.values())
 
-    e2e = run_e2e(args, pkg, ctx, torch, step, stream, sh, world)
+    e2e = None if args.no_e2e else run_e2e(args, pkg, ctx, torch, step, stream, world)
 
     if rank != 0:
         if world > 1:
@@ -264,7 +286,8 @@ def run_b200(args, world, rank, local):
         "roofline": {"bound": "hbm", "kernel": f"ew_flat ({dom_name})", "achieved": round(achieved, 1),
                      "peak": peak, "peak_source": f"{peak_kind} hbm_gbs", "unit": "GB/s",
                      "frac": round(achieved / peak, 4), "traffic": traffic,
-                     "algorithmic_bytes_per_launch": dom_bytes},
+                     "algorithmic_bytes_per_launch": dom_bytes, "launch_ms": round(dom_ms, 5),
+                     "share_of_step": round(dom_ms / kernel_ms, 4)},
         "per_op_gbs": {k: round(b / (t / 1e3) / 1e9, 1) for k, (b, t) in per_op.items()},
         "e2e": e2e,
         "gpu_launches": gpu_launches,
@@ -277,16 +300,18 @@ def run_b200(args, world, rank, local):
         dist.destroy_process_group()
 
 
-def run_e2e(args, pkg, ctx, torch, step, stream, sh, world):
+def run_e2e(args, pkg, ctx, torch, step, stream, world):
     """The same metric through the C ABI with host buffers: every step copies
     the four source tensors from pinned host memory, runs the 16 ops and
-    reads all 16 outputs back."""
+    reads all 16 outputs back (captured once, replayed per step)."""
     lib = pkg.lib()
+    sh = stream.handle
+    device = torch.device("cuda", ctx.device)
     srcs = []  # (pinned host, device tensor)
     for dt_name in ("f32", "f16"):
         for arr in step.host[dt_name]:
             h = torch.from_numpy(arr.copy()).pin_memory()
-            d = torch.empty_like(h, device=stream.device)
+            d = torch.empty_like(h, device=device)
             srcs.append((h, d))
     f32x, f32a, f16x, f16a = (d for _, d in srcs)
     outs = []
@@ -312,25 +337,30 @@ def run_e2e(args, pkg, ctx, torch, step, stream, sh, world):
         for h, d in outs:
             lib.emel_cuda_memcpy_d2h(ctx.handle, sh, h.data_ptr(), d.data_ptr(), h.numel() * h.element_size())
 
+    torch.cuda.synchronize()
+    g = pkg.Graph(ctx, stream)
+    with g:
+        one()
     steps = max(3, min(args.steps, 20))
     for _ in range(2):
-        one()
-    torch.cuda.synchronize()
-    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    t0.record()
+        g.launch()
+    stream.synchronize()
+    t0, t1 = pkg.CudaEvent(ctx), pkg.CudaEvent(ctx)
+    t0.record(sh)
     for _ in range(steps):
-        one()
-    t1.record()
-    torch.cuda.synchronize()
-    ms = t0.elapsed_time(t1)
+        g.launch()
+    t1.record(sh)
+    stream.synchronize()
+    ms = t0.elapsed_ms(t1)
     if world > 1:
         import torch.distributed as dist
-        m = torch.tensor([ms], dtype=torch.float64, device=stream.device)
+        m = torch.tensor([ms], dtype=torch.float64, device=device)
         dist.all_reduce(m, op=dist.ReduceOp.MAX)
         ms = float(m.item())
     value = world * steps * step.step_bytes / (ms / 1e3) / 1e9
     return {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
-            "steps": steps, "path": "emel_cuda_memcpy_h2d + emel_cuda_unary x16 + emel_cuda_memcpy_d2h (pinned host)"}
+            "steps": steps,
+            "path": "graph of emel_cuda_memcpy_h2d x4 + emel_cuda_unary x16 + emel_cuda_memcpy_d2h x16 (pinned host)"}
 
 
 # ---------------------------------------------------------------------------
@@ -453,6 +483,8 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--ref-seconds", type=float, default=60.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
+    ap.add_argument("--only", default="", help="comma list of ops to run, e.g. gelu_f32,relu_f16 (profiling)")
     args = ap.parse_args()
     world, rank, local = dist_env()
     if args.warmup < 3:

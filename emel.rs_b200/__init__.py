@@ -119,6 +119,14 @@ SIGNATURES = {
     "emel_cuda_stream_destroy": (_I, [_CTX, _V]),
     "emel_cuda_stream_synchronize": (_I, [_CTX, _V]),
     "emel_cuda_launch_count": (ctypes.c_uint64, [_CTX]),
+    "emel_cuda_event_create": (_I, [_CTX, ctypes.POINTER(_V)]),
+    "emel_cuda_event_record": (_I, [_CTX, _V, _V]),
+    "emel_cuda_event_elapsed_ms": (_I, [_CTX, _V, _V, ctypes.POINTER(ctypes.c_float)]),
+    "emel_cuda_event_destroy": (_I, [_CTX, _V]),
+    "emel_cuda_graph_begin": (_I, [_CTX, _V]),
+    "emel_cuda_graph_end": (_I, [_CTX, _V, ctypes.POINTER(_V)]),
+    "emel_cuda_graph_launch": (_I, [_CTX, _V, _V]),
+    "emel_cuda_graph_destroy": (_I, [_CTX, _V]),
     "emel_cuda_binary": (_I, [_CTX, _V, _I, _P, _P, _P]),
     "emel_cuda_broadcast_row": (_I, [_CTX, _V, _I, _P, _P, _P]),
     "emel_cuda_binary_repeat": (_I, [_CTX, _V, _I, _P, _P, _P]),
@@ -263,6 +271,70 @@ class Context:
 
     def synchronize(self, stream=None):
         _check(self._lib.emel_cuda_stream_synchronize(self.handle, stream), "stream synchronize")
+
+
+class Stream:
+    """A non-blocking stream created by the library (capturable)."""
+
+    def __init__(self, ctx: Context):
+        self.ctx = ctx
+        h = ctypes.c_void_p()
+        _check(ctx._lib.emel_cuda_stream_create(ctx.handle, ctypes.byref(h)), "stream create")
+        self.handle = h
+
+    def synchronize(self):
+        self.ctx.synchronize(self.handle)
+
+    def close(self):
+        if self.handle:
+            self.ctx._lib.emel_cuda_stream_destroy(self.ctx.handle, self.handle)
+            self.handle = None
+
+
+class CudaEvent:
+    """A timing event (emel_cuda_event_*)."""
+
+    def __init__(self, ctx: Context):
+        self.ctx = ctx
+        h = ctypes.c_void_p()
+        _check(ctx._lib.emel_cuda_event_create(ctx.handle, ctypes.byref(h)), "event create")
+        self.handle = h
+
+    def record(self, stream):
+        _check(self.ctx._lib.emel_cuda_event_record(self.ctx.handle, self.handle, stream), "event record")
+
+    def elapsed_ms(self, end: "CudaEvent") -> float:
+        ms = ctypes.c_float()
+        _check(self.ctx._lib.emel_cuda_event_elapsed_ms(self.ctx.handle, self.handle, end.handle, ctypes.byref(ms)),
+               "event elapsed")
+        return ms.value
+
+
+class Graph:
+    """Captures every entry point called on `stream` inside the `with` block
+    into one CUDA graph; launch() replays it."""
+
+    def __init__(self, ctx: Context, stream: Stream):
+        self.ctx, self.stream, self.handle = ctx, stream, None
+
+    def __enter__(self):
+        _check(self.ctx._lib.emel_cuda_graph_begin(self.ctx.handle, self.stream.handle), "graph begin")
+        return self
+
+    def __exit__(self, exc_type, exc, tb):
+        h = ctypes.c_void_p()
+        st = self.ctx._lib.emel_cuda_graph_end(self.ctx.handle, self.stream.handle, ctypes.byref(h))
+        if exc_type is None:
+            _check(st, "graph end")
+        self.handle = h
+
+    def launch(self):
+        _check(self.ctx._lib.emel_cuda_graph_launch(self.ctx.handle, self.handle, self.stream.handle), "graph launch")
+
+    def close(self):
+        if self.handle:
+            self.ctx._lib.emel_cuda_graph_destroy(self.ctx.handle, self.handle)
+            self.handle = None
 
 
 class DeviceBuffer:

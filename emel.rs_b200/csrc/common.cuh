@@ -102,8 +102,11 @@ __device__ __forceinline__ float lm_log1p(float x) { return x86_nan1((float)log1
 __device__ __forceinline__ float lm_sin(float x) { return x86_nan1((float)sin((double)x), x); }
 __device__ __forceinline__ float lm_cos(float x) { return x86_nan1((float)cos((double)x), x); }
 
-// f32::clamp: both comparisons false for NaN, which passes through.
+// f32::clamp: both comparisons false for NaN, which passes through with its
+// payload.  The NaN test is on the integer bits so the compiler cannot fold
+// the selection into a NaN-canonicalising min/max.
 __device__ __forceinline__ float clamp_rs(float v, float lo, float hi) {
+    if (is_nan(v)) return v;
     if (v < lo) return lo;
     if (v > hi) return hi;
     return v;
@@ -160,8 +163,8 @@ __device__ __forceinline__ float unary_apply(float v, UnaryParams p) {
     if constexpr (OP == kSin) return lm_sin(v);
     if constexpr (OP == kCos) return lm_cos(v);
     if constexpr (OP == kScale) return f_mul(v, p.a);
-    if constexpr (OP == kClamp) return v < p.a ? p.a : (v > p.b ? p.b : v);
-    if constexpr (OP == kLeakyRelu) return v < 0.0f ? f_mul(v, p.a) : v;
+    if constexpr (OP == kClamp) return clamp_rs(v, p.a, p.b);
+    if constexpr (OP == kLeakyRelu) return is_nan(v) ? v : (v < 0.0f ? f_mul(v, p.a) : v);
     if constexpr (OP == kAdd1) return f_add(v, p.a);
     if constexpr (OP == kCopy) return v;
     return v;

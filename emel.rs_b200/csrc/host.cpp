@@ -466,6 +466,103 @@ emel_cuda_status emel_cuda_stream_synchronize(emel_cuda_context* ctx, void* stre
     return device_status(ctx, cudaStreamSynchronize((cudaStream_t)stream));
 }
 
+// ---- events and launch capture ---------------------------------------------
+
+emel_cuda_status emel_cuda_event_create(emel_cuda_context* ctx, void** out) {
+    if (ctx == nullptr || out == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    cudaEvent_t e = nullptr;
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = cudaEventCreate(&e);
+    *out = e;
+    return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_event_record(emel_cuda_context* ctx, void* event, void* stream) {
+    if (ctx == nullptr || event == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
+    cudaError_t err = cudaStreamIsCapturing((cudaStream_t)stream, &cap);
+    if (err == cudaSuccess) {
+        // inside a capture only an external record becomes a graph node
+        err = cap == cudaStreamCaptureStatusActive
+                  ? cudaEventRecordWithFlags((cudaEvent_t)event, (cudaStream_t)stream, cudaEventRecordExternal)
+                  : cudaEventRecord((cudaEvent_t)event, (cudaStream_t)stream);
+    }
+    return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_event_elapsed_ms(emel_cuda_context* ctx, void* start, void* end, float* ms) {
+    if (ctx == nullptr || start == nullptr || end == nullptr || ms == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    return device_status(ctx, cudaEventElapsedTime(ms, (cudaEvent_t)start, (cudaEvent_t)end));
+}
+
+emel_cuda_status emel_cuda_event_destroy(emel_cuda_context* ctx, void* event) {
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    return device_status(ctx, cudaEventDestroy((cudaEvent_t)event));
+}
+
+}  // extern "C"
+
+struct emel_cuda_graph {
+    cudaGraph_t graph;
+    cudaGraphExec_t exec;
+    uint64_t kernels;  // kernels captured: a replay launches this many
+};
+
+namespace {
+thread_local uint64_t capture_launch_base = 0;
+}
+
+extern "C" {
+
+emel_cuda_status emel_cuda_graph_begin(emel_cuda_context* ctx, void* stream) {
+    if (ctx == nullptr || stream == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = cudaStreamBeginCapture((cudaStream_t)stream, cudaStreamCaptureModeThreadLocal);
+    capture_launch_base = ctx->launches;
+    return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_graph_end(emel_cuda_context* ctx, void* stream, emel_cuda_graph** out) {
+    if (ctx == nullptr || stream == nullptr || out == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    *out = nullptr;
+    cudaGraph_t g = nullptr;
+    cudaError_t err = cudaStreamEndCapture((cudaStream_t)stream, &g);
+    // captured kernels did not run: the replay accounts for them
+    const uint64_t captured = ctx->launches - capture_launch_base;
+    ctx->launches = capture_launch_base;
+    if (err != cudaSuccess) return device_status(ctx, err);
+    cudaGraphExec_t exec = nullptr;
+    err = cudaGraphInstantiate(&exec, g, 0);
+    if (err != cudaSuccess) {
+        cudaGraphDestroy(g);
+        return device_status(ctx, err);
+    }
+    auto* h = new (std::nothrow) emel_cuda_graph{g, exec, captured};
+    if (h == nullptr) {
+        cudaGraphExecDestroy(exec);
+        cudaGraphDestroy(g);
+        return EMEL_CUDA_OUT_OF_MEMORY;
+    }
+    *out = h;
+    return EMEL_CUDA_OK;
+}
+
+emel_cuda_status emel_cuda_graph_launch(emel_cuda_context* ctx, emel_cuda_graph* graph, void* stream) {
+    if (ctx == nullptr || graph == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = cudaGraphLaunch(graph->exec, (cudaStream_t)stream);
+    if (err == cudaSuccess) ctx->launches += graph->kernels;
+    return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_graph_destroy(emel_cuda_context* ctx, emel_cuda_graph* graph) {
+    if (ctx == nullptr || graph == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    cudaError_t err = cudaGraphExecDestroy(graph->exec);
+    cudaError_t err2 = cudaGraphDestroy(graph->graph);
+    delete graph;
+    return device_status(ctx, err != cudaSuccess ? err : err2);
+}
+
 // ---- binary family ---------------------------------------------------------
 
 emel_cuda_status emel_cuda_binary(emel_cuda_context* ctx, void* stream, int op, const emel_tensor_view* lhs,

@@ -137,8 +137,30 @@ EMEL_CUDA_API emel_cuda_status emel_cuda_memset(emel_cuda_context* ctx, void* st
 EMEL_CUDA_API emel_cuda_status emel_cuda_stream_create(emel_cuda_context* ctx, void** out);
 EMEL_CUDA_API emel_cuda_status emel_cuda_stream_destroy(emel_cuda_context* ctx, void* stream);
 EMEL_CUDA_API emel_cuda_status emel_cuda_stream_synchronize(emel_cuda_context* ctx, void* stream);
-/* Number of kernels this context has launched (all entry points). */
+/* Number of kernels this context has launched (all entry points; a graph
+ * replay counts the kernels it contains). */
 EMEL_CUDA_API uint64_t emel_cuda_launch_count(const emel_cuda_context* ctx);
+
+/* Timing events.  Recorded on a stream that is being captured, an event
+ * becomes an event-record node of the graph, so kernels inside a replayed
+ * graph can be timed.  No counterpart in the reference (it has no device). */
+EMEL_CUDA_API emel_cuda_status emel_cuda_event_create(emel_cuda_context* ctx, void** out);
+EMEL_CUDA_API emel_cuda_status emel_cuda_event_record(emel_cuda_context* ctx, void* event, void* stream);
+EMEL_CUDA_API emel_cuda_status emel_cuda_event_elapsed_ms(emel_cuda_context* ctx, void* start, void* end, float* ms);
+EMEL_CUDA_API emel_cuda_status emel_cuda_event_destroy(emel_cuda_context* ctx, void* event);
+
+/* Launch capture: every entry point called on `stream` between begin and
+ * end is recorded (validated immediately, launched only on replay) into a
+ * CUDA graph that emel_cuda_graph_launch replays with one host call.  This
+ * is the device-side form of a fixed operator schedule such as an
+ * emel-graph processor step (crates/emel-graph/src/processor/sm.rs:159-199).
+ * `stream` must be a stream from emel_cuda_stream_create (not the legacy
+ * default stream).  No counterpart in the reference. */
+typedef struct emel_cuda_graph emel_cuda_graph;
+EMEL_CUDA_API emel_cuda_status emel_cuda_graph_begin(emel_cuda_context* ctx, void* stream);
+EMEL_CUDA_API emel_cuda_status emel_cuda_graph_end(emel_cuda_context* ctx, void* stream, emel_cuda_graph** out);
+EMEL_CUDA_API emel_cuda_status emel_cuda_graph_launch(emel_cuda_context* ctx, emel_cuda_graph* graph, void* stream);
+EMEL_CUDA_API emel_cuda_status emel_cuda_graph_destroy(emel_cuda_context* ctx, emel_cuda_graph* graph);
 
 /* ---- binary family --------------------------------------------------- */
 

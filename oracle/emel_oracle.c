@@ -16,6 +16,22 @@
 
 typedef unsigned __int128 u128;
 
+/* The reference's f32 libm calls.  By default they are the host's glibc
+ * float functions (what Rust's f32::exp etc. call on Linux).  Built with
+ * -DORACLE_CR_LIBM they are evaluated in binary64 and rounded once, i.e. the
+ * reference loops running on a platform whose float libm is correctly
+ * rounded (as glibc's newer float functions are): the device kernels, which
+ * evaluate the same way, must match that build bit for bit. */
+#ifdef ORACLE_CR_LIBM
+#define expf(x) ((float)exp((double)(x)))
+#define expm1f(x) ((float)expm1((double)(x)))
+#define tanhf(x) ((float)tanh((double)(x)))
+#define log1pf(x) ((float)log1p((double)(x)))
+#define logf(x) ((float)log((double)(x)))
+#define sinf(x) ((float)sin((double)(x)))
+#define cosf(x) ((float)cos((double)(x)))
+#endif
+
 enum { DT_F32 = 0, DT_F16 = 1, DT_I32 = 26, DT_I64 = 27 };
 
 /* ---------------------------------------------------------------------- */

@@ -13,6 +13,7 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "liboracle.so"
+CR_LIB_PATH = HERE / "liboracle_cr.so"  # libm calls evaluated in binary64, rounded once
 
 DTYPE_CODE = {np.dtype(np.float32): 0, np.dtype(np.float16): 1, np.dtype(np.int32): 26, np.dtype(np.int64): 27}
 
@@ -52,20 +53,22 @@ def host_view(array, ne=None, nb=None):
     return make_view(array.ctypes.data, array.nbytes, ne, nb, code)
 
 
-_lib = None
+_libs = {}
 
 
 def build():
     subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
 
 
-def load():
-    global _lib
-    if _lib is not None:
-        return _lib
-    if not LIB_PATH.exists():
+def load(cr=False):
+    """The oracle with the host's glibc float libm (default), or with
+    correctly rounded libm calls (cr=True)."""
+    if cr in _libs:
+        return _libs[cr]
+    path = CR_LIB_PATH if cr else LIB_PATH
+    if not path.exists():
         build()
-    lib = ctypes.CDLL(str(LIB_PATH))
+    lib = ctypes.CDLL(str(path))
     P = ctypes.POINTER(View)
     sigs = {
         "oracle_binary": [ctypes.c_int, P, P, P],
@@ -104,5 +107,5 @@ def load():
     lib.oracle_fp32_to_fp16.restype = ctypes.c_uint16
     lib.oracle_fp16_to_fp32.argtypes = [ctypes.c_uint16]
     lib.oracle_fp16_to_fp32.restype = ctypes.c_float
-    _lib = lib
+    _libs[cr] = lib
     return lib
