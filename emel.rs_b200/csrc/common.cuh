@@ -19,6 +19,7 @@
 #include <cuda_fp16.h>
 #include <cstdint>
 
+#include "fastmath.cuh"
 #include "plan.hpp"
 
 namespace emel {
@@ -94,9 +95,11 @@ struct UnaryParams {
 };
 
 // One libm call of the reference evaluated as binary64 and rounded once.
-__device__ __forceinline__ float lm_exp(float x) { return x86_nan1((float)exp((double)x), x); }
-__device__ __forceinline__ float lm_expm1(float x) { return x86_nan1((float)expm1((double)x), x); }
-__device__ __forceinline__ float lm_tanh(float x) { return x86_nan1((float)tanh((double)x), x); }
+// exp / expm1 / tanh use the table-driven binary64 core (fastmath.cuh);
+// log, log1p, sin and cos call CUDA's binary64 functions.
+__device__ __forceinline__ float lm_exp(float x) { return x86_nan1(fast_expf(x), x); }
+__device__ __forceinline__ float lm_expm1(float x) { return x86_nan1(fast_expm1f(x), x); }
+__device__ __forceinline__ float lm_tanh(float x) { return x86_nan1(fast_tanhf(x), x); }
 __device__ __forceinline__ float lm_log(float x) { return x86_nan1((float)log((double)x), x); }
 __device__ __forceinline__ float lm_log1p(float x) { return x86_nan1((float)log1p((double)x), x); }
 __device__ __forceinline__ float lm_sin(float x) { return x86_nan1((float)sin((double)x), x); }

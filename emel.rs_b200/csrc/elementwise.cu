@@ -49,11 +49,53 @@ struct SiluBackFn {
 };
 
 template <typename T, typename F>
-__device__ __forceinline__ Vec16<T> apply_vec(const F& f, const Vec16<T>& a, const Vec16<T>& b) {
+__device__ __forceinline__ Vec16<T> apply_vec_scalar(const F& f, const Vec16<T>& a, const Vec16<T>& b) {
     Vec16<T> r;
 #pragma unroll
     for (int k = 0; k < Vec16<T>::N; ++k) vset(r, k, f(vget(a, k), F::kBinary ? vget(b, k) : 0.0f));
     return r;
+}
+
+// True when any of the eight binary16 lanes of `v` is a NaN.
+__device__ __forceinline__ bool any_nan_h8(const Vec16<uint16_t>& v) {
+    const uint4 u = *reinterpret_cast<const uint4*>(&v);
+    const unsigned m = __vcmpgtu2(u.x & 0x7fff7fffu, 0x7c007c00u) | __vcmpgtu2(u.y & 0x7fff7fffu, 0x7c007c00u) |
+                       __vcmpgtu2(u.z & 0x7fff7fffu, 0x7c007c00u) | __vcmpgtu2(u.w & 0x7fff7fffu, 0x7c007c00u);
+    return m != 0;
+}
+
+template <typename T, typename F>
+__device__ __forceinline__ Vec16<T> apply_vec(const F& f, const Vec16<T>& a, const Vec16<T>& b) {
+    if constexpr (sizeof(T) == 2) {
+        // binary16: NaN-free vectors convert lanes in pairs (cvt.f32.f16 /
+        // cvt.rn.f16x2.f32); any NaN in or out takes the per-lane path that
+        // applies the reference's NaN encodings.
+        if (!any_nan_h8(a) && !(F::kBinary && any_nan_h8(b))) {
+            const uint4 ua = *reinterpret_cast<const uint4*>(&a);
+            const uint4 ub = *reinterpret_cast<const uint4*>(&b);
+            const unsigned wa[4] = {ua.x, ua.y, ua.z, ua.w};
+            const unsigned wb[4] = {ub.x, ub.y, ub.z, ub.w};
+            unsigned wr[4];
+            bool nan_out = false;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float2 xa = __half22float2(*reinterpret_cast<const __half2*>(&wa[k]));
+                float2 xb = make_float2(0.0f, 0.0f);
+                if constexpr (F::kBinary) xb = __half22float2(*reinterpret_cast<const __half2*>(&wb[k]));
+                const float r0 = f(xa.x, xb.x);
+                const float r1 = f(xa.y, xb.y);
+                nan_out |= is_nan(r0) | is_nan(r1);
+                const __half2 h = __floats2half2_rn(r0, r1);
+                wr[k] = *reinterpret_cast<const unsigned*>(&h);
+            }
+            if (!nan_out) {
+                Vec16<T> r;
+                *reinterpret_cast<uint4*>(&r) = make_uint4(wr[0], wr[1], wr[2], wr[3]);
+                return r;
+            }
+        }
+    }
+    return apply_vec_scalar<T>(f, a, b);
 }
 
 template <typename T, typename F>

@@ -1,0 +1,20 @@
+"""The device exponential core (fastmath.cuh) compiled for the host: its
+exp / expm1 / tanh equal binary64 libm rounded once to binary32 (the
+correctly-rounded-libm oracle's definition) on a strided sweep of every
+binary32 with |x| <= 90, allowing at most a handful of 1-ulp ties."""
+
+import subprocess
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def test_fast_exponential_core_matches_binary64_libm(tmp_path):
+    exe = tmp_path / "fastmath_check"
+    subprocess.run(["g++", "-O2", "-std=c++17", "-ffp-contract=off", "-I", str(ROOT / "emel.rs_b200" / "csrc"),
+                    str(ROOT / "tests" / "cpp" / "fastmath_check.cpp"), "-o", str(exe), "-lm"], check=True)
+    out = subprocess.run([str(exe), "1009"], capture_output=True, text=True, check=True).stdout.split()
+    n, d_exp, d_expm1, d_tanh, worst = map(int, out)
+    assert n > 1_000_000
+    assert d_exp <= 2 and d_expm1 <= 2 and d_tanh <= 2, out
+    assert worst <= 1, out
