@@ -115,46 +115,72 @@ __device__ __forceinline__ float clamp_rs(float v, float lo, float hi) {
     return v;
 }
 
-template <int OP>
-__device__ __forceinline__ float unary_apply(float v, UnaryParams p) {
+// Arithmetic policy for the formulas.  Exact = the reference's x86 NaN
+// semantics on every operation; Fast = plain IEEE operations.  The two agree
+// bit for bit on every non-NaN result (NaN payloads are the only difference,
+// and a selection on a NaN intermediate does not depend on its payload), so
+// the heavy formulas run Fast and recompute Exact only when the result is NaN.
+template <bool EXACT>
+struct Arith {
+    static __device__ __forceinline__ float add(float a, float b) { return EXACT ? f_add(a, b) : __fadd_rn(a, b); }
+    static __device__ __forceinline__ float sub(float a, float b) { return EXACT ? f_sub(a, b) : __fsub_rn(a, b); }
+    static __device__ __forceinline__ float mul(float a, float b) { return EXACT ? f_mul(a, b) : __fmul_rn(a, b); }
+    static __device__ __forceinline__ float div(float a, float b) { return EXACT ? f_div(a, b) : __fdiv_rn(a, b); }
+    static __device__ __forceinline__ float exp(float x) { return EXACT ? lm_exp(x) : fast_expf(x); }
+    static __device__ __forceinline__ float expm1(float x) { return EXACT ? lm_expm1(x) : fast_expm1f(x); }
+    static __device__ __forceinline__ float tanh(float x) { return EXACT ? lm_tanh(x) : fast_tanhf(x); }
+    static __device__ __forceinline__ float log1p(float x) { return EXACT ? lm_log1p(x) : (float)log1p((double)x); }
+    // fp16_to_f32(fp32_to_fp16(v)) (unary.rs:533,539)
+    static __device__ __forceinline__ float round_f16(float v) {
+        return EXACT ? f16_bits_to_f32(f32_to_f16_bits(v)) : __half2float(__float2half_rn(v));
+    }
+    // Fast keeps "NaN in, NaN out" (any payload) so the exact recompute triggers.
+    static __device__ __forceinline__ float clamp(float v, float lo, float hi) {
+        return EXACT ? clamp_rs(v, lo, hi) : (v < lo ? lo : (v > hi ? hi : v));
+    }
+};
+
+template <int OP, bool EXACT>
+__device__ __forceinline__ float unary_formula(float v, UnaryParams p) {
+    using A = Arith<EXACT>;
     if constexpr (OP == kAbs) return f_abs(v);
     if constexpr (OP == kSgn) return is_nan(v) ? bitsf(0x7fc00000u) : bitsf((fbits(v) & 0x80000000u) | 0x3f800000u);
     if constexpr (OP == kNeg) return f_neg(v);
     if constexpr (OP == kStep) return v > 0.0f ? 1.0f : 0.0f;
-    if constexpr (OP == kTanh) return lm_tanh(v);
-    if constexpr (OP == kElu) return v >= 0.0f ? v : lm_expm1(v);
+    if constexpr (OP == kTanh) return A::tanh(v);
+    if constexpr (OP == kElu) return v >= 0.0f ? v : A::expm1(v);
     if constexpr (OP == kRelu) return v > 0.0f ? v : 0.0f;
-    if constexpr (OP == kSigmoid) return f_div(1.0f, f_add(1.0f, lm_exp(f_neg(v))));
+    if constexpr (OP == kSigmoid) return A::div(1.0f, A::add(1.0f, A::exp(f_neg(v))));
     if constexpr (OP == kGelu) {
         if (v <= -10.0f) return 0.0f;
         if (v >= 10.0f) return v;
-        const float q = f16_bits_to_f32(f32_to_f16_bits(v));
-        const float cube = f_mul(f_mul(f_mul(0.044715f, q), q), q);
-        const float inner = f_mul(0.7978846f, f_add(q, cube));
-        const float approx = f_mul(f_mul(0.5f, q), f_add(1.0f, lm_tanh(inner)));
-        return f16_bits_to_f32(f32_to_f16_bits(approx));
+        const float q = A::round_f16(v);
+        const float cube = A::mul(A::mul(A::mul(0.044715f, q), q), q);
+        const float inner = A::mul(0.7978846f, A::add(q, cube));
+        const float approx = A::mul(A::mul(0.5f, q), A::add(1.0f, A::tanh(inner)));
+        return A::round_f16(approx);
     }
     if constexpr (OP == kGeluQuick) {
-        const float inner = f_mul(f_mul(0.7978846f, v), f_add(1.0f, f_mul(f_mul(0.044715f, v), v)));
-        return f_mul(f_mul(0.5f, v), f_add(1.0f, lm_tanh(inner)));
+        const float inner = A::mul(A::mul(0.7978846f, v), A::add(1.0f, A::mul(A::mul(0.044715f, v), v)));
+        return A::mul(A::mul(0.5f, v), A::add(1.0f, A::tanh(inner)));
     }
-    if constexpr (OP == kSilu) return f_div(v, f_add(1.0f, lm_exp(f_neg(v))));
-    if constexpr (OP == kHardswish) return f_div(f_mul(v, clamp_rs(f_add(v, 3.0f), 0.0f, 6.0f)), 6.0f);
-    if constexpr (OP == kHardsigmoid) return f_div(clamp_rs(f_add(v, 3.0f), 0.0f, 6.0f), 6.0f);
-    if constexpr (OP == kExp) return lm_exp(v);
-    if constexpr (OP == kExpm1) return lm_expm1(v);
-    if constexpr (OP == kSoftplus) return lm_log1p(lm_exp(v));
+    if constexpr (OP == kSilu) return A::div(v, A::add(1.0f, A::exp(f_neg(v))));
+    if constexpr (OP == kHardswish) return A::div(A::mul(v, A::clamp(A::add(v, 3.0f), 0.0f, 6.0f)), 6.0f);
+    if constexpr (OP == kHardsigmoid) return A::div(A::clamp(A::add(v, 3.0f), 0.0f, 6.0f), 6.0f);
+    if constexpr (OP == kExp) return A::exp(v);
+    if constexpr (OP == kExpm1) return A::expm1(v);
+    if constexpr (OP == kSoftplus) return A::log1p(A::exp(v));
     if constexpr (OP == kGeluErf) {
         const float sign = v < 0.0f ? -1.0f : 1.0f;
-        const float x = f_div(f_abs(v), 1.41421356237309504880f);
-        const float t = f_div(1.0f, f_add(1.0f, f_mul(0.3275911f, x)));
-        float poly = f_sub(f_mul(1.0614054f, t), 1.4531521f);
-        poly = f_add(f_mul(poly, t), 1.4214138f);
-        poly = f_sub(f_mul(poly, t), 0.28449672f);
-        poly = f_add(f_mul(poly, t), 0.2548296f);
-        poly = f_mul(poly, t);
-        const float erf = f_mul(sign, f_sub(1.0f, f_mul(poly, lm_exp(f_mul(f_neg(x), x)))));
-        return f_mul(f_mul(0.5f, v), f_add(1.0f, erf));
+        const float x = A::div(f_abs(v), 1.41421356237309504880f);
+        const float t = A::div(1.0f, A::add(1.0f, A::mul(0.3275911f, x)));
+        float poly = A::sub(A::mul(1.0614054f, t), 1.4531521f);
+        poly = A::add(A::mul(poly, t), 1.4214138f);
+        poly = A::sub(A::mul(poly, t), 0.28449672f);
+        poly = A::add(A::mul(poly, t), 0.2548296f);
+        poly = A::mul(poly, t);
+        const float erf = A::mul(sign, A::sub(1.0f, A::mul(poly, A::exp(A::mul(f_neg(x), x)))));
+        return A::mul(A::mul(0.5f, v), A::add(1.0f, erf));
     }
     if constexpr (OP == kFloor) return x86_nan1(floorf(v), v);
     if constexpr (OP == kCeil) return x86_nan1(ceilf(v), v);
@@ -171,6 +197,22 @@ __device__ __forceinline__ float unary_apply(float v, UnaryParams p) {
     if constexpr (OP == kAdd1) return f_add(v, p.a);
     if constexpr (OP == kCopy) return v;
     return v;
+}
+
+template <int OP>
+constexpr bool kHeavyFormula = OP == kTanh || OP == kElu || OP == kSigmoid || OP == kGelu || OP == kGeluQuick ||
+                               OP == kSilu || OP == kHardswish || OP == kHardsigmoid || OP == kExp || OP == kExpm1 ||
+                               OP == kSoftplus || OP == kGeluErf;
+
+template <int OP>
+__device__ __forceinline__ float unary_apply(float v, UnaryParams p) {
+    if constexpr (kHeavyFormula<OP>) {
+        const float r = unary_formula<OP, false>(v, p);
+        if (!is_nan(r)) return r;
+        return unary_formula<OP, true>(v, p);
+    } else {
+        return unary_formula<OP, true>(v, p);
+    }
 }
 
 // ---------------------------------------------------------------------------

@@ -42,11 +42,14 @@ static __device__ const double kExpT[64] = {EMEL_EXP_TABLE_VALUES};
 #endif
 static const double kExpTHost[64] = {EMEL_EXP_TABLE_VALUES};
 
-EMEL_HD int nearest_int(double x) {
+// Low 32 bits of a binary64's encoding.
+EMEL_HD int low_word(double x) {
 #if defined(__CUDA_ARCH__)
-    return __double2int_rn(x);
+    return __double2loint(x);
 #else
-    return (int)std::nearbyint(x);
+    unsigned long long u;
+    std::memcpy(&u, &x, 8);
+    return (int)(unsigned)(u & 0xffffffffull);
 #endif
 }
 
@@ -68,10 +71,15 @@ EMEL_HD double exp_table(int j) {
 #endif
 }
 
-// Returns s = 2^k T[j] and p = expm1(r) for |z| <= 200.
+// Returns s = 2^k T[j] and p = expm1(r) for |z| <= 200.  n = nearest(z*64/ln2)
+// comes from adding 1.5 * 2^52 (where the binary64 spacing is 1): the low
+// word of the sum is n and subtracting the constant back is exact, so no
+// float<->int conversion is issued.
 EMEL_HD void exp_split(double z, double& s, double& p) {
-    const int n = nearest_int(z * kExpInvL);
-    const double nd = (double)n;
+    constexpr double kShift = 0x1.8p52;
+    const double t = std::fma(z, kExpInvL, kShift);
+    const int n = low_word(t);
+    const double nd = t - kShift;
     double r = std::fma(-nd, kExpLhi, z);
     r = std::fma(-nd, kExpLlo, r);
     double q = std::fma(r, 1.0 / 720.0, 1.0 / 120.0);
