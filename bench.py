@@ -197,6 +197,26 @@ class Cfg2Step:
             self.run(stream.handle, events)
         return g
 
+    def calibration_graphs(self, stream):
+        """One graph per op: the op over every buffer pair of its dtype, back
+        to back, between two events.  Returns (name, bytes, reps, graph, e0, e1)."""
+        out = []
+        h = self.ctx.handle
+        for name, nbytes, fn, args, (sv, dv) in self.launches:
+            dt = name.rsplit("_", 1)[1]
+            pairs = [views for nm, _, _, _, views in self.launches if nm.rsplit("_", 1)[1] == dt]
+            e0, e1 = self.pkg.CudaEvent(self.ctx), self.pkg.CudaEvent(self.ctx)
+            g = self.pkg.Graph(self.ctx, stream)
+            with g:
+                e0.record(stream.handle)
+                for psv, pdv in pairs:
+                    st = fn(h, stream.handle, args[0], ctypes.byref(psv), ctypes.byref(pdv))
+                    if st != 0:
+                        raise RuntimeError(self.ctx.last_error)
+                e1.record(stream.handle)
+            out.append((name, nbytes, len(pairs), g, e0, e1))
+        return out
+
 
 def run_b200(args, world, rank, local):
     import torch
@@ -215,16 +235,9 @@ def run_b200(args, world, rank, local):
     stream = pkg.Stream(ctx)
     sh = stream.handle
 
-    # The step is captured once as a CUDA graph; a few more captures carry
-    # event-record nodes between the kernels and are replayed at spread-out
-    # positions of the timed region to time each kernel in place.
+    # The step is captured once as a CUDA graph and replayed K times.
     plain = step.capture(stream)
-    n_timed = min(8, args.steps)
-    timed = []
-    for _ in range(n_timed):
-        evs = [pkg.CudaEvent(ctx) for _ in range(len(step.launches) + 1)]
-        timed.append((step.capture(stream, evs), evs))
-    at = {int(round(j * args.steps / n_timed)): j for j in range(n_timed)}
+    calib = step.calibration_graphs(stream)
 
     for _ in range(args.warmup):
         plain.launch()
@@ -237,28 +250,34 @@ def run_b200(args, world, rank, local):
     with ClockSampler(local) as clocks:
         t0.record(sh)
         for s in range(args.steps):
-            if s in at:
-                timed[at[s]][0].launch()
-            else:
-                plain.launch()
+            plain.launch()
         t1.record(sh)
         stream.synchronize()
+        gpu_launches = ctx.launches - launches_before
+        # Per-kernel durations, right after the timed region on the same
+        # stream: each op runs 8 times back to back over 8 distinct buffer
+        # pairs of its dtype (117-235 MB, no L2 reuse) between one event pair.
+        # An event pair costs ~5 us inside a graph, so bracketing single
+        # launches would overstate short kernels; over 8 launches the bias is
+        # under 0.7 us per launch.
+        per_op = {}
+        for name, nbytes, reps, g, e0, e1 in calib:
+            d = []
+            for _ in range(3):
+                g.launch()
+                stream.synchronize()
+                d.append(e0.elapsed_ms(e1) / reps)
+            per_op[name] = (nbytes, statistics.median(d))
     if world > 1:
         dist.barrier()
-    gpu_launches = ctx.launches - launches_before
     ms = t0.elapsed_ms(t1)
     ms_t = torch.tensor([ms], dtype=torch.float64, device=device)
     if world > 1:
         dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
     ms_max = float(ms_t.item())
 
-    # per-kernel average durations over the timed replays
-    per_op = {}
-    for i, (name, nbytes, *_rest) in enumerate(step.launches):
-        d = [evs[i].elapsed_ms(evs[i + 1]) for _, evs in timed]
-        per_op[name] = (nbytes, statistics.mean(d))
-    # the dominant kernel: the unary instantiation with the largest share of
-    # step time (all 16 launches are the same ew_flat streaming kernel)
+    # the dominant kernel: the op with the largest share of the step's kernel
+    # time (all 16 launches are instantiations of the ew_flat streaming kernel)
     dom_name, (dom_bytes, dom_ms) = max(per_op.items(), key=lambda kv: kv[1][1])
     kernel_ms = sum(t for _, t in per_op.values())
 

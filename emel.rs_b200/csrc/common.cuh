@@ -129,7 +129,7 @@ struct Arith {
     static __device__ __forceinline__ float exp(float x) { return EXACT ? lm_exp(x) : fast_expf(x); }
     static __device__ __forceinline__ float expm1(float x) { return EXACT ? lm_expm1(x) : fast_expm1f(x); }
     static __device__ __forceinline__ float tanh(float x) { return EXACT ? lm_tanh(x) : fast_tanhf(x); }
-    static __device__ __forceinline__ float log1p(float x) { return EXACT ? lm_log1p(x) : (float)log1p((double)x); }
+    static __device__ __forceinline__ float log1p(float x) { return EXACT ? lm_log1p(x) : (float)::log1p((double)x); }
     // fp16_to_f32(fp32_to_fp16(v)) (unary.rs:533,539)
     static __device__ __forceinline__ float round_f16(float v) {
         return EXACT ? f16_bits_to_f32(f32_to_f16_bits(v)) : __half2float(__float2half_rn(v));
@@ -140,7 +140,7 @@ struct Arith {
     }
 };
 
-template <int OP, bool EXACT>
+template <int OP, bool EXACT, bool IN_F16 = false>
 __device__ __forceinline__ float unary_formula(float v, UnaryParams p) {
     using A = Arith<EXACT>;
     if constexpr (OP == kAbs) return f_abs(v);
@@ -154,11 +154,13 @@ __device__ __forceinline__ float unary_formula(float v, UnaryParams p) {
     if constexpr (OP == kGelu) {
         if (v <= -10.0f) return 0.0f;
         if (v >= 10.0f) return v;
-        const float q = A::round_f16(v);
+        // an f16 input is already binary16, and an f16 store rounds the
+        // output the same way: the fast path skips both round trips
+        const float q = (IN_F16 && !EXACT) ? v : A::round_f16(v);
         const float cube = A::mul(A::mul(A::mul(0.044715f, q), q), q);
         const float inner = A::mul(0.7978846f, A::add(q, cube));
         const float approx = A::mul(A::mul(0.5f, q), A::add(1.0f, A::tanh(inner)));
-        return A::round_f16(approx);
+        return (IN_F16 && !EXACT) ? approx : A::round_f16(approx);
     }
     if constexpr (OP == kGeluQuick) {
         const float inner = A::mul(A::mul(0.7978846f, v), A::add(1.0f, A::mul(A::mul(0.044715f, v), v)));
@@ -204,14 +206,15 @@ constexpr bool kHeavyFormula = OP == kTanh || OP == kElu || OP == kSigmoid || OP
                                OP == kSilu || OP == kHardswish || OP == kHardsigmoid || OP == kExp || OP == kExpm1 ||
                                OP == kSoftplus || OP == kGeluErf;
 
-template <int OP>
+// IN_F16: the value came from, and the result goes to, binary16 storage.
+template <int OP, bool IN_F16 = false>
 __device__ __forceinline__ float unary_apply(float v, UnaryParams p) {
     if constexpr (kHeavyFormula<OP>) {
-        const float r = unary_formula<OP, false>(v, p);
+        const float r = unary_formula<OP, false, IN_F16>(v, p);
         if (!is_nan(r)) return r;
-        return unary_formula<OP, true>(v, p);
+        return unary_formula<OP, true, IN_F16>(v, p);
     } else {
-        return unary_formula<OP, true>(v, p);
+        return unary_formula<OP, true, IN_F16>(v, p);
     }
 }
 

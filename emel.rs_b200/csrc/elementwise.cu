@@ -25,11 +25,11 @@ namespace {
 
 constexpr int kThreads = 256;
 
-template <int OP>
+template <int OP, bool IN_F16>
 struct UnaryFn {
     UnaryParams p;
     static constexpr bool kBinary = false;
-    __device__ __forceinline__ float operator()(float a, float) const { return unary_apply<OP>(a, p); }
+    __device__ __forceinline__ float operator()(float a, float) const { return unary_apply<OP, IN_F16>(a, p); }
 };
 
 template <int OP>
@@ -274,9 +274,8 @@ cudaError_t launch_ew(const LaunchEnv& env, const EwPlan& p, const F& f) {
 
 template <int OP>
 cudaError_t unary_typed(const LaunchEnv& env, const EwPlan& p, float pa, float pb) {
-    UnaryFn<OP> f{UnaryParams{pa, pb}};
-    if (p.dtype == DType::F16) return launch_ew<uint16_t>(env, p, f);
-    return launch_ew<float>(env, p, f);
+    if (p.dtype == DType::F16) return launch_ew<uint16_t>(env, p, UnaryFn<OP, true>{UnaryParams{pa, pb}});
+    return launch_ew<float>(env, p, UnaryFn<OP, false>{UnaryParams{pa, pb}});
 }
 
 template <int OP>
