@@ -121,8 +121,10 @@ SIGNATURES = {
     "emel_cuda_launch_count": (ctypes.c_uint64, [_CTX]),
     "emel_cuda_event_create": (_I, [_CTX, ctypes.POINTER(_V)]),
     "emel_cuda_event_record": (_I, [_CTX, _V, _V]),
+    "emel_cuda_event_record_timed": (_I, [_CTX, _V, _V]),
     "emel_cuda_event_elapsed_ms": (_I, [_CTX, _V, _V, ctypes.POINTER(ctypes.c_float)]),
     "emel_cuda_event_destroy": (_I, [_CTX, _V]),
+    "emel_cuda_stream_wait_event": (_I, [_CTX, _V, _V]),
     "emel_cuda_graph_begin": (_I, [_CTX, _V]),
     "emel_cuda_graph_end": (_I, [_CTX, _V, ctypes.POINTER(_V)]),
     "emel_cuda_graph_launch": (_I, [_CTX, _V, _V]),
@@ -285,6 +287,9 @@ class Stream:
     def synchronize(self):
         self.ctx.synchronize(self.handle)
 
+    def wait(self, event: "CudaEvent"):
+        _check(self.ctx._lib.emel_cuda_stream_wait_event(self.ctx.handle, self.handle, event.handle), "stream wait")
+
     def close(self):
         if self.handle:
             self.ctx._lib.emel_cuda_stream_destroy(self.ctx.handle, self.handle)
@@ -301,7 +306,12 @@ class CudaEvent:
         self.handle = h
 
     def record(self, stream):
+        """Plain record; inside a capture it is a dependency (fork / join)."""
         _check(self.ctx._lib.emel_cuda_event_record(self.ctx.handle, self.handle, stream), "event record")
+
+    def record_timed(self, stream):
+        """Inside a capture: an event-record node, for timing graph kernels."""
+        _check(self.ctx._lib.emel_cuda_event_record_timed(self.ctx.handle, self.handle, stream), "event record")
 
     def elapsed_ms(self, end: "CudaEvent") -> float:
         ms = ctypes.c_float()

@@ -206,13 +206,20 @@ constexpr bool kHeavyFormula = OP == kTanh || OP == kElu || OP == kSigmoid || OP
                                OP == kSilu || OP == kHardswish || OP == kHardsigmoid || OP == kExp || OP == kExpm1 ||
                                OP == kSoftplus || OP == kGeluErf;
 
+// The exact (NaN-payload) recompute is rare; keeping it out of line keeps
+// the hot loop small.
+template <int OP, bool IN_F16>
+__device__ __noinline__ float unary_exact_slow(float v, UnaryParams p) {
+    return unary_formula<OP, true, IN_F16>(v, p);
+}
+
 // IN_F16: the value came from, and the result goes to, binary16 storage.
 template <int OP, bool IN_F16 = false>
 __device__ __forceinline__ float unary_apply(float v, UnaryParams p) {
     if constexpr (kHeavyFormula<OP>) {
         const float r = unary_formula<OP, false, IN_F16>(v, p);
         if (!is_nan(r)) return r;
-        return unary_formula<OP, true, IN_F16>(v, p);
+        return unary_exact_slow<OP, IN_F16>(v, p);
     } else {
         return unary_formula<OP, true, IN_F16>(v, p);
     }

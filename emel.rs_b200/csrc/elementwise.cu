@@ -48,8 +48,19 @@ struct SiluBackFn {
     }
 };
 
+// Per-lane path (binary16 vectors with a NaN in or out take it rarely; f32
+// vectors always).  Out of line for binary16 so the packed loop stays small.
+template <typename T, typename F>
+__device__ __noinline__ Vec16<T> apply_vec_lanes(const F& f, const Vec16<T>& a, const Vec16<T>& b) {
+    Vec16<T> r;
+#pragma unroll
+    for (int k = 0; k < Vec16<T>::N; ++k) vset(r, k, f(vget(a, k), F::kBinary ? vget(b, k) : 0.0f));
+    return r;
+}
+
 template <typename T, typename F>
 __device__ __forceinline__ Vec16<T> apply_vec_scalar(const F& f, const Vec16<T>& a, const Vec16<T>& b) {
+    if constexpr (sizeof(T) == 2) return apply_vec_lanes<T>(f, a, b);
     Vec16<T> r;
 #pragma unroll
     for (int k = 0; k < Vec16<T>::N; ++k) vset(r, k, f(vget(a, k), F::kBinary ? vget(b, k) : 0.0f));

@@ -479,6 +479,11 @@ emel_cuda_status emel_cuda_event_create(emel_cuda_context* ctx, void** out) {
 
 emel_cuda_status emel_cuda_event_record(emel_cuda_context* ctx, void* event, void* stream) {
     if (ctx == nullptr || event == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    return device_status(ctx, cudaEventRecord((cudaEvent_t)event, (cudaStream_t)stream));
+}
+
+emel_cuda_status emel_cuda_event_record_timed(emel_cuda_context* ctx, void* event, void* stream) {
+    if (ctx == nullptr || event == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
     cudaError_t err = cudaStreamIsCapturing((cudaStream_t)stream, &cap);
     if (err == cudaSuccess) {
@@ -498,6 +503,11 @@ emel_cuda_status emel_cuda_event_elapsed_ms(emel_cuda_context* ctx, void* start,
 emel_cuda_status emel_cuda_event_destroy(emel_cuda_context* ctx, void* event) {
     if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
     return device_status(ctx, cudaEventDestroy((cudaEvent_t)event));
+}
+
+emel_cuda_status emel_cuda_stream_wait_event(emel_cuda_context* ctx, void* stream, void* event) {
+    if (ctx == nullptr || event == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    return device_status(ctx, cudaStreamWaitEvent((cudaStream_t)stream, (cudaEvent_t)event, 0));
 }
 
 }  // extern "C"

@@ -141,13 +141,19 @@ EMEL_CUDA_API emel_cuda_status emel_cuda_stream_synchronize(emel_cuda_context* c
  * replay counts the kernels it contains). */
 EMEL_CUDA_API uint64_t emel_cuda_launch_count(const emel_cuda_context* ctx);
 
-/* Timing events.  Recorded on a stream that is being captured, an event
- * becomes an event-record node of the graph, so kernels inside a replayed
- * graph can be timed.  No counterpart in the reference (it has no device). */
+/* Events.  emel_cuda_event_record on a stream being captured records a
+ * dependency (fork / join of graph branches); emel_cuda_event_record_timed
+ * there becomes an event-record node of the graph instead, so kernels
+ * inside a replayed graph can be timed.  Outside a capture both record
+ * normally.  No counterpart in the reference (it has no device). */
 EMEL_CUDA_API emel_cuda_status emel_cuda_event_create(emel_cuda_context* ctx, void** out);
 EMEL_CUDA_API emel_cuda_status emel_cuda_event_record(emel_cuda_context* ctx, void* event, void* stream);
+EMEL_CUDA_API emel_cuda_status emel_cuda_event_record_timed(emel_cuda_context* ctx, void* event, void* stream);
 EMEL_CUDA_API emel_cuda_status emel_cuda_event_elapsed_ms(emel_cuda_context* ctx, void* start, void* end, float* ms);
 EMEL_CUDA_API emel_cuda_status emel_cuda_event_destroy(emel_cuda_context* ctx, void* event);
+/* Makes `stream` wait for `event` (captured as a graph dependency: fork and
+ * join of independent branches).  No counterpart in the reference. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_stream_wait_event(emel_cuda_context* ctx, void* stream, void* event);
 
 /* Launch capture: every entry point called on `stream` between begin and
  * end is recorded (validated immediately, launched only on replay) into a
