@@ -147,6 +147,7 @@ SIGNATURES = {
     "emel_cuda_soft_max_ext": (_I, [_CTX, _V, _P, _P, _P, _F]),
     "emel_cuda_sum": (_I, [_CTX, _V, _P, _P]),
     "emel_cuda_sum_f64": (_I, [_CTX, _V, _P, _V]),
+    "emel_cuda_sum_noalloc": (_I, [_V, _P, _P]),
     "emel_cuda_mean": (_I, [_CTX, _V, _P, _P]),
     "emel_cuda_sum_rows": (_I, [_CTX, _V, _P, _P]),
     "emel_cuda_argmax": (_I, [_CTX, _V, _P, _P]),

@@ -920,3 +920,18 @@ emel_cuda_status emel_cuda_argmax_rows(emel_cuda_context* ctx, void* stream, con
 }
 
 }  // extern "C"
+
+namespace emel {
+
+// The OpSum request checks of emel_cuda_sum (reductions.rs:452-458,
+// 520-530), for entry points that run without a context.
+emel_cuda_status check_scalar_sum(const emel_tensor_view* src, const emel_tensor_view* dst, RowPlan* plan) {
+    Checked cs, cd;
+    if (!validate_as(src, EMEL_DTYPE_F32, false, &cs) || !validate_as(dst, EMEL_DTYPE_F32, false, &cd))
+        return EMEL_CUDA_INVALID_VIEW;
+    if (!scalar_shape(dst)) return EMEL_CUDA_SHAPE_MISMATCH;
+    *plan = plan_rows(src, cs, nullptr, nullptr);
+    return EMEL_CUDA_OK;
+}
+
+}  // namespace emel

@@ -265,3 +265,78 @@ cudaError_t launch_argmax(const LaunchEnv& env, const RowPlan& p, int out_kind, 
 }
 
 }  // namespace emel
+
+// ---------------------------------------------------------------------------
+// Whole-tensor sum without allocation (emel_cuda_sum_noalloc).
+//
+// Its scratch is a file-scope device array instead of a context workspace:
+// a 256-byte header holding the last-CTA ticket, then room for
+// kNoAllocMaxPartials per-CTA partial sums.  Host code cannot use the
+// array's name as a device address, so the first call on each device asks
+// the runtime for it (cudaGetSymbolAddress, with that device current) and
+// keeps it.  The kernel is the one emel_cuda_sum launches, with the same grid
+// for the same device and input, so both entry points return the same bits.
+// ---------------------------------------------------------------------------
+#include <mutex>
+
+#include "emel_cuda.h"
+
+namespace emel {
+
+emel_cuda_status check_scalar_sum(const emel_tensor_view* src, const emel_tensor_view* dst, RowPlan* plan);
+
+namespace {
+
+constexpr int kNoAllocMaxPartials = 2048;  // one per CTA: 4 CTAs per SM up to 512 SMs
+constexpr int kNoAllocMaxDevices = 64;
+constexpr size_t kNoAllocHeader = 256;     // ticket, padded to the partials' alignment
+
+__device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocHeader + kNoAllocMaxPartials * sizeof(double)];
+
+std::mutex g_noalloc_mutex;
+void* g_noalloc_addr[kNoAllocMaxDevices];
+int g_noalloc_sms[kNoAllocMaxDevices];
+
+}  // namespace
+}  // namespace emel
+
+extern "C" emel_cuda_status emel_cuda_sum_noalloc(void* stream, const emel_tensor_view* src,
+                                                   const emel_tensor_view* dst) {
+    using namespace emel;
+    RowPlan p;
+    const emel_cuda_status checked = check_scalar_sum(src, dst, &p);
+    if (checked != EMEL_CUDA_OK) return checked;
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0) return EMEL_CUDA_DEVICE_ERROR;
+    if (dev >= kNoAllocMaxDevices) return EMEL_CUDA_INVALID_ARGUMENT;
+    void* scratch = nullptr;
+    int sms = 0;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mutex);
+        if (g_noalloc_addr[dev] == nullptr) {
+            void* addr = nullptr;
+            if (cudaGetSymbolAddress(&addr, g_noalloc_scratch) != cudaSuccess || addr == nullptr)
+                return EMEL_CUDA_DEVICE_ERROR;
+            int n = 0;
+            if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0)
+                return EMEL_CUDA_DEVICE_ERROR;
+            g_noalloc_sms[dev] = n;
+            g_noalloc_addr[dev] = addr;
+        }
+        scratch = g_noalloc_addr[dev];
+        sms = g_noalloc_sms[dev];
+    }
+    LaunchEnv env{};
+    env.stream = static_cast<cudaStream_t>(stream);
+    env.sm_count = sms;
+    env.device = dev;
+    const uint32_t grid = reduce_grid(env, p.rows * p.ne[0]);
+    if (grid > (uint32_t)kNoAllocMaxPartials) return EMEL_CUDA_OUT_OF_MEMORY;  // the scratch is too small
+    unsigned* ticket = static_cast<unsigned*>(scratch);
+    double* partials = reinterpret_cast<double*>(static_cast<char*>(scratch) + kNoAllocHeader);
+    // the array keeps the previous call's contents: the ticket must start at 0
+    if (cudaMemsetAsync(ticket, 0, sizeof(unsigned), env.stream) != cudaSuccess) return EMEL_CUDA_DEVICE_ERROR;
+    if (p.flat) sum_all<true><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, 0, dst->data);
+    else sum_all<false><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, 0, dst->data);
+    return cudaGetLastError() == cudaSuccess ? EMEL_CUDA_OK : EMEL_CUDA_DEVICE_ERROR;
+}

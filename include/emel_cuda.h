@@ -253,6 +253,31 @@ EMEL_CUDA_API emel_cuda_status emel_cuda_soft_max_ext(emel_cuda_context* ctx, vo
 /* reductions::OpSum (reductions.rs:90-103, 671-681): dst ne == [1,1,1,1]. */
 EMEL_CUDA_API emel_cuda_status emel_cuda_sum(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
                                const emel_tensor_view* dst);
+/* emel_cuda_sum for callers that cannot allocate device memory.  No
+ * counterpart in the reference (its kernels never touch a device).
+ *
+ * Who needs it: a host application that owns all device memory and hands a
+ * plugin only the buffers to work on (its allocator has reserved the whole
+ * device, or its contract forbids the plugin from allocating), and
+ * latency-critical code that must not call cudaMalloc/cudaFree because they
+ * can synchronise the device.  Such callers cannot create a context (that
+ * allocates the reduction workspace), so this call takes no context: it
+ * runs on the current device and enqueues on `stream` (NULL = the legacy
+ * default stream).  It calls no allocating routine.
+ *
+ * Same validation and result as emel_cuda_sum (dst ne == [1,1,1,1], F32).
+ * Its scratch is one fixed static device array -- a ticket plus 2048
+ * per-block partial sums, 16.25 KiB -- that every GPU which loads this
+ * library keeps until the process exits.  A device that would need more
+ * than 2048 blocks (more than 512 SMs) gets EMEL_CUDA_OUT_OF_MEMORY and
+ * nothing is launched.  The first call on each device looks up the array's
+ * device address (cudaGetSymbolAddress with that device current); make that
+ * first call before any stream capture on the device.  All calls share the
+ * one array and each starts by clearing its ticket: calls whose work
+ * overlaps on the GPU (other streams, other threads) race on it and can
+ * return wrong sums, so issue them one after another. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_sum_noalloc(void* stream, const emel_tensor_view* src,
+                                                     const emel_tensor_view* dst);
 /* The f64 accumulator of OpSum, written to device memory `out` (one double):
  * the per-shard partial of a multi-GPU whole-tensor sum. */
 EMEL_CUDA_API emel_cuda_status emel_cuda_sum_f64(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src, double* out);
