@@ -409,6 +409,187 @@ def run_e2e(args, pkg, ctx, torch, step, stream, world):
 
 
 # ---------------------------------------------------------------------------
+# Per-op suite over all five configurations (BASELINE table; 1 GPU)
+# ---------------------------------------------------------------------------
+L2_BYTES = 126 * 1024 * 1024
+
+
+def run_suite(args):
+    """Times every operator of every configuration: each op is captured R
+    times back to back over enough rotating buffer sets that a set is
+    evicted from L2 before it is read again, and the graph is timed with
+    events.  Prints one JSON line per op and returns them."""
+    import torch
+
+    pkg = load_package()
+    from emel_rs_b200 import workloads as W
+
+    lib = pkg.lib()
+    ctx = pkg.Context(0)
+    stream = pkg.Stream(ctx)
+    sh = stream.handle
+    dev = torch.device("cuda", 0)
+    peak, peak_kind = peaks()
+    out = []
+
+    def view(t, ne, nb=None, code=0):
+        v = pkg.CView()
+        v.data = t.data_ptr()
+        v.storage_bytes = t.numel() * t.element_size()
+        nb = nb or pkg.contiguous_nb(ne, code)
+        for d in range(4):
+            v.ne[d] = ne[d]
+            v.nb[d] = nb[d]
+        v.dtype = code
+        return v
+
+    def sets_for(nbytes):
+        return max(1, min(8, -(-3 * L2_BYTES // max(1, nbytes))))
+
+    only = set(args.only.split(",")) if args.only else None
+
+    def measure(cfg, name, nbytes, elems, make_launch, sets):
+        if only and name not in only:
+            return
+        torch.cuda.synchronize()  # inputs were uploaded on torch's stream
+        launches = [make_launch(k) for k in range(sets)]
+        reps = max(sets, 8)
+        for L in launches:
+            L()
+        stream.synchronize()
+        g = pkg.Graph(ctx, stream)
+        e0, e1 = pkg.CudaEvent(ctx), pkg.CudaEvent(ctx)
+        with g:
+            e0.record_timed(sh)
+            for r in range(reps):
+                launches[r % sets]()
+            e1.record_timed(sh)
+        times = []
+        for _ in range(5):
+            g.launch()
+            stream.synchronize()
+            times.append(e0.elapsed_ms(e1) / reps)
+        g.close()
+        ms = statistics.median(times)
+        gbs = nbytes / (ms / 1e3) / 1e9
+        line = {"suite": cfg, "op": name, "gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4),
+                "gelems": round(elems / (ms / 1e3) / 1e9, 2), "us_per_launch": round(ms * 1e3, 2),
+                "algorithmic_bytes": nbytes, "buffer_sets": sets, "peak": f"{peak} GB/s ({peak_kind})"}
+        print(json.dumps(line), flush=True)
+        out.append(line)
+
+    def chk(st):
+        if st != 0:
+            raise RuntimeError(f"status {st}: {ctx.last_error}")
+
+    B = ctypes.byref
+    # cfg1: row-broadcast binary ops
+    src0, src1 = W.cfg1()
+    spec = W.cfg1_spec()
+    nb_ = spec.ops[0].bytes
+    S = sets_for(nb_)
+    a = [torch.from_numpy(src0).to(dev) for _ in range(S)]
+    b = torch.from_numpy(src1).to(dev)
+    d = [torch.empty_like(a[0]) for _ in range(S)]
+    ne = [W.CFG1_NE[0], W.CFG1_NE[1], 1, 1]
+    va = [view(t, ne) for t in a]
+    vb = view(b, [W.CFG1_NE[0], 1, 1, 1])
+    vd = [view(t, ne) for t in d]
+    for op, opname in enumerate(("add", "sub", "mul", "div")):
+        measure("cfg1", f"broadcast_row_{opname}", nb_, spec.ops[0].elements,
+                lambda k, op=op: (lambda: chk(lib.emel_cuda_broadcast_row(ctx.handle, sh, op, B(va[k]), B(vb), B(vd[k])))),
+                S)
+    del a, d
+    # cfg2: unary sweep
+    x, xa = W.cfg2()
+    ne = [W.CFG2_NE[0], W.CFG2_NE[1], 1, 1]
+    for dt, code, tdt in (("f32", 0, torch.float32), ("f16", 1, torch.float16)):
+        n = x.size * (4 if dt == "f32" else 2) * 2
+        S = sets_for(n)
+        for opname, opc in OPS:
+            base = torch.from_numpy(xa if opname in ("sqrt", "pow2") else x).to(dev).to(tdt)
+            srcs = [base.clone() for _ in range(S)]
+            dsts = [torch.empty_like(base) for _ in range(S)]
+            vs = [view(t, ne, code=code) for t in srcs]
+            vo = [view(t, ne, code=code) for t in dsts]
+            measure("cfg2", f"{opname}_{dt}", n, x.size,
+                    lambda k, opc=opc: (lambda: chk(lib.emel_cuda_unary(ctx.handle, sh, opc, B(vs[k]), B(vo[k])))), S)
+            del srcs, dsts
+    # cfg3: row normalisation
+    x3, w3 = W.cfg3()
+    ne = [W.CFG3_NE[0], W.CFG3_NE[1], 1, 1]
+    spec = W.cfg3_spec()
+    xs = torch.from_numpy(x3).to(dev)
+    ws = torch.from_numpy(w3).to(dev)
+    ys = torch.empty_like(xs)
+    ys2 = torch.empty_like(xs)
+    rows = torch.empty(W.CFG3_NE[1], device=dev)
+    vx, vw, vy, vy2 = view(xs, ne), view(ws, [W.CFG3_NE[0], 1, 1, 1]), view(ys, ne), view(ys2, ne)
+    vr = view(rows, [1, W.CFG3_NE[1], 1, 1])
+    measure("cfg3", "rms_norm", spec.ops[0].bytes, spec.ops[0].elements,
+            lambda k: (lambda: chk(lib.emel_cuda_rms_norm(ctx.handle, sh, B(vx), B(vy), 1e-6))), 1)
+    measure("cfg3", "rms_norm_mul_fused", spec.ops[1].bytes, spec.ops[1].elements,
+            lambda k: (lambda: chk(lib.emel_cuda_rms_norm_mul(ctx.handle, sh, B(vx), B(vw), B(vy), 1e-6))), 1)
+    measure("cfg3", "rms_norm_then_mul_two_ops", spec.ops[0].bytes + spec.ops[1].bytes, spec.ops[0].elements,
+            lambda k: (lambda: (chk(lib.emel_cuda_rms_norm(ctx.handle, sh, B(vx), B(vy), 1e-6)),
+                                chk(lib.emel_cuda_broadcast_row(ctx.handle, sh, 2, B(vy), B(vw), B(vy2))))), 1)
+    measure("cfg3", "norm", spec.ops[2].bytes, spec.ops[2].elements,
+            lambda k: (lambda: chk(lib.emel_cuda_norm(ctx.handle, sh, B(vx), B(vy), 1e-5))), 1)
+    measure("cfg3", "sum_rows", spec.ops[3].bytes, spec.ops[3].elements,
+            lambda k: (lambda: chk(lib.emel_cuda_sum_rows(ctx.handle, sh, B(vx), B(vr)))), 1)
+    del xs, ys, ys2
+    # cfg4a: masked, scaled softmax
+    scores, mask = W.cfg4a()
+    kv, q, h = W.CFG4A_NE
+    spec = W.cfg4_spec()
+    ts = torch.from_numpy(scores).to(dev)
+    tm = torch.from_numpy(mask).to(dev)
+    to = torch.empty_like(ts)
+    vs_, vm, vo_ = view(ts, [kv, q, h, 1]), view(tm, [kv, q, 1, 1], code=1), view(to, [kv, q, h, 1])
+    measure("cfg4", "soft_max_ext_scale_mask", spec.ops[0].bytes, spec.ops[0].elements,
+            lambda k: (lambda: chk(lib.emel_cuda_soft_max_ext(ctx.handle, sh, B(vs_), B(vm), B(vo_),
+                                                                float(W.CFG4A_SCALE)))), 1)
+    del ts, to
+    # cfg4b: vocab softmax and per-row argmax
+    logits, _ = W.cfg4b()
+    v, rws = W.CFG4B_NE
+    S = sets_for(spec.ops[1].bytes)
+    tl = [torch.from_numpy(logits).to(dev) for _ in range(S)]
+    tlo = [torch.empty_like(tl[0]) for _ in range(S)]
+    ti = torch.empty(rws, dtype=torch.int64, device=dev)
+    vl = [view(t, [v, rws, 1, 1]) for t in tl]
+    vlo = [view(t, [v, rws, 1, 1]) for t in tlo]
+    vi = view(ti, [1, rws, 1, 1], code=27)
+    measure("cfg4", "soft_max_vocab", spec.ops[1].bytes, spec.ops[1].elements,
+            lambda k: (lambda: chk(lib.emel_cuda_soft_max(ctx.handle, sh, B(vl[k]), B(vlo[k])))), S)
+    measure("cfg4", "argmax_rows_vocab", spec.ops[2].bytes, spec.ops[2].elements,
+            lambda k: (lambda: chk(lib.emel_cuda_argmax_rows(ctx.handle, sh, B(vl[k]), B(vi)))), S)
+    del tl, tlo
+    # cfg5: permuted repeat broadcast, whole-tensor sum and argmax
+    s0, s1 = W.cfg5()
+    ne5, nb5 = W.cfg5_src0_view()
+    spec = W.cfg5_spec()
+    t0 = torch.from_numpy(s0).to(dev)
+    t1 = torch.from_numpy(s1).to(dev)
+    td = torch.empty_like(t0)
+    tsum = torch.empty(1, device=dev)
+    targ = torch.empty(1, dtype=torch.int64, device=dev)
+    v0 = view(t0, ne5, nb5)
+    v1 = view(t1, [128, 1, 8192, 1])
+    vd5 = view(td, ne5)
+    one = [1, 1, 1, 1]
+    vsum, varg = view(tsum, one), view(targ, one, code=27)
+    for op, opname in ((2, "mul"), (0, "add")):
+        measure("cfg5", f"repeat_{opname}_permuted", spec.ops[0].bytes, spec.ops[0].elements,
+                lambda k, op=op: (lambda: chk(lib.emel_cuda_binary_repeat(ctx.handle, sh, op, B(v0), B(v1), B(vd5)))), 1)
+    measure("cfg5", "sum_whole_permuted", spec.ops[2].bytes, spec.ops[2].elements,
+            lambda k: (lambda: chk(lib.emel_cuda_sum(ctx.handle, sh, B(v0), B(vsum)))), 1)
+    measure("cfg5", "argmax_whole_permuted", spec.ops[3].bytes, spec.ops[3].elements,
+            lambda k: (lambda: chk(lib.emel_cuda_argmax(ctx.handle, sh, B(v0), B(varg)))), 1)
+    return out
+
+
+# ---------------------------------------------------------------------------
 # CPU lanes (the oracle: C restatement of the reference loops)
 # ---------------------------------------------------------------------------
 def cpu_workload():
@@ -529,14 +710,18 @@ def main():
     ap.add_argument("--ref-seconds", type=float, default=60.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end measurement")
-    ap.add_argument("--only", default="", help="comma list of ops to run, e.g. gelu_f32,relu_f16 (profiling)")
+    ap.add_argument("--only", default="", help="comma list of ops to run, e.g. gelu_f32,relu_f16 (profiling; with --suite: suite op names)")
     ap.add_argument("--branches", type=int, default=4, help="parallel graph branches for the 16 independent ops")
+    ap.add_argument("--suite", action="store_true", help="per-op lines for every configuration (1 GPU)")
     args = ap.parse_args()
     world, rank, local = dist_env()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference(args, world, rank)
+        return
+    if args.suite:
+        run_suite(args)
         return
     run_b200(args, world, rank, local)
 

@@ -463,7 +463,23 @@ emel_cuda_status emel_cuda_stream_destroy(emel_cuda_context* ctx, void* stream) 
 
 emel_cuda_status emel_cuda_stream_synchronize(emel_cuda_context* ctx, void* stream) {
     if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
-    return device_status(ctx, cudaStreamSynchronize((cudaStream_t)stream));
+    const cudaStream_t s = (cudaStream_t)stream;
+    cudaError_t err = cudaStreamSynchronize(s);
+    // A kernel whose bounded wait expired left the fault word set: report it
+    // once and re-arm it.
+    uint32_t fault = 0;
+    char* word = static_cast<char*>(ctx->workspace) + emel::kFaultWordOffset;
+    if (err == cudaSuccess) err = cudaMemcpyAsync(&fault, word, sizeof(fault), cudaMemcpyDeviceToHost, s);
+    if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+    if (err == cudaSuccess && fault != 0) {
+        err = cudaMemsetAsync(word, 0, sizeof(fault), s);
+        if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+        if (err == cudaSuccess) {
+            std::snprintf(ctx->last_error, sizeof(ctx->last_error), "a bounded device wait expired");
+            return EMEL_CUDA_TIMEOUT;
+        }
+    }
+    return device_status(ctx, err);
 }
 
 // ---- events and launch capture ---------------------------------------------

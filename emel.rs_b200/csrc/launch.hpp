@@ -28,6 +28,16 @@ cudaError_t launch_sum(const LaunchEnv& env, const RowPlan& plan, int mode, void
 cudaError_t launch_argmax(const LaunchEnv& env, const RowPlan& plan, int out_kind, int dst_dtype, int64_t index_base,
                           void* out);
 
+// Ring-staged norm / rms_norm / rms_norm * weight / soft_max (rowring.cu).
+// Returns false, launching nothing, when the view does not qualify.
+// op: 0 norm, 1 rms_norm, 2 rms_norm * weight, 3 soft_max.
+bool launch_row_ring(const LaunchEnv& env, const RowPlan& plan, int op, float param, bool apply_scale,
+                     cudaError_t* err);
+
+// Byte offset, inside the workspace's 256-byte header, of the fault word a
+// kernel sets when one of its bounded waits expires.
+constexpr uint64_t kFaultWordOffset = 64;
+
 // Bytes of workspace the whole-tensor reductions need.
 uint64_t reduction_workspace_bytes(int sm_count);
 

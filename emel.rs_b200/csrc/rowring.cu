@@ -1,0 +1,460 @@
+// Row operators on a shared-memory ring fed by the TMA bulk-copy engine:
+// norm, rms_norm, rms_norm * weight and soft_max (with scale and mask).
+//
+// Each of these needs every element of a row more than once (a statistic,
+// then the output), so the row must stay on chip between the passes.  A
+// persistent CTA owns the rows blockIdx.x, blockIdx.x + gridDim.x, ... and
+// keeps S of them in flight in a ring of shared-memory stages:
+//
+//   * one thread issues `cp.async.bulk` copies (global -> shared, completion
+//     counted in bytes on the stage's mbarrier) S rows ahead, so HBM sees
+//     S row reads per CTA in flight while the CTA computes;
+//   * all threads wait for the stage's phase (bounded by the global timer),
+//     then run the passes over the staged row from shared memory (16-byte
+//     reads, conflict-free), with f64 block reductions between passes;
+//   * results go straight from registers to global memory (16-byte
+//     streaming stores when the destination rows allow it);
+//   * after a barrier the stage is refilled with the row S ahead.
+//
+// The soft_max_ext mask row, when it is contiguous and 16-byte aligned, is
+// copied into the same stage by a second bulk copy on the same mbarrier; the
+// rms_norm weight row is loaded into shared memory once per CTA.
+//
+// Arithmetic is the resident-row kernels' (rows.cu), term for term; only the
+// grouping of the f64 partial sums differs.
+//
+// A wait that does not complete within two seconds sets the context's fault
+// word (read back by emel_cuda_stream_synchronize as EMEL_CUDA_TIMEOUT);
+// the CTA then waits, again bounded, for the copies it still has in flight
+// and returns.
+#include "common.cuh"
+#include "launch.hpp"
+#include "rowreduce.cuh"
+
+namespace emel {
+
+namespace {
+
+constexpr int kRingStagesMax = 4;
+constexpr int kRingThreads = 256;
+constexpr uint32_t kRingSmemPerSm = 220 * 1024;
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+constexpr uint32_t kStageAlign = 128;
+
+enum RingOp { kRingNorm = 0, kRingRms = 1, kRingRmsMul = 2, kRingSoftMax = 3 };
+
+// aux_mode
+enum { kAuxNone = 0, kAuxWeight = 1, kAuxMaskStaged = 2, kAuxMaskLoads = 3 };
+
+struct RingArgs {
+    const char* src;
+    char* dst;
+    const char* aux;
+    uint32_t* fault;
+    uint32_t ne0;  // multiple of 4
+    uint32_t rows;
+    uint32_t ne1, ne2;
+    FastDiv d1, d2;
+    int64_t src_st[4];  // element strides; src_st[0] == 1
+    int64_t dst_st[4];
+    int64_t aux_st[4];
+    uint32_t aux_ne2, aux_ne3;
+    FastDiv a2, a3;
+    int aux_mode;
+    int aux_f16;
+    int dst_vec;
+    int apply_scale;
+    uint32_t stage_bytes;
+    uint32_t mask_offset;
+    uint32_t weight_bytes;
+    int stages;
+    float param;  // eps (norms) or scale (soft_max)
+};
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+
+// global -> shared bulk copy through the TMA engine; bytes and both
+// addresses are multiples of 16.
+__device__ __forceinline__ void bulk_load(void* dst_smem, const void* src, uint32_t bytes, uint64_t* bar) {
+    asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst_smem)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Waits for the phase with the given parity; false after kWaitLimitNs (or
+// 2^30 polls, whichever comes first).
+__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
+    if (mbar_try(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    for (uint32_t i = 0; i < (1u << 30); ++i) {
+        if (mbar_try(bar, parity)) return true;
+        if ((i & 63u) == 0 && global_ns() - t0 > kWaitLimitNs) return false;
+    }
+    return false;
+}
+
+__device__ __forceinline__ void row_coords(uint32_t r, const RingArgs& a, uint32_t& i1, uint32_t& i2, uint32_t& i3) {
+    const uint32_t q = fdiv(r, a.d1);
+    i1 = r - q * a.ne1;
+    i3 = fdiv(q, a.d2);
+    i2 = q - i3 * a.ne2;
+}
+
+__device__ __forceinline__ int64_t row_offset(uint32_t r, const RingArgs& a, const int64_t* st) {
+    uint32_t i1, i2, i3;
+    row_coords(r, a, i1, i2, i3);
+    return (int64_t)i1 * st[1] + (int64_t)i2 * st[2] + (int64_t)i3 * st[3];
+}
+
+// Mask row (i1, i2 % m2, i3 % m3) of soft_max_ext (reductions.rs:597-606).
+__device__ __forceinline__ int64_t mask_offset(uint32_t r, const RingArgs& a) {
+    uint32_t i1, i2, i3;
+    row_coords(r, a, i1, i2, i3);
+    const uint32_t m2 = i2 - fdiv(i2, a.a2) * a.aux_ne2;
+    const uint32_t m3 = i3 - fdiv(i3, a.a3) * a.aux_ne3;
+    return (int64_t)i1 * a.aux_st[1] + (int64_t)m2 * a.aux_st[2] + (int64_t)m3 * a.aux_st[3];
+}
+
+template <int T>
+__device__ __forceinline__ double block_sum(double v, GroupScratch<T>* s) {
+    return group_sum<T>(v, s);
+}
+
+__device__ __forceinline__ float4 ld_f4(const float* p) { return *reinterpret_cast<const float4*>(p); }
+
+template <int OP>
+__device__ __forceinline__ void store4(const RingArgs& a, float* drow, uint32_t v, float4 y) {
+    if (a.dst_vec) {
+        __stcs(reinterpret_cast<float4*>(drow) + v, y);
+    } else {
+        const int64_t s0 = a.dst_st[0];
+        const int64_t c = (int64_t)v * 4;
+        drow[c * s0] = y.x;
+        drow[(c + 1) * s0] = y.y;
+        drow[(c + 2) * s0] = y.z;
+        drow[(c + 3) * s0] = y.w;
+    }
+}
+
+// The four mask values of vector v (columns 4v .. 4v+3).
+__device__ __forceinline__ float4 mask4(const RingArgs& a, const unsigned char* stage, int64_t moff, uint32_t v) {
+    if (a.aux_mode == kAuxMaskStaged) {
+        const unsigned char* m = stage + a.mask_offset;
+        if (a.aux_f16) {
+            const uint2 h = reinterpret_cast<const uint2*>(m)[v];
+            return make_float4(f16_bits_to_f32(h.x & 0xffffu), f16_bits_to_f32(h.x >> 16), f16_bits_to_f32(h.y & 0xffffu),
+                               f16_bits_to_f32(h.y >> 16));
+        }
+        return reinterpret_cast<const float4*>(m)[v];
+    }
+    const int64_t s0 = a.aux_st[0];
+    const int64_t c = (int64_t)v * 4;
+    float r[4];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const int64_t e = moff + (c + k) * s0;
+        r[k] = a.aux_f16 ? f16_bits_to_f32(reinterpret_cast<const uint16_t*>(a.aux)[e])
+                         : reinterpret_cast<const float*>(a.aux)[e];
+    }
+    return make_float4(r[0], r[1], r[2], r[3]);
+}
+
+template <int OP, int T>
+__global__ void __launch_bounds__(T, 1024 / T) row_ring(RingArgs a) {
+    extern __shared__ __align__(128) unsigned char ring_smem[];
+    __shared__ __align__(8) uint64_t full[kRingStagesMax];
+    __shared__ GroupScratch<T> red;
+    const int tid = threadIdx.x;
+    const int S = a.stages;
+    const uint32_t mine = a.rows > blockIdx.x ? (a.rows - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+    const float* wsm = reinterpret_cast<const float*>(ring_smem);
+    unsigned char* stage0 = ring_smem + a.weight_bytes;
+    const uint32_t nvec = a.ne0 / 4;
+    const uint32_t msize = a.aux_f16 ? 2u : 4u;
+
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    if constexpr (OP == kRingRmsMul) {
+        float* w = reinterpret_cast<float*>(ring_smem);
+        for (uint32_t c = tid; c < a.ne0; c += T) w[c] = reinterpret_cast<const float*>(a.aux)[(int64_t)c * a.aux_st[0]];
+    }
+    __syncthreads();
+
+    auto issue = [&](uint32_t k) {
+        const uint32_t r = blockIdx.x + k * gridDim.x;
+        const int s = (int)(k % (uint32_t)S);
+        unsigned char* st = stage0 + (size_t)s * a.stage_bytes;
+        const uint32_t rb = a.ne0 * 4u;
+        const uint32_t mb = a.aux_mode == kAuxMaskStaged ? a.ne0 * msize : 0u;
+        mbar_expect_tx(&full[s], rb + mb);
+        bulk_load(st, a.src + row_offset(r, a, a.src_st) * 4, rb, &full[s]);
+        if (mb) bulk_load(st + a.mask_offset, a.aux + mask_offset(r, a) * msize, mb, &full[s]);
+    };
+    if (tid == 0)
+        for (uint32_t k = 0; k < mine && k < (uint32_t)S; ++k) issue(k);
+
+    for (uint32_t k = 0; k < mine; ++k) {
+        const int s = (int)(k % (uint32_t)S);
+        const uint32_t parity = (k / (uint32_t)S) & 1u;
+        const bool ok = mbar_wait(&full[s], parity);
+        if (!__syncthreads_and(ok)) {
+            if (tid == 0) {
+                atomicExch(a.fault, 1u);
+                for (uint32_t j = k; j < mine && j < k + (uint32_t)S; ++j)
+                    mbar_wait(&full[j % (uint32_t)S], (j / (uint32_t)S) & 1u);
+            }
+            return;
+        }
+        unsigned char* stage = stage0 + (size_t)s * a.stage_bytes;
+        float* row = reinterpret_cast<float*>(stage);
+        const uint32_t r = blockIdx.x + k * gridDim.x;
+        float* drow = reinterpret_cast<float*>(a.dst) + row_offset(r, a, a.dst_st);
+
+        if constexpr (OP == kRingNorm) {
+            double acc = 0.0;
+            for (uint32_t v = tid; v < nvec; v += T) {
+                const float4 x = ld_f4(row + 4 * v);
+                acc += (double)x.x;
+                acc += (double)x.y;
+                acc += (double)x.z;
+                acc += (double)x.w;
+            }
+            acc = block_sum<T>(acc, &red);
+            const float mean = __double2float_rn(acc / (double)a.ne0);
+            double vs = 0.0;
+            for (uint32_t v = tid; v < nvec; v += T) {
+                const float4 x = ld_f4(row + 4 * v);
+                double c = (double)__fsub_rn(x.x, mean);
+                vs += c * c;
+                c = (double)__fsub_rn(x.y, mean);
+                vs += c * c;
+                c = (double)__fsub_rn(x.z, mean);
+                vs += c * c;
+                c = (double)__fsub_rn(x.w, mean);
+                vs += c * c;
+            }
+            vs = block_sum<T>(vs, &red);
+            const float variance = __double2float_rn(vs / (double)a.ne0);
+            const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(variance, a.param)));
+            for (uint32_t v = tid; v < nvec; v += T) {
+                const float4 x = ld_f4(row + 4 * v);
+                store4<OP>(a, drow, v,
+                           make_float4(f_mul(f_sub(x.x, mean), scale), f_mul(f_sub(x.y, mean), scale),
+                                       f_mul(f_sub(x.z, mean), scale), f_mul(f_sub(x.w, mean), scale)));
+            }
+        } else if constexpr (OP == kRingRms || OP == kRingRmsMul) {
+            double acc = 0.0;
+            for (uint32_t v = tid; v < nvec; v += T) {
+                const float4 x = ld_f4(row + 4 * v);
+                acc += (double)__fmul_rn(x.x, x.x);
+                acc += (double)__fmul_rn(x.y, x.y);
+                acc += (double)__fmul_rn(x.z, x.z);
+                acc += (double)__fmul_rn(x.w, x.w);
+            }
+            acc = block_sum<T>(acc, &red);
+            const float mean = __double2float_rn(acc / (double)a.ne0);
+            const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.param)));
+            for (uint32_t v = tid; v < nvec; v += T) {
+                const float4 x = ld_f4(row + 4 * v);
+                float4 y = make_float4(f_mul(x.x, scale), f_mul(x.y, scale), f_mul(x.z, scale), f_mul(x.w, scale));
+                if constexpr (OP == kRingRmsMul) {
+                    const float4 w = ld_f4(wsm + 4 * v);
+                    y = make_float4(f_mul(y.x, w.x), f_mul(y.y, w.y), f_mul(y.z, w.z), f_mul(y.w, w.w));
+                }
+                store4<OP>(a, drow, v, y);
+            }
+        } else {
+            // soft_max (reductions.rs:565-638): v = x * scale (+ mask); max
+            // (starting from element 0); e = exp(v - max); sum in f64; e / sum.
+            const int64_t moff = a.aux_mode == kAuxMaskLoads ? mask_offset(r, a) : 0;
+            float m = bitsf(0x7fc00000u);  // NaN = "no value yet"
+            for (uint32_t v = tid; v < nvec; v += T) {
+                float4 x = ld_f4(row + 4 * v);
+                if (a.apply_scale) {
+                    x = make_float4(f_mul(x.x, a.param), f_mul(x.y, a.param), f_mul(x.z, a.param), f_mul(x.w, a.param));
+                    if (a.aux_mode != kAuxNone) {
+                        const float4 mk = mask4(a, stage, moff, v);
+                        x = make_float4(f_add(x.x, mk.x), f_add(x.y, mk.y), f_add(x.z, mk.z), f_add(x.w, mk.w));
+                    }
+                    reinterpret_cast<float4*>(row)[v] = x;
+                }
+                m = max_nn(m, x.x);
+                m = max_nn(m, x.y);
+                m = max_nn(m, x.z);
+                m = max_nn(m, x.w);
+            }
+            m = group_max<T>(m, &red);  // its barriers also publish row[0]
+            const float first = row[0];
+            if (is_nan(first)) m = first;  // reductions.rs:572: the scan starts from element 0
+            double acc = 0.0;
+            for (uint32_t v = tid; v < nvec; v += T) {
+                const float4 x = ld_f4(row + 4 * v);
+                const float4 e = make_float4(lm_exp(f_sub(x.x, m)), lm_exp(f_sub(x.y, m)), lm_exp(f_sub(x.z, m)),
+                                             lm_exp(f_sub(x.w, m)));
+                reinterpret_cast<float4*>(row)[v] = e;
+                acc += (double)e.x;
+                acc += (double)e.y;
+                acc += (double)e.z;
+                acc += (double)e.w;
+            }
+            acc = block_sum<T>(acc, &red);
+            const float denom = __double2float_rn(acc);
+            for (uint32_t v = tid; v < nvec; v += T) {
+                const float4 e = ld_f4(row + 4 * v);
+                store4<OP>(a, drow, v, make_float4(f_div(e.x, denom), f_div(e.y, denom), f_div(e.z, denom), f_div(e.w, denom)));
+            }
+        }
+        __syncthreads();  // every thread is done with this stage
+        if (tid == 0 && k + (uint32_t)S < mine) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(k + (uint32_t)S);
+        }
+    }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+uint32_t round_up(uint64_t v, uint32_t a) { return (uint32_t)((v + a - 1) / a * a); }
+
+bool fits_u32(uint64_t v) { return v > 0 && v <= 0xffffffffull; }
+
+// Occupancy first: as many CTAs per SM as registers and two stages each
+// allow (each CTA's row passes are a chain of dependent steps and barriers,
+// so throughput comes from several rows in progress per SM); then deeper
+// rings (up to kRingStagesMax) while shared memory lasts.
+template <int OP, int T>
+cudaError_t launch_ring_kernel(const LaunchEnv& env, RingArgs a, uint64_t rows, bool* launched) {
+    static int configured_device_mask = 0;  // bit per device with the attribute set
+    const int bit = env.device < 31 ? (1 << env.device) : 0;
+    if (!(configured_device_mask & bit)) {
+        const cudaError_t err =
+            cudaFuncSetAttribute(row_ring<OP, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRingSmemPerSm);
+        if (err != cudaSuccess) return err;
+        configured_device_mask |= bit;
+    }
+    *launched = false;
+    const uint32_t two = a.weight_bytes + 2 * a.stage_bytes;
+    if (two > kRingSmemPerSm) return cudaSuccess;
+    int ctas = 0;
+    cudaError_t err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctas, row_ring<OP, T>, T, two);
+    if (err != cudaSuccess) return err;
+    if (ctas < 1) return cudaSuccess;
+    if (ctas > 8) ctas = 8;
+    auto stages_for = [&](int c) -> uint32_t {
+        const uint32_t budget = kRingSmemPerSm / (uint32_t)c;
+        return budget > a.weight_bytes ? (budget - a.weight_bytes) / a.stage_bytes : 0u;
+    };
+    uint32_t stages = stages_for(ctas);
+    while (stages < 2 && ctas > 1) stages = stages_for(--ctas);
+    if (stages < 2) return cudaSuccess;
+    a.stages = (int)(stages > (uint32_t)kRingStagesMax ? kRingStagesMax : stages);
+    const uint32_t smem = a.weight_bytes + (uint32_t)a.stages * a.stage_bytes;
+    const uint64_t cap = (uint64_t)env.sm_count * ctas;
+    const uint32_t grid = (uint32_t)(rows < cap ? rows : cap);
+    row_ring<OP, T><<<grid, T, smem, env.stream>>>(a);
+    *launched = true;
+    return cudaGetLastError();
+}
+
+}  // namespace
+
+// Plans and launches the ring kernel when the view qualifies: rows of
+// ne0 % 4 == 0 floats, unit stride in dim 0, every row start 16-byte
+// aligned, and (for soft_max) dense src/dst so the f64 sum applies.  Returns
+// false (nothing launched) otherwise.  op: 0 norm, 1 rms_norm, 2 rms_norm *
+// weight, 3 soft_max.
+bool launch_row_ring(const LaunchEnv& env, const RowPlan& p, int op, float param, bool apply_scale,
+                     cudaError_t* err) {
+    const uint64_t ne0 = p.ne[0];
+    if (ne0 < 1024 || ne0 % 4 != 0 || !fits_u32(p.rows) || !fits_u32(p.ne[1]) || !fits_u32(p.ne[2])) return false;
+    if (p.dst_ordinal || p.src.st[0] != 1 || !aligned16(p.src.ptr)) return false;
+    for (int d = 1; d < 4; ++d)
+        if (p.src.st[d] % 4 != 0) return false;
+    if (op == 3 && !p.dense) return false;
+    RingArgs a{};
+    a.src = p.src.ptr;
+    a.dst = p.dst.ptr;
+    a.fault = reinterpret_cast<uint32_t*>(static_cast<char*>(env.workspace) + kFaultWordOffset);
+    a.ne0 = (uint32_t)ne0;
+    a.rows = (uint32_t)p.rows;
+    a.ne1 = (uint32_t)p.ne[1];
+    a.ne2 = (uint32_t)p.ne[2];
+    a.d1 = make_fastdiv(a.ne1);
+    a.d2 = make_fastdiv(a.ne2);
+    for (int d = 0; d < 4; ++d) {
+        a.src_st[d] = p.src.st[d];
+        a.dst_st[d] = p.dst.st[d];
+    }
+    a.dst_vec = p.dst.st[0] == 1 && aligned16(p.dst.ptr) && p.dst.st[1] % 4 == 0 && p.dst.st[2] % 4 == 0 &&
+                p.dst.st[3] % 4 == 0;
+    a.apply_scale = apply_scale ? 1 : 0;
+    a.param = param;
+    a.aux_mode = kAuxNone;
+    uint32_t mask_bytes = 0;
+    if (op == 2) {
+        a.aux_mode = kAuxWeight;
+        a.aux = p.aux.ptr;
+        a.aux_st[0] = p.aux.st[0];
+        a.weight_bytes = round_up(ne0 * 4, kStageAlign);
+    } else if (op == 3 && apply_scale && p.has_aux) {
+        a.aux = p.aux.ptr;
+        a.aux_f16 = p.aux_dtype == (int)DType::F16 ? 1 : 0;
+        for (int d = 0; d < 4; ++d) a.aux_st[d] = p.aux.st[d];
+        if (!fits_u32(p.aux.ne[2]) || !fits_u32(p.aux.ne[3])) return false;
+        a.aux_ne2 = (uint32_t)p.aux.ne[2];
+        a.aux_ne3 = (uint32_t)p.aux.ne[3];
+        a.a2 = make_fastdiv(a.aux_ne2);
+        a.a3 = make_fastdiv(a.aux_ne3);
+        const uint32_t ms = a.aux_f16 ? 2 : 4;
+        bool staged = p.aux.st[0] == 1 && (ne0 * ms) % 16 == 0 && aligned16(p.aux.ptr);
+        for (int d = 1; d < 4; ++d) staged = staged && ((uint64_t)p.aux.st[d] * ms) % 16 == 0;
+        a.aux_mode = staged ? kAuxMaskStaged : kAuxMaskLoads;
+        if (staged) mask_bytes = round_up(ne0 * ms, kStageAlign);
+    }
+    const uint32_t row_bytes = round_up(ne0 * 4, kStageAlign);
+    a.mask_offset = row_bytes;
+    a.stage_bytes = row_bytes + mask_bytes;
+    cudaError_t e;
+    bool launched = false;
+    switch (op) {
+    case 0: e = launch_ring_kernel<kRingNorm, kRingThreads>(env, a, p.rows, &launched); break;
+    case 1: e = launch_ring_kernel<kRingRms, kRingThreads>(env, a, p.rows, &launched); break;
+    case 2: e = launch_ring_kernel<kRingRmsMul, kRingThreads>(env, a, p.rows, &launched); break;
+    default: e = launch_ring_kernel<kRingSoftMax, kRingThreads>(env, a, p.rows, &launched); break;
+    }
+    if (e == cudaSuccess && !launched) return false;
+    ++*env.launches;
+    *err = e;
+    return true;
+}
+
+}  // namespace emel

@@ -23,6 +23,7 @@
 
 #include "common.cuh"
 #include "launch.hpp"
+#include "rowreduce.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -31,94 +32,6 @@ namespace emel {
 namespace {
 
 constexpr int kMaxE = 32;  // elements per thread for register-resident rows
-
-// ---------------------------------------------------------------------------
-// Group reductions (G threads; G <= 32 uses shuffles only).
-// ---------------------------------------------------------------------------
-template <int G>
-struct GroupScratch {
-    double d[G > 32 ? G / 32 : 1];
-    float f[G > 32 ? G / 32 : 1];
-    int64_t i[G > 32 ? G / 32 : 1];
-    uint32_t h[G > 32 ? G / 32 : 1];
-};
-
-template <int G>
-__device__ __forceinline__ double group_sum(double v, GroupScratch<G>* s) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-    if constexpr (G > 32) {
-        const int lane = threadIdx.x & 31, warp = (threadIdx.x % G) / 32;
-        __syncthreads();
-        if (lane == 0) s->d[warp] = v;
-        __syncthreads();
-        v = 0.0;
-#pragma unroll
-        for (int w = 0; w < G / 32; ++w) v += s->d[w];
-    }
-    return v;
-}
-
-// max that ignores NaN (the reference never selects a NaN unless it is the
-// first element, which callers handle separately)
-__device__ __forceinline__ float max_nn(float a, float b) { return is_nan(a) ? b : (is_nan(b) ? a : (b > a ? b : a)); }
-
-template <int G>
-__device__ __forceinline__ float group_max(float v, GroupScratch<G>* s) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) v = max_nn(v, __shfl_xor_sync(0xffffffffu, v, o));
-    if constexpr (G > 32) {
-        const int lane = threadIdx.x & 31, warp = (threadIdx.x % G) / 32;
-        __syncthreads();
-        if (lane == 0) s->f[warp] = v;
-        __syncthreads();
-        v = s->f[0];
-#pragma unroll
-        for (int w = 1; w < G / 32; ++w) v = max_nn(v, s->f[w]);
-    }
-    return v;
-}
-
-// (has, value, index): prefer has, then larger value, then smaller index.
-struct ArgBest {
-    float v;
-    int64_t i;
-    uint32_t has;
-};
-
-__device__ __forceinline__ ArgBest arg_better(ArgBest a, ArgBest b) {
-    if (!b.has) return a;
-    if (!a.has) return b;
-    if (b.v > a.v) return b;
-    if (a.v > b.v) return a;
-    return b.i < a.i ? b : a;
-}
-
-template <int G>
-__device__ __forceinline__ ArgBest group_argmax(ArgBest v, GroupScratch<G>* s) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) {
-        ArgBest w;
-        w.v = __shfl_xor_sync(0xffffffffu, v.v, o);
-        w.i = __shfl_xor_sync(0xffffffffu, v.i, o);
-        w.has = __shfl_xor_sync(0xffffffffu, v.has, o);
-        v = arg_better(v, w);
-    }
-    if constexpr (G > 32) {
-        const int lane = threadIdx.x & 31, warp = (threadIdx.x % G) / 32;
-        __syncthreads();
-        if (lane == 0) {
-            s->f[warp] = v.v;
-            s->i[warp] = v.i;
-            s->h[warp] = v.has;
-        }
-        __syncthreads();
-        v = ArgBest{s->f[0], s->i[0], s->h[0]};
-#pragma unroll
-        for (int w = 1; w < G / 32; ++w) v = arg_better(v, ArgBest{s->f[w], s->i[w], s->h[w]});
-    }
-    return v;
-}
 
 // ---------------------------------------------------------------------------
 // Row addressing.
@@ -599,6 +512,8 @@ static int resident_group(uint64_t ne0) {
     norm_rows<G, VEC, OP><<<row_grid(env, p.rows, cta_of<G>() / G, 2048 / cta_of<G>()), cta_of<G>(), 0, env.stream>>>(p, eps)
 
 cudaError_t launch_norm(const LaunchEnv& env, const RowPlan& p, int op, float eps) {
+    cudaError_t ring_err;
+    if (launch_row_ring(env, p, op, eps, false, &ring_err)) return ring_err;
     const int g = resident_group(p.ne[0]);
     if (g == 0) {
         const uint32_t grid = row_grid(env, p.rows, 1, 2);
@@ -629,6 +544,8 @@ cudaError_t launch_norm(const LaunchEnv& env, const RowPlan& p, int op, float ep
 uint64_t soft_max_cluster_capacity() { return 8ull * 1024 * kMaxE; }
 
 cudaError_t launch_soft_max(const LaunchEnv& env, const RowPlan& p, bool apply_scale, float scale) {
+    cudaError_t ring_err;
+    if (launch_row_ring(env, p, 3, scale, apply_scale, &ring_err)) return ring_err;
     const bool long_row = resident_group(p.ne[0]) == 0 && (!p.vec || p.ne[0] > soft_max_cluster_capacity());
     if (p.dst_ordinal || (!p.dense && p.ne[0] * sizeof(float) > 200 * 1024) || (p.dense && long_row)) {
         softmax_rows_stream<<<row_grid(env, p.rows, 1, 2), 1024, 0, env.stream>>>(p, apply_scale, scale);

@@ -136,6 +136,9 @@ EMEL_CUDA_API emel_cuda_status emel_cuda_memcpy_d2h(emel_cuda_context* ctx, void
 EMEL_CUDA_API emel_cuda_status emel_cuda_memset(emel_cuda_context* ctx, void* stream, void* dst, int value, uint64_t bytes);
 EMEL_CUDA_API emel_cuda_status emel_cuda_stream_create(emel_cuda_context* ctx, void** out);
 EMEL_CUDA_API emel_cuda_status emel_cuda_stream_destroy(emel_cuda_context* ctx, void* stream);
+/* Waits for the stream.  Returns EMEL_CUDA_TIMEOUT (once) when a kernel of
+ * this context gave up a bounded device wait since the last call; the
+ * outputs of the work enqueued since then are unspecified. */
 EMEL_CUDA_API emel_cuda_status emel_cuda_stream_synchronize(emel_cuda_context* ctx, void* stream);
 /* Number of kernels this context has launched (all entry points; a graph
  * replay counts the kernels it contains). */

@@ -1,0 +1,217 @@
+"""Multi-GPU sharded path on real devices: one process per GPU, NCCL.
+
+Each rank holds the dim-3 slices [b, e) of the tensor (config 5's permuted
+view, or a small contiguous case), runs the repeat broadcast on its shard
+(checked bit-exactly against the oracle for that shard), computes its sum
+and argmax partials on the device (emel_cuda_sum_f64,
+emel_cuda_argmax_partial_compute), all-gathers them over NCCL and combines
+them in rank order.  The parent checks every rank's combined answer against
+the oracle's whole-tensor OpSum / OpArgmax.  Skipped unless the process
+sees at least `world` GPUs."""
+
+import ctypes
+import os
+import socket
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+ROOT = Path(__file__).resolve().parent.parent
+
+pytestmark = pytest.mark.gpu
+
+SMALL = {
+    "uneven_split_tie_across_shards": dict(ne=[32, 4, 8, 5], plant=[(3, 40.0), (-7, 40.0)], nan0=False),
+    "nan_at_element_zero": dict(ne=[32, 4, 8, 4], plant=[(100, 9.0)], nan0=True),
+}
+
+
+def free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def gpu_count():
+    import torch
+    return torch.cuda.device_count() if torch.cuda.is_available() else 0
+
+
+def small_tensor(case):
+    ne = case["ne"]
+    rng = np.random.default_rng(sum(ne))
+    x = rng.standard_normal(int(np.prod(ne))).astype(np.float32)
+    for idx, val in case["plant"]:
+        x[idx] = val
+    if case["nan0"]:
+        x[0] = np.nan
+    return x
+
+
+def cfg5_slices(W, begin, end):
+    """Storage of dim-3 slices [begin, end) of config 5's src0, and src1."""
+    parts = []
+    src1 = None
+    for j in range(begin, end):
+        s0, src1 = W.cfg5(ne3=1, shard=j)
+        parts.append(s0)
+    return np.concatenate(parts, axis=0), src1
+
+
+def worker(rank, world, port, case_name, q):
+    try:
+        sys.path.insert(0, str(ROOT))
+        sys.path.insert(0, str(ROOT / "oracle"))
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        from datetime import timedelta
+
+        import torch
+        import torch.distributed as dist
+
+        import oracle
+        from __graft_entry__ import load_package
+
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                                device_id=dev)
+        pkg = load_package()
+        from emel_rs_b200 import distributed as D
+        from emel_rs_b200 import workloads as W
+
+        lib = pkg.lib()
+        ctx = pkg.Context(rank)
+        olib = oracle.load()
+        repeat_ok = None
+        if case_name == "cfg5":
+            b, e = D.shard_bounds(W.CFG5_NE[3], world, rank)
+            s0, s1 = cfg5_slices(W, b, e)
+            ne, nb = W.cfg5_src0_view(ne3=e - b)
+            plane = ne[0] * ne[1] * ne[2]
+            t0 = torch.from_numpy(s0).to(dev)
+            t1 = torch.from_numpy(s1).to(dev)
+            td = torch.empty_like(t0)
+            v0, v1, vd = pkg.CView(), pkg.CView(), pkg.CView()
+            for v, t, vne, vnb in ((v0, t0, ne, nb), (v1, t1, [128, 1, 8192, 1], None),
+                                   (vd, td, ne, None)):
+                v.data = t.data_ptr()
+                v.storage_bytes = t.numel() * 4
+                vnb = vnb or pkg.contiguous_nb(vne)
+                for d in range(4):
+                    v.ne[d], v.nb[d] = vne[d], vnb[d]
+                v.dtype = 0
+            torch.cuda.synchronize()
+            st = lib.emel_cuda_binary_repeat(ctx.handle, None, 2, ctypes.byref(v0), ctypes.byref(v1), ctypes.byref(vd))
+            assert st == 0, ctx.last_error
+            ctx.synchronize()
+            got = td.cpu().numpy()
+            want = np.empty_like(s0)
+            o0 = oracle.host_view(s0, ne, nb)
+            o1 = oracle.host_view(s1, [128, 1, 8192, 1])
+            od = oracle.host_view(want, ne)
+            assert olib.oracle_binary_repeat(2, ctypes.byref(o0), ctypes.byref(o1), ctypes.byref(od)) == 0
+            repeat_ok = bool(np.array_equal(got.view(np.uint32), want.view(np.uint32)))
+            src_view = v0
+        else:
+            case = SMALL[case_name]
+            ne = case["ne"]
+            x = small_tensor(case)
+            b, e = D.shard_bounds(ne[3], world, rank)
+            plane = ne[0] * ne[1] * ne[2]
+            shard = np.ascontiguousarray(x[b * plane:e * plane])
+            t0 = torch.from_numpy(shard).to(dev)
+            src_view = pkg.CView()
+            src_view.data = t0.data_ptr()
+            src_view.storage_bytes = t0.numel() * 4
+            sne = [ne[0], ne[1], ne[2], e - b]
+            snb = pkg.contiguous_nb(sne)
+            for d in range(4):
+                src_view.ne[d], src_view.nb[d] = sne[d], snb[d]
+            src_view.dtype = 0
+            torch.cuda.synchronize()
+        acc = torch.empty(1, dtype=torch.float64, device=dev)
+        part = torch.empty(24, dtype=torch.uint8, device=dev)
+        st = lib.emel_cuda_sum_f64(ctx.handle, None, ctypes.byref(src_view), ctypes.c_void_p(acc.data_ptr()))
+        assert st == 0, ctx.last_error
+        st = lib.emel_cuda_argmax_partial_compute(ctx.handle, None, ctypes.byref(src_view), b * plane,
+                                                  ctypes.c_void_p(part.data_ptr()))
+        assert st == 0, ctx.last_error
+        ctx.synchronize()
+        local_sum = float(acc.cpu().item())
+        local_part = D.read_partial(pkg, ctx, part.data_ptr())
+        total32, total64 = D.global_sum(torch, dist, local_sum, device=dev)
+        gidx, gval = D.global_argmax(pkg, torch, dist, local_part, device=dev)
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, float(total32), total64, gidx, repeat_ok))
+    except Exception as exc:  # report to the parent instead of hanging it
+        q.put((rank, "error", repr(exc), None, None))
+
+
+def run_ranks(world, case_name):
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    procs = [ctx.Process(target=worker, args=(r, world, port, case_name, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        results = [q.get(timeout=600) for _ in procs]
+    finally:
+        for p in procs:
+            p.join(timeout=120)
+            if p.is_alive():
+                p.kill()
+    assert all(r[1] != "error" for r in results), results
+    return results
+
+
+def whole_tensor_answers(x, ne, nb=None):
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+    olib = oracle.load()
+    v = oracle.host_view(x, ne, nb)
+    out = np.zeros(1, np.float32)
+    ov = oracle.host_view(out, [1, 1, 1, 1])
+    assert olib.oracle_sum(ctypes.byref(v), ctypes.byref(ov)) == 0
+    idx = ctypes.c_int64()
+    assert olib.oracle_argmax_index(ctypes.byref(v), ctypes.byref(idx), None) == 0
+    return float(out[0]), idx.value
+
+
+def check(results, want_sum, want_idx):
+    for rank, total32, total64, gidx, repeat_ok in results:
+        if not np.isnan(want_sum):
+            assert abs(total32 - want_sum) <= 1e-5 * max(1.0, abs(want_sum)), (rank, total32, want_sum)
+        assert gidx == want_idx, (rank, gidx, want_idx)
+        assert repeat_ok in (None, True), rank
+
+
+@pytest.mark.parametrize("case_name", list(SMALL))
+def test_two_gpu_partials_match_whole_tensor(case_name):
+    if gpu_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    results = run_ranks(2, case_name)
+    case = SMALL[case_name]
+    want_sum, want_idx = whole_tensor_answers(small_tensor(case), case["ne"])
+    check(results, want_sum, want_idx)
+
+
+def test_cfg5_sharded_over_all_gpus():
+    world = gpu_count()
+    if world < 2:
+        pytest.skip("needs 2 GPUs")
+    world = min(world, 8)
+    results = run_ranks(world, "cfg5")
+    sys.path.insert(0, str(ROOT))
+    from __graft_entry__ import load_package
+    load_package()
+    from emel_rs_b200 import workloads as W
+    x, _ = cfg5_slices(W, 0, W.CFG5_NE[3])
+    ne, nb = W.cfg5_src0_view()
+    want_sum, want_idx = whole_tensor_answers(x, ne, nb)
+    check(results, want_sum, want_idx)

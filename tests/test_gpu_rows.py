@@ -212,3 +212,120 @@ def test_mask_broadcast_over_heads_with_f32_mask(emel, kern, oracle_lib):
     got, want = run_row_op(emel, kern, oracle_lib, "soft_max_ext", x, [kv, q, h, 1],
                            mask=(mask, [kv, q + 3, 1, 1], None), scale=0.37)
     close(got, want, 1e-30, "softmax f32 mask with extra rows")
+
+
+# ---- ring-staged rows (bulk copies into shared memory) -----------------------
+# Rows of >= 1024 floats with unit dim-0 stride and 16-byte aligned starts run
+# on the ring kernel; these cases cover its addressing: padded row strides,
+# 4-D views, strided destinations and weights, masks broadcast over dims 2/3,
+# and masks that cannot be bulk-copied.
+def padded_view(ne, pad_elems):
+    """Contiguous rows of ne0 floats padded by pad_elems, dims 1..3 nested."""
+    nb = [4, (ne[0] + pad_elems) * 4]
+    nb.append(nb[1] * ne[1])
+    nb.append(nb[2] * ne[2])
+    return nb
+
+
+def storage_for(ne, nb, rng, dtype=np.float32):
+    span = sum((ne[d] - 1) * nb[d] for d in range(4)) // np.dtype(dtype).itemsize + 1
+    return (rng.standard_normal(span) * 2).astype(dtype)
+
+
+@pytest.mark.parametrize("kind", ["norm", "rms_norm", "soft_max"])
+def test_ring_padded_4d_rows(emel, kern, oracle_lib, kind):
+    rng = np.random.default_rng(41)
+    ne = [2048, 5, 3, 2]
+    nb = padded_view(ne, 12)
+    x = storage_for(ne, nb, rng)
+    if kind == "soft_max":  # soft_max's f64 path needs dense views: pad only the destination
+        xd = (rng.standard_normal(int(np.prod(ne))) * 2).astype(np.float32)
+        got, want = run_row_op(emel, kern, oracle_lib, kind, xd, ne, out_ne=ne)
+    else:
+        got, want = run_row_op(emel, kern, oracle_lib, kind, x, ne, nb, eps=1e-5, out_ne=ne, out_nb=nb)
+    close(got, want, 1e-30, f"ring {kind} padded 4-D")
+
+
+@pytest.mark.parametrize("kind", ["norm", "rms_norm"])
+def test_ring_strided_destination(emel, kern, oracle_lib, kind):
+    rng = np.random.default_rng(42)
+    ne = [1024, 37, 1, 1]
+    x = (rng.standard_normal(int(np.prod(ne))) * 3).astype(np.float32)
+    out_nb = [8, 8 * 1024, 8 * 1024 * 37, 8 * 1024 * 37]  # every other float
+    ctx = kern.ctx
+    px = gh.Pair(emel, ctx, x, ne)
+    po = gh.Pair(emel, ctx, np.full(2 * x.size, 3.0, np.float32), ne, out_nb)
+    want = po.host.copy()
+    B = ctypes.byref
+    wv = gh.oracle.make_view(want.ctypes.data, want.nbytes, po.ne, po.nb, po.code)
+    if kind == "norm":
+        ost = oracle_lib.oracle_norm(B(px.oview()), B(wv), 1e-6)
+        ev = emel.OpNorm(px.dview(), po.dview(), 1e-6)
+    else:
+        ost = oracle_lib.oracle_rms_norm(B(px.oview()), B(wv), 1e-6)
+        ev = emel.OpRmsNorm(px.dview(), po.dview(), 1e-6)
+    assert ost == 0
+    assert kern.process_event(ev) == emel.Status.OK
+    got = po.download()
+    for p in (px, po):
+        p.free()
+    close(got, want, 1e-30, f"ring {kind} strided dst")
+    assert np.all(got[1::2] == 3.0)  # the skipped floats are untouched
+
+
+def test_ring_rms_norm_mul_strided_weight_many_rows(emel, kern, oracle_lib):
+    rng = np.random.default_rng(43)
+    ne = [1024, 5000, 1, 1]  # many rows per CTA: every stage's phase wraps several times
+    x = rng.standard_normal(int(np.prod(ne))).astype(np.float32)
+    w = rng.uniform(0.5, 1.5, 2048).astype(np.float32)
+    ctx = kern.ctx
+    px = gh.Pair(emel, ctx, x, ne)
+    pw = gh.Pair(emel, ctx, w, [1024, 1, 1, 1], [8, 8192, 8192, 8192])
+    po = gh.Pair(emel, ctx, np.zeros_like(x), ne)
+    want = np.zeros_like(x)
+    B = ctypes.byref
+    wv = gh.oracle.make_view(want.ctypes.data, want.nbytes, po.ne, po.nb, po.code)
+    assert oracle_lib.oracle_rms_norm_mul(B(px.oview()), B(pw.oview()), B(wv), 1e-6) == 0
+    assert kern.process_event(emel.OpRmsNormMul(px.dview(), pw.dview(), po.dview(), 1e-6)) == emel.Status.OK
+    got = po.download()
+    for p in (px, pw, po):
+        p.free()
+    close(got, want, 1e-30, "ring rms_norm * strided weight")
+
+
+@pytest.mark.parametrize("mask_kind", ["f16_broadcast_dims23", "f32_extra_rows", "f16_unaligned"])
+def test_ring_softmax_ext_masks(emel, kern, oracle_lib, mask_kind):
+    rng = np.random.default_rng(44)
+    kv, q, h, b = 1536, 6, 4, 3
+    x = (rng.standard_normal(kv * q * h * b) * 2).astype(np.float32)
+    if mask_kind == "f16_broadcast_dims23":
+        m = np.where(rng.random(kv * q * 2) < 0.3, -np.inf, rng.standard_normal(kv * q * 2)).astype(np.float16)
+        mask = (m, [kv, q, 2, 1], None)  # dim 2 repeats every 2 heads, dim 3 broadcast
+    elif mask_kind == "f32_extra_rows":
+        m = np.where(rng.random(kv * (q + 5)) < 0.3, -np.inf, rng.standard_normal(kv * (q + 5))).astype(np.float32)
+        mask = (m, [kv, q + 5, 1, 1], None)
+    else:  # starts one element in: not 16-byte aligned, read with plain loads
+        m = np.where(rng.random(kv * q + 1) < 0.3, -np.inf, rng.standard_normal(kv * q + 1)).astype(np.float16)
+        mask = (m[1:].copy(), [kv, q, 1, 1], None)
+        full = m  # device copy below keeps the one-element offset
+        ctx = kern.ctx
+        pfull = gh.Pair(emel, ctx, full, [kv * q + 1, 1, 1, 1])
+        pm_view = pfull.dview()
+        px = gh.Pair(emel, ctx, x, [kv, q, h, b])
+        po = gh.Pair(emel, ctx, np.zeros_like(x), [kv, q, h, b])
+        mv = emel.TensorView(pm_view.ptr + 2, pm_view.storage_bytes - 2,
+                             emel.Layout.new(1, [kv, q, 1, 1], [2, 2 * kv, 2 * kv * q, 2 * kv * q]))
+        want = np.zeros_like(x)
+        B = ctypes.byref
+        host_mask = mask[0]
+        hm = gh.oracle.host_view(host_mask, [kv, q, 1, 1])
+        wv = gh.oracle.make_view(want.ctypes.data, want.nbytes, po.ne, po.nb, po.code)
+        assert oracle_lib.oracle_soft_max_ext(B(px.oview()), B(hm), B(wv), 0.3) == 0
+        assert kern.process_event(emel.OpSoftMaxExt(px.dview(), mv, po.dview(), 0.3)) == emel.Status.OK
+        got = po.download()
+        for p in (pfull, px, po):
+            p.free()
+        close(got, want, 1e-30, "ring softmax unaligned f16 mask")
+        return
+    got, want = run_row_op(emel, kern, oracle_lib, "soft_max_ext", x, [kv, q, h, b], mask=mask, scale=0.3)
+    close(got, want, 1e-30, f"ring softmax {mask_kind}")
