@@ -140,6 +140,16 @@ struct Arith {
     }
 };
 
+// GELU's tanh approximation of an already binary16-rounded input q
+// (unary.rs:533-539, between the two binary16 round trips).
+template <bool EXACT>
+__device__ __forceinline__ float gelu_tanh_core(float q) {
+    using A = Arith<EXACT>;
+    const float cube = A::mul(A::mul(A::mul(0.044715f, q), q), q);
+    const float inner = A::mul(0.7978846f, A::add(q, cube));
+    return A::mul(A::mul(0.5f, q), A::add(1.0f, A::tanh(inner)));
+}
+
 template <int OP, bool EXACT, bool IN_F16 = false>
 __device__ __forceinline__ float unary_formula(float v, UnaryParams p) {
     using A = Arith<EXACT>;
@@ -157,9 +167,7 @@ __device__ __forceinline__ float unary_formula(float v, UnaryParams p) {
         // an f16 input is already binary16, and an f16 store rounds the
         // output the same way: the fast path skips both round trips
         const float q = (IN_F16 && !EXACT) ? v : A::round_f16(v);
-        const float cube = A::mul(A::mul(A::mul(0.044715f, q), q), q);
-        const float inner = A::mul(0.7978846f, A::add(q, cube));
-        const float approx = A::mul(A::mul(0.5f, q), A::add(1.0f, A::tanh(inner)));
+        const float approx = gelu_tanh_core<EXACT>(q);
         return (IN_F16 && !EXACT) ? approx : A::round_f16(approx);
     }
     if constexpr (OP == kGeluQuick) {

@@ -30,6 +30,7 @@
 #include "common.cuh"
 #include "launch.hpp"
 #include "rowreduce.cuh"
+#include "tma.cuh"
 
 namespace emel {
 
@@ -38,7 +39,6 @@ namespace {
 constexpr int kRingStagesMax = 4;
 constexpr int kRingThreads = 256;
 constexpr uint32_t kRingSmemPerSm = 220 * 1024;
-constexpr uint64_t kWaitLimitNs = 2000000000ull;
 constexpr uint32_t kStageAlign = 128;
 
 enum RingOp { kRingNorm = 0, kRingRms = 1, kRingRmsMul = 2, kRingSoftMax = 3 };
@@ -70,55 +70,6 @@ struct RingArgs {
     int stages;
     float param;  // eps (norms) or scale (soft_max)
 };
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
-
-__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
-    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
-}
-
-__device__ __forceinline__ void mbar_expect_tx(uint64_t* bar, uint32_t bytes) {
-    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes) : "memory");
-}
-
-// global -> shared bulk copy through the TMA engine; bytes and both
-// addresses are multiples of 16.
-__device__ __forceinline__ void bulk_load(void* dst_smem, const void* src, uint32_t bytes, uint64_t* bar) {
-    asm volatile("cp.async.bulk.shared::cta.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-                     smem_u32(dst_smem)),
-                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
-                 : "memory");
-}
-
-__device__ __forceinline__ bool mbar_try(uint64_t* bar, uint32_t parity) {
-    uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(smem_u32(bar)), "r"(parity)
-        : "memory");
-    return ok != 0;
-}
-
-__device__ __forceinline__ uint64_t global_ns() {
-    uint64_t t;
-    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
-    return t;
-}
-
-// Waits for the phase with the given parity; false after kWaitLimitNs (or
-// 2^30 polls, whichever comes first).
-__device__ __noinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
-    if (mbar_try(bar, parity)) return true;
-    const uint64_t t0 = global_ns();
-    for (uint32_t i = 0; i < (1u << 30); ++i) {
-        if (mbar_try(bar, parity)) return true;
-        if ((i & 63u) == 0 && global_ns() - t0 > kWaitLimitNs) return false;
-    }
-    return false;
-}
 
 __device__ __forceinline__ void row_coords(uint32_t r, const RingArgs& a, uint32_t& i1, uint32_t& i2, uint32_t& i3) {
     const uint32_t q = fdiv(r, a.d1);
@@ -201,7 +152,7 @@ __global__ void __launch_bounds__(T, 1024 / T) row_ring(RingArgs a) {
 
     if (tid == 0) {
         for (int s = 0; s < S; ++s) mbar_init(&full[s], 1);
-        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        mbar_init_fence();
     }
     if constexpr (OP == kRingRmsMul) {
         float* w = reinterpret_cast<float*>(ring_smem);

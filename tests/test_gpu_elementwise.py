@@ -276,6 +276,55 @@ def test_cfg2_unary_sweep_full_size(emel, kern, olib, dtype):
         check_unary(op, got, want, want_cr, f"cfg2 {name} {np.dtype(dtype).name}")
 
 
+@pytest.mark.parametrize("op", UNARY_ALL)
+def test_f16_every_input_large_tensor_matches_small(emel, kern, olib, op):
+    """Every binary16 bit pattern (NaN payloads, infinities, subnormals, both
+    zeros), once in a small tensor and 16 times plus a 5-element tail in a
+    tensor of more than 2^20 elements.  Large dense binary16 tensors of the
+    transcendental ops take the per-launch domain-table path, small ones the
+    direct kernels: both must give the same bits, and match the oracle."""
+    every = np.arange(65536, dtype=np.uint16).view(np.float16)
+    small, want, want_cr = run_unary(emel, kern, olib, op, every)
+    check_unary(op, small, want, want_cr, f"f16 every input op={op}")
+    big = np.concatenate([np.tile(every, 16), every[1000:1005]])
+    got_big, _, _ = run_unary_device_only(emel, kern, op, big)
+    gh.assert_bits_equal(got_big, np.concatenate([np.tile(small, 16), small[1000:1005]]),
+                         f"f16 op={op}: large (table) vs small (direct)")
+
+
+def test_gelu_f32_large_tensor_matches_small(emel, kern, olib):
+    """binary32 GELU on more than 2^20 dense elements uses the binary16 domain
+    table (the formula sees only binary16-rounded inputs); smaller tensors
+    use the direct kernel.  Both must agree bit for bit, including inputs
+    next to +-10 that round to +-10 in binary16, NaN payloads and
+    infinities, and match the oracle."""
+    rng = np.random.default_rng(8)
+    near = np.array([9.99609375, 9.996094, 9.9960937, 9.999999, 10.0, -9.99609375, -9.996094, -9.999999, -10.0,
+                     np.nextafter(np.float32(10), np.float32(0)), np.nextafter(np.float32(-10), np.float32(0)),
+                     65519.0, 65520.0, 1e-8, -1e-8, 6e-8, 0.0, -0.0, np.inf, -np.inf], dtype=np.float32)
+    nans = np.array([0x7fc00000, 0xffc00000, 0x7f800001, 0xff812345, 0x7fbfffff], dtype=np.uint32).view(np.float32)
+    x = np.concatenate([rng.uniform(-11, 11, 1 << 21).astype(np.float32), near, nans,
+                        (rng.standard_normal(1 << 16) * 1e-3).astype(np.float32)])
+    got_big, _, _ = run_unary_device_only(emel, kern, 8, x)
+    parts = [run_unary_device_only(emel, kern, 8, c)[0] for c in np.array_split(x, 4)]
+    gh.assert_bits_equal(got_big, np.concatenate(parts), "gelu f32: large (table) vs small (direct)")
+    small = np.concatenate([near, nans, x[:200000]])
+    got, want, want_cr = run_unary(emel, kern, olib, 8, small)
+    check_unary(8, got, want, want_cr, "gelu f32 edge values")
+
+
+def run_unary_device_only(emel, kern, op, x):
+    ctx = kern.ctx
+    px = gh.Pair(emel, ctx, x)
+    po = gh.Pair(emel, ctx, np.zeros_like(x))
+    st = kern.process_event(emel.OpUnaryTyped(emel.UnaryOp(op), px.dview(), po.dview()))
+    assert st == emel.Status.OK, ctx.last_error
+    got = po.download()
+    px.free()
+    po.free()
+    return got, None, None
+
+
 def test_unary_strided_and_count_equal_views(emel, kern, olib):
     rng = np.random.default_rng(3)
     x = rng.standard_normal(4000).astype(np.float32)
