@@ -137,6 +137,44 @@ __device__ __forceinline__ float4 mask4(const RingArgs& a, const unsigned char* 
     return make_float4(r[0], r[1], r[2], r[3]);
 }
 
+// v = x * scale (+ mask) for the fast soft_max pass: plain IEEE operations
+// and hardware binary16 conversion (NaN payloads are irrelevant there: a
+// NaN sends the row to the exact pass).
+__device__ __forceinline__ float4 scaled4_fast(const RingArgs& a, const float* row, const unsigned char* stage,
+                                               int64_t moff, uint32_t v) {
+    float4 x = ld_f4(row + 4 * v);
+    if (!a.apply_scale) return x;
+    x = make_float4(__fmul_rn(x.x, a.param), __fmul_rn(x.y, a.param), __fmul_rn(x.z, a.param), __fmul_rn(x.w, a.param));
+    if (a.aux_mode == kAuxNone) return x;
+    float4 mk;
+    if (a.aux_mode == kAuxMaskStaged && a.aux_f16) {
+        const uint2 h = reinterpret_cast<const uint2*>(stage + a.mask_offset)[v];
+        const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+        const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
+        mk = make_float4(lo.x, lo.y, hi.x, hi.y);
+    } else {
+        mk = mask4(a, stage, moff, v);
+    }
+    return make_float4(__fadd_rn(x.x, mk.x), __fadd_rn(x.y, mk.y), __fadd_rn(x.z, mk.z), __fadd_rn(x.w, mk.w));
+}
+
+// exp of a non-NaN z <= 0 (fast_expf without its overflow branch).
+__device__ __forceinline__ float exp_nonpositive(float z) { return z < -104.0f ? 0.0f : (float)exp_core((double)z); }
+
+// e / d rounded once, for 0 <= e <= 1 and a finite d >= 1, given
+// inv = RN(1 / d): q0 = RN(e * inv) is within one ulp of e / d, the FMA
+// residual e - d * q0 is exact, and RN(q0 + residual * inv) is the
+// correctly rounded quotient (Markstein's theorem on reciprocal-based
+// division).  Quotients that could leave the normal range use the divider.
+__device__ __forceinline__ float div_by(float e, float d, float inv) {
+    if (e >= 0x1p-60f) {
+        const float q0 = __fmul_rn(e, inv);
+        const float res = __fmaf_rn(-d, q0, e);
+        return __fmaf_rn(res, inv, q0);
+    }
+    return __fdiv_rn(e, d);
+}
+
 template <int OP, int T>
 __global__ void __launch_bounds__(T, 1024 / T) row_ring(RingArgs a) {
     extern __shared__ __align__(128) unsigned char ring_smem[];
@@ -246,42 +284,80 @@ __global__ void __launch_bounds__(T, 1024 / T) row_ring(RingArgs a) {
         } else {
             // soft_max (reductions.rs:565-638): v = x * scale (+ mask); max
             // (starting from element 0); e = exp(v - max); sum in f64; e / sum.
+            //
+            // Fast pass: plain IEEE arithmetic.  While no v is NaN and the
+            // maximum is finite no step can produce a NaN, so the x86 NaN
+            // rules never apply and the plain results are the reference's
+            // bits.  A NaN lane reports +inf to the max reduction; a row
+            // whose maximum comes back non-finite is redone exactly below.
             const int64_t moff = a.aux_mode == kAuxMaskLoads ? mask_offset(r, a) : 0;
-            float m = bitsf(0x7fc00000u);  // NaN = "no value yet"
+            float m = bitsf(0x7fc00000u);  // NaN = "no value yet" (fmaxf skips it)
+            bool odd = false;
             for (uint32_t v = tid; v < nvec; v += T) {
-                float4 x = ld_f4(row + 4 * v);
-                if (a.apply_scale) {
-                    x = make_float4(f_mul(x.x, a.param), f_mul(x.y, a.param), f_mul(x.z, a.param), f_mul(x.w, a.param));
-                    if (a.aux_mode != kAuxNone) {
-                        const float4 mk = mask4(a, stage, moff, v);
-                        x = make_float4(f_add(x.x, mk.x), f_add(x.y, mk.y), f_add(x.z, mk.z), f_add(x.w, mk.w));
-                    }
-                    reinterpret_cast<float4*>(row)[v] = x;
+                const float4 s = scaled4_fast(a, row, stage, moff, v);
+                odd = odd || is_nan(s.x) || is_nan(s.y) || is_nan(s.z) || is_nan(s.w);
+                m = fmaxf(fmaxf(m, s.x), fmaxf(s.y, fmaxf(s.z, s.w)));
+            }
+            m = group_max<T>(odd ? INFINITY : m, &red);
+            if (isfinite(m)) {
+                double acc = 0.0;
+                for (uint32_t v = tid; v < nvec; v += T) {
+                    const float4 s = scaled4_fast(a, row, stage, moff, v);
+                    const float4 e = make_float4(exp_nonpositive(__fsub_rn(s.x, m)), exp_nonpositive(__fsub_rn(s.y, m)),
+                                                 exp_nonpositive(__fsub_rn(s.z, m)), exp_nonpositive(__fsub_rn(s.w, m)));
+                    reinterpret_cast<float4*>(row)[v] = e;
+                    acc += (double)e.x;
+                    acc += (double)e.y;
+                    acc += (double)e.z;
+                    acc += (double)e.w;
                 }
-                m = max_nn(m, x.x);
-                m = max_nn(m, x.y);
-                m = max_nn(m, x.z);
-                m = max_nn(m, x.w);
-            }
-            m = group_max<T>(m, &red);  // its barriers also publish row[0]
-            const float first = row[0];
-            if (is_nan(first)) m = first;  // reductions.rs:572: the scan starts from element 0
-            double acc = 0.0;
-            for (uint32_t v = tid; v < nvec; v += T) {
-                const float4 x = ld_f4(row + 4 * v);
-                const float4 e = make_float4(lm_exp(f_sub(x.x, m)), lm_exp(f_sub(x.y, m)), lm_exp(f_sub(x.z, m)),
-                                             lm_exp(f_sub(x.w, m)));
-                reinterpret_cast<float4*>(row)[v] = e;
-                acc += (double)e.x;
-                acc += (double)e.y;
-                acc += (double)e.z;
-                acc += (double)e.w;
-            }
-            acc = block_sum<T>(acc, &red);
-            const float denom = __double2float_rn(acc);
-            for (uint32_t v = tid; v < nvec; v += T) {
-                const float4 e = ld_f4(row + 4 * v);
-                store4<OP>(a, drow, v, make_float4(f_div(e.x, denom), f_div(e.y, denom), f_div(e.z, denom), f_div(e.w, denom)));
+                acc = block_sum<T>(acc, &red);
+                const float denom = __double2float_rn(acc);  // >= 1: the maximum contributes exp(0)
+                const float inv = __frcp_rn(denom);
+                for (uint32_t v = tid; v < nvec; v += T) {
+                    const float4 e = ld_f4(row + 4 * v);
+                    store4<OP>(a, drow, v,
+                               make_float4(div_by(e.x, denom, inv), div_by(e.y, denom, inv), div_by(e.z, denom, inv),
+                                           div_by(e.w, denom, inv)));
+                }
+            } else {
+                m = bitsf(0x7fc00000u);
+                for (uint32_t v = tid; v < nvec; v += T) {
+                    float4 x = ld_f4(row + 4 * v);
+                    if (a.apply_scale) {
+                        x = make_float4(f_mul(x.x, a.param), f_mul(x.y, a.param), f_mul(x.z, a.param), f_mul(x.w, a.param));
+                        if (a.aux_mode != kAuxNone) {
+                            const float4 mk = mask4(a, stage, moff, v);
+                            x = make_float4(f_add(x.x, mk.x), f_add(x.y, mk.y), f_add(x.z, mk.z), f_add(x.w, mk.w));
+                        }
+                        reinterpret_cast<float4*>(row)[v] = x;
+                    }
+                    m = max_nn(m, x.x);
+                    m = max_nn(m, x.y);
+                    m = max_nn(m, x.z);
+                    m = max_nn(m, x.w);
+                }
+                m = group_max<T>(m, &red);  // its barriers also publish row[0]
+                const float first = row[0];
+                if (is_nan(first)) m = first;  // reductions.rs:572: the scan starts from element 0
+                double acc = 0.0;
+                for (uint32_t v = tid; v < nvec; v += T) {
+                    const float4 x = ld_f4(row + 4 * v);
+                    const float4 e = make_float4(lm_exp(f_sub(x.x, m)), lm_exp(f_sub(x.y, m)), lm_exp(f_sub(x.z, m)),
+                                                 lm_exp(f_sub(x.w, m)));
+                    reinterpret_cast<float4*>(row)[v] = e;
+                    acc += (double)e.x;
+                    acc += (double)e.y;
+                    acc += (double)e.z;
+                    acc += (double)e.w;
+                }
+                acc = block_sum<T>(acc, &red);
+                const float denom = __double2float_rn(acc);
+                for (uint32_t v = tid; v < nvec; v += T) {
+                    const float4 e = ld_f4(row + 4 * v);
+                    store4<OP>(a, drow, v,
+                               make_float4(f_div(e.x, denom), f_div(e.y, denom), f_div(e.z, denom), f_div(e.w, denom)));
+                }
             }
         }
         __syncthreads();  // every thread is done with this stage

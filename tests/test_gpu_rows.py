@@ -329,3 +329,28 @@ def test_ring_softmax_ext_masks(emel, kern, oracle_lib, mask_kind):
         return
     got, want = run_row_op(emel, kern, oracle_lib, "soft_max_ext", x, [kv, q, h, b], mask=mask, scale=0.3)
     close(got, want, 1e-30, f"ring softmax {mask_kind}")
+
+
+def test_ring_softmax_special_rows_take_the_exact_pass(emel, kern, oracle_lib):
+    """Rows of 2048 with NaN (first element, middle), +inf, all -inf and a NaN
+    in the mask: the fast pass hands these rows to the exact one, whose NaN
+    payloads follow the reference; ordinary rows alongside stay exact too."""
+    rng = np.random.default_rng(45)
+    kv, q = 2048, 8
+    x = (rng.standard_normal(kv * q) * 3).astype(np.float32).reshape(q, kv)
+    x[1, 0] = np.uint32(0x7fa00001).view(np.float32)  # signalling NaN first
+    x[2, 700] = np.nan
+    x[3, 5] = np.inf
+    x[4, :] = -np.inf
+    x[5, 3] = -np.inf
+    mask = np.zeros((q, kv), np.float16)
+    mask[6, 1000] = np.float16(np.nan)
+    mask[7, :] = -np.inf
+    mask[7, 9] = 0
+    for scale, m in ((1.0, None), (0.5, (mask.ravel(), [kv, q, 1, 1], None))):
+        kind = "soft_max" if m is None else "soft_max_ext"
+        got, want = run_row_op(emel, kern, oracle_lib, kind, x.ravel(), [kv, q, 1, 1], mask=m, scale=scale)
+        nan = np.isnan(want)
+        assert np.array_equal(np.isnan(got), nan), f"ring {kind}: NaN positions"
+        gh.assert_bits_equal(got[nan], want[nan], f"ring {kind} special rows: NaN payloads")
+        close(got[~nan], want[~nan], 1e-30, f"ring {kind} special rows")
