@@ -874,7 +874,8 @@ emel_cuda_status emel_cuda_sum_rows(emel_cuda_context* ctx, void* stream, const 
         return EMEL_CUDA_INVALID_VIEW;
     if (!rows_shape(src, dst)) return EMEL_CUDA_SHAPE_MISMATCH;
     if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
-    const emel::RowPlan p = plan_rows(src, cs, dst, &cd);
+    emel::RowPlan p = plan_rows(src, cs, dst, &cd);
+    p.vec = p.ne[0] % 4 == 0 && row_vec_ok(p.src);  // dst is written one value per row
     cudaError_t err = select_device(ctx);
     if (err == cudaSuccess) err = emel::launch_sum_rows(env_of(ctx, stream), p);
     return device_status(ctx, err);
@@ -935,6 +936,7 @@ emel_cuda_status emel_cuda_argmax_rows(emel_cuda_context* ctx, void* stream, con
     if (!rows_shape(src, dst)) return EMEL_CUDA_SHAPE_MISMATCH;
     if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
     emel::RowPlan p = plan_rows(src, cs, dst, &cd);
+    p.vec = p.ne[0] % 4 == 0 && row_vec_ok(p.src);  // dst is written one index per row
     cudaError_t err = select_device(ctx);
     if (err == cudaSuccess) err = emel::launch_argmax_rows(env_of(ctx, stream), p, (int)dst->dtype);
     return device_status(ctx, err);

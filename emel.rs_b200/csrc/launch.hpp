@@ -34,6 +34,12 @@ cudaError_t launch_argmax(const LaunchEnv& env, const RowPlan& plan, int out_kin
 bool launch_row_ring(const LaunchEnv& env, const RowPlan& plan, int op, float param, bool apply_scale,
                      cudaError_t* err);
 
+// Few long rows (rowsplit.cu): one 8-CTA cluster per row.
+bool split_rows_wanted(const LaunchEnv& env, const RowPlan& plan);
+cudaError_t launch_argmax_rows_split(const LaunchEnv& env, const RowPlan& plan, int dst_dtype);
+cudaError_t launch_sum_rows_split(const LaunchEnv& env, const RowPlan& plan);
+cudaError_t launch_soft_max_split(const LaunchEnv& env, const RowPlan& plan, bool apply_scale, float scale);
+
 // Byte offset, inside the workspace's 256-byte header, of the fault word a
 // kernel sets when one of its bounded waits expires.
 constexpr uint64_t kFaultWordOffset = 64;

@@ -546,6 +546,7 @@ uint64_t soft_max_cluster_capacity() { return 8ull * 1024 * kMaxE; }
 cudaError_t launch_soft_max(const LaunchEnv& env, const RowPlan& p, bool apply_scale, float scale) {
     cudaError_t ring_err;
     if (launch_row_ring(env, p, 3, scale, apply_scale, &ring_err)) return ring_err;
+    if (p.dense && split_rows_wanted(env, p)) return launch_soft_max_split(env, p, apply_scale, scale);
     const bool long_row = resident_group(p.ne[0]) == 0 && (!p.vec || p.ne[0] > soft_max_cluster_capacity());
     if (p.dst_ordinal || (!p.dense && p.ne[0] * sizeof(float) > 200 * 1024) || (p.dense && long_row)) {
         softmax_rows_stream<<<row_grid(env, p.rows, 1, 2), 1024, 0, env.stream>>>(p, apply_scale, scale);
@@ -607,6 +608,7 @@ static int stream_group(uint64_t ne0) {
 }
 
 cudaError_t launch_sum_rows(const LaunchEnv& env, const RowPlan& p) {
+    if (split_rows_wanted(env, p)) return launch_sum_rows_split(env, p);
     const int g = stream_group(p.ne[0]);
     if (g == 32) sum_rows_kernel<32><<<row_grid(env, p.rows, 8, 8), 256, 0, env.stream>>>(p);
     else if (g == 256) sum_rows_kernel<256><<<row_grid(env, p.rows, 1, 8), 256, 0, env.stream>>>(p);
@@ -616,6 +618,7 @@ cudaError_t launch_sum_rows(const LaunchEnv& env, const RowPlan& p) {
 }
 
 cudaError_t launch_argmax_rows(const LaunchEnv& env, const RowPlan& p, int dst_dtype) {
+    if (split_rows_wanted(env, p)) return launch_argmax_rows_split(env, p, dst_dtype);
     const int g = stream_group(p.ne[0]);
     if (g == 32) argmax_rows_kernel<32><<<row_grid(env, p.rows, 8, 8), 256, 0, env.stream>>>(p, dst_dtype);
     else if (g == 256) argmax_rows_kernel<256><<<row_grid(env, p.rows, 1, 8), 256, 0, env.stream>>>(p, dst_dtype);

@@ -1,0 +1,342 @@
+// Row operators over few, long rows (vocabulary logits: 151,936 columns,
+// tens of rows): one thread-block cluster of kSplitCluster CTAs per row, CTA
+// k owning the k-th contiguous chunk of columns, partial results exchanged
+// through distributed shared memory and folded in rank order (so the result
+// does not depend on timing).  One CTA per row would leave most SMs idle.
+//
+//   * argmax_rows: one pass; partial (value, index) per CTA, earliest index
+//     on ties, NaN at column 0 pins the index to 0 (reductions.rs:715-730);
+//   * sum_rows: one pass; f64 partial per CTA (reductions.rs:684-700);
+//   * soft_max (dense views): pass 1 reads the chunk from HBM for the
+//     maximum, pass 2 re-reads it (from L2: a cluster's chunks are in flight
+//     together) and writes e = exp(v - max) to dst, pass 3 divides dst by
+//     the f64 sum in place.  The fast/exact split is the ring kernel's: plain
+//     IEEE arithmetic unless a NaN or a non-finite maximum shows up, in which
+//     case every CTA of the cluster redoes the row with the x86 NaN rules.
+#include <cooperative_groups.h>
+
+#include "common.cuh"
+#include "launch.hpp"
+#include "rowreduce.cuh"
+
+namespace cg = cooperative_groups;
+
+namespace emel {
+
+namespace {
+
+constexpr int kSplitThreads = 256;  // 64 vocabulary rows x 8 CTAs stay resident at once
+constexpr int kSplitCluster = 8;
+
+__device__ __forceinline__ int64_t split_row_base(const RowOperand& o, uint64_t r, uint64_t ne1, uint64_t ne2) {
+    const uint64_t i1 = r % ne1, q = r / ne1, i2 = q % ne2, i3 = q / ne2;
+    return (int64_t)i1 * o.st[1] + (int64_t)i2 * o.st[2] + (int64_t)i3 * o.st[3];
+}
+
+__device__ __forceinline__ int64_t split_mask_base(const RowOperand& m, uint64_t r, uint64_t ne1, uint64_t ne2) {
+    const uint64_t i1 = r % ne1, q = r / ne1, i2 = q % ne2, i3 = q / ne2;
+    return (int64_t)i1 * m.st[1] + (int64_t)(i2 % m.ne[2]) * m.st[2] + (int64_t)(i3 % m.ne[3]) * m.st[3];
+}
+
+struct Chunk {
+    uint64_t col0, col1;
+};
+
+__device__ __forceinline__ Chunk my_chunk(uint64_t ne0, uint64_t chunk, unsigned rank) {
+    const uint64_t c0 = (uint64_t)rank * chunk;
+    return Chunk{c0 < ne0 ? c0 : ne0, c0 + chunk < ne0 ? c0 + chunk : ne0};
+}
+
+__device__ __forceinline__ void arg_take(ArgBest& b, float v, int64_t i) {
+    if ((!b.has && !is_nan(v)) || v > b.v) {
+        b.v = v;
+        b.i = i;
+        b.has = 1;
+    }
+}
+
+__global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitThreads)
+    argmax_rows_split(RowPlan p, int dst_dtype, uint64_t chunk) {
+    __shared__ GroupScratch<kSplitThreads> s;
+    __shared__ float pv;
+    __shared__ int64_t pi;
+    __shared__ uint32_t ph;
+    cg::cluster_group cluster = cg::this_cluster();
+    const unsigned rank = cluster.block_rank();
+    const uint64_t r = blockIdx.x / kSplitCluster;
+    const Chunk ch = my_chunk(p.ne[0], chunk, rank);
+    const float* row = reinterpret_cast<const float*>(p.src.ptr) + split_row_base(p.src, r, p.ne[1], p.ne[2]);
+    ArgBest b{0.0f, 0, 0};
+    if (p.vec) {
+        const float4* r4 = reinterpret_cast<const float4*>(row);
+        const uint64_t v0 = ch.col0 / 4, v1 = ch.col1 / 4;  // chunk edges are multiples of 4 (ne0 too)
+        uint64_t v = v0 + threadIdx.x;
+        for (; v + 3 * kSplitThreads < v1; v += 4 * kSplitThreads) {
+            float4 q[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) q[k] = __ldcs(r4 + v + k * kSplitThreads);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int64_t c = (int64_t)(v + k * kSplitThreads) * 4;
+                arg_take(b, q[k].x, c);
+                arg_take(b, q[k].y, c + 1);
+                arg_take(b, q[k].z, c + 2);
+                arg_take(b, q[k].w, c + 3);
+            }
+        }
+        for (; v < v1; v += kSplitThreads) {
+            const float4 q = __ldcs(r4 + v);
+            const int64_t c = (int64_t)v * 4;
+            arg_take(b, q.x, c);
+            arg_take(b, q.y, c + 1);
+            arg_take(b, q.z, c + 2);
+            arg_take(b, q.w, c + 3);
+        }
+    } else {
+        for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kSplitThreads)
+            arg_take(b, row[(int64_t)c * p.src.st[0]], (int64_t)c);
+    }
+    b = group_argmax<kSplitThreads>(b, &s);
+    if (threadIdx.x == 0) {
+        pv = b.v;
+        pi = b.i;
+        ph = b.has;
+    }
+    cluster.sync();
+    if (rank == 0 && threadIdx.x == 0) {
+        ArgBest best{0.0f, 0, 0};
+        for (int k = 0; k < kSplitCluster; ++k)
+            best = arg_better(best, ArgBest{*cluster.map_shared_rank(&pv, k), *cluster.map_shared_rank(&pi, k),
+                                            *cluster.map_shared_rank(&ph, k)});
+        const int64_t idx = (is_nan(row[0]) || !best.has) ? 0 : best.i;
+        const int64_t off = split_row_base(p.dst, r, p.ne[1], p.ne[2]);
+        if (dst_dtype == (int)DType::I64) reinterpret_cast<int64_t*>(p.dst.ptr)[off] = idx;
+        else if (dst_dtype == (int)DType::I32) reinterpret_cast<int32_t*>(p.dst.ptr)[off] = (int32_t)idx;
+        else reinterpret_cast<float*>(p.dst.ptr)[off] = (float)idx;
+    }
+    cluster.sync();  // peers' shared memory stays alive until rank 0 has read it
+}
+
+__global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitThreads)
+    sum_rows_split(RowPlan p, uint64_t chunk) {
+    __shared__ GroupScratch<kSplitThreads> s;
+    __shared__ double part;
+    cg::cluster_group cluster = cg::this_cluster();
+    const unsigned rank = cluster.block_rank();
+    const uint64_t r = blockIdx.x / kSplitCluster;
+    const Chunk ch = my_chunk(p.ne[0], chunk, rank);
+    const float* row = reinterpret_cast<const float*>(p.src.ptr) + split_row_base(p.src, r, p.ne[1], p.ne[2]);
+    double acc = 0.0;
+    if (p.vec) {
+        const float4* r4 = reinterpret_cast<const float4*>(row);
+        for (uint64_t v = ch.col0 / 4 + threadIdx.x; v < ch.col1 / 4; v += kSplitThreads) {
+            const float4 q = __ldcs(r4 + v);
+            acc += (double)q.x;
+            acc += (double)q.y;
+            acc += (double)q.z;
+            acc += (double)q.w;
+        }
+    } else {
+        for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kSplitThreads) acc += (double)row[(int64_t)c * p.src.st[0]];
+    }
+    acc = group_sum<kSplitThreads>(acc, &s);
+    if (threadIdx.x == 0) part = acc;
+    cluster.sync();
+    if (rank == 0 && threadIdx.x == 0) {
+        double t = 0.0;
+        for (int k = 0; k < kSplitCluster; ++k) t += *cluster.map_shared_rank(&part, k);
+        reinterpret_cast<float*>(p.dst.ptr)[split_row_base(p.dst, r, p.ne[1], p.ne[2])] = __double2float_rn(t);
+    }
+    cluster.sync();
+}
+
+// --- soft_max -----------------------------------------------------------------
+struct SoftmaxRow {
+    const float* x;
+    float* y;
+    int64_t xs, ys;  // dim-0 strides (elements)
+    int64_t mbase;
+    bool has_mask;
+};
+
+__device__ __forceinline__ float mask_at(const RowPlan& p, const SoftmaxRow& w, uint64_t c) {
+    const int64_t e = w.mbase + (int64_t)c * p.aux.st[0];
+    return p.aux_dtype == (int)DType::F16 ? f16_bits_to_f32(reinterpret_cast<const uint16_t*>(p.aux.ptr)[e])
+                                          : reinterpret_cast<const float*>(p.aux.ptr)[e];
+}
+
+template <bool EXACT>
+__device__ __forceinline__ float value_at(const RowPlan& p, const SoftmaxRow& w, uint64_t c, bool apply_scale,
+                                          float scale) {
+    float v = w.x[(int64_t)c * w.xs];
+    if (!apply_scale) return v;
+    v = EXACT ? f_mul(v, scale) : __fmul_rn(v, scale);
+    if (w.has_mask) v = EXACT ? f_add(v, mask_at(p, w, c)) : __fadd_rn(v, mask_at(p, w, c));
+    return v;
+}
+
+__device__ __forceinline__ float exp_nonpositive_split(float z) {
+    return z < -104.0f ? 0.0f : (float)exp_core((double)z);
+}
+
+// See rowring.cu: correctly rounded e / d for 0 <= e <= 1, finite d >= 1.
+__device__ __forceinline__ float div_by_split(float e, float d, float inv) {
+    if (e >= 0x1p-60f) {
+        const float q0 = __fmul_rn(e, inv);
+        const float res = __fmaf_rn(-d, q0, e);
+        return __fmaf_rn(res, inv, q0);
+    }
+    return __fdiv_rn(e, d);
+}
+
+__global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitThreads)
+    softmax_rows_split(RowPlan p, bool apply_scale, float scale, uint64_t chunk) {
+    __shared__ GroupScratch<kSplitThreads> s;
+    __shared__ float part_max;
+    __shared__ double part_sum;
+    cg::cluster_group cluster = cg::this_cluster();
+    const unsigned rank = cluster.block_rank();
+    const uint64_t r = blockIdx.x / kSplitCluster;
+    const Chunk ch = my_chunk(p.ne[0], chunk, rank);
+    SoftmaxRow w;
+    w.x = reinterpret_cast<const float*>(p.src.ptr) + split_row_base(p.src, r, p.ne[1], p.ne[2]);
+    w.y = reinterpret_cast<float*>(p.dst.ptr) + split_row_base(p.dst, r, p.ne[1], p.ne[2]);
+    w.xs = p.src.st[0];
+    w.ys = p.dst.st[0];
+    w.has_mask = apply_scale && p.has_aux;
+    w.mbase = w.has_mask ? split_mask_base(p.aux, r, p.ne[1], p.ne[2]) : 0;
+    const bool vec = p.vec && !w.has_mask;
+    const float4* x4 = reinterpret_cast<const float4*>(w.x);
+    float4* y4 = reinterpret_cast<float4*>(w.y);
+    auto scale4 = [&](float4 q) {
+        return apply_scale ? make_float4(__fmul_rn(q.x, scale), __fmul_rn(q.y, scale), __fmul_rn(q.z, scale),
+                                         __fmul_rn(q.w, scale))
+                           : q;
+    };
+
+    // pass 1: maximum (fast values); a NaN lane reports +inf
+    float m = bitsf(0x7fc00000u);
+    bool odd = false;
+    if (vec) {
+        for (uint64_t v = ch.col0 / 4 + threadIdx.x; v < ch.col1 / 4; v += kSplitThreads) {
+            const float4 q = scale4(__ldcg(x4 + v));
+            odd = odd || is_nan(q.x) || is_nan(q.y) || is_nan(q.z) || is_nan(q.w);
+            m = fmaxf(fmaxf(m, q.x), fmaxf(q.y, fmaxf(q.z, q.w)));
+        }
+    } else {
+        for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kSplitThreads) {
+            const float v = value_at<false>(p, w, c, apply_scale, scale);
+            odd = odd || is_nan(v);
+            m = fmaxf(m, v);
+        }
+    }
+    m = group_max<kSplitThreads>(odd ? INFINITY : m, &s);
+    if (threadIdx.x == 0) part_max = m;
+    cluster.sync();
+    float gm = bitsf(0x7fc00000u);
+    for (int k = 0; k < kSplitCluster; ++k) gm = max_nn(gm, *cluster.map_shared_rank(&part_max, k));
+
+    double acc = 0.0;
+    if (isfinite(gm)) {
+        // pass 2: e = exp(v - max) into dst, f64 sum
+        if (vec) {
+            for (uint64_t v = ch.col0 / 4 + threadIdx.x; v < ch.col1 / 4; v += kSplitThreads) {
+                const float4 q = scale4(__ldcg(x4 + v));
+                const float4 e = make_float4(exp_nonpositive_split(__fsub_rn(q.x, gm)), exp_nonpositive_split(__fsub_rn(q.y, gm)),
+                                             exp_nonpositive_split(__fsub_rn(q.z, gm)), exp_nonpositive_split(__fsub_rn(q.w, gm)));
+                y4[v] = e;
+                acc += (double)e.x;
+                acc += (double)e.y;
+                acc += (double)e.z;
+                acc += (double)e.w;
+            }
+        } else {
+            for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kSplitThreads) {
+                const float e = exp_nonpositive_split(__fsub_rn(value_at<false>(p, w, c, apply_scale, scale), gm));
+                w.y[(int64_t)c * w.ys] = e;
+                acc += (double)e;
+            }
+        }
+    } else {
+        // exact pass: the reference's NaN rules (first element pins a NaN max)
+        const float v0 = value_at<true>(p, w, 0, apply_scale, scale);
+        float em = bitsf(0x7fc00000u);
+        __syncthreads();
+        for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kSplitThreads)
+            em = max_nn(em, value_at<true>(p, w, c, apply_scale, scale));
+        em = group_max<kSplitThreads>(em, &s);
+        if (threadIdx.x == 0) part_max = em;
+        cluster.sync();
+        gm = bitsf(0x7fc00000u);
+        for (int k = 0; k < kSplitCluster; ++k) gm = max_nn(gm, *cluster.map_shared_rank(&part_max, k));
+        if (is_nan(v0)) gm = v0;
+        for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kSplitThreads) {
+            const float e = lm_exp(f_sub(value_at<true>(p, w, c, apply_scale, scale), gm));
+            w.y[(int64_t)c * w.ys] = e;
+            acc += (double)e;
+        }
+    }
+    acc = group_sum<kSplitThreads>(acc, &s);
+    if (threadIdx.x == 0) part_sum = acc;
+    cluster.sync();  // also orders every CTA's pass-2 stores before pass 3 reads its own
+    double total = 0.0;
+    for (int k = 0; k < kSplitCluster; ++k) total += *cluster.map_shared_rank(&part_sum, k);
+    const float denom = __double2float_rn(total);
+    // pass 3: divide in place (each thread rereads the values it wrote)
+    if (isfinite(gm) && isfinite(denom)) {
+        const float inv = __frcp_rn(denom);
+        if (vec) {
+            for (uint64_t v = ch.col0 / 4 + threadIdx.x; v < ch.col1 / 4; v += kSplitThreads) {
+                const float4 e = y4[v];
+                __stcs(y4 + v, make_float4(div_by_split(e.x, denom, inv), div_by_split(e.y, denom, inv),
+                                           div_by_split(e.z, denom, inv), div_by_split(e.w, denom, inv)));
+            }
+        } else {
+            for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kSplitThreads) {
+                float* o = w.y + (int64_t)c * w.ys;
+                *o = div_by_split(*o, denom, inv);
+            }
+        }
+    } else {
+        for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kSplitThreads) {
+            float* o = w.y + (int64_t)c * w.ys;
+            *o = f_div(*o, denom);
+        }
+    }
+    cluster.sync();  // peers' shared memory stays alive until every CTA has read it
+}
+
+uint64_t split_chunk(uint64_t ne0) {
+    uint64_t c = (ne0 + kSplitCluster - 1) / kSplitCluster;
+    return (c + 3) / 4 * 4;  // keeps every chunk's first column 16-byte aligned
+}
+
+}  // namespace
+
+bool split_rows_wanted(const LaunchEnv& env, const RowPlan& p) {
+    // few rows, each long enough to give eight CTAs real work
+    return p.ne[0] >= 16384 && p.rows <= (uint64_t)env.sm_count && p.rows * kSplitCluster <= 0x7fffffffull &&
+           !p.dst_ordinal;
+}
+
+cudaError_t launch_argmax_rows_split(const LaunchEnv& env, const RowPlan& p, int dst_dtype) {
+    argmax_rows_split<<<(unsigned)(p.rows * kSplitCluster), kSplitThreads, 0, env.stream>>>(p, dst_dtype,
+                                                                                            split_chunk(p.ne[0]));
+    ++*env.launches;
+    return cudaGetLastError();
+}
+
+cudaError_t launch_sum_rows_split(const LaunchEnv& env, const RowPlan& p) {
+    sum_rows_split<<<(unsigned)(p.rows * kSplitCluster), kSplitThreads, 0, env.stream>>>(p, split_chunk(p.ne[0]));
+    ++*env.launches;
+    return cudaGetLastError();
+}
+
+cudaError_t launch_soft_max_split(const LaunchEnv& env, const RowPlan& p, bool apply_scale, float scale) {
+    softmax_rows_split<<<(unsigned)(p.rows * kSplitCluster), kSplitThreads, 0, env.stream>>>(p, apply_scale, scale,
+                                                                                             split_chunk(p.ne[0]));
+    ++*env.launches;
+    return cudaGetLastError();
+}
+
+}  // namespace emel

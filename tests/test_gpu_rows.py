@@ -354,3 +354,51 @@ def test_ring_softmax_special_rows_take_the_exact_pass(emel, kern, oracle_lib):
         assert np.array_equal(np.isnan(got), nan), f"ring {kind}: NaN positions"
         gh.assert_bits_equal(got[nan], want[nan], f"ring {kind} special rows: NaN payloads")
         close(got[~nan], want[~nan], 1e-30, f"ring {kind} special rows")
+
+
+# ---- few long rows: one cluster of CTAs per row --------------------------------
+def test_split_argmax_rows_ties_across_chunks_and_nans(emel, kern, oracle_lib):
+    """Rows of 151936 split over eight CTAs: equal maxima in two chunks pick
+    the earlier column; a NaN at column 0 pins 0; NaNs elsewhere are skipped;
+    an all-NaN row gives 0."""
+    rng = np.random.default_rng(46)
+    v, rows = 151936, 6
+    x = rng.standard_normal(v * rows).astype(np.float32).reshape(rows, v)
+    x[0, 150000] = 50.0
+    x[0, 19000] = 50.0       # same maximum, earlier chunk
+    x[1, 0] = np.nan
+    x[1, 77] = 99.0
+    x[2, ::3] = np.nan
+    x[3, :] = np.nan
+    x[4, 151935] = 1e30      # last column
+    x[5, :] = -np.inf
+    for dt in (np.int64, np.int32, np.float32):
+        got, want = run_row_op(emel, kern, oracle_lib, "argmax_rows", x.ravel(), [v, rows, 1, 1], out_dtype=dt)
+        assert np.array_equal(got, want), (np.dtype(dt).name, got, want)
+    assert got.astype(np.int64).tolist()[:2] == [19000, 0]
+
+
+@pytest.mark.parametrize("width", [40001, 151936])
+def test_split_sum_rows(emel, kern, oracle_lib, width):
+    rng = np.random.default_rng(width)
+    x = (rng.standard_normal(width * 5) * 10).astype(np.float32)
+    got, want = run_row_op(emel, kern, oracle_lib, "sum_rows", x, [width, 5, 1, 1])
+    close(got, want, 1e-3, f"split sum_rows width={width}")
+
+
+def test_split_softmax_special_rows_and_mask(emel, kern, oracle_lib):
+    rng = np.random.default_rng(47)
+    v, rows = 40000, 6
+    x = (rng.standard_normal(v * rows) * 3).astype(np.float32).reshape(rows, v)
+    x[1, 0] = np.uint32(0x7fa00001).view(np.float32)
+    x[2, 30000] = np.nan
+    x[3, 123] = np.inf
+    x[4, :] = -np.inf
+    mask = np.where(rng.random((rows, v)) < 0.1, -np.inf, 0.0).astype(np.float16)
+    mask[5, 5] = np.float16(np.nan)
+    for kind, m, scale in (("soft_max", None, 1.0), ("soft_max_ext", (mask.ravel(), [v, rows, 1, 1], None), 0.7)):
+        got, want = run_row_op(emel, kern, oracle_lib, kind, x.ravel(), [v, rows, 1, 1], mask=m, scale=scale)
+        nan = np.isnan(want)
+        assert np.array_equal(np.isnan(got), nan), f"split {kind}: NaN positions"
+        gh.assert_bits_equal(got[nan], want[nan], f"split {kind}: NaN payloads")
+        close(got[~nan], want[~nan], 1e-30, f"split {kind}")
