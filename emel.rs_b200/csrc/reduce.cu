@@ -80,37 +80,85 @@ __device__ __forceinline__ const float* row_ptr(const RowPlan& p, uint64_t r) {
 }
 
 // Flat = the view is one dense run of p.rows * ne0 floats.
-template <bool FLAT>
+// Source walks.  MODE 1: the view is one dense, 16-byte aligned run.
+// MODE 2: rows of ne0 % 4 == 0 floats with unit dim-0 stride and 16-byte
+// aligned starts (e.g. a permuted view whose rows stay contiguous); vector
+// v of the logical order is found with 32-bit magic-number divisions.
+// MODE 0: anything else, one element at a time (warps walk rows).
+struct VecWalk {
+    const float* base;
+    FastDiv dv, d1, d2;
+    uint32_t vpr, ne1, ne2;
+    int64_t s1, s2, s3;
+    uint64_t nvec;
+};
+
+template <int MODE>
+__device__ __forceinline__ VecWalk vec_walk(const RowPlan& p) {
+    VecWalk w{};
+    w.base = reinterpret_cast<const float*>(p.src.ptr);
+    w.nvec = p.rows * p.ne[0] / 4;
+    if constexpr (MODE == 2) {
+        w.vpr = (uint32_t)(p.ne[0] / 4);
+        w.ne1 = (uint32_t)p.ne[1];
+        w.ne2 = (uint32_t)p.ne[2];
+        w.dv = make_fastdiv(w.vpr);
+        w.d1 = make_fastdiv(w.ne1);
+        w.d2 = make_fastdiv(w.ne2);
+        w.s1 = p.src.st[1];
+        w.s2 = p.src.st[2];
+        w.s3 = p.src.st[3];
+    }
+    return w;
+}
+
+// Vector v of the logical order (elements 4v .. 4v+3).
+template <int MODE>
+__device__ __forceinline__ float4 vec_load(const VecWalk& w, uint64_t v) {
+    if constexpr (MODE == 1) {
+        return __ldcs(reinterpret_cast<const float4*>(w.base) + v);
+    } else {
+        const uint32_t row = fdiv((uint32_t)v, w.dv);
+        const uint32_t c4 = (uint32_t)v - row * w.vpr;
+        const uint32_t q = fdiv(row, w.d1), i1 = row - q * w.ne1;
+        const uint32_t i3 = fdiv(q, w.d2), i2 = q - i3 * w.ne2;
+        const float* r = w.base + (int64_t)i1 * w.s1 + (int64_t)i2 * w.s2 + (int64_t)i3 * w.s3;
+        return __ldcs(reinterpret_cast<const float4*>(r) + c4);
+    }
+}
+
+template <int MODE>
 __device__ __forceinline__ double partial_sum(const RowPlan& p) {
     double acc = 0.0;
     const uint64_t gthreads = (uint64_t)gridDim.x * blockDim.x;
     const uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if constexpr (FLAT) {
-        const float* x = reinterpret_cast<const float*>(p.src.ptr);
-        const uint64_t n = p.rows * p.ne[0];
-        const uint64_t nvec = n / 4;
+    if constexpr (MODE != 0) {
+        const VecWalk w = vec_walk<MODE>(p);
         uint64_t i = gid;
-        for (; i + gthreads < nvec; i += 2 * gthreads) {
-            const float4 a = __ldcs(reinterpret_cast<const float4*>(x) + i);
-            const float4 b = __ldcs(reinterpret_cast<const float4*>(x) + i + gthreads);
+        for (; i + 3 * gthreads < w.nvec; i += 4 * gthreads) {
+            float4 q[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) q[k] = vec_load<MODE>(w, i + k * gthreads);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                acc += (double)q[k].x;
+                acc += (double)q[k].y;
+                acc += (double)q[k].z;
+                acc += (double)q[k].w;
+            }
+        }
+        for (; i < w.nvec; i += gthreads) {
+            const float4 a = vec_load<MODE>(w, i);
             acc += (double)a.x;
             acc += (double)a.y;
             acc += (double)a.z;
             acc += (double)a.w;
-            acc += (double)b.x;
-            acc += (double)b.y;
-            acc += (double)b.z;
-            acc += (double)b.w;
         }
-        if (i < nvec) {
-            const float4 a = __ldcs(reinterpret_cast<const float4*>(x) + i);
-            acc += (double)a.x;
-            acc += (double)a.y;
-            acc += (double)a.z;
-            acc += (double)a.w;
+        if constexpr (MODE == 1) {
+            const uint64_t n = p.rows * p.ne[0];
+            const uint64_t t = w.nvec * 4 + gid;
+            if (t < n) acc += (double)w.base[t];
         }
-        const uint64_t t = nvec * 4 + gid;
-        if (t < n) acc += (double)x[t];
     } else {
         // warps walk rows; lanes walk columns
         const uint64_t warp = gid / 32, nwarps = gthreads / 32;
@@ -123,24 +171,40 @@ __device__ __forceinline__ double partial_sum(const RowPlan& p) {
     return acc;
 }
 
-template <bool FLAT>
+template <int MODE>
 __device__ __forceinline__ ArgPart partial_arg(const RowPlan& p) {
     ArgPart b{0.0f, 0, 0};
     const uint64_t gthreads = (uint64_t)gridDim.x * blockDim.x;
     const uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    if constexpr (FLAT) {
-        const float* x = reinterpret_cast<const float*>(p.src.ptr);
-        const uint64_t n = p.rows * p.ne[0];
-        const uint64_t nvec = n / 4;
-        for (uint64_t i = gid; i < nvec; i += gthreads) {
-            const float4 a = __ldcs(reinterpret_cast<const float4*>(x) + i);
+    if constexpr (MODE != 0) {
+        // vector v holds logical elements 4v .. 4v+3 in both walks
+        const VecWalk w = vec_walk<MODE>(p);
+        uint64_t i = gid;
+        for (; i + 3 * gthreads < w.nvec; i += 4 * gthreads) {
+            float4 q[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) q[k] = vec_load<MODE>(w, i + k * gthreads);
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const int64_t e = (int64_t)(4 * (i + k * gthreads));
+                arg_take(b, q[k].x, e);
+                arg_take(b, q[k].y, e + 1);
+                arg_take(b, q[k].z, e + 2);
+                arg_take(b, q[k].w, e + 3);
+            }
+        }
+        for (; i < w.nvec; i += gthreads) {
+            const float4 a = vec_load<MODE>(w, i);
             arg_take(b, a.x, (int64_t)(4 * i));
             arg_take(b, a.y, (int64_t)(4 * i + 1));
             arg_take(b, a.z, (int64_t)(4 * i + 2));
             arg_take(b, a.w, (int64_t)(4 * i + 3));
         }
-        const uint64_t t = nvec * 4 + gid;
-        if (t < n) arg_take(b, x[t], (int64_t)t);
+        if constexpr (MODE == 1) {
+            const uint64_t n = p.rows * p.ne[0];
+            const uint64_t t = w.nvec * 4 + gid;
+            if (t < n) arg_take(b, w.base[t], (int64_t)t);
+        }
     } else {
         const uint64_t warp = gid / 32, nwarps = gthreads / 32;
         const uint32_t lane = threadIdx.x & 31;
@@ -164,10 +228,10 @@ __device__ __forceinline__ bool last_cta(unsigned* ticket) {
     return is_last;
 }
 
-template <bool FLAT>
+template <int MODE>
 __global__ void __launch_bounds__(kThreads) sum_all(RowPlan p, double* partials, unsigned* ticket, int mode, void* out) {
     __shared__ double sh[kThreads / 32];
-    double acc = block_sum(partial_sum<FLAT>(p), sh);
+    double acc = block_sum(partial_sum<MODE>(p), sh);
     if (threadIdx.x == 0) partials[blockIdx.x] = acc;
     if (!last_cta(ticket)) return;
     // fixed-order fold: thread t adds partials t, t+256, ... then a fixed tree
@@ -183,11 +247,11 @@ __global__ void __launch_bounds__(kThreads) sum_all(RowPlan p, double* partials,
     }
 }
 
-template <bool FLAT>
+template <int MODE>
 __global__ void __launch_bounds__(kThreads) argmax_all(RowPlan p, ArgPart* partials, unsigned* ticket, int out_kind,
                                                        int dst_dtype, int64_t index_base, void* out) {
     __shared__ ArgPart sh[kThreads / 32];
-    ArgPart b = block_arg(partial_arg<FLAT>(p), sh);
+    ArgPart b = block_arg(partial_arg<MODE>(p), sh);
     if (threadIdx.x == 0) partials[blockIdx.x] = b;
     if (!last_cta(ticket)) return;
     ArgPart t{0.0f, 0, 0};
@@ -241,14 +305,24 @@ static uint32_t reduce_grid(const LaunchEnv& env, uint64_t n) {
     return (uint32_t)(g == 0 ? 1 : g);
 }
 
-static bool flat(const RowPlan& p) { return p.flat; }
+// 1: one dense run; 2: contiguous 16-byte aligned rows whose vector count
+// fits 32-bit addressing; 0: element by element.
+static int walk_mode(const RowPlan& p) {
+    if (p.flat) return 1;
+    const uint64_t nvec = p.rows * p.ne[0] / 4;
+    if (p.vec && nvec < (1ull << 32) && p.ne[1] < (1ull << 32) && p.ne[2] < (1ull << 32)) return 2;
+    return 0;
+}
 
 cudaError_t launch_sum(const LaunchEnv& env, const RowPlan& p, int mode, void* out) {
     unsigned* ticket = reinterpret_cast<unsigned*>(env.workspace);
     double* partials = reinterpret_cast<double*>(reinterpret_cast<char*>(env.workspace) + 256);
     const uint32_t grid = reduce_grid(env, p.rows * p.ne[0]);
-    if (flat(p)) sum_all<true><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, mode, out);
-    else sum_all<false><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, mode, out);
+    switch (walk_mode(p)) {
+    case 1: sum_all<1><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, mode, out); break;
+    case 2: sum_all<2><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, mode, out); break;
+    default: sum_all<0><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, mode, out); break;
+    }
     ++*env.launches;
     return cudaGetLastError();
 }
@@ -258,8 +332,11 @@ cudaError_t launch_argmax(const LaunchEnv& env, const RowPlan& p, int out_kind, 
     unsigned* ticket = reinterpret_cast<unsigned*>(env.workspace);
     ArgPart* partials = reinterpret_cast<ArgPart*>(reinterpret_cast<char*>(env.workspace) + 256);
     const uint32_t grid = reduce_grid(env, p.rows * p.ne[0]);
-    if (flat(p)) argmax_all<true><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, out_kind, dst_dtype, index_base, out);
-    else argmax_all<false><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, out_kind, dst_dtype, index_base, out);
+    switch (walk_mode(p)) {
+    case 1: argmax_all<1><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, out_kind, dst_dtype, index_base, out); break;
+    case 2: argmax_all<2><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, out_kind, dst_dtype, index_base, out); break;
+    default: argmax_all<0><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, out_kind, dst_dtype, index_base, out); break;
+    }
     ++*env.launches;
     return cudaGetLastError();
 }
@@ -336,7 +413,10 @@ extern "C" emel_cuda_status emel_cuda_sum_noalloc(void* stream, const emel_tenso
     double* partials = reinterpret_cast<double*>(static_cast<char*>(scratch) + kNoAllocHeader);
     // the array keeps the previous call's contents: the ticket must start at 0
     if (cudaMemsetAsync(ticket, 0, sizeof(unsigned), env.stream) != cudaSuccess) return EMEL_CUDA_DEVICE_ERROR;
-    if (p.flat) sum_all<true><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, 0, dst->data);
-    else sum_all<false><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, 0, dst->data);
+    switch (walk_mode(p)) {
+    case 1: sum_all<1><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, 0, dst->data); break;
+    case 2: sum_all<2><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, 0, dst->data); break;
+    default: sum_all<0><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, 0, dst->data); break;
+    }
     return cudaGetLastError() == cudaSuccess ? EMEL_CUDA_OK : EMEL_CUDA_DEVICE_ERROR;
 }

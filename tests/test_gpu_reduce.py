@@ -120,6 +120,36 @@ def test_argmax_strided(emel, kern):
     assert int(got) == want
 
 
+@pytest.mark.parametrize("ne0", [4, 8, 128])
+def test_contiguous_rows_walk_ties_and_nans(emel, kern, oracle_lib, ne0):
+    """Padded and permuted views whose rows stay contiguous and 16-byte
+    aligned take the vectorised row walk: sums match, argmax ties keep the
+    earliest logical index across rows, NaN at logical element 0 pins 0."""
+    rng = np.random.default_rng(ne0)
+    ne = [ne0, 37, 5, 3]
+    row = ne0 + 8  # padded rows
+    nb = [4, 4 * row, 4 * row * 37, 4 * row * 37 * 5]
+    span = sum((ne[d] - 1) * nb[d] for d in range(4)) // 4 + 1
+    x = rng.standard_normal(span).astype(np.float32)
+
+    def at(i0, i1, i2, i3):
+        return (i0 * nb[0] + i1 * nb[1] + i2 * nb[2] + i3 * nb[3]) // 4
+
+    got, want, px, po, wv = device_sum(emel, kern, x, ne, nb)
+    assert oracle_lib.oracle_sum(ctypes.byref(px.oview()), ctypes.byref(wv)) == 0
+    assert abs(float(got) - float(want[0])) <= 1e-5 * max(abs(float(want[0])), 1.0), (got, want)
+    px.free()
+    po.free()
+    x[at(ne0 - 1, 30, 4, 2)] = 50.0
+    x[at(0, 2, 1, 1)] = 50.0  # same value, earlier logical index
+    x[at(1 % ne0, 3, 0, 0)] = np.nan
+    got, want = device_argmax(emel, kern, x, ne, nb)
+    assert int(got) == want == ((1 * 5 + 1) * 37 + 2) * ne0
+    x[at(0, 0, 0, 0)] = np.nan
+    got, want = device_argmax(emel, kern, x, ne, nb)
+    assert int(got) == want == 0
+
+
 def test_cfg5_whole_tensor_sum_and_argmax_full_size(emel, kern, oracle_lib):
     """2^28 elements viewed through the dims-1/2-swapped layout."""
     from emel_rs_b200 import workloads
