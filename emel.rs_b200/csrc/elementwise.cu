@@ -189,6 +189,78 @@ __global__ void __launch_bounds__(kThreads) ew_rows(EwPlan p, F f, int gshift) {
     }
 }
 
+// Vector walk over rows whose every operand has unit dim-0 stride and
+// 16-byte aligned starts (row broadcast, the repeat broadcast, permuted or
+// padded views): grid-stride over the 16-byte vectors of the logical order,
+// U independent vectors per thread per iteration; each vector's row and the
+// broadcast operand's wrapped row come from 32-bit magic-number divisions.
+struct RowsWalk {
+    FastDiv dv, d1, d2;  // vectors per row, ne1, ne2
+    FastDiv m1, m2, m3;  // src1 extents (broadcast wrap)
+    uint32_t vpr, ne1, ne2;
+    uint32_t nvec;
+};
+
+template <typename T, typename F>
+__global__ void __launch_bounds__(kThreads) ew_rows_vec(EwPlan p, F f, RowsWalk w) {
+    constexpr int N = Vec16<T>::N;
+    constexpr int U = 4;
+    const uint32_t stride = gridDim.x * blockDim.x;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < w.nvec; i += U * stride) {
+        Vec16<T> a[U], b[U];
+        T* d[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const uint32_t v = i + k * stride;
+            d[k] = nullptr;
+            if (v >= w.nvec) continue;
+            const uint32_t row = fdiv(v, w.dv), c = (v - row * w.vpr) * N;
+            const uint32_t q = fdiv(row, w.d1), i1 = row - q * w.ne1;
+            const uint32_t i3 = fdiv(q, w.d2), i2 = q - i3 * w.ne2;
+            d[k] = at<T>(p.dst, (int64_t)i1 * p.dst.st[1] + (int64_t)i2 * p.dst.st[2] + (int64_t)i3 * p.dst.st[3]) + c;
+            a[k] = ld_stream(at<T>(p.src0, (int64_t)i1 * p.src0.st[1] + (int64_t)i2 * p.src0.st[2] +
+                                               (int64_t)i3 * p.src0.st[3]) + c);
+            if constexpr (F::kBinary) {
+                uint32_t j1 = i1, j2 = i2, j3 = i3;
+                if (p.src1_bcast) {
+                    j1 = i1 - fdiv(i1, w.m1) * w.m1.d;
+                    j2 = i2 - fdiv(i2, w.m2) * w.m2.d;
+                    j3 = i3 - fdiv(i3, w.m3) * w.m3.d;
+                }
+                b[k] = ld_keep(at<T>(p.src1, (int64_t)j1 * p.src1.st[1] + (int64_t)j2 * p.src1.st[2] +
+                                                 (int64_t)j3 * p.src1.st[3]) + c);
+            } else {
+                b[k] = Vec16<T>{};
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k)
+            if (d[k] != nullptr) st_stream(d[k], apply_vec<T>(f, a[k], b[k]));
+    }
+}
+
+bool rows_walk(const EwPlan& p, RowsWalk* w) {
+    const uint64_t N = p.dtype == DType::F16 ? 8 : 4;
+    const uint64_t nvec = p.count / N;
+    if (!p.vec || p.ne[0] % N != 0 || nvec >= (1ull << 31) || p.ne[1] >= (1ull << 31) || p.ne[2] >= (1ull << 31))
+        return false;
+    if (p.src1_bcast && p.src1.ne[0] != p.ne[0]) return false;
+    w->vpr = (uint32_t)(p.ne[0] / N);
+    w->ne1 = (uint32_t)p.ne[1];
+    w->ne2 = (uint32_t)p.ne[2];
+    w->nvec = (uint32_t)nvec;
+    w->dv = make_fastdiv(w->vpr);
+    w->d1 = make_fastdiv(w->ne1);
+    w->d2 = make_fastdiv(w->ne2);
+    const uint64_t b1 = p.src1.ne[1] ? p.src1.ne[1] : 1, b2 = p.src1.ne[2] ? p.src1.ne[2] : 1,
+                   b3 = p.src1.ne[3] ? p.src1.ne[3] : 1;
+    if (b1 >= (1ull << 31) || b2 >= (1ull << 31) || b3 >= (1ull << 31)) return false;
+    w->m1 = make_fastdiv((uint32_t)b1);
+    w->m2 = make_fastdiv((uint32_t)b2);
+    w->m3 = make_fastdiv((uint32_t)b3);
+    return true;
+}
+
 template <typename T, typename F>
 __global__ void __launch_bounds__(kThreads) ew_generic(EwPlan p, F f, FastDiv d0, FastDiv d1, FastDiv d2) {
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
@@ -263,6 +335,11 @@ cudaError_t launch_ew(const LaunchEnv& env, const EwPlan& p, const F& f) {
         break;
     }
     case EwKind::Rows: {
+        RowsWalk w;
+        if (rows_walk(p, &w)) {
+            ew_rows_vec<T, F><<<grid_for(env, w.nvec, 4), kThreads, 0, env.stream>>>(p, f, w);
+            break;
+        }
         const uint64_t per_row = p.vec ? p.ne[0] / Vec16<T>::N : p.ne[0];
         int gshift = 5;
         while (gshift < 8 && (1ull << gshift) < per_row) ++gshift;
