@@ -18,6 +18,7 @@
 // Grids are sized in multiples of the SM count (148 on B200).
 #include "common.cuh"
 #include "launch.hpp"
+#include "pdl.cuh"
 #include "tma.cuh"
 
 namespace emel {
@@ -30,18 +31,21 @@ template <int OP, bool IN_F16>
 struct UnaryFn {
     UnaryParams p;
     static constexpr bool kBinary = false;
+    static constexpr int kUnroll = kHeavyFormula<OP> ? 2 : 4;  // arithmetic-bound ops need fewer loads in flight
     __device__ __forceinline__ float operator()(float a, float) const { return unary_apply<OP, IN_F16>(a, p); }
 };
 
 template <int OP>
 struct BinaryFn {
     static constexpr bool kBinary = true;
+    static constexpr int kUnroll = 4;
     __device__ __forceinline__ float operator()(float a, float b) const { return binary_apply<OP>(a, b); }
 };
 
 // activation.rs:467-481, silu_back as a two-input formula: grad * silu'(x).
 struct SiluBackFn {
     static constexpr bool kBinary = true;
+    static constexpr int kUnroll = 2;
     __device__ __forceinline__ float operator()(float x, float grad) const {
         const float sigmoid = f_div(1.0f, f_add(1.0f, lm_exp(f_neg(x))));
         const float derivative = f_mul(sigmoid, f_add(1.0f, f_mul(x, f_sub(1.0f, sigmoid))));
@@ -113,23 +117,25 @@ __device__ __forceinline__ Vec16<T> apply_vec(const F& f, const Vec16<T>& a, con
 template <typename T, typename F>
 __global__ void __launch_bounds__(kThreads) ew_flat(T* __restrict__ dst, const T* __restrict__ a,
                                                     const T* __restrict__ b, uint64_t n, F f) {
+    pdl_enter();
     constexpr int N = Vec16<T>::N;
+    constexpr int U = F::kUnroll;  // vectors in flight per thread
     const uint64_t nvec = n / N;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     const uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     uint64_t i = gid;
-    for (; i + stride < nvec; i += 2 * stride) {
-        const Vec16<T> a0 = ld_stream(a + i * N);
-        const Vec16<T> a1 = ld_stream(a + (i + stride) * N);
-        Vec16<T> b0{}, b1{};
-        if constexpr (F::kBinary) {
-            b0 = ld_stream(b + i * N);
-            b1 = ld_stream(b + (i + stride) * N);
+    for (; i + (U - 1) * stride < nvec; i += U * stride) {
+        Vec16<T> a0[U], b0[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            a0[k] = ld_stream(a + (i + k * stride) * N);
+            if constexpr (F::kBinary) b0[k] = ld_stream(b + (i + k * stride) * N);
+            else b0[k] = Vec16<T>{};
         }
-        st_stream(dst + i * N, apply_vec<T>(f, a0, b0));
-        st_stream(dst + (i + stride) * N, apply_vec<T>(f, a1, b1));
+#pragma unroll
+        for (int k = 0; k < U; ++k) st_stream(dst + (i + k * stride) * N, apply_vec<T>(f, a0[k], b0[k]));
     }
-    if (i < nvec) {
+    for (; i < nvec; i += stride) {
         const Vec16<T> a0 = ld_stream(a + i * N);
         Vec16<T> b0{};
         if constexpr (F::kBinary) b0 = ld_stream(b + i * N);
@@ -151,6 +157,7 @@ __device__ __forceinline__ T* at(const Operand& o, int64_t elems) {
 // Row workers: G = 1 << gshift threads per row.
 template <typename T, typename F>
 __global__ void __launch_bounds__(kThreads) ew_rows(EwPlan p, F f, int gshift) {
+    pdl_enter();
     constexpr int N = Vec16<T>::N;
     const uint32_t G = 1u << gshift;
     const uint32_t lane = threadIdx.x & (G - 1);
@@ -203,6 +210,7 @@ struct RowsWalk {
 
 template <typename T, typename F>
 __global__ void __launch_bounds__(kThreads) ew_rows_vec(EwPlan p, F f, RowsWalk w) {
+    pdl_enter();
     constexpr int N = Vec16<T>::N;
     constexpr int U = 4;
     const uint32_t stride = gridDim.x * blockDim.x;
@@ -263,6 +271,7 @@ bool rows_walk(const EwPlan& p, RowsWalk* w) {
 
 template <typename T, typename F>
 __global__ void __launch_bounds__(kThreads) ew_generic(EwPlan p, F f, FastDiv d0, FastDiv d1, FastDiv d2) {
+    pdl_enter();
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < p.count; i += stride) {
         const uint32_t o = (uint32_t)i;
@@ -307,6 +316,7 @@ __device__ __forceinline__ int64_t repeat_elems(const EwPlan& p, uint64_t ordina
 
 template <typename T, typename F>
 __global__ void __launch_bounds__(kThreads) ew_ordinal(EwPlan p, F f) {
+    pdl_enter();
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < p.count; i += stride) {
         const float x = Elem<T>::load(at<T>(p.src0, ordinal_elems(p.src0, i)));
@@ -329,15 +339,19 @@ cudaError_t launch_ew(const LaunchEnv& env, const EwPlan& p, const F& f) {
     switch (p.kind) {
     case EwKind::Flat: {
         const uint64_t nvec = p.count / Vec16<T>::N;
-        ew_flat<T, F><<<grid_for(env, nvec, 2), kThreads, 0, env.stream>>>(
+        const cudaError_t err = launch_dependent(
+            ew_flat<T, F>, dim3(grid_for(env, nvec, F::kUnroll)), dim3(kThreads), 0, env.stream,
             reinterpret_cast<T*>(p.dst.ptr), reinterpret_cast<const T*>(p.src0.ptr),
             reinterpret_cast<const T*>(p.src1.ptr), p.count, f);
+        if (err != cudaSuccess) return err;
         break;
     }
     case EwKind::Rows: {
         RowsWalk w;
         if (rows_walk(p, &w)) {
-            ew_rows_vec<T, F><<<grid_for(env, w.nvec, 4), kThreads, 0, env.stream>>>(p, f, w);
+            const cudaError_t err =
+                launch_dependent(ew_rows_vec<T, F>, dim3(grid_for(env, w.nvec, 4)), dim3(kThreads), 0, env.stream, p, f, w);
+            if (err != cudaSuccess) return err;
             break;
         }
         const uint64_t per_row = p.vec ? p.ne[0] / Vec16<T>::N : p.ne[0];
@@ -345,16 +359,24 @@ cudaError_t launch_ew(const LaunchEnv& env, const EwPlan& p, const F& f) {
         while (gshift < 8 && (1ull << gshift) < per_row) ++gshift;
         const uint64_t rows = p.count / p.ne[0];
         const uint64_t threads = rows << gshift;
-        ew_rows<T, F><<<grid_for(env, threads, 1), kThreads, 0, env.stream>>>(p, f, gshift);
+        const cudaError_t err =
+            launch_dependent(ew_rows<T, F>, dim3(grid_for(env, threads, 1)), dim3(kThreads), 0, env.stream, p, f, gshift);
+        if (err != cudaSuccess) return err;
         break;
     }
     case EwKind::Generic: {
-        ew_generic<T, F><<<grid_for(env, p.count, 1), kThreads, 0, env.stream>>>(
-            p, f, make_fastdiv((uint32_t)p.ne[0]), make_fastdiv((uint32_t)p.ne[1]), make_fastdiv((uint32_t)p.ne[2]));
+        const cudaError_t err = launch_dependent(ew_generic<T, F>, dim3(grid_for(env, p.count, 1)), dim3(kThreads), 0,
+                                                 env.stream, p, f, make_fastdiv((uint32_t)p.ne[0]),
+                                                 make_fastdiv((uint32_t)p.ne[1]), make_fastdiv((uint32_t)p.ne[2]));
+        if (err != cudaSuccess) return err;
         break;
     }
-    case EwKind::Ordinal:
-        ew_ordinal<T, F><<<grid_for(env, p.count, 1), kThreads, 0, env.stream>>>(p, f);
+    case EwKind::Ordinal: {
+        const cudaError_t err =
+            launch_dependent(ew_ordinal<T, F>, dim3(grid_for(env, p.count, 1)), dim3(kThreads), 0, env.stream, p, f);
+        if (err != cudaSuccess) return err;
+        break;
+    }
         break;
     }
     ++*env.launches;
@@ -479,6 +501,7 @@ __global__ void __launch_bounds__(kTableThreads, 1) table_stream(typename K::Ele
         mbar_init_fence();
     }
     wait_for_prerequisite_grid();  // the table is complete and visible
+    allow_dependent_launch();
     __syncthreads();
     if (threadIdx.x == 0) {
         mbar_expect_tx(&bar, kTableBytes);

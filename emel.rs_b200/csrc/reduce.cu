@@ -9,6 +9,7 @@
 // the ticket.  With the grid fixed per device, the result is deterministic.
 #include "common.cuh"
 #include "launch.hpp"
+#include "pdl.cuh"
 
 namespace emel {
 
@@ -230,6 +231,7 @@ __device__ __forceinline__ bool last_cta(unsigned* ticket) {
 
 template <int MODE>
 __global__ void __launch_bounds__(kThreads) sum_all(RowPlan p, double* partials, unsigned* ticket, int mode, void* out) {
+    pdl_enter();
     __shared__ double sh[kThreads / 32];
     double acc = block_sum(partial_sum<MODE>(p), sh);
     if (threadIdx.x == 0) partials[blockIdx.x] = acc;
@@ -250,6 +252,7 @@ __global__ void __launch_bounds__(kThreads) sum_all(RowPlan p, double* partials,
 template <int MODE>
 __global__ void __launch_bounds__(kThreads) argmax_all(RowPlan p, ArgPart* partials, unsigned* ticket, int out_kind,
                                                        int dst_dtype, int64_t index_base, void* out) {
+    pdl_enter();
     __shared__ ArgPart sh[kThreads / 32];
     ArgPart b = block_arg(partial_arg<MODE>(p), sh);
     if (threadIdx.x == 0) partials[blockIdx.x] = b;
@@ -318,13 +321,14 @@ cudaError_t launch_sum(const LaunchEnv& env, const RowPlan& p, int mode, void* o
     unsigned* ticket = reinterpret_cast<unsigned*>(env.workspace);
     double* partials = reinterpret_cast<double*>(reinterpret_cast<char*>(env.workspace) + 256);
     const uint32_t grid = reduce_grid(env, p.rows * p.ne[0]);
+    cudaError_t err;
     switch (walk_mode(p)) {
-    case 1: sum_all<1><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, mode, out); break;
-    case 2: sum_all<2><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, mode, out); break;
-    default: sum_all<0><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, mode, out); break;
+    case 1: err = launch_dependent(sum_all<1>, dim3(grid), dim3(kThreads), 0, env.stream, p, partials, ticket, mode, out); break;
+    case 2: err = launch_dependent(sum_all<2>, dim3(grid), dim3(kThreads), 0, env.stream, p, partials, ticket, mode, out); break;
+    default: err = launch_dependent(sum_all<0>, dim3(grid), dim3(kThreads), 0, env.stream, p, partials, ticket, mode, out); break;
     }
     ++*env.launches;
-    return cudaGetLastError();
+    return err != cudaSuccess ? err : cudaGetLastError();
 }
 
 cudaError_t launch_argmax(const LaunchEnv& env, const RowPlan& p, int out_kind, int dst_dtype, int64_t index_base,
@@ -332,13 +336,14 @@ cudaError_t launch_argmax(const LaunchEnv& env, const RowPlan& p, int out_kind, 
     unsigned* ticket = reinterpret_cast<unsigned*>(env.workspace);
     ArgPart* partials = reinterpret_cast<ArgPart*>(reinterpret_cast<char*>(env.workspace) + 256);
     const uint32_t grid = reduce_grid(env, p.rows * p.ne[0]);
+    cudaError_t err;
     switch (walk_mode(p)) {
-    case 1: argmax_all<1><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, out_kind, dst_dtype, index_base, out); break;
-    case 2: argmax_all<2><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, out_kind, dst_dtype, index_base, out); break;
-    default: argmax_all<0><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, out_kind, dst_dtype, index_base, out); break;
+    case 1: err = launch_dependent(argmax_all<1>, dim3(grid), dim3(kThreads), 0, env.stream, p, partials, ticket, out_kind, dst_dtype, index_base, out); break;
+    case 2: err = launch_dependent(argmax_all<2>, dim3(grid), dim3(kThreads), 0, env.stream, p, partials, ticket, out_kind, dst_dtype, index_base, out); break;
+    default: err = launch_dependent(argmax_all<0>, dim3(grid), dim3(kThreads), 0, env.stream, p, partials, ticket, out_kind, dst_dtype, index_base, out); break;
     }
     ++*env.launches;
-    return cudaGetLastError();
+    return err != cudaSuccess ? err : cudaGetLastError();
 }
 
 }  // namespace emel

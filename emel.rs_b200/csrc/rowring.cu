@@ -30,6 +30,7 @@
 #include "common.cuh"
 #include "launch.hpp"
 #include "rowreduce.cuh"
+#include "pdl.cuh"
 #include "tma.cuh"
 
 namespace emel {
@@ -180,6 +181,7 @@ __global__ void __launch_bounds__(T, 1024 / T) row_ring(RingArgs a) {
     extern __shared__ __align__(128) unsigned char ring_smem[];
     __shared__ __align__(8) uint64_t full[kRingStagesMax];
     __shared__ GroupScratch<T> red;
+    pdl_enter();
     const int tid = threadIdx.x;
     const int S = a.stages;
     const uint32_t mine = a.rows > blockIdx.x ? (a.rows - 1 - blockIdx.x) / gridDim.x + 1 : 0;
@@ -407,9 +409,9 @@ cudaError_t launch_ring_kernel(const LaunchEnv& env, RingArgs a, uint64_t rows, 
     const uint32_t smem = a.weight_bytes + (uint32_t)a.stages * a.stage_bytes;
     const uint64_t cap = (uint64_t)env.sm_count * ctas;
     const uint32_t grid = (uint32_t)(rows < cap ? rows : cap);
-    row_ring<OP, T><<<grid, T, smem, env.stream>>>(a);
+    err = launch_dependent(row_ring<OP, T>, dim3(grid), dim3(T), smem, env.stream, a);
     *launched = true;
-    return cudaGetLastError();
+    return err != cudaSuccess ? err : cudaGetLastError();
 }
 
 }  // namespace

@@ -17,6 +17,7 @@
 
 #include "common.cuh"
 #include "launch.hpp"
+#include "pdl.cuh"
 #include "rowreduce.cuh"
 
 namespace cg = cooperative_groups;
@@ -57,6 +58,7 @@ __device__ __forceinline__ void arg_take(ArgBest& b, float v, int64_t i) {
 
 __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitThreads)
     argmax_rows_split(RowPlan p, int dst_dtype, uint64_t chunk) {
+    pdl_enter();
     __shared__ GroupScratch<kSplitThreads> s;
     __shared__ float pv;
     __shared__ int64_t pi;
@@ -119,6 +121,7 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitTh
 
 __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitThreads)
     sum_rows_split(RowPlan p, uint64_t chunk) {
+    pdl_enter();
     __shared__ GroupScratch<kSplitThreads> s;
     __shared__ double part;
     cg::cluster_group cluster = cg::this_cluster();
@@ -191,6 +194,7 @@ __device__ __forceinline__ float div_by_split(float e, float d, float inv) {
 
 __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitThreads)
     softmax_rows_split(RowPlan p, bool apply_scale, float scale, uint64_t chunk) {
+    pdl_enter();
     __shared__ GroupScratch<kSplitThreads> s;
     __shared__ float part_max;
     __shared__ double part_sum;
@@ -320,23 +324,25 @@ bool split_rows_wanted(const LaunchEnv& env, const RowPlan& p) {
 }
 
 cudaError_t launch_argmax_rows_split(const LaunchEnv& env, const RowPlan& p, int dst_dtype) {
-    argmax_rows_split<<<(unsigned)(p.rows * kSplitCluster), kSplitThreads, 0, env.stream>>>(p, dst_dtype,
-                                                                                            split_chunk(p.ne[0]));
+    const cudaError_t err = launch_dependent(argmax_rows_split, dim3((unsigned)(p.rows * kSplitCluster)),
+                                             dim3(kSplitThreads), 0, env.stream, p, dst_dtype, split_chunk(p.ne[0]));
     ++*env.launches;
-    return cudaGetLastError();
+    return err != cudaSuccess ? err : cudaGetLastError();
 }
 
 cudaError_t launch_sum_rows_split(const LaunchEnv& env, const RowPlan& p) {
-    sum_rows_split<<<(unsigned)(p.rows * kSplitCluster), kSplitThreads, 0, env.stream>>>(p, split_chunk(p.ne[0]));
+    const cudaError_t err = launch_dependent(sum_rows_split, dim3((unsigned)(p.rows * kSplitCluster)),
+                                             dim3(kSplitThreads), 0, env.stream, p, split_chunk(p.ne[0]));
     ++*env.launches;
-    return cudaGetLastError();
+    return err != cudaSuccess ? err : cudaGetLastError();
 }
 
 cudaError_t launch_soft_max_split(const LaunchEnv& env, const RowPlan& p, bool apply_scale, float scale) {
-    softmax_rows_split<<<(unsigned)(p.rows * kSplitCluster), kSplitThreads, 0, env.stream>>>(p, apply_scale, scale,
-                                                                                             split_chunk(p.ne[0]));
+    const cudaError_t err = launch_dependent(softmax_rows_split, dim3((unsigned)(p.rows * kSplitCluster)),
+                                             dim3(kSplitThreads), 0, env.stream, p, apply_scale, scale,
+                                             split_chunk(p.ne[0]));
     ++*env.launches;
-    return cudaGetLastError();
+    return err != cudaSuccess ? err : cudaGetLastError();
 }
 
 }  // namespace emel
