@@ -32,6 +32,7 @@ struct UnaryFn {
     UnaryParams p;
     static constexpr bool kBinary = false;
     static constexpr int kUnroll = kHeavyFormula<OP> ? 2 : 4;  // arithmetic-bound ops need fewer loads in flight
+    static constexpr int kMinBlocks = kHeavyFormula<OP> ? 6 : 8;  // register cap keeping 6 or 8 CTAs per SM
     __device__ __forceinline__ float operator()(float a, float) const { return unary_apply<OP, IN_F16>(a, p); }
 };
 
@@ -39,6 +40,7 @@ template <int OP>
 struct BinaryFn {
     static constexpr bool kBinary = true;
     static constexpr int kUnroll = 4;
+    static constexpr int kMinBlocks = 8;
     __device__ __forceinline__ float operator()(float a, float b) const { return binary_apply<OP>(a, b); }
 };
 
@@ -46,6 +48,7 @@ struct BinaryFn {
 struct SiluBackFn {
     static constexpr bool kBinary = true;
     static constexpr int kUnroll = 2;
+    static constexpr int kMinBlocks = 6;
     __device__ __forceinline__ float operator()(float x, float grad) const {
         const float sigmoid = f_div(1.0f, f_add(1.0f, lm_exp(f_neg(x))));
         const float derivative = f_mul(sigmoid, f_add(1.0f, f_mul(x, f_sub(1.0f, sigmoid))));
@@ -115,7 +118,7 @@ __device__ __forceinline__ Vec16<T> apply_vec(const F& f, const Vec16<T>& a, con
 }
 
 template <typename T, typename F>
-__global__ void __launch_bounds__(kThreads) ew_flat(T* __restrict__ dst, const T* __restrict__ a,
+__global__ void __launch_bounds__(kThreads, F::kMinBlocks) ew_flat(T* __restrict__ dst, const T* __restrict__ a,
                                                     const T* __restrict__ b, uint64_t n, F f) {
     pdl_enter();
     constexpr int N = Vec16<T>::N;

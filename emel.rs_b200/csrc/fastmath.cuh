@@ -143,26 +143,30 @@ EMEL_HD double tanh_abs_core(double ay) {
 // binary32 entry points: correctly rounded except within ~2^-51 of a
 // rounding boundary.  Out-of-range arguments saturate the way the binary32
 // result does (exp: inf / +0, expm1: inf / -1, tanh: +-1); NaN propagates.
+// Branch-free: the argument is clamped into the core's range (comparisons
+// with NaN are false, so a NaN passes through), the core is evaluated, and
+// the saturated cases are selected afterwards.
 EMEL_HD float fast_expf(float x) {
-    if (x > 89.0f) return INFINITY;
-    if (x < -104.0f) return 0.0f;
-    return (float)exp_core((double)x);  // NaN flows through the core
+    const float xc = x > 89.0f ? 89.0f : (x < -104.0f ? -104.0f : x);
+    const float r = (float)exp_core((double)xc);
+    return x > 89.0f ? INFINITY : (x < -104.0f ? 0.0f : r);
 }
 
 EMEL_HD float fast_expm1f(float x) {
-    if (x > 89.0f) return INFINITY;
-    if (x < -18.0f) return -1.0f;
+    const float xc = x > 89.0f ? 89.0f : (x < -18.0f ? -18.0f : x);
+    const float r = (float)expm1_core((double)xc);
     if (x == 0.0f) return x;  // keeps the sign of zero
-    return (float)expm1_core((double)x);
+    return x > 89.0f ? INFINITY : (x < -18.0f ? -1.0f : r);
 }
 
 // tanh(y) rounds to +-1 in binary32 once |y| > 9.02.
 EMEL_HD float fast_tanhf(float y) {
     const float ay = std::fabs(y);
-    if (ay >= 10.0f) return y < 0.0f ? -1.0f : 1.0f;
-    if (y == 0.0f) return y;
-    const float t = (float)tanh_abs_core((double)ay);
-    return y < 0.0f ? -t : t;
+    const float ac = ay >= 10.0f ? 10.0f : ay;
+    const float t = (float)tanh_abs_core((double)ac);
+    const float s = y < 0.0f ? -1.0f : 1.0f;
+    const float r = ay >= 10.0f ? s : (y < 0.0f ? -t : t);
+    return y == 0.0f ? y : r;
 }
 
 }  // namespace emel

@@ -1,7 +1,8 @@
 """The device exponential core (fastmath.cuh) compiled for the host: its
 exp / expm1 / tanh equal binary64 libm rounded once to binary32 (the
-correctly-rounded-libm oracle's definition) on a strided sweep of every
-binary32 with |x| <= 90, allowing at most a handful of 1-ulp ties."""
+correctly-rounded-libm oracle's definition) on a strided sweep of all
+binary32 bit patterns (saturating arguments, infinities and NaNs included),
+allowing at most a handful of 1-ulp ties."""
 
 import subprocess
 from pathlib import Path
@@ -14,6 +15,11 @@ def test_fast_exponential_core_matches_binary64_libm(tmp_path):
     subprocess.run(["g++", "-O2", "-std=c++17", "-ffp-contract=off", "-I", str(ROOT / "emel.rs_b200" / "csrc"),
                     str(ROOT / "tests" / "cpp" / "fastmath_check.cpp"), "-o", str(exe), "-lm"], check=True)
     out = subprocess.run([str(exe), "1009"], capture_output=True, text=True, check=True).stdout.split()
+    # plus every binary32 in the windows around the saturation thresholds
+    edge = subprocess.run([str(exe), "edges"], capture_output=True, text=True, check=True).stdout.split()
+    n_e, e_exp, e_expm1, e_tanh, worst_e = map(int, edge)
+    assert n_e > 1_000_000
+    assert e_exp <= 2 and e_expm1 <= 2 and e_tanh <= 2 and worst_e <= 1, edge
     n, d_exp, d_expm1, d_tanh, worst = map(int, out)
     assert n > 1_000_000
     assert d_exp <= 2 and d_expm1 <= 2 and d_tanh <= 2, out
