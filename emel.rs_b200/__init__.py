@@ -17,6 +17,7 @@ raises.
 """
 
 import ctypes
+import struct
 import enum
 from dataclasses import dataclass
 from pathlib import Path
@@ -44,6 +45,8 @@ class Status(enum.IntEnum):
     INVALID_PARAMETERS = 3
     UNEXPECTED_EVENT = 4
     INTERNAL = 5
+    INVALID_SHAPE = 6
+    UNSUPPORTED_OPERATION = 7
     DEVICE_ERROR = 16
     TIMEOUT = 17
     INVALID_ARGUMENT = 18
@@ -98,6 +101,14 @@ class CArgmaxPartial(ctypes.Structure):
     """emel_cuda_argmax_partial."""
     _fields_ = [("value", ctypes.c_float), ("has_value", ctypes.c_uint32), ("index", ctypes.c_int64),
                 ("first_is_nan", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
+
+
+class CGenericRequest(ctypes.Structure):
+    """emel_cuda_generic_request: GenericRequest (generic.rs:634-645)."""
+    _fields_ = [("op", ctypes.c_uint32), ("unary_subop", ctypes.c_uint32),
+                ("src0", ctypes.POINTER(CView)), ("src1", ctypes.POINTER(CView)),
+                ("src2", ctypes.POINTER(CView)), ("dst", ctypes.POINTER(CView)),
+                ("params", ctypes.c_uint8 * 64), ("params_len", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
 
 
 # Every symbol include/emel_cuda.h declares, with its ctypes signature.
@@ -155,6 +166,7 @@ SIGNATURES = {
     "emel_cuda_argmax_combine": (_I, [ctypes.POINTER(CArgmaxPartial), _I, ctypes.POINTER(ctypes.c_int64),
                                       ctypes.POINTER(ctypes.c_float)]),
     "emel_cuda_argmax_rows": (_I, [_CTX, _V, _P, _P]),
+    "emel_cuda_generic": (_I, [_CTX, _V, ctypes.POINTER(CGenericRequest)]),
 }
 
 _lib = None
@@ -639,6 +651,76 @@ OpMean = _reduce("emel_cuda_mean", "reductions::OpMean (reductions.rs:120-133)."
 OpSumRows = _reduce("emel_cuda_sum_rows", "reductions::OpSumRows (reductions.rs:105-118).")
 OpArgmax = _reduce("emel_cuda_argmax", "reductions::OpArgmax (reductions.rs:135-148).")
 OpArgmaxRows = _reduce("emel_cuda_argmax_rows", "Per-row argmax (reductions.rs:715-730 per row).")
+
+
+class KernelOperation(enum.IntEnum):
+    """KernelOperation wire codes of the routes the device table executes
+    (generic.rs:220-316); every other code in 0..94 is accepted by the
+    envelope and answered with UNSUPPORTED_OPERATION."""
+    DUP = 0
+    ADD = 1
+    ADD1 = 3
+    SUB = 5
+    MUL = 6
+    DIV = 7
+    SQR = 8
+    SQRT = 9
+    LOG = 10
+    SIN = 11
+    COS = 12
+    SUM = 13
+    MEAN = 16
+    ARGMAX = 17
+    REPEAT = 19
+    SILU_BACK = 22
+    NORM = 23
+    RMS_NORM = 24
+    SCALE = 32
+    SOFT_MAX = 46
+    CLAMP = 50
+    LEAKY_RELU = 70
+    UNARY = 85
+
+
+def op_params(*values):
+    """OpParams from 4-byte slots: floats as f32, ints as i32 (native order)."""
+    raw = b"".join(struct.pack("=f", v) if isinstance(v, float) else struct.pack("=i", v) for v in values)
+    if len(raw) > 64:
+        raise ValueError("op_params holds 64 bytes")
+    return raw
+
+
+@dataclass
+class GenericEvent(Event):
+    """GenericEvent(GenericRequest) (generic.rs:634-797): an op-coded request
+    with up to three sources, a destination, the op_params bytes and, for
+    KernelOperation.UNARY, a UnarySubOp code."""
+    op: int
+    src0: Optional[TensorView] = None
+    src1: Optional[TensorView] = None
+    src2: Optional[TensorView] = None
+    dst: Optional[TensorView] = None
+    params: bytes = b""
+    unary: int = 0
+
+    def request(self) -> CGenericRequest:
+        r = CGenericRequest()
+        r.op = int(self.op)
+        r.unary_subop = int(self.unary)
+        self._keep = []
+        for name in ("src0", "src1", "src2", "dst"):
+            v = getattr(self, name)
+            if v is not None:
+                c = v.c()
+                self._keep.append(c)
+                setattr(r, name, ctypes.pointer(c))
+        ctypes.memmove(r.params, bytes(self.params), len(self.params))
+        r.params_len = len(self.params)
+        return r
+
+    def dispatch(self, ctx, stream):
+        r = self.request()
+        return ctx._lib.emel_cuda_generic(ctx.handle if ctx is not None else None, stream, ctypes.byref(r))
 
 
 class Kernel:

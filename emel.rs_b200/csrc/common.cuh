@@ -40,6 +40,16 @@ __device__ __forceinline__ float x86_nan2(float r, float a, float b) {
     return bitsf(kIndefiniteNaN);
 }
 
+// Result of a fused multiply-add (a * b + c): the first NaN operand in
+// source order, quietened, or the invalid-operation QNaN.
+__device__ __forceinline__ float x86_nan3(float r, float a, float b, float c) {
+    if (!is_nan(r)) return r;
+    if (is_nan(a)) return quiet(a);
+    if (is_nan(b)) return quiet(b);
+    if (is_nan(c)) return quiet(c);
+    return bitsf(kIndefiniteNaN);
+}
+
 // Result of a one-input libm/SSE operation: a NaN input comes back quietened,
 // a NaN produced from a number is the invalid-operation QNaN.
 __device__ __forceinline__ float x86_nan1(float r, float a) {
@@ -134,6 +144,9 @@ struct Arith {
     static __device__ __forceinline__ float round_f16(float v) {
         return EXACT ? f16_bits_to_f32(f32_to_f16_bits(v)) : __half2float(__float2half_rn(v));
     }
+    static __device__ __forceinline__ float fma(float a, float b, float c) {
+        return EXACT ? x86_nan3(__fmaf_rn(a, b, c), a, b, c) : __fmaf_rn(a, b, c);
+    }
     // Fast keeps "NaN in, NaN out" (any payload) so the exact recompute triggers.
     static __device__ __forceinline__ float clamp(float v, float lo, float hi) {
         return EXACT ? clamp_rs(v, lo, hi) : (v < lo ? lo : (v > hi ? hi : v));
@@ -169,6 +182,13 @@ __device__ __forceinline__ float unary_formula(float v, UnaryParams p) {
         const float q = (IN_F16 && !EXACT) ? v : A::round_f16(v);
         const float approx = gelu_tanh_core<EXACT>(q);
         return (IN_F16 && !EXACT) ? approx : A::round_f16(approx);
+    }
+    if constexpr (OP == kGeluGeneric) {
+        // generic.rs:1330-1337: no binary16 rounding (the "rounded" value is
+        // the input's own bits), no +-10 clamp, and the cubic term fused:
+        // 0.5 * v * (1 + tanh(0.7978846 * fma(0.044715 * v * v, v, v)))
+        const float cubic = A::fma(A::mul(A::mul(0.044715f, v), v), v, v);
+        return A::mul(A::mul(0.5f, v), A::add(1.0f, A::tanh(A::mul(0.7978846f, cubic))));
     }
     if constexpr (OP == kGeluQuick) {
         const float inner = A::mul(A::mul(0.7978846f, v), A::add(1.0f, A::mul(A::mul(0.044715f, v), v)));
@@ -211,6 +231,7 @@ __device__ __forceinline__ float unary_formula(float v, UnaryParams p) {
 
 template <int OP>
 constexpr bool kHeavyFormula = OP == kTanh || OP == kElu || OP == kSigmoid || OP == kGelu || OP == kGeluQuick ||
+                               OP == kGeluGeneric ||
                                OP == kSilu || OP == kHardswish || OP == kHardsigmoid || OP == kExp || OP == kExpm1 ||
                                OP == kSoftplus || OP == kGeluErf;
 

@@ -330,6 +330,47 @@ __global__ void __launch_bounds__(kThreads) ew_ordinal(EwPlan p, F f) {
     }
 }
 
+// The generic envelope's repeat (generic.rs:1641-1665): dst ordinal o ->
+// coordinates in dst's extents -> each taken modulo src's extent -> src
+// element; copied as raw 32-bit words (NaN payloads kept).  32-bit
+// magic-number decode when every extent and the count fit, else 64-bit.
+struct RepeatArgs {
+    FastDiv d0, d1, d2;      // dst extents
+    FastDiv m0, m1, m2, m3;  // src extents (modulo)
+    bool small;
+};
+
+__global__ void __launch_bounds__(kThreads) repeat_copy(EwPlan p, RepeatArgs r) {
+    pdl_enter();
+    const uint32_t* src = reinterpret_cast<const uint32_t*>(p.src0.ptr);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(p.dst.ptr);
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    for (uint64_t i = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x; i < p.count; i += stride) {
+        uint64_t c[4];
+        if (r.small) {
+            const uint32_t o = (uint32_t)i;
+            const uint32_t q0 = fdiv(o, r.d0), q1 = fdiv(q0, r.d1), q2 = fdiv(q1, r.d2);
+            c[0] = o - q0 * r.d0.d;
+            c[1] = q0 - q1 * r.d1.d;
+            c[2] = q1 - q2 * r.d2.d;
+            c[3] = q2;
+        } else {
+            uint64_t o = i;
+            for (int d = 0; d < 4; ++d) {
+                c[d] = o % p.ne[d];
+                o /= p.ne[d];
+            }
+        }
+        int64_t od = 0, os = 0;
+#pragma unroll
+        for (int d = 0; d < 4; ++d) {
+            od += (int64_t)c[d] * p.dst.st[d];
+            os += (int64_t)(c[d] % p.src0.ne[d]) * p.src0.st[d];
+        }
+        dst[od] = src[os];
+    }
+}
+
 uint32_t grid_for(const LaunchEnv& env, uint64_t work_items, int per_thread) {
     const uint64_t want = (work_items + (uint64_t)kThreads * per_thread - 1) / ((uint64_t)kThreads * per_thread);
     const uint64_t cap = (uint64_t)env.sm_count * 8;  // 8 x 256 threads = 2048 resident threads per SM
@@ -399,7 +440,7 @@ cudaError_t launch_ew(const LaunchEnv& env, const EwPlan& p, const F& f) {
 // HBM speed for every op instead of being bound by the binary64 libm cores.
 // ---------------------------------------------------------------------------
 template <int OP>
-constexpr bool kTableOp = kHeavyFormula<OP> || OP == kSqrt || OP == kLog || OP == kSin || OP == kCos;
+constexpr bool kTableOp = (kHeavyFormula<OP> || OP == kSqrt || OP == kLog || OP == kSin || OP == kCos) && OP < 128;
 
 constexpr uint64_t kTableMinCount = 1ull << 20;  // below this the table costs more than it saves
 constexpr int kTableThreads = 640;  // leaves registers for two build CTAs per SM
@@ -609,10 +650,25 @@ cudaError_t launch_unary(const LaunchEnv& env, const EwPlan& p, int op, float pa
         EMEL_UNARY_CASE(kGeluErf) EMEL_UNARY_CASE(kFloor) EMEL_UNARY_CASE(kCeil) EMEL_UNARY_CASE(kRound)
         EMEL_UNARY_CASE(kTrunc) EMEL_UNARY_CASE(kSqr) EMEL_UNARY_CASE(kSqrt) EMEL_UNARY_CASE(kLog)
         EMEL_UNARY_CASE(kSin) EMEL_UNARY_CASE(kCos) EMEL_UNARY_CASE(kScale) EMEL_UNARY_CASE(kClamp)
-        EMEL_UNARY_CASE(kLeakyRelu) EMEL_UNARY_CASE(kAdd1) EMEL_UNARY_CASE(kCopy)
+        EMEL_UNARY_CASE(kLeakyRelu) EMEL_UNARY_CASE(kAdd1) EMEL_UNARY_CASE(kCopy) EMEL_UNARY_CASE(kGeluGeneric)
 #undef EMEL_UNARY_CASE
     default: return cudaErrorInvalidValue;
     }
+}
+
+cudaError_t launch_repeat(const LaunchEnv& env, const EwPlan& p) {
+    RepeatArgs r{};
+    r.small = p.count < (1ull << 32);
+    for (int d = 0; d < 4; ++d) r.small = r.small && p.ne[d] < (1ull << 31);
+    if (r.small) {
+        r.d0 = make_fastdiv((uint32_t)p.ne[0]);
+        r.d1 = make_fastdiv((uint32_t)p.ne[1]);
+        r.d2 = make_fastdiv((uint32_t)p.ne[2]);
+    }
+    const cudaError_t err =
+        launch_dependent(repeat_copy, dim3(grid_for(env, p.count, 1)), dim3(kThreads), 0, env.stream, p, r);
+    ++*env.launches;
+    return err != cudaSuccess ? err : cudaGetLastError();
 }
 
 cudaError_t launch_binary(const LaunchEnv& env, const EwPlan& p, int op) {

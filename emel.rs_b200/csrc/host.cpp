@@ -958,3 +958,217 @@ emel_cuda_status check_scalar_sum(const emel_tensor_view* src, const emel_tensor
 }
 
 }  // namespace emel
+
+// ===========================================================================
+// Generic operation envelope (emel_cuda_generic)
+// ===========================================================================
+namespace {
+
+using u128g = unsigned __int128;
+
+// validate_span (generic.rs:822-862): every extent nonzero, the element count
+// representable, no zero stride on an extent > 1, and the highest byte inside
+// the storage.  F32 views resolve the implicit nb[0] == 0 form.
+bool generic_span_valid(const emel_tensor_view* v, uint64_t nb[4], uint64_t* count) {
+    if (v->dtype == EMEL_DTYPE_F32) {
+        if (!strides_of(*v, 4, nb)) return false;
+    } else {
+        for (int d = 0; d < 4; ++d) nb[d] = v->nb[d];
+    }
+    uint64_t c = 1;
+    for (int d = 0; d < 4; ++d) {
+        if (v->ne[d] == 0 || __builtin_mul_overflow(c, v->ne[d], &c)) return false;
+        if (v->ne[d] > 1 && nb[d] == 0) return false;
+    }
+    u128g max_offset = 0;
+    for (int d = 0; d < 4; ++d) {
+        const u128g term = (u128g)(v->ne[d] - 1) * (u128g)nb[d];
+        if (__builtin_add_overflow(max_offset, term, &max_offset)) return false;
+    }
+    u128g end;
+    if (__builtin_add_overflow(max_offset, (u128g)1, &end)) return false;
+    if (end > (u128g)v->storage_bytes) return false;
+    *count = c;
+    return true;
+}
+
+// RawTensorView::f32_valid (generic.rs:467-473): an F32 view whose span is
+// valid and whose every byte stride is at least 4.
+bool generic_f32_valid(const emel_tensor_view* v, Checked* out) {
+    if (v == nullptr || v->dtype != EMEL_DTYPE_F32) return false;
+    Checked c;
+    c.elem = 4;
+    if (!generic_span_valid(v, c.nb, &c.count)) return false;
+    for (int d = 0; d < 4; ++d)
+        if (c.nb[d] < 4) return false;
+    *out = c;
+    return true;
+}
+
+// The device reads binary32 with aligned loads.
+bool generic_device_aligned(const emel_tensor_view* v, const Checked& c) {
+    if (reinterpret_cast<uintptr_t>(v->data) % 4 != 0) return false;
+    for (int d = 0; d < 4; ++d)
+        if (c.nb[d] % 4 != 0) return false;
+    return true;
+}
+
+// parameter_f32 (generic.rs:907-911): slot k is bytes [4k, 4k + 4) of the
+// initialised prefix.
+bool generic_param(const emel_cuda_generic_request* r, int slot, float* out) {
+    const uint32_t end = (uint32_t)slot * 4u + 4u;
+    if (end > r->params_len) return false;
+    std::memcpy(out, r->params + slot * 4, 4);
+    return true;
+}
+
+enum class GenericKind { Copy, Binary, Scalar, Clamp, SiluBack, Repeat, Unary, Sum, Mean, Argmax, SoftMax, Norm };
+
+}  // namespace
+
+extern "C" emel_cuda_status emel_cuda_generic(emel_cuda_context* ctx, void* stream,
+                                              const emel_cuda_generic_request* r) {
+    if (r == nullptr || r->op >= 95 || r->params_len > 64) return EMEL_CUDA_INVALID_ARGUMENT;
+    // GenericRequest::validate (generic.rs:747-766): every present view
+    const emel_tensor_view* all[4] = {r->src0, r->src1, r->src2, r->dst};
+    for (const emel_tensor_view* v : all) {
+        uint64_t nb[4], count;
+        if (v != nullptr && !generic_span_valid(v, nb, &count)) return EMEL_CUDA_INVALID_SHAPE;
+    }
+    // maintained routes of the device table (sm.rs:324-419)
+    GenericKind kind;
+    int code = 0;
+    switch (r->op) {
+    case 0: kind = GenericKind::Copy; break;
+    case 1: kind = GenericKind::Binary; code = EMEL_BINARY_ADD; break;
+    case 5: kind = GenericKind::Binary; code = EMEL_BINARY_SUB; break;
+    case 6: kind = GenericKind::Binary; code = EMEL_BINARY_MUL; break;
+    case 7: kind = GenericKind::Binary; code = EMEL_BINARY_DIV; break;
+    case 3: kind = GenericKind::Scalar; code = emel::kAdd1; break;
+    case 32: kind = GenericKind::Scalar; code = emel::kScale; break;
+    case 70: kind = GenericKind::Scalar; code = emel::kLeakyRelu; break;
+    case 50: kind = GenericKind::Clamp; code = emel::kClamp; break;
+    case 22: kind = GenericKind::SiluBack; break;
+    case 19: kind = GenericKind::Repeat; break;
+    case 8: kind = GenericKind::Unary; code = EMEL_UNARY_SQR; break;
+    case 9: kind = GenericKind::Unary; code = EMEL_UNARY_SQRT; break;
+    case 10: kind = GenericKind::Unary; code = EMEL_UNARY_LOG; break;
+    case 11: kind = GenericKind::Unary; code = EMEL_UNARY_SIN; break;
+    case 12: kind = GenericKind::Unary; code = EMEL_UNARY_COS; break;
+    case 13: kind = GenericKind::Sum; break;
+    case 16: kind = GenericKind::Mean; break;
+    case 17: kind = GenericKind::Argmax; break;
+    case 46: kind = GenericKind::SoftMax; break;
+    case 23: kind = GenericKind::Norm; code = 3; break;
+    case 24: kind = GenericKind::Norm; code = 4; break;
+    case 85:
+        // generic.rs:1307-1350 (execute_generic_unary); any other subop is a
+        // known-invalid request (actor.rs guard_generic_known_invalid)
+        kind = GenericKind::Unary;
+        switch (r->unary_subop) {
+        case 0: code = EMEL_UNARY_ABS; break;
+        case 2: code = EMEL_UNARY_NEG; break;
+        case 4: code = EMEL_UNARY_TANH; break;
+        case 5: code = EMEL_UNARY_ELU; break;
+        case 6: code = EMEL_UNARY_RELU; break;
+        case 8: code = emel::kGeluGeneric; break;
+        case 10: code = EMEL_UNARY_SILU; break;
+        case 13: code = EMEL_UNARY_EXP; break;
+        default: return EMEL_CUDA_INVALID_SHAPE;
+        }
+        break;
+    default:
+        return EMEL_CUDA_UNSUPPORTED_OPERATION;
+    }
+    // operand rules of the route (generic.rs:938-990, 1136-1190)
+    Checked c0, c1, cd;
+    const bool v0 = generic_f32_valid(r->src0, &c0);
+    const bool v1 = generic_f32_valid(r->src1, &c1);
+    const bool vd = generic_f32_valid(r->dst, &cd);
+    float pa = 0.0f, pb = 0.0f;
+    bool ok = false;
+    switch (kind) {
+    case GenericKind::Copy:
+    case GenericKind::Unary:
+    case GenericKind::SoftMax: ok = v0 && vd && c0.count == cd.count; break;
+    case GenericKind::Binary: ok = v0 && v1 && vd && c0.count == c1.count && c0.count == cd.count; break;
+    case GenericKind::Scalar:
+        ok = v0 && vd && c0.count == cd.count && generic_param(r, 0, &pa) && std::isfinite(pa);
+        break;
+    case GenericKind::Clamp:
+        ok = v0 && vd && c0.count == cd.count && generic_param(r, 0, &pa) && generic_param(r, 1, &pb) &&
+             std::isfinite(pa) && std::isfinite(pb) && pa <= pb;
+        break;
+    case GenericKind::SiluBack: ok = v0 && v1 && vd && same_ne(r->src0, r->src1) && same_ne(r->src0, r->dst); break;
+    case GenericKind::Repeat:
+        ok = v0 && vd;
+        for (int d = 0; ok && d < 4; ++d) ok = r->dst->ne[d] % r->src0->ne[d] == 0;
+        break;
+    case GenericKind::Sum:
+    case GenericKind::Mean:
+    case GenericKind::Argmax: ok = v0 && vd && cd.count == 1; break;
+    case GenericKind::Norm:
+        ok = v0 && vd && same_ne(r->src0, r->dst) && generic_param(r, 0, &pa) && std::isfinite(pa) && pa >= 0.0f;
+        break;
+    }
+    if (!ok) return EMEL_CUDA_INVALID_SHAPE;
+    const bool uses1 = kind == GenericKind::Binary || kind == GenericKind::SiluBack;
+    if (!generic_device_aligned(r->src0, c0) || !generic_device_aligned(r->dst, cd) ||
+        (uses1 && !generic_device_aligned(r->src1, c1))) {
+        if (ctx != nullptr)
+            std::snprintf(ctx->last_error, sizeof(ctx->last_error), "device views need 4-byte aligned data and strides");
+        return EMEL_CUDA_INVALID_ARGUMENT;
+    }
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    cudaError_t err = select_device(ctx);
+    if (err != cudaSuccess) return device_status(ctx, err);
+    const emel::LaunchEnv env = env_of(ctx, stream);
+    switch (kind) {
+    case GenericKind::Copy:
+    case GenericKind::Unary:
+    case GenericKind::Scalar:
+    case GenericKind::Clamp: {
+        const emel_tensor_view* views[3] = {r->dst, r->src0, nullptr};
+        const Checked* cks[3] = {&cd, &c0, nullptr};
+        const int op = kind == GenericKind::Copy ? (int)emel::kCopy : code;
+        err = emel::launch_unary(env, plan_equal_count(DType::F32, views, cks, 2), op, pa, pb);
+        break;
+    }
+    case GenericKind::Binary:
+    case GenericKind::SiluBack: {
+        const emel_tensor_view* views[3] = {r->dst, r->src0, r->src1};
+        const Checked* cks[3] = {&cd, &c0, &c1};
+        err = emel::launch_binary(env, plan_equal_count(DType::F32, views, cks, 3),
+                                  kind == GenericKind::Binary ? code : (int)emel::kSiluBack);
+        break;
+    }
+    case GenericKind::Repeat: {
+        emel::EwPlan p{};
+        p.dtype = DType::F32;
+        p.count = cd.count;
+        for (int d = 0; d < 4; ++d) p.ne[d] = r->dst->ne[d];
+        p.dst = operand(r->dst, cd);
+        p.src0 = operand(r->src0, c0);
+        err = emel::launch_repeat(env, p);
+        break;
+    }
+    case GenericKind::Sum:
+    case GenericKind::Mean:
+        err = emel::launch_sum(env, plan_rows(r->src0, c0, nullptr, nullptr), kind == GenericKind::Sum ? 0 : 1,
+                               r->dst->data);
+        break;
+    case GenericKind::Argmax:
+        err = emel::launch_argmax(env, plan_rows(r->src0, c0, nullptr, nullptr), 0, (int)DType::F32, 0, r->dst->data);
+        break;
+    case GenericKind::SoftMax: {
+        emel::RowPlan p = plan_rows(r->src0, c0, r->dst, &cd);
+        if (!same_ne(r->src0, r->dst)) p.dst_ordinal = true;
+        err = emel::launch_soft_max_generic(env, p);
+        break;
+    }
+    case GenericKind::Norm:
+        err = emel::launch_norm_generic(env, plan_rows(r->src0, c0, r->dst, &cd), code, pa);
+        break;
+    }
+    return device_status(ctx, err);
+}

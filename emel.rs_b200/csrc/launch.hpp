@@ -30,9 +30,16 @@ cudaError_t launch_argmax(const LaunchEnv& env, const RowPlan& plan, int out_kin
 
 // Ring-staged norm / rms_norm / rms_norm * weight / soft_max (rowring.cu).
 // Returns false, launching nothing, when the view does not qualify.
-// op: 0 norm, 1 rms_norm, 2 rms_norm * weight, 3 soft_max.
+// op: 0 norm, 1 rms_norm, 2 rms_norm * weight, 3 soft_max, 4 / 5 the
+// generic envelope's norm / rms_norm.
 bool launch_row_ring(const LaunchEnv& env, const RowPlan& plan, int op, float param, bool apply_scale,
                      cudaError_t* err);
+
+// The generic operation envelope (generic.rs): its norm (3) / rms_norm (4)
+// numerics, its soft_max, and repeat as a modulo-broadcast copy.
+cudaError_t launch_norm_generic(const LaunchEnv& env, const RowPlan& plan, int op, float eps);
+cudaError_t launch_soft_max_generic(const LaunchEnv& env, const RowPlan& plan);
+cudaError_t launch_repeat(const LaunchEnv& env, const EwPlan& plan);
 
 // Few long rows (rowsplit.cu): one 8-CTA cluster per row.
 bool split_rows_wanted(const LaunchEnv& env, const RowPlan& plan);

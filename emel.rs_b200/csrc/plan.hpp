@@ -19,7 +19,8 @@ enum UnaryOp : int {
     kGeluQuick = 9, kSilu = 10, kHardswish = 11, kHardsigmoid = 12, kExp = 13, kExpm1 = 14, kSoftplus = 15,
     kGeluErf = 16, kFloor = 18, kCeil = 19, kRound = 20, kTrunc = 21,
     kSqr = 64, kSqrt = 65, kLog = 66, kSin = 67, kCos = 68,
-    kScale = 128, kClamp = 129, kLeakyRelu = 130, kAdd1 = 131, kCopy = 132
+    kScale = 128, kClamp = 129, kLeakyRelu = 130, kAdd1 = 131, kCopy = 132,
+    kGeluGeneric = 133  // the generic envelope's GELU (generic.rs:1330-1337)
 };
 
 // One operand over the iteration space: base address and element strides per

@@ -42,7 +42,8 @@ constexpr int kRingThreads = 256;
 constexpr uint32_t kRingSmemPerSm = 220 * 1024;
 constexpr uint32_t kStageAlign = 128;
 
-enum RingOp { kRingNorm = 0, kRingRms = 1, kRingRmsMul = 2, kRingSoftMax = 3 };
+// 4 / 5: the generic envelope's norm / rms_norm numerics (generic.rs:1992-2050).
+enum RingOp { kRingNorm = 0, kRingRms = 1, kRingRmsMul = 2, kRingSoftMax = 3, kRingNormGeneric = 4, kRingRmsGeneric = 5 };
 
 // aux_mode
 enum { kAuxNone = 0, kAuxWeight = 1, kAuxMaskStaged = 2, kAuxMaskLoads = 3 };
@@ -230,7 +231,7 @@ __global__ void __launch_bounds__(T, 1024 / T) row_ring(RingArgs a) {
         const uint32_t r = blockIdx.x + k * gridDim.x;
         float* drow = reinterpret_cast<float*>(a.dst) + row_offset(r, a, a.dst_st);
 
-        if constexpr (OP == kRingNorm) {
+        if constexpr (OP == kRingNorm || OP == kRingNormGeneric) {
             double acc = 0.0;
             for (uint32_t v = tid; v < nvec; v += T) {
                 const float4 x = ld_f4(row + 4 * v);
@@ -244,25 +245,33 @@ __global__ void __launch_bounds__(T, 1024 / T) row_ring(RingArgs a) {
             double vs = 0.0;
             for (uint32_t v = tid; v < nvec; v += T) {
                 const float4 x = ld_f4(row + 4 * v);
-                double c = (double)__fsub_rn(x.x, mean);
-                vs += c * c;
-                c = (double)__fsub_rn(x.y, mean);
-                vs += c * c;
-                c = (double)__fsub_rn(x.z, mean);
-                vs += c * c;
-                c = (double)__fsub_rn(x.w, mean);
-                vs += c * c;
+                const float cs[4] = {__fsub_rn(x.x, mean), __fsub_rn(x.y, mean), __fsub_rn(x.z, mean),
+                                     __fsub_rn(x.w, mean)};
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    if constexpr (OP == kRingNormGeneric) {
+                        vs += (double)__fmul_rn(cs[k], cs[k]);  // squared in binary32
+                    } else {
+                        const double c = (double)cs[k];
+                        vs += c * c;
+                    }
+                }
             }
             vs = block_sum<T>(vs, &red);
-            const float variance = __double2float_rn(vs / (double)a.ne0);
-            const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(variance, a.param)));
+            float scale;
+            if constexpr (OP == kRingNormGeneric) {
+                scale = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(vs / (double)a.ne0, (double)a.param))));
+            } else {
+                const float variance = __double2float_rn(vs / (double)a.ne0);
+                scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(variance, a.param)));
+            }
             for (uint32_t v = tid; v < nvec; v += T) {
                 const float4 x = ld_f4(row + 4 * v);
                 store4<OP>(a, drow, v,
                            make_float4(f_mul(f_sub(x.x, mean), scale), f_mul(f_sub(x.y, mean), scale),
                                        f_mul(f_sub(x.z, mean), scale), f_mul(f_sub(x.w, mean), scale)));
             }
-        } else if constexpr (OP == kRingRms || OP == kRingRmsMul) {
+        } else if constexpr (OP == kRingRms || OP == kRingRmsMul || OP == kRingRmsGeneric) {
             double acc = 0.0;
             for (uint32_t v = tid; v < nvec; v += T) {
                 const float4 x = ld_f4(row + 4 * v);
@@ -273,7 +282,9 @@ __global__ void __launch_bounds__(T, 1024 / T) row_ring(RingArgs a) {
             }
             acc = block_sum<T>(acc, &red);
             const float mean = __double2float_rn(acc / (double)a.ne0);
-            const float scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.param)));
+            const float scale = OP == kRingRmsGeneric
+                                    ? __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn((double)mean, (double)a.param))))
+                                    : __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, a.param)));
             for (uint32_t v = tid; v < nvec; v += T) {
                 const float4 x = ld_f4(row + 4 * v);
                 float4 y = make_float4(f_mul(x.x, scale), f_mul(x.y, scale), f_mul(x.z, scale), f_mul(x.w, scale));
@@ -420,7 +431,7 @@ cudaError_t launch_ring_kernel(const LaunchEnv& env, RingArgs a, uint64_t rows, 
 // ne0 % 4 == 0 floats, unit stride in dim 0, every row start 16-byte
 // aligned, and (for soft_max) dense src/dst so the f64 sum applies.  Returns
 // false (nothing launched) otherwise.  op: 0 norm, 1 rms_norm, 2 rms_norm *
-// weight, 3 soft_max.
+// weight, 3 soft_max, 4 / 5 the generic envelope's norm / rms_norm.
 bool launch_row_ring(const LaunchEnv& env, const RowPlan& p, int op, float param, bool apply_scale,
                      cudaError_t* err) {
     const uint64_t ne0 = p.ne[0];
@@ -478,7 +489,9 @@ bool launch_row_ring(const LaunchEnv& env, const RowPlan& p, int op, float param
     case 0: e = launch_ring_kernel<kRingNorm, kRingThreads>(env, a, p.rows, &launched); break;
     case 1: e = launch_ring_kernel<kRingRms, kRingThreads>(env, a, p.rows, &launched); break;
     case 2: e = launch_ring_kernel<kRingRmsMul, kRingThreads>(env, a, p.rows, &launched); break;
-    default: e = launch_ring_kernel<kRingSoftMax, kRingThreads>(env, a, p.rows, &launched); break;
+    case 3: e = launch_ring_kernel<kRingSoftMax, kRingThreads>(env, a, p.rows, &launched); break;
+    case 4: e = launch_ring_kernel<kRingNormGeneric, kRingThreads>(env, a, p.rows, &launched); break;
+    default: e = launch_ring_kernel<kRingRmsGeneric, kRingThreads>(env, a, p.rows, &launched); break;
     }
     if (e == cudaSuccess && !launched) return false;
     ++*env.launches;

@@ -224,6 +224,10 @@ __global__ void __launch_bounds__(G > 256 ? G : 256) softmax_rows(RowPlan p, boo
 // Non-dense views: the reference sums exp values sequentially in f32
 // (reductions.rs:620-626).  One CTA per row stages exp values in shared
 // memory and thread 0 adds them in row order.
+// FIRST_PIN: the typed loop's scan starts from element 0, so a NaN there is
+// the maximum (reductions.rs:572); the generic envelope's loop starts from
+// -inf and skips NaNs (generic.rs:1966-1971).
+template <bool FIRST_PIN>
 __global__ void __launch_bounds__(256) softmax_rows_seq(RowPlan p, bool apply_scale, float scale) {
     extern __shared__ float ebuf[];
     __shared__ GroupScratch<256> s;
@@ -246,7 +250,8 @@ __global__ void __launch_bounds__(256) softmax_rows_seq(RowPlan p, bool apply_sc
         }
         m = group_max<256>(m, &s);
         __syncthreads();
-        if (is_nan(ebuf[0])) m = ebuf[0];
+        if (FIRST_PIN && is_nan(ebuf[0])) m = ebuf[0];
+        if (!FIRST_PIN && is_nan(m)) m = -INFINITY;  // no comparable value: the -inf start stays
         for (uint64_t c = lane; c < ne0; c += 256) ebuf[c] = lm_exp(f_sub(ebuf[c], m));
         __syncthreads();
         if (lane == 0) {
@@ -421,9 +426,15 @@ __device__ __forceinline__ float* dst_elem(const RowPlan& p, uint64_t r, uint64_
     return reinterpret_cast<float*>(p.dst.ptr) + off;
 }
 
+// OP 0 norm, 1 rms_norm, 2 rms_norm * weight (normalization.rs:316-362);
+// OP 3 / 4: the generic envelope's norm / rms_norm (generic.rs:1992-2050),
+// whose variance squares in binary32 and whose scale is 1 / sqrt(. + eps)
+// evaluated in binary64 and rounded once.
 template <int OP>
 __global__ void __launch_bounds__(1024) norm_rows_stream(RowPlan p, float eps) {
     __shared__ GroupScratch<1024> s;
+    constexpr bool kNorm = OP == 0 || OP == 3;
+    constexpr bool kGeneric = OP >= 3;
     const uint64_t ne0 = p.ne[0];
     for (uint64_t r = blockIdx.x; r < p.rows; r += gridDim.x) {
         const float* xrow = reinterpret_cast<const float*>(p.src.ptr) + row_base(p.src, r, p.ne[1], p.ne[2]);
@@ -431,26 +442,37 @@ __global__ void __launch_bounds__(1024) norm_rows_stream(RowPlan p, float eps) {
         double acc = 0.0;
         for (uint64_t c = threadIdx.x; c < ne0; c += 1024) {
             const float x = xrow[(int64_t)c * st0];
-            acc += OP == 0 ? (double)x : (double)__fmul_rn(x, x);
+            acc += kNorm ? (double)x : (double)__fmul_rn(x, x);
         }
         acc = group_sum<1024>(acc, &s);
         const float mean = __double2float_rn(acc / (double)ne0);
         float scale;
-        if constexpr (OP == 0) {
+        if constexpr (kNorm) {
             double vs = 0.0;
             for (uint64_t c = threadIdx.x; c < ne0; c += 1024) {
-                const double d = (double)__fsub_rn(xrow[(int64_t)c * st0], mean);
-                vs += d * d;
+                const float cf = __fsub_rn(xrow[(int64_t)c * st0], mean);
+                if constexpr (kGeneric) {
+                    vs += (double)__fmul_rn(cf, cf);
+                } else {
+                    const double d = (double)cf;
+                    vs += d * d;
+                }
             }
             vs = group_sum<1024>(vs, &s);
-            const float variance = __double2float_rn(vs / (double)ne0);
-            scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(variance, eps)));
+            if constexpr (kGeneric) {
+                scale = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn(vs / (double)ne0, (double)eps))));
+            } else {
+                const float variance = __double2float_rn(vs / (double)ne0);
+                scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(variance, eps)));
+            }
+        } else if constexpr (kGeneric) {
+            scale = __double2float_rn(__ddiv_rn(1.0, __dsqrt_rn(__dadd_rn((double)mean, (double)eps))));
         } else {
             scale = __fdiv_rn(1.0f, __fsqrt_rn(__fadd_rn(mean, eps)));
         }
         for (uint64_t c = threadIdx.x; c < ne0; c += 1024) {
             const float x = xrow[(int64_t)c * st0];
-            float y = OP == 0 ? f_mul(f_sub(x, mean), scale) : f_mul(x, scale);
+            float y = kNorm ? f_mul(f_sub(x, mean), scale) : f_mul(x, scale);
             if constexpr (OP == 2) y = f_mul(y, reinterpret_cast<const float*>(p.aux.ptr)[(int64_t)c * p.aux.st[0]]);
             dst_elem(p, r, c)[0] = y;
         }
@@ -460,6 +482,7 @@ __global__ void __launch_bounds__(1024) norm_rows_stream(RowPlan p, float eps) {
 // soft_max over rows re-read per pass.  Dense layouts sum in f64 across the
 // CTA; non-dense layouts keep the reference's sequential f32 sum by having
 // thread 0 walk the row in order (correct for any width, slow by design).
+template <bool FIRST_PIN>
 __global__ void __launch_bounds__(1024) softmax_rows_stream(RowPlan p, bool apply_scale, float scale) {
     __shared__ GroupScratch<1024> s;
     __shared__ float total;
@@ -479,7 +502,8 @@ __global__ void __launch_bounds__(1024) softmax_rows_stream(RowPlan p, bool appl
         for (uint64_t c = threadIdx.x; c < ne0; c += 1024) m = max_nn(m, value(c));
         m = group_max<1024>(m, &s);
         const float v0 = value(0);
-        if (is_nan(v0)) m = v0;
+        if (FIRST_PIN && is_nan(v0)) m = v0;
+        if (!FIRST_PIN && is_nan(m)) m = -INFINITY;
         if (p.dense) {
             double acc = 0.0;
             for (uint64_t c = threadIdx.x; c < ne0; c += 1024) acc += (double)lm_exp(f_sub(value(c), m));
@@ -541,6 +565,36 @@ cudaError_t launch_norm(const LaunchEnv& env, const RowPlan& p, int op, float ep
     return cudaGetLastError();
 }
 
+// The generic envelope's norm (op 3) / rms_norm (op 4): the ring when the
+// view qualifies, else one 1024-thread CTA per row.
+cudaError_t launch_norm_generic(const LaunchEnv& env, const RowPlan& p, int op, float eps) {
+    cudaError_t ring_err;
+    if (!p.dst_ordinal && launch_row_ring(env, p, op == 3 ? 4 : 5, eps, false, &ring_err)) return ring_err;
+    const uint32_t grid = row_grid(env, p.rows, 1, 2);
+    if (op == 3) norm_rows_stream<3><<<grid, 1024, 0, env.stream>>>(p, eps);
+    else norm_rows_stream<4><<<grid, 1024, 0, env.stream>>>(p, eps);
+    ++*env.launches;
+    return cudaGetLastError();
+}
+
+// The generic envelope's soft_max (generic.rs:1952-1989): maximum from -inf
+// over non-NaN values, exp written out, a sequential binary32 sum per row,
+// then a division.  Rows that fit in shared memory are staged there; longer
+// ones are re-read.
+cudaError_t launch_soft_max_generic(const LaunchEnv& env, const RowPlan& p) {
+    if (!p.dst_ordinal && p.ne[0] * sizeof(float) <= 200 * 1024) {
+        const size_t smem = p.ne[0] * sizeof(float);
+        cudaFuncSetAttribute(softmax_rows_seq<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        softmax_rows_seq<false><<<row_grid(env, p.rows, 1, 8), 256, smem, env.stream>>>(p, false, 1.0f);
+    } else {
+        RowPlan q = p;
+        q.dense = false;  // the sequential binary32 sum
+        softmax_rows_stream<false><<<row_grid(env, p.rows, 1, 2), 1024, 0, env.stream>>>(q, false, 1.0f);
+    }
+    ++*env.launches;
+    return cudaGetLastError();
+}
+
 uint64_t soft_max_cluster_capacity() { return 8ull * 1024 * kMaxE; }
 
 cudaError_t launch_soft_max(const LaunchEnv& env, const RowPlan& p, bool apply_scale, float scale) {
@@ -549,14 +603,14 @@ cudaError_t launch_soft_max(const LaunchEnv& env, const RowPlan& p, bool apply_s
     if (p.dense && split_rows_wanted(env, p)) return launch_soft_max_split(env, p, apply_scale, scale);
     const bool long_row = resident_group(p.ne[0]) == 0 && (!p.vec || p.ne[0] > soft_max_cluster_capacity());
     if (p.dst_ordinal || (!p.dense && p.ne[0] * sizeof(float) > 200 * 1024) || (p.dense && long_row)) {
-        softmax_rows_stream<<<row_grid(env, p.rows, 1, 2), 1024, 0, env.stream>>>(p, apply_scale, scale);
+        softmax_rows_stream<true><<<row_grid(env, p.rows, 1, 2), 1024, 0, env.stream>>>(p, apply_scale, scale);
         ++*env.launches;
         return cudaGetLastError();
     }
     if (!p.dense) {
         const size_t smem = p.ne[0] * sizeof(float);
-        cudaFuncSetAttribute(softmax_rows_seq, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        softmax_rows_seq<<<row_grid(env, p.rows, 1, 8), 256, smem, env.stream>>>(p, apply_scale, scale);
+        cudaFuncSetAttribute(softmax_rows_seq<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        softmax_rows_seq<true><<<row_grid(env, p.rows, 1, 8), 256, smem, env.stream>>>(p, apply_scale, scale);
         ++*env.launches;
         return cudaGetLastError();
     }

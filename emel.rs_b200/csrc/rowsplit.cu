@@ -43,6 +43,22 @@ struct Chunk {
     uint64_t col0, col1;
 };
 
+// Visits the 16-byte vectors v0 + tid, v0 + tid + T, ... below v1, issuing U
+// loads before using any of them (one load in flight per thread would leave
+// the chunk's passes latency-bound).
+template <int U, typename Load, typename Use>
+__device__ __forceinline__ void batched(uint64_t v0, uint64_t v1, Load load, Use use) {
+    uint64_t v = v0 + threadIdx.x;
+    for (; v + (U - 1) * kSplitThreads < v1; v += U * kSplitThreads) {
+        float4 q[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) q[k] = load(v + k * kSplitThreads);
+#pragma unroll
+        for (int k = 0; k < U; ++k) use(v + k * kSplitThreads, q[k]);
+    }
+    for (; v < v1; v += kSplitThreads) use(v, load(v));
+}
+
 __device__ __forceinline__ Chunk my_chunk(uint64_t ne0, uint64_t chunk, unsigned rank) {
     const uint64_t c0 = (uint64_t)rank * chunk;
     return Chunk{c0 < ne0 ? c0 : ne0, c0 + chunk < ne0 ? c0 + chunk : ne0};
@@ -132,13 +148,13 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitTh
     double acc = 0.0;
     if (p.vec) {
         const float4* r4 = reinterpret_cast<const float4*>(row);
-        for (uint64_t v = ch.col0 / 4 + threadIdx.x; v < ch.col1 / 4; v += kSplitThreads) {
-            const float4 q = __ldcs(r4 + v);
-            acc += (double)q.x;
-            acc += (double)q.y;
-            acc += (double)q.z;
-            acc += (double)q.w;
-        }
+        batched<8>(ch.col0 / 4, ch.col1 / 4, [&](uint64_t v) { return __ldcs(r4 + v); },
+                   [&](uint64_t, float4 q) {
+                       acc += (double)q.x;
+                       acc += (double)q.y;
+                       acc += (double)q.z;
+                       acc += (double)q.w;
+                   });
     } else {
         for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kSplitThreads) acc += (double)row[(int64_t)c * p.src.st[0]];
     }
@@ -222,11 +238,12 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitTh
     float m = bitsf(0x7fc00000u);
     bool odd = false;
     if (vec) {
-        for (uint64_t v = ch.col0 / 4 + threadIdx.x; v < ch.col1 / 4; v += kSplitThreads) {
-            const float4 q = scale4(__ldcg(x4 + v));
-            odd = odd || is_nan(q.x) || is_nan(q.y) || is_nan(q.z) || is_nan(q.w);
-            m = fmaxf(fmaxf(m, q.x), fmaxf(q.y, fmaxf(q.z, q.w)));
-        }
+        batched<8>(ch.col0 / 4, ch.col1 / 4, [&](uint64_t v) { return __ldcg(x4 + v); },
+                   [&](uint64_t, float4 raw) {
+                       const float4 q = scale4(raw);
+                       odd = odd || is_nan(q.x) || is_nan(q.y) || is_nan(q.z) || is_nan(q.w);
+                       m = fmaxf(fmaxf(m, q.x), fmaxf(q.y, fmaxf(q.z, q.w)));
+                   });
     } else {
         for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kSplitThreads) {
             const float v = value_at<false>(p, w, c, apply_scale, scale);
@@ -244,16 +261,18 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitTh
     if (isfinite(gm)) {
         // pass 2: e = exp(v - max) into dst, f64 sum
         if (vec) {
-            for (uint64_t v = ch.col0 / 4 + threadIdx.x; v < ch.col1 / 4; v += kSplitThreads) {
-                const float4 q = scale4(__ldcg(x4 + v));
-                const float4 e = make_float4(exp_nonpositive_split(__fsub_rn(q.x, gm)), exp_nonpositive_split(__fsub_rn(q.y, gm)),
-                                             exp_nonpositive_split(__fsub_rn(q.z, gm)), exp_nonpositive_split(__fsub_rn(q.w, gm)));
-                y4[v] = e;
-                acc += (double)e.x;
-                acc += (double)e.y;
-                acc += (double)e.z;
-                acc += (double)e.w;
-            }
+            batched<4>(ch.col0 / 4, ch.col1 / 4, [&](uint64_t v) { return __ldcg(x4 + v); },
+                       [&](uint64_t v, float4 raw) {
+                           const float4 q = scale4(raw);
+                           const float4 e = make_float4(
+                               exp_nonpositive_split(__fsub_rn(q.x, gm)), exp_nonpositive_split(__fsub_rn(q.y, gm)),
+                               exp_nonpositive_split(__fsub_rn(q.z, gm)), exp_nonpositive_split(__fsub_rn(q.w, gm)));
+                           y4[v] = e;
+                           acc += (double)e.x;
+                           acc += (double)e.y;
+                           acc += (double)e.z;
+                           acc += (double)e.w;
+                       });
         } else {
             for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kSplitThreads) {
                 const float e = exp_nonpositive_split(__fsub_rn(value_at<false>(p, w, c, apply_scale, scale), gm));
@@ -290,11 +309,11 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitTh
     if (isfinite(gm) && isfinite(denom)) {
         const float inv = __frcp_rn(denom);
         if (vec) {
-            for (uint64_t v = ch.col0 / 4 + threadIdx.x; v < ch.col1 / 4; v += kSplitThreads) {
-                const float4 e = y4[v];
-                __stcs(y4 + v, make_float4(div_by_split(e.x, denom, inv), div_by_split(e.y, denom, inv),
-                                           div_by_split(e.z, denom, inv), div_by_split(e.w, denom, inv)));
-            }
+            batched<8>(ch.col0 / 4, ch.col1 / 4, [&](uint64_t v) { return y4[v]; },
+                       [&](uint64_t v, float4 e) {
+                           __stcs(y4 + v, make_float4(div_by_split(e.x, denom, inv), div_by_split(e.y, denom, inv),
+                                                      div_by_split(e.z, denom, inv), div_by_split(e.w, denom, inv)));
+                       });
         } else {
             for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kSplitThreads) {
                 float* o = w.y + (int64_t)c * w.ys;

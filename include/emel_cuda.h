@@ -58,6 +58,8 @@ typedef enum emel_cuda_status {
     EMEL_CUDA_INVALID_PARAMETERS = 3, /* NormalizationError::InvalidParameters */
     EMEL_CUDA_UNEXPECTED_EVENT = 4,   /* *Error::UnexpectedEvent */
     EMEL_CUDA_INTERNAL = 5,           /* *Error::Internal */
+    EMEL_CUDA_INVALID_SHAPE = 6,      /* Error::InvalidShape (generic envelope, actor.rs:88-90) */
+    EMEL_CUDA_UNSUPPORTED_OPERATION = 7, /* Error::UnsupportedOperation (actor.rs:92) */
     EMEL_CUDA_DEVICE_ERROR = 16,      /* a CUDA runtime call failed */
     EMEL_CUDA_TIMEOUT = 17,           /* a bounded device wait expired */
     EMEL_CUDA_INVALID_ARGUMENT = 18,  /* null context / output pointer */
@@ -318,6 +320,41 @@ EMEL_CUDA_API emel_cuda_status emel_cuda_argmax_combine(const emel_cuda_argmax_p
  * [1, ne1, ne2, ne3], dtype F32, I32 or I64; the index is the column. */
 EMEL_CUDA_API emel_cuda_status emel_cuda_argmax_rows(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
                                        const emel_tensor_view* dst);
+
+/* ---- generic operation envelope -------------------------------------- */
+/* The op-coded boundary for graph-driven dispatch: GenericRequest with
+ * KernelOperation wire codes (generic.rs:24-316), up to three sources, a
+ * destination and the 64-byte op_params buffer (generic.rs:580-735),
+ * dispatched as Kernel::process_event(GenericEvent) (actor.rs:951-960,
+ * sm.rs:320-425).  Executed with the generic loops' own numerics
+ * (generic.rs:1263-2050, which differ from the typed events in places:
+ * GELU without binary16 rounding and with a fused cubic term, soft_max with
+ * a sequential binary32 sum and no NaN pin, norms squaring in binary32):
+ *   Dup 0, Add 1, Add1 3, Sub 5, Mul 6, Div 7, Sqr 8, Sqrt 9, Log 10, Sin 11,
+ *   Cos 12, Sum 13, Mean 16, Argmax 17, Repeat 19, SiluBack 22, Norm 23,
+ *   RmsNorm 24, Scale 32, SoftMax 46, Clamp 50, LeakyRelu 70, and Unary 85
+ *   with subops Abs 0, Neg 2, Tanh 4, Elu 5, Relu 6, Gelu 8, Silu 10, Exp 13.
+ * Scalars are op_params slots of 4 bytes (f32 at slot 0, clamp max at slot
+ * 1, norm eps at slot 0).  Statuses follow the reference state machine: a
+ * view that fails GenericRequest::validate, or a maintained operation whose
+ * operands do not fit it, is EMEL_CUDA_INVALID_SHAPE; any other operation
+ * code (including the reference's CPU-only routes such as Cumsum, Concat,
+ * MulMat) is EMEL_CUDA_UNSUPPORTED_OPERATION.  Device addition: F32 views
+ * whose data pointer or byte strides are not multiples of 4 are
+ * EMEL_CUDA_INVALID_ARGUMENT (the reference reads them byte by byte). */
+typedef struct emel_cuda_generic_request {
+    uint32_t op;          /* KernelOperation wire code, 0..94 */
+    uint32_t unary_subop; /* UnarySubOp wire code (unary.rs:101-160) when op == 85 */
+    const emel_tensor_view* src0; /* nullable */
+    const emel_tensor_view* src1; /* nullable */
+    const emel_tensor_view* src2; /* nullable */
+    const emel_tensor_view* dst;  /* nullable */
+    uint8_t params[64];   /* op_params */
+    uint32_t params_len;  /* initialised prefix, <= 64 (OpParams::new) */
+    uint32_t reserved;
+} emel_cuda_generic_request;
+EMEL_CUDA_API emel_cuda_status emel_cuda_generic(emel_cuda_context* ctx, void* stream,
+                                                 const emel_cuda_generic_request* request);
 
 #ifdef __cplusplus
 }

@@ -874,3 +874,254 @@ int oracle_argmax_rows(const oracle_view* src, const oracle_view* dst) {
     }
     return ORACLE_OK;
 }
+
+/* ---------------------------------------------------------------------- */
+/* Generic operation envelope: crates/emel-kernels/src/any/generic.rs      */
+/* ---------------------------------------------------------------------- */
+
+/* validate_span (generic.rs:822-862). */
+static int generic_span(const oracle_view* v, uint64_t nb[4], uint64_t* count) {
+    if (v->dtype == DT_F32) {
+        if (!effective_strides(v, 4, nb)) return 0;
+    } else {
+        memcpy(nb, v->nb, sizeof(uint64_t) * 4);
+    }
+    uint64_t c = 1;
+    for (int d = 0; d < 4; ++d) {
+        if (v->ne[d] == 0 || __builtin_mul_overflow(c, v->ne[d], &c)) return 0;
+        if (v->ne[d] > 1 && nb[d] == 0) return 0;
+    }
+    u128 max_offset = 0;
+    for (int d = 0; d < 4; ++d) {
+        u128 term = (u128)(v->ne[d] - 1) * (u128)nb[d];
+        if (__builtin_add_overflow(max_offset, term, &max_offset)) return 0;
+    }
+    u128 end;
+    if (__builtin_add_overflow(max_offset, (u128)1, &end)) return 0;
+    if (end > (u128)v->storage_bytes) return 0;
+    *count = c;
+    return 1;
+}
+
+/* RawTensorView::f32_valid (generic.rs:467-473). */
+static int generic_f32(const oracle_view* v, uint64_t nb[4], uint64_t* count) {
+    if (v == NULL || v->dtype != DT_F32) return 0;
+    if (!generic_span(v, nb, count)) return 0;
+    for (int d = 0; d < 4; ++d)
+        if (nb[d] < 4) return 0;
+    return 1;
+}
+
+/* read_f32_index / write_f32_index (generic.rs:474-482, 553-578): ordinal ->
+ * coordinates -> byte offset; unaligned bytes are fine on the host. */
+static float generic_read(const oracle_view* v, const uint64_t nb[4], uint64_t index) {
+    float f;
+    memcpy(&f, (const unsigned char*)v->data + ordinal_offset(v, nb, index), 4);
+    return f;
+}
+
+static void generic_write(const oracle_view* v, const uint64_t nb[4], uint64_t index, float value) {
+    memcpy((unsigned char*)v->data + ordinal_offset(v, nb, index), &value, 4);
+}
+
+static int generic_param(const oracle_generic_request* r, int slot, float* out) {
+    uint32_t end = (uint32_t)slot * 4u + 4u;
+    if (end > r->params_len) return 0;
+    memcpy(out, r->params + slot * 4, 4);
+    return 1;
+}
+
+/* f32::max(a, b) with the first argument the running maximum: a NaN operand
+ * is ignored (an equal pair keeps the running value). */
+static inline float rs_max(float a, float b) {
+    if (isnan(b)) return a;
+    if (isnan(a)) return b;
+    return b > a ? b : a;
+}
+
+/* execute_generic_unary formulas (generic.rs:1307-1350). */
+static float generic_unary_apply(int code, float v) {
+    switch (code) {
+    case 0: return fabsf(v);
+    case 1: return -v;
+    case 2: return tanhf(v);
+    case 3: return v > 0.0f ? v : expm1f(v);
+    case 4: return rs_max(v, 0.0f) == 0.0f ? 0.0f : rs_max(v, 0.0f); /* f32::max(v, 0.0); zeros -> +0 */
+    case 5: {
+        float rounded = v; /* f32::from_ne_bytes(value.to_ne_bytes()) */
+        return 0.5f * rounded * (1.0f + tanhf(0.7978846f * fmaf(0.044715f * rounded * rounded, rounded, rounded)));
+    }
+    case 6: return v / (1.0f + expf(-v));
+    case 7: return expf(v);
+    case 8: return v * v;
+    case 9: return sqrtf(v);
+    case 10: return logf(v);
+    case 11: return sinf(v);
+    case 12: return cosf(v);
+    default: return v;
+    }
+}
+
+int oracle_generic(const oracle_generic_request* r) {
+    if (r == NULL || r->op >= 95 || r->params_len > 64) return ORACLE_INVALID_ARGUMENT;
+    const oracle_view* all[4] = {r->src0, r->src1, r->src2, r->dst};
+    for (int k = 0; k < 4; ++k) {
+        uint64_t nb[4], count;
+        if (all[k] != NULL && !generic_span(all[k], nb, &count)) return ORACLE_INVALID_SHAPE;
+    }
+    uint64_t n0[4], n1[4], nd[4], c0 = 0, c1 = 0, cd = 0;
+    const int v0 = generic_f32(r->src0, n0, &c0);
+    const int v1 = generic_f32(r->src1, n1, &c1);
+    const int vd = generic_f32(r->dst, nd, &cd);
+    float pa = 0.0f, pb = 0.0f;
+    int unary_code = -1;
+    switch (r->op) {
+    case 85:
+        switch (r->unary_subop) { /* UnarySubOp -> execute_generic_unary selector */
+        case 0: unary_code = 0; break;
+        case 2: unary_code = 1; break;
+        case 4: unary_code = 2; break;
+        case 5: unary_code = 3; break;
+        case 6: unary_code = 4; break;
+        case 8: unary_code = 5; break;
+        case 10: unary_code = 6; break;
+        case 13: unary_code = 7; break;
+        default: return ORACLE_INVALID_SHAPE;
+        }
+        /* fallthrough */
+    case 8: case 9: case 10: case 11: case 12:
+        if (unary_code < 0) unary_code = (int)r->op; /* 8..12: sqr sqrt ln sin cos */
+        /* fallthrough */
+    case 0:
+        if (!(v0 && vd && c0 == cd)) return ORACLE_INVALID_SHAPE;
+        for (uint64_t i = 0; i < c0; ++i) {
+            float x = generic_read(r->src0, n0, i);
+            generic_write(r->dst, nd, i, r->op == 0 ? x : generic_unary_apply(unary_code, x));
+        }
+        return ORACLE_OK;
+    case 1: case 5: case 6: case 7: { /* execute_generic_binary (generic.rs:1280-1305) */
+        if (!(v0 && v1 && vd && c0 == c1 && c0 == cd)) return ORACLE_INVALID_SHAPE;
+        for (uint64_t i = 0; i < c0; ++i) {
+            float a = generic_read(r->src0, n0, i), b = generic_read(r->src1, n1, i), y;
+            switch (r->op) {
+            case 1: y = a + b; break;
+            case 5: y = a - b; break;
+            case 6: y = a * b; break;
+            default: y = a / b; break;
+            }
+            generic_write(r->dst, nd, i, y);
+        }
+        return ORACLE_OK;
+    }
+    case 3: case 32: case 70: { /* execute_generic_scalar (generic.rs:1515-1544) */
+        if (!(v0 && vd && c0 == cd && generic_param(r, 0, &pa) && isfinite(pa))) return ORACLE_INVALID_SHAPE;
+        for (uint64_t i = 0; i < c0; ++i) {
+            float x = generic_read(r->src0, n0, i);
+            float y = r->op == 3 ? x + pa : (r->op == 32 ? x * pa : (x < 0.0f ? x * pa : x));
+            generic_write(r->dst, nd, i, y);
+        }
+        return ORACLE_OK;
+    }
+    case 50: /* execute_generic_clamp (generic.rs:1546-1563): f32::clamp */
+        if (!(v0 && vd && c0 == cd && generic_param(r, 0, &pa) && generic_param(r, 1, &pb) && isfinite(pa) &&
+              isfinite(pb) && pa <= pb))
+            return ORACLE_INVALID_SHAPE;
+        for (uint64_t i = 0; i < c0; ++i) generic_write(r->dst, nd, i, clampf_rs(generic_read(r->src0, n0, i), pa, pb));
+        return ORACLE_OK;
+    case 22: /* execute_generic_silu_back (generic.rs:1565-1585) */
+        if (!(v0 && v1 && vd && same_ne(r->src0, r->src1) && same_ne(r->src0, r->dst))) return ORACLE_INVALID_SHAPE;
+        for (uint64_t i = 0; i < c0; ++i) {
+            float x = generic_read(r->src0, n0, i);
+            float sigmoid = 1.0f / (1.0f + expf(-x));
+            float derivative = sigmoid * (1.0f + x * (1.0f - sigmoid));
+            generic_write(r->dst, nd, i, generic_read(r->src1, n1, i) * derivative);
+        }
+        return ORACLE_OK;
+    case 19: { /* execute_generic_repeat (generic.rs:1641-1665) */
+        if (!(v0 && vd)) return ORACLE_INVALID_SHAPE;
+        for (int d = 0; d < 4; ++d)
+            if (r->dst->ne[d] % r->src0->ne[d] != 0) return ORACLE_INVALID_SHAPE;
+        for (uint64_t o = 0; o < cd; ++o) {
+            uint64_t rest = o, src_ordinal = 0, stride = 1;
+            for (int d = 0; d < 4; ++d) {
+                uint64_t coordinate = rest % r->dst->ne[d];
+                rest /= r->dst->ne[d];
+                src_ordinal += (coordinate % r->src0->ne[d]) * stride;
+                stride *= r->src0->ne[d];
+            }
+            uint32_t word; /* a raw copy */
+            memcpy(&word, (const unsigned char*)r->src0->data + ordinal_offset(r->src0, n0, src_ordinal), 4);
+            memcpy((unsigned char*)r->dst->data + ordinal_offset(r->dst, nd, o), &word, 4);
+        }
+        return ORACLE_OK;
+    }
+    case 13: case 16: { /* execute_generic_reduce_sum / _mean (generic.rs:1354-1392) */
+        if (!(v0 && vd && cd == 1)) return ORACLE_INVALID_SHAPE;
+        double sum = 0.0;
+        for (uint64_t i = 0; i < c0; ++i) sum += (double)generic_read(r->src0, n0, i);
+        generic_write(r->dst, nd, 0, r->op == 13 ? (float)sum : (float)(sum / (double)c0));
+        return ORACLE_OK;
+    }
+    case 17: { /* execute_generic_argmax (generic.rs:1394-1416) */
+        if (!(v0 && vd && cd == 1)) return ORACLE_INVALID_SHAPE;
+        uint64_t best_index = 0;
+        float best = generic_read(r->src0, n0, 0);
+        for (uint64_t i = 1; i < c0; ++i) {
+            float x = generic_read(r->src0, n0, i);
+            if (x > best) {
+                best = x;
+                best_index = i;
+            }
+        }
+        generic_write(r->dst, nd, 0, (float)best_index);
+        return ORACLE_OK;
+    }
+    case 46: { /* execute_generic_soft_max (generic.rs:1952-1989) */
+        if (!(v0 && vd && c0 == cd)) return ORACLE_INVALID_SHAPE;
+        uint64_t width = r->src0->ne[0], rows = c0 / width;
+        for (uint64_t row = 0; row < rows; ++row) {
+            float maximum = -INFINITY;
+            for (uint64_t c = 0; c < width; ++c) maximum = rs_max(maximum, generic_read(r->src0, n0, row * width + c));
+            float sum = 0.0f;
+            for (uint64_t c = 0; c < width; ++c) {
+                float e = expf(generic_read(r->src0, n0, row * width + c) - maximum);
+                generic_write(r->dst, nd, row * width + c, e);
+                sum += e;
+            }
+            for (uint64_t c = 0; c < width; ++c)
+                generic_write(r->dst, nd, row * width + c, generic_read(r->dst, nd, row * width + c) / sum);
+        }
+        return ORACLE_OK;
+    }
+    case 23: case 24: { /* execute_generic_norm (generic.rs:1992-2050) */
+        if (!(v0 && vd && same_ne(r->src0, r->dst) && generic_param(r, 0, &pa) && isfinite(pa) && pa >= 0.0f))
+            return ORACLE_INVALID_SHAPE;
+        const int rms = r->op == 24;
+        uint64_t width = r->src0->ne[0], rows = c0 / width;
+        for (uint64_t row = 0; row < rows; ++row) {
+            double sum = 0.0;
+            for (uint64_t c = 0; c < width; ++c) {
+                float x = generic_read(r->src0, n0, row * width + c);
+                sum += rms ? (double)(x * x) : (double)x;
+            }
+            float mean = (float)(sum / (double)width);
+            double variance = 0.0;
+            if (!rms) {
+                for (uint64_t c = 0; c < width; ++c) {
+                    float centered = generic_read(r->src0, n0, row * width + c) - mean;
+                    variance += (double)(centered * centered);
+                }
+                variance /= (double)width;
+            }
+            float scale = (float)(1.0 / sqrt((rms ? (double)mean : variance) + (double)pa));
+            for (uint64_t c = 0; c < width; ++c) {
+                float x = generic_read(r->src0, n0, row * width + c);
+                generic_write(r->dst, nd, row * width + c, rms ? x * scale : (x - mean) * scale);
+            }
+        }
+        return ORACLE_OK;
+    }
+    default:
+        return ORACLE_UNSUPPORTED_OPERATION;
+    }
+}

@@ -45,6 +45,8 @@ enum {
     ORACLE_SHAPE_MISMATCH = 2,
     ORACLE_INVALID_PARAMETERS = 3,
     ORACLE_UNEXPECTED_EVENT = 4,
+    ORACLE_INVALID_SHAPE = 6,
+    ORACLE_UNSUPPORTED_OPERATION = 7,
     ORACLE_INVALID_ARGUMENT = 18
 };
 
@@ -78,6 +80,24 @@ int oracle_sum_rows(const oracle_view* src, const oracle_view* dst);
 int oracle_argmax(const oracle_view* src, const oracle_view* dst);
 int oracle_argmax_index(const oracle_view* src, int64_t* index, float* value);
 int oracle_argmax_rows(const oracle_view* src, const oracle_view* dst);
+
+/* The generic operation envelope (generic.rs:580-766 GenericRequest, the
+ * maintained routes of sm.rs:324-425 restricted to the device table's
+ * elementwise / broadcast / reduction set; same layout as
+ * emel_cuda_generic_request).  Other operation codes return
+ * ORACLE_UNSUPPORTED_OPERATION, as the device table does. */
+typedef struct oracle_generic_request {
+    uint32_t op;
+    uint32_t unary_subop;
+    const oracle_view* src0;
+    const oracle_view* src1;
+    const oracle_view* src2;
+    const oracle_view* dst;
+    uint8_t params[64];
+    uint32_t params_len;
+    uint32_t reserved;
+} oracle_generic_request;
+int oracle_generic(const oracle_generic_request* request);
 
 /* Row-range variants used by the multi-threaded CPU baseline: identical
  * arithmetic, restricted to rows [row_begin, row_end) of a validated request

@@ -60,6 +60,29 @@ def build():
     subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
 
 
+class GenericRequest(ctypes.Structure):
+    """oracle_generic_request (same layout as emel_cuda_generic_request)."""
+    _fields_ = [("op", ctypes.c_uint32), ("unary_subop", ctypes.c_uint32),
+                ("src0", ctypes.POINTER(View)), ("src1", ctypes.POINTER(View)),
+                ("src2", ctypes.POINTER(View)), ("dst", ctypes.POINTER(View)),
+                ("params", ctypes.c_uint8 * 64), ("params_len", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
+
+
+def generic_request(op, src0=None, src1=None, src2=None, dst=None, params=b"", unary=0):
+    """An oracle_generic_request over host views (keeps them alive)."""
+    r = GenericRequest()
+    r.op = op
+    r.unary_subop = unary
+    r._keep = []
+    for name, v in (("src0", src0), ("src1", src1), ("src2", src2), ("dst", dst)):
+        if v is not None:
+            r._keep.append(v)
+            setattr(r, name, ctypes.pointer(v))
+    ctypes.memmove(r.params, bytes(params), len(params))
+    r.params_len = len(params)
+    return r
+
+
 def load(cr=False):
     """The oracle with the host's glibc float libm (default), or with
     correctly rounded libm calls (cr=True)."""
@@ -94,6 +117,7 @@ def load(cr=False):
         "oracle_argmax": [P, P],
         "oracle_argmax_index": [P, ctypes.POINTER(ctypes.c_int64), ctypes.POINTER(ctypes.c_float)],
         "oracle_argmax_rows": [P, P],
+        "oracle_generic": [ctypes.POINTER(GenericRequest)],
     }
     for name, args in sigs.items():
         fn = getattr(lib, name)
