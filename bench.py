@@ -9,6 +9,7 @@ every input element read once, every output element written once).
     python bench.py [--gpus N --steps K --warmup W]       # B200 device table
     python bench.py --impl reference ...                   # CPU reference lane
     python bench.py --suite                                # per-op lines, all configs
+    python bench.py --workload cfg5 [--gpus N]             # config 5 sharded, strong scaling
 
 Multi-GPU (torchrun, one process per GPU): every rank runs the same
 per-GPU workload on its own seeded data (weak scaling, no collective on the
@@ -590,6 +591,129 @@ def run_suite(args):
 
 
 # ---------------------------------------------------------------------------
+# Configuration 5 sharded over the GPUs (strong scaling)
+# ---------------------------------------------------------------------------
+def run_cfg5(args, world, rank, local):
+    """The 1.07 GB permuted tensor of configuration 5 split along dim 3
+    across the ranks (total work fixed: strong scaling).  One step = repeat
+    mul and repeat add with the replicated src1, then the whole-tensor sum
+    and argmax as per-shard partials all-gathered over NCCL (the only
+    communication) and combined in rank order on every rank."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    pkg = load_package()
+    from emel_rs_b200 import distributed as D
+    from emel_rs_b200 import workloads as W
+
+    lib = pkg.lib()
+    ctx = pkg.Context(local)
+    stream = pkg.Stream(ctx)
+    sh = stream.handle
+    b, e = D.shard_bounds(W.CFG5_NE[3], world, rank)
+    parts = []
+    s1 = None
+    for j in range(b, e):
+        s0, s1 = W.cfg5(ne3=1, shard=j)
+        parts.append(torch.from_numpy(s0))
+    src0 = torch.cat(parts).to(device) if parts else torch.empty(0, device=device)
+    src1 = torch.from_numpy(s1).to(device)
+    ne, nb = W.cfg5_src0_view(ne3=e - b)
+    mul_out = torch.empty_like(src0)
+    add_out = torch.empty_like(src0)
+    acc = torch.empty(1, dtype=torch.float64, device=device)
+    part = torch.empty(24, dtype=torch.uint8, device=device)
+    gathered_sum = torch.empty(world, dtype=torch.float64, device=device)
+    gathered_part = torch.empty(world * 24, dtype=torch.uint8, device=device)
+    torch.cuda.synchronize()
+
+    def view(t, vne, vnb=None):
+        v = pkg.CView()
+        v.data = t.data_ptr()
+        v.storage_bytes = t.numel() * t.element_size()
+        vnb = vnb or pkg.contiguous_nb(vne)
+        for d in range(4):
+            v.ne[d], v.nb[d] = vne[d], vnb[d]
+        v.dtype = 0
+        return v
+
+    v0, v1 = view(src0, ne, nb), view(src1, [128, 1, 8192, 1])
+    vm, va = view(mul_out, ne), view(add_out, ne)
+    B = ctypes.byref
+    plane = ne[0] * ne[1] * ne[2]
+    raw = sh.value if isinstance(sh, ctypes.c_void_p) else sh
+    torch_stream = torch.cuda.ExternalStream(int(raw or 0), device=device)
+
+    def step():
+        for st in (lib.emel_cuda_binary_repeat(ctx.handle, sh, 2, B(v0), B(v1), B(vm)),
+                   lib.emel_cuda_binary_repeat(ctx.handle, sh, 0, B(v0), B(v1), B(va)),
+                   lib.emel_cuda_sum_f64(ctx.handle, sh, B(v0), ctypes.c_void_p(acc.data_ptr())),
+                   lib.emel_cuda_argmax_partial_compute(ctx.handle, sh, B(v0), b * plane,
+                                                        ctypes.c_void_p(part.data_ptr()))):
+            if st != 0:
+                raise RuntimeError(ctx.last_error)
+        if world > 1:
+            with torch.cuda.stream(torch_stream):
+                dist.all_gather_into_tensor(gathered_sum, acc)
+                dist.all_gather_into_tensor(gathered_part, part)
+
+    for _ in range(args.warmup):
+        step()
+    stream.synchronize()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    t0, t1 = pkg.CudaEvent(ctx), pkg.CudaEvent(ctx)
+    stream.synchronize()
+    with ClockSampler(local) as clocks:
+        t0.record(sh)
+        for _ in range(args.steps):
+            step()
+        t1.record(sh)
+        stream.synchronize()
+        torch.cuda.synchronize()
+    ms = t0.elapsed_ms(t1) / args.steps
+    if world > 1:
+        t = torch.tensor([ms], dtype=torch.float64, device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    # combined answers (rank order) from the last step
+    if world > 1:
+        sums = gathered_sum.cpu().tolist()
+        raw = gathered_part.cpu().numpy().tobytes()
+        partials = [D.unpack_partial(raw[24 * k:24 * (k + 1)]) for k in range(world)]
+    else:
+        sums = [float(acc.cpu().item())]
+        partials = [D.read_partial(pkg, ctx, part.data_ptr())]
+    total32, _ = D.combine_sum(sums)
+    index, _ = D.combine_argmax(pkg, partials)
+    n = 128 * 32 * 8192 * 8
+    step_bytes = 2 * (2 * n * 4 + 128 * 8192 * 4) + 2 * n * 4
+    if rank == 0:
+        value = step_bytes / (ms / 1e3) / 1e9
+        print(json.dumps({
+            "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded per dim-3 slice)",
+            "config": {"workload": "cfg5 sharded: src0 [128,32,8192,8] (dims 1/2 swapped view) split along dim 3; "
+                                   "repeat mul + repeat add with replicated src1 [128,1,8192,1], whole sum and "
+                                   "argmax as per-shard partials + NCCL all-gather",
+                       "bytes_per_step": step_bytes, "l2": "inputs 1.07 GB / N per GPU, larger than L2 up to N=8",
+                       "parallelism": f"dim-3 shards over {world} GPU(s)"},
+            "result": {"sum": float(total32), "argmax": int(index)},
+            "clocks": clocks.summary(),
+        }), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ---------------------------------------------------------------------------
 # CPU lanes (the oracle: C restatement of the reference loops)
 # ---------------------------------------------------------------------------
 def cpu_workload():
@@ -713,6 +837,9 @@ def main():
     ap.add_argument("--only", default="", help="comma list of ops to run, e.g. gelu_f32,relu_f16 (profiling; with --suite: suite op names)")
     ap.add_argument("--branches", type=int, default=4, help="parallel graph branches for the 16 independent ops")
     ap.add_argument("--suite", action="store_true", help="per-op lines for every configuration (1 GPU)")
+    ap.add_argument("--workload", choices=["cfg2", "cfg5"], default="cfg2",
+                    help="cfg2: the default 16-op unary sweep (weak scaling); cfg5: the sharded 4-D "
+                         "broadcast + whole-tensor reductions (strong scaling)")
     args = ap.parse_args()
     world, rank, local = dist_env()
     if args.warmup < 3:
@@ -722,6 +849,9 @@ def main():
         return
     if args.suite:
         run_suite(args)
+        return
+    if args.workload == "cfg5":
+        run_cfg5(args, world, rank, local)
         return
     run_b200(args, world, rank, local)
 
