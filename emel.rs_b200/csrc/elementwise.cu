@@ -250,6 +250,53 @@ __global__ void __launch_bounds__(kThreads) ew_rows_vec(EwPlan p, F f, RowsWalk 
     }
 }
 
+// A dense tensor with one broadcast row (the row-broadcast event,
+// broadcast.rs:352-390: src1 ne == [ne0, 1, 1, 1]): vector i of dst and src0
+// is i, and src1's vector is i modulo the row's vector count -- one
+// magic-number division per vector instead of the row walk's four.
+template <typename T, typename F>
+__global__ void __launch_bounds__(kThreads) ew_row_broadcast(EwPlan p, F f, FastDiv dv, uint32_t nvec) {
+    pdl_enter();
+    constexpr int N = Vec16<T>::N;
+    constexpr int U = 4;
+    const T* a = reinterpret_cast<const T*>(p.src0.ptr);
+    const T* b = reinterpret_cast<const T*>(p.src1.ptr);
+    T* d = reinterpret_cast<T*>(p.dst.ptr);
+    const uint32_t stride = gridDim.x * blockDim.x;
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += U * stride) {
+        Vec16<T> av[U], bv[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const uint32_t v = i + k * stride;
+            if (v >= nvec) continue;
+            av[k] = ld_stream(a + (size_t)v * N);
+            bv[k] = ld_keep(b + (size_t)(v - fdiv(v, dv) * dv.d) * N);
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const uint32_t v = i + k * stride;
+            if (v < nvec) st_stream(d + (size_t)v * N, apply_vec<T>(f, av[k], bv[k]));
+        }
+    }
+}
+
+// dst and src0 dense (rows of ne0 back to back), src1 a single contiguous row.
+bool dense_row_broadcast(const EwPlan& p) {
+    if (!p.vec || !p.src1_bcast || p.src1.st[0] != 1) return false;
+    if (p.src1.ne[1] != 1 || p.src1.ne[2] != 1 || p.src1.ne[3] != 1 || p.src1.ne[0] != p.ne[0]) return false;
+    const uint64_t N = p.dtype == DType::F16 ? 8 : 4;
+    if (p.ne[0] % N != 0 || p.count / N >= (1ull << 31) || p.ne[0] / N >= (1ull << 31)) return false;
+    const Operand* ops[2] = {&p.dst, &p.src0};
+    for (const Operand* o : ops) {
+        int64_t expect = 1;
+        for (int d = 0; d < 4; ++d) {
+            if (p.ne[d] > 1 && o->st[d] != expect) return false;
+            expect *= (int64_t)p.ne[d];
+        }
+    }
+    return true;
+}
+
 bool rows_walk(const EwPlan& p, RowsWalk* w) {
     const uint64_t N = p.dtype == DType::F16 ? 8 : 4;
     const uint64_t nvec = p.count / N;
@@ -391,6 +438,16 @@ cudaError_t launch_ew(const LaunchEnv& env, const EwPlan& p, const F& f) {
         break;
     }
     case EwKind::Rows: {
+        if constexpr (F::kBinary) {
+            if (dense_row_broadcast(p)) {
+                const uint32_t n = (uint32_t)(p.count / Vec16<T>::N);
+                const cudaError_t err = launch_dependent(
+                    ew_row_broadcast<T, F>, dim3(grid_for(env, n, 4)), dim3(kThreads), 0, env.stream, p, f,
+                    make_fastdiv((uint32_t)(p.ne[0] / Vec16<T>::N)), n);
+                if (err != cudaSuccess) return err;
+                break;
+            }
+        }
         RowsWalk w;
         if (rows_walk(p, &w)) {
             const cudaError_t err =

@@ -16,7 +16,7 @@ namespace emel {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kCtasPerSm = 4;
+constexpr int kCtasPerSm = 8;  // 2048 threads per SM, four 16-byte loads each in flight
 
 struct ArgPart {
     float v;
@@ -369,7 +369,7 @@ emel_cuda_status check_scalar_sum(const emel_tensor_view* src, const emel_tensor
 
 namespace {
 
-constexpr int kNoAllocMaxPartials = 2048;  // one per CTA: 4 CTAs per SM up to 512 SMs
+constexpr int kNoAllocMaxPartials = 2048;  // one per CTA: 8 CTAs per SM up to 256 SMs
 constexpr int kNoAllocMaxDevices = 64;
 constexpr size_t kNoAllocHeader = 256;     // ticket, padded to the partials' alignment
 
