@@ -500,7 +500,7 @@ template <int OP>
 constexpr bool kTableOp = (kHeavyFormula<OP> || OP == kSqrt || OP == kLog || OP == kSin || OP == kCos) && OP < 128;
 
 constexpr uint64_t kTableMinCount = 1ull << 20;  // below this the table costs more than it saves
-constexpr int kTableThreads = 640;  // leaves registers for two build CTAs per SM
+constexpr int kTableThreads = 1024;  // one stream CTA fills an SM; every build CTA is resident before it is scheduled
 constexpr uint32_t kTableBytes = 65536u * 2u;
 
 // griddepcontrol: the table build lets the stream kernel be scheduled as
@@ -587,7 +587,7 @@ __global__ void __launch_bounds__(kTableThreads, 1) table_stream(typename K::Ele
     extern __shared__ __align__(128) uint16_t tab[];
     __shared__ __align__(8) uint64_t bar;
     constexpr int L = K::kLanes;
-    constexpr int U = 4;
+    constexpr int U = 8;  // 8 vectors per thread in flight: 128 KB of loads per SM
     const uint64_t nvec = n / L;
     const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
     const uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
