@@ -110,6 +110,30 @@ struct UnaryParams {
 __device__ __forceinline__ float lm_exp(float x) { return x86_nan1(fast_expf(x), x); }
 __device__ __forceinline__ float lm_expm1(float x) { return x86_nan1(fast_expm1f(x), x); }
 __device__ __forceinline__ float lm_tanh(float x) { return x86_nan1(fast_tanhf(x), x); }
+// exp(z) for the fast soft_max passes (z <= 0, or NaN): branch-free.  The
+// argument is clamped into the core's range, the core is evaluated, and
+// z < -104 (a binary32 result of +0) is selected afterwards; a NaN z passes
+// both comparisons and gives NaN.
+__device__ __forceinline__ float softmax_exp(float z) {
+    const float zc = z < -104.0f ? -104.0f : z;
+    const float r = (float)exp_core((double)zc);
+    return z < -104.0f ? 0.0f : r;
+}
+
+// e / d rounded once for 0 <= e <= 1 and a finite d >= 1, given
+// inv = RN(1 / d): q0 = RN(e * inv) is within one ulp of e / d, the FMA
+// residual e - d * q0 is exact, and RN(q0 + residual * inv) is the
+// correctly rounded quotient (Markstein's theorem on reciprocal-based
+// division).  e = 0 gives +0 through the same steps; 0 < e < 2^-60, whose
+// quotient could leave the normal range, uses the divider.
+__device__ __forceinline__ float softmax_div(float e, float d, float inv) {
+    const float q0 = __fmul_rn(e, inv);
+    const float res = __fmaf_rn(-d, q0, e);
+    const float q = __fmaf_rn(res, inv, q0);
+    if (e < 0x1p-60f && e != 0.0f) return __fdiv_rn(e, d);
+    return q;
+}
+
 __device__ __forceinline__ float lm_log(float x) { return x86_nan1((float)log((double)x), x); }
 __device__ __forceinline__ float lm_log1p(float x) { return x86_nan1((float)log1p((double)x), x); }
 __device__ __forceinline__ float lm_sin(float x) { return x86_nan1((float)sin((double)x), x); }

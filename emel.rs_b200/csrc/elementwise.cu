@@ -32,7 +32,7 @@ struct UnaryFn {
     UnaryParams p;
     static constexpr bool kBinary = false;
     static constexpr int kUnroll = kHeavyFormula<OP> ? 2 : 4;  // arithmetic-bound ops need fewer loads in flight
-    static constexpr int kMinBlocks = kHeavyFormula<OP> ? 6 : 8;  // register cap keeping 6 or 8 CTAs per SM
+    static constexpr int kMinBlocks = 4;  // 64 registers: a tighter cap spills the vectors in flight
     __device__ __forceinline__ float operator()(float a, float) const { return unary_apply<OP, IN_F16>(a, p); }
 };
 
@@ -40,7 +40,7 @@ template <int OP>
 struct BinaryFn {
     static constexpr bool kBinary = true;
     static constexpr int kUnroll = 4;
-    static constexpr int kMinBlocks = 8;
+    static constexpr int kMinBlocks = 3;  // two operands of four vectors each: 85 registers
     __device__ __forceinline__ float operator()(float a, float b) const { return binary_apply<OP>(a, b); }
 };
 
@@ -48,7 +48,7 @@ struct BinaryFn {
 struct SiluBackFn {
     static constexpr bool kBinary = true;
     static constexpr int kUnroll = 2;
-    static constexpr int kMinBlocks = 6;
+    static constexpr int kMinBlocks = 4;
     __device__ __forceinline__ float operator()(float x, float grad) const {
         const float sigmoid = f_div(1.0f, f_add(1.0f, lm_exp(f_neg(x))));
         const float derivative = f_mul(sigmoid, f_add(1.0f, f_mul(x, f_sub(1.0f, sigmoid))));

@@ -160,25 +160,43 @@ __device__ __forceinline__ float4 scaled4_fast(const RingArgs& a, const float* r
     return make_float4(__fadd_rn(x.x, mk.x), __fadd_rn(x.y, mk.y), __fadd_rn(x.z, mk.z), __fadd_rn(x.w, mk.w));
 }
 
-// exp of a non-NaN z <= 0 (fast_expf without its overflow branch).
-__device__ __forceinline__ float exp_nonpositive(float z) { return z < -104.0f ? 0.0f : (float)exp_core((double)z); }
-
-// e / d rounded once, for 0 <= e <= 1 and a finite d >= 1, given
-// inv = RN(1 / d): q0 = RN(e * inv) is within one ulp of e / d, the FMA
-// residual e - d * q0 is exact, and RN(q0 + residual * inv) is the
-// correctly rounded quotient (Markstein's theorem on reciprocal-based
-// division).  Quotients that could leave the normal range use the divider.
-__device__ __forceinline__ float div_by(float e, float d, float inv) {
-    if (e >= 0x1p-60f) {
-        const float q0 = __fmul_rn(e, inv);
-        const float res = __fmaf_rn(-d, q0, e);
-        return __fmaf_rn(res, inv, q0);
-    }
-    return __fdiv_rn(e, d);
+// Reductions for the register-resident soft_max rows.  They skip the
+// leading barrier of group_max / group_sum: each uses its own scratch array
+// and, between two uses of the same array, every thread passes the other
+// reduction's barrier and the next row's stage wait, so no reader of the
+// previous value is left.  fmaxf skips NaN; the sign of a zero maximum does
+// not change any exp(v - max).
+template <int T>
+__device__ __forceinline__ float row_max_fast(float v, GroupScratch<T>* s) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    const int lane = threadIdx.x & 31, warp = threadIdx.x / 32;
+    if (lane == 0) s->f[warp] = v;
+    __syncthreads();
+    v = s->f[0];
+#pragma unroll
+    for (int w = 1; w < T / 32; ++w) v = fmaxf(v, s->f[w]);
+    return v;
 }
 
-template <int OP, int T>
-__global__ void __launch_bounds__(T, 1024 / T) row_ring(RingArgs a) {
+template <int T>
+__device__ __forceinline__ double row_sum_fast(double v, GroupScratch<T>* s) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    const int lane = threadIdx.x & 31, warp = threadIdx.x / 32;
+    if (lane == 0) s->d[warp] = v;
+    __syncthreads();
+    v = 0.0;
+#pragma unroll
+    for (int w = 0; w < T / 32; ++w) v += s->d[w];
+    return v;
+}
+
+// R > 0 (soft_max only): each thread keeps its R vectors of the row in
+// registers (rows of at most 4 * T * R elements); R == 0 loops over the
+// staged row for every pass.
+template <int OP, int T, int R>
+__global__ void __launch_bounds__(T, R >= 8 ? 2 : (R >= 4 ? 3 : 1024 / T)) row_ring(RingArgs a) {
     extern __shared__ __align__(128) unsigned char ring_smem[];
     __shared__ __align__(8) uint64_t full[kRingStagesMax];
     __shared__ GroupScratch<T> red;
@@ -304,20 +322,74 @@ __global__ void __launch_bounds__(T, 1024 / T) row_ring(RingArgs a) {
             // bits.  A NaN lane reports +inf to the max reduction; a row
             // whose maximum comes back non-finite is redone exactly below.
             const int64_t moff = a.aux_mode == kAuxMaskLoads ? mask_offset(r, a) : 0;
-            float m = bitsf(0x7fc00000u);  // NaN = "no value yet" (fmaxf skips it)
-            bool odd = false;
-            for (uint32_t v = tid; v < nvec; v += T) {
-                const float4 s = scaled4_fast(a, row, stage, moff, v);
-                odd = odd || is_nan(s.x) || is_nan(s.y) || is_nan(s.z) || is_nan(s.w);
-                m = fmaxf(fmaxf(m, s.x), fmaxf(s.y, fmaxf(s.z, s.w)));
+            if constexpr (R > 0) {
+                // Register-resident fast pass: the row is read from the stage
+                // once.  No NaN check is needed while reading: a NaN v, or a
+                // maximum of +-inf (inf - inf, -inf - -inf), makes some
+                // v - max NaN, its exp NaN and the f64 sum NaN, while
+                // otherwise every exp is at most 1 and the sum is finite.  A
+                // row whose sum comes back non-finite is redone exactly
+                // below from the untouched stage.
+                float4 sv[R];
+                float m = -INFINITY;
+#pragma unroll
+                for (int i = 0; i < R; ++i) {
+                    const uint32_t v = tid + (uint32_t)(i * T);
+                    if (v < nvec) {
+                        sv[i] = scaled4_fast(a, row, stage, moff, v);
+                        m = fmaxf(m, fmaxf(fmaxf(sv[i].x, sv[i].y), fmaxf(sv[i].z, sv[i].w)));
+                    }
+                }
+                m = row_max_fast<T>(m, &red);
+                double acc = 0.0;
+#pragma unroll
+                for (int i = 0; i < R; ++i) {
+                    const uint32_t v = tid + (uint32_t)(i * T);
+                    if (v < nvec) {
+                        sv[i] = make_float4(softmax_exp(__fsub_rn(sv[i].x, m)), softmax_exp(__fsub_rn(sv[i].y, m)),
+                                            softmax_exp(__fsub_rn(sv[i].z, m)), softmax_exp(__fsub_rn(sv[i].w, m)));
+                        acc += (double)sv[i].x;
+                        acc += (double)sv[i].y;
+                        acc += (double)sv[i].z;
+                        acc += (double)sv[i].w;
+                    }
+                }
+                acc = row_sum_fast<T>(acc, &red);
+                if (isfinite(acc)) {
+                    // every thread has finished reading the stage: refill it now
+                    if (tid == 0 && k + (uint32_t)S < mine) {
+                        asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                        issue(k + (uint32_t)S);
+                    }
+                    const float denom = __double2float_rn(acc);  // >= 1: the maximum contributes exp(0)
+                    const float inv = __frcp_rn(denom);
+#pragma unroll
+                    for (int i = 0; i < R; ++i) {
+                        const uint32_t v = tid + (uint32_t)(i * T);
+                        if (v < nvec)
+                            store4<OP>(a, drow, v,
+                                       make_float4(softmax_div(sv[i].x, denom, inv), softmax_div(sv[i].y, denom, inv),
+                                                   softmax_div(sv[i].z, denom, inv), softmax_div(sv[i].w, denom, inv)));
+                    }
+                    continue;
+                }
             }
-            m = group_max<T>(odd ? INFINITY : m, &red);
-            if (isfinite(m)) {
+            float m = bitsf(0x7fc00000u);  // NaN = "no value yet" (fmaxf skips it)
+            if constexpr (R == 0) {
+                bool odd = false;
+                for (uint32_t v = tid; v < nvec; v += T) {
+                    const float4 s = scaled4_fast(a, row, stage, moff, v);
+                    odd = odd || is_nan(s.x) || is_nan(s.y) || is_nan(s.z) || is_nan(s.w);
+                    m = fmaxf(fmaxf(m, s.x), fmaxf(s.y, fmaxf(s.z, s.w)));
+                }
+                m = group_max<T>(odd ? INFINITY : m, &red);
+            }
+            if (R == 0 && isfinite(m)) {
                 double acc = 0.0;
                 for (uint32_t v = tid; v < nvec; v += T) {
                     const float4 s = scaled4_fast(a, row, stage, moff, v);
-                    const float4 e = make_float4(exp_nonpositive(__fsub_rn(s.x, m)), exp_nonpositive(__fsub_rn(s.y, m)),
-                                                 exp_nonpositive(__fsub_rn(s.z, m)), exp_nonpositive(__fsub_rn(s.w, m)));
+                    const float4 e = make_float4(softmax_exp(__fsub_rn(s.x, m)), softmax_exp(__fsub_rn(s.y, m)),
+                                                 softmax_exp(__fsub_rn(s.z, m)), softmax_exp(__fsub_rn(s.w, m)));
                     reinterpret_cast<float4*>(row)[v] = e;
                     acc += (double)e.x;
                     acc += (double)e.y;
@@ -330,8 +402,8 @@ __global__ void __launch_bounds__(T, 1024 / T) row_ring(RingArgs a) {
                 for (uint32_t v = tid; v < nvec; v += T) {
                     const float4 e = ld_f4(row + 4 * v);
                     store4<OP>(a, drow, v,
-                               make_float4(div_by(e.x, denom, inv), div_by(e.y, denom, inv), div_by(e.z, denom, inv),
-                                           div_by(e.w, denom, inv)));
+                               make_float4(softmax_div(e.x, denom, inv), softmax_div(e.y, denom, inv), softmax_div(e.z, denom, inv),
+                                           softmax_div(e.w, denom, inv)));
                 }
             } else {
                 m = bitsf(0x7fc00000u);
@@ -391,13 +463,13 @@ bool fits_u32(uint64_t v) { return v > 0 && v <= 0xffffffffull; }
 // allow (each CTA's row passes are a chain of dependent steps and barriers,
 // so throughput comes from several rows in progress per SM); then deeper
 // rings (up to kRingStagesMax) while shared memory lasts.
-template <int OP, int T>
+template <int OP, int T, int R = 0>
 cudaError_t launch_ring_kernel(const LaunchEnv& env, RingArgs a, uint64_t rows, bool* launched) {
     static int configured_device_mask = 0;  // bit per device with the attribute set
     const int bit = env.device < 31 ? (1 << env.device) : 0;
     if (!(configured_device_mask & bit)) {
         const cudaError_t err =
-            cudaFuncSetAttribute(row_ring<OP, T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRingSmemPerSm);
+            cudaFuncSetAttribute(row_ring<OP, T, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRingSmemPerSm);
         if (err != cudaSuccess) return err;
         configured_device_mask |= bit;
     }
@@ -405,7 +477,7 @@ cudaError_t launch_ring_kernel(const LaunchEnv& env, RingArgs a, uint64_t rows, 
     const uint32_t two = a.weight_bytes + 2 * a.stage_bytes;
     if (two > kRingSmemPerSm) return cudaSuccess;
     int ctas = 0;
-    cudaError_t err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctas, row_ring<OP, T>, T, two);
+    cudaError_t err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctas, row_ring<OP, T, R>, T, two);
     if (err != cudaSuccess) return err;
     if (ctas < 1) return cudaSuccess;
     if (ctas > 8) ctas = 8;
@@ -420,7 +492,7 @@ cudaError_t launch_ring_kernel(const LaunchEnv& env, RingArgs a, uint64_t rows, 
     const uint32_t smem = a.weight_bytes + (uint32_t)a.stages * a.stage_bytes;
     const uint64_t cap = (uint64_t)env.sm_count * ctas;
     const uint32_t grid = (uint32_t)(rows < cap ? rows : cap);
-    err = launch_dependent(row_ring<OP, T>, dim3(grid), dim3(T), smem, env.stream, a);
+    err = launch_dependent(row_ring<OP, T, R>, dim3(grid), dim3(T), smem, env.stream, a);
     *launched = true;
     return err != cudaSuccess ? err : cudaGetLastError();
 }
@@ -489,7 +561,16 @@ bool launch_row_ring(const LaunchEnv& env, const RowPlan& p, int op, float param
     case 0: e = launch_ring_kernel<kRingNorm, kRingThreads>(env, a, p.rows, &launched); break;
     case 1: e = launch_ring_kernel<kRingRms, kRingThreads>(env, a, p.rows, &launched); break;
     case 2: e = launch_ring_kernel<kRingRmsMul, kRingThreads>(env, a, p.rows, &launched); break;
-    case 3: e = launch_ring_kernel<kRingSoftMax, kRingThreads>(env, a, p.rows, &launched); break;
+    case 3: {
+        // vectors per thread, rounded up to a power of two, up to 8
+        const uint64_t per = (ne0 / 4 + kRingThreads - 1) / kRingThreads;
+        if (per <= 1) e = launch_ring_kernel<kRingSoftMax, kRingThreads, 1>(env, a, p.rows, &launched);
+        else if (per <= 2) e = launch_ring_kernel<kRingSoftMax, kRingThreads, 2>(env, a, p.rows, &launched);
+        else if (per <= 4) e = launch_ring_kernel<kRingSoftMax, kRingThreads, 4>(env, a, p.rows, &launched);
+        else if (per <= 8) e = launch_ring_kernel<kRingSoftMax, kRingThreads, 8>(env, a, p.rows, &launched);
+        else e = launch_ring_kernel<kRingSoftMax, kRingThreads>(env, a, p.rows, &launched);
+        break;
+    }
     case 4: e = launch_ring_kernel<kRingNormGeneric, kRingThreads>(env, a, p.rows, &launched); break;
     default: e = launch_ring_kernel<kRingRmsGeneric, kRingThreads>(env, a, p.rows, &launched); break;
     }

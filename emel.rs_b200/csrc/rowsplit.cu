@@ -194,20 +194,6 @@ __device__ __forceinline__ float value_at(const RowPlan& p, const SoftmaxRow& w,
     return v;
 }
 
-__device__ __forceinline__ float exp_nonpositive_split(float z) {
-    return z < -104.0f ? 0.0f : (float)exp_core((double)z);
-}
-
-// See rowring.cu: correctly rounded e / d for 0 <= e <= 1, finite d >= 1.
-__device__ __forceinline__ float div_by_split(float e, float d, float inv) {
-    if (e >= 0x1p-60f) {
-        const float q0 = __fmul_rn(e, inv);
-        const float res = __fmaf_rn(-d, q0, e);
-        return __fmaf_rn(res, inv, q0);
-    }
-    return __fdiv_rn(e, d);
-}
-
 __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitThreads)
     softmax_rows_split(RowPlan p, bool apply_scale, float scale, uint64_t chunk) {
     pdl_enter();
@@ -265,8 +251,8 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitTh
                        [&](uint64_t v, float4 raw) {
                            const float4 q = scale4(raw);
                            const float4 e = make_float4(
-                               exp_nonpositive_split(__fsub_rn(q.x, gm)), exp_nonpositive_split(__fsub_rn(q.y, gm)),
-                               exp_nonpositive_split(__fsub_rn(q.z, gm)), exp_nonpositive_split(__fsub_rn(q.w, gm)));
+                               softmax_exp(__fsub_rn(q.x, gm)), softmax_exp(__fsub_rn(q.y, gm)),
+                               softmax_exp(__fsub_rn(q.z, gm)), softmax_exp(__fsub_rn(q.w, gm)));
                            y4[v] = e;
                            acc += (double)e.x;
                            acc += (double)e.y;
@@ -275,7 +261,7 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitTh
                        });
         } else {
             for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kSplitThreads) {
-                const float e = exp_nonpositive_split(__fsub_rn(value_at<false>(p, w, c, apply_scale, scale), gm));
+                const float e = softmax_exp(__fsub_rn(value_at<false>(p, w, c, apply_scale, scale), gm));
                 w.y[(int64_t)c * w.ys] = e;
                 acc += (double)e;
             }
@@ -311,13 +297,13 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitTh
         if (vec) {
             batched<8>(ch.col0 / 4, ch.col1 / 4, [&](uint64_t v) { return y4[v]; },
                        [&](uint64_t v, float4 e) {
-                           __stcs(y4 + v, make_float4(div_by_split(e.x, denom, inv), div_by_split(e.y, denom, inv),
-                                                      div_by_split(e.z, denom, inv), div_by_split(e.w, denom, inv)));
+                           __stcs(y4 + v, make_float4(softmax_div(e.x, denom, inv), softmax_div(e.y, denom, inv),
+                                                      softmax_div(e.z, denom, inv), softmax_div(e.w, denom, inv)));
                        });
         } else {
             for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kSplitThreads) {
                 float* o = w.y + (int64_t)c * w.ys;
-                *o = div_by_split(*o, denom, inv);
+                *o = softmax_div(*o, denom, inv);
             }
         }
     } else {

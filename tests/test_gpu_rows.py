@@ -331,13 +331,17 @@ def test_ring_softmax_ext_masks(emel, kern, oracle_lib, mask_kind):
     close(got, want, 1e-30, f"ring softmax {mask_kind}")
 
 
-def test_ring_softmax_special_rows_take_the_exact_pass(emel, kern, oracle_lib):
-    """Rows of 2048 with NaN (first element, middle), +inf, all -inf and a NaN
-    in the mask: the fast pass hands these rows to the exact one, whose NaN
-    payloads follow the reference; ordinary rows alongside stay exact too."""
+@pytest.mark.parametrize("kv", [2048, 6000, 20000])
+def test_ring_softmax_special_rows_take_the_exact_pass(emel, kern, oracle_lib, kv):
+    """Rows with NaN (first element, middle), +inf, all -inf and a NaN in the
+    mask: the fast pass hands these rows to the exact one, whose NaN payloads
+    follow the reference; ordinary rows alongside stay exact too, including
+    exps far below 2^-60 (subnormal quotients).  Widths 2048 and 6000 keep
+    the row in registers (6000: a partial last vector slot), 20000 loops."""
     rng = np.random.default_rng(45)
-    kv, q = 2048, 8
+    q = 8
     x = (rng.standard_normal(kv * q) * 3).astype(np.float32).reshape(q, kv)
+    x[0, 10:30] = np.linspace(-110.0, -40.0, 20, dtype=np.float32)
     x[1, 0] = np.uint32(0x7fa00001).view(np.float32)  # signalling NaN first
     x[2, 700] = np.nan
     x[3, 5] = np.inf
