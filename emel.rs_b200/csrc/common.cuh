@@ -125,14 +125,22 @@ __device__ __forceinline__ float softmax_exp(float z) {
 // residual e - d * q0 is exact, and RN(q0 + residual * inv) is the
 // correctly rounded quotient (Markstein's theorem on reciprocal-based
 // division).  e = 0 gives +0 through the same steps; 0 < e < 2^-60, whose
-// quotient could leave the normal range, uses the divider.
-__device__ __forceinline__ float softmax_div(float e, float d, float inv) {
+// quotient could leave the normal range, uses the divider (softmax_div).
+__device__ __forceinline__ float markstein_div(float e, float d, float inv) {
     const float q0 = __fmul_rn(e, inv);
-    const float res = __fmaf_rn(-d, q0, e);
-    const float q = __fmaf_rn(res, inv, q0);
+    return __fmaf_rn(__fmaf_rn(-d, q0, e), inv, q0);
+}
+
+__device__ __forceinline__ float softmax_div(float e, float d, float inv) {
+    const float q = markstein_div(e, d, inv);
     if (e < 0x1p-60f && e != 0.0f) return __fdiv_rn(e, d);
     return q;
 }
+
+// While every v - max of a soft_max row is >= kSoftmaxPlainDivFloor, each
+// e is at least e^-41 > 2^-60 (or exactly 1), so markstein_div needs no
+// range check.
+constexpr float kSoftmaxPlainDivFloor = -41.0f;
 
 __device__ __forceinline__ float lm_log(float x) { return x86_nan1((float)log((double)x), x); }
 __device__ __forceinline__ float lm_log1p(float x) { return x86_nan1((float)log1p((double)x), x); }

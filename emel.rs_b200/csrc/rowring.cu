@@ -192,10 +192,100 @@ __device__ __forceinline__ double row_sum_fast(double v, GroupScratch<T>* s) {
     return v;
 }
 
+// soft_max operand modes of the register-resident pass (compile-time, so
+// the per-vector work has no mode branches): v = x; v = x * scale; and
+// v = x * scale + mask with the mask row staged as f16 or f32, or read with
+// loads (any strides).
+enum SmMode { kSmPlain = 0, kSmScale = 1, kSmMaskF16 = 2, kSmMaskF32 = 3, kSmMaskLoads = 4 };
+
+template <int MODE>
+__device__ __forceinline__ float4 sm_operand4(const RingArgs& a, const float* row, const unsigned char* stage,
+                                              int64_t moff, uint32_t v) {
+    float4 x = ld_f4(row + 4 * v);
+    if constexpr (MODE == kSmPlain) return x;
+    x = make_float4(__fmul_rn(x.x, a.param), __fmul_rn(x.y, a.param), __fmul_rn(x.z, a.param), __fmul_rn(x.w, a.param));
+    if constexpr (MODE == kSmScale) return x;
+    float4 mk;
+    if constexpr (MODE == kSmMaskF16) {
+        const uint2 h = reinterpret_cast<const uint2*>(stage + a.mask_offset)[v];
+        const float2 lo = __half22float2(*reinterpret_cast<const __half2*>(&h.x));
+        const float2 hi = __half22float2(*reinterpret_cast<const __half2*>(&h.y));
+        mk = make_float4(lo.x, lo.y, hi.x, hi.y);
+    } else if constexpr (MODE == kSmMaskF32) {
+        mk = reinterpret_cast<const float4*>(stage + a.mask_offset)[v];
+    } else {
+        mk = mask4(a, stage, moff, v);
+    }
+    return make_float4(__fadd_rn(x.x, mk.x), __fadd_rn(x.y, mk.y), __fadd_rn(x.z, mk.z), __fadd_rn(x.w, mk.w));
+}
+
+// Maximum, exps and their f64 sum for the thread's R vectors (kept in sv);
+// zmin = the smallest v - max seen (for the division's range check).
+// GUARD: the row does not fill all R * T vector slots.
+template <int T, int R, int MODE, bool GUARD>
+__device__ __forceinline__ double sm_exp_pass(const RingArgs& a, const float* row, const unsigned char* stage,
+                                              int64_t moff, uint32_t nvec, float4 (&sv)[R], float& zmin,
+                                              GroupScratch<T>* red) {
+    float m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+        const uint32_t v = threadIdx.x + (uint32_t)(i * T);
+        if (!GUARD || v < nvec) {
+            sv[i] = sm_operand4<MODE>(a, row, stage, moff, v);
+            m = fmaxf(m, fmaxf(fmaxf(sv[i].x, sv[i].y), fmaxf(sv[i].z, sv[i].w)));
+        }
+    }
+    m = row_max_fast<T>(m, red);
+    double acc = 0.0;
+    float zl = 0.0f;
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+        const uint32_t v = threadIdx.x + (uint32_t)(i * T);
+        if (!GUARD || v < nvec) {
+            const float4 z = make_float4(__fsub_rn(sv[i].x, m), __fsub_rn(sv[i].y, m), __fsub_rn(sv[i].z, m),
+                                         __fsub_rn(sv[i].w, m));
+            zl = fminf(zl, fminf(fminf(z.x, z.y), fminf(z.z, z.w)));
+            sv[i] = make_float4(softmax_exp(z.x), softmax_exp(z.y), softmax_exp(z.z), softmax_exp(z.w));
+            acc += (double)sv[i].x;
+            acc += (double)sv[i].y;
+            acc += (double)sv[i].z;
+            acc += (double)sv[i].w;
+        }
+    }
+    zmin = zl;
+    return row_sum_fast<T>(acc, red);
+}
+
+// e / denom for the thread's vectors: without range checks when the
+// thread's smallest v - max is at least kSoftmaxPlainDivFloor.
+template <int OP, int T, int R, bool GUARD>
+__device__ __forceinline__ void sm_div_pass(const RingArgs& a, float* drow, uint32_t nvec, const float4 (&sv)[R],
+                                            float denom, float inv, bool careful) {
+    if (!careful) {
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+            const uint32_t v = threadIdx.x + (uint32_t)(i * T);
+            if (!GUARD || v < nvec)
+                store4<OP>(a, drow, v,
+                           make_float4(markstein_div(sv[i].x, denom, inv), markstein_div(sv[i].y, denom, inv),
+                                       markstein_div(sv[i].z, denom, inv), markstein_div(sv[i].w, denom, inv)));
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < R; ++i) {
+            const uint32_t v = threadIdx.x + (uint32_t)(i * T);
+            if (!GUARD || v < nvec)
+                store4<OP>(a, drow, v,
+                           make_float4(softmax_div(sv[i].x, denom, inv), softmax_div(sv[i].y, denom, inv),
+                                       softmax_div(sv[i].z, denom, inv), softmax_div(sv[i].w, denom, inv)));
+        }
+    }
+}
+
 // R > 0 (soft_max only): each thread keeps its R vectors of the row in
-// registers (rows of at most 4 * T * R elements); R == 0 loops over the
-// staged row for every pass.
-template <int OP, int T, int R>
+// registers (rows of at most 4 * T * R elements), MODE being the operand
+// mode (SmMode); R == 0 loops over the staged row for every pass.
+template <int OP, int T, int R, int MODE>
 __global__ void __launch_bounds__(T, R >= 8 ? 2 : (R >= 4 ? 3 : 1024 / T)) row_ring(RingArgs a) {
     extern __shared__ __align__(128) unsigned char ring_smem[];
     __shared__ __align__(8) uint64_t full[kRingStagesMax];
@@ -219,9 +309,8 @@ __global__ void __launch_bounds__(T, R >= 8 ? 2 : (R >= 4 ? 3 : 1024 / T)) row_r
     }
     __syncthreads();
 
-    auto issue = [&](uint32_t k) {
+    auto issue = [&](uint32_t k, int s) {  // row k into stage s
         const uint32_t r = blockIdx.x + k * gridDim.x;
-        const int s = (int)(k % (uint32_t)S);
         unsigned char* st = stage0 + (size_t)s * a.stage_bytes;
         const uint32_t rb = a.ne0 * 4u;
         const uint32_t mb = a.aux_mode == kAuxMaskStaged ? a.ne0 * msize : 0u;
@@ -230,11 +319,11 @@ __global__ void __launch_bounds__(T, R >= 8 ? 2 : (R >= 4 ? 3 : 1024 / T)) row_r
         if (mb) bulk_load(st + a.mask_offset, a.aux + mask_offset(r, a) * msize, mb, &full[s]);
     };
     if (tid == 0)
-        for (uint32_t k = 0; k < mine && k < (uint32_t)S; ++k) issue(k);
+        for (uint32_t k = 0; k < mine && k < (uint32_t)S; ++k) issue(k, (int)k);
 
-    for (uint32_t k = 0; k < mine; ++k) {
-        const int s = (int)(k % (uint32_t)S);
-        const uint32_t parity = (k / (uint32_t)S) & 1u;
+    int s = 0;            // stage of row k: k % S
+    uint32_t parity = 0;  // phase parity of row k: (k / S) & 1
+    for (uint32_t k = 0; k < mine; ++k, s = s + 1 == S ? 0 : s + 1, parity ^= (s == 0)) {
         const bool ok = mbar_wait(&full[s], parity);
         if (!__syncthreads_and(ok)) {
             if (tid == 0) {
@@ -331,46 +420,21 @@ __global__ void __launch_bounds__(T, R >= 8 ? 2 : (R >= 4 ? 3 : 1024 / T)) row_r
                 // row whose sum comes back non-finite is redone exactly
                 // below from the untouched stage.
                 float4 sv[R];
-                float m = -INFINITY;
-#pragma unroll
-                for (int i = 0; i < R; ++i) {
-                    const uint32_t v = tid + (uint32_t)(i * T);
-                    if (v < nvec) {
-                        sv[i] = scaled4_fast(a, row, stage, moff, v);
-                        m = fmaxf(m, fmaxf(fmaxf(sv[i].x, sv[i].y), fmaxf(sv[i].z, sv[i].w)));
-                    }
-                }
-                m = row_max_fast<T>(m, &red);
-                double acc = 0.0;
-#pragma unroll
-                for (int i = 0; i < R; ++i) {
-                    const uint32_t v = tid + (uint32_t)(i * T);
-                    if (v < nvec) {
-                        sv[i] = make_float4(softmax_exp(__fsub_rn(sv[i].x, m)), softmax_exp(__fsub_rn(sv[i].y, m)),
-                                            softmax_exp(__fsub_rn(sv[i].z, m)), softmax_exp(__fsub_rn(sv[i].w, m)));
-                        acc += (double)sv[i].x;
-                        acc += (double)sv[i].y;
-                        acc += (double)sv[i].z;
-                        acc += (double)sv[i].w;
-                    }
-                }
-                acc = row_sum_fast<T>(acc, &red);
+                float zmin;
+                const bool guard = nvec != (uint32_t)(R * T);
+                const double acc = guard ? sm_exp_pass<T, R, MODE, true>(a, row, stage, moff, nvec, sv, zmin, &red)
+                                         : sm_exp_pass<T, R, MODE, false>(a, row, stage, moff, nvec, sv, zmin, &red);
                 if (isfinite(acc)) {
                     // every thread has finished reading the stage: refill it now
                     if (tid == 0 && k + (uint32_t)S < mine) {
                         asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                        issue(k + (uint32_t)S);
+                        issue(k + (uint32_t)S, s);
                     }
                     const float denom = __double2float_rn(acc);  // >= 1: the maximum contributes exp(0)
                     const float inv = __frcp_rn(denom);
-#pragma unroll
-                    for (int i = 0; i < R; ++i) {
-                        const uint32_t v = tid + (uint32_t)(i * T);
-                        if (v < nvec)
-                            store4<OP>(a, drow, v,
-                                       make_float4(softmax_div(sv[i].x, denom, inv), softmax_div(sv[i].y, denom, inv),
-                                                   softmax_div(sv[i].z, denom, inv), softmax_div(sv[i].w, denom, inv)));
-                    }
+                    const bool careful = !(zmin >= kSoftmaxPlainDivFloor);
+                    if (guard) sm_div_pass<OP, T, R, true>(a, drow, nvec, sv, denom, inv, careful);
+                    else sm_div_pass<OP, T, R, false>(a, drow, nvec, sv, denom, inv, careful);
                     continue;
                 }
             }
@@ -448,7 +512,7 @@ __global__ void __launch_bounds__(T, R >= 8 ? 2 : (R >= 4 ? 3 : 1024 / T)) row_r
         __syncthreads();  // every thread is done with this stage
         if (tid == 0 && k + (uint32_t)S < mine) {
             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-            issue(k + (uint32_t)S);
+            issue(k + (uint32_t)S, s);
         }
     }
 }
@@ -463,13 +527,13 @@ bool fits_u32(uint64_t v) { return v > 0 && v <= 0xffffffffull; }
 // allow (each CTA's row passes are a chain of dependent steps and barriers,
 // so throughput comes from several rows in progress per SM); then deeper
 // rings (up to kRingStagesMax) while shared memory lasts.
-template <int OP, int T, int R = 0>
+template <int OP, int T, int R = 0, int MODE = 0>
 cudaError_t launch_ring_kernel(const LaunchEnv& env, RingArgs a, uint64_t rows, bool* launched) {
     static int configured_device_mask = 0;  // bit per device with the attribute set
     const int bit = env.device < 31 ? (1 << env.device) : 0;
     if (!(configured_device_mask & bit)) {
         const cudaError_t err =
-            cudaFuncSetAttribute(row_ring<OP, T, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRingSmemPerSm);
+            cudaFuncSetAttribute(row_ring<OP, T, R, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRingSmemPerSm);
         if (err != cudaSuccess) return err;
         configured_device_mask |= bit;
     }
@@ -477,7 +541,7 @@ cudaError_t launch_ring_kernel(const LaunchEnv& env, RingArgs a, uint64_t rows, 
     const uint32_t two = a.weight_bytes + 2 * a.stage_bytes;
     if (two > kRingSmemPerSm) return cudaSuccess;
     int ctas = 0;
-    cudaError_t err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctas, row_ring<OP, T, R>, T, two);
+    cudaError_t err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&ctas, row_ring<OP, T, R, MODE>, T, two);
     if (err != cudaSuccess) return err;
     if (ctas < 1) return cudaSuccess;
     if (ctas > 8) ctas = 8;
@@ -492,9 +556,21 @@ cudaError_t launch_ring_kernel(const LaunchEnv& env, RingArgs a, uint64_t rows, 
     const uint32_t smem = a.weight_bytes + (uint32_t)a.stages * a.stage_bytes;
     const uint64_t cap = (uint64_t)env.sm_count * ctas;
     const uint32_t grid = (uint32_t)(rows < cap ? rows : cap);
-    err = launch_dependent(row_ring<OP, T, R>, dim3(grid), dim3(T), smem, env.stream, a);
+    err = launch_dependent(row_ring<OP, T, R, MODE>, dim3(grid), dim3(T), smem, env.stream, a);
     *launched = true;
     return err != cudaSuccess ? err : cudaGetLastError();
+}
+
+template <int R>
+cudaError_t launch_softmax_ring(const LaunchEnv& env, const RingArgs& a, uint64_t rows, bool* launched) {
+    if (!a.apply_scale) return launch_ring_kernel<kRingSoftMax, kRingThreads, R, kSmPlain>(env, a, rows, launched);
+    switch (a.aux_mode) {
+    case kAuxNone: return launch_ring_kernel<kRingSoftMax, kRingThreads, R, kSmScale>(env, a, rows, launched);
+    case kAuxMaskStaged:
+        return a.aux_f16 ? launch_ring_kernel<kRingSoftMax, kRingThreads, R, kSmMaskF16>(env, a, rows, launched)
+                         : launch_ring_kernel<kRingSoftMax, kRingThreads, R, kSmMaskF32>(env, a, rows, launched);
+    default: return launch_ring_kernel<kRingSoftMax, kRingThreads, R, kSmMaskLoads>(env, a, rows, launched);
+    }
 }
 
 }  // namespace
@@ -564,10 +640,10 @@ bool launch_row_ring(const LaunchEnv& env, const RowPlan& p, int op, float param
     case 3: {
         // vectors per thread, rounded up to a power of two, up to 8
         const uint64_t per = (ne0 / 4 + kRingThreads - 1) / kRingThreads;
-        if (per <= 1) e = launch_ring_kernel<kRingSoftMax, kRingThreads, 1>(env, a, p.rows, &launched);
-        else if (per <= 2) e = launch_ring_kernel<kRingSoftMax, kRingThreads, 2>(env, a, p.rows, &launched);
-        else if (per <= 4) e = launch_ring_kernel<kRingSoftMax, kRingThreads, 4>(env, a, p.rows, &launched);
-        else if (per <= 8) e = launch_ring_kernel<kRingSoftMax, kRingThreads, 8>(env, a, p.rows, &launched);
+        if (per <= 1) e = launch_softmax_ring<1>(env, a, p.rows, &launched);
+        else if (per <= 2) e = launch_softmax_ring<2>(env, a, p.rows, &launched);
+        else if (per <= 4) e = launch_softmax_ring<4>(env, a, p.rows, &launched);
+        else if (per <= 8) e = launch_softmax_ring<8>(env, a, p.rows, &launched);
         else e = launch_ring_kernel<kRingSoftMax, kRingThreads>(env, a, p.rows, &launched);
         break;
     }

@@ -26,8 +26,9 @@ namespace emel {
 
 namespace {
 
-constexpr int kSplitThreads = 256;  // 64 vocabulary rows x 8 CTAs stay resident at once
+constexpr int kSplitThreads = 256;
 constexpr int kSplitCluster = 8;
+constexpr int kSplitCtasPerSm = 4;  // register cap: 148 SMs x 4 >= 64 vocabulary rows x 8 CTAs, all resident
 
 __device__ __forceinline__ int64_t split_row_base(const RowOperand& o, uint64_t r, uint64_t ne1, uint64_t ne2) {
     const uint64_t i1 = r % ne1, q = r / ne1, i2 = q % ne2, i3 = q / ne2;
@@ -44,8 +45,9 @@ struct Chunk {
 };
 
 // Visits the 16-byte vectors v0 + tid, v0 + tid + T, ... below v1, issuing U
-// loads before using any of them (one load in flight per thread would leave
-// the chunk's passes latency-bound).
+// loads before using any of them, the last batch included (its loads past
+// v1 are skipped): one load in flight per thread would leave the chunk's
+// passes latency-bound.
 template <int U, typename Load, typename Use>
 __device__ __forceinline__ void batched(uint64_t v0, uint64_t v1, Load load, Use use) {
     uint64_t v = v0 + threadIdx.x;
@@ -56,7 +58,23 @@ __device__ __forceinline__ void batched(uint64_t v0, uint64_t v1, Load load, Use
 #pragma unroll
         for (int k = 0; k < U; ++k) use(v + k * kSplitThreads, q[k]);
     }
-    for (; v < v1; v += kSplitThreads) use(v, load(v));
+    if (v < v1) {  // the partial last batch, its loads still issued together
+        float4 q[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k)
+            if (v + k * kSplitThreads < v1) q[k] = load(v + k * kSplitThreads);
+#pragma unroll
+        for (int k = 0; k < U; ++k)
+            if (v + k * kSplitThreads < v1) use(v + k * kSplitThreads, q[k]);
+    }
+}
+
+// NaN-propagating maximum (PTX max.NaN): a NaN anywhere in a chunk reaches
+// the row's maximum.
+__device__ __forceinline__ float max_nan(float a, float b) {
+    float d;
+    asm("max.NaN.f32 %0, %1, %2;" : "=f"(d) : "f"(a), "f"(b));
+    return d;
 }
 
 __device__ __forceinline__ Chunk my_chunk(uint64_t ne0, uint64_t chunk, unsigned rank) {
@@ -72,7 +90,7 @@ __device__ __forceinline__ void arg_take(ArgBest& b, float v, int64_t i) {
     }
 }
 
-__global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitThreads)
+__global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitThreads, kSplitCtasPerSm)
     argmax_rows_split(RowPlan p, int dst_dtype, uint64_t chunk) {
     pdl_enter();
     __shared__ GroupScratch<kSplitThreads> s;
@@ -86,30 +104,20 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitTh
     const float* row = reinterpret_cast<const float*>(p.src.ptr) + split_row_base(p.src, r, p.ne[1], p.ne[2]);
     ArgBest b{0.0f, 0, 0};
     if (p.vec) {
+        // one (value, index) chain per vector lane, folded afterwards by
+        // arg_better (larger value, then smaller index): the sequential
+        // scan's answer, with four independent compare chains
+        ArgBest bl[4] = {b, b, b, b};
         const float4* r4 = reinterpret_cast<const float4*>(row);
-        const uint64_t v0 = ch.col0 / 4, v1 = ch.col1 / 4;  // chunk edges are multiples of 4 (ne0 too)
-        uint64_t v = v0 + threadIdx.x;
-        for (; v + 3 * kSplitThreads < v1; v += 4 * kSplitThreads) {
-            float4 q[4];
-#pragma unroll
-            for (int k = 0; k < 4; ++k) q[k] = __ldcs(r4 + v + k * kSplitThreads);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int64_t c = (int64_t)(v + k * kSplitThreads) * 4;
-                arg_take(b, q[k].x, c);
-                arg_take(b, q[k].y, c + 1);
-                arg_take(b, q[k].z, c + 2);
-                arg_take(b, q[k].w, c + 3);
-            }
-        }
-        for (; v < v1; v += kSplitThreads) {
-            const float4 q = __ldcs(r4 + v);
-            const int64_t c = (int64_t)v * 4;
-            arg_take(b, q.x, c);
-            arg_take(b, q.y, c + 1);
-            arg_take(b, q.z, c + 2);
-            arg_take(b, q.w, c + 3);
-        }
+        batched<8>(ch.col0 / 4, ch.col1 / 4, [&](uint64_t v) { return __ldcs(r4 + v); },
+                   [&](uint64_t v, float4 q) {
+                       const int64_t c = (int64_t)v * 4;
+                       arg_take(bl[0], q.x, c);
+                       arg_take(bl[1], q.y, c + 1);
+                       arg_take(bl[2], q.z, c + 2);
+                       arg_take(bl[3], q.w, c + 3);
+                   });
+        b = arg_better(arg_better(bl[0], bl[1]), arg_better(bl[2], bl[3]));
     } else {
         for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kSplitThreads)
             arg_take(b, row[(int64_t)c * p.src.st[0]], (int64_t)c);
@@ -135,7 +143,7 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitTh
     cluster.sync();  // peers' shared memory stays alive until rank 0 has read it
 }
 
-__global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitThreads)
+__global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitThreads, kSplitCtasPerSm)
     sum_rows_split(RowPlan p, uint64_t chunk) {
     pdl_enter();
     __shared__ GroupScratch<kSplitThreads> s;
@@ -194,7 +202,7 @@ __device__ __forceinline__ float value_at(const RowPlan& p, const SoftmaxRow& w,
     return v;
 }
 
-__global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitThreads)
+__global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitThreads, kSplitCtasPerSm)
     softmax_rows_split(RowPlan p, bool apply_scale, float scale, uint64_t chunk) {
     pdl_enter();
     __shared__ GroupScratch<kSplitThreads> s;
@@ -220,39 +228,45 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitTh
                            : q;
     };
 
-    // pass 1: maximum (fast values); a NaN lane reports +inf
-    float m = bitsf(0x7fc00000u);
-    bool odd = false;
+    // pass 1: maximum of the fast values, NaN-propagating: a NaN anywhere,
+    // or a maximum of +-inf, leaves the row's maximum non-finite
+    float m = -INFINITY;
     if (vec) {
         batched<8>(ch.col0 / 4, ch.col1 / 4, [&](uint64_t v) { return __ldcg(x4 + v); },
                    [&](uint64_t, float4 raw) {
                        const float4 q = scale4(raw);
-                       odd = odd || is_nan(q.x) || is_nan(q.y) || is_nan(q.z) || is_nan(q.w);
-                       m = fmaxf(fmaxf(m, q.x), fmaxf(q.y, fmaxf(q.z, q.w)));
+                       m = max_nan(max_nan(m, q.x), max_nan(q.y, max_nan(q.z, q.w)));
                    });
     } else {
-        for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kSplitThreads) {
-            const float v = value_at<false>(p, w, c, apply_scale, scale);
-            odd = odd || is_nan(v);
-            m = fmaxf(m, v);
-        }
+        for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kSplitThreads)
+            m = max_nan(m, value_at<false>(p, w, c, apply_scale, scale));
     }
-    m = group_max<kSplitThreads>(odd ? INFINITY : m, &s);
-    if (threadIdx.x == 0) part_max = m;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, o));
+    if ((threadIdx.x & 31) == 0) s.f[threadIdx.x / 32] = m;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        float cm = s.f[0];
+        for (int k = 1; k < kSplitThreads / 32; ++k) cm = max_nan(cm, s.f[k]);
+        part_max = cm;
+    }
     cluster.sync();
-    float gm = bitsf(0x7fc00000u);
-    for (int k = 0; k < kSplitCluster; ++k) gm = max_nn(gm, *cluster.map_shared_rank(&part_max, k));
+    float gm = *cluster.map_shared_rank(&part_max, 0);
+    for (int k = 1; k < kSplitCluster; ++k) gm = max_nan(gm, *cluster.map_shared_rank(&part_max, k));
 
     double acc = 0.0;
+    float zmin = 0.0f;  // smallest v - max among this thread's values
     if (isfinite(gm)) {
         // pass 2: e = exp(v - max) into dst, f64 sum
         if (vec) {
-            batched<4>(ch.col0 / 4, ch.col1 / 4, [&](uint64_t v) { return __ldcg(x4 + v); },
+            batched<8>(ch.col0 / 4, ch.col1 / 4, [&](uint64_t v) { return __ldcg(x4 + v); },
                        [&](uint64_t v, float4 raw) {
                            const float4 q = scale4(raw);
-                           const float4 e = make_float4(
-                               softmax_exp(__fsub_rn(q.x, gm)), softmax_exp(__fsub_rn(q.y, gm)),
-                               softmax_exp(__fsub_rn(q.z, gm)), softmax_exp(__fsub_rn(q.w, gm)));
+                           const float4 z = make_float4(__fsub_rn(q.x, gm), __fsub_rn(q.y, gm), __fsub_rn(q.z, gm),
+                                                        __fsub_rn(q.w, gm));
+                           zmin = fminf(zmin, fminf(fminf(z.x, z.y), fminf(z.z, z.w)));
+                           const float4 e = make_float4(softmax_exp(z.x), softmax_exp(z.y), softmax_exp(z.z),
+                                                        softmax_exp(z.w));
                            y4[v] = e;
                            acc += (double)e.x;
                            acc += (double)e.y;
@@ -261,7 +275,9 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitTh
                        });
         } else {
             for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kSplitThreads) {
-                const float e = softmax_exp(__fsub_rn(value_at<false>(p, w, c, apply_scale, scale), gm));
+                const float z = __fsub_rn(value_at<false>(p, w, c, apply_scale, scale), gm);
+                zmin = fminf(zmin, z);
+                const float e = softmax_exp(z);
                 w.y[(int64_t)c * w.ys] = e;
                 acc += (double)e;
             }
@@ -294,7 +310,13 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitTh
     // pass 3: divide in place (each thread rereads the values it wrote)
     if (isfinite(gm) && isfinite(denom)) {
         const float inv = __frcp_rn(denom);
-        if (vec) {
+        if (vec && zmin >= kSoftmaxPlainDivFloor) {
+            batched<8>(ch.col0 / 4, ch.col1 / 4, [&](uint64_t v) { return y4[v]; },
+                       [&](uint64_t v, float4 e) {
+                           __stcs(y4 + v, make_float4(markstein_div(e.x, denom, inv), markstein_div(e.y, denom, inv),
+                                                      markstein_div(e.z, denom, inv), markstein_div(e.w, denom, inv)));
+                       });
+        } else if (vec) {
             batched<8>(ch.col0 / 4, ch.col1 / 4, [&](uint64_t v) { return y4[v]; },
                        [&](uint64_t v, float4 e) {
                            __stcs(y4 + v, make_float4(softmax_div(e.x, denom, inv), softmax_div(e.y, denom, inv),
