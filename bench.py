@@ -626,10 +626,11 @@ def run_cfg5(args, world, rank, local):
     ne, nb = W.cfg5_src0_view(ne3=e - b)
     mul_out = torch.empty_like(src0)
     add_out = torch.empty_like(src0)
-    acc = torch.empty(1, dtype=torch.float64, device=device)
-    part = torch.empty(24, dtype=torch.uint8, device=device)
-    gathered_sum = torch.empty(world, dtype=torch.float64, device=device)
-    gathered_part = torch.empty(world * 24, dtype=torch.uint8, device=device)
+    # one 32-byte partial per rank: the f64 sum, then the argmax partial
+    partial = torch.zeros(32, dtype=torch.uint8, device=device)
+    acc = partial[0:8].view(torch.float64)
+    part = partial[8:32]
+    gathered = torch.empty(world * 32, dtype=torch.uint8, device=device)
     torch.cuda.synchronize()
 
     def view(t, vne, vnb=None):
@@ -646,24 +647,34 @@ def run_cfg5(args, world, rank, local):
     vm, va = view(mul_out, ne), view(add_out, ne)
     B = ctypes.byref
     plane = ne[0] * ne[1] * ne[2]
-    raw = sh.value if isinstance(sh, ctypes.c_void_p) else sh
-    torch_stream = torch.cuda.ExternalStream(int(raw or 0), device=device)
+    exchange = D.PeerExchange(pkg, ctx, dist, world, rank) if world > 1 else None
+
+    def call(st):
+        if st != 0:
+            raise RuntimeError(ctx.last_error)
 
     def step():
-        for st in (lib.emel_cuda_binary_repeat(ctx.handle, sh, 2, B(v0), B(v1), B(vm)),
-                   lib.emel_cuda_binary_repeat(ctx.handle, sh, 0, B(v0), B(v1), B(va)),
-                   lib.emel_cuda_sum_f64(ctx.handle, sh, B(v0), ctypes.c_void_p(acc.data_ptr())),
-                   lib.emel_cuda_argmax_partial_compute(ctx.handle, sh, B(v0), b * plane,
-                                                        ctypes.c_void_p(part.data_ptr()))):
-            if st != 0:
-                raise RuntimeError(ctx.last_error)
-        if world > 1:
-            with torch.cuda.stream(torch_stream):
-                dist.all_gather_into_tensor(gathered_sum, acc)
-                dist.all_gather_into_tensor(gathered_part, part)
+        # partials first: their exchange over NVLink (peer stores) lands while
+        # the two repeat broadcasts stream; the wait at the end gathers them
+        call(lib.emel_cuda_sum_f64(ctx.handle, sh, B(v0), ctypes.c_void_p(acc.data_ptr())))
+        call(lib.emel_cuda_argmax_partial_compute(ctx.handle, sh, B(v0), b * plane, ctypes.c_void_p(part.data_ptr())))
+        if exchange:
+            exchange.publish(sh, partial.data_ptr())
+        call(lib.emel_cuda_binary_repeat(ctx.handle, sh, 2, B(v0), B(v1), B(vm)))
+        call(lib.emel_cuda_binary_repeat(ctx.handle, sh, 0, B(v0), B(v1), B(va)))
+        if exchange:
+            exchange.wait(sh, gathered.data_ptr())
 
     for _ in range(args.warmup):
         step()
+    stream.synchronize()
+    torch.cuda.synchronize()
+    # the step (six kernels) replayed as one CUDA graph
+    graph = pkg.Graph(ctx, stream)
+    with graph:
+        step()
+    for _ in range(3):
+        graph.launch()
     stream.synchronize()
     torch.cuda.synchronize()
     if world > 1:
@@ -673,7 +684,7 @@ def run_cfg5(args, world, rank, local):
     with ClockSampler(local) as clocks:
         t0.record(sh)
         for _ in range(args.steps):
-            step()
+            graph.launch()
         t1.record(sh)
         stream.synchronize()
         torch.cuda.synchronize()
@@ -683,15 +694,8 @@ def run_cfg5(args, world, rank, local):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item())
     # combined answers (rank order) from the last step
-    if world > 1:
-        sums = gathered_sum.cpu().tolist()
-        raw = gathered_part.cpu().numpy().tobytes()
-        partials = [D.unpack_partial(raw[24 * k:24 * (k + 1)]) for k in range(world)]
-    else:
-        sums = [float(acc.cpu().item())]
-        partials = [D.read_partial(pkg, ctx, part.data_ptr())]
-    total32, _ = D.combine_sum(sums)
-    index, _ = D.combine_argmax(pkg, partials)
+    raw = (gathered if world > 1 else partial).cpu().numpy().tobytes()
+    total32, index = D.combine_gathered(pkg, raw, world)
     n = 128 * 32 * 8192 * 8
     step_bytes = 2 * (2 * n * 4 + 128 * 8192 * 4) + 2 * n * 4
     if rank == 0:
@@ -702,13 +706,17 @@ def run_cfg5(args, world, rank, local):
             "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded per dim-3 slice)",
             "config": {"workload": "cfg5 sharded: src0 [128,32,8192,8] (dims 1/2 swapped view) split along dim 3; "
                                    "repeat mul + repeat add with replicated src1 [128,1,8192,1], whole sum and "
-                                   "argmax as per-shard partials + NCCL all-gather",
+                                   "argmax as per-shard partials exchanged by peer stores over NVLink (library "
+                                   "kernels, no collective library; one CUDA graph per step)",
                        "bytes_per_step": step_bytes, "l2": "inputs 1.07 GB / N per GPU, larger than L2 up to N=8",
                        "parallelism": f"dim-3 shards over {world} GPU(s)"},
             "result": {"sum": float(total32), "argmax": int(index)},
             "clocks": clocks.summary(),
         }), flush=True)
+    graph.close()
     if world > 1:
+        dist.barrier()  # every rank's last wait is done: the peer buffers may go
+        exchange.close()
         dist.barrier()
         dist.destroy_process_group()
 

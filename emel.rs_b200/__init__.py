@@ -167,6 +167,12 @@ SIGNATURES = {
                                       ctypes.POINTER(ctypes.c_float)]),
     "emel_cuda_argmax_rows": (_I, [_CTX, _V, _P, _P]),
     "emel_cuda_generic": (_I, [_CTX, _V, ctypes.POINTER(CGenericRequest)]),
+    "emel_cuda_exchange_create": (_I, [_CTX, _I, _I, ctypes.c_uint32, ctypes.c_uint32, ctypes.POINTER(_V)]),
+    "emel_cuda_exchange_handle": (_I, [_V, _V]),
+    "emel_cuda_exchange_connect": (_I, [_CTX, _V, _V]),
+    "emel_cuda_exchange_publish": (_I, [_CTX, _V, _V, _V]),
+    "emel_cuda_exchange_wait": (_I, [_CTX, _V, _V, _V]),
+    "emel_cuda_exchange_destroy": (_I, [_CTX, _V]),
 }
 
 _lib = None

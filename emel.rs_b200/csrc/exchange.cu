@@ -1,0 +1,104 @@
+// Peer exchange of small per-rank payloads (the whole-tensor sum and argmax
+// partials of a sharded tensor) over NVLink, without a collective library.
+//
+// Each rank owns one buffer that every peer maps (CUDA IPC).  Publishing
+// epoch e (a device-side counter, so a replayed CUDA graph advances it) is
+// one tiny kernel: thread r stores this rank's payload into rank r's buffer,
+// slot [e & 1][rank], with plain stores over NVLink, then stores e into that
+// buffer's flag word for this rank with release semantics at system scope.
+// Waiting is a second tiny kernel: thread r polls its own buffer's flag word
+// for rank r with acquire loads until it reaches e, then copies slot
+// [e & 1][r] into the caller's gathered array (rank order).
+//
+// Two slot banks make reuse safe: a rank publishes epoch e + 2 into bank
+// e & 1 only after its wait for epoch e + 1 saw every peer's flag, and each
+// peer published e + 1 after its own wait for e had copied bank e & 1.
+//
+// Every poll is bounded by the global timer (the limit given at creation)
+// and by an iteration count; on expiry the wait sets the context's fault word
+// (emel_cuda_stream_synchronize then returns EMEL_CUDA_TIMEOUT) and returns.
+#include <cstdint>
+
+#include "launch.hpp"
+
+namespace emel {
+
+namespace {
+
+__device__ __forceinline__ void store_release_sys(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+__device__ __forceinline__ uint32_t load_acquire_sys(const uint32_t* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+__device__ __forceinline__ uint64_t now_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+__device__ __forceinline__ char* slot(char* buffer, uint32_t epoch, int rank, uint32_t slot_bytes) {
+    return buffer + kExchangeHeaderBytes + ((uint64_t)(epoch & 1u) * kExchangeMaxRanks + (uint64_t)rank) * slot_bytes;
+}
+
+__global__ void __launch_bounds__(kExchangeMaxRanks) exchange_publish(ExchangeArgs a) {
+    __shared__ uint32_t epoch;
+    if (threadIdx.x == 0) epoch = ++*a.epoch;
+    __syncthreads();
+    const int r = threadIdx.x;
+    if (r >= a.world) return;
+    const uint4* src = static_cast<const uint4*>(a.payload);
+    uint4* dst = reinterpret_cast<uint4*>(slot(a.peers[r], epoch, a.rank, a.slot_bytes));
+    for (uint32_t i = 0; i < a.bytes / 16; ++i) dst[i] = src[i];
+    // release: the payload stores above are visible to rank r before the flag
+    store_release_sys(reinterpret_cast<uint32_t*>(a.peers[r]) + a.rank, epoch);
+}
+
+__global__ void __launch_bounds__(kExchangeMaxRanks) exchange_wait(ExchangeArgs a, void* gathered) {
+    const int r = threadIdx.x;
+    if (r >= a.world) return;
+    const uint32_t epoch = *a.epoch;  // set by this rank's publish, earlier on the stream
+    char* own = a.peers[a.rank];
+    const uint32_t* flag = reinterpret_cast<const uint32_t*>(own) + r;
+    const uint64_t t0 = now_ns();
+    bool ok = false;
+    for (uint32_t i = 0; i < (1u << 28); ++i) {
+        if ((int32_t)(load_acquire_sys(flag) - epoch) >= 0) {
+            ok = true;
+            break;
+        }
+        if ((i & 255u) == 255u) {
+            if (now_ns() - t0 > a.timeout_ns) break;
+            __nanosleep(200);
+        }
+    }
+    if (!ok) {
+        atomicExch(a.fault, 1u);
+        return;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(slot(own, epoch, r, a.slot_bytes));
+    uint4* dst = reinterpret_cast<uint4*>(static_cast<char*>(gathered) + (uint64_t)r * a.bytes);
+    for (uint32_t i = 0; i < a.bytes / 16; ++i) dst[i] = src[i];
+}
+
+}  // namespace
+
+uint64_t exchange_buffer_bytes(uint32_t slot_bytes) {
+    return kExchangeHeaderBytes + 2ull * kExchangeMaxRanks * slot_bytes;
+}
+
+cudaError_t launch_exchange_publish(cudaStream_t stream, const ExchangeArgs& args) {
+    exchange_publish<<<1, kExchangeMaxRanks, 0, stream>>>(args);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_exchange_wait(cudaStream_t stream, const ExchangeArgs& args, void* gathered) {
+    exchange_wait<<<1, kExchangeMaxRanks, 0, stream>>>(args, gathered);
+    return cudaGetLastError();
+}
+
+}  // namespace emel

@@ -586,6 +586,152 @@ emel_cuda_status emel_cuda_graph_launch(emel_cuda_context* ctx, emel_cuda_graph*
     return device_status(ctx, err);
 }
 
+// ---- peer exchange over NVLink ----------------------------------------------
+
+}  // extern "C"
+
+struct emel_cuda_exchange {
+    int device;
+    int world;
+    int rank;
+    uint32_t bytes;
+    uint64_t timeout_ns;
+    char* buffer;      // this rank's buffer (cudaMalloc, shared by IPC)
+    uint32_t* epoch;   // this rank's step counter (device)
+    char* peers[emel::kExchangeMaxRanks];
+    bool opened[emel::kExchangeMaxRanks];  // peers[r] came from cudaIpcOpenMemHandle
+    bool connected;
+};
+
+namespace {
+
+static_assert(sizeof(cudaIpcMemHandle_t) == EMEL_CUDA_EXCHANGE_HANDLE_BYTES, "IPC handle size");
+
+void exchange_close_peers(emel_cuda_exchange* ex) {
+    for (int r = 0; r < emel::kExchangeMaxRanks; ++r) {
+        if (ex->opened[r]) cudaIpcCloseMemHandle(ex->peers[r]);
+        ex->opened[r] = false;
+        ex->peers[r] = nullptr;
+    }
+    ex->connected = false;
+}
+
+bool aligned16_ptr(const void* p) { return p != nullptr && (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+emel::ExchangeArgs exchange_args(emel_cuda_context* ctx, const emel_cuda_exchange* ex, const void* payload) {
+    emel::ExchangeArgs a{};
+    for (int r = 0; r < ex->world; ++r) a.peers[r] = ex->peers[r];
+    a.payload = payload;
+    a.epoch = ex->epoch;
+    a.fault = reinterpret_cast<uint32_t*>(static_cast<char*>(ctx->workspace) + emel::kFaultWordOffset);
+    a.world = ex->world;
+    a.rank = ex->rank;
+    a.bytes = ex->bytes;
+    a.slot_bytes = ex->bytes;
+    a.timeout_ns = ex->timeout_ns;
+    return a;
+}
+
+}  // namespace
+
+extern "C" {
+
+emel_cuda_status emel_cuda_exchange_create(emel_cuda_context* ctx, int world, int rank, uint32_t bytes_per_rank,
+                                           uint32_t timeout_ms, emel_cuda_exchange** out) {
+    if (ctx == nullptr || out == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    *out = nullptr;
+    if (world < 1 || world > emel::kExchangeMaxRanks || rank < 0 || rank >= world || bytes_per_rank == 0 ||
+        bytes_per_rank % 16 != 0 || bytes_per_rank > emel::kExchangeMaxBytes || timeout_ms == 0)
+        return EMEL_CUDA_INVALID_ARGUMENT;
+    cudaError_t err = select_device(ctx);
+    if (err != cudaSuccess) return device_status(ctx, err);
+    auto* ex = new (std::nothrow) emel_cuda_exchange();
+    if (ex == nullptr) return EMEL_CUDA_OUT_OF_MEMORY;
+    ex->device = ctx->device;
+    ex->world = world;
+    ex->rank = rank;
+    ex->bytes = bytes_per_rank;
+    ex->timeout_ns = (uint64_t)timeout_ms * 1000000ull;
+    const uint64_t bytes = emel::exchange_buffer_bytes(bytes_per_rank);
+    err = cudaMalloc(&ex->buffer, bytes);
+    if (err == cudaSuccess) err = cudaMalloc(&ex->epoch, 16);
+    if (err == cudaSuccess) err = cudaMemset(ex->buffer, 0, bytes);
+    if (err == cudaSuccess) err = cudaMemset(ex->epoch, 0, 16);
+    if (err == cudaSuccess) err = cudaDeviceSynchronize();
+    if (err != cudaSuccess) {
+        emel_cuda_status st = device_status(ctx, err);
+        if (ex->buffer) cudaFree(ex->buffer);
+        if (ex->epoch) cudaFree(ex->epoch);
+        delete ex;
+        return st;
+    }
+    *out = ex;
+    return EMEL_CUDA_OK;
+}
+
+emel_cuda_status emel_cuda_exchange_handle(const emel_cuda_exchange* ex, void* handle_out) {
+    if (ex == nullptr || handle_out == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    if (cudaSetDevice(ex->device) != cudaSuccess) return EMEL_CUDA_DEVICE_ERROR;
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, ex->buffer) != cudaSuccess) return EMEL_CUDA_DEVICE_ERROR;
+    std::memcpy(handle_out, &h, sizeof(h));
+    return EMEL_CUDA_OK;
+}
+
+emel_cuda_status emel_cuda_exchange_connect(emel_cuda_context* ctx, emel_cuda_exchange* ex, const void* handles) {
+    if (ctx == nullptr || ex == nullptr || handles == nullptr || ex->connected) return EMEL_CUDA_INVALID_ARGUMENT;
+    cudaError_t err = select_device(ctx);
+    if (err != cudaSuccess) return device_status(ctx, err);
+    const auto* h = static_cast<const unsigned char*>(handles);
+    for (int r = 0; r < ex->world; ++r) {
+        if (r == ex->rank) {
+            ex->peers[r] = ex->buffer;
+            continue;
+        }
+        cudaIpcMemHandle_t hr;
+        std::memcpy(&hr, h + (size_t)r * sizeof(hr), sizeof(hr));
+        void* p = nullptr;
+        err = cudaIpcOpenMemHandle(&p, hr, cudaIpcMemLazyEnablePeerAccess);
+        if (err != cudaSuccess) {
+            exchange_close_peers(ex);
+            return device_status(ctx, err);
+        }
+        ex->peers[r] = static_cast<char*>(p);
+        ex->opened[r] = true;
+    }
+    ex->connected = true;
+    return EMEL_CUDA_OK;
+}
+
+emel_cuda_status emel_cuda_exchange_publish(emel_cuda_context* ctx, void* stream, emel_cuda_exchange* ex,
+                                            const void* payload) {
+    if (ctx == nullptr || ex == nullptr || !ex->connected || !aligned16_ptr(payload)) return EMEL_CUDA_INVALID_ARGUMENT;
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = emel::launch_exchange_publish((cudaStream_t)stream, exchange_args(ctx, ex, payload));
+    if (err == cudaSuccess) ++ctx->launches;
+    return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_exchange_wait(emel_cuda_context* ctx, void* stream, emel_cuda_exchange* ex,
+                                         void* gathered) {
+    if (ctx == nullptr || ex == nullptr || !ex->connected || !aligned16_ptr(gathered)) return EMEL_CUDA_INVALID_ARGUMENT;
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess)
+        err = emel::launch_exchange_wait((cudaStream_t)stream, exchange_args(ctx, ex, nullptr), gathered);
+    if (err == cudaSuccess) ++ctx->launches;
+    return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_exchange_destroy(emel_cuda_context* ctx, emel_cuda_exchange* ex) {
+    if (ctx == nullptr || ex == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    cudaError_t err = select_device(ctx);
+    exchange_close_peers(ex);
+    if (err == cudaSuccess) err = cudaFree(ex->buffer);
+    const cudaError_t err2 = cudaFree(ex->epoch);
+    delete ex;
+    return device_status(ctx, err != cudaSuccess ? err : err2);
+}
+
 emel_cuda_status emel_cuda_graph_destroy(emel_cuda_context* ctx, emel_cuda_graph* graph) {
     if (ctx == nullptr || graph == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
     cudaError_t err = cudaGraphExecDestroy(graph->exec);

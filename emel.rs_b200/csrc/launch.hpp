@@ -61,4 +61,28 @@ constexpr int f16_table_slot(int op) { return op < 64 ? op : 22 + (op - 64); }
 // Bytes of workspace the whole-tensor reductions need.
 uint64_t reduction_workspace_bytes(int sm_count);
 
+// Peer exchange over NVLink (exchange.cu).  Every rank owns one buffer of
+// kExchangeHeaderBytes flag words (flag r = the last epoch rank r published
+// into this buffer) followed by two banks (epoch parity) of kExchangeMaxRanks
+// slots; peers[r] is rank r's buffer as mapped in this process.
+constexpr int kExchangeMaxRanks = 64;
+constexpr uint32_t kExchangeHeaderBytes = 256;
+constexpr uint32_t kExchangeMaxBytes = 1024;
+
+struct ExchangeArgs {
+    char* peers[kExchangeMaxRanks];
+    const void* payload;  // this rank's payload (device, 16-byte aligned)
+    uint32_t* epoch;      // this rank's epoch counter (device)
+    uint32_t* fault;      // the context's fault word
+    int world;
+    int rank;
+    uint32_t bytes;       // payload bytes, a multiple of 16
+    uint32_t slot_bytes;  // slot stride
+    uint64_t timeout_ns;
+};
+
+uint64_t exchange_buffer_bytes(uint32_t slot_bytes);
+cudaError_t launch_exchange_publish(cudaStream_t stream, const ExchangeArgs& args);
+cudaError_t launch_exchange_wait(cudaStream_t stream, const ExchangeArgs& args, void* gathered);
+
 }  // namespace emel

@@ -4,8 +4,10 @@ Tensors are partitioned along their outermost independent dimension
 (dim 3 for the 4-D broadcast workload, rows or heads for the row
 operators); the small broadcast operand is replicated on every rank.
 Elementwise and row operators need no communication.  Only whole-tensor
-sum and argmax combine per-shard partials, with one tiny all-gather over
-the process group (NCCL over NVLink on B200; gloo on CPU for tests):
+sum and argmax combine per-shard partials, with one tiny all-gather: on
+B200 through PeerExchange (peer stores over NVLink by two small kernels of
+the library, emel_cuda_exchange_*), or over a process group (NCCL, or gloo
+on CPU for tests):
 
   * sum: each rank's f64 accumulator (emel_cuda_sum_f64); the partials are
     added in rank order and rounded once to f32, so the result does not
@@ -84,3 +86,54 @@ def read_partial(pkg, ctx, device_ptr):
         raise RuntimeError(ctx.last_error)
     ctx.synchronize()
     return hp.value, hp.has_value, hp.index, hp.first_is_nan
+
+
+EXCHANGE_BYTES = 32  # one rank's payload: f64 shard sum, then its argmax partial
+
+
+class PeerExchange:
+    """The library's NVLink peer exchange (emel_cuda_exchange_*): every rank
+    publishes a fixed-size device payload into every rank's buffer and waits
+    for all of them, on a stream, inside captured graphs too.  Buffer handles
+    travel once over the process group (`dist`) at construction."""
+
+    def __init__(self, pkg, ctx, dist, world, rank, nbytes=EXCHANGE_BYTES, timeout_ms=10000):
+        self.pkg, self.ctx, self.lib = pkg, ctx, pkg.lib()
+        self.world, self.rank, self.nbytes = world, rank, nbytes
+        h = ctypes.c_void_p()
+        self._check(self.lib.emel_cuda_exchange_create(ctx.handle, world, rank, nbytes, timeout_ms, ctypes.byref(h)),
+                    "exchange create")
+        self.handle = h
+        mine = (ctypes.c_uint8 * 64)()
+        self._check(self.lib.emel_cuda_exchange_handle(self.handle, mine), "exchange handle")
+        handles = [None] * world
+        dist.all_gather_object(handles, bytes(mine))
+        flat = (ctypes.c_uint8 * (64 * world)).from_buffer_copy(b"".join(handles))
+        self._check(self.lib.emel_cuda_exchange_connect(ctx.handle, self.handle, flat), "exchange connect")
+
+    def _check(self, st, what):
+        if st != 0:
+            raise RuntimeError(f"{what} failed: status {st}: {self.ctx.last_error}")
+
+    def publish(self, stream, payload_ptr):
+        self._check(self.lib.emel_cuda_exchange_publish(self.ctx.handle, stream, self.handle,
+                                                         ctypes.c_void_p(payload_ptr)), "exchange publish")
+
+    def wait(self, stream, gathered_ptr):
+        self._check(self.lib.emel_cuda_exchange_wait(self.ctx.handle, stream, self.handle,
+                                                      ctypes.c_void_p(gathered_ptr)), "exchange wait")
+
+    def close(self):
+        if self.handle:
+            self.lib.emel_cuda_exchange_destroy(self.ctx.handle, self.handle)
+            self.handle = None
+
+
+def combine_gathered(pkg, raw, world):
+    """Sum and argmax of the whole tensor from `world` 32-byte exchange
+    payloads (rank order): (f32 sum, index)."""
+    sums = [struct.unpack("<d", raw[32 * k:32 * k + 8])[0] for k in range(world)]
+    partials = [unpack_partial(raw[32 * k + 8:32 * (k + 1)]) for k in range(world)]
+    total32, _ = combine_sum(sums)
+    index, _ = combine_argmax(pkg, partials)
+    return total32, index

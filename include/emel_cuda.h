@@ -356,6 +356,39 @@ typedef struct emel_cuda_generic_request {
 EMEL_CUDA_API emel_cuda_status emel_cuda_generic(emel_cuda_context* ctx, void* stream,
                                                  const emel_cuda_generic_request* request);
 
+/* ---- peer exchange over NVLink (multi-GPU partials) -------------------- */
+/* One process per GPU shards a tensor; each rank's small partial (the f64
+ * sum and the emel_cuda_argmax_partial of its shard) must reach every rank.
+ * No counterpart in the reference (a single-process CPU library): this
+ * replaces the collective of the sharded plan.  Every rank creates an
+ * exchange with the same world size and payload size, shares the 64-byte
+ * handle of its buffer with the others (any host channel), and connects
+ * with all handles in rank order.  Then, per step and on a stream:
+ *   emel_cuda_exchange_publish stores this rank's payload into every rank's
+ *     buffer over NVLink (peer stores, release flag at system scope);
+ *   emel_cuda_exchange_wait waits (bounded by timeout_ms) until every rank
+ *     published the same step, then writes all payloads, rank order, to
+ *     `gathered`.  A wait that expires sets the context's fault word:
+ *     emel_cuda_stream_synchronize returns EMEL_CUDA_TIMEOUT.
+ * Publish/wait calls alternate, one pair per step on every rank (a device
+ * counter numbers the steps, so a captured graph may replay them).
+ * payload and gathered are device pointers, 16-byte aligned; bytes_per_rank
+ * is a multiple of 16, at most 1024; world is 1..64.  Destroy only after
+ * every rank's last wait has completed (a host barrier). */
+typedef struct emel_cuda_exchange emel_cuda_exchange;
+#define EMEL_CUDA_EXCHANGE_HANDLE_BYTES 64
+EMEL_CUDA_API emel_cuda_status emel_cuda_exchange_create(emel_cuda_context* ctx, int world, int rank,
+                                                         uint32_t bytes_per_rank, uint32_t timeout_ms,
+                                                         emel_cuda_exchange** out);
+EMEL_CUDA_API emel_cuda_status emel_cuda_exchange_handle(const emel_cuda_exchange* ex, void* handle_out);
+EMEL_CUDA_API emel_cuda_status emel_cuda_exchange_connect(emel_cuda_context* ctx, emel_cuda_exchange* ex,
+                                                          const void* handles);
+EMEL_CUDA_API emel_cuda_status emel_cuda_exchange_publish(emel_cuda_context* ctx, void* stream, emel_cuda_exchange* ex,
+                                                          const void* payload);
+EMEL_CUDA_API emel_cuda_status emel_cuda_exchange_wait(emel_cuda_context* ctx, void* stream, emel_cuda_exchange* ex,
+                                                       void* gathered);
+EMEL_CUDA_API emel_cuda_status emel_cuda_exchange_destroy(emel_cuda_context* ctx, emel_cuda_exchange* ex);
+
 #ifdef __cplusplus
 }
 #endif

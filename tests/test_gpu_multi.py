@@ -150,13 +150,13 @@ def worker(rank, world, port, case_name, q):
         q.put((rank, "error", repr(exc), None, None))
 
 
-def run_ranks(world, case_name):
+def run_ranks(world, case_name, target=None):
     import torch.multiprocessing as mp
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = free_port()
-    procs = [ctx.Process(target=worker, args=(r, world, port, case_name, q)) for r in range(world)]
+    procs = [ctx.Process(target=target or worker, args=(r, world, port, case_name, q)) for r in range(world)]
     for p in procs:
         p.start()
     try:
@@ -215,3 +215,115 @@ def test_cfg5_sharded_over_all_gpus():
     ne, nb = W.cfg5_src0_view()
     want_sum, want_idx = whole_tensor_answers(x, ne, nb)
     check(results, want_sum, want_idx)
+
+
+# ---- NVLink peer exchange (emel_cuda_exchange_*) -----------------------------
+def pattern(rank, step):
+    return bytes((rank * 37 + step * 11 + i) % 256 for i in range(32))
+
+
+def exchange_worker(rank, world, port, mode, q):
+    """Publishes a per-rank, per-step 32-byte pattern and checks every rank's
+    gathered array: eager steps, then replays of a captured graph (the step
+    counter lives on the device).  mode "timeout": afterwards rank 0 alone
+    publishes and waits on a second exchange with a 300 ms limit; its wait
+    must expire, report EMEL_CUDA_TIMEOUT and leave the context usable."""
+    try:
+        sys.path.insert(0, str(ROOT))
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        from datetime import timedelta
+
+        import torch
+        import torch.distributed as dist
+
+        from __graft_entry__ import load_package
+
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                                device_id=dev)
+        pkg = load_package()
+        from emel_rs_b200 import distributed as D
+
+        lib = pkg.lib()
+        ctx = pkg.Context(rank)
+        stream = pkg.Stream(ctx)
+        sh = stream.handle
+        ex = D.PeerExchange(pkg, ctx, dist, world, rank, timeout_ms=10000)
+        payload = torch.zeros(32, dtype=torch.uint8, device=dev)
+        gathered = torch.zeros(world * 32, dtype=torch.uint8, device=dev)
+
+        def set_payload(step):
+            payload.copy_(torch.frombuffer(bytearray(pattern(rank, step)), dtype=torch.uint8))
+            torch.cuda.synchronize()
+
+        def gathered_ok(step):
+            return gathered.cpu().numpy().tobytes() == b"".join(pattern(r, step) for r in range(world))
+
+        eager_ok = True
+        for step in range(12):
+            set_payload(step)
+            ex.publish(sh, payload.data_ptr())
+            ex.wait(sh, gathered.data_ptr())
+            stream.synchronize()
+            eager_ok = eager_ok and gathered_ok(step)
+        graph = pkg.Graph(ctx, stream)
+        with graph:
+            ex.publish(sh, payload.data_ptr())
+            ex.wait(sh, gathered.data_ptr())
+        graph_ok = True
+        for step in range(12, 20):
+            set_payload(step)
+            graph.launch()
+            stream.synchronize()
+            graph_ok = graph_ok and gathered_ok(step)
+        graph.close()
+        timeout_status = usable = None
+        short = None
+        if mode == "timeout":
+            short = D.PeerExchange(pkg, ctx, dist, world, rank, timeout_ms=300)
+            dist.barrier()
+            if rank == 0:
+                set_payload(99)
+                short.publish(sh, payload.data_ptr())
+                short.wait(sh, gathered.data_ptr())
+                timeout_status = lib.emel_cuda_stream_synchronize(ctx.handle, sh)
+                x = torch.full((4096,), -2.0, device=dev)
+                y = torch.empty_like(x)
+                v, w = pkg.CView(), pkg.CView()
+                for t, cv in ((x, v), (y, w)):
+                    cv.data, cv.storage_bytes, cv.dtype = t.data_ptr(), t.numel() * 4, 0
+                    for d, (n, b) in enumerate(zip([4096, 1, 1, 1], pkg.contiguous_nb([4096, 1, 1, 1]))):
+                        cv.ne[d], cv.nb[d] = n, b
+                st = lib.emel_cuda_unary(ctx.handle, sh, 6, ctypes.byref(v), ctypes.byref(w))  # relu
+                st2 = lib.emel_cuda_stream_synchronize(ctx.handle, sh)
+                usable = st == 0 and st2 == 0 and bool((y.cpu() == 0).all())
+        dist.barrier()
+        ex.close()
+        if short is not None:
+            short.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, eager_ok, graph_ok, timeout_status, usable))
+    except Exception as exc:  # report to the parent instead of hanging it
+        q.put((rank, "error", repr(exc), None, None))
+
+
+def test_peer_exchange_eager_and_graph_replays():
+    world = gpu_count()
+    if world < 2:
+        pytest.skip("needs 2 GPUs")
+    results = run_ranks(min(world, 8), "steps", target=exchange_worker)
+    for rank, eager_ok, graph_ok, _, _ in results:
+        assert eager_ok and graph_ok, rank
+
+
+def test_peer_exchange_wait_expires_without_a_publisher():
+    if gpu_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    sys.path.insert(0, str(ROOT))
+    results = run_ranks(2, "timeout", target=exchange_worker)
+    by_rank = {r[0]: r for r in results}
+    assert by_rank[0][1] and by_rank[0][2] and by_rank[1][1] and by_rank[1][2]
+    assert by_rank[0][3] == 17, by_rank[0]  # EMEL_CUDA_TIMEOUT
+    assert by_rank[0][4] is True, by_rank[0]
