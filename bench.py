@@ -587,6 +587,18 @@ def run_suite(args):
             lambda k: (lambda: chk(lib.emel_cuda_sum(ctx.handle, sh, B(v0), B(vsum)))), 1)
     measure("cfg5", "argmax_whole_permuted", spec.ops[3].bytes, spec.ops[3].elements,
             lambda k: (lambda: chk(lib.emel_cuda_argmax(ctx.handle, sh, B(v0), B(varg)))), 1)
+    del t0, t1, td
+    # gated linear units (glu.rs) on configuration 2's feed-forward shape
+    spec = W.glu_spec()
+    xg = W.glu_ffn()
+    sets = sets_for(spec.ops[0].bytes)
+    tin = [torch.from_numpy(xg).to(dev) for _ in range(sets)]
+    tout = [torch.empty(W.GLU_N, device=dev) for _ in range(sets)]
+    for subop, o in enumerate(spec.ops):
+        measure("glu", o.name, o.bytes, o.elements,
+                lambda k, subop=subop: (lambda: chk(lib.emel_cuda_glu(
+                    ctx.handle, sh, subop, ctypes.c_void_p(tin[k].data_ptr()), 2 * W.GLU_N,
+                    ctypes.c_void_p(tout[k].data_ptr()), W.GLU_N))), sets)
     return out
 
 

@@ -167,6 +167,7 @@ SIGNATURES = {
                                       ctypes.POINTER(ctypes.c_float)]),
     "emel_cuda_argmax_rows": (_I, [_CTX, _V, _P, _P]),
     "emel_cuda_generic": (_I, [_CTX, _V, ctypes.POINTER(CGenericRequest)]),
+    "emel_cuda_glu": (_I, [_CTX, _V, _I, _V, ctypes.c_uint64, _V, ctypes.c_uint64]),
     "emel_cuda_exchange_create": (_I, [_CTX, _I, _I, ctypes.c_uint32, ctypes.c_uint32, ctypes.POINTER(_V)]),
     "emel_cuda_exchange_handle": (_I, [_V, _V]),
     "emel_cuda_exchange_connect": (_I, [_CTX, _V, _V]),
@@ -727,6 +728,31 @@ class GenericEvent(Event):
     def dispatch(self, ctx, stream):
         r = self.request()
         return ctx._lib.emel_cuda_generic(ctx.handle if ctx is not None else None, stream, ctypes.byref(r))
+
+
+class GluSubOp(enum.IntEnum):
+    """glu::GluSubOp wire codes (glu.rs:22-38)."""
+    REGLU = 0
+    GEGLU = 1
+    SWIGLU = 2
+    SWIGLU_OAI = 3
+    GEGLU_ERF = 4
+    GEGLU_QUICK = 5
+
+
+@dataclass
+class OpGlu(Event):
+    """glu::OpGlu::new(input, output, subop) (glu.rs:66-82) over device f32
+    arrays: `input` and `output` are (device pointer, element count) pairs,
+    the counterpart of the reference's slices."""
+    input: tuple
+    output: tuple
+    subop: GluSubOp
+
+    def dispatch(self, ctx, stream):
+        (ip, il), (op, ol) = self.input, self.output
+        return ctx._lib.emel_cuda_glu(ctx.handle, stream, int(self.subop), ctypes.c_void_p(ip), il,
+                                      ctypes.c_void_p(op), ol)
 
 
 class Kernel:

@@ -287,6 +287,46 @@ __device__ __forceinline__ float unary_apply(float v, UnaryParams p) {
 }
 
 // ---------------------------------------------------------------------------
+// Gated linear units (glu.rs:99-127, 264-277): out = value * gate(g).
+// Rust's f32::max(0.0) / f32::min(7.0) against a constant compile on x86-64
+// to maxss / minss with the constant as the second operand, which returns
+// that constant for a NaN input and for a tie: relu(-0.0) = +0.0.
+// ---------------------------------------------------------------------------
+template <bool EXACT>
+__device__ __forceinline__ float glu_silu(float v) {
+    using A = Arith<EXACT>;
+    return A::div(v, A::add(1.0f, A::exp(f_neg(v))));
+}
+
+template <int SUB, bool EXACT>
+__device__ __forceinline__ float glu_formula(float value, float g) {
+    using A = Arith<EXACT>;
+    if constexpr (SUB == kReGlu) return A::mul(value, g > 0.0f ? g : 0.0f);
+    if constexpr (SUB == kGeGlu) return A::mul(value, unary_formula<kGeluQuick, EXACT>(g, UnaryParams{}));
+    if constexpr (SUB == kSwiGlu) return A::mul(value, glu_silu<EXACT>(g));
+    if constexpr (SUB == kSwiGluOai) {
+        const float gate = g < 7.0f ? g : 7.0f;
+        const float v = value < 7.0f ? value : 7.0f;
+        return A::mul(A::div(glu_silu<EXACT>(A::mul(1.702f, gate)), 1.702f), A::add(v, 1.0f));
+    }
+    if constexpr (SUB == kGeGluErf) return A::mul(value, unary_formula<kGeluErf, EXACT>(g, UnaryParams{}));
+    // kGeGluQuick: value * (1 / (1 + exp(-1.702 * g)))
+    return A::mul(value, A::div(1.0f, A::add(1.0f, A::exp(A::mul(-1.702f, g)))));
+}
+
+template <int SUB>
+__device__ __noinline__ float glu_exact_slow(float value, float g) {
+    return glu_formula<SUB, true>(value, g);
+}
+
+template <int SUB>
+__device__ __forceinline__ float glu_apply(float value, float g) {
+    const float r = glu_formula<SUB, false>(value, g);
+    if (!is_nan(r)) return r;
+    return glu_exact_slow<SUB>(value, g);
+}
+
+// ---------------------------------------------------------------------------
 // Element access for the two floating storage types.
 // ---------------------------------------------------------------------------
 template <typename T>

@@ -56,6 +56,15 @@ struct SiluBackFn {
     }
 };
 
+// glu.rs: (value, gate) pairs from the two halves of the input.
+template <int SUB>
+struct GluFn {
+    static constexpr bool kBinary = true;
+    static constexpr int kUnroll = SUB == kReGlu ? 4 : 2;
+    static constexpr int kMinBlocks = 3;
+    __device__ __forceinline__ float operator()(float value, float g) const { return glu_apply<SUB>(value, g); }
+};
+
 // Per-lane path (binary16 vectors with a NaN in or out take it rarely; f32
 // vectors always).  Out of line for binary16 so the packed loop stays small.
 template <typename T, typename F>
@@ -735,6 +744,12 @@ cudaError_t launch_binary(const LaunchEnv& env, const EwPlan& p, int op) {
     case kMul: return binary_typed<kMul>(env, p);
     case kDiv: return binary_typed<kDiv>(env, p);
     case kSiluBack: return launch_ew<float>(env, p, SiluBackFn{});
+    case kGluBase + kReGlu: return launch_ew<float>(env, p, GluFn<kReGlu>{});
+    case kGluBase + kGeGlu: return launch_ew<float>(env, p, GluFn<kGeGlu>{});
+    case kGluBase + kSwiGlu: return launch_ew<float>(env, p, GluFn<kSwiGlu>{});
+    case kGluBase + kSwiGluOai: return launch_ew<float>(env, p, GluFn<kSwiGluOai>{});
+    case kGluBase + kGeGluErf: return launch_ew<float>(env, p, GluFn<kGeGluErf>{});
+    case kGluBase + kGeGluQuick: return launch_ew<float>(env, p, GluFn<kGeGluQuick>{});
     default: return cudaErrorInvalidValue;
     }
 }

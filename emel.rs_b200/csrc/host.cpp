@@ -873,6 +873,42 @@ emel_cuda_status emel_cuda_silu_back(emel_cuda_context* ctx, void* stream, const
     return device_status(ctx, err);
 }
 
+// ---- gated linear units ------------------------------------------------------
+
+emel_cuda_status emel_cuda_glu(emel_cuda_context* ctx, void* stream, int subop, const float* input,
+                               uint64_t input_len, float* output, uint64_t output_len) {
+    if (ctx == nullptr || subop < emel::kReGlu || subop > emel::kGeGluQuick) return EMEL_CUDA_INVALID_ARGUMENT;
+    // glu.rs:84-91 (split_len) behind guard_invalid (glu.rs:258-260)
+    if (input_len == 0 || input_len % 2 != 0 || output_len != input_len / 2) return EMEL_CUDA_INVALID_SHAPE;
+    if (input == nullptr || output == nullptr || (reinterpret_cast<uintptr_t>(input) & 3u) != 0 ||
+        (reinterpret_cast<uintptr_t>(output) & 3u) != 0 || input_len > (UINT64_MAX / 8))
+        return EMEL_CUDA_INVALID_ARGUMENT;
+    const uint64_t n = output_len;
+    // values = input[0, n), gates = input[n, 2n), output[0, n): three 1-D F32 views
+    emel_tensor_view vv{}, gv{}, ov{};
+    const void* ptrs[3] = {input, input + n, output};
+    emel_tensor_view* vs[3] = {&vv, &gv, &ov};
+    for (int k = 0; k < 3; ++k) {
+        vs[k]->data = const_cast<void*>(ptrs[k]);
+        vs[k]->storage_bytes = n * 4;
+        vs[k]->ne[0] = n;
+        vs[k]->ne[1] = vs[k]->ne[2] = vs[k]->ne[3] = 1;
+        vs[k]->nb[0] = 4;
+        vs[k]->nb[1] = vs[k]->nb[2] = vs[k]->nb[3] = n * 4;
+        vs[k]->dtype = EMEL_DTYPE_F32;
+    }
+    Checked cv, cg, co;
+    if (!validate_as(&vv, EMEL_DTYPE_F32, false, &cv) || !validate_as(&gv, EMEL_DTYPE_F32, false, &cg) ||
+        !validate_as(&ov, EMEL_DTYPE_F32, false, &co))
+        return EMEL_CUDA_INVALID_ARGUMENT;
+    const emel_tensor_view* views[3] = {&ov, &vv, &gv};
+    const Checked* cks[3] = {&co, &cv, &cg};
+    const emel::EwPlan plan = plan_equal_count(DType::F32, views, cks, 3);
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = emel::launch_binary(env_of(ctx, stream), plan, emel::kGluBase + subop);
+    return device_status(ctx, err);
+}
+
 // ---- row normalisation --------------------------------------------------------
 
 static emel_cuda_status norm_common(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,

@@ -13,6 +13,11 @@ enum class DType : int { F32 = 0, F16 = 1, I32 = 26, I64 = 27 };
 // Binary formula codes (emel_cuda_binary_op); 16 = silu_back (grad * silu'(x)).
 enum BinaryOp : int { kAdd = 0, kSub = 1, kMul = 2, kDiv = 3, kSiluBack = 16 };
 
+// Gated linear units (glu.rs:22-38 GluSubOp wire codes), run as two-input
+// elementwise ops (value, gate) under BinaryOp code kGluBase + subop.
+enum GluSubOp : int { kReGlu = 0, kGeGlu = 1, kSwiGlu = 2, kSwiGluOai = 3, kGeGluErf = 4, kGeGluQuick = 5 };
+constexpr int kGluBase = 32;
+
 // Unary formula codes (emel_cuda_unary_op); parameterised ops use codes >= 128.
 enum UnaryOp : int {
     kAbs = 0, kSgn = 1, kNeg = 2, kStep = 3, kTanh = 4, kElu = 5, kRelu = 6, kSigmoid = 7, kGelu = 8,

@@ -183,3 +183,23 @@ def cfg5_spec(ne3=CFG5_NE[3]):
 
 SPECS: Dict[str, callable] = {"cfg1": cfg1_spec, "cfg2": cfg2_spec, "cfg3": cfg3_spec, "cfg4": cfg4_spec,
                               "cfg5": cfg5_spec}
+
+
+# Gated linear units (glu.rs) -- no configuration in the benchmark set names
+# them; the bench suite uses the feed-forward gate of configuration 2's shape:
+# value and gate halves of [14336, 512] each, value ~ N(0, 1), gate ~ N(0, 2).
+GLU_N = CFG2_NE[0] * CFG2_NE[1]
+GLU_OPS = ("reglu", "geglu", "swiglu", "swiglu_oai", "geglu_erf", "geglu_quick")
+
+
+def glu_ffn(seed=7):
+    rng = np.random.default_rng(seed)
+    values = normal(rng, (GLU_N,), 1.0).astype(np.float32)
+    gates = normal(rng, (GLU_N,), 2.0).astype(np.float32)
+    return np.concatenate([values, gates])
+
+
+def glu_spec():
+    # read 2n floats, write n
+    return Config("glu", [OpSpec(op, 3 * GLU_N * F32, GLU_N) for op in GLU_OPS])
+

@@ -321,6 +321,22 @@ EMEL_CUDA_API emel_cuda_status emel_cuda_argmax_combine(const emel_cuda_argmax_p
 EMEL_CUDA_API emel_cuda_status emel_cuda_argmax_rows(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
                                        const emel_tensor_view* dst);
 
+/* ---- gated linear units ---------------------------------------------- */
+/* glu::OpGlu::new(input, output, subop) (glu.rs:66-92) dispatched by
+ * GluKernel::process_event (glu.rs:199-212): output[i] = value[i] *
+ * gate(g[i]) with value = input[0, n), g = input[n, 2n), n = output_len
+ * (glu.rs:114-123, 264-277).  subop: the GluSubOp wire codes (glu.rs:22-38)
+ * ReGlu 0 (relu), GeGlu 1 (tanh GELU), SwiGlu 2 (silu), SwiGluOai 3
+ * (silu(1.702 min(g, 7)) / 1.702 * (min(v, 7) + 1)), GeGluErf 4, GeGluQuick 5
+ * (sigmoid(1.702 g)).  input_len == 0, odd, or output_len != input_len / 2
+ * is EMEL_CUDA_INVALID_SHAPE (GluError::InvalidShape, glu.rs:84-91) and
+ * writes nothing.  Device additions: a null context, an unknown subop, a
+ * null or not 4-byte aligned pointer is EMEL_CUDA_INVALID_ARGUMENT.  input
+ * and output are device arrays of f32 (elements, not bytes); output may be
+ * exactly either half of input, no other overlap. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_glu(emel_cuda_context* ctx, void* stream, int subop, const float* input,
+                                             uint64_t input_len, float* output, uint64_t output_len);
+
 /* ---- generic operation envelope -------------------------------------- */
 /* The op-coded boundary for graph-driven dispatch: GenericRequest with
  * KernelOperation wire codes (generic.rs:24-316), up to three sources, a

@@ -536,6 +536,33 @@ int oracle_silu_back(const oracle_view* src, const oracle_view* grad, const orac
     return ORACLE_OK;
 }
 
+/* Gated linear units: glu.rs:84-91 (split_len), 99-127 (gates), 114-123
+ * (apply_split), 264-277 (SwiGluOai).  f32::max(0.0) / f32::min(7.0) are
+ * written as the comparisons x86's maxss / minss perform with the constant
+ * as second operand (a NaN or tied input yields the constant). */
+static float glu_one(int subop, float value, float g) {
+    switch (subop) {
+    case 0: return value * (g > 0.0f ? g : 0.0f);
+    case 1: return value * unary_apply(U_GELU_QUICK, g);
+    case 2: return value * unary_apply(U_SILU, g);
+    case 3: {
+        float gate = g < 7.0f ? g : 7.0f;
+        float v = value < 7.0f ? value : 7.0f;
+        return unary_apply(U_SILU, 1.702f * gate) / 1.702f * (v + 1.0f);
+    }
+    case 4: return value * unary_apply(U_GELU_ERF, g);
+    default: return value * (1.0f / (1.0f + expf(-1.702f * g)));
+    }
+}
+
+int oracle_glu(int subop, const float* input, uint64_t input_len, float* output, uint64_t output_len) {
+    if (subop < 0 || subop > 5) return ORACLE_UNEXPECTED_EVENT; /* not expressible in the reference */
+    if (input_len == 0 || input_len % 2 != 0 || output_len != input_len / 2) return ORACLE_INVALID_SHAPE;
+    const uint64_t n = output_len;
+    for (uint64_t i = 0; i < n; ++i) output[i] = glu_one(subop, input[i], input[n + i]);
+    return ORACLE_OK;
+}
+
 /* elementwise.rs:219-225 guards, 280-291 loop. */
 int oracle_add1(const oracle_view* src, const oracle_view* dst, float scalar) {
     uint64_t n;

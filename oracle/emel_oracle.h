@@ -63,6 +63,8 @@ int oracle_scale(const oracle_view* src, const oracle_view* dst, float scale);
 int oracle_clamp(const oracle_view* src, const oracle_view* dst, float lo, float hi);
 int oracle_leaky_relu(const oracle_view* src, const oracle_view* dst, float slope);
 int oracle_silu_back(const oracle_view* src, const oracle_view* grad, const oracle_view* dst);
+/* glu.rs OpGlu: output[i] = input[i] * gate(input[n + i]), n = output_len. */
+int oracle_glu(int subop, const float* input, uint64_t input_len, float* output, uint64_t output_len);
 int oracle_add1(const oracle_view* src, const oracle_view* dst, float scalar);
 int oracle_copy(const oracle_view* src, const oracle_view* dst);
 

@@ -103,6 +103,7 @@ def load(cr=False):
         "oracle_clamp": [P, P, ctypes.c_float, ctypes.c_float],
         "oracle_leaky_relu": [P, P, ctypes.c_float],
         "oracle_silu_back": [P, P, P],
+        "oracle_glu": [ctypes.c_int, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_uint64],
         "oracle_add1": [P, P, ctypes.c_float],
         "oracle_copy": [P, P],
         "oracle_norm": [P, P, ctypes.c_float],
