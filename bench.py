@@ -587,6 +587,9 @@ def run_suite(args):
             lambda k: (lambda: chk(lib.emel_cuda_sum(ctx.handle, sh, B(v0), B(vsum)))), 1)
     measure("cfg5", "argmax_whole_permuted", spec.ops[3].bytes, spec.ops[3].elements,
             lambda k: (lambda: chk(lib.emel_cuda_argmax(ctx.handle, sh, B(v0), B(varg)))), 1)
+    # shape.rs OpCont of the permuted view (a strided gather into dense rows)
+    measure("cfg5", "cont_permuted", 2 * spec.ops[2].bytes, spec.ops[2].elements,
+            lambda k: (lambda: chk(lib.emel_cuda_cont(ctx.handle, sh, B(v0), B(vd5)))), 1)
     del t0, t1, td
     # gated linear units (glu.rs) on configuration 2's feed-forward shape
     spec = W.glu_spec()

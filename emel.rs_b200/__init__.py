@@ -47,6 +47,7 @@ class Status(enum.IntEnum):
     INTERNAL = 5
     INVALID_SHAPE = 6
     UNSUPPORTED_OPERATION = 7
+    INVALID_LAYOUT = 8
     DEVICE_ERROR = 16
     TIMEOUT = 17
     INVALID_ARGUMENT = 18
@@ -167,6 +168,8 @@ SIGNATURES = {
                                       ctypes.POINTER(ctypes.c_float)]),
     "emel_cuda_argmax_rows": (_I, [_CTX, _V, _P, _P]),
     "emel_cuda_generic": (_I, [_CTX, _V, ctypes.POINTER(CGenericRequest)]),
+    "emel_cuda_cpy": (_I, [_CTX, _V, _P, _P]),
+    "emel_cuda_cont": (_I, [_CTX, _V, _P, _P]),
     "emel_cuda_glu": (_I, [_CTX, _V, _I, _V, ctypes.c_uint64, _V, ctypes.c_uint64]),
     "emel_cuda_exchange_create": (_I, [_CTX, _I, _I, ctypes.c_uint32, ctypes.c_uint32, ctypes.POINTER(_V)]),
     "emel_cuda_exchange_handle": (_I, [_V, _V]),
@@ -582,6 +585,26 @@ class CopyTensor(Event):
 
     def dispatch(self, ctx, stream):
         return ctx._lib.emel_cuda_copy(ctx.handle, stream, _r(self.src), _r(self.dst))
+
+
+@dataclass
+class OpCpy(Event):
+    """shape::OpCpy (shape.rs:55-69): ordinal copy between count-equal views."""
+    src: TensorView
+    dst: TensorView
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_cpy(ctx.handle, stream, _r(self.src), _r(self.dst))
+
+
+@dataclass
+class OpCont(Event):
+    """shape::OpCont (shape.rs:71-84): OpCpy into a dense row-major destination."""
+    src: TensorView
+    dst: TensorView
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_cont(ctx.handle, stream, _r(self.src), _r(self.dst))
 
 
 @dataclass

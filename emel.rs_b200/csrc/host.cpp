@@ -856,6 +856,41 @@ emel_cuda_status emel_cuda_copy(emel_cuda_context* ctx, void* stream, const emel
     return same_shape_unary(ctx, stream, src, dst, emel::kCopy, 0.0f, 0.0f);
 }
 
+// shape.rs OpCpy / OpCont: count-equal ordinal copy (unary plan with the
+// identity formula: a load and a store per element, bits unchanged).
+static bool dense_contiguous_f32(const emel_tensor_view* v) {
+    if (v->dtype != EMEL_DTYPE_F32) return false;
+    uint64_t expected = 4;
+    for (int d = 0; d < 4; ++d) {
+        if (v->nb[d] != expected) return false;
+        if (__builtin_mul_overflow(expected, v->ne[d], &expected)) return false;
+    }
+    return true;
+}
+
+static emel_cuda_status shape_copy(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                   const emel_tensor_view* dst, bool cont) {
+    Checked cs, cd;
+    if (!validate_as(src, EMEL_DTYPE_F32, false, &cs) || !validate_as(dst, EMEL_DTYPE_F32, false, &cd))
+        return EMEL_CUDA_INVALID_VIEW;
+    if (cs.count != cd.count) return EMEL_CUDA_SHAPE_MISMATCH;
+    if (cont && !dense_contiguous_f32(dst)) return EMEL_CUDA_INVALID_LAYOUT;
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    const emel_tensor_view* views[3] = {dst, src, nullptr};
+    const Checked* cks[3] = {&cd, &cs, nullptr};
+    return run_unary_plan(ctx, stream, plan_equal_count(DType::F32, views, cks, 2), emel::kCopy, 0.0f, 0.0f);
+}
+
+emel_cuda_status emel_cuda_cpy(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                               const emel_tensor_view* dst) {
+    return shape_copy(ctx, stream, src, dst, false);
+}
+
+emel_cuda_status emel_cuda_cont(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                const emel_tensor_view* dst) {
+    return shape_copy(ctx, stream, src, dst, true);
+}
+
 emel_cuda_status emel_cuda_silu_back(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
                                      const emel_tensor_view* grad, const emel_tensor_view* dst) {
     Checked cs, cg, cd;

@@ -60,6 +60,7 @@ typedef enum emel_cuda_status {
     EMEL_CUDA_INTERNAL = 5,           /* *Error::Internal */
     EMEL_CUDA_INVALID_SHAPE = 6,      /* Error::InvalidShape (generic envelope, actor.rs:88-90) */
     EMEL_CUDA_UNSUPPORTED_OPERATION = 7, /* Error::UnsupportedOperation (actor.rs:92) */
+    EMEL_CUDA_INVALID_LAYOUT = 8,     /* ShapeError::InvalidLayout (shape.rs:30-31) */
     EMEL_CUDA_DEVICE_ERROR = 16,      /* a CUDA runtime call failed */
     EMEL_CUDA_TIMEOUT = 17,           /* a bounded device wait expired */
     EMEL_CUDA_INVALID_ARGUMENT = 18,  /* null context / output pointer */
@@ -320,6 +321,21 @@ EMEL_CUDA_API emel_cuda_status emel_cuda_argmax_combine(const emel_cuda_argmax_p
  * [1, ne1, ne2, ne3], dtype F32, I32 or I64; the index is the column. */
 EMEL_CUDA_API emel_cuda_status emel_cuda_argmax_rows(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
                                        const emel_tensor_view* dst);
+
+/* ---- shape copies ----------------------------------------------------- */
+/* shape::OpCpy (shape.rs:55-69; guards 453-466, loop copy_view 438-444):
+ * dst.write(i, src.read(i)) for every ordinal i of two F32 views with equal
+ * element counts (extents may differ).  Invalid view -> INVALID_VIEW,
+ * counts differ -> SHAPE_MISMATCH; nothing is written then.  Bits are
+ * copied unchanged (NaN payloads included). */
+EMEL_CUDA_API emel_cuda_status emel_cuda_cpy(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                             const emel_tensor_view* dst);
+/* shape::OpCont (shape.rs:71-84; guards 492-512): OpCpy into a destination
+ * whose byte strides are exactly dense row-major (Layout::is_dense_contiguous,
+ * tensor_view.rs:281-314; nb[0] == 0 does not qualify), else
+ * EMEL_CUDA_INVALID_LAYOUT (checked after the view and count guards). */
+EMEL_CUDA_API emel_cuda_status emel_cuda_cont(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                              const emel_tensor_view* dst);
 
 /* ---- gated linear units ---------------------------------------------- */
 /* glu::OpGlu::new(input, output, subop) (glu.rs:66-92) dispatched by

@@ -581,6 +581,34 @@ int oracle_copy(const oracle_view* src, const oracle_view* dst) {
     return ORACLE_OK;
 }
 
+/* shape.rs: OpCpy (guards 453-466, copy_view 438-444) copies by ordinal
+ * between count-equal views of any extents; OpCont (guards 492-512)
+ * additionally requires a destination whose byte strides are exactly the
+ * dense row-major ones (Layout::is_dense_contiguous, tensor_view.rs:281-314:
+ * the implicit nb[0] == 0 form does not qualify). */
+static int dense_contiguous_f32(const oracle_view* v) {
+    if (v->dtype != DT_F32) return 0;
+    uint64_t expected = 4;
+    for (int d = 0; d < 4; ++d) {
+        if (v->nb[d] != expected) return 0;
+        if (__builtin_mul_overflow(expected, v->ne[d], &expected)) return 0;
+    }
+    return 1;
+}
+
+static int shape_copy(const oracle_view* src, const oracle_view* dst, int cont) {
+    uint64_t ns, nd;
+    if (!validate_as(src, DT_F32, 0, &ns) || !validate_as(dst, DT_F32, 0, &nd)) return ORACLE_INVALID_VIEW;
+    if (ns != nd) return ORACLE_SHAPE_MISMATCH;
+    if (cont && !dense_contiguous_f32(dst)) return ORACLE_INVALID_LAYOUT;
+    ORACLE_MAP(src, dst, ns, v);
+    return ORACLE_OK;
+}
+
+int oracle_cpy(const oracle_view* src, const oracle_view* dst) { return shape_copy(src, dst, 0); }
+
+int oracle_cont(const oracle_view* src, const oracle_view* dst) { return shape_copy(src, dst, 1); }
+
 /* ---------------------------------------------------------------------- */
 /* Row normalisation: normalization.rs                                     */
 /* ---------------------------------------------------------------------- */

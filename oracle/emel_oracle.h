@@ -47,6 +47,7 @@ enum {
     ORACLE_UNEXPECTED_EVENT = 4,
     ORACLE_INVALID_SHAPE = 6,
     ORACLE_UNSUPPORTED_OPERATION = 7,
+    ORACLE_INVALID_LAYOUT = 8,
     ORACLE_INVALID_ARGUMENT = 18
 };
 
@@ -63,6 +64,9 @@ int oracle_scale(const oracle_view* src, const oracle_view* dst, float scale);
 int oracle_clamp(const oracle_view* src, const oracle_view* dst, float lo, float hi);
 int oracle_leaky_relu(const oracle_view* src, const oracle_view* dst, float slope);
 int oracle_silu_back(const oracle_view* src, const oracle_view* grad, const oracle_view* dst);
+/* shape.rs OpCpy / OpCont. */
+int oracle_cpy(const oracle_view* src, const oracle_view* dst);
+int oracle_cont(const oracle_view* src, const oracle_view* dst);
 /* glu.rs OpGlu: output[i] = input[i] * gate(input[n + i]), n = output_len. */
 int oracle_glu(int subop, const float* input, uint64_t input_len, float* output, uint64_t output_len);
 int oracle_add1(const oracle_view* src, const oracle_view* dst, float scalar);

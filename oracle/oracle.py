@@ -106,6 +106,8 @@ def load(cr=False):
         "oracle_glu": [ctypes.c_int, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_uint64],
         "oracle_add1": [P, P, ctypes.c_float],
         "oracle_copy": [P, P],
+        "oracle_cpy": [P, P],
+        "oracle_cont": [P, P],
         "oracle_norm": [P, P, ctypes.c_float],
         "oracle_rms_norm": [P, P, ctypes.c_float],
         "oracle_rms_norm_mul": [P, P, P, ctypes.c_float],
