@@ -48,6 +48,8 @@ class Status(enum.IntEnum):
     INVALID_SHAPE = 6
     UNSUPPORTED_OPERATION = 7
     INVALID_LAYOUT = 8
+    INDEX_OUT_OF_BOUNDS = 9
+    UNSUPPORTED_SOURCE_STRIDE = 10
     DEVICE_ERROR = 16
     TIMEOUT = 17
     INVALID_ARGUMENT = 18
@@ -168,6 +170,7 @@ SIGNATURES = {
                                       ctypes.POINTER(ctypes.c_float)]),
     "emel_cuda_argmax_rows": (_I, [_CTX, _V, _P, _P]),
     "emel_cuda_generic": (_I, [_CTX, _V, ctypes.POINTER(CGenericRequest)]),
+    "emel_cuda_get_rows": (_I, [_CTX, _V, _P, _P, _P]),
     "emel_cuda_cpy": (_I, [_CTX, _V, _P, _P]),
     "emel_cuda_cont": (_I, [_CTX, _V, _P, _P]),
     "emel_cuda_glu": (_I, [_CTX, _V, _I, _V, ctypes.c_uint64, _V, ctypes.c_uint64]),
@@ -585,6 +588,19 @@ class CopyTensor(Event):
 
     def dispatch(self, ctx, stream):
         return ctx._lib.emel_cuda_copy(ctx.handle, stream, _r(self.src), _r(self.dst))
+
+
+@dataclass
+class OpGetRows(Event):
+    """get_rows::OpGetRows and its F16 / BF16 / Q4_0 / Q8_0 / Q4_K variants
+    (get_rows.rs:219-512), chosen by the source view's dtype; `indices` is
+    an I32 view with ne[3] == 1."""
+    src: TensorView
+    indices: TensorView
+    dst: TensorView
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_get_rows(ctx.handle, stream, _r(self.src), _r(self.indices), _r(self.dst))
 
 
 @dataclass

@@ -472,16 +472,23 @@ emel_cuda_status emel_cuda_stream_synchronize(emel_cuda_context* ctx, void* stre
     cudaError_t err = cudaStreamSynchronize(s);
     // A kernel whose bounded wait expired left the fault word set: report it
     // once and re-arm it.
-    uint32_t fault = 0;
-    char* word = static_cast<char*>(ctx->workspace) + emel::kFaultWordOffset;
-    if (err == cudaSuccess) err = cudaMemcpyAsync(&fault, word, sizeof(fault), cudaMemcpyDeviceToHost, s);
+    // [0] the fault word (offset 64), [2] the rejected-request word (offset 72)
+    uint32_t words[3] = {0, 0, 0};
+    char* base = static_cast<char*>(ctx->workspace) + emel::kFaultWordOffset;
+    static_assert(emel::kRejectWordOffset == emel::kFaultWordOffset + 8, "header words");
+    if (err == cudaSuccess) err = cudaMemcpyAsync(words, base, sizeof(words), cudaMemcpyDeviceToHost, s);
     if (err == cudaSuccess) err = cudaStreamSynchronize(s);
-    if (err == cudaSuccess && fault != 0) {
-        err = cudaMemsetAsync(word, 0, sizeof(fault), s);
+    if (err == cudaSuccess && (words[0] != 0 || words[2] != 0)) {
+        err = cudaMemsetAsync(base, 0, sizeof(words), s);
         if (err == cudaSuccess) err = cudaStreamSynchronize(s);
         if (err == cudaSuccess) {
-            std::snprintf(ctx->last_error, sizeof(ctx->last_error), "a bounded device wait expired");
-            return EMEL_CUDA_TIMEOUT;
+            if (words[0] != 0) {
+                std::snprintf(ctx->last_error, sizeof(ctx->last_error), "a bounded device wait expired");
+                return EMEL_CUDA_TIMEOUT;
+            }
+            std::snprintf(ctx->last_error, sizeof(ctx->last_error), "a request was rejected on the device (status %u)",
+                          words[2]);
+            return (emel_cuda_status)words[2];
         }
     }
     return device_status(ctx, err);
@@ -905,6 +912,204 @@ emel_cuda_status emel_cuda_silu_back(emel_cuda_context* ctx, void* stream, const
     const emel::EwPlan plan = plan_equal_count(DType::F32, views, cks, 3);
     cudaError_t err = select_device(ctx);
     if (err == cudaSuccess) err = emel::launch_binary(env_of(ctx, stream), plan, emel::kSiluBack);
+    return device_status(ctx, err);
+}
+
+// ---- row gather (get_rows.rs) -------------------------------------------------
+
+namespace {
+
+struct GrIndex {
+    uint64_t ne[3] = {0, 0, 0};
+    uint64_t st[3] = {0, 0, 0};  // elements
+    uint64_t count = 0;
+    bool valid = false;
+};
+
+// IndexView::with_strides (get_rows.rs:44-139, 180-215) over an I32 view
+// with ne[3] == 1; nb[0] == 0 selects the implicit contiguous strides.
+GrIndex gr_index_view(const emel_tensor_view* v) {
+    GrIndex x;
+    if (v == nullptr || v->dtype != EMEL_DTYPE_I32 || v->ne[3] != 1 || v->reserved != 0) return x;
+    uint64_t bs[3];
+    bool strides_valid = true, shape_valid = true, zero = false;
+    const bool implicit = v->nb[0] == 0;
+    if (implicit) {
+        bs[0] = 4;
+        for (int d = 1; d < 3; ++d)
+            if (__builtin_mul_overflow(bs[d - 1], v->ne[d - 1], &bs[d])) {
+                strides_valid = false;
+                bs[d] = 0;
+            }
+    } else {
+        for (int d = 0; d < 3; ++d) bs[d] = v->nb[d];
+    }
+    uint64_t count = 1;
+    for (int d = 0; d < 3; ++d) {
+        x.ne[d] = v->ne[d];
+        if (v->ne[d] > 1 && bs[d] == 0 && !implicit) strides_valid = false;
+        if (bs[d] != 0 && (bs[d] < 4 || bs[d] % 4 != 0)) strides_valid = false;
+        x.st[d] = bs[d] / 4;
+        if (v->ne[d] == 0) zero = true;
+        else if (!zero && __builtin_mul_overflow(count, v->ne[d], &count)) {
+            shape_valid = false;
+            count = 0;
+        }
+    }
+    if (zero) count = 0;
+    bool span = true;
+    if (!zero) {
+        u128 max_offset = 0;
+        for (int d = 0; d < 3; ++d) max_offset += (u128)(v->ne[d] - 1) * (u128)bs[d];
+        span = max_offset + 4 <= (u128)(v->storage_bytes / 4) * 4;
+    }
+    x.count = count;
+    x.valid = strides_valid && shape_valid && span && (zero || v->data != nullptr);
+    return x;
+}
+
+bool gr_empty_f32_source_valid(const emel_tensor_view* v) {
+    if (v->dtype != EMEL_DTYPE_F32 || v->ne[0] == 0 || v->ne[1] == 0 || (v->nb[0] != 0 && v->nb[0] != 4)) return false;
+    if (v->nb[0] != 0)
+        for (int d = 0; d < 4; ++d)
+            if (v->ne[d] > 1 && v->nb[d] == 0) return false;
+    return true;
+}
+
+bool gr_destination_valid(const emel_tensor_view* dst, uint64_t count) {
+    Checked cd;
+    if (count == 0) return dst->dtype == EMEL_DTYPE_F32 && dense_contiguous_f32(dst);
+    return validate_as(dst, EMEL_DTYPE_F32, false, &cd) && dense_contiguous_f32(dst);
+}
+
+// F16View::validate (f16_matmul.rs:45-85) / Bf16View::validate (get_rows.rs:300-340)
+bool gr_half_view_valid(const emel_tensor_view* v, uint32_t dtype, uint64_t s[4]) {
+    if (v->dtype != dtype || v->data == nullptr) return false;
+    uint64_t count = 1;
+    for (int d = 0; d < 4; ++d)
+        if (v->ne[d] == 0 || __builtin_mul_overflow(count, v->ne[d], &count)) return false;
+    if (v->nb[0] != 0) {
+        for (int d = 0; d < 4; ++d) s[d] = v->nb[d];
+    } else {
+        s[0] = 2;
+        for (int d = 1; d < 4; ++d)
+            if (__builtin_mul_overflow(s[d - 1], v->ne[d - 1], &s[d])) return false;
+    }
+    for (int d = 0; d < 4; ++d) {
+        if (dtype == EMEL_DTYPE_F16) {
+            if (v->ne[d] > 1 && (s[d] < 2 || s[d] % 2 != 0)) return false;
+        } else if (v->nb[0] != 0) {
+            if ((v->ne[d] > 1 && v->nb[d] == 0) || (v->nb[d] != 0 && (v->nb[d] < 2 || v->nb[d] % 2 != 0)))
+                return false;
+        }
+    }
+    u128 max_offset = 0;
+    for (int d = 0; d < 4; ++d) max_offset += (u128)(v->ne[d] - 1) * (u128)s[d];
+    return max_offset + 2 <= (u128)(v->storage_bytes / 2) * 2;
+}
+
+// PackedRowView::validate (tensor_view.rs:483-526)
+bool gr_packed_view_valid(const emel_tensor_view* v, uint32_t code, uint64_t bv, uint64_t bb, uint64_t* row_bytes) {
+    if (v->dtype != code || v->data == nullptr) return false;
+    for (int d = 0; d < 4; ++d)
+        if (v->ne[d] == 0) return false;
+    if (v->ne[0] % bv != 0 || v->nb[0] != 1) return false;
+    uint64_t rb, s2, s3;
+    if (__builtin_mul_overflow(v->ne[0] / bv, bb, &rb)) return false;
+    if (__builtin_mul_overflow(rb, v->ne[1], &s2)) return false;
+    if (__builtin_mul_overflow(s2, v->ne[2], &s3)) return false;
+    if (rb == 0 || v->nb[1] != rb || v->nb[2] != s2 || v->nb[3] != s3) return false;
+    u128 max_offset = 0;
+    for (int d = 1; d < 4; ++d) max_offset += (u128)(v->ne[d] - 1) * (u128)v->nb[d];
+    *row_bytes = rb;
+    return max_offset + rb <= (u128)v->storage_bytes;
+}
+
+bool gr_shape_valid(const emel_tensor_view* src, const GrIndex& x, const emel_tensor_view* dst) {
+    return src->ne[0] > 0 && src->ne[1] > 0 && dst->ne[0] == src->ne[0] && dst->ne[1] == x.ne[0] &&
+           dst->ne[2] == x.ne[1] && dst->ne[3] == x.ne[2] && src->ne[2] == x.ne[1] && src->ne[3] == x.ne[2];
+}
+
+}  // namespace
+
+emel_cuda_status emel_cuda_get_rows(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                    const emel_tensor_view* indices, const emel_tensor_view* dst) {
+    if (src == nullptr || indices == nullptr || dst == nullptr) return EMEL_CUDA_INVALID_VIEW;
+    const GrIndex ix = gr_index_view(indices);
+    const uint32_t t = src->dtype;
+    emel::GatherPlan p{};
+    uint64_t hs[4] = {0, 0, 0, 0}, row_bytes = 0, fs[4] = {0, 0, 0, 0};
+    bool views = false;
+    Checked cs;
+    switch (t) {
+    case EMEL_DTYPE_F32:
+        p.kind = emel::kGatherF32;
+        views = ix.valid && (ix.count == 0 ? gr_empty_f32_source_valid(src) : validate_as(src, EMEL_DTYPE_F32, true, &cs)) &&
+                gr_destination_valid(dst, ix.count);
+        break;
+    case EMEL_DTYPE_F16:
+    case EMEL_DTYPE_BF16: {
+        p.kind = t == EMEL_DTYPE_F16 ? emel::kGatherF16 : emel::kGatherBF16;
+        Checked cd;
+        views = ix.valid && gr_half_view_valid(src, t, hs) && validate_as(dst, EMEL_DTYPE_F32, false, &cd) &&
+                dense_contiguous_f32(dst);
+        break;
+    }
+    case EMEL_DTYPE_Q4_0:
+    case EMEL_DTYPE_Q8_0:
+    case EMEL_DTYPE_Q4_K: {
+        p.kind = t == EMEL_DTYPE_Q4_0 ? emel::kGatherQ4_0 : (t == EMEL_DTYPE_Q8_0 ? emel::kGatherQ8_0 : emel::kGatherQ4_K);
+        const uint64_t bv = t == EMEL_DTYPE_Q4_K ? 256 : 32;
+        const uint64_t bb = t == EMEL_DTYPE_Q4_0 ? 18 : (t == EMEL_DTYPE_Q8_0 ? 34 : 144);
+        Checked cd;
+        views = ix.valid && gr_packed_view_valid(src, t, bv, bb, &row_bytes) &&
+                (ix.count == 0 ? dense_contiguous_f32(dst)
+                               : (validate_as(dst, EMEL_DTYPE_F32, false, &cd) && dense_contiguous_f32(dst))) &&
+                dst->dtype == EMEL_DTYPE_F32;
+        break;
+    }
+    default:
+        return EMEL_CUDA_INVALID_VIEW;
+    }
+    // get_rows.rs guard order: view, shape, source stride (F32), indices (on the device)
+    if (!views) return EMEL_CUDA_INVALID_VIEW;
+    if (!gr_shape_valid(src, ix, dst)) return EMEL_CUDA_SHAPE_MISMATCH;
+    if (t == EMEL_DTYPE_F32 && !(src->nb[0] == 0 || (src->nb[0] >= 4 && src->nb[0] % 4 == 0)))
+        return EMEL_CUDA_UNSUPPORTED_SOURCE_STRIDE;
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    if (ix.count == 0) return EMEL_CUDA_OK;  // the reference's metadata-only no-op
+    // device additions: element-aligned pointers
+    const uintptr_t sa = reinterpret_cast<uintptr_t>(src->data), ia = reinterpret_cast<uintptr_t>(indices->data);
+    const uintptr_t da = reinterpret_cast<uintptr_t>(dst->data);
+    if ((ia & 3u) || (da & 3u) || (t == EMEL_DTYPE_F32 ? (sa & 3u) : (sa & 1u)) ||
+        (t == EMEL_DTYPE_F32 && (src->nb[1] % 4 || src->nb[2] % 4 || src->nb[3] % 4)))
+        return EMEL_CUDA_INVALID_ARGUMENT;
+    p.src = static_cast<const char*>(src->data);
+    p.dst = static_cast<float*>(dst->data);
+    p.idx = static_cast<const int32_t*>(indices->data);
+    for (int d = 0; d < 3; ++d) {
+        p.idx_ne[d] = ix.ne[d];
+        p.idx_st[d] = (int64_t)ix.st[d];
+    }
+    p.cols = src->ne[0];
+    p.rows = src->ne[1];
+    p.batches = src->ne[2];
+    p.row_bytes = row_bytes;
+    p.dst_rows = ix.count;
+    if (t == EMEL_DTYPE_F32) {
+        for (int d = 0; d < 4; ++d) fs[d] = cs.nb[d];
+        for (int d = 0; d < 4; ++d) p.src_st[d] = (int64_t)fs[d];
+        p.vec = p.cols % 4 == 0 && (da & 15u) == 0;
+    } else if (t == EMEL_DTYPE_F16 || t == EMEL_DTYPE_BF16) {
+        for (int d = 0; d < 4; ++d) p.src_st[d] = (int64_t)hs[d];
+        p.vec = hs[0] == 2 && p.cols % 8 == 0 && (da & 15u) == 0;
+    }
+    char* ws = static_cast<char*>(ctx->workspace);
+    p.flag = reinterpret_cast<uint32_t*>(ws + emel::kCallFlagOffset);
+    p.reject = reinterpret_cast<uint32_t*>(ws + emel::kRejectWordOffset);
+    p.reject_code = EMEL_CUDA_INDEX_OUT_OF_BOUNDS;
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = emel::launch_get_rows(env_of(ctx, stream), p);
     return device_status(ctx, err);
 }
 

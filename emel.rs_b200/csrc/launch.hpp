@@ -61,6 +61,33 @@ constexpr int f16_table_slot(int op) { return op < 64 ? op : 22 + (op - 64); }
 // Bytes of workspace the whole-tensor reductions need.
 uint64_t reduction_workspace_bytes(int sm_count);
 
+// Row gather (getrows.cu).
+enum GatherKind : int { kGatherF32 = 0, kGatherF16 = 1, kGatherBF16 = 2, kGatherQ4_0 = 3, kGatherQ8_0 = 4, kGatherQ4_K = 5 };
+
+// Workspace header words of the index guard: the context's sticky rejected
+// status (reported by emel_cuda_stream_synchronize) and one call's flag.
+constexpr uint64_t kRejectWordOffset = 72;
+constexpr uint64_t kCallFlagOffset = 80;
+
+struct GatherPlan {
+    int kind;
+    bool vec;               // F32 / F16 / BF16: rows may move as 16-byte vectors
+    const char* src;
+    float* dst;             // dense [cols, dst_rows]
+    const int32_t* idx;
+    uint64_t idx_ne[3];
+    int64_t idx_st[3];      // elements
+    uint64_t cols, rows, batches;
+    int64_t src_st[4];      // bytes (F32: dims 1..3 used; F16 / BF16: all four)
+    uint64_t row_bytes;     // quantized rows
+    uint64_t dst_rows;      // number of indices
+    uint32_t* flag;
+    uint32_t* reject;
+    uint32_t reject_code;
+};
+
+cudaError_t launch_get_rows(const LaunchEnv& env, const GatherPlan& plan);
+
 // Peer exchange over NVLink (exchange.cu).  Every rank owns one buffer of
 // kExchangeHeaderBytes flag words (flag r = the last epoch rank r published
 // into this buffer) followed by two banks (epoch parity) of kExchangeMaxRanks

@@ -42,9 +42,13 @@ extern "C" {
 enum emel_cuda_dtype {
     EMEL_DTYPE_F32 = 0,
     EMEL_DTYPE_F16 = 1,
+    EMEL_DTYPE_Q4_0 = 2,  /* packed blocks: ne[0] values, nb[0] == 1 (byte rows) */
+    EMEL_DTYPE_Q8_0 = 8,
+    EMEL_DTYPE_Q4_K = 12,
     EMEL_DTYPE_I32 = 26,
     EMEL_DTYPE_I64 = 27,
-    EMEL_DTYPE_F64 = 28
+    EMEL_DTYPE_F64 = 28,
+    EMEL_DTYPE_BF16 = 30
 };
 
 /* One status per reference error variant: BinaryError (binary.rs:20-29),
@@ -61,6 +65,8 @@ typedef enum emel_cuda_status {
     EMEL_CUDA_INVALID_SHAPE = 6,      /* Error::InvalidShape (generic envelope, actor.rs:88-90) */
     EMEL_CUDA_UNSUPPORTED_OPERATION = 7, /* Error::UnsupportedOperation (actor.rs:92) */
     EMEL_CUDA_INVALID_LAYOUT = 8,     /* ShapeError::InvalidLayout (shape.rs:30-31) */
+    EMEL_CUDA_INDEX_OUT_OF_BOUNDS = 9, /* GetRowsError::IndexOutOfBounds (get_rows.rs:522-535) */
+    EMEL_CUDA_UNSUPPORTED_SOURCE_STRIDE = 10, /* GetRowsError::UnsupportedSourceStride */
     EMEL_CUDA_DEVICE_ERROR = 16,      /* a CUDA runtime call failed */
     EMEL_CUDA_TIMEOUT = 17,           /* a bounded device wait expired */
     EMEL_CUDA_INVALID_ARGUMENT = 18,  /* null context / output pointer */
@@ -141,7 +147,10 @@ EMEL_CUDA_API emel_cuda_status emel_cuda_stream_create(emel_cuda_context* ctx, v
 EMEL_CUDA_API emel_cuda_status emel_cuda_stream_destroy(emel_cuda_context* ctx, void* stream);
 /* Waits for the stream.  Returns EMEL_CUDA_TIMEOUT (once) when a kernel of
  * this context gave up a bounded device wait since the last call; the
- * outputs of the work enqueued since then are unspecified. */
+ * outputs of the work enqueued since then are unspecified.  Otherwise
+ * returns (once) the status of a request the device rejected since the last
+ * call (emel_cuda_get_rows: EMEL_CUDA_INDEX_OUT_OF_BOUNDS; that request wrote
+ * nothing). */
 EMEL_CUDA_API emel_cuda_status emel_cuda_stream_synchronize(emel_cuda_context* ctx, void* stream);
 /* Number of kernels this context has launched (all entry points; a graph
  * replay counts the kernels it contains). */
@@ -321,6 +330,27 @@ EMEL_CUDA_API emel_cuda_status emel_cuda_argmax_combine(const emel_cuda_argmax_p
  * [1, ne1, ne2, ne3], dtype F32, I32 or I64; the index is the column. */
 EMEL_CUDA_API emel_cuda_status emel_cuda_argmax_rows(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
                                        const emel_tensor_view* dst);
+
+/* ---- row gather --------------------------------------------------------- */
+/* get_rows::{OpGetRows, OpGetRowsF16, OpGetRowsBf16, OpGetRowsQ4_0,
+ * OpGetRowsQ8_0, OpGetRowsQ4K} (get_rows.rs:219-512) in one entry point,
+ * chosen by src->dtype (F32, F16, BF16, Q4_0, Q8_0, Q4_K): dst row r (dense
+ * F32 [ne0, i0, i1, i2]) is source row indices[r] of source batch (i1, i2),
+ * decoded to f32 (loops get_rows.rs:1453-1800; decoders quant.rs:106-205,
+ * quant_more.rs:438-468; F16 bits as f16_matmul.rs:508-532).  indices: an I32
+ * view with ne[3] == 1 (IndexView, get_rows.rs:44-215; nb[0] == 0 selects
+ * contiguous strides).  Guards in the reference's order: INVALID_VIEW,
+ * SHAPE_MISMATCH, UNSUPPORTED_SOURCE_STRIDE (F32 source nb[0] not 0 and
+ * not a multiple of 4), then INDEX_OUT_OF_BOUNDS.  The index guard runs on
+ * the device (the indices are device memory): when an index is outside
+ * [0, ne1) the call still returns OK, nothing is written, and the next
+ * emel_cuda_stream_synchronize on the context returns
+ * EMEL_CUDA_INDEX_OUT_OF_BOUNDS (once).  No indices: a no-op after the
+ * view and shape guards.  Device additions: element-aligned pointers
+ * (4 bytes for F32 data and row strides, 2 for F16 / BF16 / packed),
+ * else EMEL_CUDA_INVALID_ARGUMENT. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_get_rows(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                                  const emel_tensor_view* indices, const emel_tensor_view* dst);
 
 /* ---- shape copies ----------------------------------------------------- */
 /* shape::OpCpy (shape.rs:55-69; guards 453-466, loop copy_view 438-444):

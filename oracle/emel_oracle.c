@@ -610,6 +610,324 @@ int oracle_cpy(const oracle_view* src, const oracle_view* dst) { return shape_co
 int oracle_cont(const oracle_view* src, const oracle_view* dst) { return shape_copy(src, dst, 1); }
 
 /* ---------------------------------------------------------------------- */
+/* Row gather: get_rows.rs (F32, F16, BF16, Q4_0, Q8_0, Q4_K sources)      */
+/* ---------------------------------------------------------------------- */
+
+enum { DT_Q4_0 = 2, DT_Q8_0 = 8, DT_Q4_K = 12, DT_BF16 = 30 };
+
+typedef struct {
+    const int32_t* data;
+    uint64_t ne[3];
+    uint64_t st[3]; /* element strides */
+    uint64_t count;
+    int valid;
+} gr_index;
+
+/* IndexView::with_strides (get_rows.rs:44-139, 180-215): an I32 view with
+ * ne[3] == 1; nb[0] == 0 selects the implicit contiguous strides. */
+static gr_index gr_index_view(const oracle_view* v) {
+    gr_index x;
+    memset(&x, 0, sizeof x);
+    if (v == NULL || v->dtype != DT_I32 || v->ne[3] != 1) return x;
+    x.data = (const int32_t*)v->data;
+    const uint64_t len = v->storage_bytes / 4;
+    uint64_t bs[3];
+    int strides_valid = 1, shape_valid = 1, zero = 0;
+    const int implicit = v->nb[0] == 0;
+    if (implicit) {
+        bs[0] = 4;
+        for (int d = 1; d < 3; ++d)
+            if (__builtin_mul_overflow(bs[d - 1], v->ne[d - 1], &bs[d])) {
+                strides_valid = 0;
+                bs[d] = 0;
+            }
+    } else {
+        for (int d = 0; d < 3; ++d) bs[d] = v->nb[d];
+    }
+    uint64_t count = 1;
+    for (int d = 0; d < 3; ++d) {
+        x.ne[d] = v->ne[d];
+        if (v->ne[d] > 1 && bs[d] == 0 && !implicit) strides_valid = 0;
+        if (bs[d] != 0 && (bs[d] < 4 || bs[d] % 4 != 0)) strides_valid = 0;
+        x.st[d] = bs[d] / 4;
+        if (v->ne[d] == 0) zero = 1;
+        else if (!zero && __builtin_mul_overflow(count, v->ne[d], &count)) {
+            shape_valid = 0;
+            count = 0;
+        }
+    }
+    if (zero) count = 0;
+    int span = 1;
+    if (!zero) {
+        u128 max_offset = 0;
+        for (int d = 0; d < 3; ++d) max_offset += (u128)(v->ne[d] - 1) * (u128)bs[d];
+        span = max_offset + 4 <= (u128)len * 4;
+    }
+    x.count = count;
+    x.valid = strides_valid && shape_valid && span;
+    return x;
+}
+
+static int32_t gr_index_read(const gr_index* x, uint64_t ordinal) {
+    const uint64_t i0 = ordinal % x->ne[0], rem = ordinal / x->ne[0];
+    const uint64_t i1 = rem % x->ne[1], i2 = rem / x->ne[1];
+    return x->data[i0 * x->st[0] + i1 * x->st[1] + i2 * x->st[2]];
+}
+
+/* shape_valid (get_rows.rs:1045-1054) and its per-dtype copies */
+static int gr_shape_valid(const oracle_view* src, const gr_index* x, const oracle_view* dst) {
+    return src->ne[0] > 0 && src->ne[1] > 0 && dst->ne[0] == src->ne[0] && dst->ne[1] == x->ne[0] &&
+           dst->ne[2] == x->ne[1] && dst->ne[3] == x->ne[2] && src->ne[2] == x->ne[1] && src->ne[3] == x->ne[2];
+}
+
+/* indices_valid (get_rows.rs:1254-1265): 0 <= row < src.ne[1] */
+static int gr_indices_valid(const gr_index* x, uint64_t rows) {
+    for (uint64_t o = 0; o < x->count; ++o) {
+        const int32_t r = gr_index_read(x, o);
+        if (r < 0 || (uint64_t)r >= rows) return 0;
+    }
+    return 1;
+}
+
+/* empty_index_source_valid (get_rows.rs:1000-1022) */
+static int gr_empty_f32_source_valid(const oracle_view* v) {
+    if (v->dtype != DT_F32 || v->ne[0] == 0 || v->ne[1] == 0 || (v->nb[0] != 0 && v->nb[0] != 4)) return 0;
+    if (v->nb[0] != 0)
+        for (int d = 0; d < 4; ++d)
+            if (v->ne[d] > 1 && v->nb[d] == 0) return 0;
+    return 1;
+}
+
+/* destination_valid (get_rows.rs:1024-1031) */
+static int gr_destination_valid(const oracle_view* dst, uint64_t count) {
+    if (count == 0) return dst->dtype == DT_F32 && dense_contiguous_f32(dst);
+    return validate_as(dst, DT_F32, 0, NULL) && dense_contiguous_f32(dst);
+}
+
+/* F16View::validate (f16_matmul.rs:45-85) / Bf16View::validate (get_rows.rs:300-340) */
+static int gr_half_view_valid(const oracle_view* v, uint32_t dtype) {
+    if (v->dtype != dtype) return 0;
+    uint64_t count;
+    if (!element_count(v, &count)) return 0;
+    uint64_t s[4];
+    if (v->nb[0] != 0) {
+        for (int d = 0; d < 4; ++d) s[d] = v->nb[d];
+    } else {
+        s[0] = 2;
+        for (int d = 1; d < 4; ++d)
+            if (__builtin_mul_overflow(s[d - 1], v->ne[d - 1], &s[d])) return 0;
+    }
+    for (int d = 0; d < 4; ++d) {
+        if (dtype == DT_F16) {
+            if (v->ne[d] > 1 && (s[d] < 2 || s[d] % 2 != 0)) return 0;
+        } else if (v->nb[0] != 0) {
+            if ((v->ne[d] > 1 && v->nb[d] == 0) || (v->nb[d] != 0 && (v->nb[d] < 2 || v->nb[d] % 2 != 0))) return 0;
+        }
+    }
+    u128 max_offset = 0;
+    for (int d = 0; d < 4; ++d) max_offset += (u128)(v->ne[d] - 1) * (u128)s[d];
+    return max_offset + 2 <= (u128)(v->storage_bytes / 2) * 2;
+}
+
+/* PackedRowView::validate (tensor_view.rs:483-526) */
+static int gr_packed_view_valid(const oracle_view* v, uint32_t code, uint64_t block_values, uint64_t block_bytes) {
+    if (v->dtype != code) return 0;
+    for (int d = 0; d < 4; ++d)
+        if (v->ne[d] == 0) return 0;
+    if (v->ne[0] % block_values != 0 || v->nb[0] != 1) return 0;
+    uint64_t row_bytes, s2, s3;
+    if (__builtin_mul_overflow(v->ne[0] / block_values, block_bytes, &row_bytes)) return 0;
+    if (__builtin_mul_overflow(row_bytes, v->ne[1], &s2)) return 0;
+    if (__builtin_mul_overflow(s2, v->ne[2], &s3)) return 0;
+    if (row_bytes == 0 || v->nb[1] != row_bytes || v->nb[2] != s2 || v->nb[3] != s3) return 0;
+    u128 max_offset = 0;
+    for (int d = 1; d < 4; ++d) max_offset += (u128)(v->ne[d] - 1) * (u128)v->nb[d];
+    return max_offset + row_bytes <= (u128)v->storage_bytes;
+}
+
+/* f16_to_f32 (f16_matmul.rs:508-532): exact, NaN payload kept as is */
+static float gr_f16_bits_to_f32(uint16_t h) {
+    const uint32_t sign = (uint32_t)(h & 0x8000u) << 16;
+    const uint32_t e = (h >> 10) & 0x1fu, f = h & 0x3ffu;
+    uint32_t bits;
+    if (e == 0) {
+        if (f == 0) {
+            bits = sign;
+        } else {
+            uint32_t n = f, shift = 0;
+            while ((n & 0x400u) == 0) {
+                n <<= 1;
+                ++shift;
+            }
+            bits = sign | ((127u - (14u + shift)) << 23) | ((n & 0x3ffu) << 13);
+        }
+    } else if (e == 0x1f) {
+        bits = sign | 0x7f800000u | (f << 13);
+    } else {
+        bits = sign | ((e + 112u) << 23) | (f << 13);
+    }
+    float r;
+    memcpy(&r, &bits, 4);
+    return r;
+}
+
+/* fp16_to_f32 (quant.rs:287-302), the magic-number conversion, in binary32
+ * arithmetic as written (a NaN comes out of the multiply quietened). */
+static float gr_quant_fp16_to_f32(uint16_t h) {
+    const uint32_t word = (uint32_t)h << 16;
+    const uint32_t sign = word & 0x80000000u;
+    const uint32_t doubled = word + word;
+    uint32_t a = (doubled >> 4) + (0xe0u << 23), b = 0x07800000u, c = (doubled >> 17) | (126u << 23);
+    float fa, fb, fc;
+    memcpy(&fa, &a, 4);
+    memcpy(&fb, &b, 4);
+    memcpy(&fc, &c, 4);
+    const float normalized = fa * fb;
+    const float denormalized = fc - 0.5f;
+    uint32_t nbits, dbits;
+    memcpy(&nbits, &normalized, 4);
+    memcpy(&dbits, &denormalized, 4);
+    const uint32_t bits = doubled < (1u << 27) ? (sign | dbits) : (sign | nbits);
+    float r;
+    memcpy(&r, &bits, 4);
+    return r;
+}
+
+static uint16_t gr_le16(const uint8_t* p) { return (uint16_t)(p[0] | (p[1] << 8)); }
+
+/* Q4_0Row::decode_block (quant.rs:106-134) */
+static void gr_q4_0_block(const uint8_t* b, float* out) {
+    const float scale = gr_quant_fp16_to_f32(gr_le16(b));
+    for (int i = 0; i < 16; ++i) {
+        const uint8_t p = b[i + 2];
+        out[i] = ((float)(p & 0x0f) - 8.0f) * scale;
+        out[i + 16] = ((float)(p >> 4) - 8.0f) * scale;
+    }
+}
+
+/* Q8_0Row::decode_block (quant.rs:178-205) */
+static void gr_q8_0_block(const uint8_t* b, float* out) {
+    const float scale = gr_quant_fp16_to_f32(gr_le16(b));
+    for (int i = 0; i < 32; ++i) out[i] = (float)(int8_t)b[i + 2] * scale;
+}
+
+/* q4_k_scale_min (quant_more.rs:952-961) */
+static void gr_q4_k_scale_min(int j, const uint8_t* q, uint8_t* sc, uint8_t* m) {
+    if (j < 4) {
+        *sc = q[j] & 0x3f;
+        *m = q[j + 4] & 0x3f;
+    } else {
+        *sc = (uint8_t)((q[j + 4] & 0x0f) | ((q[j - 4] >> 6) << 4));
+        *m = (uint8_t)((q[j + 4] >> 4) | ((q[j] >> 6) << 4));
+    }
+}
+
+/* Q4KRow::decode_block (quant_more.rs:438-468) */
+static void gr_q4_k_block(const uint8_t* b, float* out) {
+    const float scale = gr_quant_fp16_to_f32(gr_le16(b));
+    const float minimum = gr_quant_fp16_to_f32(gr_le16(b + 2));
+    const uint8_t* scales = b + 4;
+    for (int g = 0; g < 4; ++g) {
+        uint8_t sa, ma, sb, mb;
+        gr_q4_k_scale_min(2 * g, scales, &sa, &ma);
+        gr_q4_k_scale_min(2 * g + 1, scales, &sb, &mb);
+        const float d0 = scale * (float)sa, d1 = scale * (float)sb;
+        const float m0 = minimum * (float)ma, m1 = minimum * (float)mb;
+        const uint8_t* q = b + 16 + 32 * g;
+        for (int l = 0; l < 32; ++l) {
+            out[64 * g + l] = d0 * (float)(q[l] & 0x0f) - m0;
+            out[64 * g + 32 + l] = d1 * (float)(q[l] >> 4) - m1;
+        }
+    }
+}
+
+/* One entry point for every source type (the reference has one event per
+ * type: OpGetRows, OpGetRowsF16, OpGetRowsBf16, OpGetRowsQ4_0, OpGetRowsQ8_0,
+ * OpGetRowsQ4K); guards in each event's order, then the gather loops of
+ * get_rows.rs:1453-1800. */
+int oracle_get_rows(const oracle_view* src, const oracle_view* indices, const oracle_view* dst) {
+    if (src == NULL || indices == NULL || dst == NULL) return ORACLE_INVALID_VIEW;
+    const gr_index ix = gr_index_view(indices);
+    const uint32_t t = src->dtype;
+    uint64_t bv = 0, bb = 0;
+    int views;
+    if (t == DT_F32) {
+        views = ix.valid && (ix.count == 0 ? gr_empty_f32_source_valid(src) : validate_as(src, DT_F32, 1, NULL)) &&
+                gr_destination_valid(dst, ix.count);
+    } else if (t == DT_F16 || t == DT_BF16) {
+        views = ix.valid && gr_half_view_valid(src, t) && validate_as(dst, DT_F32, 0, NULL) &&
+                dense_contiguous_f32(dst);
+    } else if (t == DT_Q4_0 || t == DT_Q8_0 || t == DT_Q4_K) {
+        bv = t == DT_Q4_K ? 256 : 32;
+        bb = t == DT_Q4_0 ? 18 : (t == DT_Q8_0 ? 34 : 144);
+        views = ix.valid && gr_packed_view_valid(src, t, bv, bb) &&
+                (ix.count == 0 ? dense_contiguous_f32(dst) : (validate_as(dst, DT_F32, 0, NULL) && dense_contiguous_f32(dst))) &&
+                dst->dtype == DT_F32;
+    } else {
+        return ORACLE_INVALID_VIEW;
+    }
+    if (!views) return ORACLE_INVALID_VIEW;
+    if (!gr_shape_valid(src, &ix, dst)) return ORACLE_SHAPE_MISMATCH;
+    if (t == DT_F32 && !(src->nb[0] == 0 || (src->nb[0] >= 4 && src->nb[0] % 4 == 0)))
+        return ORACLE_UNSUPPORTED_SOURCE_STRIDE;
+    if (!gr_indices_valid(&ix, src->ne[1])) return ORACLE_INDEX_OUT_OF_BOUNDS;
+    if (ix.count == 0) return ORACLE_OK;
+
+    const uint64_t cols = src->ne[0], rows = src->ne[1], batches = src->ne[2];
+    float* out = (float*)dst->data;
+    uint64_t s[4] = {0, 0, 0, 0};
+    if (t == DT_F32) effective_strides(src, 4, s);
+    if (t == DT_F16 || t == DT_BF16) {
+        if (src->nb[0] != 0) {
+            for (int d = 0; d < 4; ++d) s[d] = src->nb[d];
+        } else {
+            s[0] = 2;
+            for (int d = 1; d < 4; ++d) s[d] = s[d - 1] * src->ne[d - 1];
+        }
+    }
+    float block[256];
+    uint64_t dst_row = 0;
+    for (uint64_t i2 = 0; i2 < ix.ne[2]; ++i2)
+        for (uint64_t i1 = 0; i1 < ix.ne[1]; ++i1)
+            for (uint64_t i0 = 0; i0 < ix.ne[0]; ++i0, ++dst_row) {
+                const uint64_t index = (uint64_t)gr_index_read(&ix, dst_row);
+                float* o = out + dst_row * cols;
+                if (t == DT_F32) {
+                    /* read_row_contiguous (tensor_view.rs:756-769): columns 4 bytes apart */
+                    const char* base = (const char*)src->data + index * s[1] + i1 * s[2] + i2 * s[3];
+                    memcpy(o, base, cols * 4);
+                } else if (t == DT_F16 || t == DT_BF16) {
+                    /* F16View / Bf16View read of ordinal ((i2 * ne2 + i1) * rows + index) * cols + c */
+                    const uint64_t first = ((i2 * batches + i1) * rows + index) * cols;
+                    for (uint64_t c = 0; c < cols; ++c) {
+                        uint64_t rem = first + c, off = 0;
+                        for (int d = 0; d < 4; ++d) {
+                            off += (rem % src->ne[d]) * s[d];
+                            rem /= src->ne[d];
+                        }
+                        const uint16_t h = *(const uint16_t*)((const char*)src->data + off);
+                        if (t == DT_F16) {
+                            o[c] = gr_f16_bits_to_f32(h);
+                        } else {
+                            const uint32_t bits = (uint32_t)h << 16;
+                            memcpy(&o[c], &bits, 4);
+                        }
+                    }
+                } else {
+                    const uint64_t row_bytes = cols / bv * bb;
+                    const uint8_t* r = (const uint8_t*)src->data + ((i2 * batches + i1) * rows + index) * row_bytes;
+                    for (uint64_t blk = 0; blk < cols / bv; ++blk) {
+                        if (t == DT_Q4_0) gr_q4_0_block(r + blk * bb, block);
+                        else if (t == DT_Q8_0) gr_q8_0_block(r + blk * bb, block);
+                        else gr_q4_k_block(r + blk * bb, block);
+                        memcpy(o + blk * bv, block, bv * 4);
+                    }
+                }
+            }
+    return ORACLE_OK;
+}
+
+/* ---------------------------------------------------------------------- */
 /* Row normalisation: normalization.rs                                     */
 /* ---------------------------------------------------------------------- */
 

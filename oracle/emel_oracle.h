@@ -48,6 +48,8 @@ enum {
     ORACLE_INVALID_SHAPE = 6,
     ORACLE_UNSUPPORTED_OPERATION = 7,
     ORACLE_INVALID_LAYOUT = 8,
+    ORACLE_INDEX_OUT_OF_BOUNDS = 9,
+    ORACLE_UNSUPPORTED_SOURCE_STRIDE = 10,
     ORACLE_INVALID_ARGUMENT = 18
 };
 
@@ -64,6 +66,10 @@ int oracle_scale(const oracle_view* src, const oracle_view* dst, float scale);
 int oracle_clamp(const oracle_view* src, const oracle_view* dst, float lo, float hi);
 int oracle_leaky_relu(const oracle_view* src, const oracle_view* dst, float slope);
 int oracle_silu_back(const oracle_view* src, const oracle_view* grad, const oracle_view* dst);
+/* get_rows.rs: every source type through one entry point (src dtype F32,
+ * F16, BF16 30, Q4_0 2, Q8_0 8, Q4_K 12; indices I32 with ne[3] == 1; dst
+ * dense F32). */
+int oracle_get_rows(const oracle_view* src, const oracle_view* indices, const oracle_view* dst);
 /* shape.rs OpCpy / OpCont. */
 int oracle_cpy(const oracle_view* src, const oracle_view* dst);
 int oracle_cont(const oracle_view* src, const oracle_view* dst);

@@ -107,6 +107,7 @@ def load(cr=False):
         "oracle_add1": [P, P, ctypes.c_float],
         "oracle_copy": [P, P],
         "oracle_cpy": [P, P],
+        "oracle_get_rows": [P, P, P],
         "oracle_cont": [P, P],
         "oracle_norm": [P, P, ctypes.c_float],
         "oracle_rms_norm": [P, P, ctypes.c_float],
