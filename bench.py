@@ -602,6 +602,28 @@ def run_suite(args):
                 lambda k, subop=subop: (lambda: chk(lib.emel_cuda_glu(
                     ctx.handle, sh, subop, ctypes.c_void_p(tin[k].data_ptr()), 2 * W.GLU_N,
                     ctypes.c_void_p(tout[k].data_ptr()), W.GLU_N))), sets)
+    del tin, tout
+    # row gather (get_rows.rs): 8192 token rows of a [4096, 32000] table
+    spec = W.emb_spec()
+    tok = torch.from_numpy(W.emb_tokens()).to(dev)
+    vidx = view(tok, [W.EMB_TOKENS, 1, 1, 1], code=26)
+    for fmt, o in zip(W.EMB_FORMATS, spec.ops):
+        if only and o.name not in only:
+            continue
+        data, ne, nb, code = W.emb_table(fmt)
+        ttab = torch.from_numpy(data).to(dev)
+        vtab = pkg.CView()
+        vtab.data, vtab.storage_bytes, vtab.dtype = ttab.data_ptr(), ttab.numel(), code
+        for d in range(4):
+            vtab.ne[d], vtab.nb[d] = ne[d], nb[d]
+        sets = sets_for(o.bytes)
+        touts = [torch.empty(W.EMB_TOKENS * W.EMB_COLS, device=dev) for _ in range(sets)]
+        vouts = [view(t, [W.EMB_COLS, W.EMB_TOKENS, 1, 1]) for t in touts]
+        measure("get_rows", o.name, o.bytes, o.elements,
+                lambda k, vtab=vtab, vouts=vouts: (lambda: chk(lib.emel_cuda_get_rows(
+                    ctx.handle, sh, B(vtab), B(vidx), B(vouts[k])))), sets)
+        chk(lib.emel_cuda_stream_synchronize(ctx.handle, sh))
+        del ttab, touts
     return out
 
 

@@ -77,46 +77,63 @@ __device__ __forceinline__ float half_value(uint16_t h) {
 
 // ---- F32 / F16 / BF16 ---------------------------------------------------------
 template <int KIND>
+__device__ __forceinline__ void half_store8(float* out, uint64_t v, uint4 u) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+    float f[8];
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        f[2 * k] = half_value<KIND>((uint16_t)(w[k] & 0xffffu));
+        f[2 * k + 1] = half_value<KIND>((uint16_t)(w[k] >> 16));
+    }
+    __stcs(reinterpret_cast<float4*>(out) + 2 * v, make_float4(f[0], f[1], f[2], f[3]));
+    __stcs(reinterpret_cast<float4*>(out) + 2 * v + 1, make_float4(f[4], f[5], f[6], f[7]));
+}
+
+template <int KIND>
 __global__ void __launch_bounds__(kGatherThreads) gather_plain(GatherPlan p) {
+    constexpr int U = 4;  // 16-byte loads in flight per thread
     pdl_enter();
     if (*reinterpret_cast<volatile uint32_t*>(p.flag) != 0u) return;
     const uint64_t cols = p.cols;
-    for (uint64_t r = blockIdx.x; r < p.dst_rows; r += gridDim.x) {
+    uint64_t r = blockIdx.x;
+    int32_t next = r < p.dst_rows ? index_of(p, r) : 0;
+    for (; r < p.dst_rows; r += gridDim.x) {
         uint64_t i1, i2;
         row_coords(p, r, i1, i2);
-        const uint64_t index = (uint64_t)index_of(p, r);
+        const uint64_t index = (uint64_t)next;
+        if (r + gridDim.x < p.dst_rows) next = index_of(p, r + gridDim.x);  // in flight during this row
         const char* row = p.src + index * p.src_st[1] + i1 * p.src_st[2] + i2 * p.src_st[3];
         float* out = p.dst + r * cols;
-        if constexpr (KIND == kGatherF32) {
-            // read_row_contiguous (tensor_view.rs:756-769): columns 4 bytes apart
-            const float* in = reinterpret_cast<const float*>(row);
-            if (p.vec && (reinterpret_cast<uintptr_t>(in) & 15u) == 0) {
-                const uint64_t nv = cols / 4;
-                for (uint64_t v = threadIdx.x; v < nv; v += kGatherThreads)
-                    __stcs(reinterpret_cast<float4*>(out) + v, __ldcs(reinterpret_cast<const float4*>(in) + v));
-            } else {
-                for (uint64_t c = threadIdx.x; c < cols; c += kGatherThreads) out[c] = in[c];
-            }
-        } else {
-            if (p.vec && (reinterpret_cast<uintptr_t>(row) & 15u) == 0) {
-                // 8 halves per 16-byte load, two 16-byte stores
-                const uint64_t nv = cols / 8;
-                for (uint64_t v = threadIdx.x; v < nv; v += kGatherThreads) {
-                    const uint4 u = __ldcs(reinterpret_cast<const uint4*>(row) + v);
-                    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
-                    float f[8];
+        const bool vec = p.vec && (reinterpret_cast<uintptr_t>(row) & 15u) == 0;
+        if (vec) {
+            // F32: 4 floats per vector (read_row_contiguous, tensor_view.rs:756-769:
+            // columns 4 bytes apart); F16 / BF16: 8 halves per vector
+            const uint64_t nv = KIND == kGatherF32 ? cols / 4 : cols / 8;
+            const uint4* in = reinterpret_cast<const uint4*>(row);
+            uint64_t v = threadIdx.x;
+            for (; v + (U - 1) * kGatherThreads < nv; v += U * kGatherThreads) {
+                uint4 q[U];
 #pragma unroll
-                    for (int k = 0; k < 4; ++k) {
-                        f[2 * k] = half_value<KIND>((uint16_t)(w[k] & 0xffffu));
-                        f[2 * k + 1] = half_value<KIND>((uint16_t)(w[k] >> 16));
-                    }
-                    __stcs(reinterpret_cast<float4*>(out) + 2 * v, make_float4(f[0], f[1], f[2], f[3]));
-                    __stcs(reinterpret_cast<float4*>(out) + 2 * v + 1, make_float4(f[4], f[5], f[6], f[7]));
+                for (int k = 0; k < U; ++k) q[k] = __ldcs(in + v + k * kGatherThreads);
+#pragma unroll
+                for (int k = 0; k < U; ++k) {
+                    if constexpr (KIND == kGatherF32)
+                        __stcs(reinterpret_cast<uint4*>(out) + v + k * kGatherThreads, q[k]);
+                    else
+                        half_store8<KIND>(out, v + k * kGatherThreads, q[k]);
                 }
-            } else {
-                for (uint64_t c = threadIdx.x; c < cols; c += kGatherThreads)
-                    out[c] = half_value<KIND>(*reinterpret_cast<const uint16_t*>(row + c * p.src_st[0]));
             }
+            for (; v < nv; v += kGatherThreads) {
+                const uint4 q = __ldcs(in + v);
+                if constexpr (KIND == kGatherF32) __stcs(reinterpret_cast<uint4*>(out) + v, q);
+                else half_store8<KIND>(out, v, q);
+            }
+        } else if constexpr (KIND == kGatherF32) {
+            const float* in = reinterpret_cast<const float*>(row);
+            for (uint64_t c = threadIdx.x; c < cols; c += kGatherThreads) out[c] = in[c];
+        } else {
+            for (uint64_t c = threadIdx.x; c < cols; c += kGatherThreads)
+                out[c] = half_value<KIND>(*reinterpret_cast<const uint16_t*>(row + c * p.src_st[0]));
         }
     }
 }
@@ -140,15 +157,18 @@ struct QuantFormat<kGatherQ4_K> {
 __device__ __forceinline__ uint16_t ld_le16(const unsigned char* b) { return (uint16_t)(b[0] | (b[1] << 8)); }
 
 // Values v .. v + 3 (v % 4 == 0) of the block at `b` (quant.rs:106-134,
-// 178-205; quant_more.rs:438-468, 952-961), in the reference's binary32
-// operation order with the x86 NaN rules.
-template <int KIND>
-__device__ __forceinline__ float4 decode4(const unsigned char* b, int v) {
+// 178-205; quant_more.rs:438-468, 952-961) in the reference's binary32
+// operation order.  EXACT applies the x86 NaN rules to every operation; the
+// plain pass agrees with it on every non-NaN result, so a NaN result is
+// recomputed exactly.
+template <int KIND, bool EXACT>
+__device__ __forceinline__ float4 decode4_as(const unsigned char* b, int v) {
+    using A = Arith<EXACT>;
     float r[4];
     if constexpr (KIND == kGatherQ8_0) {
         const float scale = f16_quant_scale(ld_le16(b));
 #pragma unroll
-        for (int k = 0; k < 4; ++k) r[k] = f_mul((float)(int8_t)b[2 + v + k], scale);
+        for (int k = 0; k < 4; ++k) r[k] = A::mul((float)(int8_t)b[2 + v + k], scale);
     } else if constexpr (KIND == kGatherQ4_0) {
         const float scale = f16_quant_scale(ld_le16(b));
         const bool high = v >= 16;
@@ -156,7 +176,7 @@ __device__ __forceinline__ float4 decode4(const unsigned char* b, int v) {
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             const unsigned q = high ? (b[2 + j + k] >> 4) : (b[2 + j + k] & 0x0fu);
-            r[k] = f_mul(__fsub_rn((float)q, 8.0f), scale);
+            r[k] = A::mul(__fsub_rn((float)q, 8.0f), scale);
         }
     } else {
         const float scale = f16_quant_scale(ld_le16(b));
@@ -173,15 +193,27 @@ __device__ __forceinline__ float4 decode4(const unsigned char* b, int v) {
             sv = (sc[s + 4] & 0x0fu) | ((unsigned)(sc[s - 4] >> 6) << 4);
             mv = (unsigned)(sc[s + 4] >> 4) | ((unsigned)(sc[s] >> 6) << 4);
         }
-        const float d = f_mul(scale, (float)sv), m = f_mul(minimum, (float)mv);
+        const float d = A::mul(scale, (float)sv), m = A::mul(minimum, (float)mv);
         const unsigned char* q = b + 16 + 32 * g + (high ? within - 32 : within);
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
             const unsigned n = high ? (q[k] >> 4) : (q[k] & 0x0fu);
-            r[k] = f_sub(f_mul(d, (float)n), m);
+            r[k] = A::sub(A::mul(d, (float)n), m);
         }
     }
     return make_float4(r[0], r[1], r[2], r[3]);
+}
+
+template <int KIND>
+__device__ __noinline__ float4 decode4_exact(const unsigned char* b, int v) {
+    return decode4_as<KIND, true>(b, v);
+}
+
+template <int KIND>
+__device__ __forceinline__ float4 decode4(const unsigned char* b, int v) {
+    const float4 r = decode4_as<KIND, false>(b, v);
+    if (!(is_nan(r.x) || is_nan(r.y) || is_nan(r.z) || is_nan(r.w))) return r;
+    return decode4_exact<KIND>(b, v);
 }
 
 // Copies `bytes` bytes from global `src` into shared `dst` with the widest
@@ -229,6 +261,19 @@ __global__ void __launch_bounds__(kGatherThreads) gather_quant(GatherPlan p) {
     }
 }
 
+// Resident CTAs per SM of `kernel` (registers decide it): the gather grid
+// is one full wave, so no CTA waits behind the rows of another.
+template <typename K>
+int resident_ctas(K kernel) {
+    static int cached = 0;
+    if (cached == 0) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kGatherThreads, 0) != cudaSuccess || n < 1) n = 1;
+        cached = n;
+    }
+    return cached;
+}
+
 template <typename K>
 cudaError_t launch_pair(const LaunchEnv& env, const GatherPlan& p, K kernel) {
     const uint64_t check_grid = (p.dst_rows + kGatherThreads - 1) / kGatherThreads;
@@ -237,7 +282,7 @@ cudaError_t launch_pair(const LaunchEnv& env, const GatherPlan& p, K kernel) {
     ++*env.launches;
     cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return err;
-    const uint64_t cap = (uint64_t)env.sm_count * 8;
+    const uint64_t cap = (uint64_t)env.sm_count * resident_ctas(kernel);
     err = launch_dependent(kernel, dim3((unsigned)(p.dst_rows < cap ? p.dst_rows : cap)), dim3(kGatherThreads), 0,
                            env.stream, p);
     ++*env.launches;

@@ -203,3 +203,53 @@ def glu_spec():
     # read 2n floats, write n
     return Config("glu", [OpSpec(op, 3 * GLU_N * F32, GLU_N) for op in GLU_OPS])
 
+
+# Row gather (get_rows.rs) -- no configuration in the benchmark set names it;
+# the bench suite gathers 8192 token rows from a [4096, 32000] embedding
+# table stored as F32, F16, BF16, Q8_0, Q4_0 and Q4_K (random block bytes
+# with binary16 scales in [2^-7, 1)).
+EMB_COLS, EMB_ROWS, EMB_TOKENS = 4096, 32000, 8192
+EMB_FORMATS = {"f32": (0, 4, 1, 4), "f16": (1, 2, 1, 2), "bf16": (30, 2, 1, 2),
+               "q8_0": (8, 34, 32, 0), "q4_0": (2, 18, 32, 0), "q4_k": (12, 144, 256, 0)}
+
+
+def emb_row_bytes(fmt):
+    code, unit, per, _ = EMB_FORMATS[fmt]
+    return EMB_COLS // per * unit
+
+
+def emb_table(fmt, seed=11):
+    """Host bytes of the table in `fmt` (uint8 array) and its (ne, nb)."""
+    code, unit, per, elem = EMB_FORMATS[fmt]
+    rng = np.random.default_rng(seed)
+    row_bytes = emb_row_bytes(fmt)
+    if fmt == "f32":
+        data = rng.standard_normal(EMB_COLS * EMB_ROWS).astype(np.float32).view(np.uint8)
+    elif fmt in ("f16", "bf16"):
+        x = rng.standard_normal(EMB_COLS * EMB_ROWS).astype(np.float32)
+        h = x.astype(np.float16).view(np.uint16) if fmt == "f16" else (x.view(np.uint32) >> 16).astype(np.uint16)
+        data = h.view(np.uint8)
+    else:
+        data = rng.integers(0, 256, size=row_bytes * EMB_ROWS, dtype=np.uint32).astype(np.uint8)
+        blocks = data.reshape(-1, unit)
+        scales = rng.integers(0x2000, 0x3c00, size=blocks.shape[0])
+        blocks[:, 0] = scales & 0xff
+        blocks[:, 1] = scales >> 8
+        if fmt == "q4_k":
+            mins = rng.integers(0x2000, 0x3c00, size=blocks.shape[0])
+            blocks[:, 2] = mins & 0xff
+            blocks[:, 3] = mins >> 8
+    ne = [EMB_COLS, EMB_ROWS, 1, 1]
+    nb = [elem if elem else 1, row_bytes, row_bytes * EMB_ROWS, row_bytes * EMB_ROWS]
+    return data, ne, nb, code
+
+
+def emb_tokens(seed=12):
+    return np.random.default_rng(seed).integers(0, EMB_ROWS, size=EMB_TOKENS).astype(np.int32)
+
+
+def emb_spec():
+    # rows read + rows written + the indices
+    return Config("get_rows", [OpSpec(f"get_rows_{fmt}", EMB_TOKENS * (emb_row_bytes(fmt) + EMB_COLS * F32 + 4),
+                                      EMB_TOKENS * EMB_COLS) for fmt in EMB_FORMATS])
+
