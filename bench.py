@@ -624,6 +624,23 @@ def run_suite(args):
                     ctx.handle, sh, B(vtab), B(vidx), B(vouts[k])))), sets)
         chk(lib.emel_cuda_stream_synchronize(ctx.handle, sh))
         del ttab, touts
+    # rotary position embedding (rope.rs) of query rows
+    spec = W.rope_spec()
+    xr, pr_pos = W.rope_inputs()
+    ne_r = list(W.ROPE_NE)
+    sets = sets_for(spec.ops[0].bytes)
+    txr = [torch.from_numpy(xr).to(dev) for _ in range(sets)]
+    tyr = [torch.empty_like(t) for t in txr]
+    tpos = torch.from_numpy(pr_pos).to(dev)
+    vpos = view(tpos, [ne_r[2], 1, 1, 1], code=26)
+    vxr = [view(t, ne_r) for t in txr]
+    vyr = [view(t, ne_r) for t in tyr]
+    for o, mode in zip(spec.ops, (2, 0)):
+        prm = pkg.CRopeParams(n_dims=128, mode=mode, freq_base=10000.0, freq_scale=1.0, ext_factor=0.0,
+                              attn_factor=1.0)
+        measure("rope", o.name, o.bytes, o.elements,
+                lambda k, prm=prm: (lambda: chk(lib.emel_cuda_rope(ctx.handle, sh, B(vxr[k]), B(vpos), B(vyr[k]),
+                                                                     B(prm)))), sets)
     return out
 
 

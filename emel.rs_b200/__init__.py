@@ -50,6 +50,7 @@ class Status(enum.IntEnum):
     INVALID_LAYOUT = 8
     INDEX_OUT_OF_BOUNDS = 9
     UNSUPPORTED_SOURCE_STRIDE = 10
+    INVALID_MODE = 11
     DEVICE_ERROR = 16
     TIMEOUT = 17
     INVALID_ARGUMENT = 18
@@ -114,6 +115,12 @@ class CGenericRequest(ctypes.Structure):
                 ("params", ctypes.c_uint8 * 64), ("params_len", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
 
 
+class CRopeParams(ctypes.Structure):
+    """emel_rope_params: rope::RopeParams (rope.rs:33-48)."""
+    _fields_ = [("n_dims", ctypes.c_int32), ("mode", ctypes.c_int32), ("freq_base", ctypes.c_float),
+                ("freq_scale", ctypes.c_float), ("ext_factor", ctypes.c_float), ("attn_factor", ctypes.c_float)]
+
+
 # Every symbol include/emel_cuda.h declares, with its ctypes signature.
 _P = ctypes.POINTER(CView)
 _V = ctypes.c_void_p
@@ -171,6 +178,7 @@ SIGNATURES = {
     "emel_cuda_argmax_rows": (_I, [_CTX, _V, _P, _P]),
     "emel_cuda_generic": (_I, [_CTX, _V, ctypes.POINTER(CGenericRequest)]),
     "emel_cuda_get_rows": (_I, [_CTX, _V, _P, _P, _P]),
+    "emel_cuda_rope": (_I, [_CTX, _V, _P, _P, _P, ctypes.POINTER(CRopeParams)]),
     "emel_cuda_cpy": (_I, [_CTX, _V, _P, _P]),
     "emel_cuda_cont": (_I, [_CTX, _V, _P, _P]),
     "emel_cuda_glu": (_I, [_CTX, _V, _I, _V, ctypes.c_uint64, _V, ctypes.c_uint64]),
@@ -418,7 +426,10 @@ class Event:
 
 
 def _r(view):
-    return ctypes.byref(view.c()) if view is not None else None
+    """A TensorView (or an already-built CView) as an emel_tensor_view pointer."""
+    if view is None:
+        return None
+    return ctypes.byref(view if isinstance(view, CView) else view.c())
 
 
 @dataclass
@@ -601,6 +612,20 @@ class OpGetRows(Event):
 
     def dispatch(self, ctx, stream):
         return ctx._lib.emel_cuda_get_rows(ctx.handle, stream, _r(self.src), _r(self.indices), _r(self.dst))
+
+
+@dataclass
+class OpRope(Event):
+    """rope::OpRope (rope.rs:135-160); params: CRopeParams or a dict of its fields."""
+    source: TensorView
+    positions: TensorView
+    destination: TensorView
+    params: object
+
+    def dispatch(self, ctx, stream):
+        pr = self.params if isinstance(self.params, CRopeParams) else CRopeParams(**self.params)
+        return ctx._lib.emel_cuda_rope(ctx.handle, stream, _r(self.source), _r(self.positions), _r(self.destination),
+                                       ctypes.byref(pr))
 
 
 @dataclass

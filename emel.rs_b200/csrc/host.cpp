@@ -1113,6 +1113,93 @@ emel_cuda_status emel_cuda_get_rows(emel_cuda_context* ctx, void* stream, const 
     return device_status(ctx, err);
 }
 
+// ---- rotary position embedding (rope.rs) -----------------------------------
+
+static bool rope_positions_valid(const emel_tensor_view* v) {
+    // Layout::validate_i32 (tensor_view.rs:388-447): raw strides, each >= 4 and a multiple of 4
+    if (v == nullptr || v->dtype != EMEL_DTYPE_I32 || v->data == nullptr || v->reserved != 0) return false;
+    uint64_t count = 1;
+    for (int d = 0; d < 4; ++d) {
+        if (v->ne[d] == 0 || __builtin_mul_overflow(count, v->ne[d], &count)) return false;
+        if (v->nb[d] < 4 || v->nb[d] % 4 != 0) return false;
+    }
+    u128 max_offset = 0;
+    for (int d = 0; d < 4; ++d) max_offset += (u128)(v->ne[d] - 1) * (u128)v->nb[d];
+    return max_offset + 4 <= (u128)(v->storage_bytes / 4) * 4;
+}
+
+static bool dense_contiguous_i32(const emel_tensor_view* v) {
+    if (v->dtype != EMEL_DTYPE_I32) return false;
+    uint64_t expected = 4;
+    for (int d = 0; d < 4; ++d) {
+        if (v->nb[d] != expected) return false;
+        if (__builtin_mul_overflow(expected, v->ne[d], &expected)) return false;
+    }
+    return true;
+}
+
+emel_cuda_status emel_cuda_rope(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                const emel_tensor_view* positions, const emel_tensor_view* dst,
+                                const emel_rope_params* params) {
+    if (params == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    Checked cs, cd;
+    // rope.rs:338-440, transitions in order: view, parameters, mode / shape
+    if (src == nullptr || dst == nullptr || !validate_as(src, EMEL_DTYPE_F32, false, &cs) ||
+        !rope_positions_valid(positions) || !validate_as(dst, EMEL_DTYPE_F32, false, &cd))
+        return EMEL_CUDA_INVALID_VIEW;
+    const emel_rope_params pr = *params;
+    const uint64_t cols = src->ne[0];
+    const bool params_ok = pr.n_dims > 0 && pr.n_dims % 2 == 0 && (uint64_t)pr.n_dims <= cols &&
+                           pr.ext_factor == 0.0f && std::isfinite(pr.freq_base) && pr.freq_base > 0.0f &&
+                           std::isfinite(pr.freq_scale) && pr.freq_scale > 0.0f && std::isfinite(pr.attn_factor);
+    if (!params_ok) return EMEL_CUDA_INVALID_PARAMETERS;
+    const bool shape_ok = same_ne(src, dst) && cols > 0 && positions->ne[0] == src->ne[2] && positions->ne[1] == 1 &&
+                          positions->ne[2] == 1 && positions->ne[3] == 1 && src->ne[2] > 0;
+    const bool known = pr.mode == emel::kRopeNorm || pr.mode == emel::kRopeNeox || pr.mode == emel::kRopeTimestep;
+    const bool layout_ok = pr.mode != emel::kRopeTimestep ||
+                           ((uint64_t)pr.n_dims == cols && dense_contiguous_f32(src) &&
+                            dense_contiguous_i32(positions) && dense_contiguous_f32(dst));
+    if (shape_ok && !known) return EMEL_CUDA_INVALID_MODE;
+    if (!shape_ok || !layout_ok) return EMEL_CUDA_SHAPE_MISMATCH;
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    if ((reinterpret_cast<uintptr_t>(src->data) | reinterpret_cast<uintptr_t>(dst->data) |
+         reinterpret_cast<uintptr_t>(positions->data)) & 3u)
+        return EMEL_CUDA_INVALID_ARGUMENT;
+    // the kernel counts a position's (row, pair) items in 32 bits
+    if ((u128)src->ne[1] * (u128)(cols > 2 * 2048 ? 2048 : cols) * 256u >= ((u128)1 << 32)) return EMEL_CUDA_INVALID_ARGUMENT;
+    emel::RopePlan p{};
+    p.mode = pr.mode;
+    p.src = static_cast<const char*>(src->data);
+    p.dst = static_cast<char*>(dst->data);
+    p.positions = static_cast<const char*>(positions->data);
+    p.pos_stride = (int64_t)positions->nb[0];
+    for (int d = 0; d < 4; ++d) {
+        p.src_st[d] = (int64_t)cs.nb[d];
+        p.dst_st[d] = (int64_t)cd.nb[d];
+    }
+    p.cols = cols;
+    p.rows = src->ne[1];
+    p.npos = src->ne[2];
+    p.batches = src->ne[3];
+    p.n_dims = (uint64_t)pr.n_dims;
+    // the two per-operation scalars, with the same libm calls as the reference (rope.rs:536-540, 592)
+    p.theta_scale = powf(pr.freq_base, -2.0f / (float)pr.n_dims);
+    p.neg_log_period = -logf(pr.freq_base);
+    p.freq_scale = pr.freq_scale;
+    p.attn_factor = pr.attn_factor;
+    // 16-byte vectors: unit dim-0 stride, 16-byte aligned row starts, and whole
+    // vectors of pairs (norm: n_dims % 4, neox: (n_dims / 2) % 4; a table
+    // chunk of 2048 pairs keeps both)
+    bool vec = pr.mode != emel::kRopeTimestep && cs.nb[0] == 4 && cd.nb[0] == 4 &&
+               (pr.mode == emel::kRopeNorm ? pr.n_dims % 4 == 0 : (pr.n_dims / 2) % 4 == 0) &&
+               ((reinterpret_cast<uintptr_t>(src->data) | reinterpret_cast<uintptr_t>(dst->data)) & 15u) == 0;
+    for (int d = 1; d < 4; ++d) vec = vec && cs.nb[d] % 16 == 0 && cd.nb[d] % 16 == 0;
+    p.vec = vec;
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = emel::launch_rope(env_of(ctx, stream), p);
+    return device_status(ctx, err);
+}
+
 // ---- gated linear units ------------------------------------------------------
 
 emel_cuda_status emel_cuda_glu(emel_cuda_context* ctx, void* stream, int subop, const float* input,

@@ -88,6 +88,27 @@ struct GatherPlan {
 
 cudaError_t launch_get_rows(const LaunchEnv& env, const GatherPlan& plan);
 
+// Rotary position embedding (rope.cu).
+enum RopeMode : int { kRopeNorm = 0, kRopeNeox = 2, kRopeTimestep = 4 };
+
+struct RopePlan {
+    int mode;
+    bool vec;               // norm / neox on 16-byte aligned unit-stride rows (see emel_cuda_rope)
+    const char* src;
+    char* dst;
+    const char* positions;
+    int64_t pos_stride;     // bytes
+    int64_t src_st[4];      // bytes
+    int64_t dst_st[4];
+    uint64_t cols, rows, npos, batches;
+    uint64_t n_dims;
+    float theta_scale;      // powf(freq_base, -2 / n_dims), from the host
+    float neg_log_period;   // -logf(freq_base), from the host
+    float freq_scale, attn_factor;
+};
+
+cudaError_t launch_rope(const LaunchEnv& env, const RopePlan& plan);
+
 // Peer exchange over NVLink (exchange.cu).  Every rank owns one buffer of
 // kExchangeHeaderBytes flag words (flag r = the last epoch rank r published
 // into this buffer) followed by two banks (epoch parity) of kExchangeMaxRanks

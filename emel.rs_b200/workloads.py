@@ -253,3 +253,20 @@ def emb_spec():
     return Config("get_rows", [OpSpec(f"get_rows_{fmt}", EMB_TOKENS * (emb_row_bytes(fmt) + EMB_COLS * F32 + 4),
                                       EMB_TOKENS * EMB_COLS) for fmt in EMB_FORMATS])
 
+
+# Rotary position embedding (rope.rs) -- no configuration in the benchmark
+# set names it; the suite rotates query rows [128 dims, 32 heads, 4096
+# positions] (N(0, 1) values, positions 0 .. 4095) in neox and norm modes.
+ROPE_NE = (128, 32, 4096, 1)
+
+
+def rope_inputs(seed=13):
+    rng = np.random.default_rng(seed)
+    x = normal(rng, (int(np.prod(ROPE_NE)),), 1.0).astype(np.float32)
+    return x, np.arange(ROPE_NE[2], dtype=np.int32)
+
+
+def rope_spec():
+    n = int(np.prod(ROPE_NE))
+    return Config("rope", [OpSpec(f"rope_{m}", 2 * n * F32 + ROPE_NE[2] * 4, n) for m in ("neox", "norm")])
+

@@ -67,6 +67,7 @@ typedef enum emel_cuda_status {
     EMEL_CUDA_INVALID_LAYOUT = 8,     /* ShapeError::InvalidLayout (shape.rs:30-31) */
     EMEL_CUDA_INDEX_OUT_OF_BOUNDS = 9, /* GetRowsError::IndexOutOfBounds (get_rows.rs:522-535) */
     EMEL_CUDA_UNSUPPORTED_SOURCE_STRIDE = 10, /* GetRowsError::UnsupportedSourceStride */
+    EMEL_CUDA_INVALID_MODE = 11,      /* RopeError::InvalidMode (rope.rs:104-117) */
     EMEL_CUDA_DEVICE_ERROR = 16,      /* a CUDA runtime call failed */
     EMEL_CUDA_TIMEOUT = 17,           /* a bounded device wait expired */
     EMEL_CUDA_INVALID_ARGUMENT = 18,  /* null context / output pointer */
@@ -351,6 +352,33 @@ EMEL_CUDA_API emel_cuda_status emel_cuda_argmax_rows(emel_cuda_context* ctx, voi
  * else EMEL_CUDA_INVALID_ARGUMENT. */
 EMEL_CUDA_API emel_cuda_status emel_cuda_get_rows(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
                                                   const emel_tensor_view* indices, const emel_tensor_view* dst);
+
+/* ---- rotary position embedding ---------------------------------------- */
+/* rope::RopeParams (rope.rs:33-48). */
+typedef struct emel_rope_params {
+    int32_t n_dims;      /* rotated dimensions, even, <= src->ne[0] */
+    int32_t mode;        /* 0 norm, 2 neox, 4 timestep (rope.rs:25-30) */
+    float freq_base;
+    float freq_scale;
+    float ext_factor;    /* must be 0 */
+    float attn_factor;
+} emel_rope_params;
+/* rope::OpRope (rope.rs:135-160) dispatched by RopeKernel::process_event:
+ * src / dst F32 views of equal extents [cols, rows, positions, batches],
+ * positions an I32 view [positions, 1, 1, 1] with explicit strides.
+ * norm / neox rotate pairs (2k, 2k + 1) / (k, k + n_dims / 2) of every row
+ * by theta_k = position * theta_scale^k (a binary32 product chain, theta_scale
+ * = powf(freq_base, -2 / n_dims)) times freq_scale, with cos / sin scaled by
+ * attn_factor and a' = fma(a, c, -(b s)), b' = fma(a, s, b c), and copy
+ * columns n_dims .. cols - 1 (rope.rs:523-583); timestep (n_dims == cols,
+ * dense views) writes the rotated real / imaginary halves (rope.rs:585-646).
+ * Statuses in the reference's transition order: INVALID_VIEW,
+ * INVALID_PARAMETERS, INVALID_MODE (shape valid, unknown mode), SHAPE_MISMATCH
+ * (also timestep without its dense layout); nothing is written then.
+ * Device addition: pointers must be 4-byte aligned (INVALID_ARGUMENT). */
+EMEL_CUDA_API emel_cuda_status emel_cuda_rope(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                              const emel_tensor_view* positions, const emel_tensor_view* dst,
+                                              const emel_rope_params* params);
 
 /* ---- shape copies ----------------------------------------------------- */
 /* shape::OpCpy (shape.rs:55-69; guards 453-466, loop copy_view 438-444):

@@ -928,6 +928,116 @@ int oracle_get_rows(const oracle_view* src, const oracle_view* indices, const or
 }
 
 /* ---------------------------------------------------------------------- */
+/* Rotary position embedding: rope.rs                                      */
+/* ---------------------------------------------------------------------- */
+
+enum { ROPE_NORM = 0, ROPE_NEOX = 2, ROPE_TIMESTEP = 4 };
+
+/* Layout::validate_i32 (tensor_view.rs:388-390 -> 392-447): raw strides
+ * (no implicit form for I32), each >= 4 and a multiple of 4. */
+static int rope_positions_valid(const oracle_view* v) {
+    if (v == NULL || v->dtype != DT_I32) return 0;
+    uint64_t count;
+    if (!element_count(v, &count)) return 0;
+    for (int d = 0; d < 4; ++d)
+        if (v->nb[d] < 4 || v->nb[d] % 4 != 0) return 0;
+    u128 max_offset = 0;
+    for (int d = 0; d < 4; ++d) max_offset += (u128)(v->ne[d] - 1) * (u128)v->nb[d];
+    return max_offset + 4 <= (u128)(v->storage_bytes / 4) * 4;
+}
+
+static int dense_contiguous_i32(const oracle_view* v) {
+    if (v->dtype != DT_I32) return 0;
+    uint64_t expected = 4;
+    for (int d = 0; d < 4; ++d) {
+        if (v->nb[d] != expected) return 0;
+        if (__builtin_mul_overflow(expected, v->ne[d], &expected)) return 0;
+    }
+    return 1;
+}
+
+/* Guards of rope.rs:338-440 in transition order (view, parameters, then
+ * shape / mode / the timestep layout), then execute_rotation (rope.rs:523-
+ * 583) or execute_timestep (rope.rs:585-646).  The dense variants
+ * (rope.rs:477-521) compute the same values.  The per-operation scalars use
+ * the host libm exactly as the reference does: theta_scale =
+ * powf(freq_base, -2 / n_dims) and -logf(freq_base) ((logf) bypasses the
+ * correctly-rounded build's macro: the device library computes these two on
+ * the host with the same calls). */
+int oracle_rope(const oracle_view* src, const oracle_view* positions, const oracle_view* dst,
+                const oracle_rope_params* pr) {
+    uint64_t n;
+    if (!validate_as(src, DT_F32, 0, &n) || !rope_positions_valid(positions) || !validate_as(dst, DT_F32, 0, NULL))
+        return ORACLE_INVALID_VIEW;
+    const uint64_t cols = src->ne[0];
+    const int params_ok = pr->n_dims > 0 && pr->n_dims % 2 == 0 && (uint64_t)pr->n_dims <= cols &&
+                          pr->ext_factor == 0.0f && isfinite(pr->freq_base) && pr->freq_base > 0.0f &&
+                          isfinite(pr->freq_scale) && pr->freq_scale > 0.0f && isfinite(pr->attn_factor);
+    if (!params_ok) return ORACLE_INVALID_PARAMETERS;
+    const int shape_ok = same_ne(src, dst) && cols > 0 && positions->ne[0] == src->ne[2] && positions->ne[1] == 1 &&
+                         positions->ne[2] == 1 && positions->ne[3] == 1 && src->ne[2] > 0;
+    const int mode = pr->mode;
+    const int known = mode == ROPE_NORM || mode == ROPE_NEOX || mode == ROPE_TIMESTEP;
+    const int layout_ok = mode != ROPE_TIMESTEP || ((uint64_t)pr->n_dims == cols && dense_contiguous_f32(src) &&
+                                                    dense_contiguous_i32(positions) && dense_contiguous_f32(dst));
+    if (shape_ok && !known) return ORACLE_INVALID_MODE;
+    if (!shape_ok || !layout_ok) return ORACLE_SHAPE_MISMATCH;
+
+    uint64_t ss[4], sd[4];
+    effective_strides(src, 4, ss);
+    effective_strides(dst, 4, sd);
+    const uint64_t rows = src->ne[1], npos = src->ne[2], batches = src->ne[3];
+    const char* sb = (const char*)src->data;
+    char* db = (char*)dst->data;
+#define ROPE_AT(base, st, c, r, p, b) ((float*)((base) + (c) * (st)[0] + (r) * (st)[1] + (p) * (st)[2] + (b) * (st)[3]))
+    if (mode != ROPE_TIMESTEP) {
+        const uint64_t half = (uint64_t)pr->n_dims / 2;
+        const float theta_scale = powf(pr->freq_base, -2.0f / (float)pr->n_dims);
+        for (uint64_t b = 0; b < batches; ++b)
+            for (uint64_t p = 0; p < npos; ++p) {
+                /* I32View::read_at (rope.rs:85-101): raw strides */
+                const int32_t pos_i = *(const int32_t*)((const char*)positions->data + p * positions->nb[0]);
+                const float position = (float)pos_i;
+                for (uint64_t r = 0; r < rows; ++r) {
+                    float theta = position;
+                    for (uint64_t k = 0; k < half; ++k) {
+                        const float rotated = theta * pr->freq_scale;
+                        const float cosine = cosf(rotated) * pr->attn_factor;
+                        const float sine = sinf(rotated) * pr->attn_factor;
+                        const uint64_t ia = mode == ROPE_NEOX ? k : 2 * k, ib = mode == ROPE_NEOX ? k + half : 2 * k + 1;
+                        const float first = *ROPE_AT(sb, ss, ia, r, p, b), second = *ROPE_AT(sb, ss, ib, r, p, b);
+                        *ROPE_AT(db, sd, ia, r, p, b) = fmaf(first, cosine, -(second * sine));
+                        *ROPE_AT(db, sd, ib, r, p, b) = fmaf(first, sine, second * cosine);
+                        theta *= theta_scale;
+                    }
+                    for (uint64_t c = (uint64_t)pr->n_dims; c < cols; ++c)
+                        *ROPE_AT(db, sd, c, r, p, b) = *ROPE_AT(sb, ss, c, r, p, b);
+                }
+            }
+    } else {
+        const uint64_t half = cols / 2;
+        const float neg_log_period = -(logf)(pr->freq_base);
+        for (uint64_t b = 0; b < batches; ++b)
+            for (uint64_t p = 0; p < npos; ++p) {
+                const float position = (float)((const int32_t*)positions->data)[p];
+                for (uint64_t r = 0; r < rows; ++r)
+                    for (uint64_t k = 0; k < half; ++k) {
+                        const float real = *ROPE_AT(sb, ss, 2 * k, r, p, b), imag = *ROPE_AT(sb, ss, 2 * k + 1, r, p, b);
+                        const float frequency = expf(neg_log_period * (float)k / (float)half);
+                        const float argument = position * frequency * pr->freq_scale;
+                        const float cosine = cosf(argument) * pr->attn_factor;
+                        const float sine = sinf(argument) * pr->attn_factor;
+                        const volatile float rc = real * cosine, is = imag * sine, rs = real * sine, ic = imag * cosine;
+                        *ROPE_AT(db, sd, k, r, p, b) = rc - is;
+                        *ROPE_AT(db, sd, half + k, r, p, b) = rs + ic;
+                    }
+            }
+    }
+#undef ROPE_AT
+    return ORACLE_OK;
+}
+
+/* ---------------------------------------------------------------------- */
 /* Row normalisation: normalization.rs                                     */
 /* ---------------------------------------------------------------------- */
 

@@ -50,6 +50,7 @@ enum {
     ORACLE_INVALID_LAYOUT = 8,
     ORACLE_INDEX_OUT_OF_BOUNDS = 9,
     ORACLE_UNSUPPORTED_SOURCE_STRIDE = 10,
+    ORACLE_INVALID_MODE = 11,
     ORACLE_INVALID_ARGUMENT = 18
 };
 
@@ -66,6 +67,17 @@ int oracle_scale(const oracle_view* src, const oracle_view* dst, float scale);
 int oracle_clamp(const oracle_view* src, const oracle_view* dst, float lo, float hi);
 int oracle_leaky_relu(const oracle_view* src, const oracle_view* dst, float slope);
 int oracle_silu_back(const oracle_view* src, const oracle_view* grad, const oracle_view* dst);
+/* rope.rs RopeParams (rope.rs:33-48) and OpRope. */
+typedef struct oracle_rope_params {
+    int32_t n_dims;
+    int32_t mode;
+    float freq_base;
+    float freq_scale;
+    float ext_factor;
+    float attn_factor;
+} oracle_rope_params;
+int oracle_rope(const oracle_view* src, const oracle_view* positions, const oracle_view* dst,
+                const oracle_rope_params* params);
 /* get_rows.rs: every source type through one entry point (src dtype F32,
  * F16, BF16 30, Q4_0 2, Q8_0 8, Q4_K 12; indices I32 with ne[3] == 1; dst
  * dense F32). */

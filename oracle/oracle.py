@@ -60,6 +60,12 @@ def build():
     subprocess.run(["make", "-s", "-C", str(HERE)], check=True)
 
 
+class RopeParams(ctypes.Structure):
+    """oracle_rope_params / emel_rope_params (rope.rs:33-48)."""
+    _fields_ = [("n_dims", ctypes.c_int32), ("mode", ctypes.c_int32), ("freq_base", ctypes.c_float),
+                ("freq_scale", ctypes.c_float), ("ext_factor", ctypes.c_float), ("attn_factor", ctypes.c_float)]
+
+
 class GenericRequest(ctypes.Structure):
     """oracle_generic_request (same layout as emel_cuda_generic_request)."""
     _fields_ = [("op", ctypes.c_uint32), ("unary_subop", ctypes.c_uint32),
@@ -108,6 +114,7 @@ def load(cr=False):
         "oracle_copy": [P, P],
         "oracle_cpy": [P, P],
         "oracle_get_rows": [P, P, P],
+        "oracle_rope": [P, P, P, ctypes.POINTER(RopeParams)],
         "oracle_cont": [P, P],
         "oracle_norm": [P, P, ctypes.c_float],
         "oracle_rms_norm": [P, P, ctypes.c_float],
