@@ -641,6 +641,21 @@ def run_suite(args):
         measure("rope", o.name, o.bytes, o.elements,
                 lambda k, prm=prm: (lambda: chk(lib.emel_cuda_rope(ctx.handle, sh, B(vxr[k]), B(vpos), B(vyr[k]),
                                                                      B(prm)))), sets)
+    del txr, tyr
+    # vocabulary matvec + argmax (matmul.rs OpMulMatArgmax)
+    spec = W.mv_spec()
+    if not only or spec.ops[0].name in only:
+        lm, rv = W.mv_inputs()
+        tl, tr = torch.from_numpy(lm).to(dev), torch.from_numpy(rv).to(dev)
+        del lm
+        tv = torch.empty(1, device=dev)
+        ti = torch.empty(1, dtype=torch.int32, device=dev)
+        vl, vr, vv = view(tl, [W.MV_K, W.MV_ROWS, 1, 1]), view(tr, [1, W.MV_K, 1, 1]), view(tv, [1, 1, 1, 1])
+        o = spec.ops[0]
+        measure("matvec", o.name, o.bytes, o.elements,
+                lambda k: (lambda: chk(lib.emel_cuda_mul_mat_argmax(ctx.handle, sh, B(vl), B(vr), B(vv),
+                                                                    ctypes.c_void_p(ti.data_ptr())))), 1)
+        del tl, tr
     return out
 
 

@@ -178,6 +178,7 @@ SIGNATURES = {
     "emel_cuda_argmax_rows": (_I, [_CTX, _V, _P, _P]),
     "emel_cuda_generic": (_I, [_CTX, _V, ctypes.POINTER(CGenericRequest)]),
     "emel_cuda_get_rows": (_I, [_CTX, _V, _P, _P, _P]),
+    "emel_cuda_mul_mat_argmax": (_I, [_CTX, _V, _P, _P, _P, _V]),
     "emel_cuda_rope": (_I, [_CTX, _V, _P, _P, _P, ctypes.POINTER(CRopeParams)]),
     "emel_cuda_cpy": (_I, [_CTX, _V, _P, _P]),
     "emel_cuda_cont": (_I, [_CTX, _V, _P, _P]),
@@ -626,6 +627,20 @@ class OpRope(Event):
         pr = self.params if isinstance(self.params, CRopeParams) else CRopeParams(**self.params)
         return ctx._lib.emel_cuda_rope(ctx.handle, stream, _r(self.source), _r(self.positions), _r(self.destination),
                                        ctypes.byref(pr))
+
+
+@dataclass
+class OpMulMatArgmax(Event):
+    """matmul::OpMulMatArgmax (matmul.rs:167-192): lhs [k, m], rhs [1, k],
+    dst [1]; the best row goes to the device int32 at `index_ptr`."""
+    lhs: TensorView
+    rhs: TensorView
+    destination: TensorView
+    index_ptr: int
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_mul_mat_argmax(ctx.handle, stream, _r(self.lhs), _r(self.rhs),
+                                                 _r(self.destination), ctypes.c_void_p(self.index_ptr))
 
 
 @dataclass

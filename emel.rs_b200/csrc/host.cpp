@@ -1200,6 +1200,46 @@ emel_cuda_status emel_cuda_rope(emel_cuda_context* ctx, void* stream, const emel
     return device_status(ctx, err);
 }
 
+// ---- vocabulary matvec + argmax (matmul.rs OpMulMatArgmax, F32) -----------------
+
+emel_cuda_status emel_cuda_mul_mat_argmax(emel_cuda_context* ctx, void* stream, const emel_tensor_view* lhs,
+                                          const emel_tensor_view* rhs, const emel_tensor_view* dst,
+                                          int32_t* index_out) {
+    Checked cl, cr, cd;
+    // argmax_views_valid (matmul.rs:1416-1423)
+    if (lhs == nullptr || rhs == nullptr || dst == nullptr || !validate_as(lhs, EMEL_DTYPE_F32, false, &cl) ||
+        !validate_as(rhs, EMEL_DTYPE_F32, false, &cr) || !validate_as(dst, EMEL_DTYPE_F32, false, &cd) ||
+        !dense_contiguous_f32(lhs) || !dense_contiguous_f32(rhs) || !dense_contiguous_f32(dst))
+        return EMEL_CUDA_INVALID_VIEW;
+    // argmax_shape_valid (matmul.rs:1504-1520): lhs [k, m], rhs [1, k], dst [1]
+    const uint64_t* l = lhs->ne;
+    const uint64_t* r = rhs->ne;
+    const uint64_t* d = dst->ne;
+    if (!(l[0] > 0 && l[1] > 0 && l[2] == 1 && l[3] == 1 && r[0] == 1 && r[1] == l[0] && r[2] == 1 && r[3] == 1 &&
+          d[0] == 1 && d[1] == 1 && d[2] == 1 && d[3] == 1))
+        return EMEL_CUDA_SHAPE_MISMATCH;
+    if (ctx == nullptr || index_out == nullptr || (reinterpret_cast<uintptr_t>(index_out) & 3u) ||
+        ((reinterpret_cast<uintptr_t>(lhs->data) | reinterpret_cast<uintptr_t>(rhs->data) |
+          reinterpret_cast<uintptr_t>(dst->data)) & 3u) ||
+        l[1] > 0x7fffffffull)
+        return EMEL_CUDA_INVALID_ARGUMENT;
+    emel::MvArgmaxPlan p{};
+    p.lhs = static_cast<const float*>(lhs->data);
+    p.rhs = static_cast<const float*>(rhs->data);
+    p.k = l[0];
+    p.rows = l[1];
+    p.vec = p.k % 4 == 0 && ((reinterpret_cast<uintptr_t>(lhs->data) | reinterpret_cast<uintptr_t>(rhs->data)) & 15u) == 0;
+    p.dst_value = static_cast<float*>(dst->data);
+    p.dst_index = index_out;
+    char* ws = static_cast<char*>(ctx->workspace);
+    p.ticket = reinterpret_cast<unsigned*>(ws);
+    p.partials = ws + 256;
+    p.fault = reinterpret_cast<uint32_t*>(ws + emel::kFaultWordOffset);
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = emel::launch_mul_mat_argmax(env_of(ctx, stream), p);
+    return device_status(ctx, err);
+}
+
 // ---- gated linear units ------------------------------------------------------
 
 emel_cuda_status emel_cuda_glu(emel_cuda_context* ctx, void* stream, int subop, const float* input,

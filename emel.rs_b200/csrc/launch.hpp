@@ -109,6 +109,21 @@ struct RopePlan {
 
 cudaError_t launch_rope(const LaunchEnv& env, const RopePlan& plan);
 
+// Vocabulary matvec + argmax (matvec.cu).
+struct MvArgmaxPlan {
+    const float* lhs;   // dense [k, rows]
+    const float* rhs;   // dense [k]
+    uint64_t k, rows;
+    bool vec;           // k % 4 == 0 and 16-byte aligned operands: bulk-copy tiles
+    float* dst_value;
+    int32_t* dst_index;
+    unsigned* ticket;   // workspace
+    void* partials;     // workspace, 16 bytes per CTA
+    uint32_t* fault;
+};
+
+cudaError_t launch_mul_mat_argmax(const LaunchEnv& env, const MvArgmaxPlan& plan);
+
 // Peer exchange over NVLink (exchange.cu).  Every rank owns one buffer of
 // kExchangeHeaderBytes flag words (flag r = the last epoch rank r published
 // into this buffer) followed by two banks (epoch parity) of kExchangeMaxRanks

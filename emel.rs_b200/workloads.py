@@ -270,3 +270,20 @@ def rope_spec():
     n = int(np.prod(ROPE_NE))
     return Config("rope", [OpSpec(f"rope_{m}", 2 * n * F32 + ROPE_NE[2] * 4, n) for m in ("neox", "norm")])
 
+
+# Vocabulary matvec + argmax (matmul.rs OpMulMatArgmax, F32): the next-token
+# step after the last hidden state -- lhs [4096, 151936] N(0, 1) / 64 (the
+# vocabulary of configuration 4b), rhs [1, 4096] N(0, 1).
+MV_K, MV_ROWS = 4096, 151936
+
+
+def mv_inputs(seed=14):
+    rng = np.random.default_rng(seed)
+    lhs = (normal(rng, (MV_ROWS * MV_K,), 1.0) / 64.0).astype(np.float32)
+    rhs = normal(rng, (MV_K,), 1.0).astype(np.float32)
+    return lhs, rhs
+
+
+def mv_spec():
+    return Config("matvec", [OpSpec("mul_mat_argmax_vocab", (MV_K * MV_ROWS + MV_K) * F32 + 8, MV_K * MV_ROWS)])
+

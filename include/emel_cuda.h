@@ -380,6 +380,24 @@ EMEL_CUDA_API emel_cuda_status emel_cuda_rope(emel_cuda_context* ctx, void* stre
                                               const emel_tensor_view* positions, const emel_tensor_view* dst,
                                               const emel_rope_params* params);
 
+/* ---- vocabulary matvec + argmax ---------------------------------------- */
+/* matmul::OpMulMatArgmax (matmul.rs:167-192) dispatched by
+ * MatmulArgmaxKernel::process_event (matmul.rs:969-987): lhs [k, m, 1, 1],
+ * rhs [1, k, 1, 1], dst [1, 1, 1, 1], all dense F32 (matmul.rs:1416-1423,
+ * 1504-1520).  The score of row r is one sequential binary32 sum of
+ * lhs[r, i] * rhs[i] (separate products, the reference's order,
+ * matmul.rs:3018-3052); the answer is the first row with the largest score
+ * (row 0 starts the scan, a later row needs a strictly larger score).
+ * Writes the best score to dst[0] and the row to *index_out (a device
+ * int32; the reference returns it as the event's Ok value).  Statuses:
+ * INVALID_VIEW, SHAPE_MISMATCH (nothing written).  Device additions: m <
+ * 2^31, 4-byte aligned pointers, non-null index_out, else
+ * INVALID_ARGUMENT.  Uses the context's reduction workspace (one call at a
+ * time per context). */
+EMEL_CUDA_API emel_cuda_status emel_cuda_mul_mat_argmax(emel_cuda_context* ctx, void* stream,
+                                                        const emel_tensor_view* lhs, const emel_tensor_view* rhs,
+                                                        const emel_tensor_view* dst, int32_t* index_out);
+
 /* ---- shape copies ----------------------------------------------------- */
 /* shape::OpCpy (shape.rs:55-69; guards 453-466, loop copy_view 438-444):
  * dst.write(i, src.read(i)) for every ordinal i of two F32 views with equal

@@ -1038,6 +1038,42 @@ int oracle_rope(const oracle_view* src, const oracle_view* positions, const orac
 }
 
 /* ---------------------------------------------------------------------- */
+/* Vocabulary matvec + argmax: matmul.rs OpMulMatArgmax (F32)               */
+/* ---------------------------------------------------------------------- */
+
+/* argmax_views_valid / argmax_shape_valid (matmul.rs:1416-1423, 1504-1520)
+ * and effect_mul_mat_argmax_execute (matmul.rs:3018-3052): each row's dot
+ * product is one sequential binary32 sum of separate products; the first
+ * row starts the scan, a later row wins only with a strictly larger score. */
+int oracle_mul_mat_argmax(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst, int32_t* index_out) {
+    if (!validate_as(lhs, DT_F32, 0, NULL) || !validate_as(rhs, DT_F32, 0, NULL) || !validate_as(dst, DT_F32, 0, NULL) ||
+        !dense_contiguous_f32(lhs) || !dense_contiguous_f32(rhs) || !dense_contiguous_f32(dst))
+        return ORACLE_INVALID_VIEW;
+    const uint64_t* l = lhs->ne;
+    const uint64_t* r = rhs->ne;
+    const uint64_t* d = dst->ne;
+    if (!(l[0] > 0 && l[1] > 0 && l[2] == 1 && l[3] == 1 && r[0] == 1 && r[1] == l[0] && r[2] == 1 && r[3] == 1 &&
+          d[0] == 1 && d[1] == 1 && d[2] == 1 && d[3] == 1))
+        return ORACLE_SHAPE_MISMATCH;
+    const uint64_t k = l[0], rows = l[1];
+    const float* a = (const float*)lhs->data;
+    const float* v = (const float*)rhs->data;
+    int32_t best_index = 0;
+    float best = -INFINITY;
+    for (uint64_t row = 0; row < rows; ++row) {
+        float acc = 0.0f;
+        for (uint64_t i = 0; i < k; ++i) acc += a[row * k + i] * v[i];
+        if (acc > best || row == 0) {
+            best = acc;
+            best_index = (int32_t)row;
+        }
+    }
+    *(float*)dst->data = best;
+    if (index_out) *index_out = best_index;
+    return ORACLE_OK;
+}
+
+/* ---------------------------------------------------------------------- */
 /* Row normalisation: normalization.rs                                     */
 /* ---------------------------------------------------------------------- */
 

@@ -67,6 +67,8 @@ int oracle_scale(const oracle_view* src, const oracle_view* dst, float scale);
 int oracle_clamp(const oracle_view* src, const oracle_view* dst, float lo, float hi);
 int oracle_leaky_relu(const oracle_view* src, const oracle_view* dst, float slope);
 int oracle_silu_back(const oracle_view* src, const oracle_view* grad, const oracle_view* dst);
+/* matmul.rs OpMulMatArgmax: lhs [k, m] dense, rhs [1, k] dense, dst [1]. */
+int oracle_mul_mat_argmax(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst, int32_t* index_out);
 /* rope.rs RopeParams (rope.rs:33-48) and OpRope. */
 typedef struct oracle_rope_params {
     int32_t n_dims;

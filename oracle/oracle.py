@@ -114,6 +114,7 @@ def load(cr=False):
         "oracle_copy": [P, P],
         "oracle_cpy": [P, P],
         "oracle_get_rows": [P, P, P],
+        "oracle_mul_mat_argmax": [P, P, P, ctypes.POINTER(ctypes.c_int32)],
         "oracle_rope": [P, P, P, ctypes.POINTER(RopeParams)],
         "oracle_cont": [P, P],
         "oracle_norm": [P, P, ctypes.c_float],
