@@ -483,168 +483,192 @@ def run_suite(args):
         if st != 0:
             raise RuntimeError(f"status {st}: {ctx.last_error}")
 
+    # with --only, a configuration's data is built only when one of its ops
+    # is selected (keys: suite names, or the op names themselves)
+    suite_ops = {"cfg1": [f"broadcast_row_{o}" for o in ("add", "sub", "mul", "div")],
+                 "cfg2": [f"{o}_{dt}" for o, _ in OPS for dt in ("f32", "f16")],
+                 "cfg3": ["rms_norm", "rms_norm_mul_fused", "rms_norm_then_mul_two_ops", "norm", "sum_rows"],
+                 "cfg5": ["repeat_mul_permuted", "repeat_add_permuted", "sum_whole_permuted",
+                          "argmax_whole_permuted", "cont_permuted"],
+                 "glu": list(W.GLU_OPS), "get_rows": [f"get_rows_{f}" for f in W.EMB_FORMATS],
+                 "rope": ["rope_neox", "rope_norm"], "matvec": ["mul_mat_argmax_vocab"]}
+
+    def wants(*keys):
+        if not only:
+            return True
+        return any(key in only or any(name in only for name in suite_ops.get(key, [])) for key in keys)
+
     B = ctypes.byref
     # cfg1: row-broadcast binary ops
-    src0, src1 = W.cfg1()
-    spec = W.cfg1_spec()
-    nb_ = spec.ops[0].bytes
-    S = sets_for(nb_)
-    a = [torch.from_numpy(src0).to(dev) for _ in range(S)]
-    b = torch.from_numpy(src1).to(dev)
-    d = [torch.empty_like(a[0]) for _ in range(S)]
-    ne = [W.CFG1_NE[0], W.CFG1_NE[1], 1, 1]
-    va = [view(t, ne) for t in a]
-    vb = view(b, [W.CFG1_NE[0], 1, 1, 1])
-    vd = [view(t, ne) for t in d]
-    for op, opname in enumerate(("add", "sub", "mul", "div")):
-        measure("cfg1", f"broadcast_row_{opname}", nb_, spec.ops[0].elements,
-                lambda k, op=op: (lambda: chk(lib.emel_cuda_broadcast_row(ctx.handle, sh, op, B(va[k]), B(vb), B(vd[k])))),
-                S)
-    del a, d
+    if wants("cfg1",):
+        src0, src1 = W.cfg1()
+        spec = W.cfg1_spec()
+        nb_ = spec.ops[0].bytes
+        S = sets_for(nb_)
+        a = [torch.from_numpy(src0).to(dev) for _ in range(S)]
+        b = torch.from_numpy(src1).to(dev)
+        d = [torch.empty_like(a[0]) for _ in range(S)]
+        ne = [W.CFG1_NE[0], W.CFG1_NE[1], 1, 1]
+        va = [view(t, ne) for t in a]
+        vb = view(b, [W.CFG1_NE[0], 1, 1, 1])
+        vd = [view(t, ne) for t in d]
+        for op, opname in enumerate(("add", "sub", "mul", "div")):
+            measure("cfg1", f"broadcast_row_{opname}", nb_, spec.ops[0].elements,
+                    lambda k, op=op: (lambda: chk(lib.emel_cuda_broadcast_row(ctx.handle, sh, op, B(va[k]), B(vb), B(vd[k])))),
+                    S)
+        del a, d
     # cfg2: unary sweep
-    x, xa = W.cfg2()
-    ne = [W.CFG2_NE[0], W.CFG2_NE[1], 1, 1]
-    for dt, code, tdt in (("f32", 0, torch.float32), ("f16", 1, torch.float16)):
-        n = x.size * (4 if dt == "f32" else 2) * 2
-        S = sets_for(n)
-        for opname, opc in OPS:
-            base = torch.from_numpy(xa if opname in ("sqrt", "pow2") else x).to(dev).to(tdt)
-            srcs = [base.clone() for _ in range(S)]
-            dsts = [torch.empty_like(base) for _ in range(S)]
-            vs = [view(t, ne, code=code) for t in srcs]
-            vo = [view(t, ne, code=code) for t in dsts]
-            measure("cfg2", f"{opname}_{dt}", n, x.size,
-                    lambda k, opc=opc: (lambda: chk(lib.emel_cuda_unary(ctx.handle, sh, opc, B(vs[k]), B(vo[k])))), S)
-            del srcs, dsts
+    if wants("cfg2",):
+        x, xa = W.cfg2()
+        ne = [W.CFG2_NE[0], W.CFG2_NE[1], 1, 1]
+        for dt, code, tdt in (("f32", 0, torch.float32), ("f16", 1, torch.float16)):
+            n = x.size * (4 if dt == "f32" else 2) * 2
+            S = sets_for(n)
+            for opname, opc in OPS:
+                base = torch.from_numpy(xa if opname in ("sqrt", "pow2") else x).to(dev).to(tdt)
+                srcs = [base.clone() for _ in range(S)]
+                dsts = [torch.empty_like(base) for _ in range(S)]
+                vs = [view(t, ne, code=code) for t in srcs]
+                vo = [view(t, ne, code=code) for t in dsts]
+                measure("cfg2", f"{opname}_{dt}", n, x.size,
+                        lambda k, opc=opc: (lambda: chk(lib.emel_cuda_unary(ctx.handle, sh, opc, B(vs[k]), B(vo[k])))), S)
+                del srcs, dsts
     # cfg3: row normalisation
-    x3, w3 = W.cfg3()
-    ne = [W.CFG3_NE[0], W.CFG3_NE[1], 1, 1]
-    spec = W.cfg3_spec()
-    xs = torch.from_numpy(x3).to(dev)
-    ws = torch.from_numpy(w3).to(dev)
-    ys = torch.empty_like(xs)
-    ys2 = torch.empty_like(xs)
-    rows = torch.empty(W.CFG3_NE[1], device=dev)
-    vx, vw, vy, vy2 = view(xs, ne), view(ws, [W.CFG3_NE[0], 1, 1, 1]), view(ys, ne), view(ys2, ne)
-    vr = view(rows, [1, W.CFG3_NE[1], 1, 1])
-    measure("cfg3", "rms_norm", spec.ops[0].bytes, spec.ops[0].elements,
-            lambda k: (lambda: chk(lib.emel_cuda_rms_norm(ctx.handle, sh, B(vx), B(vy), 1e-6))), 1)
-    measure("cfg3", "rms_norm_mul_fused", spec.ops[1].bytes, spec.ops[1].elements,
-            lambda k: (lambda: chk(lib.emel_cuda_rms_norm_mul(ctx.handle, sh, B(vx), B(vw), B(vy), 1e-6))), 1)
-    measure("cfg3", "rms_norm_then_mul_two_ops", spec.ops[0].bytes + spec.ops[1].bytes, spec.ops[0].elements,
-            lambda k: (lambda: (chk(lib.emel_cuda_rms_norm(ctx.handle, sh, B(vx), B(vy), 1e-6)),
-                                chk(lib.emel_cuda_broadcast_row(ctx.handle, sh, 2, B(vy), B(vw), B(vy2))))), 1)
-    measure("cfg3", "norm", spec.ops[2].bytes, spec.ops[2].elements,
-            lambda k: (lambda: chk(lib.emel_cuda_norm(ctx.handle, sh, B(vx), B(vy), 1e-5))), 1)
-    measure("cfg3", "sum_rows", spec.ops[3].bytes, spec.ops[3].elements,
-            lambda k: (lambda: chk(lib.emel_cuda_sum_rows(ctx.handle, sh, B(vx), B(vr)))), 1)
-    del xs, ys, ys2
+    if wants("cfg3",):
+        x3, w3 = W.cfg3()
+        ne = [W.CFG3_NE[0], W.CFG3_NE[1], 1, 1]
+        spec = W.cfg3_spec()
+        xs = torch.from_numpy(x3).to(dev)
+        ws = torch.from_numpy(w3).to(dev)
+        ys = torch.empty_like(xs)
+        ys2 = torch.empty_like(xs)
+        rows = torch.empty(W.CFG3_NE[1], device=dev)
+        vx, vw, vy, vy2 = view(xs, ne), view(ws, [W.CFG3_NE[0], 1, 1, 1]), view(ys, ne), view(ys2, ne)
+        vr = view(rows, [1, W.CFG3_NE[1], 1, 1])
+        measure("cfg3", "rms_norm", spec.ops[0].bytes, spec.ops[0].elements,
+                lambda k: (lambda: chk(lib.emel_cuda_rms_norm(ctx.handle, sh, B(vx), B(vy), 1e-6))), 1)
+        measure("cfg3", "rms_norm_mul_fused", spec.ops[1].bytes, spec.ops[1].elements,
+                lambda k: (lambda: chk(lib.emel_cuda_rms_norm_mul(ctx.handle, sh, B(vx), B(vw), B(vy), 1e-6))), 1)
+        measure("cfg3", "rms_norm_then_mul_two_ops", spec.ops[0].bytes + spec.ops[1].bytes, spec.ops[0].elements,
+                lambda k: (lambda: (chk(lib.emel_cuda_rms_norm(ctx.handle, sh, B(vx), B(vy), 1e-6)),
+                                    chk(lib.emel_cuda_broadcast_row(ctx.handle, sh, 2, B(vy), B(vw), B(vy2))))), 1)
+        measure("cfg3", "norm", spec.ops[2].bytes, spec.ops[2].elements,
+                lambda k: (lambda: chk(lib.emel_cuda_norm(ctx.handle, sh, B(vx), B(vy), 1e-5))), 1)
+        measure("cfg3", "sum_rows", spec.ops[3].bytes, spec.ops[3].elements,
+                lambda k: (lambda: chk(lib.emel_cuda_sum_rows(ctx.handle, sh, B(vx), B(vr)))), 1)
+        del xs, ys, ys2
     # cfg4a: masked, scaled softmax
-    scores, mask = W.cfg4a()
-    kv, q, h = W.CFG4A_NE
-    spec = W.cfg4_spec()
-    ts = torch.from_numpy(scores).to(dev)
-    tm = torch.from_numpy(mask).to(dev)
-    to = torch.empty_like(ts)
-    vs_, vm, vo_ = view(ts, [kv, q, h, 1]), view(tm, [kv, q, 1, 1], code=1), view(to, [kv, q, h, 1])
-    measure("cfg4", "soft_max_ext_scale_mask", spec.ops[0].bytes, spec.ops[0].elements,
-            lambda k: (lambda: chk(lib.emel_cuda_soft_max_ext(ctx.handle, sh, B(vs_), B(vm), B(vo_),
-                                                                float(W.CFG4A_SCALE)))), 1)
-    del ts, to
+    if wants("soft_max_ext_scale_mask",):
+        scores, mask = W.cfg4a()
+        kv, q, h = W.CFG4A_NE
+        spec = W.cfg4_spec()
+        ts = torch.from_numpy(scores).to(dev)
+        tm = torch.from_numpy(mask).to(dev)
+        to = torch.empty_like(ts)
+        vs_, vm, vo_ = view(ts, [kv, q, h, 1]), view(tm, [kv, q, 1, 1], code=1), view(to, [kv, q, h, 1])
+        measure("cfg4", "soft_max_ext_scale_mask", spec.ops[0].bytes, spec.ops[0].elements,
+                lambda k: (lambda: chk(lib.emel_cuda_soft_max_ext(ctx.handle, sh, B(vs_), B(vm), B(vo_),
+                                                                    float(W.CFG4A_SCALE)))), 1)
+        del ts, to
     # cfg4b: vocab softmax and per-row argmax
-    logits, _ = W.cfg4b()
-    v, rws = W.CFG4B_NE
-    S = sets_for(spec.ops[1].bytes)
-    tl = [torch.from_numpy(logits).to(dev) for _ in range(S)]
-    tlo = [torch.empty_like(tl[0]) for _ in range(S)]
-    ti = torch.empty(rws, dtype=torch.int64, device=dev)
-    vl = [view(t, [v, rws, 1, 1]) for t in tl]
-    vlo = [view(t, [v, rws, 1, 1]) for t in tlo]
-    vi = view(ti, [1, rws, 1, 1], code=27)
-    measure("cfg4", "soft_max_vocab", spec.ops[1].bytes, spec.ops[1].elements,
-            lambda k: (lambda: chk(lib.emel_cuda_soft_max(ctx.handle, sh, B(vl[k]), B(vlo[k])))), S)
-    measure("cfg4", "argmax_rows_vocab", spec.ops[2].bytes, spec.ops[2].elements,
-            lambda k: (lambda: chk(lib.emel_cuda_argmax_rows(ctx.handle, sh, B(vl[k]), B(vi)))), S)
-    del tl, tlo
+    if wants("soft_max_vocab", "argmax_rows_vocab"):
+        logits, _ = W.cfg4b()
+        v, rws = W.CFG4B_NE
+        S = sets_for(spec.ops[1].bytes)
+        tl = [torch.from_numpy(logits).to(dev) for _ in range(S)]
+        tlo = [torch.empty_like(tl[0]) for _ in range(S)]
+        ti = torch.empty(rws, dtype=torch.int64, device=dev)
+        vl = [view(t, [v, rws, 1, 1]) for t in tl]
+        vlo = [view(t, [v, rws, 1, 1]) for t in tlo]
+        vi = view(ti, [1, rws, 1, 1], code=27)
+        measure("cfg4", "soft_max_vocab", spec.ops[1].bytes, spec.ops[1].elements,
+                lambda k: (lambda: chk(lib.emel_cuda_soft_max(ctx.handle, sh, B(vl[k]), B(vlo[k])))), S)
+        measure("cfg4", "argmax_rows_vocab", spec.ops[2].bytes, spec.ops[2].elements,
+                lambda k: (lambda: chk(lib.emel_cuda_argmax_rows(ctx.handle, sh, B(vl[k]), B(vi)))), S)
+        del tl, tlo
     # cfg5: permuted repeat broadcast, whole-tensor sum and argmax
-    s0, s1 = W.cfg5()
-    ne5, nb5 = W.cfg5_src0_view()
-    spec = W.cfg5_spec()
-    t0 = torch.from_numpy(s0).to(dev)
-    t1 = torch.from_numpy(s1).to(dev)
-    td = torch.empty_like(t0)
-    tsum = torch.empty(1, device=dev)
-    targ = torch.empty(1, dtype=torch.int64, device=dev)
-    v0 = view(t0, ne5, nb5)
-    v1 = view(t1, [128, 1, 8192, 1])
-    vd5 = view(td, ne5)
-    one = [1, 1, 1, 1]
-    vsum, varg = view(tsum, one), view(targ, one, code=27)
-    for op, opname in ((2, "mul"), (0, "add")):
-        measure("cfg5", f"repeat_{opname}_permuted", spec.ops[0].bytes, spec.ops[0].elements,
-                lambda k, op=op: (lambda: chk(lib.emel_cuda_binary_repeat(ctx.handle, sh, op, B(v0), B(v1), B(vd5)))), 1)
-    measure("cfg5", "sum_whole_permuted", spec.ops[2].bytes, spec.ops[2].elements,
-            lambda k: (lambda: chk(lib.emel_cuda_sum(ctx.handle, sh, B(v0), B(vsum)))), 1)
-    measure("cfg5", "argmax_whole_permuted", spec.ops[3].bytes, spec.ops[3].elements,
-            lambda k: (lambda: chk(lib.emel_cuda_argmax(ctx.handle, sh, B(v0), B(varg)))), 1)
-    # shape.rs OpCont of the permuted view (a strided gather into dense rows)
-    measure("cfg5", "cont_permuted", 2 * spec.ops[2].bytes, spec.ops[2].elements,
-            lambda k: (lambda: chk(lib.emel_cuda_cont(ctx.handle, sh, B(v0), B(vd5)))), 1)
-    del t0, t1, td
+    if wants("cfg5",):
+        s0, s1 = W.cfg5()
+        ne5, nb5 = W.cfg5_src0_view()
+        spec = W.cfg5_spec()
+        t0 = torch.from_numpy(s0).to(dev)
+        t1 = torch.from_numpy(s1).to(dev)
+        td = torch.empty_like(t0)
+        tsum = torch.empty(1, device=dev)
+        targ = torch.empty(1, dtype=torch.int64, device=dev)
+        v0 = view(t0, ne5, nb5)
+        v1 = view(t1, [128, 1, 8192, 1])
+        vd5 = view(td, ne5)
+        one = [1, 1, 1, 1]
+        vsum, varg = view(tsum, one), view(targ, one, code=27)
+        for op, opname in ((2, "mul"), (0, "add")):
+            measure("cfg5", f"repeat_{opname}_permuted", spec.ops[0].bytes, spec.ops[0].elements,
+                    lambda k, op=op: (lambda: chk(lib.emel_cuda_binary_repeat(ctx.handle, sh, op, B(v0), B(v1), B(vd5)))), 1)
+        measure("cfg5", "sum_whole_permuted", spec.ops[2].bytes, spec.ops[2].elements,
+                lambda k: (lambda: chk(lib.emel_cuda_sum(ctx.handle, sh, B(v0), B(vsum)))), 1)
+        measure("cfg5", "argmax_whole_permuted", spec.ops[3].bytes, spec.ops[3].elements,
+                lambda k: (lambda: chk(lib.emel_cuda_argmax(ctx.handle, sh, B(v0), B(varg)))), 1)
+        # shape.rs OpCont of the permuted view (a strided gather into dense rows)
+        measure("cfg5", "cont_permuted", 2 * spec.ops[2].bytes, spec.ops[2].elements,
+                lambda k: (lambda: chk(lib.emel_cuda_cont(ctx.handle, sh, B(v0), B(vd5)))), 1)
+        del t0, t1, td
     # gated linear units (glu.rs) on configuration 2's feed-forward shape
-    spec = W.glu_spec()
-    xg = W.glu_ffn()
-    sets = sets_for(spec.ops[0].bytes)
-    tin = [torch.from_numpy(xg).to(dev) for _ in range(sets)]
-    tout = [torch.empty(W.GLU_N, device=dev) for _ in range(sets)]
-    for subop, o in enumerate(spec.ops):
-        measure("glu", o.name, o.bytes, o.elements,
-                lambda k, subop=subop: (lambda: chk(lib.emel_cuda_glu(
-                    ctx.handle, sh, subop, ctypes.c_void_p(tin[k].data_ptr()), 2 * W.GLU_N,
-                    ctypes.c_void_p(tout[k].data_ptr()), W.GLU_N))), sets)
-    del tin, tout
+    if wants("glu",):
+        spec = W.glu_spec()
+        xg = W.glu_ffn()
+        sets = sets_for(spec.ops[0].bytes)
+        tin = [torch.from_numpy(xg).to(dev) for _ in range(sets)]
+        tout = [torch.empty(W.GLU_N, device=dev) for _ in range(sets)]
+        for subop, o in enumerate(spec.ops):
+            measure("glu", o.name, o.bytes, o.elements,
+                    lambda k, subop=subop: (lambda: chk(lib.emel_cuda_glu(
+                        ctx.handle, sh, subop, ctypes.c_void_p(tin[k].data_ptr()), 2 * W.GLU_N,
+                        ctypes.c_void_p(tout[k].data_ptr()), W.GLU_N))), sets)
+        del tin, tout
     # row gather (get_rows.rs): 8192 token rows of a [4096, 32000] table
-    spec = W.emb_spec()
-    tok = torch.from_numpy(W.emb_tokens()).to(dev)
-    vidx = view(tok, [W.EMB_TOKENS, 1, 1, 1], code=26)
-    for fmt, o in zip(W.EMB_FORMATS, spec.ops):
-        if only and o.name not in only:
-            continue
-        data, ne, nb, code = W.emb_table(fmt)
-        ttab = torch.from_numpy(data).to(dev)
-        vtab = pkg.CView()
-        vtab.data, vtab.storage_bytes, vtab.dtype = ttab.data_ptr(), ttab.numel(), code
-        for d in range(4):
-            vtab.ne[d], vtab.nb[d] = ne[d], nb[d]
-        sets = sets_for(o.bytes)
-        touts = [torch.empty(W.EMB_TOKENS * W.EMB_COLS, device=dev) for _ in range(sets)]
-        vouts = [view(t, [W.EMB_COLS, W.EMB_TOKENS, 1, 1]) for t in touts]
-        measure("get_rows", o.name, o.bytes, o.elements,
-                lambda k, vtab=vtab, vouts=vouts: (lambda: chk(lib.emel_cuda_get_rows(
-                    ctx.handle, sh, B(vtab), B(vidx), B(vouts[k])))), sets)
-        chk(lib.emel_cuda_stream_synchronize(ctx.handle, sh))
-        del ttab, touts
+    if wants("get_rows",):
+        spec = W.emb_spec()
+        tok = torch.from_numpy(W.emb_tokens()).to(dev)
+        vidx = view(tok, [W.EMB_TOKENS, 1, 1, 1], code=26)
+        for fmt, o in zip(W.EMB_FORMATS, spec.ops):
+            if only and o.name not in only:
+                continue
+            data, ne, nb, code = W.emb_table(fmt)
+            ttab = torch.from_numpy(data).to(dev)
+            vtab = pkg.CView()
+            vtab.data, vtab.storage_bytes, vtab.dtype = ttab.data_ptr(), ttab.numel(), code
+            for d in range(4):
+                vtab.ne[d], vtab.nb[d] = ne[d], nb[d]
+            sets = sets_for(o.bytes)
+            touts = [torch.empty(W.EMB_TOKENS * W.EMB_COLS, device=dev) for _ in range(sets)]
+            vouts = [view(t, [W.EMB_COLS, W.EMB_TOKENS, 1, 1]) for t in touts]
+            measure("get_rows", o.name, o.bytes, o.elements,
+                    lambda k, vtab=vtab, vouts=vouts: (lambda: chk(lib.emel_cuda_get_rows(
+                        ctx.handle, sh, B(vtab), B(vidx), B(vouts[k])))), sets)
+            chk(lib.emel_cuda_stream_synchronize(ctx.handle, sh))
+            del ttab, touts
     # rotary position embedding (rope.rs) of query rows
-    spec = W.rope_spec()
-    xr, pr_pos = W.rope_inputs()
-    ne_r = list(W.ROPE_NE)
-    sets = sets_for(spec.ops[0].bytes)
-    txr = [torch.from_numpy(xr).to(dev) for _ in range(sets)]
-    tyr = [torch.empty_like(t) for t in txr]
-    tpos = torch.from_numpy(pr_pos).to(dev)
-    vpos = view(tpos, [ne_r[2], 1, 1, 1], code=26)
-    vxr = [view(t, ne_r) for t in txr]
-    vyr = [view(t, ne_r) for t in tyr]
-    for o, mode in zip(spec.ops, (2, 0)):
-        prm = pkg.CRopeParams(n_dims=128, mode=mode, freq_base=10000.0, freq_scale=1.0, ext_factor=0.0,
-                              attn_factor=1.0)
-        measure("rope", o.name, o.bytes, o.elements,
-                lambda k, prm=prm: (lambda: chk(lib.emel_cuda_rope(ctx.handle, sh, B(vxr[k]), B(vpos), B(vyr[k]),
-                                                                     B(prm)))), sets)
-    del txr, tyr
+    if wants("rope",):
+        spec = W.rope_spec()
+        xr, pr_pos = W.rope_inputs()
+        ne_r = list(W.ROPE_NE)
+        sets = sets_for(spec.ops[0].bytes)
+        txr = [torch.from_numpy(xr).to(dev) for _ in range(sets)]
+        tyr = [torch.empty_like(t) for t in txr]
+        tpos = torch.from_numpy(pr_pos).to(dev)
+        vpos = view(tpos, [ne_r[2], 1, 1, 1], code=26)
+        vxr = [view(t, ne_r) for t in txr]
+        vyr = [view(t, ne_r) for t in tyr]
+        for o, mode in zip(spec.ops, (2, 0)):
+            prm = pkg.CRopeParams(n_dims=128, mode=mode, freq_base=10000.0, freq_scale=1.0, ext_factor=0.0,
+                                  attn_factor=1.0)
+            measure("rope", o.name, o.bytes, o.elements,
+                    lambda k, prm=prm: (lambda: chk(lib.emel_cuda_rope(ctx.handle, sh, B(vxr[k]), B(vpos), B(vyr[k]),
+                                                                         B(prm)))), sets)
+        del txr, tyr
     # vocabulary matvec + argmax (matmul.rs OpMulMatArgmax)
-    spec = W.mv_spec()
-    if not only or spec.ops[0].name in only:
+    if wants("matvec",):
+        spec = W.mv_spec()
         lm, rv = W.mv_inputs()
         tl, tr = torch.from_numpy(lm).to(dev), torch.from_numpy(rv).to(dev)
         del lm
