@@ -449,7 +449,7 @@ def run_suite(args):
 
     only = set(args.only.split(",")) if args.only else None
 
-    def measure(cfg, name, nbytes, elems, make_launch, sets):
+    def measure(cfg, name, nbytes, elems, make_launch, sets, extra=None):
         if only and name not in only:
             return
         torch.cuda.synchronize()  # inputs were uploaded on torch's stream
@@ -476,6 +476,8 @@ def run_suite(args):
         line = {"suite": cfg, "op": name, "gbs": round(gbs, 1), "frac_of_peak": round(gbs / peak, 4),
                 "gelems": round(elems / (ms / 1e3) / 1e9, 2), "us_per_launch": round(ms * 1e3, 2),
                 "algorithmic_bytes": nbytes, "buffer_sets": sets, "peak": f"{peak} GB/s ({peak_kind})"}
+        if extra is not None:
+            line.update(extra(ms))
         print(json.dumps(line), flush=True)
         out.append(line)
 
@@ -491,7 +493,8 @@ def run_suite(args):
                  "cfg5": ["repeat_mul_permuted", "repeat_add_permuted", "sum_whole_permuted",
                           "argmax_whole_permuted", "cont_permuted"],
                  "glu": list(W.GLU_OPS), "get_rows": [f"get_rows_{f}" for f in W.EMB_FORMATS],
-                 "rope": ["rope_neox", "rope_norm"], "matvec": ["mul_mat_argmax_vocab"]}
+                 "rope": ["rope_neox", "rope_norm"], "matvec": ["mul_mat_argmax_vocab"],
+                 "attention": [o.name for o in W.fa_spec().ops], "diag": [o.name for o in W.diag_spec().ops]}
 
     def wants(*keys):
         if not only:
@@ -680,6 +683,46 @@ def run_suite(args):
                 lambda k: (lambda: chk(lib.emel_cuda_mul_mat_argmax(ctx.handle, sh, B(vl), B(vr), B(vv),
                                                                     ctypes.c_void_p(ti.data_ptr())))), 1)
         del tl, tr
+    # causal masks (diag.rs OpDiagMaskInf / OpDiagMaskZero) over a score matrix
+    if wants("diag",):
+        x = W.diag_inputs()
+        n = x.size
+        sets = sets_for(n * 8)
+        tx = [torch.from_numpy(x).to(dev) for _ in range(sets)]
+        ty = [torch.empty_like(t) for t in tx]
+        del x
+        for o, mode in zip(W.diag_spec().ops, (0, 1)):
+            measure("diag", o.name, o.bytes, o.elements,
+                    lambda k, mode=mode: (lambda: chk(lib.emel_cuda_diag_mask(
+                        ctx.handle, sh, mode, ctypes.c_void_p(tx[k].data_ptr()), n,
+                        ctypes.c_void_p(ty[k].data_ptr()), n, 0))), sets)
+        del tx, ty
+    # single-query attention (flash_attn.rs OpFlashAttnExt): one CTA per query
+    # head runs the reference's per-token binary16 recurrence, so the time is
+    # tokens x the recurrence's latency; ns_per_token reports that bound
+    if wants("attention",):
+        for o, tokens in zip(W.fa_spec().ops, W.FA_TOKENS):
+            if not wants(o.name) and only:
+                continue
+            q, kh, vh = W.fa_inputs(tokens)
+            sets = sets_for(o.bytes)
+            tq = torch.from_numpy(q).to(dev)
+            tk = [torch.from_numpy(kh.view(np.int16)).to(dev) for _ in range(sets)]
+            tvv = [torch.from_numpy(vh.view(np.int16)).to(dev) for _ in range(sets)]
+            to = torch.empty_like(tq)
+            del kh, vh
+            qne, kne = [W.FA_D, 1, W.FA_HEADS, 1], [W.FA_D, tokens, W.FA_KV_HEADS, 1]
+            vq, vo = view(tq, qne), view(to, qne)
+            vk = [view(t, kne, code=1) for t in tk]
+            vv = [view(t, kne, code=1) for t in tvv]
+            measure("attention", o.name, o.bytes, o.elements,
+                    lambda k, vk=vk, vv=vv: (lambda: chk(lib.emel_cuda_flash_attn_ext(
+                        ctx.handle, sh, B(vq), B(vk[k]), B(vv[k]), B(vo), None))), sets,
+                    extra=lambda ms, tokens=tokens: {"ns_per_token": round(ms * 1e6 / tokens, 2),
+                                                     "heads": W.FA_HEADS, "kv_heads": W.FA_KV_HEADS,
+                                                     "head_dim": W.FA_D, "tokens": tokens})
+            chk(lib.emel_cuda_stream_synchronize(ctx.handle, sh))
+            del tk, tvv
     return out
 
 

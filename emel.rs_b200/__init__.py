@@ -51,6 +51,7 @@ class Status(enum.IntEnum):
     INDEX_OUT_OF_BOUNDS = 9
     UNSUPPORTED_SOURCE_STRIDE = 10
     INVALID_MODE = 11
+    INVALID_REQUEST = 12
     DEVICE_ERROR = 16
     TIMEOUT = 17
     INVALID_ARGUMENT = 18
@@ -121,6 +122,21 @@ class CRopeParams(ctypes.Structure):
                 ("freq_scale", ctypes.c_float), ("ext_factor", ctypes.c_float), ("attn_factor", ctypes.c_float)]
 
 
+class CFlashAttnOptions(ctypes.Structure):
+    """emel_flash_attn_options: flash_attn::FlashAttnOptions (flash_attn.rs:24-31)."""
+    _fields_ = [("scale", ctypes.c_float), ("has_scale", ctypes.c_uint32),
+                ("masked_total_tokens", ctypes.c_uint32), ("has_masked_total_tokens", ctypes.c_uint32)]
+
+    @classmethod
+    def of(cls, scale=None, masked_total_tokens=None):
+        o = cls()
+        if scale is not None:
+            o.scale, o.has_scale = scale, 1
+        if masked_total_tokens is not None:
+            o.masked_total_tokens, o.has_masked_total_tokens = masked_total_tokens, 1
+        return o
+
+
 # Every symbol include/emel_cuda.h declares, with its ctypes signature.
 _P = ctypes.POINTER(CView)
 _V = ctypes.c_void_p
@@ -179,7 +195,12 @@ SIGNATURES = {
     "emel_cuda_generic": (_I, [_CTX, _V, ctypes.POINTER(CGenericRequest)]),
     "emel_cuda_get_rows": (_I, [_CTX, _V, _P, _P, _P]),
     "emel_cuda_mul_mat_argmax": (_I, [_CTX, _V, _P, _P, _P, _V]),
+    "emel_cuda_mul_mat_argmax_q8_0": (_I, [_CTX, _V, _P, _P, _P, _V]),
     "emel_cuda_rope": (_I, [_CTX, _V, _P, _P, _P, ctypes.POINTER(CRopeParams)]),
+    "emel_cuda_diag": (_I, [_CTX, _V, _V, ctypes.c_uint64, _V, ctypes.c_uint64]),
+    "emel_cuda_diag_mask": (_I, [_CTX, _V, _I, _V, ctypes.c_uint64, _V, ctypes.c_uint64, ctypes.c_int32]),
+    "emel_cuda_flash_attn_ext": (_I, [_CTX, _V, _P, _P, _P, _P, ctypes.POINTER(CFlashAttnOptions)]),
+    "emel_cuda_flash_attn_workspace": (_I, [_CTX, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]),
     "emel_cuda_cpy": (_I, [_CTX, _V, _P, _P]),
     "emel_cuda_cont": (_I, [_CTX, _V, _P, _P]),
     "emel_cuda_glu": (_I, [_CTX, _V, _I, _V, ctypes.c_uint64, _V, ctypes.c_uint64]),
@@ -641,6 +662,88 @@ class OpMulMatArgmax(Event):
     def dispatch(self, ctx, stream):
         return ctx._lib.emel_cuda_mul_mat_argmax(ctx.handle, stream, _r(self.lhs), _r(self.rhs),
                                                  _r(self.destination), ctypes.c_void_p(self.index_ptr))
+
+
+@dataclass
+class OpDiag(Event):
+    """diag::OpDiag::new(input, output) (diag.rs:44-66): device pointers to
+    input_len and input_len^2 floats."""
+    input: int
+    input_len: int
+    output: int
+    output_len: int
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_diag(ctx.handle, stream, ctypes.c_void_p(self.input), self.input_len,
+                                       ctypes.c_void_p(self.output), self.output_len)
+
+
+@dataclass
+class _DiagMask(Event):
+    input: int
+    input_len: int
+    output: int
+    output_len: int
+    n_past: int
+    MODE = 0
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_diag_mask(ctx.handle, stream, self.MODE, ctypes.c_void_p(self.input),
+                                            self.input_len, ctypes.c_void_p(self.output), self.output_len,
+                                            self.n_past)
+
+
+class OpDiagMaskInf(_DiagMask):
+    """diag::OpDiagMaskInf::new(input, output, n_past) (diag.rs:68-86)."""
+    MODE = 0
+
+
+class OpDiagMaskZero(_DiagMask):
+    """diag::OpDiagMaskZero::new(input, output, n_past) (diag.rs:88-108)."""
+    MODE = 1
+
+
+@dataclass
+class OpFlashAttnExt(Event):
+    """flash_attn::OpFlashAttnExt::new(query, key, value, destination, options)
+    (flash_attn.rs:78-99): query / destination F32 [d, 1, heads, 1], key /
+    value F16 [d, tokens, kv_heads, 1]; options: FlashAttnOptions fields
+    (scale, masked_total_tokens), None for the defaults."""
+    query: TensorView
+    key: TensorView
+    value: TensorView
+    destination: TensorView
+    scale: Optional[float] = None
+    masked_total_tokens: Optional[int] = None
+
+    def dispatch(self, ctx, stream):
+        opts = CFlashAttnOptions.of(self.scale, self.masked_total_tokens)
+        return ctx._lib.emel_cuda_flash_attn_ext(ctx.handle, stream, _r(self.query), _r(self.key), _r(self.value),
+                                                 _r(self.destination), ctypes.byref(opts))
+
+
+def flash_attn_workspace(ctx: "Context"):
+    """FlashAttnKernel::prepared_tokens / reuse_count (flash_attn.rs:205-215)
+    of the context: (tokens of the last accepted call, consecutive repeats)."""
+    prepared, reuse = ctypes.c_uint64(), ctypes.c_uint64()
+    _check(ctx._lib.emel_cuda_flash_attn_workspace(ctx.handle, ctypes.byref(prepared), ctypes.byref(reuse)),
+           "flash_attn_workspace")
+    return prepared.value, reuse.value
+
+
+@dataclass
+class OpMulMatArgmaxQ8_0(Event):
+    """matmul::OpMulMatArgmaxQ8_0 (matmul.rs:500-520): lhs Q8_0 packed rows
+    [k, m], rhs [1, k] F32, dst [1]; the best row goes to the device int32
+    at `index_ptr`."""
+    lhs: TensorView
+    rhs: TensorView
+    destination: TensorView
+    index_ptr: int
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_mul_mat_argmax_q8_0(ctx.handle, stream, _r(self.lhs), _r(self.rhs),
+                                                      _r(self.destination), ctypes.c_void_p(self.index_ptr))
 
 
 @dataclass

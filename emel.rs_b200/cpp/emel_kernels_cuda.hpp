@@ -106,6 +106,7 @@ enum class Error : int {
     Timeout = EMEL_CUDA_TIMEOUT,
     InvalidArgument = EMEL_CUDA_INVALID_ARGUMENT,
     OutOfMemory = EMEL_CUDA_OUT_OF_MEMORY,
+    InvalidRequest = EMEL_CUDA_INVALID_REQUEST,  // FlashAttnError::InvalidRequest (flash_attn.rs:35-44)
 };
 using BinaryError = Error;
 using BroadcastError = Error;
@@ -113,6 +114,7 @@ using UnaryError = Error;
 using NormalizationError = Error;
 using ReductionError = Error;
 using ActivationError = Error;
+using FlashAttnError = Error;
 
 // Result<(), Error>: empty when Ok.
 class Result {
@@ -226,6 +228,21 @@ struct OpSoftMaxExt {
     float scale;
 };
 
+// flash_attn::FlashAttnOptions / OpFlashAttnExt (flash_attn.rs:24-31, 62-99):
+// query / destination F32 [d, 1, heads, 1]; key / value F16 [d, tokens,
+// kv_heads, 1].  Absent options resolve at dispatch (1 / sqrt(d), tokens).
+struct FlashAttnOptions {
+    std::optional<float> scale;
+    std::optional<uint32_t> masked_total_tokens;
+};
+struct OpFlashAttnExt {
+    OpFlashAttnExt(TensorView q, TensorView k, TensorView v, TensorViewMut d, FlashAttnOptions o = {})
+        : query(q), key(k), value(v), destination(d), options(o) {}
+    TensorView query, key, value;
+    TensorViewMut destination;
+    FlashAttnOptions options;
+};
+
 // ---- the actor -------------------------------------------------------------
 // Single-writer like the reference's Kernel (not thread-safe): one context,
 // one stream; process_event enqueues and, unless asynchronous, waits.
@@ -313,6 +330,20 @@ private:
     emel_cuda_status dispatch(const OpArgmax& e) {
         auto s = e.src.c(), d = e.dst.c();
         return emel_cuda_argmax(ctx_, stream_, &s, &d);
+    }
+
+    emel_cuda_status dispatch(const OpFlashAttnExt& e) {
+        auto q = e.query.c(), k = e.key.c(), v = e.value.c(), d = e.destination.c();
+        emel_flash_attn_options o{};
+        if (e.options.scale) {
+            o.scale = *e.options.scale;
+            o.has_scale = 1;
+        }
+        if (e.options.masked_total_tokens) {
+            o.masked_total_tokens = *e.options.masked_total_tokens;
+            o.has_masked_total_tokens = 1;
+        }
+        return emel_cuda_flash_attn_ext(ctx_, stream_, &q, &k, &v, &d, &o);
     }
 
     emel_cuda_context* ctx_ = nullptr;

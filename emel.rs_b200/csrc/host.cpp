@@ -24,6 +24,8 @@ struct emel_cuda_context {
     uint64_t workspace_bytes;
     void* tables;  // binary16 domain tables (one slot per unary op)
     uint64_t launches;
+    uint64_t fa_prepared_tokens;  // FlashAttnWorkspace::prepared_tokens (flash_attn.rs:117-118)
+    uint64_t fa_reuse_count;      // FlashAttnWorkspace::reuse_count
     char last_error[256];
 };
 
@@ -1238,6 +1240,182 @@ emel_cuda_status emel_cuda_mul_mat_argmax(emel_cuda_context* ctx, void* stream, 
     cudaError_t err = select_device(ctx);
     if (err == cudaSuccess) err = emel::launch_mul_mat_argmax(env_of(ctx, stream), p);
     return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_mul_mat_argmax_q8_0(emel_cuda_context* ctx, void* stream, const emel_tensor_view* lhs,
+                                               const emel_tensor_view* rhs, const emel_tensor_view* dst,
+                                               int32_t* index_out) {
+    Checked cr, cd;
+    uint64_t row_bytes = 0;
+    // quantized_views_valid (matmul.rs:1522-1542): Q8_0 packed rows of at most
+    // 1024 blocks, dense F32 rhs and destination
+    if (lhs == nullptr || rhs == nullptr || dst == nullptr || !gr_packed_view_valid(lhs, EMEL_DTYPE_Q8_0, 32, 34, &row_bytes) ||
+        lhs->ne[0] / 32 > 1024 || !validate_as(rhs, EMEL_DTYPE_F32, false, &cr) ||
+        !validate_as(dst, EMEL_DTYPE_F32, false, &cd) || !dense_contiguous_f32(rhs) || !dense_contiguous_f32(dst))
+        return EMEL_CUDA_INVALID_VIEW;
+    // quantized_shape_valid (matmul.rs:1544-1564)
+    const uint64_t* l = lhs->ne;
+    const uint64_t* r = rhs->ne;
+    const uint64_t* d = dst->ne;
+    if (!(l[0] > 0 && l[1] > 0 && l[2] == 1 && l[3] == 1 && r[0] == 1 && r[1] == l[0] && r[2] == 1 && r[3] == 1 &&
+          d[0] == 1 && d[1] == 1 && d[2] == 1 && d[3] == 1))
+        return EMEL_CUDA_SHAPE_MISMATCH;
+    if (ctx == nullptr || index_out == nullptr || (reinterpret_cast<uintptr_t>(index_out) & 3u) ||
+        ((reinterpret_cast<uintptr_t>(lhs->data) | reinterpret_cast<uintptr_t>(rhs->data) |
+          reinterpret_cast<uintptr_t>(dst->data)) & 3u) ||
+        l[1] > 0x7fffffffull)
+        return EMEL_CUDA_INVALID_ARGUMENT;
+    emel::MvArgmaxPlan p{};
+    p.rhs = static_cast<const float*>(rhs->data);
+    p.k = l[0];
+    p.rows = l[1];
+    p.dst_value = static_cast<float*>(dst->data);
+    p.dst_index = index_out;
+    char* ws = static_cast<char*>(ctx->workspace);
+    p.ticket = reinterpret_cast<unsigned*>(ws);
+    p.partials = ws + 256;
+    p.fault = reinterpret_cast<uint32_t*>(ws + emel::kFaultWordOffset);
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess)
+        err = emel::launch_mul_mat_argmax_q8_0(env_of(ctx, stream), p, static_cast<const uint8_t*>(lhs->data));
+    return device_status(ctx, err);
+}
+
+// ---- single-query attention -------------------------------------------------
+
+// dense_f32_layout (flash_attn.rs:305-325): effective strides exactly row-major.
+static bool fa_dense_f32(const emel_tensor_view* v) {
+    uint64_t s[4];
+    if (v->dtype != EMEL_DTYPE_F32 || !strides_of(*v, 4, s)) return false;
+    uint64_t expected = 4;
+    for (int d = 0; d < 4; ++d) {
+        if (s[d] != expected) return false;
+        if (__builtin_mul_overflow(expected, v->ne[d], &expected)) return false;
+    }
+    return true;
+}
+
+emel_cuda_status emel_cuda_flash_attn_ext(emel_cuda_context* ctx, void* stream, const emel_tensor_view* query,
+                                          const emel_tensor_view* key, const emel_tensor_view* value,
+                                          const emel_tensor_view* dst, const emel_flash_attn_options* options) {
+    if (query == nullptr || key == nullptr || value == nullptr || dst == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    // OpFlashAttnExt::new (flash_attn.rs:78-99): resolve the optional parameters
+    const uint64_t head_dim = query->ne[0], heads = query->ne[2], tokens = key->ne[1], kv_heads = key->ne[2];
+    float scale = 1.0f / std::sqrt((float)head_dim);
+    uint64_t masked_total = tokens;
+    if (options != nullptr && options->has_scale) scale = options->scale;
+    if (options != nullptr && options->has_masked_total_tokens) masked_total = options->masked_total_tokens;
+    // valid_request (flash_attn.rs:262-303): every rule maps to InvalidRequest
+    Checked cq, cd;
+    uint64_t ks[4], vs[4];
+    const bool valid =
+        validate_as(query, EMEL_DTYPE_F32, false, &cq) && validate_as(dst, EMEL_DTYPE_F32, false, &cd) &&
+        gr_half_view_valid(key, EMEL_DTYPE_F16, ks) && gr_half_view_valid(value, EMEL_DTYPE_F16, vs) &&
+        fa_dense_f32(query) && fa_dense_f32(dst) && head_dim != 0 && query->ne[1] == 1 && heads != 0 && tokens != 0 &&
+        kv_heads != 0 && key->ne[0] == head_dim && value->ne[0] == head_dim && value->ne[1] == tokens &&
+        value->ne[2] == kv_heads && dst->ne[0] == head_dim && dst->ne[1] == 1 && dst->ne[2] == heads &&
+        query->ne[3] == 1 && key->ne[3] == 1 && value->ne[3] == 1 && dst->ne[3] == 1 && heads % kv_heads == 0 &&
+        head_dim <= 4096 && masked_total >= tokens && std::isfinite(scale) && scale > 0.0f;
+    if (!valid) return EMEL_CUDA_INVALID_REQUEST;
+    // device additions: element-aligned pointers, a grid of one CTA per head
+    const uintptr_t a32 = reinterpret_cast<uintptr_t>(query->data) | reinterpret_cast<uintptr_t>(dst->data);
+    const uintptr_t a16 = reinterpret_cast<uintptr_t>(key->data) | reinterpret_cast<uintptr_t>(value->data);
+    if (ctx == nullptr || (a32 & 3u) != 0 || (a16 & 1u) != 0 || heads > 0x7fffffffull)
+        return EMEL_CUDA_INVALID_ARGUMENT;
+    emel::FlashAttnPlan p{};
+    p.q = static_cast<const float*>(query->data);
+    p.k = static_cast<const char*>(key->data);
+    p.v = static_cast<const char*>(value->data);
+    p.dst = static_cast<float*>(dst->data);
+    for (int d = 0; d < 3; ++d) {
+        // a singleton dimension's stride is never multiplied by a nonzero coordinate
+        p.ks[d] = key->ne[d] > 1 ? ks[d] : 0;
+        p.vs[d] = value->ne[d] > 1 ? vs[d] : 0;
+    }
+    p.d = head_dim;
+    p.tokens = tokens;
+    p.heads = heads;
+    p.rep = heads / kv_heads;
+    p.scale = scale;
+    p.k_rows = head_dim % 8 == 0 && (head_dim == 1 || p.ks[0] == 2) && ((reinterpret_cast<uintptr_t>(key->data) |
+                                                                        p.ks[1] | p.ks[2]) & 15u) == 0;
+    p.v_bulk = head_dim % 8 == 0 && p.vs[0] == 2 &&
+               ((reinterpret_cast<uintptr_t>(value->data) | p.vs[1] | p.vs[2]) & 15u) == 0;
+    p.v_dense = p.v_bulk && (tokens == 1 || p.vs[1] == head_dim * 2);
+    p.fault = reinterpret_cast<uint32_t*>(static_cast<char*>(ctx->workspace) + emel::kFaultWordOffset);
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = emel::launch_flash_attn(env_of(ctx, stream), p);
+    if (err == cudaSuccess) {
+        // FlashAttnWorkspace bookkeeping (flash_attn.rs:337-341)
+        if (ctx->fa_prepared_tokens == tokens) ++ctx->fa_reuse_count;
+        ctx->fa_prepared_tokens = tokens;
+    }
+    return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_flash_attn_workspace(const emel_cuda_context* ctx, uint64_t* prepared_tokens,
+                                                uint64_t* reuse_count) {
+    if (ctx == nullptr || prepared_tokens == nullptr || reuse_count == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    *prepared_tokens = ctx->fa_prepared_tokens;
+    *reuse_count = ctx->fa_reuse_count;
+    return EMEL_CUDA_OK;
+}
+
+// ---- diagonal family ---------------------------------------------------------
+
+// square_side (diag.rs:107-120): the side of a non-empty perfect square.
+static bool diag_square_side(uint64_t len, uint64_t* side) {
+    if (len == 0) return false;
+    uint64_t s = (uint64_t)std::sqrt((double)len);
+    while (s > 0 && (u128)s * s > len) --s;
+    while ((u128)(s + 1) * (s + 1) <= len) ++s;
+    if ((u128)s * s != len) return false;
+    *side = s;
+    return true;
+}
+
+static bool ranges_overlap(const void* a, uint64_t abytes, const void* b, uint64_t bbytes) {
+    const uintptr_t x = reinterpret_cast<uintptr_t>(a), y = reinterpret_cast<uintptr_t>(b);
+    return x < y + bbytes && y < x + abytes;
+}
+
+static emel_cuda_status diag_launch(emel_cuda_context* ctx, void* stream, const float* input, float* output,
+                                    uint64_t side, uint64_t n_past, int mode) {
+    emel::DiagPlan p{};
+    p.in = input;
+    p.out = output;
+    p.side = side;
+    p.n_past = n_past;
+    p.vec = side % 4 == 0 && ((reinterpret_cast<uintptr_t>(input) | reinterpret_cast<uintptr_t>(output)) & 15u) == 0;
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = emel::launch_diag(env_of(ctx, stream), p, mode);
+    return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_diag(emel_cuda_context* ctx, void* stream, const float* input, uint64_t input_len,
+                                float* output, uint64_t output_len) {
+    // OpDiag::side (diag.rs:56-65) behind guard_diag_valid
+    const uint64_t n = input_len;
+    if (n == 0 || (u128)n * n != (u128)output_len) return EMEL_CUDA_INVALID_SHAPE;
+    if (ctx == nullptr || input == nullptr || output == nullptr ||
+        ((reinterpret_cast<uintptr_t>(input) | reinterpret_cast<uintptr_t>(output)) & 3u) != 0 ||
+        output_len > UINT64_MAX / 8 || ranges_overlap(input, n * 4, output, output_len * 4))
+        return EMEL_CUDA_INVALID_ARGUMENT;
+    return diag_launch(ctx, stream, input, output, n, 0, emel::kDiag);
+}
+
+emel_cuda_status emel_cuda_diag_mask(emel_cuda_context* ctx, void* stream, int mode, const float* input,
+                                     uint64_t input_len, float* output, uint64_t output_len, int32_t n_past) {
+    if (mode != EMEL_DIAG_MASK_INF && mode != EMEL_DIAG_MASK_ZERO) return EMEL_CUDA_INVALID_ARGUMENT;
+    // mask_valid (diag.rs:122-124)
+    uint64_t side = 0;
+    if (n_past < 0 || input_len != output_len || !diag_square_side(input_len, &side)) return EMEL_CUDA_INVALID_SHAPE;
+    if (ctx == nullptr || input == nullptr || output == nullptr ||
+        ((reinterpret_cast<uintptr_t>(input) | reinterpret_cast<uintptr_t>(output)) & 3u) != 0 ||
+        input_len > UINT64_MAX / 8 || (input != output && ranges_overlap(input, input_len * 4, output, output_len * 4)))
+        return EMEL_CUDA_INVALID_ARGUMENT;
+    return diag_launch(ctx, stream, input, output, side, (uint64_t)n_past,
+                       mode == EMEL_DIAG_MASK_INF ? emel::kDiagMaskInf : emel::kDiagMaskZero);
 }
 
 // ---- gated linear units ------------------------------------------------------

@@ -123,6 +123,38 @@ struct MvArgmaxPlan {
 };
 
 cudaError_t launch_mul_mat_argmax(const LaunchEnv& env, const MvArgmaxPlan& plan);
+// Q8_0 rows (lhs: packed 34-byte blocks, rows of k / 32 blocks, 4-byte
+// aligned base); plan.lhs unused, plan.k a multiple of 32 up to 32768.
+cudaError_t launch_mul_mat_argmax_q8_0(const LaunchEnv& env, const MvArgmaxPlan& plan, const uint8_t* lhs);
+
+// Single-query attention (attention.cu): one CTA per query head.
+struct FlashAttnPlan {
+    const float* q;     // dense [d, 1, heads]
+    const char* k;      // binary16 [d, tokens, kv_heads], byte strides ks
+    const char* v;      // binary16, byte strides vs
+    float* dst;         // dense [d, 1, heads]
+    uint64_t ks[3], vs[3];
+    uint64_t d, tokens, heads, rep;  // rep = heads / kv_heads
+    float scale;
+    bool k_rows;        // key rows unit-stride, 16-byte aligned, d % 8 == 0: vector loads
+    bool v_bulk;        // value rows unit-stride, 16-byte aligned, d % 8 == 0: TMA bulk copies
+    bool v_dense;       // ... and consecutive tokens adjacent: one copy per tile
+    uint32_t* fault;    // set when a bounded wait expires
+};
+
+cudaError_t launch_flash_attn(const LaunchEnv& env, const FlashAttnPlan& plan);
+
+// Diagonal family (diag.cu): side x side row-major F32 matrices.
+enum DiagMode : int { kDiag = 0, kDiagMaskInf = 1, kDiagMaskZero = 2 };
+struct DiagPlan {
+    const float* in;    // diag: [side]; masks: [side * side] (may equal out)
+    float* out;         // [side * side]
+    uint64_t side;
+    uint64_t n_past;    // masks: columns <= row + n_past keep the input
+    bool vec;           // side % 4 == 0 and 16-byte aligned pointers
+};
+
+cudaError_t launch_diag(const LaunchEnv& env, const DiagPlan& plan, int mode);
 
 // Peer exchange over NVLink (exchange.cu).  Every rank owns one buffer of
 // kExchangeHeaderBytes flag words (flag r = the last epoch rank r published

@@ -216,6 +216,83 @@ __global__ void __launch_bounds__(kMvRows) mv_argmax_plain(MvArgmaxPlan p) {
     finish(p, scratch[0]);
 }
 
+// ---- Q8_0 rows (matmul.rs OpMulMatArgmaxQ8_0) -------------------------------
+// The rhs is quantized to Q8_0 in every CTA's shared memory (quantize_q8_0,
+// matmul.rs:1629-1653: one warp per 32-value block, amax by a max-reduction,
+// which is exact).  A warp owns one row at a time: lane l forms the integer
+// dot of block b0 + l (dp4a on 32-bit words rebuilt from the 2-byte-aligned
+// 34-byte block) and its term float(dot) * (d_lhs * d_rhs); the row's sum
+// then folds the terms in block order (a broadcast of each lane's term to
+// every lane, one binary32 add each), which is dot_q8_0's order
+// (matmul.rs:1893-1910).
+constexpr int kQ8Threads = 256;
+constexpr int kQ8Warps = kQ8Threads / 32;
+
+__global__ void __launch_bounds__(kQ8Threads) mv_argmax_q8_0(MvArgmaxPlan p, const uint8_t* lhs) {
+    extern __shared__ __align__(16) uint32_t q8_smem[];
+    __shared__ MvPart warp_best[kQ8Warps];
+    const uint32_t blocks = (uint32_t)(p.k / 32);
+    uint32_t* rq = q8_smem;                                       // [blocks][9]: 8 words of quants + pad
+    float* rd = reinterpret_cast<float*>(q8_smem + blocks * 9);   // [blocks]: rhs scales
+    pdl_enter();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (uint32_t b = warp; b < blocks; b += kQ8Warps) {
+        const float x = p.rhs[(uint64_t)b * 32 + lane];
+        float amax = fabsf(x);
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, o));
+        const float scale = __fdiv_rn(amax, 127.0f);
+        const float inverse = scale == 0.0f ? 0.0f : __fdiv_rn(1.0f, scale);
+        float q = roundf(__fmul_rn(x, inverse));
+        q = is_nan(q) ? 0.0f : fminf(fmaxf(q, -127.0f), 127.0f);
+        reinterpret_cast<int8_t*>(rq + b * 9)[lane] = (int8_t)(int)q;
+        if (lane == 0) rd[b] = f16_bits_to_f32(f32_to_f16_bits(scale));
+    }
+    __syncthreads();
+    const uint64_t row_bytes = (uint64_t)blocks * 34;
+    MvPart best{0.0f, 0, 0u, 0u};
+    for (uint64_t row = (uint64_t)blockIdx.x * kQ8Warps + warp; row < p.rows; row += (uint64_t)gridDim.x * kQ8Warps) {
+        const uint8_t* rp = lhs + row * row_bytes;
+        float sum = 0.0f;
+        for (uint32_t b0 = 0; b0 < blocks; b0 += 32) {
+            const uint32_t b = b0 + lane;
+            float term = 0.0f;
+            if (b < blocks) {
+                const uint64_t off = (uint64_t)b * 34;
+                const bool odd = ((uintptr_t)(rp + off) & 3u) != 0;  // block starts 2 bytes into a word
+                const uint32_t* wp = reinterpret_cast<const uint32_t*>(rp + off - (odd ? 2 : 0));
+                uint32_t w[9];
+#pragma unroll
+                for (int j = 0; j < 8; ++j) w[j] = __ldg(wp + j);
+                // the last word: whole when the block ends on it, else its first half
+                w[8] = odd ? __ldg(wp + 8) : (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(wp + 8));
+                const uint32_t dbits = odd ? (w[0] >> 16) : (w[0] & 0xffffu);
+                const uint32_t* r = rq + b * 9;
+                int integer = 0;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    const uint32_t qw = odd ? w[j + 1] : __byte_perm(w[j], w[j + 1], 0x5432);
+                    integer = __dp4a((int)qw, (int)r[j], integer);
+                }
+                term = __fmul_rn((float)integer, __fmul_rn(f16_bits_to_f32((uint16_t)dbits), rd[b]));
+            }
+            const uint32_t n = blocks - b0 < 32u ? blocks - b0 : 32u;
+            for (uint32_t j = 0; j < n; ++j) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, term, (int)j));
+        }
+        const bool nan = is_nan(sum);
+        best = mv_better(best, MvPart{sum, (int32_t)row, nan ? 0u : 1u, (nan && row == 0) ? 1u : 0u});
+    }
+    if (lane == 0) warp_best[warp] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        MvPart b = warp_best[0];
+        for (int w = 1; w < kQ8Warps; ++w) b = mv_better(b, warp_best[w]);
+        warp_best[0] = b;
+    }
+    __syncthreads();
+    finish(p, warp_best[0]);
+}
+
 }  // namespace
 
 namespace {
@@ -273,6 +350,24 @@ cudaError_t launch_mul_mat_argmax(const LaunchEnv& env, const MvArgmaxPlan& p) {
         err = launch_dependent(mv_argmax_plain, dim3((unsigned)(tiles < cap ? tiles : cap)), dim3(kMvRows), 0,
                                env.stream, p);
     }
+    ++*env.launches;
+    return err != cudaSuccess ? err : cudaGetLastError();
+}
+
+cudaError_t launch_mul_mat_argmax_q8_0(const LaunchEnv& env, const MvArgmaxPlan& p, const uint8_t* lhs) {
+    const uint64_t groups = (p.rows + kQ8Warps - 1) / kQ8Warps;
+    const uint64_t cap = (uint64_t)env.sm_count * 4;
+    const size_t smem = (size_t)(p.k / 32) * (9 * 4 + 4);
+    static int configured_device_mask = 0;
+    const int bit = env.device < 31 ? (1 << env.device) : 0;
+    if (!(configured_device_mask & bit)) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(mv_argmax_q8_0, cudaFuncAttributeMaxDynamicSharedMemorySize, 1024 * 40);
+        if (e != cudaSuccess) return e;
+        configured_device_mask |= bit;
+    }
+    const cudaError_t err = launch_dependent(mv_argmax_q8_0, dim3((unsigned)(groups < cap ? groups : cap)),
+                                             dim3(kQ8Threads), smem, env.stream, p, lhs);
     ++*env.launches;
     return err != cudaSuccess ? err : cudaGetLastError();
 }

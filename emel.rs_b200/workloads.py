@@ -287,3 +287,44 @@ def mv_inputs(seed=14):
 def mv_spec():
     return Config("matvec", [OpSpec("mul_mat_argmax_vocab", (MV_K * MV_ROWS + MV_K) * F32 + 8, MV_K * MV_ROWS)])
 
+
+
+# Single-query attention (flash_attn.rs OpFlashAttnExt): one decode step of a
+# model with 32 query heads, 8 key/value heads and head_dim 128 (the head
+# shape of configuration 4a) over 4096 and 32768 cached tokens; query
+# N(0, 1) in binary32, key / value N(0, 1) in binary16.  Algorithmic bytes:
+# query and output once, every key / value element once.
+FA_D, FA_HEADS, FA_KV_HEADS = 128, 32, 8
+FA_TOKENS = (4096, 32768)
+
+
+def fa_inputs(tokens, seed=15):
+    rng = np.random.default_rng(seed + tokens)
+    q = normal(rng, (FA_HEADS * FA_D,))
+    k = normal(rng, (FA_KV_HEADS * tokens * FA_D,)).astype(np.float16)
+    v = normal(rng, (FA_KV_HEADS * tokens * FA_D,)).astype(np.float16)
+    return q, k, v
+
+
+def fa_spec():
+    return Config("attention", [OpSpec(f"flash_attn_decode_{t // 1024}k",
+                                       2 * FA_HEADS * FA_D * F32 + 2 * FA_KV_HEADS * t * FA_D * 2,
+                                       FA_HEADS * t * FA_D) for t in FA_TOKENS])
+
+
+# Diagonal family (diag.rs): a causal mask over a [4096, 4096] score matrix
+# (n_past 0, the query / key extent of configuration 4a), N(0, 1) scores.
+# Algorithmic bytes: the kept lower triangle read once, every element written.
+DIAG_SIDE = 4096
+
+
+def diag_inputs(seed=16):
+    rng = np.random.default_rng(seed)
+    return normal(rng, (DIAG_SIDE * DIAG_SIDE,))
+
+
+def diag_spec():
+    n = DIAG_SIDE * DIAG_SIDE
+    kept = DIAG_SIDE * (DIAG_SIDE + 1) // 2
+    return Config("diag", [OpSpec("diag_mask_inf_causal", (kept + n) * F32, n),
+                           OpSpec("diag_mask_zero_causal", (kept + n) * F32, n)])

@@ -68,6 +68,7 @@ typedef enum emel_cuda_status {
     EMEL_CUDA_INDEX_OUT_OF_BOUNDS = 9, /* GetRowsError::IndexOutOfBounds (get_rows.rs:522-535) */
     EMEL_CUDA_UNSUPPORTED_SOURCE_STRIDE = 10, /* GetRowsError::UnsupportedSourceStride */
     EMEL_CUDA_INVALID_MODE = 11,      /* RopeError::InvalidMode (rope.rs:104-117) */
+    EMEL_CUDA_INVALID_REQUEST = 12,   /* FlashAttnError::InvalidRequest (flash_attn.rs:35-44) */
     EMEL_CUDA_DEVICE_ERROR = 16,      /* a CUDA runtime call failed */
     EMEL_CUDA_TIMEOUT = 17,           /* a bounded device wait expired */
     EMEL_CUDA_INVALID_ARGUMENT = 18,  /* null context / output pointer */
@@ -397,6 +398,83 @@ EMEL_CUDA_API emel_cuda_status emel_cuda_rope(emel_cuda_context* ctx, void* stre
 EMEL_CUDA_API emel_cuda_status emel_cuda_mul_mat_argmax(emel_cuda_context* ctx, void* stream,
                                                         const emel_tensor_view* lhs, const emel_tensor_view* rhs,
                                                         const emel_tensor_view* dst, int32_t* index_out);
+
+/* ---- diagonal family ---------------------------------------------------- */
+/* diag::OpDiag::new(input, output) (diag.rs:44-66) dispatched by
+ * DiagKernel::process_event: output (input_len^2 floats, row-major) becomes
+ * the diagonal matrix of input, +0 off the diagonal (diag.rs:332-343).
+ * input_len == 0 or output_len != input_len^2 is EMEL_CUDA_INVALID_SHAPE
+ * (DiagError::InvalidShape) and writes nothing.  Device additions: a null
+ * context, null or not 4-byte aligned pointers, or overlapping input and
+ * output are EMEL_CUDA_INVALID_ARGUMENT.  Lengths count floats. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_diag(emel_cuda_context* ctx, void* stream, const float* input,
+                                              uint64_t input_len, float* output, uint64_t output_len);
+enum emel_diag_mask_mode { EMEL_DIAG_MASK_INF = 0, EMEL_DIAG_MASK_ZERO = 1 };
+/* diag::OpDiagMaskInf / OpDiagMaskZero::new(input, output, n_past)
+ * (diag.rs:68-108): for a side x side row-major matrix, output[row, col] =
+ * -inf (EMEL_DIAG_MASK_INF) or +0 (EMEL_DIAG_MASK_ZERO) where col > row +
+ * n_past, else input[row, col] with its bits (diag.rs:144-161).  n_past <
+ * 0, input_len != output_len, or a length that is not a non-zero perfect
+ * square is EMEL_CUDA_INVALID_SHAPE (mask_valid, diag.rs:122-124) and
+ * writes nothing.  Device additions: an unknown mode, a null context, null
+ * or not 4-byte aligned pointers, or partially overlapping slices are
+ * EMEL_CUDA_INVALID_ARGUMENT; output == input (in place) is allowed. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_diag_mask(emel_cuda_context* ctx, void* stream, int mode,
+                                                   const float* input, uint64_t input_len, float* output,
+                                                   uint64_t output_len, int32_t n_past);
+
+/* ---- single-query attention ------------------------------------------- */
+/* flash_attn.rs FlashAttnOptions (flash_attn.rs:24-31): has_scale == 0
+ * selects 1 / sqrt(head_dim); has_masked_total_tokens == 0 selects the
+ * key's token count.  A null options pointer is both defaults. */
+typedef struct emel_flash_attn_options {
+    float scale;
+    uint32_t has_scale;
+    uint32_t masked_total_tokens;
+    uint32_t has_masked_total_tokens;
+} emel_flash_attn_options;
+/* flash_attn::OpFlashAttnExt::new(query, key, value, destination, options)
+ * (flash_attn.rs:78-99) dispatched by FlashAttnKernel::process_event
+ * (flash_attn.rs:198-203): query and dst F32 [head_dim, 1, heads, 1], dense
+ * (flash_attn.rs:305-325); key and value F16 [head_dim, tokens, kv_heads, 1]
+ * (F16View, f16_matmul.rs:45-85: any even strides on multi-element
+ * dimensions); heads a multiple of kv_heads, head h reading kv head
+ * h / (heads / kv_heads); head_dim <= 4096; masked_total_tokens >= tokens;
+ * scale finite and > 0.  Any failed rule is EMEL_CUDA_INVALID_REQUEST and
+ * nothing is written.  Per head, the reference's sequential recurrence
+ * (flash_attn.rs:329-404) bit for bit: query rounded to binary16, score =
+ * binary32(binary64 sum over the row of q * k) * scale, a running maximum,
+ * a binary16 accumulator row rescaled when the maximum moves and updated
+ * with v * round16(exp(score - max)), a binary32 score sum; out = acc /
+ * sum, or 0 where the sum is 0.  Device additions: 4-byte aligned query /
+ * dst and 2-byte aligned key / value pointers, heads < 2^31, else
+ * EMEL_CUDA_INVALID_ARGUMENT.  One CTA per query head; allocates nothing. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_flash_attn_ext(emel_cuda_context* ctx, void* stream,
+                                                        const emel_tensor_view* query, const emel_tensor_view* key,
+                                                        const emel_tensor_view* value, const emel_tensor_view* dst,
+                                                        const emel_flash_attn_options* options);
+/* FlashAttnKernel::prepared_tokens / reuse_count (flash_attn.rs:205-215):
+ * the token count of the context's last accepted attention call, and how
+ * many accepted calls in a row repeated the token count before them. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_flash_attn_workspace(const emel_cuda_context* ctx,
+                                                              uint64_t* prepared_tokens, uint64_t* reuse_count);
+
+/* matmul::OpMulMatArgmaxQ8_0 (matmul.rs:500-520, routes 2958-2970): lhs
+ * Q8_0 packed rows [k, m, 1, 1] (PackedRowView, tensor_view.rs:483-526:
+ * nb[0] == 1, nb[1] == k / 32 * 34 bytes; k / 32 <= 1024 blocks), rhs dense
+ * F32 [1, k, 1, 1], dst dense F32 [1, 1, 1, 1].  The rhs is quantized to
+ * Q8_0 (quantize_q8_0, matmul.rs:1629-1653: scale = amax / 127 stored as
+ * binary16, q = clamp(round(x / scale), -127, 127)); the score of row r is
+ * the block-ordered binary32 sum of float(integer block dot) * (d_lhs *
+ * d_rhs) (dot_q8_0, matmul.rs:1893-1910); the answer is the first row with
+ * the largest score.  Writes the score to dst[0] and the row to *index_out
+ * (device int32).  Statuses: INVALID_VIEW, SHAPE_MISMATCH (nothing
+ * written).  Device additions: 4-byte aligned pointers, m < 2^31, non-null
+ * index_out, else INVALID_ARGUMENT.  Uses the context's reduction workspace
+ * (one call at a time per context). */
+EMEL_CUDA_API emel_cuda_status emel_cuda_mul_mat_argmax_q8_0(emel_cuda_context* ctx, void* stream,
+                                                             const emel_tensor_view* lhs, const emel_tensor_view* rhs,
+                                                             const emel_tensor_view* dst, int32_t* index_out);
 
 /* ---- shape copies ----------------------------------------------------- */
 /* shape::OpCpy (shape.rs:55-69; guards 453-466, loop copy_view 438-444):

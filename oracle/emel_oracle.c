@@ -563,6 +563,52 @@ int oracle_glu(int subop, const float* input, uint64_t input_len, float* output,
     return ORACLE_OK;
 }
 
+/* ---------------------------------------------------------------------- */
+/* Diagonal family: diag.rs OpDiag / OpDiagMaskInf / OpDiagMaskZero        */
+/* ---------------------------------------------------------------------- */
+
+/* square_side (diag.rs:107-120): the side of a non-empty perfect square. */
+static int diag_square_side(uint64_t len, uint64_t* side) {
+    if (len == 0) return 0;
+    uint64_t s = (uint64_t)sqrt((double)len);
+    while (s > 0 && s * s > len) --s;
+    while ((s + 1) * (s + 1) <= len) ++s;
+    if (s * s != len) return 0;
+    *side = s;
+    return 1;
+}
+
+/* OpDiag::side (diag.rs:56-65) and effect_diag (diag.rs:332-343): output
+ * filled with +0, then output[i * n + i] = input[i]. */
+int oracle_diag(const float* input, uint64_t input_len, float* output, uint64_t output_len) {
+    const uint64_t n = input_len;
+    uint64_t nn;
+    if (n == 0 || __builtin_mul_overflow(n, n, &nn) || output_len != nn) return ORACLE_INVALID_SHAPE;
+    for (uint64_t i = 0; i < nn; ++i) output[i] = 0.0f;
+    for (uint64_t i = 0; i < n; ++i) output[i * n + i] = input[i];
+    return ORACLE_OK;
+}
+
+/* mask_valid (diag.rs:122-124) and apply_mask (diag.rs:144-161): mode 0
+ * writes -inf, mode 1 writes +0 where col > row + n_past; elsewhere the
+ * input element (bits unchanged). */
+int oracle_diag_mask(int mode, const float* input, uint64_t input_len, float* output, uint64_t output_len,
+                     int32_t n_past) {
+    uint64_t side;
+    if (mode != 0 && mode != 1) return ORACLE_UNEXPECTED_EVENT;
+    if (n_past < 0 || input_len != output_len || !diag_square_side(input_len, &side)) return ORACLE_INVALID_SHAPE;
+    const float masked = mode == 0 ? -INFINITY : 0.0f;
+    for (uint64_t row = 0; row < side; ++row)
+        for (uint64_t col = 0; col < side; ++col) {
+            const uint64_t i = row * side + col;
+            if (col > row + (uint64_t)n_past)
+                output[i] = masked;
+            else
+                memcpy(&output[i], &input[i], 4);
+        }
+    return ORACLE_OK;
+}
+
 /* elementwise.rs:219-225 guards, 280-291 loop. */
 int oracle_add1(const oracle_view* src, const oracle_view* dst, float scalar) {
     uint64_t n;
@@ -1070,6 +1116,181 @@ int oracle_mul_mat_argmax(const oracle_view* lhs, const oracle_view* rhs, const 
     }
     *(float*)dst->data = best;
     if (index_out) *index_out = best_index;
+    return ORACLE_OK;
+}
+
+/* Q8_0 vocabulary matvec + argmax: matmul.rs OpMulMatArgmaxQ8_0.
+ * quantized_views_valid / quantized_shape_valid (matmul.rs:1522-1564),
+ * quantize_q8_0 (1629-1653), dot_q8_0 (1893-1910), run_argmax_q8_0
+ * (2474-2498): the rhs is quantized per 32-value block (scale = amax / 127
+ * stored as binary16, q = clamp(round(x / scale))), each lhs row is the sum
+ * over blocks, in order, of float(integer dot) * (d_lhs * d_rhs). */
+int oracle_mul_mat_argmax_q8_0(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
+                               int32_t* index_out) {
+    if (!gr_packed_view_valid(lhs, 8, 32, 34) || lhs->ne[0] / 32 > 1024 || !validate_as(rhs, DT_F32, 0, NULL) ||
+        !validate_as(dst, DT_F32, 0, NULL) || !dense_contiguous_f32(rhs) || !dense_contiguous_f32(dst))
+        return ORACLE_INVALID_VIEW;
+    const uint64_t* l = lhs->ne;
+    const uint64_t* r = rhs->ne;
+    const uint64_t* d = dst->ne;
+    if (!(l[0] > 0 && l[1] > 0 && l[2] == 1 && l[3] == 1 && r[0] == 1 && r[1] == l[0] && r[2] == 1 && r[3] == 1 &&
+          d[0] == 1 && d[1] == 1 && d[2] == 1 && d[3] == 1))
+        return ORACLE_SHAPE_MISMATCH;
+    const uint64_t blocks = l[0] / 32, rows = l[1], row_bytes = blocks * 34;
+    const float* x = (const float*)rhs->data;
+    static int8_t qs[1024 * 32];
+    static float dr[1024];
+    for (uint64_t b = 0; b < blocks; ++b) {
+        float amax = 0.0f;
+        for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(x[b * 32 + i]));
+        const float scale = amax / 127.0f;
+        const float inverse = scale == 0.0f ? 0.0f : 1.0f / scale;
+        dr[b] = gr_quant_fp16_to_f32(oracle_fp32_to_fp16(scale));
+        for (int i = 0; i < 32; ++i) {
+            float q = roundf(x[b * 32 + i] * inverse);
+            if (isnan(q)) q = 0.0f; /* `as i8` of NaN */
+            q = q < -127.0f ? -127.0f : (q > 127.0f ? 127.0f : q);
+            qs[b * 32 + i] = (int8_t)q;
+        }
+    }
+    const uint8_t* base = (const uint8_t*)lhs->data;
+    float best = -INFINITY;
+    int32_t best_index = 0;
+    for (uint64_t row = 0; row < rows; ++row) {
+        const uint8_t* rp = base + row * row_bytes;
+        float sum = 0.0f;
+        for (uint64_t b = 0; b < blocks; ++b) {
+            int32_t integer = 0;
+            for (int i = 0; i < 32; ++i) integer += (int32_t)(int8_t)rp[b * 34 + 2 + i] * (int32_t)qs[b * 32 + i];
+            sum += (float)integer * (gr_quant_fp16_to_f32(gr_le16(rp + b * 34)) * dr[b]);
+        }
+        if (sum > best || row == 0) {
+            best = sum;
+            best_index = (int32_t)row;
+        }
+    }
+    *(float*)dst->data = best;
+    if (index_out) *index_out = best_index;
+    return ORACLE_OK;
+}
+
+/* ---------------------------------------------------------------------- */
+/* Single-query attention: flash_attn.rs OpFlashAttnExt                    */
+/* ---------------------------------------------------------------------- */
+
+/* flash_attn.rs:528-557: binary32 -> binary16 bits.  Normal results round
+ * to nearest even; results below 2^-24 flush to a signed zero and the
+ * subnormal range rounds half up (not IEEE); any NaN is 0x7E00 with the
+ * input's sign. */
+uint16_t oracle_fa_f32_to_f16(float value) {
+    const uint32_t w = f2u(value);
+    const uint16_t sign = (uint16_t)((w >> 16) & 0x8000u);
+    const uint32_t e = (w >> 23) & 0xffu, frac = w & 0x7fffffu;
+    if (e == 0xffu) return (uint16_t)(sign | (frac == 0 ? 0x7c00u : 0x7e00u));
+    if (e > 142u) return (uint16_t)(sign | 0x7c00u);
+    if (e < 103u) return sign;
+    if (e < 113u) {
+        const uint32_t shift = 113u - e, m = 0x800000u | frac;
+        return (uint16_t)(sign | ((m + (1u << (shift + 12u))) >> (shift + 13u)));
+    }
+    uint16_t h = (uint16_t)(sign | ((e - 112u) << 10) | (frac >> 13));
+    const uint32_t rem = frac & 0x1fffu;
+    if (rem > 0x1000u || (rem == 0x1000u && (h & 1u))) h = (uint16_t)(h + 1u);
+    return h;
+}
+
+/* round_fp16_scalar (flash_attn.rs:420-422): through the helper above and
+ * quant.rs's magic-number widening. */
+static float fa_round16(float v) { return gr_quant_fp16_to_f32(oracle_fa_f32_to_f16(v)); }
+
+/* dense_f32_layout (flash_attn.rs:305-325): effective strides exactly
+ * row-major (nb[0] == 0 resolves to that). */
+static int fa_dense_f32(const oracle_view* v) {
+    uint64_t s[4], expected = 4;
+    if (v->dtype != DT_F32 || !effective_strides(v, 4, s)) return 0;
+    for (int d = 0; d < 4; ++d) {
+        if (s[d] != expected) return 0;
+        if (__builtin_mul_overflow(expected, v->ne[d], &expected)) return 0;
+    }
+    return 1;
+}
+
+/* OpFlashAttnExt::new (flash_attn.rs:78-99), valid_request (262-303) and
+ * execute (329-404) with its helpers (406-470): per head, one sequential
+ * pass over the key/value tokens with a running maximum, a binary16
+ * accumulator row and a binary32 score sum. */
+int oracle_flash_attn_ext(const oracle_view* q, const oracle_view* k, const oracle_view* v, const oracle_view* dst,
+                          const oracle_flash_attn_options* options) {
+    if (!q || !k || !v || !dst) return ORACLE_INVALID_ARGUMENT;
+    const uint64_t head_dim = q->ne[0], query_count = q->ne[1], heads = q->ne[2];
+    const uint64_t tokens = k->ne[1], kv_heads = k->ne[2];
+    float scale = 1.0f / sqrtf((float)head_dim);
+    uint64_t masked_total = tokens;
+    if (options && options->has_scale) scale = options->scale;
+    if (options && options->has_masked_total_tokens) masked_total = options->masked_total_tokens;
+    uint64_t ks[4], vs[4];
+    const int valid =
+        validate_as(q, DT_F32, 0, NULL) && validate_as(dst, DT_F32, 0, NULL) && gr_half_view_valid(k, DT_F16) &&
+        gr_half_view_valid(v, DT_F16) && fa_dense_f32(q) && fa_dense_f32(dst) && head_dim != 0 && query_count == 1 &&
+        heads != 0 && tokens != 0 && kv_heads != 0 && k->ne[0] == head_dim && v->ne[0] == head_dim &&
+        v->ne[1] == tokens && v->ne[2] == kv_heads && dst->ne[0] == head_dim && dst->ne[1] == query_count &&
+        dst->ne[2] == heads && q->ne[3] == 1 && k->ne[3] == 1 && v->ne[3] == 1 && dst->ne[3] == 1 &&
+        heads % kv_heads == 0 && head_dim <= 4096 && masked_total >= tokens && isfinite(scale) && scale > 0.0f;
+    if (!valid) return ORACLE_INVALID_REQUEST;
+    effective_strides(k, 2, ks);
+    effective_strides(v, 2, vs);
+    const float* qd = (const float*)q->data;
+    float* out = (float*)dst->data;
+    const unsigned char* kb = (const unsigned char*)k->data;
+    const unsigned char* vb = (const unsigned char*)v->data;
+    const uint64_t rep = heads / kv_heads;
+    uint16_t qh[4096], acc[4096];
+    for (uint64_t h = 0; h < heads; ++h) {
+        const uint64_t kvh = h / rep;
+        for (uint64_t d = 0; d < head_dim; ++d) {
+            qh[d] = oracle_fa_f32_to_f16(qd[h * head_dim + d]);
+            acc[d] = 0;
+        }
+        float score_sum = 0.0f, max_score = -INFINITY;
+        for (uint64_t t = 0; t < tokens; ++t) {
+            /* dot_product_f16_f16_scores (flash_attn.rs:424-441) */
+            double dot = 0.0;
+            for (uint64_t d = 0; d < head_dim; ++d) {
+                uint16_t kh;
+                memcpy(&kh, kb + d * ks[0] + t * ks[1] + kvh * ks[2], 2);
+                dot += (double)gr_quant_fp16_to_f32(qh[d]) * (double)gr_f16_bits_to_f32(kh);
+            }
+            const float score = (float)dot * scale;
+            const float old_max = max_score;
+            float max_scale = 1.0f, value_scale = 1.0f;
+            if (score > max_score) {
+                max_score = score;
+                max_scale = expf(old_max - max_score);
+                /* scale_f16_buffer_scalar (flash_attn.rs:443-451) */
+                const float rs = fa_round16(max_scale);
+                for (uint64_t d = 0; d < head_dim; ++d)
+                    acc[d] = oracle_fa_f32_to_f16(fa_round16(gr_quant_fp16_to_f32(acc[d]) * rs));
+            } else {
+                value_scale = expf(score - max_score);
+            }
+            /* axpy_f16_buffer_scalar (flash_attn.rs:453-470) */
+            const float alpha = fa_round16(value_scale);
+            for (uint64_t d = 0; d < head_dim; ++d) {
+                uint16_t vh;
+                memcpy(&vh, vb + d * vs[0] + t * vs[1] + kvh * vs[2], 2);
+                const float prod = gr_f16_bits_to_f32(vh) * alpha;
+                acc[d] = oracle_fa_f32_to_f16(fa_round16(gr_quant_fp16_to_f32(acc[d]) + prod));
+            }
+            score_sum = score_sum * max_scale + value_scale;
+        }
+        /* finalize_attention_output (flash_attn.rs:382-404) */
+        if (score_sum == 0.0f) {
+            for (uint64_t d = 0; d < head_dim; ++d) out[h * head_dim + d] = 0.0f;
+        } else {
+            const float inv = 1.0f / score_sum;
+            for (uint64_t d = 0; d < head_dim; ++d) out[h * head_dim + d] = gr_quant_fp16_to_f32(acc[d]) * inv;
+        }
+    }
     return ORACLE_OK;
 }
 

@@ -51,6 +51,7 @@ enum {
     ORACLE_INDEX_OUT_OF_BOUNDS = 9,
     ORACLE_UNSUPPORTED_SOURCE_STRIDE = 10,
     ORACLE_INVALID_MODE = 11,
+    ORACLE_INVALID_REQUEST = 12,
     ORACLE_INVALID_ARGUMENT = 18
 };
 
@@ -69,6 +70,28 @@ int oracle_leaky_relu(const oracle_view* src, const oracle_view* dst, float slop
 int oracle_silu_back(const oracle_view* src, const oracle_view* grad, const oracle_view* dst);
 /* matmul.rs OpMulMatArgmax: lhs [k, m] dense, rhs [1, k] dense, dst [1]. */
 int oracle_mul_mat_argmax(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst, int32_t* index_out);
+/* matmul.rs OpMulMatArgmaxQ8_0: lhs Q8_0 packed rows [k, m] (k % 32 == 0,
+ * k / 32 <= 1024), rhs [1, k] dense F32, dst [1]. */
+int oracle_mul_mat_argmax_q8_0(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
+                               int32_t* index_out);
+/* diag.rs OpDiag / OpDiagMaskInf (mode 0) / OpDiagMaskZero (mode 1) over flat
+ * f32 slices. */
+int oracle_diag(const float* input, uint64_t input_len, float* output, uint64_t output_len);
+int oracle_diag_mask(int mode, const float* input, uint64_t input_len, float* output, uint64_t output_len,
+                     int32_t n_past);
+/* flash_attn.rs FlashAttnOptions (flash_attn.rs:24-31): an absent scale is
+ * 1 / sqrt(head_dim), an absent token count is the key's ne[1]. */
+typedef struct oracle_flash_attn_options {
+    float scale;
+    uint32_t has_scale;
+    uint32_t masked_total_tokens;
+    uint32_t has_masked_total_tokens;
+} oracle_flash_attn_options;
+/* flash_attn.rs OpFlashAttnExt: query / dst dense F32 [d, 1, h, 1], key /
+ * value F16 [d, t, hkv, 1] (any even strides); options nullable. */
+uint16_t oracle_fa_f32_to_f16(float value); /* flash_attn.rs:528-557 */
+int oracle_flash_attn_ext(const oracle_view* query, const oracle_view* key, const oracle_view* value,
+                          const oracle_view* dst, const oracle_flash_attn_options* options);
 /* rope.rs RopeParams (rope.rs:33-48) and OpRope. */
 typedef struct oracle_rope_params {
     int32_t n_dims;

@@ -66,6 +66,12 @@ class RopeParams(ctypes.Structure):
                 ("freq_scale", ctypes.c_float), ("ext_factor", ctypes.c_float), ("attn_factor", ctypes.c_float)]
 
 
+class FlashAttnOptions(ctypes.Structure):
+    """oracle_flash_attn_options / emel_flash_attn_options (flash_attn.rs:24-31)."""
+    _fields_ = [("scale", ctypes.c_float), ("has_scale", ctypes.c_uint32),
+                ("masked_total_tokens", ctypes.c_uint32), ("has_masked_total_tokens", ctypes.c_uint32)]
+
+
 class GenericRequest(ctypes.Structure):
     """oracle_generic_request (same layout as emel_cuda_generic_request)."""
     _fields_ = [("op", ctypes.c_uint32), ("unary_subop", ctypes.c_uint32),
@@ -115,7 +121,12 @@ def load(cr=False):
         "oracle_cpy": [P, P],
         "oracle_get_rows": [P, P, P],
         "oracle_mul_mat_argmax": [P, P, P, ctypes.POINTER(ctypes.c_int32)],
+        "oracle_mul_mat_argmax_q8_0": [P, P, P, ctypes.POINTER(ctypes.c_int32)],
         "oracle_rope": [P, P, P, ctypes.POINTER(RopeParams)],
+        "oracle_flash_attn_ext": [P, P, P, P, ctypes.POINTER(FlashAttnOptions)],
+        "oracle_diag": [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_uint64],
+        "oracle_diag_mask": [ctypes.c_int, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_uint64,
+                             ctypes.c_int32],
         "oracle_cont": [P, P],
         "oracle_norm": [P, P, ctypes.c_float],
         "oracle_rms_norm": [P, P, ctypes.c_float],
@@ -143,5 +154,7 @@ def load(cr=False):
     lib.oracle_fp32_to_fp16.restype = ctypes.c_uint16
     lib.oracle_fp16_to_fp32.argtypes = [ctypes.c_uint16]
     lib.oracle_fp16_to_fp32.restype = ctypes.c_float
+    lib.oracle_fa_f32_to_f16.argtypes = [ctypes.c_float]
+    lib.oracle_fa_f32_to_f16.restype = ctypes.c_uint16
     _libs[cr] = lib
     return lib

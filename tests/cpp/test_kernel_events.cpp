@@ -1,7 +1,8 @@
 // C++ mirror of the reference's own unit tests, run through the device op
 // table: each case restates a known answer from
 // crates/emel-kernels/tests/any/{binary_ops,broadcast_ops,normalization_ops,
-// reductions,softmax_ops}.rs with the same inputs, events and expected values.
+// reductions,softmax_ops,flash_attn_ops}.rs with the same inputs, events and
+// expected values.
 #include <cmath>
 #include <cstdio>
 #include <cstring>
@@ -115,6 +116,28 @@ static void softmax_rows(Kernel& k) {
     CHECK(!r.is_ok() && r.error() == ReductionError::ShapeMismatch && same(dst.read(), {9, 9, 9}), "count mismatch");
 }
 
+// tools/emel-kernel-flash-attn-parity/src/main.rs:61-104 and its manifest
+// (snapshots/parity/kernel-flash-attn): exact output bits; flash_attn_ops.rs:220-250
+static void flash_attn_golden(Kernel& k) {
+    const std::vector<uint16_t> key{0x3c00, 0, 0, 0, 0, 0x3c00, 0, 0}, value{0x4000, 0x4400, 0x4600, 0x4800};
+    DeviceBuffer kb(k, key.size() * 2), vb(k, value.size() * 2);
+    kb.upload(key.data(), key.size() * 2);
+    vb.upload(value.data(), value.size() * 2);
+    Buf q(k, {1, 0, 1, 0}), out(k, std::vector<float>(4, 0.0f));
+    Layout ql = contiguous({2, 1, 2, 1});
+    Layout kvl = *Layout::contiguous(DType::F16, {2, 2, 1, 1});
+    FlashAttnOptions o{1.0f, 2u};
+    CHECK(k.process_event(OpFlashAttnExt(q.view(ql), kb.view(kvl), vb.view(kvl), out.view(ql), o)).is_ok(), "attn ok");
+    const uint32_t want[4] = {0x4044d668u, 0x40a27a4fu, 0x4044d668u, 0x40a27a4fu};
+    auto got = out.read();
+    CHECK(std::memcmp(got.data(), want, 16) == 0, "attn golden bits");
+    Buf rejected(k, std::vector<float>(4, 9.0f));
+    Result r = k.process_event(OpFlashAttnExt(q.view(ql), kb.view(kvl), vb.view(kvl), rejected.view(ql),
+                                              FlashAttnOptions{0.0f, 2u}));
+    CHECK(!r.is_ok() && r.error() == FlashAttnError::InvalidRequest && same(rejected.read(), {9, 9, 9, 9}),
+          "attn invalid scale");
+}
+
 int main() {
     Kernel k(0);
     binary_formulas(k);
@@ -123,6 +146,7 @@ int main() {
     normalization_known_answers(k);
     reductions_known_answers(k);
     softmax_rows(k);
+    flash_attn_golden(k);
     std::printf("%s: %d failure(s)\n", failures ? "FAILED" : "ok", failures);
     return failures ? 1 : 0;
 }

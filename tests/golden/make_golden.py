@@ -256,10 +256,69 @@ def main(root):
           view([0.0] * 6, d32, [4, 12, 0, 0]), [10, 40, 90, 40, 100, 180], {"op": 2},
           "crates/emel-kernels/tests/any/broadcast_ops.rs:91-108")
 
+    write_flash_attn(root)
+
     dst = Path(__file__).resolve().parent / "reference_parity.json"
     dst.write_text(json.dumps({"generated_from": "stateforward/emel.rs snapshots/parity + tools/*-parity + tests/any",
                                "cases": out}, indent=1, allow_nan=True) + "\n")
     print(f"wrote {len(out)} cases to {dst}")
+
+
+def write_flash_attn(root):
+    """tests/golden/flash_attn_parity.json: the kernel-flash-attn manifest's
+    cases with the inputs of tools/emel-kernel-flash-attn-parity/src/main.rs:61-104
+    (query [2, 1, 2, 1] F32, key / value [2, 2, 1, 1] F16 as raw bits, the key
+    buffer eight halves long as in the observer), plus the known answers of
+    crates/emel-kernels/tests/any/flash_attn_ops.rs (approximate values, with
+    the tolerance each test states)."""
+    m = parse_manifest(root, "kernel-flash-attn")
+    src = "tools/emel-kernel-flash-attn-parity/src/main.rs:61-104"
+    q = [1.0, 0.0, 1.0, 0.0]
+    key = [0x3C00, 0, 0, 0, 0, 0x3C00, 0, 0]
+    value = [0x4000, 0x4400, 0x4600, 0x4800]
+    kv = {"ne": [2, 2, 1, 1], "nb": [2, 4, 8, 8]}
+    qd = {"ne": [2, 1, 2, 1], "nb": contiguous_nb([2, 1, 2, 1])}
+    cases = []
+    for case, scale in (("canonical", 1.0), ("invalid_scale", 0.0)):
+        cases.append({"case": case, "source": src, "query": q, "query_layout": qd, "key": key, "key_layout": kv,
+                      "value": value, "value_layout": kv, "dst_layout": qd, "dst_fill": 9.0 if scale == 0.0 else 0.0,
+                      "scale": scale, "masked_total_tokens": 2, "expect_status": status_code(m[case]),
+                      "expect_bits": m[case]["bits"], "compare": "exact"})
+    t = "crates/emel-kernels/tests/any/flash_attn_ops.rs"
+    one = {"ne": [1, 1, 1, 1], "nb": [2, 2, 2, 2]}
+    one32 = {"ne": [1, 1, 1, 1], "nb": [4, 4, 4, 4]}
+
+    def known(case, source, query, ql, key_, kl, value_, vl, dl, expect, tol, scale=None, masked=None, fill=0.0,
+              status="ok"):
+        cases.append({"case": case, "source": source, "query": query, "query_layout": ql, "key": key_,
+                      "key_layout": kl, "value": value_, "value_layout": vl, "dst_layout": dl, "dst_fill": fill,
+                      "scale": scale, "masked_total_tokens": masked, "expect_status": status,
+                      "expect_values": expect, "tolerance": tol, "compare": "approx"})
+
+    known("online_attention_formula", t + ":28-85", q, qd, key[:4], kv, value, kv, qd,
+          [3.0758, 5.0758, 3.0758, 5.0758], 0.01, scale=1.0)
+    hl = {"ne": [1, 1, 2, 1], "nb": [4, 4, 4, 8]}
+    known("head_replication", t + ":87-118", [1.0, 1.0], hl, [0x3C00, 0x3C00], {"ne": [1, 2, 1, 1], "nb": [2, 2, 4, 4]},
+          [0x4000, 0x4400], {"ne": [1, 2, 1, 1], "nb": [2, 2, 4, 4]}, hl, [3.0, 3.0], 0.02, scale=1.0, masked=2)
+    known("implicit_contiguous", t + ":120-145", [1.0], {"ne": [1, 1, 1, 1], "nb": [0, 99, 0, 0]}, [0x3C00],
+          {"ne": [1, 1, 1, 1], "nb": [0, 99, 0, 0]}, [0x4000], {"ne": [1, 1, 1, 1], "nb": [0, 99, 0, 0]},
+          {"ne": [1, 1, 1, 1], "nb": [0, 99, 0, 0]}, [2.0], 0.01, scale=1.0, masked=1)
+    known("singleton_unaligned_strides", t + ":147-174", [1.0], one32, [0x3C00], {"ne": [1, 1, 1, 1], "nb": [2, 0, 1, 3]},
+          [0x4000], {"ne": [1, 1, 1, 1], "nb": [2, 1, 3, 5]}, one32, [2.0], 0.01, scale=1.0, masked=1)
+    known("multi_element_unaligned_stride", t + ":176-198", [1.0, 0.0], {"ne": [2, 1, 1, 1], "nb": [4, 8, 8, 8]},
+          [0x3C00, 0], {"ne": [2, 1, 1, 1], "nb": [3, 6, 12, 24]}, [0x4000, 0x4000],
+          {"ne": [2, 1, 1, 1], "nb": [2, 4, 4, 4]}, {"ne": [2, 1, 1, 1], "nb": [4, 8, 8, 8]}, [9.0, 9.0], 0.0,
+          fill=9.0, status="rejected")
+    known("unexpected_then_default_options", t + ":252-275", [1.0], one32, [0x3C00], one, [0x4000], one, one32,
+          [2.0], 0.01)
+    known("zero_scale_rejected", t + ":220-250", [1.0, 0.0], {"ne": [2, 1, 1, 1], "nb": [4, 8, 8, 8]}, [0, 0, 0, 0],
+          {"ne": [2, 2, 1, 1], "nb": [2, 4, 8, 8]}, [0, 0, 0, 0], {"ne": [2, 2, 1, 1], "nb": [2, 4, 8, 8]},
+          {"ne": [2, 1, 1, 1], "nb": [4, 8, 8, 8]}, [9.0, 9.0], 0.0, scale=0.0, masked=1, fill=9.0, status="rejected")
+    dst = Path(__file__).resolve().parent / "flash_attn_parity.json"
+    dst.write_text(json.dumps({"generated_from": "stateforward/emel.rs snapshots/parity/kernel-flash-attn + "
+                               "tools/emel-kernel-flash-attn-parity + tests/any/flash_attn_ops.rs",
+                               "cases": cases}, indent=1) + "\n")
+    print(f"wrote {len(cases)} cases to {dst}")
 
 
 if __name__ == "__main__":

@@ -150,6 +150,72 @@ def test_validation_matches_reference_guards(emel, oracle_lib, family, nviews):
     assert agree == 400
 
 
+def test_flash_attn_validation_matches_reference_guards(emel, oracle_lib):
+    """valid_request (flash_attn.rs:262-303) on layouts around its boundary:
+    the C ABI's outcome equals the oracle's restatement for every request."""
+    lib = emel.lib()
+    rng = np.random.default_rng(77)
+    buf = np.zeros(1 << 14, dtype=np.float32)
+    B = ctypes.byref
+    accepted = 0
+    for trial in range(600):
+        d = int(rng.choice([0, 1, 2, 4, 8]))
+        heads = int(rng.choice([0, 1, 2, 4]))
+        kvh = int(rng.choice([0, 1, 2, 3]))
+        t = int(rng.choice([0, 1, 3]))
+        qne = [d, int(rng.choice([1, 1, 1, 2])), heads, 1]
+        kne = [d if rng.random() < 0.9 else d + 1, t, kvh, int(rng.choice([1, 1, 1, 2]))]
+        vne = list(kne) if rng.random() < 0.9 else [d, t + 1, kvh, 1]
+        dne = list(qne) if rng.random() < 0.9 else [d, 1, heads + 1, 1]
+
+        def lay(ne, elem):
+            kind = rng.integers(0, 5)
+            if kind == 0:
+                nb = [0, 0, 0, 0]
+            else:
+                nb = [elem]
+                for k in range(1, 4):
+                    nb.append(nb[-1] * max(ne[k - 1], 1))
+                if kind == 2:
+                    nb = [x * 2 for x in nb]
+                elif kind == 3:
+                    nb[int(rng.integers(0, 4))] += int(rng.choice([1, 2, 3]))
+            eff = nb if nb[0] != 0 else [elem] + [elem * int(np.prod([max(n, 1) for n in ne[:k]])) for k in range(1, 4)]
+            span = sum(max(n - 1, 0) * st for n, st in zip(ne, eff)) + elem
+            return ne, nb, max(span - int(rng.choice([0, 0, 0, 1, 2])), 0)
+
+        views = [lay(qne, 4), lay(kne, 2), lay(vne, 2), lay(dne, 4)]
+        dtypes = [0, 1 if rng.random() < 0.95 else 0, 1, 0]
+        scale = [None, 0.5, 0.0, -1.0, float("inf"), float("nan")][int(rng.integers(0, 6))]
+        masked = [None, 0, 1, 3, 4][int(rng.integers(0, 5))]
+        if trial % 2 == 0:
+            # a well-formed request with one perturbation at most
+            d, kvh = int(rng.choice([1, 2, 4, 8])), int(rng.choice([1, 2]))
+            heads, t = kvh * int(rng.choice([1, 2])), int(rng.choice([1, 3]))
+            shapes = [([d, 1, heads, 1], 4), ([d, t, kvh, 1], 2), ([d, t, kvh, 1], 2), ([d, 1, heads, 1], 4)]
+            views = [lay(ne, elem) if rng.random() < 0.7 else (ne, [0, 0, 0, 0], int(np.prod(ne)) * elem)
+                     for ne, elem in shapes]
+            dtypes = [0, 1, 1, 0]
+            scale = [None, 0.5, 0.0][int(rng.integers(0, 3))]
+            masked = [None, t, t + 2, max(t - 1, 0)][int(rng.integers(0, 4))]
+        cv = [cview(emel, buf.ctypes.data, st, ne, nb, dt) for (ne, nb, st), dt in zip(views, dtypes)]
+        ov = [oview(buf.ctypes.data, st, ne, nb, dt) for (ne, nb, st), dt in zip(views, dtypes)]
+        copt = emel.CFlashAttnOptions.of(scale, masked)
+        oopt = oracle.FlashAttnOptions()
+        if scale is not None:
+            oopt.scale, oopt.has_scale = scale, 1
+        if masked is not None:
+            oopt.masked_total_tokens, oopt.has_masked_total_tokens = masked, 1
+        got = lib.emel_cuda_flash_attn_ext(None, None, B(cv[0]), B(cv[1]), B(cv[2]), B(cv[3]), B(copt))
+        want = oracle_lib.oracle_flash_attn_ext(B(ov[0]), B(ov[1]), B(ov[2]), B(ov[3]), B(oopt))
+        if want == 0:
+            assert got == ACCEPTED, (views, dtypes, scale, masked, got)
+            accepted += 1
+        else:
+            assert want == 12 and got == 12, (views, dtypes, scale, masked, got, want)
+    assert accepted >= 20
+
+
 def test_misaligned_or_null_device_pointer_is_an_invalid_view(emel):
     lib = emel.lib()
     ne, nb = [4, 1, 1, 1], [4, 16, 16, 16]
@@ -181,3 +247,38 @@ def test_argmax_combine_follows_first_index_and_nan_rules(emel):
     assert combine([(5.0, 1, 3, 1), (9.0, 1, 99, 0)])[0] == 0
     # a NaN first element in a later shard does not
     assert combine([(5.0, 1, 3, 0), (9.0, 1, 99, 1)])[0] == 99
+
+
+def test_q8_0_argmax_guards_match_oracle(emel, oracle_lib):
+    """quantized_views_valid / quantized_shape_valid (matmul.rs:1522-1564)
+    for OpMulMatArgmaxQ8_0: the C ABI's status equals the oracle's."""
+    lib = emel.lib()
+    B = ctypes.byref
+    buf = np.zeros(1 << 16, np.uint8)
+    cases = []
+    for k in (32, 64, 48):
+        rb = k // 32 * 34
+        for rows in (1, 3):
+            good_l = ([k, rows, 1, 1], [1, rb, rb * rows, rb * rows], rb * rows, 8)
+            cases.append((good_l, ([1, k, 1, 1], [4, 4, 4 * k, 4 * k], 4 * k), ([1, 1, 1, 1], [4, 4, 4, 4], 4)))
+            cases.append((good_l, ([1, k, 1, 1], [4, 4, 4 * k, 4 * k], 4 * k - 1), ([1, 1, 1, 1], [4, 4, 4, 4], 4)))
+            cases.append((good_l, ([1, k + 1, 1, 1], [4, 4, 4 * k + 4, 4 * k + 4], 4 * k + 4),
+                          ([1, 1, 1, 1], [4, 4, 4, 4], 4)))
+            cases.append((good_l, ([k, 1, 1, 1], [4, 4 * k, 4 * k, 4 * k], 4 * k), ([1, 1, 1, 1], [4, 4, 4, 4], 4)))
+            cases.append((([k, rows, 1, 1], [1, rb + 2, (rb + 2) * rows, (rb + 2) * rows], (rb + 2) * rows, 8),
+                          ([1, k, 1, 1], [4, 4, 4 * k, 4 * k], 4 * k), ([1, 1, 1, 1], [4, 4, 4, 4], 4)))
+            cases.append((([k, rows, 1, 1], [1, rb, rb * rows, rb * rows], rb * rows, 2),
+                          ([1, k, 1, 1], [4, 4, 4 * k, 4 * k], 4 * k), ([1, 1, 1, 1], [4, 4, 4, 4], 4)))
+            cases.append((good_l, ([1, k, 1, 1], [0, 0, 0, 0], 4 * k), ([1, 1, 1, 1], [4, 4, 4, 4], 4)))
+            cases.append((good_l, ([1, k, 1, 1], [4, 4, 4 * k, 4 * k], 4 * k), ([2, 1, 1, 1], [4, 8, 8, 8], 8)))
+    seen = set()
+    for (lne, lnb, ls, lcode), (rne, rnb, rs), (dne, dnb, ds) in cases:
+        lv, ov_l = cview(emel, buf.ctypes.data, ls, lne, lnb, lcode), oview(buf.ctypes.data, ls, lne, lnb, lcode)
+        rv, ov_r = cview(emel, buf.ctypes.data, rs, rne, rnb), oview(buf.ctypes.data, rs, rne, rnb)
+        dv, ov_d = cview(emel, buf.ctypes.data, ds, dne, dnb), oview(buf.ctypes.data, ds, dne, dnb)
+        idx = ctypes.c_int32()
+        got = lib.emel_cuda_mul_mat_argmax_q8_0(None, None, B(lv), B(rv), B(dv), ctypes.c_void_p(4096))
+        want = oracle_lib.oracle_mul_mat_argmax_q8_0(B(ov_l), B(ov_r), B(ov_d), B(idx))
+        assert got == (ACCEPTED if want == 0 else want), (lne, lnb, lcode, rne, rnb, rs, dne, got, want)
+        seen.add(want)
+    assert seen == {0, 1, 2}

@@ -83,3 +83,92 @@ def test_ties_nan_rows_and_pinned_row_zero(emel, kern, oracle_lib, k):
     st, sync, ost, gv, gi, wv, wi = run_both(emel, kern, oracle_lib, lhs.ravel(), rhs, k, m)
     assert st == sync == ost == 0 and gi == wi == 0
     assert gv.view(np.uint32) == wv.view(np.uint32), (hex(gv.view(np.uint32)), hex(wv.view(np.uint32)))
+
+
+# ---- Q8_0 rows (matmul.rs OpMulMatArgmaxQ8_0) ---------------------------------
+
+def q8_rows(rng, k, rows, planted=None, scale_exp=(-12, -4)):
+    """Random Q8_0 rows: binary16 scales 2^e * u, quants uniform in [-127, 127]."""
+    blocks = k // 32
+    d = (rng.uniform(0.5, 1.0, size=(rows, blocks)) * 2.0 ** rng.integers(*scale_exp, size=(rows, blocks)))
+    d = d.astype(np.float16)
+    q = rng.integers(-127, 128, size=(rows, blocks, 32), dtype=np.int8)
+    if planted is not None:
+        q[planted] = np.abs(q[planted])
+        d[planted] = np.float16(0.5)
+    blob = np.empty((rows, blocks, 34), np.uint8)
+    blob[:, :, :2] = d.view(np.uint8).reshape(rows, blocks, 2)
+    blob[:, :, 2:] = q.view(np.uint8)
+    return blob.reshape(-1)
+
+
+def run_q8_both(emel, kern, olib, blob, rhs, k, rows, offset=0):
+    ctx = kern.ctx
+    rb = k // 32 * 34
+    store = np.zeros(blob.size + offset, np.uint8)
+    store[offset:] = blob
+    bl, br = emel.DeviceBuffer(ctx, store.nbytes + 16), emel.DeviceBuffer(ctx, rhs.nbytes)
+    bd, bi = emel.DeviceBuffer(ctx, 16), emel.DeviceBuffer(ctx, 16)
+    bl.upload(store)
+    br.upload(rhs)
+    v = emel.CView()
+    v.data, v.storage_bytes, v.dtype = bl.ptr + offset, blob.nbytes, 8
+    for dim, (n, s) in enumerate(zip([k, rows, 1, 1], [1, rb, rb * rows, rb * rows])):
+        v.ne[dim], v.nb[dim] = n, s
+    st = emel.lib().emel_cuda_mul_mat_argmax_q8_0(ctx.handle, None, B(v), B(cview(emel, br, rhs.nbytes, [1, k, 1, 1])),
+                                                  B(cview(emel, bd, 4, [1, 1, 1, 1])), ctypes.c_void_p(bi.ptr))
+    sync = emel.lib().emel_cuda_stream_synchronize(ctx.handle, None)
+    got_v = bd.download(np.empty(4, np.float32))[0]
+    got_i = int(bi.download(np.empty(4, np.int32))[0])
+    out = np.full(1, 9.0, np.float32)
+    idx = ctypes.c_int32()
+    ost = olib.oracle_mul_mat_argmax_q8_0(
+        B(oracle.make_view(blob.ctypes.data, blob.nbytes, [k, rows, 1, 1], [1, rb, rb * rows, rb * rows], 8)),
+        B(oracle.make_view(rhs.ctypes.data, rhs.nbytes, [1, k, 1, 1], nb_of([1, k, 1, 1]), 0)),
+        B(oracle.make_view(out.ctypes.data, out.nbytes, [1, 1, 1, 1], nb_of([1, 1, 1, 1]), 0)), B(idx))
+    for b in (bl, br, bd, bi):
+        b.free()
+    return int(st), int(sync), ost, np.float32(got_v), got_i, out[0], idx.value
+
+
+def test_q8_0_reference_golden_vector(emel, kern, oracle_lib):
+    # snapshots/parity/kernel-argmax-parity/manifest.txt case=q8_0_success
+    blob = np.zeros(544, np.uint8)
+    for b in range(16):
+        blob[b * 34:b * 34 + 2] = (0x00, 0x3C)
+        if b >= 8:
+            blob[b * 34 + 2:b * 34 + 34] = 1
+    st, sync, ost, gv, gi, ov, oi = run_q8_both(emel, kern, oracle_lib, blob, np.ones(256, np.float32), 256, 2)
+    assert st == 0 and sync == 0 and gi == 1 and int(np.array([gv]).view(np.uint32)[0]) == 0x437FFC00
+
+
+@pytest.mark.parametrize("k,rows,offset", [(32, 1, 0), (64, 7, 0), (96, 33, 2), (4096, 1000, 0), (4096, 151936, 0),
+                                           (32768, 64, 0), (288, 257, 2)])
+def test_q8_0_parity(emel, kern, oracle_lib, k, rows, offset):
+    rng = np.random.default_rng(k + rows)
+    planted = int(rng.integers(0, rows))
+    blob = q8_rows(rng, k, rows, planted)
+    rhs = np.abs(rng.standard_normal(k)).astype(np.float32)
+    if offset:
+        offset = 4  # a 4-byte aligned base that is not 16-byte aligned
+    st, sync, ost, gv, gi, ov, oi = run_q8_both(emel, kern, oracle_lib, blob, rhs, k, rows, offset)
+    assert st == 0 and sync == 0 and ost == 0
+    assert gi == oi and np.array([gv]).view(np.uint32)[0] == np.array([ov]).view(np.uint32)[0]
+
+
+def test_q8_0_special_values(emel, kern, oracle_lib):
+    rng = np.random.default_rng(8)
+    k, rows = 128, 50
+    blob = q8_rows(rng, k, rows)
+    rhs = rng.standard_normal(k).astype(np.float32)
+    rhs[5] = np.nan        # quantizes to 0
+    rhs[40] = np.inf       # block scale inf: every quant of that block 0 or NaN -> 0
+    rhs[70:102] = 0.0      # a zero block: scale 0
+    st, sync, ost, gv, gi, ov, oi = run_q8_both(emel, kern, oracle_lib, blob, rhs, k, rows)
+    assert st == 0 and sync == 0 and ost == 0
+    assert gi == oi and (np.isnan(gv) and np.isnan(ov) or np.array([gv]).view(np.uint32)[0] == np.array([ov]).view(np.uint32)[0])
+    # equal rows: the first wins
+    one = q8_rows(rng, k, 1)
+    blob = np.concatenate([one] * 5)
+    st, sync, ost, gv, gi, ov, oi = run_q8_both(emel, kern, oracle_lib, blob, np.ones(k, np.float32), k, 5)
+    assert gi == oi == 0

@@ -70,3 +70,79 @@ def test_sequential_binary32_order(lib):
     """The score is the left-to-right binary32 sum: 1e8 + 1 - 1e8 == 0."""
     st, out, idx = run(lib, [1e8, 1, -1e8, 0.5, 0.25, 0], [3, 2, 1, 1], [1, 1, 1], [1, 3, 1, 1])
     assert st == 0 and out[0] == 0.75 and idx == 1
+
+
+# ---- Q8_0 rows (matmul.rs OpMulMatArgmaxQ8_0) ---------------------------------
+
+def q8_layout(k, rows):
+    rb = k // 32 * 34
+    return [k, rows, 1, 1], [1, rb, rb * rows, rb * rows]
+
+
+def run_q8(lib, lhs_bytes, k, rows, rhs, fill=9.0, rne=None, rnb=None, code=8):
+    lhs = np.frombuffer(bytes(lhs_bytes), np.uint8).copy()
+    rhs = np.asarray(rhs, np.float32)
+    out = np.full(1, fill, np.float32)
+    idx = ctypes.c_int32(-7)
+    lne, lnb = q8_layout(k, rows)
+    rne = rne or [1, k, 1, 1]
+    st = lib.oracle_mul_mat_argmax_q8_0(B(oracle.make_view(lhs.ctypes.data, lhs.nbytes, lne, lnb, code)),
+                                        B(oracle.make_view(rhs.ctypes.data, rhs.nbytes, rne, rnb or nb_of(rne), 0)),
+                                        B(oracle.make_view(out.ctypes.data, out.nbytes, [1, 1, 1, 1], nb_of([1, 1, 1, 1]), 0)),
+                                        B(idx))
+    return st, out, idx.value
+
+
+def q8_constant_block(encoded):
+    # tests/any/matmul_ops.rs:76-82: scale 1.0 (0x3C00), every quant `encoded`
+    return bytes([0x00, 0x3C]) + bytes([encoded & 0xFF]) * 32
+
+
+def test_q8_0_reference_golden_vector(lib):
+    # snapshots/parity/kernel-argmax-parity/manifest.txt case=q8_0_success:
+    # index=1 output_bits=437ffc00, inputs from
+    # tools/emel-kernel-argmax-parity/src/main.rs:61-71 and 114-127
+    # (16 blocks of scale 1.0, blocks 8..15 with every quant 1; rhs 256 ones)
+    lhs = bytearray(544)
+    for b in range(16):
+        lhs[b * 34:b * 34 + 2] = bytes([0x00, 0x3C])
+        if b >= 8:
+            lhs[b * 34 + 2:b * 34 + 34] = bytes([1]) * 32
+    st, out, idx = run_q8(lib, lhs, 256, 2, np.ones(256), fill=np.float32(np.uint32(0x7FC01234).view(np.float32)))
+    assert st == 0 and idx == 1 and int(out.view(np.uint32)[0]) == 0x437FFC00
+
+
+def test_q8_0_known_answers(lib):
+    # tests/any/matmul_ops.rs:1266-1308: rows of constant quants 1 and 2
+    st, out, idx = run_q8(lib, q8_constant_block(1) + q8_constant_block(2), 32, 2, np.ones(32))
+    assert st == 0 and idx == 1 and out[0] > 0
+    # first row on ties
+    st, out, idx = run_q8(lib, q8_constant_block(3) + q8_constant_block(3), 32, 2, np.ones(32))
+    assert st == 0 and idx == 0
+
+
+def test_q8_0_guards(lib):
+    blk = q8_constant_block(1) * 2
+    assert run_q8(lib, blk, 32, 2, np.ones(31), rne=[1, 31, 1, 1])[0] == 2       # rhs length differs
+    assert run_q8(lib, blk, 32, 2, np.ones(32), code=2)[0] == 1                  # not a Q8_0 view
+    assert run_q8(lib, blk, 32, 2, np.ones(64), rne=[1, 32, 1, 1], rnb=[8, 8, 256, 256])[0] == 1  # rhs not dense
+    big = q8_constant_block(1) * 1025                                             # 1025 blocks > 1024
+    assert run_q8(lib, big, 32 * 1025, 1, np.ones(32 * 1025))[0] == 1
+
+
+def test_q8_0_matches_float_scores(lib):
+    # the quantized score tracks the float score: argmax of a planted row
+    rng = np.random.default_rng(4)
+    k, rows = 256, 40
+    w = rng.standard_normal((rows, k)).astype(np.float32) * 0.05
+    w[17] = np.abs(w[17]) + 0.05
+    x = np.abs(rng.standard_normal(k)).astype(np.float32)
+    blob = bytearray()
+    for r in range(rows):
+        for b in range(k // 32):
+            blk = w[r, b * 32:(b + 1) * 32]
+            d = np.float16(np.max(np.abs(blk)) / 127.0)
+            q = np.clip(np.round(blk / np.float32(d)), -127, 127).astype(np.int8)
+            blob += d.tobytes() + q.tobytes()
+    st, out, idx = run_q8(lib, blob, k, rows, x)
+    assert st == 0 and idx == 17
