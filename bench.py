@@ -493,7 +493,7 @@ def run_suite(args):
                  "cfg5": ["repeat_mul_permuted", "repeat_add_permuted", "sum_whole_permuted",
                           "argmax_whole_permuted", "cont_permuted"],
                  "glu": list(W.GLU_OPS), "get_rows": [f"get_rows_{f}" for f in W.EMB_FORMATS],
-                 "rope": ["rope_neox", "rope_norm"], "matvec": ["mul_mat_argmax_vocab"],
+                 "rope": ["rope_neox", "rope_norm"], "matvec": ["mul_mat_argmax_vocab", "mul_mat_argmax_q8_0_vocab"],
                  "attention": [o.name for o in W.fa_spec().ops], "diag": [o.name for o in W.diag_spec().ops]}
 
     def wants(*keys):
@@ -670,7 +670,7 @@ def run_suite(args):
                                                                          B(prm)))), sets)
         del txr, tyr
     # vocabulary matvec + argmax (matmul.rs OpMulMatArgmax)
-    if wants("matvec",):
+    if not only or "matvec" in only or "mul_mat_argmax_vocab" in only:
         spec = W.mv_spec()
         lm, rv = W.mv_inputs()
         tl, tr = torch.from_numpy(lm).to(dev), torch.from_numpy(rv).to(dev)
@@ -683,6 +683,20 @@ def run_suite(args):
                 lambda k: (lambda: chk(lib.emel_cuda_mul_mat_argmax(ctx.handle, sh, B(vl), B(vr), B(vv),
                                                                     ctypes.c_void_p(ti.data_ptr())))), 1)
         del tl, tr
+    if not only or "matvec" in only or "mul_mat_argmax_q8_0_vocab" in only:
+        o = W.mvq8_spec().ops[0]
+        blob, rv = W.mvq8_inputs()
+        tq, tr = torch.from_numpy(blob).to(dev), torch.from_numpy(rv).to(dev)
+        del blob
+        tv = torch.empty(1, device=dev)
+        ti = torch.empty(1, dtype=torch.int32, device=dev)
+        rb = W.MV_K // 32 * 34
+        vq = view(tq, [W.MV_K, W.MV_ROWS, 1, 1], [1, rb, rb * W.MV_ROWS, rb * W.MV_ROWS], code=8)
+        vr, vv = view(tr, [1, W.MV_K, 1, 1]), view(tv, [1, 1, 1, 1])
+        measure("matvec", o.name, o.bytes, o.elements,
+                lambda k: (lambda: chk(lib.emel_cuda_mul_mat_argmax_q8_0(ctx.handle, sh, B(vq), B(vr), B(vv),
+                                                                         ctypes.c_void_p(ti.data_ptr())))), 1)
+        del tq, tr
     # causal masks (diag.rs OpDiagMaskInf / OpDiagMaskZero) over a score matrix
     if wants("diag",):
         x = W.diag_inputs()

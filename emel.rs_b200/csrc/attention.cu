@@ -113,7 +113,8 @@ __global__ void __launch_bounds__(fa_threads(DPT, TILE), 1) fa_decode(FlashAttnP
     float* wtot = reinterpret_cast<float*>(tiles + 2 * TILE);            // [kScoreWarps] warp maxima
     float* ssum = wtot + 8;                                              // final score sum
     int* failed = reinterpret_cast<int*>(wtot + 9);                      // a bounded wait expired
-    double* qd = reinterpret_cast<double*>(wtot + 16);                   // [d] query through binary16
+    uint32_t* flags = reinterpret_cast<uint32_t*>(wtot + 16);            // [2][8] tokens where the maximum moved
+    double* qd = reinterpret_cast<double*>(wtot + 32);                   // [d] query through binary16
     uint16_t* vtile = reinterpret_cast<uint16_t*>(qd + p.d);             // [2][TILE][d] staged V rows
     pdl_enter();
 
@@ -203,13 +204,16 @@ __global__ void __launch_bounds__(fa_threads(DPT, TILE), 1) fa_decode(FlashAttnP
                         dot = __dadd_rn(dot, __dmul_rn(qd[c + 1], (double)fa_kv((uint16_t)(word >> 16))));
                     };
                     uint64_t c0 = 0;
-                    for (; c0 + 32 <= d; c0 += 32) {  // four 16-byte loads in flight
+                    for (; c0 + 64 <= d; c0 += 64) {  // eight 16-byte loads in flight
                         const uint4* r4 = reinterpret_cast<const uint4*>(krow + c0 * 2);
-                        const uint4 w0 = r4[0], w1 = r4[1], w2 = r4[2], w3 = r4[3];
-                        pair(w0.x, c0), pair(w0.y, c0 + 2), pair(w0.z, c0 + 4), pair(w0.w, c0 + 6);
-                        pair(w1.x, c0 + 8), pair(w1.y, c0 + 10), pair(w1.z, c0 + 12), pair(w1.w, c0 + 14);
-                        pair(w2.x, c0 + 16), pair(w2.y, c0 + 18), pair(w2.z, c0 + 20), pair(w2.w, c0 + 22);
-                        pair(w3.x, c0 + 24), pair(w3.y, c0 + 26), pair(w3.z, c0 + 28), pair(w3.w, c0 + 30);
+                        uint4 w[8];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) w[e] = r4[e];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            const uint64_t c = c0 + 8 * e;
+                            pair(w[e].x, c), pair(w[e].y, c + 2), pair(w[e].z, c + 4), pair(w[e].w, c + 6);
+                        }
                     }
                     for (; c0 < d; c0 += 8) {
                         const uint4 w = *reinterpret_cast<const uint4*>(krow + c0 * 2);
@@ -251,15 +255,19 @@ __global__ void __launch_bounds__(fa_threads(DPT, TILE), 1) fa_decode(FlashAttnP
             const float prev = __shfl_up_sync(0xffffffffu, m, 1);
             const float mb = lane == 0 ? before : fa_max(before, prev);
             carry = total;
+            float rs = 1.0f, vs = 1.0f;
             if (t < T) {
                 // flash_attn.rs:364-375
-                float rs = 1.0f, vs = 1.0f;
                 if (s > mb)
                     rs = lm_exp(__fsub_rn(mb, s));
                 else
                     vs = lm_exp(__fsub_rn(s, mb));
                 tiles[(it & 1) * TILE + sj] = make_float4(rs, vs, fa_round16(rs), fa_round16(vs));
             }
+            // tokens whose binary16 rescale factor is not 1 (a rescale by 1 leaves
+            // a binary16 accumulator unchanged)
+            const uint32_t moved = __ballot_sync(0xffffffffu, t < T && fa_round16(rs) != 1.0f);
+            if (lane == 0) flags[(it & 1) * 8 + sw] = moved;
         } else if (is_acc && it > 0) {
             const uint64_t t0 = (it - 1) * TILE;
             const float4* sc = tiles + ((it - 1) & 1) * TILE;
@@ -309,16 +317,24 @@ __global__ void __launch_bounds__(fa_threads(DPT, TILE), 1) fa_decode(FlashAttnP
                 }
                 const uint32_t d32 = (uint32_t)d;
                 bool suspect = false;
+                // The hardware conversion rounds to nearest even; the reference
+                // (flash_attn.rs:528-557) differs only below 2^-14: it flushes
+                // (2^-25, 2^-24) to zero and rounds exact ties up.  Only those
+                // inputs mark the tile for an exact replay.
                 const auto fast = [&](float x) {
-                    suspect |= fabsf(x) < 6.103515625e-05f && x != 0.0f;
+                    const float ax = fabsf(x);
+                    const float t2 = __fmul_rn(ax, 33554432.0f);  // 2^25 |x|: an odd integer at a tie
+                    const bool tie_down = ax < 6.103515625e-05f && t2 == rintf(t2) && (((int)t2) & 3) == 1;
+                    suspect |= tie_down || (ax > 2.98023223876953125e-08f && ax < 5.9604644775390625e-08f);
                     return __half2float(__float2half_rn(x));
                 };
-                const auto step = [&](int j) {
+                const uint32_t* fl = flags + ((it - 1) & 1) * 8;
+                const auto step = [&](int j, bool rescale) {
                     const float4 f = sc[j];
                     float v[DPT];
 #pragma unroll
                     for (int k = 0; k < DPT; ++k) v[k] = fa_kv(vt[(uint32_t)j * d32 + off[k]]);
-                    if (f.z != 1.0f) {
+                    if (rescale && f.z != 1.0f) {
 #pragma unroll
                         for (int k = 0; k < DPT; ++k) acc[k] = fast(__fmul_rn(acc[k], f.z));
                     }
@@ -327,10 +343,16 @@ __global__ void __launch_bounds__(fa_threads(DPT, TILE), 1) fa_decode(FlashAttnP
                 };
                 int j = 0;
                 for (; j + 8 <= n; j += 8) {
+                    // one uniform test per 8 tokens: most groups never move the maximum
+                    if (((fl[j >> 5] >> (j & 31)) & 0xffu) == 0u) {
 #pragma unroll
-                    for (int u = 0; u < 8; ++u) step(j + u);
+                        for (int u = 0; u < 8; ++u) step(j + u, false);
+                    } else {
+#pragma unroll
+                        for (int u = 0; u < 8; ++u) step(j + u, true);
+                    }
                 }
-                for (; j < n; ++j) step(j);
+                for (; j < n; ++j) step(j, true);
                 if (suspect) {
 #pragma unroll
                     for (int k = 0; k < DPT; ++k) acc[k] = a0[k];
@@ -349,7 +371,15 @@ __global__ void __launch_bounds__(fa_threads(DPT, TILE), 1) fa_decode(FlashAttnP
             const uint64_t t0 = (it - 1) * TILE;
             const float4* sc = tiles + ((it - 1) & 1) * TILE;
             const int n = T - t0 < (uint64_t)TILE ? (int)(T - t0) : TILE;
-            for (int j = 0; j < n; ++j) sum = __fadd_rn(__fmul_rn(sum, sc[j].x), sc[j].y);
+            int j = 0;
+            for (; j + 8 <= n; j += 8) {
+                float2 f[8];
+#pragma unroll
+                for (int u = 0; u < 8; ++u) f[u] = make_float2(sc[j + u].x, sc[j + u].y);
+#pragma unroll
+                for (int u = 0; u < 8; ++u) sum = __fadd_rn(__fmul_rn(sum, f[u].x), f[u].y);
+            }
+            for (; j < n; ++j) sum = __fadd_rn(__fmul_rn(sum, sc[j].x), sc[j].y);
         }
         __syncthreads();
     }
@@ -371,7 +401,7 @@ template <int DPT, int TILE, int VMODE>
 cudaError_t launch_fa(const LaunchEnv& env, const FlashAttnPlan& p) {
     const int na = (int)(((p.d + DPT - 1) / DPT + 31) / 32 * 32);
     const int threads = na + TILE + 32;
-    const size_t smem = 16 + 2 * TILE * sizeof(float4) + 16 * sizeof(float) + p.d * sizeof(double) +
+    const size_t smem = 16 + 2 * TILE * sizeof(float4) + 32 * sizeof(float) + p.d * sizeof(double) +
                         (VMODE == kFaVGlobal ? 0 : 2 * (size_t)TILE * p.d * 2);
     if (smem > 48 * 1024) {
         const cudaError_t err =

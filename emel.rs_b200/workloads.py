@@ -328,3 +328,22 @@ def diag_spec():
     kept = DIAG_SIDE * (DIAG_SIDE + 1) // 2
     return Config("diag", [OpSpec("diag_mask_inf_causal", (kept + n) * F32, n),
                            OpSpec("diag_mask_zero_causal", (kept + n) * F32, n)])
+
+
+# The same vocabulary step with Q8_0 rows (matmul.rs OpMulMatArgmaxQ8_0):
+# [4096, 151936] as 128 blocks of 34 bytes per row (binary16 scales
+# 2^-10 * U(0.5, 1), quants uniform in [-127, 127]), rhs N(0, 1).
+def mvq8_inputs(seed=17):
+    rng = np.random.default_rng(seed)
+    blocks = MV_K // 32
+    blob = rng.integers(-127, 128, size=(MV_ROWS, blocks, 34), dtype=np.int8).view(np.uint8)
+    d = (rng.uniform(0.5, 1.0, size=(MV_ROWS, blocks)) / 1024.0).astype(np.float16)
+    blob[:, :, :2] = d.view(np.uint8).reshape(MV_ROWS, blocks, 2)
+    rhs = normal(rng, (MV_K,), 1.0).astype(np.float32)
+    return blob.reshape(-1), rhs
+
+
+def mvq8_spec():
+    row_bytes = MV_K // 32 * 34
+    return Config("matvec", [OpSpec("mul_mat_argmax_q8_0_vocab", MV_ROWS * row_bytes + MV_K * F32 + 8,
+                                    MV_K * MV_ROWS)])
