@@ -30,9 +30,10 @@
 //     shared memory.
 // A block barrier separates the iterations.  Shared memory holds two V
 // tiles, so TILE shrinks as head_dim grows (256 tokens up to 192 columns,
-// 32 tokens at 1536); beyond that V is read from global memory.  The accumulator chain (one
-// FMA and one binary16 round trip per token) bounds the kernel: its time is
-// tokens x the chain latency, whatever the number of heads.
+// 32 tokens at 1536); beyond that V is read from global memory.  The
+// accumulator chain (one FMA and one binary16 round trip per token) bounds
+// the kernel: its time is tokens x the chain latency, whatever the number
+// of heads.
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 
@@ -318,15 +319,18 @@ __global__ void __launch_bounds__(fa_threads(DPT, TILE), 1) fa_decode(FlashAttnP
                 const uint32_t d32 = (uint32_t)d;
                 bool suspect = false;
                 // The hardware conversion rounds to nearest even; the reference
-                // (flash_attn.rs:528-557) differs only below 2^-14: it flushes
-                // (2^-25, 2^-24) to zero and rounds exact ties up.  Only those
-                // inputs mark the tile for an exact replay.
+                // (flash_attn.rs:528-557) differs only below 2^-14, where it
+                // flushes (2^-25, 2^-24) to zero and rounds exact ties up.  A
+                // tie is |x - r| = 2^-25 (the difference is exact there); a
+                // flushed value is |x| < 2^-24 rounded to nonzero.  Only those
+                // inputs mark the tile for an exact replay; the test uses
+                // compares only, so it adds no conversion to the chain's pipe.
                 const auto fast = [&](float x) {
+                    const float r = __half2float(__float2half_rn(x));
                     const float ax = fabsf(x);
-                    const float t2 = __fmul_rn(ax, 33554432.0f);  // 2^25 |x|: an odd integer at a tie
-                    const bool tie_down = ax < 6.103515625e-05f && t2 == rintf(t2) && (((int)t2) & 3) == 1;
-                    suspect |= tie_down || (ax > 2.98023223876953125e-08f && ax < 5.9604644775390625e-08f);
-                    return __half2float(__float2half_rn(x));
+                    suspect |= ax < 6.103515625e-05f && (fabsf(__fsub_rn(x, r)) == 2.98023223876953125e-08f ||
+                                                          (ax < 5.9604644775390625e-08f && r != 0.0f));
+                    return r;
                 };
                 const uint32_t* fl = flags + ((it - 1) & 1) * 8;
                 const auto step = [&](int j, bool rescale) {

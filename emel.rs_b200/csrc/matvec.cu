@@ -219,23 +219,40 @@ __global__ void __launch_bounds__(kMvRows) mv_argmax_plain(MvArgmaxPlan p) {
 // ---- Q8_0 rows (matmul.rs OpMulMatArgmaxQ8_0) -------------------------------
 // The rhs is quantized to Q8_0 in every CTA's shared memory (quantize_q8_0,
 // matmul.rs:1629-1653: one warp per 32-value block, amax by a max-reduction,
-// which is exact).  A warp owns one row at a time: lane l forms the integer
-// dot of block b0 + l (dp4a on 32-bit words rebuilt from the 2-byte-aligned
-// 34-byte block) and its term float(dot) * (d_lhs * d_rhs); the row's sum
-// then folds the terms in block order (a broadcast of each lane's term to
-// every lane, one binary32 add each), which is dot_q8_0's order
-// (matmul.rs:1893-1910).
-constexpr int kQ8Threads = 256;
+// which is exact).  A warp owns 32 rows at a time.  For each row in turn the
+// lanes form the block terms float(integer dot) * (d_lhs * d_rhs) of 128
+// consecutive blocks (lane l: blocks l, l + 32, l + 64, l + 96, all loads
+// issued first; dp4a on 32-bit words rebuilt from the 2-byte-aligned 34-byte
+// blocks) into a padded shared tile [32 rows][129]; then lane r folds row r's
+// terms in block order, one binary32 add each -- dot_q8_0's order
+// (matmul.rs:1893-1910) -- so the 32 sequential sums run side by side.
+constexpr int kQ8Threads = 128;
 constexpr int kQ8Warps = kQ8Threads / 32;
+constexpr int kQ8Chunk = 128;                       // blocks per pass
+constexpr int kQ8TermStride = kQ8Chunk + 1;         // conflict-free column walk
+
+__device__ __forceinline__ float q8_block_term(const uint8_t* rp, uint32_t b, const uint32_t* rq, const float* rd,
+                                               const uint32_t (&w)[9], bool odd) {
+    const uint32_t dbits = odd ? (w[0] >> 16) : (w[0] & 0xffffu);
+    const uint32_t* r = rq + b * 9;
+    int integer = 0;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+        const uint32_t qw = odd ? w[j + 1] : __byte_perm(w[j], w[j + 1], 0x5432);
+        integer = __dp4a((int)qw, (int)r[j], integer);
+    }
+    return __fmul_rn((float)integer, __fmul_rn(f16_bits_to_f32((uint16_t)dbits), rd[b]));
+}
 
 __global__ void __launch_bounds__(kQ8Threads) mv_argmax_q8_0(MvArgmaxPlan p, const uint8_t* lhs) {
     extern __shared__ __align__(16) uint32_t q8_smem[];
     __shared__ MvPart warp_best[kQ8Warps];
     const uint32_t blocks = (uint32_t)(p.k / 32);
-    uint32_t* rq = q8_smem;                                       // [blocks][9]: 8 words of quants + pad
-    float* rd = reinterpret_cast<float*>(q8_smem + blocks * 9);   // [blocks]: rhs scales
-    pdl_enter();
+    uint32_t* rq = q8_smem;                                            // [blocks][9]: 8 words of quants + pad
+    float* rd = reinterpret_cast<float*>(q8_smem + blocks * 9);        // [blocks]: rhs scales
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float* terms = rd + blocks + warp * 32 * kQ8TermStride;            // this warp's [32][129] tile
+    pdl_enter();
     for (uint32_t b = warp; b < blocks; b += kQ8Warps) {
         const float x = p.rhs[(uint64_t)b * 32 + lane];
         float amax = fabsf(x);
@@ -251,36 +268,66 @@ __global__ void __launch_bounds__(kQ8Threads) mv_argmax_q8_0(MvArgmaxPlan p, con
     __syncthreads();
     const uint64_t row_bytes = (uint64_t)blocks * 34;
     MvPart best{0.0f, 0, 0u, 0u};
-    for (uint64_t row = (uint64_t)blockIdx.x * kQ8Warps + warp; row < p.rows; row += (uint64_t)gridDim.x * kQ8Warps) {
-        const uint8_t* rp = lhs + row * row_bytes;
-        float sum = 0.0f;
-        for (uint32_t b0 = 0; b0 < blocks; b0 += 32) {
-            const uint32_t b = b0 + lane;
-            float term = 0.0f;
-            if (b < blocks) {
-                const uint64_t off = (uint64_t)b * 34;
-                const bool odd = ((uintptr_t)(rp + off) & 3u) != 0;  // block starts 2 bytes into a word
-                const uint32_t* wp = reinterpret_cast<const uint32_t*>(rp + off - (odd ? 2 : 0));
-                uint32_t w[9];
+    for (uint64_t g0 = ((uint64_t)blockIdx.x * kQ8Warps + warp) * 32; g0 < p.rows;
+         g0 += (uint64_t)gridDim.x * kQ8Warps * 32) {
+        const uint32_t nrows = p.rows - g0 < 32u ? (uint32_t)(p.rows - g0) : 32u;
+        float sum = 0.0f;  // lane r: row g0 + r
+        for (uint32_t b0 = 0; b0 < blocks; b0 += kQ8Chunk) {
+            for (uint32_t r = 0; r < nrows; ++r) {
+                const uint8_t* rp = lhs + (g0 + r) * row_bytes;
+                uint32_t w[4][9];
+                bool odd[4];
 #pragma unroll
-                for (int j = 0; j < 8; ++j) w[j] = __ldg(wp + j);
-                // the last word: whole when the block ends on it, else its first half
-                w[8] = odd ? __ldg(wp + 8) : (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(wp + 8));
-                const uint32_t dbits = odd ? (w[0] >> 16) : (w[0] & 0xffffu);
-                const uint32_t* r = rq + b * 9;
-                int integer = 0;
+                for (int c = 0; c < 4; ++c) {
+                    const uint32_t b = b0 + 32 * c + lane;
+                    odd[c] = false;
+                    if (b < blocks) {
+                        const uint64_t off = (uint64_t)b * 34;
+                        odd[c] = ((uintptr_t)(rp + off) & 3u) != 0;  // block starts 2 bytes into a word
+                        const uint32_t* wp = reinterpret_cast<const uint32_t*>(rp + off - (odd[c] ? 2 : 0));
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
-                    const uint32_t qw = odd ? w[j + 1] : __byte_perm(w[j], w[j + 1], 0x5432);
-                    integer = __dp4a((int)qw, (int)r[j], integer);
+                        for (int j = 0; j < 8; ++j) w[c][j] = __ldg(wp + j);
+                        // the last word: whole when the block ends on it, else its first half
+                        w[c][8] = odd[c] ? __ldg(wp + 8) : (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(wp + 8));
+                    }
                 }
-                term = __fmul_rn((float)integer, __fmul_rn(f16_bits_to_f32((uint16_t)dbits), rd[b]));
+#pragma unroll
+                for (int c = 0; c < 4; ++c) {
+                    const uint32_t b = b0 + 32 * c + lane;
+                    if (b < blocks) terms[r * kQ8TermStride + 32 * c + lane] = q8_block_term(rp, b, rq, rd, w[c], odd[c]);
+                }
             }
-            const uint32_t n = blocks - b0 < 32u ? blocks - b0 : 32u;
-            for (uint32_t j = 0; j < n; ++j) sum = __fadd_rn(sum, __shfl_sync(0xffffffffu, term, (int)j));
+            __syncwarp();
+            if ((uint32_t)lane < nrows) {
+                const uint32_t n = blocks - b0 < (uint32_t)kQ8Chunk ? blocks - b0 : (uint32_t)kQ8Chunk;
+                const float* t = terms + lane * kQ8TermStride;
+                uint32_t j = 0;
+                for (; j + 8 <= n; j += 8) {
+                    float v[8];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) v[u] = t[j + u];
+#pragma unroll
+                    for (int u = 0; u < 8; ++u) sum = __fadd_rn(sum, v[u]);
+                }
+                for (; j < n; ++j) sum = __fadd_rn(sum, t[j]);
+            }
+            __syncwarp();
         }
-        const bool nan = is_nan(sum);
-        best = mv_better(best, MvPart{sum, (int32_t)row, nan ? 0u : 1u, (nan && row == 0) ? 1u : 0u});
+        if ((uint32_t)lane < nrows) {
+            const uint64_t row = g0 + lane;
+            const bool nan = is_nan(sum);
+            best = mv_better(best, MvPart{sum, (int32_t)row, nan ? 0u : 1u, (nan && row == 0) ? 1u : 0u});
+        }
+    }
+    // order-free fold of the lanes' and warps' candidates
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        MvPart other;
+        other.v = __shfl_xor_sync(0xffffffffu, best.v, o);
+        other.i = __shfl_xor_sync(0xffffffffu, best.i, o);
+        other.has = __shfl_xor_sync(0xffffffffu, best.has, o);
+        other.pin = __shfl_xor_sync(0xffffffffu, best.pin, o);
+        best = mv_better(best, other);
     }
     if (lane == 0) warp_best[warp] = best;
     __syncthreads();
@@ -355,14 +402,15 @@ cudaError_t launch_mul_mat_argmax(const LaunchEnv& env, const MvArgmaxPlan& p) {
 }
 
 cudaError_t launch_mul_mat_argmax_q8_0(const LaunchEnv& env, const MvArgmaxPlan& p, const uint8_t* lhs) {
-    const uint64_t groups = (p.rows + kQ8Warps - 1) / kQ8Warps;
-    const uint64_t cap = (uint64_t)env.sm_count * 4;
-    const size_t smem = (size_t)(p.k / 32) * (9 * 4 + 4);
+    const uint64_t groups = (p.rows + kQ8Warps * 32 - 1) / (kQ8Warps * 32);
+    const uint64_t cap = (uint64_t)env.sm_count * 3;
+    const size_t smem = (size_t)(p.k / 32) * (9 * 4 + 4) + (size_t)kQ8Warps * 32 * kQ8TermStride * 4;
     static int configured_device_mask = 0;
     const int bit = env.device < 31 ? (1 << env.device) : 0;
     if (!(configured_device_mask & bit)) {
         const cudaError_t e =
-            cudaFuncSetAttribute(mv_argmax_q8_0, cudaFuncAttributeMaxDynamicSharedMemorySize, 1024 * 40);
+            cudaFuncSetAttribute(mv_argmax_q8_0, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 1024 * 40 + kQ8Warps * 32 * kQ8TermStride * 4);
         if (e != cudaSuccess) return e;
         configured_device_mask |= bit;
     }
