@@ -196,6 +196,9 @@ SIGNATURES = {
     "emel_cuda_get_rows": (_I, [_CTX, _V, _P, _P, _P]),
     "emel_cuda_mul_mat_argmax": (_I, [_CTX, _V, _P, _P, _P, _V]),
     "emel_cuda_mul_mat_argmax_q8_0": (_I, [_CTX, _V, _P, _P, _P, _V]),
+    "emel_cuda_mul_mat_argmax_q4_0": (_I, [_CTX, _V, _P, _P, _P, _V]),
+    "emel_cuda_mul_mat_argmax_q4_1": (_I, [_CTX, _V, _P, _P, _P, _V]),
+    "emel_cuda_mul_mat_argmax_q5_0": (_I, [_CTX, _V, _P, _P, _P, _V]),
     "emel_cuda_rope": (_I, [_CTX, _V, _P, _P, _P, ctypes.POINTER(CRopeParams)]),
     "emel_cuda_diag": (_I, [_CTX, _V, _V, ctypes.c_uint64, _V, ctypes.c_uint64]),
     "emel_cuda_diag_mask": (_I, [_CTX, _V, _I, _V, ctypes.c_uint64, _V, ctypes.c_uint64, ctypes.c_int32]),
@@ -744,6 +747,28 @@ class OpMulMatArgmaxQ8_0(Event):
     def dispatch(self, ctx, stream):
         return ctx._lib.emel_cuda_mul_mat_argmax_q8_0(ctx.handle, stream, _r(self.lhs), _r(self.rhs),
                                                       _r(self.destination), ctypes.c_void_p(self.index_ptr))
+
+
+def _packed_argmax(suffix, doc):
+    @dataclass
+    class E(Event):
+        lhs: TensorView
+        rhs: TensorView
+        destination: TensorView
+        index_ptr: int
+
+        def dispatch(self, ctx, stream):
+            fn = getattr(ctx._lib, f"emel_cuda_mul_mat_argmax_{suffix}")
+            return fn(ctx.handle, stream, _r(self.lhs), _r(self.rhs), _r(self.destination),
+                      ctypes.c_void_p(self.index_ptr))
+    E.__doc__ = doc
+    E.__name__ = E.__qualname__ = f"OpMulMatArgmax{suffix.upper()}"
+    return E
+
+
+OpMulMatArgmaxQ4_0 = _packed_argmax("q4_0", "matmul::OpMulMatArgmaxQ4_0 (matmul.rs:490-500): Q4_0 rows.")
+OpMulMatArgmaxQ4_1 = _packed_argmax("q4_1", "matmul::OpMulMatArgmaxQ4_1 (matmul.rs:500-510): Q4_1 rows.")
+OpMulMatArgmaxQ5_0 = _packed_argmax("q5_0", "matmul::OpMulMatArgmaxQ5_0 (matmul.rs:510-516): Q5_0 rows.")
 
 
 @dataclass

@@ -1242,16 +1242,17 @@ emel_cuda_status emel_cuda_mul_mat_argmax(emel_cuda_context* ctx, void* stream, 
     return device_status(ctx, err);
 }
 
-emel_cuda_status emel_cuda_mul_mat_argmax_q8_0(emel_cuda_context* ctx, void* stream, const emel_tensor_view* lhs,
-                                               const emel_tensor_view* rhs, const emel_tensor_view* dst,
-                                               int32_t* index_out) {
+static emel_cuda_status mul_mat_argmax_packed(emel_cuda_context* ctx, void* stream, const emel_tensor_view* lhs,
+                                              const emel_tensor_view* rhs, const emel_tensor_view* dst,
+                                              int32_t* index_out, uint32_t code, uint64_t block_bytes) {
     Checked cr, cd;
     uint64_t row_bytes = 0;
-    // quantized_views_valid (matmul.rs:1522-1542): Q8_0 packed rows of at most
+    // quantized_views_valid (matmul.rs:1522-1542): packed rows of at most
     // 1024 blocks, dense F32 rhs and destination
-    if (lhs == nullptr || rhs == nullptr || dst == nullptr || !gr_packed_view_valid(lhs, EMEL_DTYPE_Q8_0, 32, 34, &row_bytes) ||
-        lhs->ne[0] / 32 > 1024 || !validate_as(rhs, EMEL_DTYPE_F32, false, &cr) ||
-        !validate_as(dst, EMEL_DTYPE_F32, false, &cd) || !dense_contiguous_f32(rhs) || !dense_contiguous_f32(dst))
+    if (lhs == nullptr || rhs == nullptr || dst == nullptr ||
+        !gr_packed_view_valid(lhs, code, 32, block_bytes, &row_bytes) || lhs->ne[0] / 32 > 1024 ||
+        !validate_as(rhs, EMEL_DTYPE_F32, false, &cr) || !validate_as(dst, EMEL_DTYPE_F32, false, &cd) ||
+        !dense_contiguous_f32(rhs) || !dense_contiguous_f32(dst))
         return EMEL_CUDA_INVALID_VIEW;
     // quantized_shape_valid (matmul.rs:1544-1564)
     const uint64_t* l = lhs->ne;
@@ -1277,8 +1278,33 @@ emel_cuda_status emel_cuda_mul_mat_argmax_q8_0(emel_cuda_context* ctx, void* str
     p.fault = reinterpret_cast<uint32_t*>(ws + emel::kFaultWordOffset);
     cudaError_t err = select_device(ctx);
     if (err == cudaSuccess)
-        err = emel::launch_mul_mat_argmax_q8_0(env_of(ctx, stream), p, static_cast<const uint8_t*>(lhs->data));
+        err = emel::launch_mul_mat_argmax_packed(env_of(ctx, stream), p, static_cast<const uint8_t*>(lhs->data),
+                                                 (int)code);
     return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_mul_mat_argmax_q8_0(emel_cuda_context* ctx, void* stream, const emel_tensor_view* lhs,
+                                               const emel_tensor_view* rhs, const emel_tensor_view* dst,
+                                               int32_t* index_out) {
+    return mul_mat_argmax_packed(ctx, stream, lhs, rhs, dst, index_out, EMEL_DTYPE_Q8_0, 34);
+}
+
+emel_cuda_status emel_cuda_mul_mat_argmax_q4_0(emel_cuda_context* ctx, void* stream, const emel_tensor_view* lhs,
+                                               const emel_tensor_view* rhs, const emel_tensor_view* dst,
+                                               int32_t* index_out) {
+    return mul_mat_argmax_packed(ctx, stream, lhs, rhs, dst, index_out, EMEL_DTYPE_Q4_0, 18);
+}
+
+emel_cuda_status emel_cuda_mul_mat_argmax_q4_1(emel_cuda_context* ctx, void* stream, const emel_tensor_view* lhs,
+                                               const emel_tensor_view* rhs, const emel_tensor_view* dst,
+                                               int32_t* index_out) {
+    return mul_mat_argmax_packed(ctx, stream, lhs, rhs, dst, index_out, EMEL_DTYPE_Q4_1, 20);
+}
+
+emel_cuda_status emel_cuda_mul_mat_argmax_q5_0(emel_cuda_context* ctx, void* stream, const emel_tensor_view* lhs,
+                                               const emel_tensor_view* rhs, const emel_tensor_view* dst,
+                                               int32_t* index_out) {
+    return mul_mat_argmax_packed(ctx, stream, lhs, rhs, dst, index_out, EMEL_DTYPE_Q5_0, 22);
 }
 
 // ---- single-query attention -------------------------------------------------

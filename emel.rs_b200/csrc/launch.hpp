@@ -123,9 +123,11 @@ struct MvArgmaxPlan {
 };
 
 cudaError_t launch_mul_mat_argmax(const LaunchEnv& env, const MvArgmaxPlan& plan);
-// Q8_0 rows (lhs: packed 34-byte blocks, rows of k / 32 blocks, 4-byte
-// aligned base); plan.lhs unused, plan.k a multiple of 32 up to 32768.
-cudaError_t launch_mul_mat_argmax_q8_0(const LaunchEnv& env, const MvArgmaxPlan& plan, const uint8_t* lhs);
+// Packed rows (lhs: Q4_0 / Q4_1 / Q5_0 / Q8_0 blocks of 32 values, rows of
+// k / 32 blocks, 4-byte aligned base); plan.lhs unused, plan.k a multiple of
+// 32 up to 32768; code: the lhs dtype code.
+constexpr int kDtypeQ4_0 = 2, kDtypeQ4_1 = 3, kDtypeQ5_0 = 6, kDtypeQ8_0 = 8;
+cudaError_t launch_mul_mat_argmax_packed(const LaunchEnv& env, const MvArgmaxPlan& plan, const uint8_t* lhs, int code);
 
 // Single-query attention (attention.cu): one CTA per query head.
 struct FlashAttnPlan {

@@ -216,42 +216,122 @@ __global__ void __launch_bounds__(kMvRows) mv_argmax_plain(MvArgmaxPlan p) {
     finish(p, scratch[0]);
 }
 
-// ---- Q8_0 rows (matmul.rs OpMulMatArgmaxQ8_0) -------------------------------
+// ---- packed rows (matmul.rs OpMulMatArgmaxQ4_0 / Q4_1 / Q5_0 / Q8_0) ---------
 // The rhs is quantized to Q8_0 in every CTA's shared memory (quantize_q8_0,
 // matmul.rs:1629-1653: one warp per 32-value block, amax by a max-reduction,
-// which is exact).  A warp owns 32 rows at a time.  For each row in turn the
-// lanes form the block terms float(integer dot) * (d_lhs * d_rhs) of 128
+// which is exact; Q4_1 also keeps each block's quant sum).  A warp owns 32
+// rows at a time.  For each row in turn the lanes form the block terms of 128
 // consecutive blocks (lane l: blocks l, l + 32, l + 64, l + 96, all loads
-// issued first; dp4a on 32-bit words rebuilt from the 2-byte-aligned 34-byte
-// blocks) into a padded shared tile [32 rows][129]; then lane r folds row r's
-// terms in block order, one binary32 add each -- dot_q8_0's order
-// (matmul.rs:1893-1910) -- so the 32 sequential sums run side by side.
+// issued first) into a padded shared tile [32 rows][129]; then lane r folds
+// row r's terms in block order, one binary32 add each -- the order of
+// dot_q4_0 / dot_q4_1 / dot_q5_0 / dot_q8_0 (matmul.rs:1804-1910) -- so the
+// 32 sequential sums run side by side.  A block is read as aligned 32-bit
+// words (predicated so no byte past it is touched), realigned when it starts
+// 2 bytes into a word, and its quants rebuilt as 8 words of 4 signed bytes in
+// the rhs order (positions 0-15 from the low nibbles, 16-31 from the high
+// ones) for dp4a.
 constexpr int kQ8Threads = 128;
 constexpr int kQ8Warps = kQ8Threads / 32;
 constexpr int kQ8Chunk = 128;                       // blocks per pass
 constexpr int kQ8TermStride = kQ8Chunk + 1;         // conflict-free column walk
 
-__device__ __forceinline__ float q8_block_term(const uint8_t* rp, uint32_t b, const uint32_t* rq, const float* rd,
-                                               const uint32_t (&w)[9], bool odd) {
-    const uint32_t dbits = odd ? (w[0] >> 16) : (w[0] & 0xffffu);
-    const uint32_t* r = rq + b * 9;
-    int integer = 0;
-#pragma unroll
-    for (int j = 0; j < 8; ++j) {
-        const uint32_t qw = odd ? w[j + 1] : __byte_perm(w[j], w[j + 1], 0x5432);
-        integer = __dp4a((int)qw, (int)r[j], integer);
-    }
-    return __fmul_rn((float)integer, __fmul_rn(f16_bits_to_f32((uint16_t)dbits), rd[b]));
+template <int CODE>
+struct PackedFmt;
+template <>
+struct PackedFmt<kDtypeQ4_0> { static constexpr int kBytes = 18; };
+template <>
+struct PackedFmt<kDtypeQ4_1> { static constexpr int kBytes = 20; };
+template <>
+struct PackedFmt<kDtypeQ5_0> { static constexpr int kBytes = 22; };
+template <>
+struct PackedFmt<kDtypeQ8_0> { static constexpr int kBytes = 34; };
+
+// byte i of a nibble bit pattern (4 bits) moved to bit 4 of byte i
+__device__ __forceinline__ uint32_t q5_spread(uint32_t b4) {
+    return ((b4 & 1u) << 4) | ((b4 & 2u) << 11) | ((b4 & 4u) << 18) | ((b4 & 8u) << 25);
 }
 
-__global__ void __launch_bounds__(kQ8Threads) mv_argmax_q8_0(MvArgmaxPlan p, const uint8_t* lhs) {
+template <int CODE>
+struct PackedBlock {
+    static constexpr int BB = PackedFmt<CODE>::kBytes;
+    static constexpr int NW = (BB + 2 + 3) / 4;  // words a block can touch
+    uint32_t w[NW];
+    bool odd;
+
+    __device__ __forceinline__ void load(const uint8_t* blk) {
+        odd = ((uintptr_t)blk & 3u) != 0;  // starts 2 bytes into a word
+        const uint32_t* wp = reinterpret_cast<const uint32_t*>(blk - (odd ? 2 : 0));
+        const int end = BB + (odd ? 2 : 0);  // bytes of the aligned window in use
+#pragma unroll
+        for (int j = 0; j < NW; ++j) {
+            if (4 * j + 4 <= end)
+                w[j] = __ldg(wp + j);
+            else if (4 * j + 2 <= end)
+                w[j] = (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(wp + j));
+            else
+                w[j] = 0u;
+        }
+    }
+    // word j of the block's bytes (block byte 4j at its low byte)
+    __device__ __forceinline__ uint32_t word(int j) const {
+        if (j + 1 < NW) return odd ? __byte_perm(w[j], w[j + 1], 0x5432) : w[j];
+        return odd ? (w[j] >> 16) : w[j];
+    }
+    // the 4 bytes starting at block byte 4j + 2
+    __device__ __forceinline__ uint32_t word2(int j) const { return __byte_perm(word(j), word(j + 1), 0x5432); }
+};
+
+template <int CODE>
+__device__ __forceinline__ float packed_block_term(const PackedBlock<CODE>& k, uint32_t b, const uint32_t* rq,
+                                                   const float* rd, const int* rs) {
+    const uint32_t* r = rq + b * 9;
+    const uint32_t w0 = k.word(0);
+    const float dl = f16_bits_to_f32((uint16_t)(w0 & 0xffffu));
+    int integer = 0;
+    if constexpr (CODE == kDtypeQ8_0) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) integer = __dp4a((int)k.word2(j), (int)r[j], integer);
+    } else if constexpr (CODE == kDtypeQ4_0) {
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t pk = k.word2(j);
+            integer = __dp4a((int)__vsub4(pk & 0x0f0f0f0fu, 0x08080808u), (int)r[j], integer);
+            integer = __dp4a((int)__vsub4((pk >> 4) & 0x0f0f0f0fu, 0x08080808u), (int)r[4 + j], integer);
+        }
+    } else if constexpr (CODE == kDtypeQ5_0) {
+        const uint32_t qh = k.word2(0);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t pk = __byte_perm(k.word(j + 1), k.word(j + 2), 0x5432);  // bytes 6 + 4j ..
+            const uint32_t lo = (pk & 0x0f0f0f0fu) | q5_spread((qh >> (4 * j)) & 0xfu);
+            const uint32_t hi = ((pk >> 4) & 0x0f0f0f0fu) | q5_spread((qh >> (16 + 4 * j)) & 0xfu);
+            integer = __dp4a((int)__vsub4(lo, 0x10101010u), (int)r[j], integer);
+            integer = __dp4a((int)__vsub4(hi, 0x10101010u), (int)r[4 + j], integer);
+        }
+    } else {  // Q4_1: unsigned nibbles, min term (matmul.rs:1832-1858)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const uint32_t pk = k.word(j + 1);  // bytes 4 + 4j ..
+            integer = __dp4a((int)(pk & 0x0f0f0f0fu), (int)r[j], integer);
+            integer = __dp4a((int)((pk >> 4) & 0x0f0f0f0fu), (int)r[4 + j], integer);
+        }
+        const float ml = f16_bits_to_f32((uint16_t)(w0 >> 16));
+        return __fmul_rn(rd[b], __fadd_rn(__fmul_rn(dl, (float)integer), __fmul_rn(ml, (float)rs[b])));
+    }
+    return __fmul_rn((float)integer, __fmul_rn(dl, rd[b]));
+}
+
+template <int CODE>
+__global__ void __launch_bounds__(kQ8Threads) mv_argmax_packed(MvArgmaxPlan p, const uint8_t* lhs) {
     extern __shared__ __align__(16) uint32_t q8_smem[];
     __shared__ MvPart warp_best[kQ8Warps];
+    constexpr int BB = PackedFmt<CODE>::kBytes;
     const uint32_t blocks = (uint32_t)(p.k / 32);
     uint32_t* rq = q8_smem;                                            // [blocks][9]: 8 words of quants + pad
     float* rd = reinterpret_cast<float*>(q8_smem + blocks * 9);        // [blocks]: rhs scales
+    int* rs = reinterpret_cast<int*>(rd + blocks);                     // [blocks]: rhs quant sums
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* terms = rd + blocks + warp * 32 * kQ8TermStride;            // this warp's [32][129] tile
+    float* terms = reinterpret_cast<float*>(rs + blocks) + warp * 32 * kQ8TermStride;  // [32][129]
     pdl_enter();
     for (uint32_t b = warp; b < blocks; b += kQ8Warps) {
         const float x = p.rhs[(uint64_t)b * 32 + lane];
@@ -262,11 +342,18 @@ __global__ void __launch_bounds__(kQ8Threads) mv_argmax_q8_0(MvArgmaxPlan p, con
         const float inverse = scale == 0.0f ? 0.0f : __fdiv_rn(1.0f, scale);
         float q = roundf(__fmul_rn(x, inverse));
         q = is_nan(q) ? 0.0f : fminf(fmaxf(q, -127.0f), 127.0f);
-        reinterpret_cast<int8_t*>(rq + b * 9)[lane] = (int8_t)(int)q;
-        if (lane == 0) rd[b] = f16_bits_to_f32(f32_to_f16_bits(scale));
+        const int qi = (int)q;
+        reinterpret_cast<int8_t*>(rq + b * 9)[lane] = (int8_t)qi;
+        int qsum = qi;
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) qsum += __shfl_xor_sync(0xffffffffu, qsum, o);
+        if (lane == 0) {
+            rd[b] = f16_bits_to_f32(f32_to_f16_bits(scale));
+            rs[b] = qsum;
+        }
     }
     __syncthreads();
-    const uint64_t row_bytes = (uint64_t)blocks * 34;
+    const uint64_t row_bytes = (uint64_t)blocks * BB;
     MvPart best{0.0f, 0, 0u, 0u};
     for (uint64_t g0 = ((uint64_t)blockIdx.x * kQ8Warps + warp) * 32; g0 < p.rows;
          g0 += (uint64_t)gridDim.x * kQ8Warps * 32) {
@@ -275,26 +362,16 @@ __global__ void __launch_bounds__(kQ8Threads) mv_argmax_q8_0(MvArgmaxPlan p, con
         for (uint32_t b0 = 0; b0 < blocks; b0 += kQ8Chunk) {
             for (uint32_t r = 0; r < nrows; ++r) {
                 const uint8_t* rp = lhs + (g0 + r) * row_bytes;
-                uint32_t w[4][9];
-                bool odd[4];
+                PackedBlock<CODE> blk[4];
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     const uint32_t b = b0 + 32 * c + lane;
-                    odd[c] = false;
-                    if (b < blocks) {
-                        const uint64_t off = (uint64_t)b * 34;
-                        odd[c] = ((uintptr_t)(rp + off) & 3u) != 0;  // block starts 2 bytes into a word
-                        const uint32_t* wp = reinterpret_cast<const uint32_t*>(rp + off - (odd[c] ? 2 : 0));
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) w[c][j] = __ldg(wp + j);
-                        // the last word: whole when the block ends on it, else its first half
-                        w[c][8] = odd[c] ? __ldg(wp + 8) : (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(wp + 8));
-                    }
+                    if (b < blocks) blk[c].load(rp + (uint64_t)b * BB);
                 }
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     const uint32_t b = b0 + 32 * c + lane;
-                    if (b < blocks) terms[r * kQ8TermStride + 32 * c + lane] = q8_block_term(rp, b, rq, rd, w[c], odd[c]);
+                    if (b < blocks) terms[r * kQ8TermStride + 32 * c + lane] = packed_block_term<CODE>(blk[c], b, rq, rd, rs);
                 }
             }
             __syncwarp();
@@ -338,6 +415,24 @@ __global__ void __launch_bounds__(kQ8Threads) mv_argmax_q8_0(MvArgmaxPlan p, con
     }
     __syncthreads();
     finish(p, warp_best[0]);
+}
+
+template <int CODE>
+cudaError_t launch_packed(const LaunchEnv& env, const MvArgmaxPlan& p, const uint8_t* lhs) {
+    const uint64_t groups = (p.rows + kQ8Warps * 32 - 1) / (kQ8Warps * 32);
+    const uint64_t cap = (uint64_t)env.sm_count * 3;
+    const size_t table = (size_t)kQ8Warps * 32 * kQ8TermStride * 4;
+    const size_t smem = (size_t)(p.k / 32) * (9 * 4 + 4 + 4) + table;
+    static int configured_device_mask = 0;
+    const int bit = env.device < 31 ? (1 << env.device) : 0;
+    if (!(configured_device_mask & bit)) {
+        const cudaError_t e = cudaFuncSetAttribute(mv_argmax_packed<CODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)(1024 * (9 * 4 + 4 + 4) + table));
+        if (e != cudaSuccess) return e;
+        configured_device_mask |= bit;
+    }
+    return launch_dependent(mv_argmax_packed<CODE>, dim3((unsigned)(groups < cap ? groups : cap)), dim3(kQ8Threads),
+                            smem, env.stream, p, lhs);
 }
 
 }  // namespace
@@ -401,21 +496,14 @@ cudaError_t launch_mul_mat_argmax(const LaunchEnv& env, const MvArgmaxPlan& p) {
     return err != cudaSuccess ? err : cudaGetLastError();
 }
 
-cudaError_t launch_mul_mat_argmax_q8_0(const LaunchEnv& env, const MvArgmaxPlan& p, const uint8_t* lhs) {
-    const uint64_t groups = (p.rows + kQ8Warps * 32 - 1) / (kQ8Warps * 32);
-    const uint64_t cap = (uint64_t)env.sm_count * 3;
-    const size_t smem = (size_t)(p.k / 32) * (9 * 4 + 4) + (size_t)kQ8Warps * 32 * kQ8TermStride * 4;
-    static int configured_device_mask = 0;
-    const int bit = env.device < 31 ? (1 << env.device) : 0;
-    if (!(configured_device_mask & bit)) {
-        const cudaError_t e =
-            cudaFuncSetAttribute(mv_argmax_q8_0, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 1024 * 40 + kQ8Warps * 32 * kQ8TermStride * 4);
-        if (e != cudaSuccess) return e;
-        configured_device_mask |= bit;
+cudaError_t launch_mul_mat_argmax_packed(const LaunchEnv& env, const MvArgmaxPlan& p, const uint8_t* lhs, int code) {
+    cudaError_t err;
+    switch (code) {
+    case kDtypeQ4_0: err = launch_packed<kDtypeQ4_0>(env, p, lhs); break;
+    case kDtypeQ4_1: err = launch_packed<kDtypeQ4_1>(env, p, lhs); break;
+    case kDtypeQ5_0: err = launch_packed<kDtypeQ5_0>(env, p, lhs); break;
+    default: err = launch_packed<kDtypeQ8_0>(env, p, lhs); break;
     }
-    const cudaError_t err = launch_dependent(mv_argmax_q8_0, dim3((unsigned)(groups < cap ? groups : cap)),
-                                             dim3(kQ8Threads), smem, env.stream, p, lhs);
     ++*env.launches;
     return err != cudaSuccess ? err : cudaGetLastError();
 }

@@ -43,6 +43,8 @@ enum emel_cuda_dtype {
     EMEL_DTYPE_F32 = 0,
     EMEL_DTYPE_F16 = 1,
     EMEL_DTYPE_Q4_0 = 2,  /* packed blocks: ne[0] values, nb[0] == 1 (byte rows) */
+    EMEL_DTYPE_Q4_1 = 3,
+    EMEL_DTYPE_Q5_0 = 6,
     EMEL_DTYPE_Q8_0 = 8,
     EMEL_DTYPE_Q4_K = 12,
     EMEL_DTYPE_I32 = 26,
@@ -473,6 +475,23 @@ EMEL_CUDA_API emel_cuda_status emel_cuda_flash_attn_workspace(const emel_cuda_co
  * index_out, else INVALID_ARGUMENT.  Uses the context's reduction workspace
  * (one call at a time per context). */
 EMEL_CUDA_API emel_cuda_status emel_cuda_mul_mat_argmax_q8_0(emel_cuda_context* ctx, void* stream,
+                                                             const emel_tensor_view* lhs, const emel_tensor_view* rhs,
+                                                             const emel_tensor_view* dst, int32_t* index_out);
+/* matmul::OpMulMatArgmaxQ4_0 / Q4_1 / Q5_0 (matmul.rs:490-520, routes
+ * 2904-2956): the same contract with Q4_0 (18-byte blocks: binary16 scale,
+ * 16 bytes of nibbles, value = nibble - 8), Q4_1 (20-byte: scale, min, 16
+ * bytes, value = nibble) and Q5_0 (22-byte: scale, 32 high bits, 16 bytes,
+ * value = (nibble | high << 4) - 16) rows; position i < 16 is byte i's low
+ * nibble, 16 + i its high nibble.  Block terms follow dot_q4_0 / dot_q4_1 /
+ * dot_q5_0 (matmul.rs:1804-1890): float(integer dot) * (d_lhs * d_rhs), and
+ * for Q4_1 d_rhs * (d_lhs * float(dot) + m_lhs * float(rhs quant sum)). */
+EMEL_CUDA_API emel_cuda_status emel_cuda_mul_mat_argmax_q4_0(emel_cuda_context* ctx, void* stream,
+                                                             const emel_tensor_view* lhs, const emel_tensor_view* rhs,
+                                                             const emel_tensor_view* dst, int32_t* index_out);
+EMEL_CUDA_API emel_cuda_status emel_cuda_mul_mat_argmax_q4_1(emel_cuda_context* ctx, void* stream,
+                                                             const emel_tensor_view* lhs, const emel_tensor_view* rhs,
+                                                             const emel_tensor_view* dst, int32_t* index_out);
+EMEL_CUDA_API emel_cuda_status emel_cuda_mul_mat_argmax_q5_0(emel_cuda_context* ctx, void* stream,
                                                              const emel_tensor_view* lhs, const emel_tensor_view* rhs,
                                                              const emel_tensor_view* dst, int32_t* index_out);
 

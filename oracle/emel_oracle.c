@@ -1119,16 +1119,26 @@ int oracle_mul_mat_argmax(const oracle_view* lhs, const oracle_view* rhs, const 
     return ORACLE_OK;
 }
 
-/* Q8_0 vocabulary matvec + argmax: matmul.rs OpMulMatArgmaxQ8_0.
- * quantized_views_valid / quantized_shape_valid (matmul.rs:1522-1564),
- * quantize_q8_0 (1629-1653), dot_q8_0 (1893-1910), run_argmax_q8_0
- * (2474-2498): the rhs is quantized per 32-value block (scale = amax / 127
- * stored as binary16, q = clamp(round(x / scale))), each lhs row is the sum
- * over blocks, in order, of float(integer dot) * (d_lhs * d_rhs). */
-int oracle_mul_mat_argmax_q8_0(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
-                               int32_t* index_out) {
-    if (!gr_packed_view_valid(lhs, 8, 32, 34) || lhs->ne[0] / 32 > 1024 || !validate_as(rhs, DT_F32, 0, NULL) ||
-        !validate_as(dst, DT_F32, 0, NULL) || !dense_contiguous_f32(rhs) || !dense_contiguous_f32(dst))
+/* Packed vocabulary matvec + argmax: matmul.rs OpMulMatArgmaxQ4_0 / Q4_1 /
+ * Q5_0 / Q8_0 (routes matmul.rs:2904-2970).  quantized_views_valid /
+ * quantized_shape_valid (matmul.rs:1522-1564), quantize_q8_0 (1629-1653),
+ * dot_q4_0 / dot_q4_1 / dot_q5_0 / dot_q8_0 (1804-1910), run_argmax_*
+ * (2193-2498): the rhs is quantized per 32-value block (scale = amax / 127
+ * stored as binary16, q = clamp(round(x / scale))); each lhs row is the sum
+ * over blocks, in order, of that block's term; the first row with the
+ * largest sum wins. */
+static int oracle_argmax_packed(int code, const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
+                                int32_t* index_out) {
+    uint64_t bb;
+    switch (code) {
+    case 2: bb = 18; break;  /* Q4_0 */
+    case 3: bb = 20; break;  /* Q4_1 */
+    case 6: bb = 22; break;  /* Q5_0 */
+    default: bb = 34; break; /* Q8_0 */
+    }
+    if (!gr_packed_view_valid(lhs, (uint32_t)code, 32, bb) || lhs->ne[0] / 32 > 1024 ||
+        !validate_as(rhs, DT_F32, 0, NULL) || !validate_as(dst, DT_F32, 0, NULL) || !dense_contiguous_f32(rhs) ||
+        !dense_contiguous_f32(dst))
         return ORACLE_INVALID_VIEW;
     const uint64_t* l = lhs->ne;
     const uint64_t* r = rhs->ne;
@@ -1136,16 +1146,16 @@ int oracle_mul_mat_argmax_q8_0(const oracle_view* lhs, const oracle_view* rhs, c
     if (!(l[0] > 0 && l[1] > 0 && l[2] == 1 && l[3] == 1 && r[0] == 1 && r[1] == l[0] && r[2] == 1 && r[3] == 1 &&
           d[0] == 1 && d[1] == 1 && d[2] == 1 && d[3] == 1))
         return ORACLE_SHAPE_MISMATCH;
-    const uint64_t blocks = l[0] / 32, rows = l[1], row_bytes = blocks * 34;
+    const uint64_t blocks = l[0] / 32, rows = l[1], row_bytes = blocks * bb;
     const float* x = (const float*)rhs->data;
     static int8_t qs[1024 * 32];
-    static float dr[1024];
+    static uint16_t dr16[1024];
     for (uint64_t b = 0; b < blocks; ++b) {
         float amax = 0.0f;
         for (int i = 0; i < 32; ++i) amax = fmaxf(amax, fabsf(x[b * 32 + i]));
         const float scale = amax / 127.0f;
         const float inverse = scale == 0.0f ? 0.0f : 1.0f / scale;
-        dr[b] = gr_quant_fp16_to_f32(oracle_fp32_to_fp16(scale));
+        dr16[b] = oracle_fp32_to_fp16(scale);
         for (int i = 0; i < 32; ++i) {
             float q = roundf(x[b * 32 + i] * inverse);
             if (isnan(q)) q = 0.0f; /* `as i8` of NaN */
@@ -1160,9 +1170,38 @@ int oracle_mul_mat_argmax_q8_0(const oracle_view* lhs, const oracle_view* rhs, c
         const uint8_t* rp = base + row * row_bytes;
         float sum = 0.0f;
         for (uint64_t b = 0; b < blocks; ++b) {
+            const uint8_t* blk = rp + b * bb;
+            const int8_t* q = qs + b * 32;
+            const float dl = gr_quant_fp16_to_f32(gr_le16(blk)), drs = gr_quant_fp16_to_f32(dr16[b]);
             int32_t integer = 0;
-            for (int i = 0; i < 32; ++i) integer += (int32_t)(int8_t)rp[b * 34 + 2 + i] * (int32_t)qs[b * 32 + i];
-            sum += (float)integer * (gr_quant_fp16_to_f32(gr_le16(rp + b * 34)) * dr[b]);
+            if (code == 8) {
+                for (int i = 0; i < 32; ++i) integer += (int32_t)(int8_t)blk[2 + i] * (int32_t)q[i];
+                sum += (float)integer * (dl * drs);
+            } else if (code == 2) {
+                for (int i = 0; i < 16; ++i) {
+                    integer += ((int32_t)(blk[2 + i] & 0x0f) - 8) * (int32_t)q[i];
+                    integer += ((int32_t)(blk[2 + i] >> 4) - 8) * (int32_t)q[i + 16];
+                }
+                sum += (float)integer * (dl * drs);
+            } else if (code == 6) {
+                const uint32_t high = (uint32_t)blk[2] | ((uint32_t)blk[3] << 8) | ((uint32_t)blk[4] << 16) |
+                                      ((uint32_t)blk[5] << 24);
+                for (int i = 0; i < 16; ++i) {
+                    const int32_t lo = (int32_t)((blk[6 + i] & 0x0f) | (((high >> i) & 1u) << 4)) - 16;
+                    const int32_t hi = (int32_t)((blk[6 + i] >> 4) | (((high >> (i + 16)) & 1u) << 4)) - 16;
+                    integer += lo * (int32_t)q[i] + hi * (int32_t)q[i + 16];
+                }
+                sum += (float)integer * (dl * drs);
+            } else { /* Q4_1: rhs_scale * (d * integer + m * rhs_sum) (matmul.rs:1832-1858) */
+                int32_t rhs_sum = 0;
+                for (int i = 0; i < 16; ++i) {
+                    integer += (int32_t)(blk[4 + i] & 0x0f) * (int32_t)q[i];
+                    integer += (int32_t)(blk[4 + i] >> 4) * (int32_t)q[i + 16];
+                    rhs_sum += (int32_t)q[i] + (int32_t)q[i + 16];
+                }
+                const float ml = gr_quant_fp16_to_f32(gr_le16(blk + 2));
+                sum += drs * (dl * (float)integer + ml * (float)rhs_sum);
+            }
         }
         if (sum > best || row == 0) {
             best = sum;
@@ -1172,6 +1211,26 @@ int oracle_mul_mat_argmax_q8_0(const oracle_view* lhs, const oracle_view* rhs, c
     *(float*)dst->data = best;
     if (index_out) *index_out = best_index;
     return ORACLE_OK;
+}
+
+int oracle_mul_mat_argmax_q8_0(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
+                               int32_t* index_out) {
+    return oracle_argmax_packed(8, lhs, rhs, dst, index_out);
+}
+
+int oracle_mul_mat_argmax_q4_0(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
+                               int32_t* index_out) {
+    return oracle_argmax_packed(2, lhs, rhs, dst, index_out);
+}
+
+int oracle_mul_mat_argmax_q4_1(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
+                               int32_t* index_out) {
+    return oracle_argmax_packed(3, lhs, rhs, dst, index_out);
+}
+
+int oracle_mul_mat_argmax_q5_0(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
+                               int32_t* index_out) {
+    return oracle_argmax_packed(6, lhs, rhs, dst, index_out);
 }
 
 /* ---------------------------------------------------------------------- */

@@ -74,6 +74,14 @@ int oracle_mul_mat_argmax(const oracle_view* lhs, const oracle_view* rhs, const 
  * k / 32 <= 1024), rhs [1, k] dense F32, dst [1]. */
 int oracle_mul_mat_argmax_q8_0(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
                                int32_t* index_out);
+/* The same with Q4_0 (18-byte), Q4_1 (20-byte) and Q5_0 (22-byte) blocks
+ * (matmul.rs OpMulMatArgmaxQ4_0 / Q4_1 / Q5_0). */
+int oracle_mul_mat_argmax_q4_0(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
+                               int32_t* index_out);
+int oracle_mul_mat_argmax_q4_1(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
+                               int32_t* index_out);
+int oracle_mul_mat_argmax_q5_0(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
+                               int32_t* index_out);
 /* diag.rs OpDiag / OpDiagMaskInf (mode 0) / OpDiagMaskZero (mode 1) over flat
  * f32 slices. */
 int oracle_diag(const float* input, uint64_t input_len, float* output, uint64_t output_len);

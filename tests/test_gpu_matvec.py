@@ -172,3 +172,77 @@ def test_q8_0_special_values(emel, kern, oracle_lib):
     blob = np.concatenate([one] * 5)
     st, sync, ost, gv, gi, ov, oi = run_q8_both(emel, kern, oracle_lib, blob, np.ones(k, np.float32), k, 5)
     assert gi == oi == 0
+
+
+# ---- Q4_0 / Q4_1 / Q5_0 rows (matmul.rs OpMulMatArgmaxQ4_0 / Q4_1 / Q5_0) -------
+
+PACKED = {2: ("q4_0", 18), 3: ("q4_1", 20), 6: ("q5_0", 22), 8: ("q8_0", 34)}
+
+
+def packed_rows(rng, code, k, rows, planted=None):
+    """Random rows of the format: binary16 scales (and Q4_1 mins) 2^e * u,
+    random nibbles / high bits / quants."""
+    blocks = k // 32
+    bb = PACKED[code][1]
+    blob = rng.integers(0, 256, size=(rows, blocks, bb), dtype=np.uint8)
+    d = (rng.uniform(0.5, 1.0, size=(rows, blocks)) * 2.0 ** rng.integers(-10, -4, size=(rows, blocks)))
+    blob[:, :, :2] = d.astype(np.float16).view(np.uint8).reshape(rows, blocks, 2)
+    if code == 3:
+        m = -(rng.uniform(0.5, 1.0, size=(rows, blocks)) * 2.0 ** -6)
+        blob[:, :, 2:4] = m.astype(np.float16).view(np.uint8).reshape(rows, blocks, 2)
+    if planted is not None:
+        blob[planted, :, :2] = np.array([0.25], np.float16).view(np.uint8)
+    return blob.reshape(-1)
+
+
+def run_packed_both(emel, kern, olib, code, blob, rhs, k, rows):
+    ctx = kern.ctx
+    suffix, bb = PACKED[code]
+    rb = k // 32 * bb
+    bl, br = emel.DeviceBuffer(ctx, blob.nbytes + 16), emel.DeviceBuffer(ctx, rhs.nbytes)
+    bd, bi = emel.DeviceBuffer(ctx, 16), emel.DeviceBuffer(ctx, 16)
+    bl.upload(blob)
+    br.upload(rhs)
+    v = emel.CView()
+    v.data, v.storage_bytes, v.dtype = bl.ptr, blob.nbytes, code
+    for dim, (n, s) in enumerate(zip([k, rows, 1, 1], [1, rb, rb * rows, rb * rows])):
+        v.ne[dim], v.nb[dim] = n, s
+    fn = getattr(emel.lib(), f"emel_cuda_mul_mat_argmax_{suffix}")
+    st = fn(ctx.handle, None, B(v), B(cview(emel, br, rhs.nbytes, [1, k, 1, 1])), B(cview(emel, bd, 4, [1, 1, 1, 1])),
+            ctypes.c_void_p(bi.ptr))
+    sync = emel.lib().emel_cuda_stream_synchronize(ctx.handle, None)
+    got_v = bd.download(np.empty(4, np.float32))[0]
+    got_i = int(bi.download(np.empty(4, np.int32))[0])
+    out = np.full(1, 9.0, np.float32)
+    idx = ctypes.c_int32()
+    ost = getattr(olib, f"oracle_mul_mat_argmax_{suffix}")(
+        B(oracle.make_view(blob.ctypes.data, blob.nbytes, [k, rows, 1, 1], [1, rb, rb * rows, rb * rows], code)),
+        B(oracle.make_view(rhs.ctypes.data, rhs.nbytes, [1, k, 1, 1], nb_of([1, k, 1, 1]), 0)),
+        B(oracle.make_view(out.ctypes.data, out.nbytes, [1, 1, 1, 1], nb_of([1, 1, 1, 1]), 0)), B(idx))
+    for b in (bl, br, bd, bi):
+        b.free()
+    return int(st), int(sync), ost, np.float32(got_v), got_i, out[0], idx.value
+
+
+def test_q5_0_reference_golden_vector(emel, kern, oracle_lib):
+    # snapshots/parity/kernel-argmax-parity/manifest.txt case=q5_0_success
+    blob = np.zeros(352, np.uint8)
+    for b in range(16):
+        blob[b * 22:b * 22 + 2] = (0x00, 0x3C)
+        if b >= 8:
+            blob[b * 22 + 2:b * 22 + 6] = 0xFF
+            blob[b * 22 + 6:b * 22 + 22] = 0x0F
+    st, sync, ost, gv, gi, ov, oi = run_packed_both(emel, kern, oracle_lib, 6, blob, np.ones(256, np.float32), 256, 2)
+    assert st == 0 and sync == 0 and gi == 1 and int(np.array([gv]).view(np.uint32)[0]) == 0x44EFFC40
+
+
+@pytest.mark.parametrize("code", [2, 3, 6])
+@pytest.mark.parametrize("k,rows", [(32, 1), (64, 9), (96, 33), (4096, 2000), (32768, 40), (288, 257)])
+def test_packed_parity(emel, kern, oracle_lib, code, k, rows):
+    rng = np.random.default_rng(code * 1000 + k + rows)
+    planted = int(rng.integers(0, rows))
+    blob = packed_rows(rng, code, k, rows, planted)
+    rhs = rng.standard_normal(k).astype(np.float32)
+    st, sync, ost, gv, gi, ov, oi = run_packed_both(emel, kern, oracle_lib, code, blob, rhs, k, rows)
+    assert st == 0 and sync == 0 and ost == 0
+    assert gi == oi and np.array([gv]).view(np.uint32)[0] == np.array([ov]).view(np.uint32)[0]

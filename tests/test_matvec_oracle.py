@@ -146,3 +146,88 @@ def test_q8_0_matches_float_scores(lib):
             blob += d.tobytes() + q.tobytes()
     st, out, idx = run_q8(lib, blob, k, rows, x)
     assert st == 0 and idx == 17
+
+
+# ---- Q4_0 / Q4_1 / Q5_0 rows (matmul.rs OpMulMatArgmaxQ4_0 / Q4_1 / Q5_0) -------
+
+BLOCK_BYTES = {2: 18, 3: 20, 6: 22, 8: 34}
+ORACLE_FN = {2: "oracle_mul_mat_argmax_q4_0", 3: "oracle_mul_mat_argmax_q4_1", 6: "oracle_mul_mat_argmax_q5_0",
+             8: "oracle_mul_mat_argmax_q8_0"}
+
+
+def run_packed(lib, code, lhs_bytes, k, rows, rhs, fill=9.0):
+    lhs = np.frombuffer(bytes(lhs_bytes), np.uint8).copy()
+    rhs = np.asarray(rhs, np.float32)
+    out = np.full(1, fill, np.float32)
+    idx = ctypes.c_int32(-7)
+    rb = k // 32 * BLOCK_BYTES[code]
+    st = getattr(lib, ORACLE_FN[code])(
+        B(oracle.make_view(lhs.ctypes.data, lhs.nbytes, [k, rows, 1, 1], [1, rb, rb * rows, rb * rows], code)),
+        B(oracle.make_view(rhs.ctypes.data, rhs.nbytes, [1, k, 1, 1], nb_of([1, k, 1, 1]), 0)),
+        B(oracle.make_view(out.ctypes.data, out.nbytes, [1, 1, 1, 1], nb_of([1, 1, 1, 1]), 0)), B(idx))
+    return st, out, idx.value
+
+
+def test_q5_0_reference_golden_vector(lib):
+    # snapshots/parity/kernel-argmax-parity/manifest.txt case=q5_0_success:
+    # index=1 output_bits=44effc40; inputs from
+    # tools/emel-kernel-argmax-parity/src/main.rs:49-59 and 114-127
+    lhs = bytearray(352)
+    for b in range(16):
+        lhs[b * 22:b * 22 + 2] = bytes([0x00, 0x3C])
+        if b >= 8:
+            lhs[b * 22 + 2:b * 22 + 6] = bytes([0xFF]) * 4
+            lhs[b * 22 + 6:b * 22 + 22] = bytes([0x0F]) * 16
+    st, out, idx = run_packed(lib, 6, lhs, 256, 2, np.ones(256))
+    assert st == 0 and idx == 1 and int(out.view(np.uint32)[0]) == 0x44EFFC40
+
+
+def nibble_block(code, encoded):
+    # tests/any/matmul_ops.rs:49-74: scale 1.0, every nibble `encoded`
+    byte = bytes([encoded | (encoded << 4)])
+    if code == 2:
+        return bytes([0x00, 0x3C]) + byte * 16
+    if code == 3:
+        return bytes([0x00, 0x3C, 0x00, 0x00]) + byte * 16
+    return bytes([0x00, 0x3C]) + bytes([0xFF]) * 4 + byte * 16
+
+
+def test_q4_q5_known_answers(lib):
+    # matmul_ops.rs:1266-1340: the second row wins, with a positive score
+    for code, (a, b) in ((2, (0x09, 0x0A)), (3, (1, 2)), (6, (0x01, 0x02))):
+        st, out, idx = run_packed(lib, code, nibble_block(code, a) + nibble_block(code, b), 32, 2, np.ones(32))
+        assert st == 0 and idx == 1 and out[0] > 0, code
+    # matmul_ops.rs:1342-1360: a Q4_1 row stride that is not 20 bytes is rejected
+    lhs = np.zeros(21, np.uint8)
+    rhs = np.ones(32, np.float32)
+    out = np.full(1, 9.0, np.float32)
+    idx = ctypes.c_int32()
+    st = lib.oracle_mul_mat_argmax_q4_1(B(oracle.make_view(lhs.ctypes.data, 21, [32, 1, 1, 1], [1, 21, 21, 21], 3)),
+                                        B(oracle.make_view(rhs.ctypes.data, 128, [1, 32, 1, 1], nb_of([1, 32, 1, 1]), 0)),
+                                        B(oracle.make_view(out.ctypes.data, 4, [1, 1, 1, 1], nb_of([1, 1, 1, 1]), 0)),
+                                        B(idx))
+    assert st == 1 and out[0] == 9.0
+
+
+def test_q4_q5_decoding_matches_float_dot(lib):
+    # a row's score equals the float dot of its decoded weights with the
+    # quantized rhs (all terms exact here: integer scales, one block)
+    rng = np.random.default_rng(21)
+    x = rng.integers(-127, 128, 32).astype(np.float32)
+    x[0] = 127.0  # amax 127: rhs scale 1, quants equal x
+    for code in (2, 3, 6):
+        nib = rng.integers(0, 16, 32)
+        hb = rng.integers(0, 2, 32)
+        if code == 2:
+            w = nib - 8
+            blk = bytes([0x00, 0x3C]) + bytes(int(nib[i] | (nib[i + 16] << 4)) for i in range(16))
+        elif code == 3:
+            w = nib + 2.0  # min 2.0 (0x4000)
+            blk = bytes([0x00, 0x3C, 0x00, 0x40]) + bytes(int(nib[i] | (nib[i + 16] << 4)) for i in range(16))
+        else:
+            w = (nib | (hb << 4)) - 16
+            high = sum(int(hb[i]) << i for i in range(32))
+            blk = bytes([0x00, 0x3C]) + high.to_bytes(4, "little") + bytes(int(nib[i] | (nib[i + 16] << 4))
+                                                                            for i in range(16))
+        st, out, idx = run_packed(lib, code, blk, 32, 1, x)
+        assert st == 0 and out[0] == np.float32(np.dot(w.astype(np.float64), x.astype(np.float64))), code
