@@ -221,8 +221,9 @@ __global__ void __launch_bounds__(kMvRows) mv_argmax_plain(MvArgmaxPlan p) {
 // matmul.rs:1629-1653: one warp per 32-value block, amax by a max-reduction,
 // which is exact; Q4_1 also keeps each block's quant sum).  A warp owns 32
 // rows at a time.  For each row in turn the lanes form the block terms of 128
-// consecutive blocks (lane l: blocks l, l + 32, l + 64, l + 96, all loads
-// issued first) into a padded shared tile [32 rows][129]; then lane r folds
+// consecutive blocks (lane l: blocks l, l + 32, l + 64, l + 96; the next
+// row's loads are issued before this row's terms are formed) into a padded
+// shared tile [32 rows][129]; then lane r folds
 // row r's terms in block order, one binary32 add each -- the order of
 // dot_q4_0 / dot_q4_1 / dot_q5_0 / dot_q8_0 (matmul.rs:1804-1910) -- so the
 // 32 sequential sums run side by side.  A block is read as aligned 32-bit
@@ -322,7 +323,7 @@ __device__ __forceinline__ float packed_block_term(const PackedBlock<CODE>& k, u
 }
 
 template <int CODE>
-__global__ void __launch_bounds__(kQ8Threads) mv_argmax_packed(MvArgmaxPlan p, const uint8_t* lhs) {
+__global__ void __launch_bounds__(kQ8Threads, 3) mv_argmax_packed(MvArgmaxPlan p, const uint8_t* lhs) {
     extern __shared__ __align__(16) uint32_t q8_smem[];
     __shared__ MvPart warp_best[kQ8Warps];
     constexpr int BB = PackedFmt<CODE>::kBytes;
@@ -360,19 +361,26 @@ __global__ void __launch_bounds__(kQ8Threads) mv_argmax_packed(MvArgmaxPlan p, c
         const uint32_t nrows = p.rows - g0 < 32u ? (uint32_t)(p.rows - g0) : 32u;
         float sum = 0.0f;  // lane r: row g0 + r
         for (uint32_t b0 = 0; b0 < blocks; b0 += kQ8Chunk) {
-            for (uint32_t r = 0; r < nrows; ++r) {
+            // row r's blocks are in registers while row r + 1's loads are in flight
+            PackedBlock<CODE> cur[4], nxt[4];
+            const auto load_row = [&](PackedBlock<CODE>(&dst)[4], uint32_t r) {
                 const uint8_t* rp = lhs + (g0 + r) * row_bytes;
-                PackedBlock<CODE> blk[4];
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     const uint32_t b = b0 + 32 * c + lane;
-                    if (b < blocks) blk[c].load(rp + (uint64_t)b * BB);
+                    if (b < blocks) dst[c].load(rp + (uint64_t)b * BB);
                 }
+            };
+            load_row(cur, 0);
+            for (uint32_t r = 0; r < nrows; ++r) {
+                if (r + 1 < nrows) load_row(nxt, r + 1);
 #pragma unroll
                 for (int c = 0; c < 4; ++c) {
                     const uint32_t b = b0 + 32 * c + lane;
-                    if (b < blocks) terms[r * kQ8TermStride + 32 * c + lane] = packed_block_term<CODE>(blk[c], b, rq, rd, rs);
+                    if (b < blocks) terms[r * kQ8TermStride + 32 * c + lane] = packed_block_term<CODE>(cur[c], b, rq, rd, rs);
                 }
+#pragma unroll
+                for (int c = 0; c < 4; ++c) cur[c] = nxt[c];
             }
             __syncwarp();
             if ((uint32_t)lane < nrows) {
