@@ -705,11 +705,17 @@ def run_suite(args):
         tx = [torch.from_numpy(x).to(dev) for _ in range(sets)]
         ty = [torch.empty_like(t) for t in tx]
         del x
-        for o, mode in zip(W.diag_spec().ops, (0, 1)):
+        ops = W.diag_spec().ops
+        for o, mode in zip(ops[:2], (0, 1)):
             measure("diag", o.name, o.bytes, o.elements,
                     lambda k, mode=mode: (lambda: chk(lib.emel_cuda_diag_mask(
                         ctx.handle, sh, mode, ctypes.c_void_p(tx[k].data_ptr()), n,
                         ctypes.c_void_p(ty[k].data_ptr()), n, 0))), sets)
+        # the mask fused with soft_max: one read of the kept triangle
+        measure("diag", ops[2].name, ops[2].bytes, ops[2].elements,
+                lambda k: (lambda: chk(lib.emel_cuda_soft_max_diag_mask_inf(
+                    ctx.handle, sh, ctypes.c_void_p(tx[k].data_ptr()), n, ctypes.c_void_p(ty[k].data_ptr()), n, 0))),
+                sets)
         del tx, ty
     # single-query attention (flash_attn.rs OpFlashAttnExt): one CTA per query
     # head runs the reference's per-token binary16 recurrence, so the time is

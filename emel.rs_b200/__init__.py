@@ -202,6 +202,7 @@ SIGNATURES = {
     "emel_cuda_rope": (_I, [_CTX, _V, _P, _P, _P, ctypes.POINTER(CRopeParams)]),
     "emel_cuda_diag": (_I, [_CTX, _V, _V, ctypes.c_uint64, _V, ctypes.c_uint64]),
     "emel_cuda_diag_mask": (_I, [_CTX, _V, _I, _V, ctypes.c_uint64, _V, ctypes.c_uint64, ctypes.c_int32]),
+    "emel_cuda_soft_max_diag_mask_inf": (_I, [_CTX, _V, _V, ctypes.c_uint64, _V, ctypes.c_uint64, ctypes.c_int32]),
     "emel_cuda_flash_attn_ext": (_I, [_CTX, _V, _P, _P, _P, _P, ctypes.POINTER(CFlashAttnOptions)]),
     "emel_cuda_flash_attn_workspace": (_I, [_CTX, ctypes.POINTER(ctypes.c_uint64), ctypes.POINTER(ctypes.c_uint64)]),
     "emel_cuda_cpy": (_I, [_CTX, _V, _P, _P]),
@@ -704,6 +705,22 @@ class OpDiagMaskInf(_DiagMask):
 class OpDiagMaskZero(_DiagMask):
     """diag::OpDiagMaskZero::new(input, output, n_past) (diag.rs:88-108)."""
     MODE = 1
+
+
+@dataclass
+class SoftMaxDiagMaskInf(Event):
+    """diag::OpDiagMaskInf then reductions::OpSoftMax over the dense [side,
+    side] result, fused (emel_cuda_soft_max_diag_mask_inf)."""
+    input: int
+    input_len: int
+    output: int
+    output_len: int
+    n_past: int
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_soft_max_diag_mask_inf(ctx.handle, stream, ctypes.c_void_p(self.input),
+                                                         self.input_len, ctypes.c_void_p(self.output),
+                                                         self.output_len, self.n_past)
 
 
 @dataclass

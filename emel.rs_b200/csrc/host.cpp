@@ -1444,6 +1444,20 @@ emel_cuda_status emel_cuda_diag_mask(emel_cuda_context* ctx, void* stream, int m
                        mode == EMEL_DIAG_MASK_INF ? emel::kDiagMaskInf : emel::kDiagMaskZero);
 }
 
+emel_cuda_status emel_cuda_soft_max_diag_mask_inf(emel_cuda_context* ctx, void* stream, const float* input,
+                                                  uint64_t input_len, float* output, uint64_t output_len,
+                                                  int32_t n_past) {
+    // the mask's guards (mask_valid, diag.rs:122-124); the soft_max of its
+    // dense [side, side] result has none left to fail
+    uint64_t side = 0;
+    if (n_past < 0 || input_len != output_len || !diag_square_side(input_len, &side)) return EMEL_CUDA_INVALID_SHAPE;
+    if (ctx == nullptr || input == nullptr || output == nullptr ||
+        ((reinterpret_cast<uintptr_t>(input) | reinterpret_cast<uintptr_t>(output)) & 3u) != 0 ||
+        input_len > UINT64_MAX / 8 || (input != output && ranges_overlap(input, input_len * 4, output, output_len * 4)))
+        return EMEL_CUDA_INVALID_ARGUMENT;
+    return diag_launch(ctx, stream, input, output, side, (uint64_t)n_past, emel::kDiagSoftMaxCausal);
+}
+
 // ---- gated linear units ------------------------------------------------------
 
 emel_cuda_status emel_cuda_glu(emel_cuda_context* ctx, void* stream, int subop, const float* input,

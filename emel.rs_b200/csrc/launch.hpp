@@ -147,7 +147,7 @@ struct FlashAttnPlan {
 cudaError_t launch_flash_attn(const LaunchEnv& env, const FlashAttnPlan& plan);
 
 // Diagonal family (diag.cu): side x side row-major F32 matrices.
-enum DiagMode : int { kDiag = 0, kDiagMaskInf = 1, kDiagMaskZero = 2 };
+enum DiagMode : int { kDiag = 0, kDiagMaskInf = 1, kDiagMaskZero = 2, kDiagSoftMaxCausal = 3 };
 struct DiagPlan {
     const float* in;    // diag: [side]; masks: [side * side] (may equal out)
     float* out;         // [side * side]

@@ -327,7 +327,8 @@ def diag_spec():
     n = DIAG_SIDE * DIAG_SIDE
     kept = DIAG_SIDE * (DIAG_SIDE + 1) // 2
     return Config("diag", [OpSpec("diag_mask_inf_causal", (kept + n) * F32, n),
-                           OpSpec("diag_mask_zero_causal", (kept + n) * F32, n)])
+                           OpSpec("diag_mask_zero_causal", (kept + n) * F32, n),
+                           OpSpec("soft_max_diag_mask_inf_causal", (kept + n) * F32, n)])
 
 
 # The same vocabulary step with Q8_0 rows (matmul.rs OpMulMatArgmaxQ8_0):

@@ -425,6 +425,17 @@ EMEL_CUDA_API emel_cuda_status emel_cuda_diag_mask(emel_cuda_context* ctx, void*
                                                    const float* input, uint64_t input_len, float* output,
                                                    uint64_t output_len, int32_t n_past);
 
+/* diag::OpDiagMaskInf::new(input, tmp, n_past) followed by
+ * reductions::OpSoftMax over tmp as a dense [side, side] view (diag.rs:
+ * 144-161, reductions.rs:565-638), in one call that reads each row's kept
+ * part only: output row r is the soft_max of input[r, 0 .. r + n_past] with
+ * +0 above it (the exact results of the two events; sums in binary64, so
+ * within the soft_max tolerance of the sequential reference sum).  Guards
+ * and device additions as emel_cuda_diag_mask; in place is allowed. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_soft_max_diag_mask_inf(emel_cuda_context* ctx, void* stream,
+                                                                const float* input, uint64_t input_len,
+                                                                float* output, uint64_t output_len, int32_t n_past);
+
 /* ---- single-query attention ------------------------------------------- */
 /* flash_attn.rs FlashAttnOptions (flash_attn.rs:24-31): has_scale == 0
  * selects 1 / sqrt(head_dim); has_masked_total_tokens == 0 selects the

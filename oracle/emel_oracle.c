@@ -1527,6 +1527,31 @@ static int soft_max_core(const oracle_view* src, const oracle_view* mask, const 
 
 int oracle_soft_max(const oracle_view* src, const oracle_view* dst) { return soft_max_core(src, NULL, dst, 1.0f, 0); }
 
+/* OpDiagMaskInf then OpSoftMax (diag.rs:144-161, reductions.rs:565-638):
+ * the two events in sequence, the mask's result held in `scratch` (side^2
+ * floats) and read by the soft_max as a dense [side, side] view. */
+int oracle_soft_max_diag_mask_inf(const float* input, uint64_t input_len, float* output, uint64_t output_len,
+                                  int32_t n_past, float* scratch) {
+    int st = oracle_diag_mask(0, input, input_len, scratch, output_len, n_past);
+    if (st != ORACLE_OK) return st;
+    uint64_t side = 0;
+    diag_square_side(input_len, &side);
+    const uint64_t ne[4] = {side, side, 1, 1};
+    const uint64_t nb[4] = {4, 4 * side, 4 * side * side, 4 * side * side};
+    oracle_view src, dst;
+    memset(&src, 0, sizeof src);
+    memset(&dst, 0, sizeof dst);
+    src.data = scratch;
+    dst.data = output;
+    src.storage_bytes = dst.storage_bytes = input_len * 4;
+    for (int d = 0; d < 4; ++d) {
+        src.ne[d] = dst.ne[d] = ne[d];
+        src.nb[d] = dst.nb[d] = nb[d];
+    }
+    src.dtype = dst.dtype = DT_F32;
+    return soft_max_core(&src, NULL, &dst, 1.0f, 0);
+}
+
 int oracle_soft_max_ext(const oracle_view* src, const oracle_view* mask, const oracle_view* dst, float scale) {
     return soft_max_core(src, mask, dst, scale, 1);
 }

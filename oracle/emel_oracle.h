@@ -87,6 +87,10 @@ int oracle_mul_mat_argmax_q5_0(const oracle_view* lhs, const oracle_view* rhs, c
 int oracle_diag(const float* input, uint64_t input_len, float* output, uint64_t output_len);
 int oracle_diag_mask(int mode, const float* input, uint64_t input_len, float* output, uint64_t output_len,
                      int32_t n_past);
+/* OpDiagMaskInf then OpSoftMax over the dense [side, side] result; scratch
+ * holds side^2 floats. */
+int oracle_soft_max_diag_mask_inf(const float* input, uint64_t input_len, float* output, uint64_t output_len,
+                                  int32_t n_past, float* scratch);
 /* flash_attn.rs FlashAttnOptions (flash_attn.rs:24-31): an absent scale is
  * 1 / sqrt(head_dim), an absent token count is the key's ne[1]. */
 typedef struct oracle_flash_attn_options {

@@ -128,6 +128,8 @@ def load(cr=False):
         "oracle_rope": [P, P, P, ctypes.POINTER(RopeParams)],
         "oracle_flash_attn_ext": [P, P, P, P, ctypes.POINTER(FlashAttnOptions)],
         "oracle_diag": [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_uint64],
+        "oracle_soft_max_diag_mask_inf": [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_uint64,
+                                          ctypes.c_int32, ctypes.c_void_p],
         "oracle_diag_mask": [ctypes.c_int, ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_uint64,
                              ctypes.c_int32],
         "oracle_cont": [P, P],

@@ -76,3 +76,27 @@ def test_shape_guards(lib):
     assert mask(lib, 0, [], 0, 0)[0] == 6                     # empty
     assert diag(lib, [], 0)[0] == 6
     assert diag(lib, [1.0, 2.0, 3.0], 9)[0] == 0
+
+
+def softmax_causal(lib, x, side, n_past):
+    x = np.asarray(x, np.float32)
+    out = np.full(side * side, 7.0, np.float32)
+    scratch = np.zeros(side * side, np.float32)
+    st = lib.oracle_soft_max_diag_mask_inf(x.ctypes.data, x.size, out.ctypes.data, out.size, n_past,
+                                           scratch.ctypes.data)
+    return st, out
+
+
+def test_softmax_after_causal_mask(lib):
+    # the two reference events in sequence: row 0 keeps one column, row 1 both
+    st, out = softmax_causal(lib, [1.0, 2.0, 3.0, 4.0], 2, 0)
+    assert st == 0
+    e = np.exp(np.float64(3.0) - 4.0)
+    assert out[0] == 1.0 and out[1] == 0.0
+    assert abs(out[2] - e / (1 + e)) < 1e-7 and abs(out[3] - 1 / (1 + e)) < 1e-7
+    # n_past beyond the side: plain soft_max rows
+    st, out = softmax_causal(lib, [1.0, 2.0, 3.0, 4.0], 2, 5)
+    assert st == 0 and abs(out[0] + out[1] - 1.0) < 1e-7 and out[1] > out[0]
+    # the mask's guards
+    assert softmax_causal(lib, [1.0, 2.0, 3.0], 2, 0)[0] == 6
+    assert softmax_causal(lib, [1.0] * 4, 2, -1)[0] == 6

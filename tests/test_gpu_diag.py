@@ -72,3 +72,55 @@ def test_guards_write_nothing(emel, kern):
     assert kern.process_event(emel.OpDiag(bi.ptr, 3, bi.ptr, 9)) == S.INVALID_ARGUMENT
     assert bo.download(np.empty(9, np.float32)).tolist() == [7.0] * 9
     bi.free(), bo.free()
+
+
+def causal_case(emel, kern, oracle_lib, x, side, n_past, in_place=False):
+    bi = dev(emel, kern.ctx, x)
+    bo = bi if in_place else dev(emel, kern.ctx, np.full(side * side, 7.0, np.float32))
+    st = kern.process_event(emel.SoftMaxDiagMaskInf(bi.ptr, side * side, bo.ptr, side * side, n_past))
+    got = bo.download(np.empty(side * side, np.float32))
+    want = np.full(side * side, 7.0, np.float32)
+    scratch = np.zeros(side * side, np.float32)
+    ost = oracle_lib.oracle_soft_max_diag_mask_inf(x.ctypes.data, x.size, want.ctypes.data, want.size, n_past,
+                                                   scratch.ctypes.data)
+    bi.free()
+    if not in_place:
+        bo.free()
+    return int(st), ost, got, want
+
+
+def close_softmax(got, want):
+    """soft_max bar: NaN positions identical, else within 1e-5 relative of
+    the row's largest magnitude (binary64 sums, only their order differs)."""
+    assert np.array_equal(np.isnan(got), np.isnan(want))
+    ok = ~np.isnan(want)
+    assert np.array_equal(got[ok] == 0, want[ok] == 0)
+    assert np.max(np.abs(got[ok] - want[ok]), initial=0.0) <= 1e-5 * max(1.0, float(np.max(np.abs(want[ok]), initial=0)))
+
+
+@pytest.mark.parametrize("side,n_past", [(1, 0), (2, 0), (7, 2), (64, 0), (300, 17), (4096, 0), (1000, 5000)])
+def test_softmax_causal(emel, kern, oracle_lib, side, n_past):
+    rng = np.random.default_rng(side + n_past)
+    x = (rng.standard_normal(side * side) * 4).astype(np.float32)
+    st, ost, got, want = causal_case(emel, kern, oracle_lib, x, side, n_past)
+    assert st == 0 and ost == 0
+    close_softmax(got, want)
+    # bit-for-bit the masked columns, and in place
+    st, ost, got2, _ = causal_case(emel, kern, oracle_lib, x, side, n_past, in_place=True)
+    assert st == 0 and np.array_equal(got.view(np.uint32), got2.view(np.uint32))
+
+
+def test_softmax_causal_special_rows(emel, kern, oracle_lib):
+    side = 40
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal(side * side).astype(np.float32)
+    x[3 * side + 1] = np.nan              # NaN in a kept column
+    x[5 * side + 0] = np.nan              # NaN at column 0 pins the maximum
+    x[7 * side + 0] = -np.inf             # row 7: first kept value -inf, others finite
+    x[8 * side:8 * side + 9] = -np.inf    # row 8: every kept value -inf
+    x[9 * side + 2] = np.inf              # an infinite maximum
+    x[10 * side + 20] = np.nan            # NaN in a masked column: masked to -inf, no effect
+    st, ost, got, want = causal_case(emel, kern, oracle_lib, x, side, 0)
+    assert st == 0 and ost == 0
+    close_softmax(got, want)
+    assert np.isnan(want[3 * side]) and not np.isnan(want[10 * side])
