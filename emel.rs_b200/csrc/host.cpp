@@ -1307,6 +1307,45 @@ emel_cuda_status emel_cuda_mul_mat_argmax_q5_0(emel_cuda_context* ctx, void* str
     return mul_mat_argmax_packed(ctx, stream, lhs, rhs, dst, index_out, EMEL_DTYPE_Q5_0, 22);
 }
 
+emel_cuda_status emel_cuda_mul_mat_argmax_q4_k(emel_cuda_context* ctx, void* stream, const emel_tensor_view* lhs,
+                                               const emel_tensor_view* rhs, const emel_tensor_view* dst,
+                                               int32_t* index_out) {
+    Checked cr, cd;
+    uint64_t row_bytes = 0;
+    // quantized_views_valid (matmul.rs:1522-1542): Q4_K packed rows of at
+    // most 128 blocks of 256 values, dense F32 rhs and destination
+    if (lhs == nullptr || rhs == nullptr || dst == nullptr ||
+        !gr_packed_view_valid(lhs, EMEL_DTYPE_Q4_K, 256, 144, &row_bytes) || lhs->ne[0] / 256 > 128 ||
+        !validate_as(rhs, EMEL_DTYPE_F32, false, &cr) || !validate_as(dst, EMEL_DTYPE_F32, false, &cd) ||
+        !dense_contiguous_f32(rhs) || !dense_contiguous_f32(dst))
+        return EMEL_CUDA_INVALID_VIEW;
+    const uint64_t* l = lhs->ne;
+    const uint64_t* r = rhs->ne;
+    const uint64_t* d = dst->ne;
+    if (!(l[0] > 0 && l[1] > 0 && l[2] == 1 && l[3] == 1 && r[0] == 1 && r[1] == l[0] && r[2] == 1 && r[3] == 1 &&
+          d[0] == 1 && d[1] == 1 && d[2] == 1 && d[3] == 1))
+        return EMEL_CUDA_SHAPE_MISMATCH;
+    if (ctx == nullptr || index_out == nullptr || (reinterpret_cast<uintptr_t>(index_out) & 3u) ||
+        ((reinterpret_cast<uintptr_t>(lhs->data) | reinterpret_cast<uintptr_t>(rhs->data) |
+          reinterpret_cast<uintptr_t>(dst->data)) & 3u) ||
+        l[1] > 0x7fffffffull)
+        return EMEL_CUDA_INVALID_ARGUMENT;
+    emel::MvArgmaxPlan p{};
+    p.rhs = static_cast<const float*>(rhs->data);
+    p.k = l[0];
+    p.rows = l[1];
+    p.dst_value = static_cast<float*>(dst->data);
+    p.dst_index = index_out;
+    char* ws = static_cast<char*>(ctx->workspace);
+    p.ticket = reinterpret_cast<unsigned*>(ws);
+    p.partials = ws + 256;
+    p.fault = reinterpret_cast<uint32_t*>(ws + emel::kFaultWordOffset);
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess)
+        err = emel::launch_mul_mat_argmax_q4_k(env_of(ctx, stream), p, static_cast<const uint8_t*>(lhs->data));
+    return device_status(ctx, err);
+}
+
 // ---- single-query attention -------------------------------------------------
 
 // dense_f32_layout (flash_attn.rs:305-325): effective strides exactly row-major.

@@ -443,6 +443,180 @@ cudaError_t launch_packed(const LaunchEnv& env, const MvArgmaxPlan& p, const uin
                             smem, env.stream, p, lhs);
 }
 
+// ---- K-quant rows (matmul.rs OpMulMatArgmaxQ4K) --------------------------------
+// quantize_q8_k (matmul.rs:1703-1745) per 256-value block in every CTA's
+// shared memory, stored for dp4a: word [b][g][j] holds the quants at
+// positions 32g + j, + 8, + 16, + 24 of block b -- the positions dot_q4_k
+// (matmul.rs:2040-2114) adds into lane sum j of group g.  A warp owns 32
+// rows; its lanes take (row, block) items of a 16-block chunk, each forming
+// that block's eight lane terms d * float(acc[j]) and its minimum term
+// dmin * float(min sum) into a padded shared tile; lane r then folds row r
+// block by block (eight lane sums and the running total, the reference's
+// order) and adds the lane sums to the total after the last block.
+constexpr int kKThreads = 128;
+constexpr int kKWarps = kKThreads / 32;
+constexpr int kKChunk = 16;                       // blocks per pass
+constexpr int kKTerms = 9;                        // eight lane terms + the minimum term
+constexpr int kKRowStride = kKChunk * kKTerms + 1;
+
+__device__ __forceinline__ int32_t q8k_nearest(float v) {
+    return (int32_t)(__float_as_uint(__fadd_rn(v, 12582912.0f)) & 0x007fffffu) - 0x00400000;
+}
+
+__global__ void __launch_bounds__(kKThreads) mv_argmax_q4_k(MvArgmaxPlan p, const uint8_t* lhs) {
+    extern __shared__ __align__(16) uint32_t k_smem[];
+    __shared__ MvPart warp_best[kKWarps];
+    const uint32_t blocks = (uint32_t)(p.k / 256);
+    uint32_t* rq = k_smem;                                           // [blocks][8 groups][8 lanes] quant words
+    float* rd = reinterpret_cast<float*>(rq + blocks * 64);          // [blocks] scales
+    int* rb = reinterpret_cast<int*>(rd + blocks);                   // [blocks][16] group sums
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    float* tile = reinterpret_cast<float*>(rb + blocks * 16) + warp * 32 * kKRowStride;
+    pdl_enter();
+    for (uint32_t b = warp; b < blocks; b += kKWarps) {
+        // lane l holds positions 8l .. 8l + 7
+        float x[8];
+        float absolute = 0.0f, maximum = 0.0f;
+        int first = 256;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            x[i] = p.rhs[(uint64_t)b * 256 + lane * 8 + i];
+            if (fabsf(x[i]) > absolute) {
+                absolute = fabsf(x[i]);
+                maximum = x[i];
+                first = lane * 8 + i;
+            }
+        }
+        // the first position of the largest magnitude (a strict '>' scan)
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float oa = __shfl_xor_sync(0xffffffffu, absolute, o);
+            const float om = __shfl_xor_sync(0xffffffffu, maximum, o);
+            const int of = __shfl_xor_sync(0xffffffffu, first, o);
+            if (oa > absolute || (oa == absolute && of < first)) {
+                absolute = oa;
+                maximum = om;
+                first = of;
+            }
+        }
+        int8_t q[8];
+        float d = 0.0f;
+        if (absolute == 0.0f) {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) q[i] = 0;
+        } else {
+            const float inverse = __fdiv_rn(-127.0f, maximum);
+            d = __fdiv_rn(1.0f, inverse);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int32_t v = q8k_nearest(__fmul_rn(inverse, x[i]));
+                q[i] = (int8_t)(v < 127 ? v : 127);
+            }
+        }
+        // position 8 * lane + i = 32 g + 8 t + jj: group g = lane / 4, t = lane % 4
+        const int g = lane >> 2, t = lane & 3;
+        int8_t* words = reinterpret_cast<int8_t*>(rq + b * 64 + g * 8);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) words[i * 4 + t] = q[i];
+        int gsum = 0;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) gsum += q[i];
+        gsum += __shfl_xor_sync(0xffffffffu, gsum, 1);  // lanes 2h, 2h + 1 hold group h of 16
+        if ((lane & 1) == 0) rb[b * 16 + (lane >> 1)] = (int)(int16_t)gsum;
+        if (lane == 0) rd[b] = d;
+    }
+    __syncthreads();
+    const uint64_t row_bytes = (uint64_t)blocks * 144;
+    MvPart best{0.0f, 0, 0u, 0u};
+    for (uint64_t g0 = ((uint64_t)blockIdx.x * kKWarps + warp) * 32; g0 < p.rows;
+         g0 += (uint64_t)gridDim.x * kKWarps * 32) {
+        const uint32_t nrows = p.rows - g0 < 32u ? (uint32_t)(p.rows - g0) : 32u;
+        float ls[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
+        float total = 0.0f;
+        for (uint32_t b0 = 0; b0 < blocks; b0 += kKChunk) {
+            const uint32_t nbc = blocks - b0 < (uint32_t)kKChunk ? blocks - b0 : (uint32_t)kKChunk;
+            for (uint32_t item = lane; item < nrows * nbc; item += 32) {
+                const uint32_t r = item / nbc, bl = item % nbc, b = b0 + bl;
+                const uint32_t* w = reinterpret_cast<const uint32_t*>(lhs + (g0 + r) * row_bytes + (uint64_t)b * 144);
+                uint32_t W[36];
+#pragma unroll
+                for (int i = 0; i < 36; ++i) W[i] = __ldg(w + i);
+                // scales / minimums (dot_q4_k's unpacking)
+                const uint32_t s0 = W[1], s1 = W[2], s2 = W[3];
+                uint32_t sc[8], mn[8];
+#pragma unroll
+                for (int l = 0; l < 4; ++l) {
+                    const uint32_t a = (s0 >> (8 * l)) & 0xffu, bb = (s1 >> (8 * l)) & 0xffu, c = (s2 >> (8 * l)) & 0xffu;
+                    sc[l] = a & 0x3fu;
+                    sc[4 + l] = (c & 0x0fu) | ((a >> 6) << 4);
+                    mn[l] = bb & 0x3fu;
+                    mn[4 + l] = (c >> 4) | ((bb >> 6) << 4);
+                }
+                int min_sum = 0;
+#pragma unroll
+                for (int h = 0; h < 16; ++h) min_sum += rb[b * 16 + h] * (int)mn[h >> 1];
+                int acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+                const uint32_t* r4 = rq + b * 64;
+#pragma unroll
+                for (int gg = 0; gg < 8; ++gg) {
+                    const int h = gg >> 1;
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        const int k0 = 4 + 8 * h + (j >> 2), bt = j & 3;
+                        const uint32_t sel = (uint32_t)bt | ((uint32_t)(bt + 4) << 4);
+                        const uint32_t lo = __byte_perm(W[k0], W[k0 + 2], sel);
+                        const uint32_t hi = __byte_perm(W[k0 + 4], W[k0 + 6], sel);
+                        uint32_t v = __byte_perm(lo, hi, 0x5410);
+                        v = (gg & 1) ? ((v >> 4) & 0x0f0f0f0fu) : (v & 0x0f0f0f0fu);
+                        acc[j] += (int)sc[gg] * __dp4a((int)v, (int)r4[gg * 8 + j], 0);
+                    }
+                }
+                const float dd = __fmul_rn(f16_bits_to_f32((uint16_t)(W[0] & 0xffffu)), rd[b]);
+                const float dm = __fmul_rn(f16_bits_to_f32((uint16_t)(W[0] >> 16)), rd[b]);
+                float* o = tile + r * kKRowStride + bl * kKTerms;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) o[j] = __fmul_rn(dd, (float)acc[j]);
+                o[8] = __fmul_rn(dm, (float)min_sum);
+            }
+            __syncwarp();
+            if ((uint32_t)lane < nrows) {
+                const float* t = tile + lane * kKRowStride;
+                for (uint32_t bl = 0; bl < nbc; ++bl) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) ls[j] = __fadd_rn(ls[j], t[bl * kKTerms + j]);
+                    total = __fsub_rn(total, t[bl * kKTerms + 8]);
+                }
+            }
+            __syncwarp();
+        }
+        if ((uint32_t)lane < nrows) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) total = __fadd_rn(total, ls[j]);
+            const uint64_t row = g0 + lane;
+            const bool nan = is_nan(total);
+            best = mv_better(best, MvPart{total, (int32_t)row, nan ? 0u : 1u, (nan && row == 0) ? 1u : 0u});
+        }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        MvPart other;
+        other.v = __shfl_xor_sync(0xffffffffu, best.v, o);
+        other.i = __shfl_xor_sync(0xffffffffu, best.i, o);
+        other.has = __shfl_xor_sync(0xffffffffu, best.has, o);
+        other.pin = __shfl_xor_sync(0xffffffffu, best.pin, o);
+        best = mv_better(best, other);
+    }
+    if (lane == 0) warp_best[warp] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        MvPart b = warp_best[0];
+        for (int w = 1; w < kKWarps; ++w) b = mv_better(b, warp_best[w]);
+        warp_best[0] = b;
+    }
+    __syncthreads();
+    finish(p, warp_best[0]);
+}
+
 }  // namespace
 
 namespace {
@@ -500,6 +674,25 @@ cudaError_t launch_mul_mat_argmax(const LaunchEnv& env, const MvArgmaxPlan& p) {
         err = launch_dependent(mv_argmax_plain, dim3((unsigned)(tiles < cap ? tiles : cap)), dim3(kMvRows), 0,
                                env.stream, p);
     }
+    ++*env.launches;
+    return err != cudaSuccess ? err : cudaGetLastError();
+}
+
+cudaError_t launch_mul_mat_argmax_q4_k(const LaunchEnv& env, const MvArgmaxPlan& p, const uint8_t* lhs) {
+    const uint64_t groups = (p.rows + kKWarps * 32 - 1) / (kKWarps * 32);
+    const uint64_t cap = (uint64_t)env.sm_count * 3;
+    const size_t table = (size_t)kKWarps * 32 * kKRowStride * 4;
+    const size_t smem = (size_t)(p.k / 256) * (64 * 4 + 4 + 16 * 4) + table;
+    static int configured_device_mask = 0;
+    const int bit = env.device < 31 ? (1 << env.device) : 0;
+    if (!(configured_device_mask & bit)) {
+        const cudaError_t e = cudaFuncSetAttribute(mv_argmax_q4_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                                   (int)(128 * (64 * 4 + 4 + 16 * 4) + table));
+        if (e != cudaSuccess) return e;
+        configured_device_mask |= bit;
+    }
+    const cudaError_t err = launch_dependent(mv_argmax_q4_k, dim3((unsigned)(groups < cap ? groups : cap)),
+                                             dim3(kKThreads), smem, env.stream, p, lhs);
     ++*env.launches;
     return err != cudaSuccess ? err : cudaGetLastError();
 }

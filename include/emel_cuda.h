@@ -505,6 +505,18 @@ EMEL_CUDA_API emel_cuda_status emel_cuda_mul_mat_argmax_q4_1(emel_cuda_context* 
 EMEL_CUDA_API emel_cuda_status emel_cuda_mul_mat_argmax_q5_0(emel_cuda_context* ctx, void* stream,
                                                              const emel_tensor_view* lhs, const emel_tensor_view* rhs,
                                                              const emel_tensor_view* dst, int32_t* index_out);
+/* matmul::OpMulMatArgmaxQ4K (matmul.rs:530-535, route via
+ * define_k_argmax_runner 2502-2534): Q4_K rows (144-byte blocks of 256
+ * values: binary16 scale and minimum scale, 12 bytes of 6-bit group scales
+ * and minimums, 128 bytes of nibbles), k / 256 <= 128 blocks.  The rhs is
+ * quantized to Q8_K (quantize_q8_k, matmul.rs:1703-1745); each row keeps
+ * eight lane sums (lane = position % 8) of d * float(scaled integer dots)
+ * and a running total of -dmin * float(minimum sums), adding the lane sums
+ * to the total after its last block (dot_q4_k, matmul.rs:2040-2114).
+ * Statuses and device additions as emel_cuda_mul_mat_argmax_q8_0. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_mul_mat_argmax_q4_k(emel_cuda_context* ctx, void* stream,
+                                                             const emel_tensor_view* lhs, const emel_tensor_view* rhs,
+                                                             const emel_tensor_view* dst, int32_t* index_out);
 
 /* ---- shape copies ----------------------------------------------------- */
 /* shape::OpCpy (shape.rs:55-69; guards 453-466, loop copy_view 438-444):

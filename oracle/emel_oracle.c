@@ -1233,6 +1233,151 @@ int oracle_mul_mat_argmax_q5_0(const oracle_view* lhs, const oracle_view* rhs, c
     return oracle_argmax_packed(6, lhs, rhs, dst, index_out);
 }
 
+/* K-quant vocabulary matvec + argmax: matmul.rs OpMulMatArgmaxQ4K / Q6K
+ * (routes through define_k_argmax_runner, matmul.rs:2502-2535).  The rhs is
+ * quantized to Q8_K per 256-value block (quantize_q8_k, matmul.rs:1703-1745:
+ * the first value of largest magnitude sets inverse = -127 / value, d =
+ * 1 / inverse, q = min(nearest_int(inverse * x), 127), 16 group sums);
+ * dot_q4_k (2040-2114) and dot_q6_k (2117-2190) keep eight lane sums,
+ * lane = position % 8, added to the row total after the last block. */
+typedef struct {
+    float d;
+    int8_t qs[256];
+    int16_t bsums[16];
+} q8k_block;
+
+/* nearest_int (matmul.rs:1696-1700): round through the 1.5 * 2^23 bias. */
+static int32_t q8k_nearest_int(float v) {
+    const float biased = v + 12582912.0f;
+    return (int32_t)(f2u(biased) & 0x007fffffu) - 0x00400000;
+}
+
+static void q8k_quantize(const float* x, uint64_t blocks, q8k_block* out) {
+    for (uint64_t b = 0; b < blocks; ++b) {
+        const float* v = x + b * 256;
+        float maximum = 0.0f, absolute = 0.0f;
+        for (int i = 0; i < 256; ++i)
+            if (fabsf(v[i]) > absolute) {
+                absolute = fabsf(v[i]);
+                maximum = v[i];
+            }
+        memset(&out[b], 0, sizeof out[b]);
+        if (absolute == 0.0f) continue;
+        const float inverse = -127.0f / maximum;
+        out[b].d = 1.0f / inverse;
+        for (int i = 0; i < 256; ++i) {
+            int32_t q = q8k_nearest_int(inverse * v[i]);
+            out[b].qs[i] = (int8_t)(q < 127 ? q : 127);
+        }
+        for (int g = 0; g < 16; ++g) {
+            int16_t sum = 0;
+            for (int i = 0; i < 16; ++i) sum = (int16_t)(sum + out[b].qs[g * 16 + i]);
+            out[b].bsums[g] = sum;
+        }
+    }
+}
+
+static float dot_q4_k_block(const uint8_t* blk, const q8k_block* r, float* lane_sums, float sum) {
+    int8_t q4[256];
+    for (int g = 0; g < 4; ++g)
+        for (int l = 0; l < 32; ++l) {
+            const uint8_t packed = blk[16 + g * 32 + l];
+            q4[g * 64 + l] = (int8_t)(packed & 0x0f);
+            q4[g * 64 + 32 + l] = (int8_t)(packed >> 4);
+        }
+    const uint8_t* sc = blk + 4;
+    uint8_t scales[8], mins[8];
+    for (int l = 0; l < 4; ++l) {
+        scales[l] = sc[l] & 0x3f;
+        scales[4 + l] = (uint8_t)((sc[8 + l] & 0x0f) | (((sc[l] >> 6) & 0x03) << 4));
+        mins[l] = sc[4 + l] & 0x3f;
+        mins[4 + l] = (uint8_t)(((sc[8 + l] >> 4) & 0x0f) | (((sc[4 + l] >> 6) & 0x03) << 4));
+    }
+    int32_t min_sum = 0;
+    for (int g = 0; g < 16; ++g) min_sum += (int32_t)r->bsums[g] * (int32_t)mins[g / 2];
+    int32_t acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int g = 0; g < 8; ++g)
+        for (int l = 0; l < 32; ++l)
+            acc[l % 8] += (int32_t)scales[g] * ((int32_t)q4[g * 32 + l] * (int32_t)r->qs[g * 32 + l]);
+    const float d = gr_quant_fp16_to_f32(gr_le16(blk)) * r->d;
+    for (int l = 0; l < 8; ++l) lane_sums[l] += d * (float)acc[l];
+    const float dmin = gr_quant_fp16_to_f32(gr_le16(blk + 2)) * r->d;
+    return sum - dmin * (float)min_sum;
+}
+
+static void dot_q6_k_block(const uint8_t* blk, const q8k_block* r, float* lane_sums) {
+    const uint8_t* ql = blk;
+    const uint8_t* qh = blk + 128;
+    const int8_t* scales = (const int8_t*)(blk + 192);
+    const float d = gr_quant_fp16_to_f32(gr_le16(blk + 208));
+    int8_t dec[256];
+    for (int c = 0; c < 2; ++c)
+        for (int i = 0; i < 32; ++i) {
+            const uint8_t high = qh[c * 32 + i];
+            dec[c * 128 + i] = (int8_t)(((ql[c * 64 + i] & 0x0f) | ((high & 3) << 4)) - 32);
+            dec[c * 128 + i + 32] = (int8_t)(((ql[c * 64 + i + 32] & 0x0f) | (((high >> 2) & 3) << 4)) - 32);
+            dec[c * 128 + i + 64] = (int8_t)((((ql[c * 64 + i] >> 4) & 0x0f) | (((high >> 4) & 3) << 4)) - 32);
+            dec[c * 128 + i + 96] = (int8_t)((((ql[c * 64 + i + 32] >> 4) & 0x0f) | (((high >> 6) & 3) << 4)) - 32);
+        }
+    int32_t sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int g = 0; g < 16; ++g) {
+        const int32_t scale = scales[g];
+        for (int l = 0; l < 16; ++l) sums[l % 8] += scale * (int32_t)dec[g * 16 + l] * (int32_t)r->qs[g * 16 + l];
+    }
+    const float sc = r->d * d;
+    for (int l = 0; l < 8; ++l) lane_sums[l] += sc * (float)sums[l];
+}
+
+static int oracle_argmax_k(int code, const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
+                           int32_t* index_out) {
+    const uint64_t bb = code == 12 ? 144 : 210;
+    if (!gr_packed_view_valid(lhs, (uint32_t)code, 256, bb) || lhs->ne[0] / 256 > 128 ||
+        !validate_as(rhs, DT_F32, 0, NULL) || !validate_as(dst, DT_F32, 0, NULL) || !dense_contiguous_f32(rhs) ||
+        !dense_contiguous_f32(dst))
+        return ORACLE_INVALID_VIEW;
+    const uint64_t* l = lhs->ne;
+    const uint64_t* r = rhs->ne;
+    const uint64_t* d = dst->ne;
+    if (!(l[0] > 0 && l[1] > 0 && l[2] == 1 && l[3] == 1 && r[0] == 1 && r[1] == l[0] && r[2] == 1 && r[3] == 1 &&
+          d[0] == 1 && d[1] == 1 && d[2] == 1 && d[3] == 1))
+        return ORACLE_SHAPE_MISMATCH;
+    const uint64_t blocks = l[0] / 256, rows = l[1], row_bytes = blocks * bb;
+    static q8k_block q8[128];
+    q8k_quantize((const float*)rhs->data, blocks, q8);
+    const uint8_t* base = (const uint8_t*)lhs->data;
+    float best = -INFINITY;
+    int32_t best_index = 0;
+    for (uint64_t row = 0; row < rows; ++row) {
+        const uint8_t* rp = base + row * row_bytes;
+        float lane_sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        float sum = 0.0f;
+        for (uint64_t b = 0; b < blocks; ++b) {
+            if (code == 12)
+                sum = dot_q4_k_block(rp + b * bb, &q8[b], lane_sums, sum);
+            else
+                dot_q6_k_block(rp + b * bb, &q8[b], lane_sums);
+        }
+        for (int k = 0; k < 8; ++k) sum += lane_sums[k];
+        if (sum > best || row == 0) {
+            best = sum;
+            best_index = (int32_t)row;
+        }
+    }
+    *(float*)dst->data = best;
+    if (index_out) *index_out = best_index;
+    return ORACLE_OK;
+}
+
+int oracle_mul_mat_argmax_q4_k(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
+                               int32_t* index_out) {
+    return oracle_argmax_k(12, lhs, rhs, dst, index_out);
+}
+
+int oracle_mul_mat_argmax_q6_k(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
+                               int32_t* index_out) {
+    return oracle_argmax_k(14, lhs, rhs, dst, index_out);
+}
+
 /* ---------------------------------------------------------------------- */
 /* Single-query attention: flash_attn.rs OpFlashAttnExt                    */
 /* ---------------------------------------------------------------------- */

@@ -82,6 +82,12 @@ int oracle_mul_mat_argmax_q4_1(const oracle_view* lhs, const oracle_view* rhs, c
                                int32_t* index_out);
 int oracle_mul_mat_argmax_q5_0(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
                                int32_t* index_out);
+/* K-quant rows (matmul.rs OpMulMatArgmaxQ4K / Q6K): 256-value blocks of 144 /
+ * 210 bytes, k / 256 <= 128 blocks; the rhs is quantized to Q8_K. */
+int oracle_mul_mat_argmax_q4_k(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
+                               int32_t* index_out);
+int oracle_mul_mat_argmax_q6_k(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
+                               int32_t* index_out);
 /* diag.rs OpDiag / OpDiagMaskInf (mode 0) / OpDiagMaskZero (mode 1) over flat
  * f32 slices. */
 int oracle_diag(const float* input, uint64_t input_len, float* output, uint64_t output_len);

@@ -246,3 +246,66 @@ def test_packed_parity(emel, kern, oracle_lib, code, k, rows):
     st, sync, ost, gv, gi, ov, oi = run_packed_both(emel, kern, oracle_lib, code, blob, rhs, k, rows)
     assert st == 0 and sync == 0 and ost == 0
     assert gi == oi and np.array([gv]).view(np.uint32)[0] == np.array([ov]).view(np.uint32)[0]
+
+
+# ---- Q4_K rows (matmul.rs OpMulMatArgmaxQ4K) -----------------------------------
+
+def q4k_rows(rng, k, rows, planted=None):
+    blocks = k // 256
+    blob = rng.integers(0, 256, size=(rows, blocks, 144), dtype=np.uint8)
+    d = rng.uniform(0.5, 1.0, size=(rows, blocks, 2)) * 2.0 ** -8
+    blob[:, :, :4] = d.astype(np.float16).view(np.uint8).reshape(rows, blocks, 4)
+    if planted is not None:
+        blob[planted, :, :2] = np.array([0.02], np.float16).view(np.uint8)
+    return blob.reshape(-1)
+
+
+def run_q4k_both(emel, kern, olib, blob, rhs, k, rows):
+    ctx = kern.ctx
+    rb = k // 256 * 144
+    bl, br = emel.DeviceBuffer(ctx, blob.nbytes + 16), emel.DeviceBuffer(ctx, rhs.nbytes)
+    bd, bi = emel.DeviceBuffer(ctx, 16), emel.DeviceBuffer(ctx, 16)
+    bl.upload(blob)
+    br.upload(rhs)
+    v = emel.CView()
+    v.data, v.storage_bytes, v.dtype = bl.ptr, blob.nbytes, 12
+    for dim, (n, s) in enumerate(zip([k, rows, 1, 1], [1, rb, rb * rows, rb * rows])):
+        v.ne[dim], v.nb[dim] = n, s
+    st = emel.lib().emel_cuda_mul_mat_argmax_q4_k(ctx.handle, None, B(v), B(cview(emel, br, rhs.nbytes, [1, k, 1, 1])),
+                                                  B(cview(emel, bd, 4, [1, 1, 1, 1])), ctypes.c_void_p(bi.ptr))
+    sync = emel.lib().emel_cuda_stream_synchronize(ctx.handle, None)
+    got_v = bd.download(np.empty(4, np.float32))[0]
+    got_i = int(bi.download(np.empty(4, np.int32))[0])
+    out = np.full(1, 9.0, np.float32)
+    idx = ctypes.c_int32()
+    ost = olib.oracle_mul_mat_argmax_q4_k(
+        B(oracle.make_view(blob.ctypes.data, blob.nbytes, [k, rows, 1, 1], [1, rb, rb * rows, rb * rows], 12)),
+        B(oracle.make_view(rhs.ctypes.data, rhs.nbytes, [1, k, 1, 1], nb_of([1, k, 1, 1]), 0)),
+        B(oracle.make_view(out.ctypes.data, out.nbytes, [1, 1, 1, 1], nb_of([1, 1, 1, 1]), 0)), B(idx))
+    for b in (bl, br, bd, bi):
+        b.free()
+    return int(st), int(sync), ost, np.float32(got_v), got_i, out[0], idx.value
+
+
+def test_q4_k_reference_golden_vector(emel, kern, oracle_lib):
+    # snapshots/parity/kernel-argmax-parity/manifest.txt case=q4_k_success
+    blob = np.zeros(288, np.uint8)
+    blob[144:146] = (0x00, 0x3C)
+    blob[148:160] = 1
+    blob[160:] = 0xFF
+    st, sync, ost, gv, gi, ov, oi = run_q4k_both(emel, kern, oracle_lib, blob, np.ones(256, np.float32), 256, 2)
+    assert st == 0 and sync == 0 and gi == 1 and int(np.array([gv]).view(np.uint32)[0]) == 0x45700000
+
+
+@pytest.mark.parametrize("k,rows", [(256, 1), (256, 33), (512, 100), (4096, 3000), (32768, 40), (4352, 65)])
+def test_q4_k_parity(emel, kern, oracle_lib, k, rows):
+    rng = np.random.default_rng(k + 7 * rows)
+    planted = int(rng.integers(0, rows))
+    blob = q4k_rows(rng, k, rows, planted)
+    rhs = rng.standard_normal(k).astype(np.float32)
+    rhs[5] = -abs(rhs[5]) - 10.0  # a negative maximum magnitude in block 0
+    if k >= 512:
+        rhs[256:512] = 0.0  # a zero block
+    st, sync, ost, gv, gi, ov, oi = run_q4k_both(emel, kern, oracle_lib, blob, rhs, k, rows)
+    assert st == 0 and sync == 0 and ost == 0
+    assert gi == oi and np.array([gv]).view(np.uint32)[0] == np.array([ov]).view(np.uint32)[0]

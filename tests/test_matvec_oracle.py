@@ -231,3 +231,47 @@ def test_q4_q5_decoding_matches_float_dot(lib):
                                                                             for i in range(16))
         st, out, idx = run_packed(lib, code, blk, 32, 1, x)
         assert st == 0 and out[0] == np.float32(np.dot(w.astype(np.float64), x.astype(np.float64))), code
+
+
+# ---- K-quant rows (matmul.rs OpMulMatArgmaxQ4K / Q6K) -------------------------
+
+K_BYTES = {12: 144, 14: 210}
+K_FN = {12: "oracle_mul_mat_argmax_q4_k", 14: "oracle_mul_mat_argmax_q6_k"}
+
+
+def run_k(lib, code, lhs_bytes, k, rows, rhs):
+    lhs = np.frombuffer(bytes(lhs_bytes), np.uint8).copy()
+    rhs = np.asarray(rhs, np.float32)
+    out = np.full(1, np.float32(np.uint32(0x7FC01234).view(np.float32)), np.float32)
+    idx = ctypes.c_int32(-7)
+    rb = k // 256 * K_BYTES[code]
+    st = getattr(lib, K_FN[code])(
+        B(oracle.make_view(lhs.ctypes.data, lhs.nbytes, [k, rows, 1, 1], [1, rb, rb * rows, rb * rows], code)),
+        B(oracle.make_view(rhs.ctypes.data, rhs.nbytes, [1, k, 1, 1], nb_of([1, k, 1, 1]), 0)),
+        B(oracle.make_view(out.ctypes.data, out.nbytes, [1, 1, 1, 1], nb_of([1, 1, 1, 1]), 0)), B(idx))
+    return st, out, idx.value
+
+
+def test_k_quant_reference_golden_vectors(lib):
+    # snapshots/parity/kernel-argmax-parity/manifest.txt: q4_k_success index=1
+    # bits 45700000, q6_k_success index=1 bits 45f80000; inputs from
+    # tools/emel-kernel-argmax-parity/src/main.rs:82-98 and 114-127
+    q4 = bytearray(288)
+    q4[144:146] = bytes([0x00, 0x3C])
+    q4[148:160] = bytes([1]) * 12
+    q4[160:] = bytes([0xFF]) * 128
+    st, out, idx = run_k(lib, 12, q4, 256, 2, np.ones(256))
+    assert st == 0 and idx == 1 and int(out.view(np.uint32)[0]) == 0x45700000
+    q6 = bytearray(420)
+    q6[210:338] = bytes([0xFF]) * 128
+    q6[338:402] = bytes([0xFF]) * 64
+    q6[402:418] = bytes([1]) * 16
+    q6[418:420] = bytes([0x00, 0x3C])
+    st, out, idx = run_k(lib, 14, q6, 256, 2, np.ones(256))
+    assert st == 0 and idx == 1 and int(out.view(np.uint32)[0]) == 0x45F80000
+
+
+def test_k_quant_guards(lib):
+    blk = bytes(144)
+    assert run_k(lib, 12, blk, 256, 1, np.ones(255))[0] in (1, 2)
+    assert run_k(lib, 12, blk * 129, 256 * 129, 1, np.ones(256 * 129))[0] == 1   # 129 blocks > 128
