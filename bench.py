@@ -493,7 +493,9 @@ def run_suite(args):
                  "cfg5": ["repeat_mul_permuted", "repeat_add_permuted", "sum_whole_permuted",
                           "argmax_whole_permuted", "cont_permuted"],
                  "glu": list(W.GLU_OPS), "get_rows": [f"get_rows_{f}" for f in W.EMB_FORMATS],
-                 "rope": ["rope_neox", "rope_norm"], "matvec": ["mul_mat_argmax_vocab", "mul_mat_argmax_q8_0_vocab"],
+                 "rope": ["rope_neox", "rope_norm"],
+                 "matvec": ["mul_mat_argmax_vocab", "mul_mat_argmax_q8_0_vocab", "mul_mat_argmax_q4_k_vocab",
+                            "mul_mat_argmax_q6_k_vocab"],
                  "attention": [o.name for o in W.fa_spec().ops], "diag": [o.name for o in W.diag_spec().ops]}
 
     def wants(*keys):
@@ -696,6 +698,23 @@ def run_suite(args):
         measure("matvec", o.name, o.bytes, o.elements,
                 lambda k: (lambda: chk(lib.emel_cuda_mul_mat_argmax_q8_0(ctx.handle, sh, B(vq), B(vr), B(vv),
                                                                          ctypes.c_void_p(ti.data_ptr())))), 1)
+        del tq, tr
+    for fmt, code in (("q4_k", 12), ("q6_k", 14)):
+        o = W.mvk_spec(fmt)
+        if only and "matvec" not in only and o.name not in only:
+            continue
+        blob, rv = W.mvk_inputs(fmt)
+        tq, tr = torch.from_numpy(blob).to(dev), torch.from_numpy(rv).to(dev)
+        del blob
+        tv = torch.empty(1, device=dev)
+        ti = torch.empty(1, dtype=torch.int32, device=dev)
+        rb = W.MV_K // 256 * W.K_BLOCK_BYTES[fmt]
+        vq = view(tq, [W.MV_K, W.MV_ROWS, 1, 1], [1, rb, rb * W.MV_ROWS, rb * W.MV_ROWS], code=code)
+        vr, vv = view(tr, [1, W.MV_K, 1, 1]), view(tv, [1, 1, 1, 1])
+        fn = getattr(lib, f"emel_cuda_mul_mat_argmax_{fmt}")
+        measure("matvec", o.name, o.bytes, o.elements,
+                lambda k, fn=fn, vq=vq, vr=vr, vv=vv, ti=ti: (lambda: chk(fn(ctx.handle, sh, B(vq), B(vr), B(vv),
+                                                                           ctypes.c_void_p(ti.data_ptr())))), 1)
         del tq, tr
     # causal masks (diag.rs OpDiagMaskInf / OpDiagMaskZero) over a score matrix
     if wants("diag",):

@@ -200,6 +200,7 @@ SIGNATURES = {
     "emel_cuda_mul_mat_argmax_q4_1": (_I, [_CTX, _V, _P, _P, _P, _V]),
     "emel_cuda_mul_mat_argmax_q5_0": (_I, [_CTX, _V, _P, _P, _P, _V]),
     "emel_cuda_mul_mat_argmax_q4_k": (_I, [_CTX, _V, _P, _P, _P, _V]),
+    "emel_cuda_mul_mat_argmax_q6_k": (_I, [_CTX, _V, _P, _P, _P, _V]),
     "emel_cuda_rope": (_I, [_CTX, _V, _P, _P, _P, ctypes.POINTER(CRopeParams)]),
     "emel_cuda_diag": (_I, [_CTX, _V, _V, ctypes.c_uint64, _V, ctypes.c_uint64]),
     "emel_cuda_diag_mask": (_I, [_CTX, _V, _I, _V, ctypes.c_uint64, _V, ctypes.c_uint64, ctypes.c_int32]),
@@ -788,6 +789,7 @@ OpMulMatArgmaxQ4_0 = _packed_argmax("q4_0", "matmul::OpMulMatArgmaxQ4_0 (matmul.
 OpMulMatArgmaxQ4_1 = _packed_argmax("q4_1", "matmul::OpMulMatArgmaxQ4_1 (matmul.rs:500-510): Q4_1 rows.")
 OpMulMatArgmaxQ5_0 = _packed_argmax("q5_0", "matmul::OpMulMatArgmaxQ5_0 (matmul.rs:510-516): Q5_0 rows.")
 OpMulMatArgmaxQ4K = _packed_argmax("q4_k", "matmul::OpMulMatArgmaxQ4K (matmul.rs:530-535): Q4_K rows.")
+OpMulMatArgmaxQ6K = _packed_argmax("q6_k", "matmul::OpMulMatArgmaxQ6K (matmul.rs:536-540): Q6_K rows.")
 
 
 @dataclass

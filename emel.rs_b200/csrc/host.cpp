@@ -1307,15 +1307,15 @@ emel_cuda_status emel_cuda_mul_mat_argmax_q5_0(emel_cuda_context* ctx, void* str
     return mul_mat_argmax_packed(ctx, stream, lhs, rhs, dst, index_out, EMEL_DTYPE_Q5_0, 22);
 }
 
-emel_cuda_status emel_cuda_mul_mat_argmax_q4_k(emel_cuda_context* ctx, void* stream, const emel_tensor_view* lhs,
-                                               const emel_tensor_view* rhs, const emel_tensor_view* dst,
-                                               int32_t* index_out) {
+static emel_cuda_status mul_mat_argmax_k(emel_cuda_context* ctx, void* stream, const emel_tensor_view* lhs,
+                                         const emel_tensor_view* rhs, const emel_tensor_view* dst, int32_t* index_out,
+                                         uint32_t code, uint64_t block_bytes) {
     Checked cr, cd;
     uint64_t row_bytes = 0;
-    // quantized_views_valid (matmul.rs:1522-1542): Q4_K packed rows of at
-    // most 128 blocks of 256 values, dense F32 rhs and destination
+    // quantized_views_valid (matmul.rs:1522-1542): K-quant rows of at most
+    // 128 blocks of 256 values, dense F32 rhs and destination
     if (lhs == nullptr || rhs == nullptr || dst == nullptr ||
-        !gr_packed_view_valid(lhs, EMEL_DTYPE_Q4_K, 256, 144, &row_bytes) || lhs->ne[0] / 256 > 128 ||
+        !gr_packed_view_valid(lhs, code, 256, block_bytes, &row_bytes) || lhs->ne[0] / 256 > 128 ||
         !validate_as(rhs, EMEL_DTYPE_F32, false, &cr) || !validate_as(dst, EMEL_DTYPE_F32, false, &cd) ||
         !dense_contiguous_f32(rhs) || !dense_contiguous_f32(dst))
         return EMEL_CUDA_INVALID_VIEW;
@@ -1342,8 +1342,20 @@ emel_cuda_status emel_cuda_mul_mat_argmax_q4_k(emel_cuda_context* ctx, void* str
     p.fault = reinterpret_cast<uint32_t*>(ws + emel::kFaultWordOffset);
     cudaError_t err = select_device(ctx);
     if (err == cudaSuccess)
-        err = emel::launch_mul_mat_argmax_q4_k(env_of(ctx, stream), p, static_cast<const uint8_t*>(lhs->data));
+        err = emel::launch_mul_mat_argmax_k(env_of(ctx, stream), p, static_cast<const uint8_t*>(lhs->data), (int)code);
     return device_status(ctx, err);
+}
+
+emel_cuda_status emel_cuda_mul_mat_argmax_q4_k(emel_cuda_context* ctx, void* stream, const emel_tensor_view* lhs,
+                                               const emel_tensor_view* rhs, const emel_tensor_view* dst,
+                                               int32_t* index_out) {
+    return mul_mat_argmax_k(ctx, stream, lhs, rhs, dst, index_out, EMEL_DTYPE_Q4_K, 144);
+}
+
+emel_cuda_status emel_cuda_mul_mat_argmax_q6_k(emel_cuda_context* ctx, void* stream, const emel_tensor_view* lhs,
+                                               const emel_tensor_view* rhs, const emel_tensor_view* dst,
+                                               int32_t* index_out) {
+    return mul_mat_argmax_k(ctx, stream, lhs, rhs, dst, index_out, EMEL_DTYPE_Q6_K, 210);
 }
 
 // ---- single-query attention -------------------------------------------------

@@ -246,6 +246,8 @@ template <>
 struct PackedFmt<kDtypeQ5_0> { static constexpr int kBytes = 22; };
 template <>
 struct PackedFmt<kDtypeQ8_0> { static constexpr int kBytes = 34; };
+template <>
+struct PackedFmt<kDtypeQ6_K> { static constexpr int kBytes = 210; };
 
 // byte i of a nibble bit pattern (4 bits) moved to bit 4 of byte i
 __device__ __forceinline__ uint32_t q5_spread(uint32_t b4) {
@@ -463,7 +465,87 @@ __device__ __forceinline__ int32_t q8k_nearest(float v) {
     return (int32_t)(__float_as_uint(__fadd_rn(v, 12582912.0f)) & 0x007fffffu) - 0x00400000;
 }
 
-__global__ void __launch_bounds__(kKThreads) mv_argmax_q4_k(MvArgmaxPlan p, const uint8_t* lhs) {
+// Q4_K term: eight lane terms d * float(acc[j]) and the minimum term.
+__device__ __forceinline__ void q4k_block_terms(const uint32_t* w, const uint32_t* r4, const int* bs, float rdb,
+                                                float* o) {
+    uint32_t W[36];
+#pragma unroll
+    for (int i = 0; i < 36; ++i) W[i] = __ldg(w + i);
+    // scales / minimums (dot_q4_k's unpacking)
+    const uint32_t s0 = W[1], s1 = W[2], s2 = W[3];
+    uint32_t sc[8], mn[8];
+#pragma unroll
+    for (int l = 0; l < 4; ++l) {
+        const uint32_t a = (s0 >> (8 * l)) & 0xffu, bb = (s1 >> (8 * l)) & 0xffu, c = (s2 >> (8 * l)) & 0xffu;
+        sc[l] = a & 0x3fu;
+        sc[4 + l] = (c & 0x0fu) | ((a >> 6) << 4);
+        mn[l] = bb & 0x3fu;
+        mn[4 + l] = (c >> 4) | ((bb >> 6) << 4);
+    }
+    int min_sum = 0;
+#pragma unroll
+    for (int h = 0; h < 16; ++h) min_sum += bs[h] * (int)mn[h >> 1];
+    int acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+    for (int gg = 0; gg < 8; ++gg) {
+        const int h = gg >> 1;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int k0 = 4 + 8 * h + (j >> 2), bt = j & 3;
+            const uint32_t sel = (uint32_t)bt | ((uint32_t)(bt + 4) << 4);
+            const uint32_t lo = __byte_perm(W[k0], W[k0 + 2], sel);
+            const uint32_t hi = __byte_perm(W[k0 + 4], W[k0 + 6], sel);
+            uint32_t v = __byte_perm(lo, hi, 0x5410);
+            v = (gg & 1) ? ((v >> 4) & 0x0f0f0f0fu) : (v & 0x0f0f0f0fu);
+            acc[j] += (int)sc[gg] * __dp4a((int)v, (int)r4[gg * 8 + j], 0);
+        }
+    }
+    const float dd = __fmul_rn(f16_bits_to_f32((uint16_t)(W[0] & 0xffffu)), rdb);
+    const float dm = __fmul_rn(f16_bits_to_f32((uint16_t)(W[0] >> 16)), rdb);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = __fmul_rn(dd, (float)acc[j]);
+    o[8] = __fmul_rn(dm, (float)min_sum);
+}
+
+// Q6_K term (dot_q6_k, matmul.rs:2117-2190): eight lane terms
+// (d_rhs * d) * float(sums[j]); decoded 4 values at a time with byte-SIMD
+// ops, and each lane sum's two positions of a 16-value group paired for dp4a.
+__device__ __forceinline__ void q6k_block_terms(const uint8_t* blk_ptr, const uint32_t* r4, float rdb, float* o) {
+    PackedBlock<kDtypeQ6_K> blk;
+    blk.load(blk_ptr);
+    int sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+    for (int g = 0; g < 16; ++g) {
+        const int c = g >> 3, sgrp = (g & 7) >> 1, i0 = 16 * (g & 1);
+        const int scale = (int)(int8_t)((blk.word(48 + (g >> 2)) >> (8 * (g & 3))) & 0xffu);
+        uint32_t D[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const int i = i0 + 4 * k;
+            const uint32_t ql = blk.word(c * 16 + ((sgrp & 1) ? 8 : 0) + (i >> 2));
+            const uint32_t nib = (sgrp < 2) ? (ql & 0x0f0f0f0fu) : ((ql >> 4) & 0x0f0f0f0fu);
+            const uint32_t qh = blk.word(32 + c * 8 + (i >> 2));
+            const uint32_t hb = ((qh >> (2 * sgrp)) & 0x03030303u) << 4;
+            D[k] = __vsub4(nib | hb, 0x20202020u);
+        }
+        const uint32_t* R = r4 + 4 * g;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int a = j < 4 ? 0 : 1, bt = j & 3;
+            const uint32_t sel = (uint32_t)bt | ((uint32_t)(bt + 4) << 4);
+            const uint32_t x = __byte_perm(D[a], D[a + 2], sel) & 0xffffu;
+            const uint32_t y = __byte_perm(R[a], R[a + 2], sel);
+            sums[j] += scale * __dp4a((int)x, (int)y, 0);
+        }
+    }
+    const float sc = __fmul_rn(rdb, f16_bits_to_f32((uint16_t)(blk.word(52) & 0xffffu)));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = __fmul_rn(sc, (float)sums[j]);
+    o[8] = 0.0f;
+}
+
+template <int CODE>
+__global__ void __launch_bounds__(kKThreads) mv_argmax_k(MvArgmaxPlan p, const uint8_t* lhs) {
     extern __shared__ __align__(16) uint32_t k_smem[];
     __shared__ MvPart warp_best[kKWarps];
     const uint32_t blocks = (uint32_t)(p.k / 256);
@@ -513,11 +595,17 @@ __global__ void __launch_bounds__(kKThreads) mv_argmax_q4_k(MvArgmaxPlan p, cons
                 q[i] = (int8_t)(v < 127 ? v : 127);
             }
         }
-        // position 8 * lane + i = 32 g + 8 t + jj: group g = lane / 4, t = lane % 4
-        const int g = lane >> 2, t = lane & 3;
-        int8_t* words = reinterpret_cast<int8_t*>(rq + b * 64 + g * 8);
+        if constexpr (CODE == kDtypeQ4_K) {
+            // position 8 * lane + i = 32 g + 8 t + i: group g = lane / 4, t = lane % 4
+            const int g = lane >> 2, t = lane & 3;
+            int8_t* words = reinterpret_cast<int8_t*>(rq + b * 64 + g * 8);
 #pragma unroll
-        for (int i = 0; i < 8; ++i) words[i * 4 + t] = q[i];
+            for (int i = 0; i < 8; ++i) words[i * 4 + t] = q[i];
+        } else {
+            int8_t* bytes = reinterpret_cast<int8_t*>(rq + b * 64);  // natural order
+#pragma unroll
+            for (int i = 0; i < 8; ++i) bytes[lane * 8 + i] = q[i];
+        }
         int gsum = 0;
 #pragma unroll
         for (int i = 0; i < 8; ++i) gsum += q[i];
@@ -526,7 +614,8 @@ __global__ void __launch_bounds__(kKThreads) mv_argmax_q4_k(MvArgmaxPlan p, cons
         if (lane == 0) rd[b] = d;
     }
     __syncthreads();
-    const uint64_t row_bytes = (uint64_t)blocks * 144;
+    constexpr uint64_t BB = CODE == kDtypeQ4_K ? 144 : 210;
+    const uint64_t row_bytes = (uint64_t)blocks * BB;
     MvPart best{0.0f, 0, 0u, 0u};
     for (uint64_t g0 = ((uint64_t)blockIdx.x * kKWarps + warp) * 32; g0 < p.rows;
          g0 += (uint64_t)gridDim.x * kKWarps * 32) {
@@ -537,46 +626,12 @@ __global__ void __launch_bounds__(kKThreads) mv_argmax_q4_k(MvArgmaxPlan p, cons
             const uint32_t nbc = blocks - b0 < (uint32_t)kKChunk ? blocks - b0 : (uint32_t)kKChunk;
             for (uint32_t item = lane; item < nrows * nbc; item += 32) {
                 const uint32_t r = item / nbc, bl = item % nbc, b = b0 + bl;
-                const uint32_t* w = reinterpret_cast<const uint32_t*>(lhs + (g0 + r) * row_bytes + (uint64_t)b * 144);
-                uint32_t W[36];
-#pragma unroll
-                for (int i = 0; i < 36; ++i) W[i] = __ldg(w + i);
-                // scales / minimums (dot_q4_k's unpacking)
-                const uint32_t s0 = W[1], s1 = W[2], s2 = W[3];
-                uint32_t sc[8], mn[8];
-#pragma unroll
-                for (int l = 0; l < 4; ++l) {
-                    const uint32_t a = (s0 >> (8 * l)) & 0xffu, bb = (s1 >> (8 * l)) & 0xffu, c = (s2 >> (8 * l)) & 0xffu;
-                    sc[l] = a & 0x3fu;
-                    sc[4 + l] = (c & 0x0fu) | ((a >> 6) << 4);
-                    mn[l] = bb & 0x3fu;
-                    mn[4 + l] = (c >> 4) | ((bb >> 6) << 4);
-                }
-                int min_sum = 0;
-#pragma unroll
-                for (int h = 0; h < 16; ++h) min_sum += rb[b * 16 + h] * (int)mn[h >> 1];
-                int acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-                const uint32_t* r4 = rq + b * 64;
-#pragma unroll
-                for (int gg = 0; gg < 8; ++gg) {
-                    const int h = gg >> 1;
-#pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const int k0 = 4 + 8 * h + (j >> 2), bt = j & 3;
-                        const uint32_t sel = (uint32_t)bt | ((uint32_t)(bt + 4) << 4);
-                        const uint32_t lo = __byte_perm(W[k0], W[k0 + 2], sel);
-                        const uint32_t hi = __byte_perm(W[k0 + 4], W[k0 + 6], sel);
-                        uint32_t v = __byte_perm(lo, hi, 0x5410);
-                        v = (gg & 1) ? ((v >> 4) & 0x0f0f0f0fu) : (v & 0x0f0f0f0fu);
-                        acc[j] += (int)sc[gg] * __dp4a((int)v, (int)r4[gg * 8 + j], 0);
-                    }
-                }
-                const float dd = __fmul_rn(f16_bits_to_f32((uint16_t)(W[0] & 0xffffu)), rd[b]);
-                const float dm = __fmul_rn(f16_bits_to_f32((uint16_t)(W[0] >> 16)), rd[b]);
+                const uint8_t* bp = lhs + (g0 + r) * row_bytes + (uint64_t)b * BB;
                 float* o = tile + r * kKRowStride + bl * kKTerms;
-#pragma unroll
-                for (int j = 0; j < 8; ++j) o[j] = __fmul_rn(dd, (float)acc[j]);
-                o[8] = __fmul_rn(dm, (float)min_sum);
+                if constexpr (CODE == kDtypeQ4_K)
+                    q4k_block_terms(reinterpret_cast<const uint32_t*>(bp), rq + b * 64, rb + b * 16, rd[b], o);
+                else
+                    q6k_block_terms(bp, rq + b * 64, rd[b], o);
             }
             __syncwarp();
             if ((uint32_t)lane < nrows) {
@@ -584,7 +639,7 @@ __global__ void __launch_bounds__(kKThreads) mv_argmax_q4_k(MvArgmaxPlan p, cons
                 for (uint32_t bl = 0; bl < nbc; ++bl) {
 #pragma unroll
                     for (int j = 0; j < 8; ++j) ls[j] = __fadd_rn(ls[j], t[bl * kKTerms + j]);
-                    total = __fsub_rn(total, t[bl * kKTerms + 8]);
+                    if constexpr (CODE == kDtypeQ4_K) total = __fsub_rn(total, t[bl * kKTerms + 8]);
                 }
             }
             __syncwarp();
@@ -678,7 +733,8 @@ cudaError_t launch_mul_mat_argmax(const LaunchEnv& env, const MvArgmaxPlan& p) {
     return err != cudaSuccess ? err : cudaGetLastError();
 }
 
-cudaError_t launch_mul_mat_argmax_q4_k(const LaunchEnv& env, const MvArgmaxPlan& p, const uint8_t* lhs) {
+template <int CODE>
+cudaError_t launch_k(const LaunchEnv& env, const MvArgmaxPlan& p, const uint8_t* lhs) {
     const uint64_t groups = (p.rows + kKWarps * 32 - 1) / (kKWarps * 32);
     const uint64_t cap = (uint64_t)env.sm_count * 3;
     const size_t table = (size_t)kKWarps * 32 * kKRowStride * 4;
@@ -686,15 +742,19 @@ cudaError_t launch_mul_mat_argmax_q4_k(const LaunchEnv& env, const MvArgmaxPlan&
     static int configured_device_mask = 0;
     const int bit = env.device < 31 ? (1 << env.device) : 0;
     if (!(configured_device_mask & bit)) {
-        const cudaError_t e = cudaFuncSetAttribute(mv_argmax_q4_k, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        const cudaError_t e = cudaFuncSetAttribute(mv_argmax_k<CODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    (int)(128 * (64 * 4 + 4 + 16 * 4) + table));
         if (e != cudaSuccess) return e;
         configured_device_mask |= bit;
     }
-    const cudaError_t err = launch_dependent(mv_argmax_q4_k, dim3((unsigned)(groups < cap ? groups : cap)),
+    const cudaError_t err = launch_dependent(mv_argmax_k<CODE>, dim3((unsigned)(groups < cap ? groups : cap)),
                                              dim3(kKThreads), smem, env.stream, p, lhs);
     ++*env.launches;
     return err != cudaSuccess ? err : cudaGetLastError();
+}
+
+cudaError_t launch_mul_mat_argmax_k(const LaunchEnv& env, const MvArgmaxPlan& p, const uint8_t* lhs, int code) {
+    return code == kDtypeQ4_K ? launch_k<kDtypeQ4_K>(env, p, lhs) : launch_k<kDtypeQ6_K>(env, p, lhs);
 }
 
 cudaError_t launch_mul_mat_argmax_packed(const LaunchEnv& env, const MvArgmaxPlan& p, const uint8_t* lhs, int code) {

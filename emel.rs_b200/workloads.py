@@ -348,3 +348,29 @@ def mvq8_spec():
     row_bytes = MV_K // 32 * 34
     return Config("matvec", [OpSpec("mul_mat_argmax_q8_0_vocab", MV_ROWS * row_bytes + MV_K * F32 + 8,
                                     MV_K * MV_ROWS)])
+
+
+# The vocabulary step with K-quant rows (matmul.rs OpMulMatArgmaxQ4K / Q6K):
+# [4096, 151936] as 16 blocks of 256 values per row, random block bytes with
+# binary16 scales 2^-10 * U(0.5, 1) (Q6_K: signed group scales in [-64, 64)).
+K_BLOCK_BYTES = {"q4_k": 144, "q6_k": 210}
+
+
+def mvk_inputs(fmt, seed=18):
+    rng = np.random.default_rng(seed)
+    blocks, bb = MV_K // 256, K_BLOCK_BYTES[fmt]
+    blob = rng.integers(0, 256, size=(MV_ROWS, blocks, bb), dtype=np.uint8)
+    if fmt == "q4_k":
+        d = (rng.uniform(0.5, 1.0, size=(MV_ROWS, blocks, 2)) / 1024.0).astype(np.float16)
+        blob[:, :, :4] = d.view(np.uint8).reshape(MV_ROWS, blocks, 4)
+    else:
+        blob[:, :, 192:208] = rng.integers(-64, 64, size=(MV_ROWS, blocks, 16), dtype=np.int8).view(np.uint8)
+        d = (rng.uniform(0.5, 1.0, size=(MV_ROWS, blocks)) / 1024.0).astype(np.float16)
+        blob[:, :, 208:210] = d.view(np.uint8).reshape(MV_ROWS, blocks, 2)
+    rhs = normal(rng, (MV_K,), 1.0).astype(np.float32)
+    return blob.reshape(-1), rhs
+
+
+def mvk_spec(fmt):
+    row_bytes = MV_K // 256 * K_BLOCK_BYTES[fmt]
+    return OpSpec(f"mul_mat_argmax_{fmt}_vocab", MV_ROWS * row_bytes + MV_K * F32 + 8, MV_K * MV_ROWS)

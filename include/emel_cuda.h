@@ -47,6 +47,7 @@ enum emel_cuda_dtype {
     EMEL_DTYPE_Q5_0 = 6,
     EMEL_DTYPE_Q8_0 = 8,
     EMEL_DTYPE_Q4_K = 12,
+    EMEL_DTYPE_Q6_K = 14,
     EMEL_DTYPE_I32 = 26,
     EMEL_DTYPE_I64 = 27,
     EMEL_DTYPE_F64 = 28,
@@ -515,6 +516,14 @@ EMEL_CUDA_API emel_cuda_status emel_cuda_mul_mat_argmax_q5_0(emel_cuda_context* 
  * to the total after its last block (dot_q4_k, matmul.rs:2040-2114).
  * Statuses and device additions as emel_cuda_mul_mat_argmax_q8_0. */
 EMEL_CUDA_API emel_cuda_status emel_cuda_mul_mat_argmax_q4_k(emel_cuda_context* ctx, void* stream,
+                                                             const emel_tensor_view* lhs, const emel_tensor_view* rhs,
+                                                             const emel_tensor_view* dst, int32_t* index_out);
+/* matmul::OpMulMatArgmaxQ6K (matmul.rs:536-540): the same with Q6_K rows
+ * (210-byte blocks: 128 bytes of low nibbles, 64 bytes of 2-bit highs, 16
+ * signed group scales, binary16 scale; value = (nibble | high << 4) - 32)
+ * and dot_q6_k's terms (matmul.rs:2117-2190): eight lane sums of
+ * (d_rhs * d) * float(scaled integer dots), no minimum term. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_mul_mat_argmax_q6_k(emel_cuda_context* ctx, void* stream,
                                                              const emel_tensor_view* lhs, const emel_tensor_view* rhs,
                                                              const emel_tensor_view* dst, int32_t* index_out);
 

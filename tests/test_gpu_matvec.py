@@ -260,26 +260,28 @@ def q4k_rows(rng, k, rows, planted=None):
     return blob.reshape(-1)
 
 
-def run_q4k_both(emel, kern, olib, blob, rhs, k, rows):
+def run_q4k_both(emel, kern, olib, blob, rhs, k, rows, code=12):
     ctx = kern.ctx
-    rb = k // 256 * 144
+    suffix, bb = {12: ("q4_k", 144), 14: ("q6_k", 210)}[code]
+    rb = k // 256 * bb
     bl, br = emel.DeviceBuffer(ctx, blob.nbytes + 16), emel.DeviceBuffer(ctx, rhs.nbytes)
     bd, bi = emel.DeviceBuffer(ctx, 16), emel.DeviceBuffer(ctx, 16)
     bl.upload(blob)
     br.upload(rhs)
     v = emel.CView()
-    v.data, v.storage_bytes, v.dtype = bl.ptr, blob.nbytes, 12
+    v.data, v.storage_bytes, v.dtype = bl.ptr, blob.nbytes, code
     for dim, (n, s) in enumerate(zip([k, rows, 1, 1], [1, rb, rb * rows, rb * rows])):
         v.ne[dim], v.nb[dim] = n, s
-    st = emel.lib().emel_cuda_mul_mat_argmax_q4_k(ctx.handle, None, B(v), B(cview(emel, br, rhs.nbytes, [1, k, 1, 1])),
-                                                  B(cview(emel, bd, 4, [1, 1, 1, 1])), ctypes.c_void_p(bi.ptr))
+    fn = getattr(emel.lib(), f"emel_cuda_mul_mat_argmax_{suffix}")
+    st = fn(ctx.handle, None, B(v), B(cview(emel, br, rhs.nbytes, [1, k, 1, 1])), B(cview(emel, bd, 4, [1, 1, 1, 1])),
+            ctypes.c_void_p(bi.ptr))
     sync = emel.lib().emel_cuda_stream_synchronize(ctx.handle, None)
     got_v = bd.download(np.empty(4, np.float32))[0]
     got_i = int(bi.download(np.empty(4, np.int32))[0])
     out = np.full(1, 9.0, np.float32)
     idx = ctypes.c_int32()
-    ost = olib.oracle_mul_mat_argmax_q4_k(
-        B(oracle.make_view(blob.ctypes.data, blob.nbytes, [k, rows, 1, 1], [1, rb, rb * rows, rb * rows], 12)),
+    ost = getattr(olib, f"oracle_mul_mat_argmax_{suffix}")(
+        B(oracle.make_view(blob.ctypes.data, blob.nbytes, [k, rows, 1, 1], [1, rb, rb * rows, rb * rows], code)),
         B(oracle.make_view(rhs.ctypes.data, rhs.nbytes, [1, k, 1, 1], nb_of([1, k, 1, 1]), 0)),
         B(oracle.make_view(out.ctypes.data, out.nbytes, [1, 1, 1, 1], nb_of([1, 1, 1, 1]), 0)), B(idx))
     for b in (bl, br, bd, bi):
@@ -307,5 +309,41 @@ def test_q4_k_parity(emel, kern, oracle_lib, k, rows):
     if k >= 512:
         rhs[256:512] = 0.0  # a zero block
     st, sync, ost, gv, gi, ov, oi = run_q4k_both(emel, kern, oracle_lib, blob, rhs, k, rows)
+    assert st == 0 and sync == 0 and ost == 0
+    assert gi == oi and np.array([gv]).view(np.uint32)[0] == np.array([ov]).view(np.uint32)[0]
+
+
+# ---- Q6_K rows (matmul.rs OpMulMatArgmaxQ6K) -----------------------------------
+
+def q6k_rows(rng, k, rows, planted=None):
+    blocks = k // 256
+    blob = rng.integers(0, 256, size=(rows, blocks, 210), dtype=np.uint8)
+    blob[:, :, 192:208] = rng.integers(-64, 64, size=(rows, blocks, 16), dtype=np.int8).view(np.uint8)
+    d = rng.uniform(0.5, 1.0, size=(rows, blocks)) * 2.0 ** -10
+    blob[:, :, 208:210] = d.astype(np.float16).view(np.uint8).reshape(rows, blocks, 2)
+    if planted is not None:
+        blob[planted, :, 208:210] = np.array([0.01], np.float16).view(np.uint8)
+        blob[planted, :, 192:208] = 60
+    return blob.reshape(-1)
+
+
+def test_q6_k_reference_golden_vector(emel, kern, oracle_lib):
+    # snapshots/parity/kernel-argmax-parity/manifest.txt case=q6_k_success
+    blob = np.zeros(420, np.uint8)
+    blob[210:338] = 0xFF
+    blob[338:402] = 0xFF
+    blob[402:418] = 1
+    blob[418:420] = (0x00, 0x3C)
+    st, sync, ost, gv, gi, ov, oi = run_q4k_both(emel, kern, oracle_lib, blob, np.ones(256, np.float32), 256, 2, 14)
+    assert st == 0 and sync == 0 and gi == 1 and int(np.array([gv]).view(np.uint32)[0]) == 0x45F80000
+
+
+@pytest.mark.parametrize("k,rows", [(256, 1), (256, 33), (512, 100), (4096, 3000), (32768, 40), (4352, 65)])
+def test_q6_k_parity(emel, kern, oracle_lib, k, rows):
+    rng = np.random.default_rng(k + 11 * rows)
+    planted = int(rng.integers(0, rows))
+    blob = q6k_rows(rng, k, rows, planted)
+    rhs = rng.standard_normal(k).astype(np.float32)
+    st, sync, ost, gv, gi, ov, oi = run_q4k_both(emel, kern, oracle_lib, blob, rhs, k, rows, 14)
     assert st == 0 and sync == 0 and ost == 0
     assert gi == oi and np.array([gv]).view(np.uint32)[0] == np.array([ov]).view(np.uint32)[0]
