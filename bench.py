@@ -494,8 +494,8 @@ def run_suite(args):
                           "argmax_whole_permuted", "cont_permuted"],
                  "glu": list(W.GLU_OPS), "get_rows": [f"get_rows_{f}" for f in W.EMB_FORMATS],
                  "rope": ["rope_neox", "rope_norm"],
-                 "matvec": ["mul_mat_argmax_vocab", "mul_mat_argmax_q8_0_vocab", "mul_mat_argmax_q4_k_vocab",
-                            "mul_mat_argmax_q6_k_vocab"],
+                 "matvec": ["mul_mat_argmax_vocab", "mul_mat_argmax_q8_0_vocab", "mul_mat_argmax_q2_k_vocab",
+                            "mul_mat_argmax_q3_k_vocab", "mul_mat_argmax_q4_k_vocab", "mul_mat_argmax_q6_k_vocab"],
                  "attention": [o.name for o in W.fa_spec().ops], "diag": [o.name for o in W.diag_spec().ops]}
 
     def wants(*keys):
@@ -699,7 +699,7 @@ def run_suite(args):
                 lambda k: (lambda: chk(lib.emel_cuda_mul_mat_argmax_q8_0(ctx.handle, sh, B(vq), B(vr), B(vv),
                                                                          ctypes.c_void_p(ti.data_ptr())))), 1)
         del tq, tr
-    for fmt, code in (("q4_k", 12), ("q6_k", 14)):
+    for fmt, code in (("q2_k", 10), ("q3_k", 11), ("q4_k", 12), ("q6_k", 14)):
         o = W.mvk_spec(fmt)
         if only and "matvec" not in only and o.name not in only:
             continue

@@ -201,6 +201,8 @@ SIGNATURES = {
     "emel_cuda_mul_mat_argmax_q5_0": (_I, [_CTX, _V, _P, _P, _P, _V]),
     "emel_cuda_mul_mat_argmax_q4_k": (_I, [_CTX, _V, _P, _P, _P, _V]),
     "emel_cuda_mul_mat_argmax_q6_k": (_I, [_CTX, _V, _P, _P, _P, _V]),
+    "emel_cuda_mul_mat_argmax_q2_k": (_I, [_CTX, _V, _P, _P, _P, _V]),
+    "emel_cuda_mul_mat_argmax_q3_k": (_I, [_CTX, _V, _P, _P, _P, _V]),
     "emel_cuda_rope": (_I, [_CTX, _V, _P, _P, _P, ctypes.POINTER(CRopeParams)]),
     "emel_cuda_diag": (_I, [_CTX, _V, _V, ctypes.c_uint64, _V, ctypes.c_uint64]),
     "emel_cuda_diag_mask": (_I, [_CTX, _V, _I, _V, ctypes.c_uint64, _V, ctypes.c_uint64, ctypes.c_int32]),
@@ -790,6 +792,8 @@ OpMulMatArgmaxQ4_1 = _packed_argmax("q4_1", "matmul::OpMulMatArgmaxQ4_1 (matmul.
 OpMulMatArgmaxQ5_0 = _packed_argmax("q5_0", "matmul::OpMulMatArgmaxQ5_0 (matmul.rs:510-516): Q5_0 rows.")
 OpMulMatArgmaxQ4K = _packed_argmax("q4_k", "matmul::OpMulMatArgmaxQ4K (matmul.rs:530-535): Q4_K rows.")
 OpMulMatArgmaxQ6K = _packed_argmax("q6_k", "matmul::OpMulMatArgmaxQ6K (matmul.rs:536-540): Q6_K rows.")
+OpMulMatArgmaxQ2K = _packed_argmax("q2_k", "matmul::OpMulMatArgmaxQ2K (matmul.rs:520-524): Q2_K rows.")
+OpMulMatArgmaxQ3K = _packed_argmax("q3_k", "matmul::OpMulMatArgmaxQ3K (matmul.rs:525-529): Q3_K rows.")
 
 
 @dataclass

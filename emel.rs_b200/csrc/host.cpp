@@ -1358,6 +1358,18 @@ emel_cuda_status emel_cuda_mul_mat_argmax_q6_k(emel_cuda_context* ctx, void* str
     return mul_mat_argmax_k(ctx, stream, lhs, rhs, dst, index_out, EMEL_DTYPE_Q6_K, 210);
 }
 
+emel_cuda_status emel_cuda_mul_mat_argmax_q2_k(emel_cuda_context* ctx, void* stream, const emel_tensor_view* lhs,
+                                               const emel_tensor_view* rhs, const emel_tensor_view* dst,
+                                               int32_t* index_out) {
+    return mul_mat_argmax_k(ctx, stream, lhs, rhs, dst, index_out, EMEL_DTYPE_Q2_K, 84);
+}
+
+emel_cuda_status emel_cuda_mul_mat_argmax_q3_k(emel_cuda_context* ctx, void* stream, const emel_tensor_view* lhs,
+                                               const emel_tensor_view* rhs, const emel_tensor_view* dst,
+                                               int32_t* index_out) {
+    return mul_mat_argmax_k(ctx, stream, lhs, rhs, dst, index_out, EMEL_DTYPE_Q3_K, 110);
+}
+
 // ---- single-query attention -------------------------------------------------
 
 // dense_f32_layout (flash_attn.rs:305-325): effective strides exactly row-major.

@@ -128,9 +128,10 @@ cudaError_t launch_mul_mat_argmax(const LaunchEnv& env, const MvArgmaxPlan& plan
 // 32 up to 32768; code: the lhs dtype code.
 constexpr int kDtypeQ4_0 = 2, kDtypeQ4_1 = 3, kDtypeQ5_0 = 6, kDtypeQ8_0 = 8;
 cudaError_t launch_mul_mat_argmax_packed(const LaunchEnv& env, const MvArgmaxPlan& plan, const uint8_t* lhs, int code);
-// K-quant rows: Q4_K (144-byte) or Q6_K (210-byte) blocks of 256 values,
-// 4-byte aligned base; plan.k a multiple of 256 up to 32768.
-constexpr int kDtypeQ4_K = 12, kDtypeQ6_K = 14;
+// K-quant rows: Q2_K (84-byte), Q3_K (110-byte), Q4_K (144-byte) or Q6_K
+// (210-byte) blocks of 256 values, 4-byte aligned base; plan.k a multiple
+// of 256 up to 32768.
+constexpr int kDtypeQ2_K = 10, kDtypeQ3_K = 11, kDtypeQ4_K = 12, kDtypeQ6_K = 14;
 cudaError_t launch_mul_mat_argmax_k(const LaunchEnv& env, const MvArgmaxPlan& plan, const uint8_t* lhs, int code);
 
 // Single-query attention (attention.cu): one CTA per query head.

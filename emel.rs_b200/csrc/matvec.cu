@@ -248,6 +248,8 @@ template <>
 struct PackedFmt<kDtypeQ8_0> { static constexpr int kBytes = 34; };
 template <>
 struct PackedFmt<kDtypeQ6_K> { static constexpr int kBytes = 210; };
+template <>
+struct PackedFmt<kDtypeQ3_K> { static constexpr int kBytes = 110; };
 
 // byte i of a nibble bit pattern (4 bits) moved to bit 4 of byte i
 __device__ __forceinline__ uint32_t q5_spread(uint32_t b4) {
@@ -445,7 +447,7 @@ cudaError_t launch_packed(const LaunchEnv& env, const MvArgmaxPlan& p, const uin
                             smem, env.stream, p, lhs);
 }
 
-// ---- K-quant rows (matmul.rs OpMulMatArgmaxQ4K) --------------------------------
+// ---- K-quant rows (matmul.rs OpMulMatArgmaxQ2K / Q3K / Q4K / Q6K) ---------------
 // quantize_q8_k (matmul.rs:1703-1745) per 256-value block in every CTA's
 // shared memory, stored for dp4a: word [b][g][j] holds the quants at
 // positions 32g + j, + 8, + 16, + 24 of block b -- the positions dot_q4_k
@@ -544,6 +546,80 @@ __device__ __forceinline__ void q6k_block_terms(const uint8_t* blk_ptr, const ui
     o[8] = 0.0f;
 }
 
+// Q2_K term (dot_q2_k, matmul.rs:1918-1962): one term per block,
+// (d_rhs * d) * float(sum) - (d_rhs * dmin) * float(minimum sum), in o[8].
+__device__ __forceinline__ void q2k_block_terms(const uint32_t* w, const uint32_t* r4, const int* bs, float rdb,
+                                                float* o) {
+    uint32_t W[21];
+#pragma unroll
+    for (int i = 0; i < 21; ++i) W[i] = __ldg(w + i);
+    int sum_mins = 0;
+#pragma unroll
+    for (int g = 0; g < 16; ++g) sum_mins += bs[g] * (int)((W[g >> 2] >> (8 * (g & 3) + 4)) & 0x0fu);
+    int sum = 0;
+#pragma unroll
+    for (int c = 0; c < 2; ++c) {
+#pragma unroll
+        for (int t = 0; t < 4; ++t) {
+            const int si = 8 * c + 2 * t;
+            const int s0 = (int)((W[si >> 2] >> (8 * (si & 3))) & 0x0fu);
+            const int s1 = (int)((W[(si + 1) >> 2] >> (8 * ((si + 1) & 3))) & 0x0fu);
+            int low = 0, high = 0;
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                low = __dp4a((int)((W[4 + 8 * c + k] >> (2 * t)) & 0x03030303u), (int)r4[32 * c + 8 * t + k], low);
+                high = __dp4a((int)((W[8 + 8 * c + k] >> (2 * t)) & 0x03030303u), (int)r4[32 * c + 8 * t + 4 + k], high);
+            }
+            sum += s0 * low + s1 * high;
+        }
+    }
+    const float d_all = __fmul_rn(rdb, f16_bits_to_f32((uint16_t)(W[20] & 0xffffu)));
+    const float d_min = __fmul_rn(rdb, f16_bits_to_f32((uint16_t)(W[20] >> 16)));
+    o[8] = __fsub_rn(__fmul_rn(d_all, (float)sum), __fmul_rn(d_min, (float)sum_mins));
+}
+
+// Q3_K term (unpack_q3_scales and dot_q3_k, matmul.rs:1964-2036): eight lane
+// terms (d_rhs * d) * float(acc[j]); values (2 bits | 4 where the hmask bit
+// is set) - 4 decoded four at a time, each lane sum's two positions of a
+// 16-value group paired for dp4a.
+__device__ __forceinline__ void q3k_block_terms(const uint8_t* blk_ptr, const uint32_t* r4, float rdb, float* o) {
+    PackedBlock<kDtypeQ3_K> blk;
+    blk.load(blk_ptr);
+    uint32_t a0 = blk.word(24), a1 = blk.word(25);
+    const uint32_t tmp = blk.word(26);
+    const uint32_t a2 = ((a0 >> 4) & 0x0f0f0f0fu) | (((tmp >> 4) & 0x03030303u) << 4);
+    const uint32_t a3 = ((a1 >> 4) & 0x0f0f0f0fu) | (((tmp >> 6) & 0x03030303u) << 4);
+    a0 = (a0 & 0x0f0f0f0fu) | ((tmp & 0x03030303u) << 4);
+    a1 = (a1 & 0x0f0f0f0fu) | (((tmp >> 2) & 0x03030303u) << 4);
+    const uint32_t aux[4] = {a0, a1, a2, a3};
+    int acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+#pragma unroll
+    for (int g = 0; g < 16; ++g) {
+        const int scale = (int)(int8_t)(uint8_t)(((aux[g >> 2] >> (8 * (g & 3))) & 0xffu) - 32u);
+        const int qbase = (g >> 3) * 32, half = (g & 1) * 16, shift = ((g >> 1) & 3) * 2, mbit = g >> 1;
+        uint32_t D[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+            const uint32_t qw = (blk.word(8 + (qbase + half) / 4 + k) >> shift) & 0x03030303u;
+            const uint32_t hb = ((blk.word(half / 4 + k) >> mbit) & 0x01010101u) << 2;
+            D[k] = __vsub4(qw | hb, 0x04040404u);
+        }
+        const uint32_t* R = r4 + 4 * g;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            const int a = j < 4 ? 0 : 1, bt = j & 3;
+            const uint32_t sel = (uint32_t)bt | ((uint32_t)(bt + 4) << 4);
+            const uint32_t x = __byte_perm(D[a], D[a + 2], sel) & 0xffffu;
+            const uint32_t y = __byte_perm(R[a], R[a + 2], sel);
+            acc[j] += scale * __dp4a((int)x, (int)y, 0);
+        }
+    }
+    const float sc = __fmul_rn(rdb, f16_bits_to_f32((uint16_t)(blk.word(27) & 0xffffu)));
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = __fmul_rn(sc, (float)acc[j]);
+    o[8] = 0.0f;
+}
+
 template <int CODE>
 __global__ void __launch_bounds__(kKThreads) mv_argmax_k(MvArgmaxPlan p, const uint8_t* lhs) {
     extern __shared__ __align__(16) uint32_t k_smem[];
@@ -614,7 +690,7 @@ __global__ void __launch_bounds__(kKThreads) mv_argmax_k(MvArgmaxPlan p, const u
         if (lane == 0) rd[b] = d;
     }
     __syncthreads();
-    constexpr uint64_t BB = CODE == kDtypeQ4_K ? 144 : 210;
+    constexpr uint64_t BB = CODE == kDtypeQ2_K ? 84 : CODE == kDtypeQ3_K ? 110 : CODE == kDtypeQ4_K ? 144 : 210;
     const uint64_t row_bytes = (uint64_t)blocks * BB;
     MvPart best{0.0f, 0, 0u, 0u};
     for (uint64_t g0 = ((uint64_t)blockIdx.x * kKWarps + warp) * 32; g0 < p.rows;
@@ -628,7 +704,11 @@ __global__ void __launch_bounds__(kKThreads) mv_argmax_k(MvArgmaxPlan p, const u
                 const uint32_t r = item / nbc, bl = item % nbc, b = b0 + bl;
                 const uint8_t* bp = lhs + (g0 + r) * row_bytes + (uint64_t)b * BB;
                 float* o = tile + r * kKRowStride + bl * kKTerms;
-                if constexpr (CODE == kDtypeQ4_K)
+                if constexpr (CODE == kDtypeQ2_K)
+                    q2k_block_terms(reinterpret_cast<const uint32_t*>(bp), rq + b * 64, rb + b * 16, rd[b], o);
+                else if constexpr (CODE == kDtypeQ3_K)
+                    q3k_block_terms(bp, rq + b * 64, rd[b], o);
+                else if constexpr (CODE == kDtypeQ4_K)
                     q4k_block_terms(reinterpret_cast<const uint32_t*>(bp), rq + b * 64, rb + b * 16, rd[b], o);
                 else
                     q6k_block_terms(bp, rq + b * 64, rd[b], o);
@@ -637,16 +717,22 @@ __global__ void __launch_bounds__(kKThreads) mv_argmax_k(MvArgmaxPlan p, const u
             if ((uint32_t)lane < nrows) {
                 const float* t = tile + lane * kKRowStride;
                 for (uint32_t bl = 0; bl < nbc; ++bl) {
+                    if constexpr (CODE == kDtypeQ2_K) {
+                        total = __fadd_rn(total, t[bl * kKTerms + 8]);
+                    } else {
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) ls[j] = __fadd_rn(ls[j], t[bl * kKTerms + j]);
-                    if constexpr (CODE == kDtypeQ4_K) total = __fsub_rn(total, t[bl * kKTerms + 8]);
+                        for (int j = 0; j < 8; ++j) ls[j] = __fadd_rn(ls[j], t[bl * kKTerms + j]);
+                        if constexpr (CODE == kDtypeQ4_K) total = __fsub_rn(total, t[bl * kKTerms + 8]);
+                    }
                 }
             }
             __syncwarp();
         }
         if ((uint32_t)lane < nrows) {
+            if constexpr (CODE != kDtypeQ2_K) {
 #pragma unroll
-            for (int j = 0; j < 8; ++j) total = __fadd_rn(total, ls[j]);
+                for (int j = 0; j < 8; ++j) total = __fadd_rn(total, ls[j]);
+            }
             const uint64_t row = g0 + lane;
             const bool nan = is_nan(total);
             best = mv_better(best, MvPart{total, (int32_t)row, nan ? 0u : 1u, (nan && row == 0) ? 1u : 0u});
@@ -754,7 +840,12 @@ cudaError_t launch_k(const LaunchEnv& env, const MvArgmaxPlan& p, const uint8_t*
 }
 
 cudaError_t launch_mul_mat_argmax_k(const LaunchEnv& env, const MvArgmaxPlan& p, const uint8_t* lhs, int code) {
-    return code == kDtypeQ4_K ? launch_k<kDtypeQ4_K>(env, p, lhs) : launch_k<kDtypeQ6_K>(env, p, lhs);
+    switch (code) {
+    case kDtypeQ2_K: return launch_k<kDtypeQ2_K>(env, p, lhs);
+    case kDtypeQ3_K: return launch_k<kDtypeQ3_K>(env, p, lhs);
+    case kDtypeQ4_K: return launch_k<kDtypeQ4_K>(env, p, lhs);
+    default: return launch_k<kDtypeQ6_K>(env, p, lhs);
+    }
 }
 
 cudaError_t launch_mul_mat_argmax_packed(const LaunchEnv& env, const MvArgmaxPlan& p, const uint8_t* lhs, int code) {

@@ -350,17 +350,22 @@ def mvq8_spec():
                                     MV_K * MV_ROWS)])
 
 
-# The vocabulary step with K-quant rows (matmul.rs OpMulMatArgmaxQ4K / Q6K):
+# The vocabulary step with K-quant rows (matmul.rs OpMulMatArgmaxQ2K / Q3K /
+# Q4K / Q6K):
 # [4096, 151936] as 16 blocks of 256 values per row, random block bytes with
 # binary16 scales 2^-10 * U(0.5, 1) (Q6_K: signed group scales in [-64, 64)).
-K_BLOCK_BYTES = {"q4_k": 144, "q6_k": 210}
+K_BLOCK_BYTES = {"q2_k": 84, "q3_k": 110, "q4_k": 144, "q6_k": 210}
 
 
 def mvk_inputs(fmt, seed=18):
     rng = np.random.default_rng(seed)
     blocks, bb = MV_K // 256, K_BLOCK_BYTES[fmt]
     blob = rng.integers(0, 256, size=(MV_ROWS, blocks, bb), dtype=np.uint8)
-    if fmt == "q4_k":
+    if fmt in ("q2_k", "q3_k"):
+        pos, nd = (80, 2) if fmt == "q2_k" else (108, 1)
+        d = (rng.uniform(0.5, 1.0, size=(MV_ROWS, blocks, nd)) / 1024.0).astype(np.float16)
+        blob[:, :, pos:pos + 2 * nd] = d.view(np.uint8).reshape(MV_ROWS, blocks, 2 * nd)
+    elif fmt == "q4_k":
         d = (rng.uniform(0.5, 1.0, size=(MV_ROWS, blocks, 2)) / 1024.0).astype(np.float16)
         blob[:, :, :4] = d.view(np.uint8).reshape(MV_ROWS, blocks, 4)
     else:

@@ -46,6 +46,8 @@ enum emel_cuda_dtype {
     EMEL_DTYPE_Q4_1 = 3,
     EMEL_DTYPE_Q5_0 = 6,
     EMEL_DTYPE_Q8_0 = 8,
+    EMEL_DTYPE_Q2_K = 10,
+    EMEL_DTYPE_Q3_K = 11,
     EMEL_DTYPE_Q4_K = 12,
     EMEL_DTYPE_Q6_K = 14,
     EMEL_DTYPE_I32 = 26,
@@ -524,6 +526,18 @@ EMEL_CUDA_API emel_cuda_status emel_cuda_mul_mat_argmax_q4_k(emel_cuda_context* 
  * and dot_q6_k's terms (matmul.rs:2117-2190): eight lane sums of
  * (d_rhs * d) * float(scaled integer dots), no minimum term. */
 EMEL_CUDA_API emel_cuda_status emel_cuda_mul_mat_argmax_q6_k(emel_cuda_context* ctx, void* stream,
+                                                             const emel_tensor_view* lhs, const emel_tensor_view* rhs,
+                                                             const emel_tensor_view* dst, int32_t* index_out);
+/* matmul::OpMulMatArgmaxQ2K / Q3K (matmul.rs:520-530): the same with Q2_K
+ * rows (84-byte blocks: 16 bytes of 4-bit scale / minimum pairs, 64 bytes of
+ * 2-bit values, binary16 scale and minimum scale; one term per block,
+ * dot_q2_k, matmul.rs:1918-1962) and Q3_K rows (110-byte blocks: 32 bytes of
+ * high-bit masks, 64 bytes of 2-bit values, 12 bytes of packed 6-bit
+ * scales, binary16 scale; eight lane sums, dot_q3_k, matmul.rs:1994-2036). */
+EMEL_CUDA_API emel_cuda_status emel_cuda_mul_mat_argmax_q2_k(emel_cuda_context* ctx, void* stream,
+                                                             const emel_tensor_view* lhs, const emel_tensor_view* rhs,
+                                                             const emel_tensor_view* dst, int32_t* index_out);
+EMEL_CUDA_API emel_cuda_status emel_cuda_mul_mat_argmax_q3_k(emel_cuda_context* ctx, void* stream,
                                                              const emel_tensor_view* lhs, const emel_tensor_view* rhs,
                                                              const emel_tensor_view* dst, int32_t* index_out);
 

@@ -1238,8 +1238,9 @@ int oracle_mul_mat_argmax_q5_0(const oracle_view* lhs, const oracle_view* rhs, c
  * quantized to Q8_K per 256-value block (quantize_q8_k, matmul.rs:1703-1745:
  * the first value of largest magnitude sets inverse = -127 / value, d =
  * 1 / inverse, q = min(nearest_int(inverse * x), 127), 16 group sums);
- * dot_q4_k (2040-2114) and dot_q6_k (2117-2190) keep eight lane sums,
- * lane = position % 8, added to the row total after the last block. */
+ * dot_q4_k (2040-2114), dot_q3_k (1994-2036) and dot_q6_k (2117-2190) keep
+ * eight lane sums, lane = position % 8, added to the row total after the
+ * last block; dot_q2_k (1918-1962) adds one term per block. */
 typedef struct {
     float d;
     int8_t qs[256];
@@ -1328,9 +1329,65 @@ static void dot_q6_k_block(const uint8_t* blk, const q8k_block* r, float* lane_s
     for (int l = 0; l < 8; ++l) lane_sums[l] += sc * (float)sums[l];
 }
 
+/* dot_q2_k (matmul.rs:1918-1962): one total per block. */
+static float dot_q2_k_block(const uint8_t* blk, const q8k_block* r, float total) {
+    const uint8_t* scales = blk;
+    const uint8_t* q = blk + 16;
+    const float d = gr_quant_fp16_to_f32(gr_le16(blk + 80));
+    const float dmin = gr_quant_fp16_to_f32(gr_le16(blk + 82));
+    int32_t sum_mins = 0;
+    for (int g = 0; g < 16; ++g) sum_mins += (int32_t)r->bsums[g] * (int32_t)(scales[g] >> 4);
+    int32_t sum = 0;
+    int si = 0;
+    for (int c = 0; c < 2; ++c)
+        for (int shift = 0; shift < 8; shift += 2) {
+            const int32_t s0 = scales[si] & 0x0f, s1 = scales[si + 1] & 0x0f;
+            int32_t low = 0, high = 0;
+            for (int i = 0; i < 16; ++i) {
+                low += (int32_t)r->qs[c * 128 + (shift / 2) * 32 + i] * (int32_t)((q[c * 32 + i] >> shift) & 3);
+                high += (int32_t)r->qs[c * 128 + (shift / 2) * 32 + 16 + i] * (int32_t)((q[c * 32 + 16 + i] >> shift) & 3);
+            }
+            sum += s0 * low + s1 * high;
+            si += 2;
+        }
+    const float d_all = r->d * d, d_min = r->d * dmin;
+    return total + (d_all * (float)sum - d_min * (float)sum_mins);
+}
+
+/* unpack_q3_scales (matmul.rs:1964-1990) and dot_q3_k (1994-2036). */
+static void dot_q3_k_block(const uint8_t* blk, const q8k_block* r, float* lane_sums) {
+    const uint8_t* hmask = blk;
+    const uint8_t* q = blk + 32;
+    const uint8_t* sb = blk + 96;
+    uint32_t aux[4];
+    aux[0] = (uint32_t)sb[0] | ((uint32_t)sb[1] << 8) | ((uint32_t)sb[2] << 16) | ((uint32_t)sb[3] << 24);
+    aux[1] = (uint32_t)sb[4] | ((uint32_t)sb[5] << 8) | ((uint32_t)sb[6] << 16) | ((uint32_t)sb[7] << 24);
+    const uint32_t tmp = (uint32_t)sb[8] | ((uint32_t)sb[9] << 8) | ((uint32_t)sb[10] << 16) | ((uint32_t)sb[11] << 24);
+    aux[2] = ((aux[0] >> 4) & 0x0f0f0f0fu) | (((tmp >> 4) & 0x03030303u) << 4);
+    aux[3] = ((aux[1] >> 4) & 0x0f0f0f0fu) | (((tmp >> 6) & 0x03030303u) << 4);
+    aux[0] = (aux[0] & 0x0f0f0f0fu) | ((tmp & 0x03030303u) << 4);
+    aux[1] = (aux[1] & 0x0f0f0f0fu) | (((tmp >> 2) & 0x03030303u) << 4);
+    int8_t scales[16];
+    for (int i = 0; i < 16; ++i) scales[i] = (int8_t)((uint8_t)(aux[i / 4] >> (8 * (i % 4))) - 32u);
+    const float d = gr_quant_fp16_to_f32(gr_le16(blk + 108));
+    int32_t acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    for (int g = 0; g < 16; ++g) {
+        const int32_t scale = scales[g];
+        const int qbase = (g / 8) * 32, half = (g % 2) * 16;
+        const uint8_t mask = (uint8_t)(1u << (g / 2));
+        for (int i = 0; i < 16; ++i) {
+            const uint8_t qbyte = q[qbase + half + i];
+            const int32_t quantized = (int32_t)((qbyte >> (((g / 2) % 4) * 2)) & 3) - ((hmask[half + i] & mask) == 0 ? 4 : 0);
+            acc[i & 7] += scale * quantized * (int32_t)r->qs[g * 16 + i];
+        }
+    }
+    const float sc = r->d * d;
+    for (int l = 0; l < 8; ++l) lane_sums[l] += sc * (float)acc[l];
+}
+
 static int oracle_argmax_k(int code, const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
                            int32_t* index_out) {
-    const uint64_t bb = code == 12 ? 144 : 210;
+    const uint64_t bb = code == 10 ? 84 : code == 11 ? 110 : code == 12 ? 144 : 210;
     if (!gr_packed_view_valid(lhs, (uint32_t)code, 256, bb) || lhs->ne[0] / 256 > 128 ||
         !validate_as(rhs, DT_F32, 0, NULL) || !validate_as(dst, DT_F32, 0, NULL) || !dense_contiguous_f32(rhs) ||
         !dense_contiguous_f32(dst))
@@ -1352,12 +1409,17 @@ static int oracle_argmax_k(int code, const oracle_view* lhs, const oracle_view* 
         float lane_sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
         float sum = 0.0f;
         for (uint64_t b = 0; b < blocks; ++b) {
-            if (code == 12)
+            if (code == 10)
+                sum = dot_q2_k_block(rp + b * bb, &q8[b], sum);
+            else if (code == 11)
+                dot_q3_k_block(rp + b * bb, &q8[b], lane_sums);
+            else if (code == 12)
                 sum = dot_q4_k_block(rp + b * bb, &q8[b], lane_sums, sum);
             else
                 dot_q6_k_block(rp + b * bb, &q8[b], lane_sums);
         }
-        for (int k = 0; k < 8; ++k) sum += lane_sums[k];
+        if (code != 10)
+            for (int k = 0; k < 8; ++k) sum += lane_sums[k];
         if (sum > best || row == 0) {
             best = sum;
             best_index = (int32_t)row;
@@ -1376,6 +1438,16 @@ int oracle_mul_mat_argmax_q4_k(const oracle_view* lhs, const oracle_view* rhs, c
 int oracle_mul_mat_argmax_q6_k(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
                                int32_t* index_out) {
     return oracle_argmax_k(14, lhs, rhs, dst, index_out);
+}
+
+int oracle_mul_mat_argmax_q2_k(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
+                               int32_t* index_out) {
+    return oracle_argmax_k(10, lhs, rhs, dst, index_out);
+}
+
+int oracle_mul_mat_argmax_q3_k(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
+                               int32_t* index_out) {
+    return oracle_argmax_k(11, lhs, rhs, dst, index_out);
 }
 
 /* ---------------------------------------------------------------------- */

@@ -88,6 +88,11 @@ int oracle_mul_mat_argmax_q4_k(const oracle_view* lhs, const oracle_view* rhs, c
                                int32_t* index_out);
 int oracle_mul_mat_argmax_q6_k(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
                                int32_t* index_out);
+/* Q2_K (84-byte) and Q3_K (110-byte) blocks (OpMulMatArgmaxQ2K / Q3K). */
+int oracle_mul_mat_argmax_q2_k(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
+                               int32_t* index_out);
+int oracle_mul_mat_argmax_q3_k(const oracle_view* lhs, const oracle_view* rhs, const oracle_view* dst,
+                               int32_t* index_out);
 /* diag.rs OpDiag / OpDiagMaskInf (mode 0) / OpDiagMaskZero (mode 1) over flat
  * f32 slices. */
 int oracle_diag(const float* input, uint64_t input_len, float* output, uint64_t output_len);

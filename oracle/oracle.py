@@ -127,6 +127,8 @@ def load(cr=False):
         "oracle_mul_mat_argmax_q5_0": [P, P, P, ctypes.POINTER(ctypes.c_int32)],
         "oracle_mul_mat_argmax_q4_k": [P, P, P, ctypes.POINTER(ctypes.c_int32)],
         "oracle_mul_mat_argmax_q6_k": [P, P, P, ctypes.POINTER(ctypes.c_int32)],
+        "oracle_mul_mat_argmax_q2_k": [P, P, P, ctypes.POINTER(ctypes.c_int32)],
+        "oracle_mul_mat_argmax_q3_k": [P, P, P, ctypes.POINTER(ctypes.c_int32)],
         "oracle_rope": [P, P, P, ctypes.POINTER(RopeParams)],
         "oracle_flash_attn_ext": [P, P, P, P, ctypes.POINTER(FlashAttnOptions)],
         "oracle_diag": [ctypes.c_void_p, ctypes.c_uint64, ctypes.c_void_p, ctypes.c_uint64],

@@ -262,7 +262,7 @@ def q4k_rows(rng, k, rows, planted=None):
 
 def run_q4k_both(emel, kern, olib, blob, rhs, k, rows, code=12):
     ctx = kern.ctx
-    suffix, bb = {12: ("q4_k", 144), 14: ("q6_k", 210)}[code]
+    suffix, bb = {10: ("q2_k", 84), 11: ("q3_k", 110), 12: ("q4_k", 144), 14: ("q6_k", 210)}[code]
     rb = k // 256 * bb
     bl, br = emel.DeviceBuffer(ctx, blob.nbytes + 16), emel.DeviceBuffer(ctx, rhs.nbytes)
     bd, bi = emel.DeviceBuffer(ctx, 16), emel.DeviceBuffer(ctx, 16)
@@ -345,5 +345,47 @@ def test_q6_k_parity(emel, kern, oracle_lib, k, rows):
     blob = q6k_rows(rng, k, rows, planted)
     rhs = rng.standard_normal(k).astype(np.float32)
     st, sync, ost, gv, gi, ov, oi = run_q4k_both(emel, kern, oracle_lib, blob, rhs, k, rows, 14)
+    assert st == 0 and sync == 0 and ost == 0
+    assert gi == oi and np.array([gv]).view(np.uint32)[0] == np.array([ov]).view(np.uint32)[0]
+
+
+# ---- Q2_K / Q3_K rows (matmul.rs OpMulMatArgmaxQ2K / Q3K) ----------------------
+
+def q23k_rows(rng, code, k, rows, planted=None):
+    blocks = k // 256
+    bb, dpos = (84, 80) if code == 10 else (110, 108)
+    blob = rng.integers(0, 256, size=(rows, blocks, bb), dtype=np.uint8)
+    nd = 2 if code == 10 else 1
+    d = rng.uniform(0.5, 1.0, size=(rows, blocks, nd)) * 2.0 ** -9
+    blob[:, :, dpos:dpos + 2 * nd] = d.astype(np.float16).view(np.uint8).reshape(rows, blocks, 2 * nd)
+    if planted is not None:
+        blob[planted, :, dpos:dpos + 2] = np.array([0.05], np.float16).view(np.uint8)
+    return blob.reshape(-1)
+
+
+def test_q2_k_q3_k_reference_golden_vectors(emel, kern, oracle_lib):
+    # kernel-argmax-parity manifest: q2_k_success (row 1, 0x46340000),
+    # q3_k_success (row 0, +0)
+    q2 = np.zeros(168, np.uint8)
+    q2[164:166] = (0x00, 0x3C)
+    q2[84:164] = 0xFF
+    st, sync, ost, gv, gi, ov, oi = run_q4k_both(emel, kern, oracle_lib, q2, np.ones(256, np.float32), 256, 2, 10)
+    assert st == 0 and sync == 0 and gi == 1 and int(np.array([gv]).view(np.uint32)[0]) == 0x46340000
+    q3 = np.zeros(220, np.uint8)
+    q3[110:206] = 0xFF
+    q3[206:218] = 0x21
+    q3[218:220] = (0x00, 0x3C)
+    st, sync, ost, gv, gi, ov, oi = run_q4k_both(emel, kern, oracle_lib, q3, np.ones(256, np.float32), 256, 2, 11)
+    assert st == 0 and sync == 0 and gi == 0 and int(np.array([gv]).view(np.uint32)[0]) == 0
+
+
+@pytest.mark.parametrize("code", [10, 11])
+@pytest.mark.parametrize("k,rows", [(256, 1), (256, 33), (512, 100), (4096, 3000), (32768, 40), (4352, 65)])
+def test_q2_k_q3_k_parity(emel, kern, oracle_lib, code, k, rows):
+    rng = np.random.default_rng(code * 100 + k + rows)
+    planted = int(rng.integers(0, rows))
+    blob = q23k_rows(rng, code, k, rows, planted)
+    rhs = rng.standard_normal(k).astype(np.float32)
+    st, sync, ost, gv, gi, ov, oi = run_q4k_both(emel, kern, oracle_lib, blob, rhs, k, rows, code)
     assert st == 0 and sync == 0 and ost == 0
     assert gi == oi and np.array([gv]).view(np.uint32)[0] == np.array([ov]).view(np.uint32)[0]

@@ -235,8 +235,9 @@ def test_q4_q5_decoding_matches_float_dot(lib):
 
 # ---- K-quant rows (matmul.rs OpMulMatArgmaxQ4K / Q6K) -------------------------
 
-K_BYTES = {12: 144, 14: 210}
-K_FN = {12: "oracle_mul_mat_argmax_q4_k", 14: "oracle_mul_mat_argmax_q6_k"}
+K_BYTES = {10: 84, 11: 110, 12: 144, 14: 210}
+K_FN = {10: "oracle_mul_mat_argmax_q2_k", 11: "oracle_mul_mat_argmax_q3_k", 12: "oracle_mul_mat_argmax_q4_k",
+        14: "oracle_mul_mat_argmax_q6_k"}
 
 
 def run_k(lib, code, lhs_bytes, k, rows, rhs):
@@ -275,3 +276,22 @@ def test_k_quant_guards(lib):
     blk = bytes(144)
     assert run_k(lib, 12, blk, 256, 1, np.ones(255))[0] in (1, 2)
     assert run_k(lib, 12, blk * 129, 256 * 129, 1, np.ones(256 * 129))[0] == 1   # 129 blocks > 128
+
+
+def test_q2_k_q3_k_reference_golden_vectors(lib):
+    # kernel-argmax-parity manifest: q2_k_success index=1 bits 46340000,
+    # q3_k_success index=0 bits 00000000; inputs from
+    # tools/emel-kernel-argmax-parity/src/main.rs:73-89 and 114-127
+    q2 = bytearray(168)
+    q2[84 + 80:84 + 82] = bytes([0x00, 0x3C])
+    q2[84:84 + 16] = bytes([0xFF]) * 16
+    q2[84 + 16:84 + 80] = bytes([0xFF]) * 64
+    st, out, idx = run_k(lib, 10, q2, 256, 2, np.ones(256))
+    assert st == 0 and idx == 1 and int(out.view(np.uint32)[0]) == 0x46340000
+    q3 = bytearray(220)
+    q3[110:142] = bytes([0xFF]) * 32
+    q3[142:206] = bytes([0xFF]) * 64
+    q3[206:218] = bytes([0x21]) * 12
+    q3[218:220] = bytes([0x00, 0x3C])
+    st, out, idx = run_k(lib, 11, q3, 256, 2, np.ones(256))
+    assert st == 0 and idx == 0 and int(out.view(np.uint32)[0]) == 0x00000000
