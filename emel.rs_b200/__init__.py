@@ -194,6 +194,7 @@ SIGNATURES = {
     "emel_cuda_argmax_rows": (_I, [_CTX, _V, _P, _P]),
     "emel_cuda_generic": (_I, [_CTX, _V, ctypes.POINTER(CGenericRequest)]),
     "emel_cuda_get_rows": (_I, [_CTX, _V, _P, _P, _P]),
+    "emel_cuda_get_rows_f32_bytes": (_I, [_CTX, _V, _P, _P, _P]),
     "emel_cuda_mul_mat_argmax": (_I, [_CTX, _V, _P, _P, _P, _V]),
     "emel_cuda_mul_mat_argmax_q8_0": (_I, [_CTX, _V, _P, _P, _P, _V]),
     "emel_cuda_mul_mat_argmax_q4_0": (_I, [_CTX, _V, _P, _P, _P, _V]),
@@ -642,6 +643,19 @@ class OpGetRows(Event):
 
     def dispatch(self, ctx, stream):
         return ctx._lib.emel_cuda_get_rows(ctx.handle, stream, _r(self.src), _r(self.indices), _r(self.dst))
+
+
+@dataclass
+class OpGetRowsF32Bytes(Event):
+    """get_rows::OpGetRowsF32Bytes (get_rows.rs:233-255): F32 rows of a
+    byte-backed source whose strides may be any byte count."""
+    src: TensorView
+    indices: TensorView
+    dst: TensorView
+
+    def dispatch(self, ctx, stream):
+        return ctx._lib.emel_cuda_get_rows_f32_bytes(ctx.handle, stream, _r(self.src), _r(self.indices),
+                                                     _r(self.dst))
 
 
 @dataclass

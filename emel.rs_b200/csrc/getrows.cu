@@ -1,7 +1,8 @@
 // Row gather (get_rows.rs): dst row r = source row idx[r] of the source
 // batch the index's outer coordinates select, decoded to f32.  Sources:
-// F32 (strided rows), F16 and BF16 (any strides), and the Q4_0 / Q8_0 /
-// Q4_K block formats (dense rows of packed blocks).
+// F32 (strided rows), byte-backed F32 (rows at any byte offset), F16 and BF16
+// (any strides), and the Q4_0 / Q8_0 / Q4_K block formats (dense rows of
+// packed blocks).
 //
 // Indices live in device memory, so the reference's index guard (every
 // index in [0, rows) before anything is written) runs on the device: a
@@ -105,10 +106,11 @@ __global__ void __launch_bounds__(kGatherThreads) gather_plain(GatherPlan p) {
         const char* row = p.src + index * p.src_st[1] + i1 * p.src_st[2] + i2 * p.src_st[3];
         float* out = p.dst + r * cols;
         const bool vec = p.vec && (reinterpret_cast<uintptr_t>(row) & 15u) == 0;
+        constexpr bool kF32 = KIND == kGatherF32 || KIND == kGatherF32Bytes;
         if (vec) {
             // F32: 4 floats per vector (read_row_contiguous, tensor_view.rs:756-769:
             // columns 4 bytes apart); F16 / BF16: 8 halves per vector
-            const uint64_t nv = KIND == kGatherF32 ? cols / 4 : cols / 8;
+            const uint64_t nv = kF32 ? cols / 4 : cols / 8;
             const uint4* in = reinterpret_cast<const uint4*>(row);
             uint64_t v = threadIdx.x;
             for (; v + (U - 1) * kGatherThreads < nv; v += U * kGatherThreads) {
@@ -117,7 +119,7 @@ __global__ void __launch_bounds__(kGatherThreads) gather_plain(GatherPlan p) {
                 for (int k = 0; k < U; ++k) q[k] = __ldcs(in + v + k * kGatherThreads);
 #pragma unroll
                 for (int k = 0; k < U; ++k) {
-                    if constexpr (KIND == kGatherF32)
+                    if constexpr (kF32)
                         __stcs(reinterpret_cast<uint4*>(out) + v + k * kGatherThreads, q[k]);
                     else
                         half_store8<KIND>(out, v + k * kGatherThreads, q[k]);
@@ -125,12 +127,27 @@ __global__ void __launch_bounds__(kGatherThreads) gather_plain(GatherPlan p) {
             }
             for (; v < nv; v += kGatherThreads) {
                 const uint4 q = __ldcs(in + v);
-                if constexpr (KIND == kGatherF32) __stcs(reinterpret_cast<uint4*>(out) + v, q);
+                if constexpr (kF32) __stcs(reinterpret_cast<uint4*>(out) + v, q);
                 else half_store8<KIND>(out, v, q);
             }
         } else if constexpr (KIND == kGatherF32) {
             const float* in = reinterpret_cast<const float*>(row);
             for (uint64_t c = threadIdx.x; c < cols; c += kGatherThreads) out[c] = in[c];
+        } else if constexpr (KIND == kGatherF32Bytes) {
+            // ByteTensorView::read_row_contiguous (tensor_view.rs:645-680): the 4 little-endian
+            // bytes at row + 4c.  A row off a word boundary is read as the aligned
+            // words that hold its bytes, each joined with the next by a funnel
+            // shift; every word read holds at least one byte of the row.
+            const uintptr_t a = reinterpret_cast<uintptr_t>(row);
+            const uint32_t sh = (uint32_t)(a & 3u) * 8u;
+            if (sh == 0) {
+                const float* in = reinterpret_cast<const float*>(row);
+                for (uint64_t c = threadIdx.x; c < cols; c += kGatherThreads) out[c] = in[c];
+            } else {
+                const uint32_t* w = reinterpret_cast<const uint32_t*>(a & ~(uintptr_t)3);
+                for (uint64_t c = threadIdx.x; c < cols; c += kGatherThreads)
+                    out[c] = __uint_as_float(__funnelshift_r(__ldg(w + c), __ldg(w + c + 1), sh));
+            }
         } else {
             for (uint64_t c = threadIdx.x; c < cols; c += kGatherThreads)
                 out[c] = half_value<KIND>(*reinterpret_cast<const uint16_t*>(row + c * p.src_st[0]));
@@ -296,6 +313,7 @@ cudaError_t launch_get_rows(const LaunchEnv& env, const GatherPlan& p) {
     if (err != cudaSuccess) return err;
     switch (p.kind) {
     case kGatherF32: return launch_pair(env, p, gather_plain<kGatherF32>);
+    case kGatherF32Bytes: return launch_pair(env, p, gather_plain<kGatherF32Bytes>);
     case kGatherF16: return launch_pair(env, p, gather_plain<kGatherF16>);
     case kGatherBF16: return launch_pair(env, p, gather_plain<kGatherBF16>);
     case kGatherQ4_0: return launch_pair(env, p, gather_quant<kGatherQ4_0>);

@@ -1115,6 +1115,80 @@ emel_cuda_status emel_cuda_get_rows(emel_cuda_context* ctx, void* stream, const 
     return device_status(ctx, err);
 }
 
+namespace {
+
+// ByteTensorView::validate (tensor_view.rs:588-643) with a non-null buffer;
+// `s` receives Layout::effective_f32_strides (tensor_view.rs:262-277).
+bool gr_byte_view_valid(const emel_tensor_view* v, uint64_t s[4]) {
+    if (v->dtype != EMEL_DTYPE_F32 || v->data == nullptr) return false;
+    uint64_t count = 1;
+    for (int d = 0; d < 4; ++d)
+        if (v->ne[d] == 0 || __builtin_mul_overflow(count, v->ne[d], &count)) return false;
+    if (v->nb[0] != 0 && (v->nb[0] < 4 || v->nb[0] % 4 != 0)) return false;
+    if (v->nb[0] != 0) {
+        for (int d = 0; d < 4; ++d)
+            if (v->ne[d] > 1 && v->nb[d] == 0) return false;
+        for (int d = 0; d < 4; ++d) s[d] = v->nb[d];
+    } else {
+        s[0] = 4;
+        for (int d = 1; d < 4; ++d)
+            if (__builtin_mul_overflow(s[d - 1], v->ne[d - 1], &s[d])) return false;
+    }
+    u128 max_offset = 0;
+    for (int d = 1; d < 4; ++d) max_offset += (u128)(v->ne[d] - 1) * (u128)s[d];
+    return max_offset + (u128)v->ne[0] * 4 <= (u128)v->storage_bytes;
+}
+
+// empty_f32_bytes_source_valid (get_rows.rs:951-971)
+bool gr_byte_empty_valid(const emel_tensor_view* v) {
+    if (v->dtype != EMEL_DTYPE_F32 || v->ne[0] == 0 || v->ne[1] == 0) return false;
+    if (v->nb[0] != 0 && (v->nb[0] < 4 || v->nb[0] % 4 != 0)) return false;
+    if (v->nb[0] != 0)
+        for (int d = 0; d < 4; ++d)
+            if (v->ne[d] > 1 && v->nb[d] == 0) return false;
+    return true;
+}
+
+}  // namespace
+
+emel_cuda_status emel_cuda_get_rows_f32_bytes(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
+                                              const emel_tensor_view* indices, const emel_tensor_view* dst) {
+    if (src == nullptr || indices == nullptr || dst == nullptr) return EMEL_CUDA_INVALID_VIEW;
+    const GrIndex ix = gr_index_view(indices);
+    uint64_t s[4] = {0, 0, 0, 0};
+    const bool views = ix.valid && (ix.count == 0 ? gr_byte_empty_valid(src) : gr_byte_view_valid(src, s)) &&
+                       gr_destination_valid(dst, ix.count);
+    // get_rows.rs guard order: view, shape, indices (on the device)
+    if (!views) return EMEL_CUDA_INVALID_VIEW;
+    if (!gr_shape_valid(src, ix, dst)) return EMEL_CUDA_SHAPE_MISMATCH;
+    if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    if (ix.count == 0) return EMEL_CUDA_OK;
+    const uintptr_t ia = reinterpret_cast<uintptr_t>(indices->data), da = reinterpret_cast<uintptr_t>(dst->data);
+    if ((ia & 3u) || (da & 3u)) return EMEL_CUDA_INVALID_ARGUMENT;
+    emel::GatherPlan p{};
+    p.kind = emel::kGatherF32Bytes;
+    p.src = static_cast<const char*>(src->data);
+    p.dst = static_cast<float*>(dst->data);
+    p.idx = static_cast<const int32_t*>(indices->data);
+    for (int d = 0; d < 3; ++d) {
+        p.idx_ne[d] = ix.ne[d];
+        p.idx_st[d] = (int64_t)ix.st[d];
+    }
+    p.cols = src->ne[0];
+    p.rows = src->ne[1];
+    p.batches = src->ne[2];
+    p.dst_rows = ix.count;
+    for (int d = 0; d < 4; ++d) p.src_st[d] = (int64_t)s[d];
+    p.vec = p.cols % 4 == 0 && (da & 15u) == 0;
+    char* ws = static_cast<char*>(ctx->workspace);
+    p.flag = reinterpret_cast<uint32_t*>(ws + emel::kCallFlagOffset);
+    p.reject = reinterpret_cast<uint32_t*>(ws + emel::kRejectWordOffset);
+    p.reject_code = EMEL_CUDA_INDEX_OUT_OF_BOUNDS;
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) err = emel::launch_get_rows(env_of(ctx, stream), p);
+    return device_status(ctx, err);
+}
+
 // ---- rotary position embedding (rope.rs) -----------------------------------
 
 static bool rope_positions_valid(const emel_tensor_view* v) {

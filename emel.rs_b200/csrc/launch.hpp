@@ -62,7 +62,8 @@ constexpr int f16_table_slot(int op) { return op < 64 ? op : 22 + (op - 64); }
 uint64_t reduction_workspace_bytes(int sm_count);
 
 // Row gather (getrows.cu).
-enum GatherKind : int { kGatherF32 = 0, kGatherF16 = 1, kGatherBF16 = 2, kGatherQ4_0 = 3, kGatherQ8_0 = 4, kGatherQ4_K = 5 };
+enum GatherKind : int { kGatherF32 = 0, kGatherF16 = 1, kGatherBF16 = 2, kGatherQ4_0 = 3, kGatherQ8_0 = 4, kGatherQ4_K = 5,
+                        kGatherF32Bytes = 6 };
 
 // Workspace header words of the index guard: the context's sticky rejected
 // status (reported by emel_cuda_stream_synchronize) and one call's flag.

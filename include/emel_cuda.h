@@ -359,6 +359,21 @@ EMEL_CUDA_API emel_cuda_status emel_cuda_argmax_rows(emel_cuda_context* ctx, voi
 EMEL_CUDA_API emel_cuda_status emel_cuda_get_rows(emel_cuda_context* ctx, void* stream, const emel_tensor_view* src,
                                                   const emel_tensor_view* indices, const emel_tensor_view* dst);
 
+/* get_rows.rs OpGetRowsF32Bytes (lines 233-255; guards 942-1003; loop
+ * 1943-1979): the F32 gather over a byte-backed source (ByteTensorView,
+ * tensor_view.rs:560-680) whose row, batch and outer strides may be any byte
+ * count, so a row may start at any byte offset.  Guards: the byte view
+ * (F32; nb[0] zero or a multiple of 4; every row's ne[0] * 4 bytes inside
+ * storage_bytes; with no indices only the metadata rules) and a dense F32
+ * destination -> EMEL_CUDA_INVALID_VIEW; shapes -> EMEL_CUDA_SHAPE_MISMATCH;
+ * indices on the device as for emel_cuda_get_rows.  Device additions:
+ * 4-byte aligned index and destination pointers (the source may have any
+ * alignment), else EMEL_CUDA_INVALID_ARGUMENT. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_get_rows_f32_bytes(emel_cuda_context* ctx, void* stream,
+                                                            const emel_tensor_view* src,
+                                                            const emel_tensor_view* indices,
+                                                            const emel_tensor_view* dst);
+
 /* ---- rotary position embedding ---------------------------------------- */
 /* rope::RopeParams (rope.rs:33-48). */
 typedef struct emel_rope_params {

@@ -891,6 +891,61 @@ static void gr_q4_k_block(const uint8_t* b, float* out) {
  * type: OpGetRows, OpGetRowsF16, OpGetRowsBf16, OpGetRowsQ4_0, OpGetRowsQ8_0,
  * OpGetRowsQ4K); guards in each event's order, then the gather loops of
  * get_rows.rs:1453-1800. */
+/* ByteTensorView::validate (tensor_view.rs:588-643): F32 metadata, nb[0]
+ * zero or a multiple of 4 that is at least 4, no zero stride on a
+ * multi-element dimension when strides are explicit, and every row's bytes
+ * (ne[0] * 4 from any outer byte offset) inside the byte storage. */
+static int gr_byte_view_valid(const oracle_view* v) {
+    if (v->dtype != DT_F32) return 0;
+    uint64_t count;
+    if (!element_count(v, &count)) return 0;
+    if (v->nb[0] != 0 && (v->nb[0] < 4 || v->nb[0] % 4 != 0)) return 0;
+    if (v->nb[0] != 0)
+        for (int d = 0; d < 4; ++d)
+            if (v->ne[d] > 1 && v->nb[d] == 0) return 0;
+    uint64_t s[4];
+    if (!effective_strides(v, 4, s)) return 0;
+    u128 max_offset = 0;
+    for (int d = 1; d < 4; ++d) max_offset += (u128)(v->ne[d] - 1) * (u128)s[d];
+    return max_offset + (u128)v->ne[0] * 4 <= (u128)v->storage_bytes;
+}
+
+/* empty_f32_bytes_source_valid (get_rows.rs:951-971) */
+static int gr_byte_empty_valid(const oracle_view* v) {
+    if (v->dtype != DT_F32 || v->ne[0] == 0 || v->ne[1] == 0) return 0;
+    if (v->nb[0] != 0 && (v->nb[0] < 4 || v->nb[0] % 4 != 0)) return 0;
+    if (v->nb[0] != 0)
+        for (int d = 0; d < 4; ++d)
+            if (v->ne[d] > 1 && v->nb[d] == 0) return 0;
+    return 1;
+}
+
+/* OpGetRowsF32Bytes (get_rows.rs:233-255; guards 942-1003 in the order view,
+ * shape, indices; loop 1943-1979): dst row r is the ne[0] * 4 bytes at source
+ * row indices[r] of batch (i1, i2), read from any byte offset. */
+int oracle_get_rows_f32_bytes(const oracle_view* src, const oracle_view* indices, const oracle_view* dst) {
+    if (src == NULL || indices == NULL || dst == NULL) return ORACLE_INVALID_VIEW;
+    const gr_index ix = gr_index_view(indices);
+    const int views = ix.valid && (ix.count == 0 ? gr_byte_empty_valid(src) : gr_byte_view_valid(src)) &&
+                      gr_destination_valid(dst, ix.count);
+    if (!views) return ORACLE_INVALID_VIEW;
+    if (!gr_shape_valid(src, &ix, dst)) return ORACLE_SHAPE_MISMATCH;
+    if (!gr_indices_valid(&ix, src->ne[1])) return ORACLE_INDEX_OUT_OF_BOUNDS;
+    if (ix.count == 0) return ORACLE_OK;
+    uint64_t s[4];
+    effective_strides(src, 4, s);
+    const uint64_t cols = src->ne[0];
+    float* out = (float*)dst->data;
+    uint64_t dst_row = 0;
+    for (uint64_t i2 = 0; i2 < ix.ne[2]; ++i2)
+        for (uint64_t i1 = 0; i1 < ix.ne[1]; ++i1)
+            for (uint64_t i0 = 0; i0 < ix.ne[0]; ++i0, ++dst_row) {
+                const uint64_t index = (uint64_t)gr_index_read(&ix, dst_row);
+                memcpy(out + dst_row * cols, (const char*)src->data + index * s[1] + i1 * s[2] + i2 * s[3], cols * 4);
+            }
+    return ORACLE_OK;
+}
+
 int oracle_get_rows(const oracle_view* src, const oracle_view* indices, const oracle_view* dst) {
     if (src == NULL || indices == NULL || dst == NULL) return ORACLE_INVALID_VIEW;
     const gr_index ix = gr_index_view(indices);

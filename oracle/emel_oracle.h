@@ -130,6 +130,8 @@ int oracle_rope(const oracle_view* src, const oracle_view* positions, const orac
  * F16, BF16 30, Q4_0 2, Q8_0 8, Q4_K 12; indices I32 with ne[3] == 1; dst
  * dense F32). */
 int oracle_get_rows(const oracle_view* src, const oracle_view* indices, const oracle_view* dst);
+/* get_rows.rs OpGetRowsF32Bytes: byte-backed F32 source rows at any byte offset. */
+int oracle_get_rows_f32_bytes(const oracle_view* src, const oracle_view* indices, const oracle_view* dst);
 /* shape.rs OpCpy / OpCont. */
 int oracle_cpy(const oracle_view* src, const oracle_view* dst);
 int oracle_cont(const oracle_view* src, const oracle_view* dst);

@@ -120,6 +120,7 @@ def load(cr=False):
         "oracle_copy": [P, P],
         "oracle_cpy": [P, P],
         "oracle_get_rows": [P, P, P],
+        "oracle_get_rows_f32_bytes": [P, P, P],
         "oracle_mul_mat_argmax": [P, P, P, ctypes.POINTER(ctypes.c_int32)],
         "oracle_mul_mat_argmax_q8_0": [P, P, P, ctypes.POINTER(ctypes.c_int32)],
         "oracle_mul_mat_argmax_q4_0": [P, P, P, ctypes.POINTER(ctypes.c_int32)],

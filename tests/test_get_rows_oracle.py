@@ -149,3 +149,67 @@ def test_empty_indices_are_a_no_op(lib):
                              B(v(ia, [0, 1, 1, 1], [4, 4, 4, 4], I32)),
                              B(v(out, [3, 0, 1, 1], [4, 12, 0, 0], F32)))  # Layout::contiguous strides
     assert st == 0 and np.all(out == 7.0)
+
+
+def f32_bytes_known_source(length):
+    # tests/any/get_rows_ops.rs:440-479: rows at byte offsets 0 and 9
+    src = np.zeros(length, np.uint8)
+    src[0:8] = np.array([1.0, 2.0], np.float32).view(np.uint8)
+    if length >= 17:
+        src[9:17] = np.array([3.0, 4.0], np.float32).view(np.uint8)
+    return src
+
+
+def test_f32_bytes_reads_unaligned_outer_source_rows(lib):
+    src = f32_bytes_known_source(17)
+    idx, iv = idx_view([1, 0], [2, 1, 1])
+    out = np.zeros(4, np.float32)
+    st = lib.oracle_get_rows_f32_bytes(B(v(src, [2, 2, 1, 1], [4, 9, 18, 18], F32)), B(iv),
+                                       B(v(out, [2, 2, 1, 1], contiguous_nb([2, 2, 1, 1]), F32)))
+    assert st == 0 and out.tolist() == [3.0, 4.0, 1.0, 2.0]
+
+
+def test_f32_bytes_rejects_short_unaligned_outer_storage(lib):
+    src = np.zeros(16, np.uint8)
+    idx, iv = idx_view([1, 0], [2, 1, 1])
+    out = np.full(4, 9.0, np.float32)
+    st = lib.oracle_get_rows_f32_bytes(B(v(src, [2, 2, 1, 1], [4, 9, 18, 18], F32)), B(iv),
+                                       B(v(out, [2, 2, 1, 1], contiguous_nb([2, 2, 1, 1]), F32)))
+    assert st == INVALID_VIEW and out.tolist() == [9.0] * 4
+
+
+def test_f32_bytes_guard_order(lib):
+    src = f32_bytes_known_source(17)
+    out = np.full(4, 9.0, np.float32)
+    ov = v(out, [2, 2, 1, 1], contiguous_nb([2, 2, 1, 1]), F32)
+    idx, iv = idx_view([1, 0], [2, 1, 1])
+    # nb[0] not a multiple of 4: InvalidView (no UnsupportedSourceStride variant on this path)
+    assert lib.oracle_get_rows_f32_bytes(B(v(src, [2, 2, 1, 1], [2, 9, 18, 18], F32)), B(iv), B(ov)) == INVALID_VIEW
+    # an F16 source: InvalidView
+    assert lib.oracle_get_rows_f32_bytes(B(v(src, [2, 2, 1, 1], [4, 9, 18, 18], F16)), B(iv), B(ov)) == INVALID_VIEW
+    # destination rows differ from the index count: ShapeMismatch
+    bad_out = v(out, [2, 1, 1, 1], contiguous_nb([2, 1, 1, 1]), F32)
+    assert lib.oracle_get_rows_f32_bytes(B(v(src, [2, 2, 1, 1], [4, 9, 18, 18], F32)), B(iv),
+                                         B(bad_out)) == SHAPE_MISMATCH
+    # an index past the rows: IndexOutOfBounds
+    idx, iv = idx_view([2, 0], [2, 1, 1])
+    assert lib.oracle_get_rows_f32_bytes(B(v(src, [2, 2, 1, 1], [4, 9, 18, 18], F32)), B(iv), B(ov)) == INDEX_OOB
+    assert out.tolist() == [9.0] * 4
+    # no indices: the metadata-only rules, nothing read
+    idx, iv = idx_view(np.zeros(0), [0, 1, 1])
+    empty = np.zeros(1, np.float32)
+    assert lib.oracle_get_rows_f32_bytes(B(v(src, [2, 2, 1, 1], [4, 9, 18, 18], F32)), B(iv),
+                                         B(v(empty, [2, 0, 1, 1], [4, 8, 0, 0], F32))) == 0
+
+
+def test_f32_bytes_matches_the_aligned_gather_on_aligned_rows(lib):
+    rng = np.random.default_rng(5)
+    src = rng.standard_normal(64 * 10).astype(np.float32)
+    idx, iv = idx_view(rng.integers(0, 10, 12), [12, 1, 1])
+    a = np.zeros(64 * 12, np.float32)
+    b = np.ones(64 * 12, np.float32)
+    sv = v(src, [64, 10, 1, 1], contiguous_nb([64, 10, 1, 1]), F32)
+    dn = [64, 12, 1, 1]
+    assert lib.oracle_get_rows(B(sv), B(iv), B(v(a, dn, contiguous_nb(dn), F32))) == 0
+    assert lib.oracle_get_rows_f32_bytes(B(sv), B(iv), B(v(b, dn, contiguous_nb(dn), F32))) == 0
+    assert np.array_equal(a.view(np.uint32), b.view(np.uint32))

@@ -191,3 +191,95 @@ def test_rejected_views_return_synchronously(emel, kern, oracle_lib):
     assert np.all(dd.download() == 7.0)
     for d in (ds, di, dd, dq):
         d.free()
+
+
+def run_bytes(emel, kern, olib, src, offset, ne, nb, idx, idx_ne, dst_offset=0, fill=7.0):
+    """emel_cuda_get_rows_f32_bytes and oracle_get_rows_f32_bytes on the byte
+    source `src[offset:]` (the device pointer is then `offset` bytes past a
+    256-byte aligned allocation)."""
+    ctx = kern.ctx
+    src = np.ascontiguousarray(src, np.uint8)
+    idx = np.asarray(idx, np.int32)
+    ine = list(idx_ne) + [1]
+    dne = [ne[0]] + list(idx_ne)
+    ds = Dev(emel, ctx, src, ne, nb, F32)
+    di = Dev(emel, ctx, idx, ine, contiguous_nb(ine), I32)
+    n_out = int(np.prod(dne))
+    dd = Dev(emel, ctx, np.full(n_out + 4, fill, np.float32), dne, contiguous_nb(dne), F32)
+    sv = ds.c()
+    sv.data, sv.storage_bytes = ds.buf.ptr + offset, src.nbytes - offset
+    dv = dd.c()
+    dv.data, dv.storage_bytes = dd.buf.ptr + 4 * dst_offset, 4 * n_out
+    st = emel.lib().emel_cuda_get_rows_f32_bytes(ctx.handle, None, B(sv), B(di.c()), B(dv))
+    sync = emel.lib().emel_cuda_stream_synchronize(ctx.handle, None)
+    got = dd.download()[dst_offset:dst_offset + n_out]
+    want = np.full(n_out, fill, np.float32)
+    tail = src[offset:]
+    ost = olib.oracle_get_rows_f32_bytes(B(oracle.make_view(tail.ctypes.data, tail.nbytes, ne, nb, F32)), B(di.o()),
+                                         B(oracle.make_view(want.ctypes.data, want.nbytes, dne,
+                                                            contiguous_nb(dne), F32)))
+    for d in (ds, di, dd):
+        d.free()
+    return int(st), int(sync), ost, got, want
+
+
+def test_f32_bytes_reference_known_answers_on_the_device(emel, kern, oracle_lib):
+    src = np.zeros(17, np.uint8)
+    src[0:8] = np.array([1.0, 2.0], np.float32).view(np.uint8)
+    src[9:17] = np.array([3.0, 4.0], np.float32).view(np.uint8)
+    st, sync, ost, got, _ = run_bytes(emel, kern, oracle_lib, src, 0, [2, 2, 1, 1], [4, 9, 18, 18], [1, 0],
+                                      [2, 1, 1])
+    assert st == sync == ost == 0 and got.tolist() == [3.0, 4.0, 1.0, 2.0]
+    st, _, ost, got, _ = run_bytes(emel, kern, oracle_lib, src[:16], 0, [2, 2, 1, 1], [4, 9, 18, 18], [1, 0],
+                                   [2, 1, 1], fill=9.0)
+    assert st == ost == 1 and got.tolist() == [9.0] * 4
+
+
+@pytest.mark.parametrize("offset", [0, 1, 2, 3, 5, 16])
+@pytest.mark.parametrize("case", ["odd_row_stride", "aligned_rows", "batches", "padded_cols"])
+def test_f32_bytes_sources(emel, kern, oracle_lib, offset, case):
+    rng = np.random.default_rng(offset * 7 + len(case))
+    if case == "odd_row_stride":
+        ne, nb, idx_ne = [1001, 70, 1, 1], None, [90, 1, 1]
+        nb = [4, 4 * 1001 + 3, (4 * 1001 + 3) * 70, (4 * 1001 + 3) * 70]
+    elif case == "aligned_rows":
+        ne, idx_ne = [4096, 40, 1, 1], [64, 1, 1]
+        nb = [4, 4 * 4096 + 16, (4 * 4096 + 16) * 40, (4 * 4096 + 16) * 40]
+    elif case == "batches":
+        ne, idx_ne = [257, 9, 3, 2], [5, 3, 2]
+        nb = [4, 4 * 257 + 1, (4 * 257 + 1) * 9 + 7, ((4 * 257 + 1) * 9 + 7) * 3 + 5]
+    else:
+        ne, idx_ne = [64, 33, 1, 1], [48, 1, 1]
+        nb = [0, 0, 0, 0]  # implicit contiguous strides
+    if nb[0] == 0:
+        span = 4 * ne[0] * ne[1] * ne[2] * ne[3]
+    else:
+        span = sum((ne[d] - 1) * nb[d] for d in range(1, 4)) + 4 * ne[0]
+    # random words, NaN payloads and signed zeros included, at any byte offset
+    src = rng.integers(0, 256, size=offset + span, dtype=np.uint8)
+    idx = rng.integers(0, ne[1], size=int(np.prod(idx_ne))).astype(np.int32)
+    st, sync, ost, got, want = run_bytes(emel, kern, oracle_lib, src, offset, ne, nb, idx, idx_ne)
+    assert st == sync == ost == 0
+    bits_equal(got, want, f"f32 bytes {case} offset {offset}")
+
+
+def test_f32_bytes_unaligned_destination_rows(emel, kern, oracle_lib):
+    rng = np.random.default_rng(3)
+    ne, nb = [512, 20, 1, 1], [4, 2051, 2051 * 20, 2051 * 20]
+    src = rng.integers(0, 256, size=3 + 19 * 2051 + 2048, dtype=np.uint8)
+    idx = rng.integers(0, 20, size=30).astype(np.int32)
+    st, sync, ost, got, want = run_bytes(emel, kern, oracle_lib, src, 3, ne, nb, idx, [30, 1, 1], dst_offset=1)
+    assert st == sync == ost == 0
+    bits_equal(got, want, "f32 bytes, destination off a 16-byte boundary")
+
+
+@pytest.mark.parametrize("bad", [-1, 20])
+def test_f32_bytes_out_of_range_index_writes_nothing(emel, kern, oracle_lib, bad):
+    rng = np.random.default_rng(9)
+    ne, nb = [300, 20, 1, 1], [4, 1203, 1203 * 20, 1203 * 20]
+    src = rng.integers(0, 256, size=1 + 19 * 1203 + 1200, dtype=np.uint8)
+    idx = rng.integers(0, 20, size=16).astype(np.int32)
+    idx[11] = bad
+    st, sync, ost, got, _ = run_bytes(emel, kern, oracle_lib, src, 1, ne, nb, idx, [16, 1, 1])
+    assert st == 0 and sync == 9 and ost == 9 and np.all(got == 7.0)
+    assert emel.lib().emel_cuda_stream_synchronize(kern.ctx.handle, None) == 0
