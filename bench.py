@@ -639,6 +639,7 @@ def run_suite(args):
             if only and o.name not in only:
                 continue
             data, ne, nb, code = W.emb_table(fmt)
+            gather = lib.emel_cuda_get_rows_f32_bytes if fmt == "f32_bytes" else lib.emel_cuda_get_rows
             ttab = torch.from_numpy(data).to(dev)
             vtab = pkg.CView()
             vtab.data, vtab.storage_bytes, vtab.dtype = ttab.data_ptr(), ttab.numel(), code
@@ -648,7 +649,7 @@ def run_suite(args):
             touts = [torch.empty(W.EMB_TOKENS * W.EMB_COLS, device=dev) for _ in range(sets)]
             vouts = [view(t, [W.EMB_COLS, W.EMB_TOKENS, 1, 1]) for t in touts]
             measure("get_rows", o.name, o.bytes, o.elements,
-                    lambda k, vtab=vtab, vouts=vouts: (lambda: chk(lib.emel_cuda_get_rows(
+                    lambda k, vtab=vtab, vouts=vouts, fn=gather: (lambda: chk(fn(
                         ctx.handle, sh, B(vtab), B(vidx), B(vouts[k])))), sets)
             chk(lib.emel_cuda_stream_synchronize(ctx.handle, sh))
             del ttab, touts

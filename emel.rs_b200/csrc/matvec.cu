@@ -263,6 +263,8 @@ struct PackedBlock {
     uint32_t w[NW];
     bool odd;
 
+    // SHARED: `blk` points into a shared-memory staging window
+    template <bool SHARED = false>
     __device__ __forceinline__ void load(const uint8_t* blk) {
         odd = ((uintptr_t)blk & 3u) != 0;  // starts 2 bytes into a word
         const uint32_t* wp = reinterpret_cast<const uint32_t*>(blk - (odd ? 2 : 0));
@@ -270,9 +272,10 @@ struct PackedBlock {
 #pragma unroll
         for (int j = 0; j < NW; ++j) {
             if (4 * j + 4 <= end)
-                w[j] = __ldg(wp + j);
+                w[j] = SHARED ? wp[j] : __ldg(wp + j);
             else if (4 * j + 2 <= end)
-                w[j] = (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(wp + j));
+                w[j] = SHARED ? (uint32_t)*reinterpret_cast<const uint16_t*>(wp + j)
+                              : (uint32_t)__ldg(reinterpret_cast<const uint16_t*>(wp + j));
             else
                 w[j] = 0u;
         }
@@ -459,9 +462,22 @@ cudaError_t launch_packed(const LaunchEnv& env, const MvArgmaxPlan& p, const uin
 // order) and adds the lane sums to the total after the last block.
 constexpr int kKThreads = 128;
 constexpr int kKWarps = kKThreads / 32;
-constexpr int kKChunk = 16;                       // blocks per pass
 constexpr int kKTerms = 9;                        // eight lane terms + the minimum term
-constexpr int kKRowStride = kKChunk * kKTerms + 1;
+
+// Staging window of one block: the aligned words that hold its BB bytes
+// (a block may start 2 bytes into a word), at an odd word stride per row so
+// the lanes' word reads fall in distinct banks.
+template <int CODE>
+struct KWindow {
+    static constexpr int BB = CODE == kDtypeQ2_K ? 84 : CODE == kDtypeQ3_K ? 110 : CODE == kDtypeQ4_K ? 144 : 210;
+    static constexpr int NW = (BB + 2 + 3) / 4;
+    static constexpr int SW = NW | 1;
+    // 16-byte staging (16-byte aligned rows): the 16-byte chunks that hold
+    // the block's bytes, at an odd number of chunks per row
+    static constexpr int NC = (15 + BB + 15) / 16;
+    static constexpr int SW16 = 4 * (NC | 1);
+    static constexpr int SWM = SW > SW16 ? SW : SW16;
+};
 
 __device__ __forceinline__ int32_t q8k_nearest(float v) {
     return (int32_t)(__float_as_uint(__fadd_rn(v, 12582912.0f)) & 0x007fffffu) - 0x00400000;
@@ -472,7 +488,7 @@ __device__ __forceinline__ void q4k_block_terms(const uint32_t* w, const uint32_
                                                 float* o) {
     uint32_t W[36];
 #pragma unroll
-    for (int i = 0; i < 36; ++i) W[i] = __ldg(w + i);
+    for (int i = 0; i < 36; ++i) W[i] = w[i];  // shared-memory window
     // scales / minimums (dot_q4_k's unpacking)
     const uint32_t s0 = W[1], s1 = W[2], s2 = W[3];
     uint32_t sc[8], mn[8];
@@ -514,7 +530,7 @@ __device__ __forceinline__ void q4k_block_terms(const uint32_t* w, const uint32_
 // ops, and each lane sum's two positions of a 16-value group paired for dp4a.
 __device__ __forceinline__ void q6k_block_terms(const uint8_t* blk_ptr, const uint32_t* r4, float rdb, float* o) {
     PackedBlock<kDtypeQ6_K> blk;
-    blk.load(blk_ptr);
+    blk.load<true>(blk_ptr);
     int sums[8] = {0, 0, 0, 0, 0, 0, 0, 0};
 #pragma unroll
     for (int g = 0; g < 16; ++g) {
@@ -552,7 +568,7 @@ __device__ __forceinline__ void q2k_block_terms(const uint32_t* w, const uint32_
                                                 float* o) {
     uint32_t W[21];
 #pragma unroll
-    for (int i = 0; i < 21; ++i) W[i] = __ldg(w + i);
+    for (int i = 0; i < 21; ++i) W[i] = w[i];  // shared-memory window
     int sum_mins = 0;
 #pragma unroll
     for (int g = 0; g < 16; ++g) sum_mins += bs[g] * (int)((W[g >> 2] >> (8 * (g & 3) + 4)) & 0x0fu);
@@ -584,7 +600,7 @@ __device__ __forceinline__ void q2k_block_terms(const uint32_t* w, const uint32_
 // 16-value group paired for dp4a.
 __device__ __forceinline__ void q3k_block_terms(const uint8_t* blk_ptr, const uint32_t* r4, float rdb, float* o) {
     PackedBlock<kDtypeQ3_K> blk;
-    blk.load(blk_ptr);
+    blk.load<true>(blk_ptr);
     uint32_t a0 = blk.word(24), a1 = blk.word(25);
     const uint32_t tmp = blk.word(26);
     const uint32_t a2 = ((a0 >> 4) & 0x0f0f0f0fu) | (((tmp >> 4) & 0x03030303u) << 4);
@@ -621,7 +637,8 @@ __device__ __forceinline__ void q3k_block_terms(const uint8_t* blk_ptr, const ui
 }
 
 template <int CODE>
-__global__ void __launch_bounds__(kKThreads) mv_argmax_k(MvArgmaxPlan p, const uint8_t* lhs) {
+__global__ void __launch_bounds__(kKThreads, CODE == kDtypeQ6_K || CODE == kDtypeQ3_K ? 6 : 8)
+    mv_argmax_k(MvArgmaxPlan p, const uint8_t* lhs) {
     extern __shared__ __align__(16) uint32_t k_smem[];
     __shared__ MvPart warp_best[kKWarps];
     const uint32_t blocks = (uint32_t)(p.k / 256);
@@ -629,7 +646,9 @@ __global__ void __launch_bounds__(kKThreads) mv_argmax_k(MvArgmaxPlan p, const u
     float* rd = reinterpret_cast<float*>(rq + blocks * 64);          // [blocks] scales
     int* rb = reinterpret_cast<int*>(rd + blocks);                   // [blocks][16] group sums
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    float* tile = reinterpret_cast<float*>(rb + blocks * 16) + warp * 32 * kKRowStride;
+    using KW = KWindow<CODE>;
+    // [2][32 rows][SWM] staging windows, 16-byte aligned
+    uint32_t* stage = k_smem + ((blocks * 81u + 3u) & ~3u) + warp * 2 * 32 * KW::SWM;
     pdl_enter();
     for (uint32_t b = warp; b < blocks; b += kKWarps) {
         // lane l holds positions 8l .. 8l + 7
@@ -690,20 +709,70 @@ __global__ void __launch_bounds__(kKThreads) mv_argmax_k(MvArgmaxPlan p, const u
         if (lane == 0) rd[b] = d;
     }
     __syncthreads();
-    constexpr uint64_t BB = CODE == kDtypeQ2_K ? 84 : CODE == kDtypeQ3_K ? 110 : CODE == kDtypeQ4_K ? 144 : 210;
+    constexpr uint64_t BB = KW::BB;
     const uint64_t row_bytes = (uint64_t)blocks * BB;
+    // 16-byte aligned rows: block b sits at the same 16-byte offset in every
+    // row and every 16-byte chunk holding its bytes lies inside the tensor
+    const bool v16 = ((reinterpret_cast<uintptr_t>(lhs) | (uintptr_t)row_bytes) & 15u) == 0;
+    const uint32_t sw = v16 ? (uint32_t)KW::SW16 : (uint32_t)KW::SW;
     MvPart best{0.0f, 0, 0u, 0u};
+    // One lane per row.  The warp stages its rows' block windows in shared
+    // memory with asynchronous word copies (every word read holds bytes of
+    // the block; a trailing half word copies 2 bytes), block b + 1 in flight
+    // while block b is consumed; every lane forms its row's terms from the
+    // window and folds them in block order.
     for (uint64_t g0 = ((uint64_t)blockIdx.x * kKWarps + warp) * 32; g0 < p.rows;
          g0 += (uint64_t)gridDim.x * kKWarps * 32) {
         const uint32_t nrows = p.rows - g0 < 32u ? (uint32_t)(p.rows - g0) : 32u;
+        const uint8_t* group = lhs + g0 * row_bytes;
         float ls[8] = {0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f, 0.0f};
         float total = 0.0f;
-        for (uint32_t b0 = 0; b0 < blocks; b0 += kKChunk) {
-            const uint32_t nbc = blocks - b0 < (uint32_t)kKChunk ? blocks - b0 : (uint32_t)kKChunk;
-            for (uint32_t item = lane; item < nrows * nbc; item += 32) {
-                const uint32_t r = item / nbc, bl = item % nbc, b = b0 + bl;
-                const uint8_t* bp = lhs + (g0 + r) * row_bytes + (uint64_t)b * BB;
-                float* o = tile + r * kKRowStride + bl * kKTerms;
+        const auto issue = [&](uint32_t b) {
+            uint32_t* buf = stage + (b & 1u) * 32 * KW::SWM;
+            if (v16) {
+                const uint32_t off16 = (uint32_t)(((uint64_t)b * BB) & 15u);
+                const uint8_t* first = group + (uint64_t)b * BB - off16;
+                for (uint32_t v = lane; v < nrows * (uint32_t)KW::NC; v += 32) {
+                    const uint32_t r = v / KW::NC, c = v % KW::NC;
+                    if (16 * c < off16 + (uint32_t)BB) {
+                        const uint32_t dst = (uint32_t)__cvta_generic_to_shared(buf + r * KW::SW16 + 4 * c);
+                        const void* src = first + r * row_bytes + 16 * c;
+                        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+                    }
+                }
+                asm volatile("cp.async.commit_group;\n" ::: "memory");
+                return;
+            }
+            for (uint32_t v = lane; v < nrows * (uint32_t)KW::NW; v += 32) {
+                const uint32_t r = v / KW::NW, j = v % KW::NW;
+                const uintptr_t at = reinterpret_cast<uintptr_t>(group + r * row_bytes + (uint64_t)b * BB);
+                const uint32_t off = (uint32_t)(at & 3u);
+                const uint32_t end = off + (uint32_t)BB;
+                if (4 * j + 2 <= end) {
+                    const uint32_t bytes = 4 * j + 4 <= end ? 4u : 2u;
+                    const uint32_t dst = (uint32_t)__cvta_generic_to_shared(buf + r * KW::SW + j);
+                    const void* src = reinterpret_cast<const void*>(at - off + 4 * j);
+                    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(dst), "l"(src), "r"(bytes)
+                                 : "memory");
+                }
+            }
+            asm volatile("cp.async.commit_group;\n" ::: "memory");
+        };
+        __syncwarp();  // the previous group's readers are done with both buffers
+        issue(0);
+        for (uint32_t b = 0; b < blocks; ++b) {
+            if (b + 1 < blocks) {
+                issue(b + 1);
+                asm volatile("cp.async.wait_group 1;\n" ::: "memory");
+            } else {
+                asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+            }
+            __syncwarp();  // every lane's copies of block b are visible
+            if ((uint32_t)lane < nrows) {
+                const uintptr_t at = reinterpret_cast<uintptr_t>(group + lane * row_bytes + (uint64_t)b * BB);
+                const uint32_t off = v16 ? (uint32_t)(((uint64_t)b * BB) & 15u) : (uint32_t)(at & 3u);
+                const uint8_t* bp = reinterpret_cast<const uint8_t*>(stage + (b & 1u) * 32 * KW::SWM + lane * sw) + off;
+                float o[kKTerms];
                 if constexpr (CODE == kDtypeQ2_K)
                     q2k_block_terms(reinterpret_cast<const uint32_t*>(bp), rq + b * 64, rb + b * 16, rd[b], o);
                 else if constexpr (CODE == kDtypeQ3_K)
@@ -712,21 +781,15 @@ __global__ void __launch_bounds__(kKThreads) mv_argmax_k(MvArgmaxPlan p, const u
                     q4k_block_terms(reinterpret_cast<const uint32_t*>(bp), rq + b * 64, rb + b * 16, rd[b], o);
                 else
                     q6k_block_terms(bp, rq + b * 64, rd[b], o);
-            }
-            __syncwarp();
-            if ((uint32_t)lane < nrows) {
-                const float* t = tile + lane * kKRowStride;
-                for (uint32_t bl = 0; bl < nbc; ++bl) {
-                    if constexpr (CODE == kDtypeQ2_K) {
-                        total = __fadd_rn(total, t[bl * kKTerms + 8]);
-                    } else {
+                if constexpr (CODE == kDtypeQ2_K) {
+                    total = __fadd_rn(total, o[8]);
+                } else {
 #pragma unroll
-                        for (int j = 0; j < 8; ++j) ls[j] = __fadd_rn(ls[j], t[bl * kKTerms + j]);
-                        if constexpr (CODE == kDtypeQ4_K) total = __fsub_rn(total, t[bl * kKTerms + 8]);
-                    }
+                    for (int j = 0; j < 8; ++j) ls[j] = __fadd_rn(ls[j], o[j]);
+                    if constexpr (CODE == kDtypeQ4_K) total = __fsub_rn(total, o[8]);
                 }
             }
-            __syncwarp();
+            __syncwarp();  // block b's readers are done before its buffer is refilled
         }
         if ((uint32_t)lane < nrows) {
             if constexpr (CODE != kDtypeQ2_K) {
@@ -822,8 +885,7 @@ cudaError_t launch_mul_mat_argmax(const LaunchEnv& env, const MvArgmaxPlan& p) {
 template <int CODE>
 cudaError_t launch_k(const LaunchEnv& env, const MvArgmaxPlan& p, const uint8_t* lhs) {
     const uint64_t groups = (p.rows + kKWarps * 32 - 1) / (kKWarps * 32);
-    const uint64_t cap = (uint64_t)env.sm_count * 3;
-    const size_t table = (size_t)kKWarps * 32 * kKRowStride * 4;
+    const size_t table = (size_t)kKWarps * 2 * 32 * KWindow<CODE>::SWM * 4 + 16;  // staging windows + alignment
     const size_t smem = (size_t)(p.k / 256) * (64 * 4 + 4 + 16 * 4) + table;
     static int configured_device_mask = 0;
     const int bit = env.device < 31 ? (1 << env.device) : 0;
@@ -833,6 +895,17 @@ cudaError_t launch_k(const LaunchEnv& env, const MvArgmaxPlan& p, const uint8_t*
         if (e != cudaSuccess) return e;
         configured_device_mask |= bit;
     }
+    // one wave of resident CTAs (registers or shared memory decide how many)
+    static size_t cached_smem = 0;
+    static int cached_ctas = 1;
+    if (smem != cached_smem) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, mv_argmax_k<CODE>, kKThreads, smem) != cudaSuccess || n < 1)
+            n = 1;
+        cached_smem = smem;
+        cached_ctas = n;
+    }
+    const uint64_t cap = (uint64_t)env.sm_count * cached_ctas;
     const cudaError_t err = launch_dependent(mv_argmax_k<CODE>, dim3((unsigned)(groups < cap ? groups : cap)),
                                              dim3(kKThreads), smem, env.stream, p, lhs);
     ++*env.launches;

@@ -207,9 +207,12 @@ def glu_spec():
 # Row gather (get_rows.rs) -- no configuration in the benchmark set names it;
 # the bench suite gathers 8192 token rows from a [4096, 32000] embedding
 # table stored as F32, F16, BF16, Q8_0, Q4_0 and Q4_K (random block bytes
-# with binary16 scales in [2^-7, 1)).
+# with binary16 scales in [2^-7, 1)), plus the byte-backed F32 table of
+# OpGetRowsF32Bytes with a row stride of 4 * 4096 + 1 bytes, so successive
+# rows start at every byte offset modulo 4.
 EMB_COLS, EMB_ROWS, EMB_TOKENS = 4096, 32000, 8192
-EMB_FORMATS = {"f32": (0, 4, 1, 4), "f16": (1, 2, 1, 2), "bf16": (30, 2, 1, 2),
+EMB_BYTES_STRIDE = 4 * EMB_COLS + 1
+EMB_FORMATS = {"f32": (0, 4, 1, 4), "f32_bytes": (0, 4, 1, 4), "f16": (1, 2, 1, 2), "bf16": (30, 2, 1, 2),
                "q8_0": (8, 34, 32, 0), "q4_0": (2, 18, 32, 0), "q4_k": (12, 144, 256, 0)}
 
 
@@ -225,6 +228,13 @@ def emb_table(fmt, seed=11):
     row_bytes = emb_row_bytes(fmt)
     if fmt == "f32":
         data = rng.standard_normal(EMB_COLS * EMB_ROWS).astype(np.float32).view(np.uint8)
+    elif fmt == "f32_bytes":
+        rows = rng.standard_normal(EMB_COLS * EMB_ROWS).astype(np.float32).view(np.uint8).reshape(EMB_ROWS, -1)
+        data = np.zeros((EMB_ROWS, EMB_BYTES_STRIDE), np.uint8)
+        data[:, :row_bytes] = rows
+        data = data.reshape(-1)
+        ne = [EMB_COLS, EMB_ROWS, 1, 1]
+        return data, ne, [4, EMB_BYTES_STRIDE, EMB_BYTES_STRIDE * EMB_ROWS, EMB_BYTES_STRIDE * EMB_ROWS], code
     elif fmt in ("f16", "bf16"):
         x = rng.standard_normal(EMB_COLS * EMB_ROWS).astype(np.float32)
         h = x.astype(np.float16).view(np.uint16) if fmt == "f16" else (x.view(np.uint32) >> 16).astype(np.uint16)
