@@ -140,7 +140,30 @@ __global__ void __launch_bounds__(kGatherThreads) gather_plain(GatherPlan p) {
             // shift; every word read holds at least one byte of the row.
             const uintptr_t a = reinterpret_cast<uintptr_t>(row);
             const uint32_t sh = (uint32_t)(a & 3u) * 8u;
-            if (sh == 0) {
+            if (p.vec) {
+                // 16-byte destination vectors: output vector v is bytes
+                // [16v, 16v + 16) of the row, held by aligned source chunks v
+                // and v + 1 (the row is off a 16-byte boundary, so both hold
+                // bytes of the row); rotate by (a & 15) / 4 words, then funnel.
+                const uint4* base = reinterpret_cast<const uint4*>(a & ~(uintptr_t)15);
+                const uint32_t q = (uint32_t)(a & 15u) >> 2;
+                const uint64_t nv = cols / 4;
+                for (uint64_t v = threadIdx.x; v < nv; v += kGatherThreads) {
+                    const uint4 x = __ldg(base + v), y = __ldg(base + v + 1);
+                    uint32_t w[8] = {x.x, x.y, x.z, x.w, y.x, y.y, y.z, y.w};
+                    if (q & 2u) {
+#pragma unroll
+                        for (int i = 0; i < 6; ++i) w[i] = w[i + 2];
+                    }
+                    if (q & 1u) {
+#pragma unroll
+                        for (int i = 0; i < 7; ++i) w[i] = w[i + 1];
+                    }
+                    __stcs(reinterpret_cast<uint4*>(out) + v,
+                           make_uint4(__funnelshift_r(w[0], w[1], sh), __funnelshift_r(w[1], w[2], sh),
+                                      __funnelshift_r(w[2], w[3], sh), __funnelshift_r(w[3], w[4], sh)));
+                }
+            } else if (sh == 0) {
                 const float* in = reinterpret_cast<const float*>(row);
                 for (uint64_t c = threadIdx.x; c < cols; c += kGatherThreads) out[c] = in[c];
             } else {

@@ -235,7 +235,7 @@ def test_f32_bytes_reference_known_answers_on_the_device(emel, kern, oracle_lib)
     assert st == ost == 1 and got.tolist() == [9.0] * 4
 
 
-@pytest.mark.parametrize("offset", [0, 1, 2, 3, 5, 16])
+@pytest.mark.parametrize("offset", [0, 1, 2, 3, 5, 9, 14, 16])
 @pytest.mark.parametrize("case", ["odd_row_stride", "aligned_rows", "batches", "padded_cols"])
 def test_f32_bytes_sources(emel, kern, oracle_lib, offset, case):
     rng = np.random.default_rng(offset * 7 + len(case))
