@@ -1,20 +1,22 @@
 """Benchmark of the emel-kernels hot path on B200.
 
-Default workload (configuration 2 of the benchmark set): the unary /
-activation sweep -- silu, gelu (tanh approximation), relu, exp, neg, sqr,
-sqrt and pow(x, 2) -- over f32 and f16 tensors of ne = [14336, 512].  One
-step = those 16 ops once.  Metric: achieved HBM GB/s (algorithmic bytes:
-every input element read once, every output element written once).
+Default workload (configuration 5 of the benchmark set): src0 f32
+ne = [128, 32, 8192, 8] (1.07 GB) stored as a view with dims 1 and 2
+swapped, split along dim 3 across the GPUs (strong scaling: the tensor is
+fixed, each of N GPUs holds 8/N slices); src1 ne = [128, 1, 8192, 1]
+replicated.  One step = whole-tensor sum and argmax, repeat-broadcast mul
+and add; with N > 1 the per-shard sum / argmax partials are exchanged over
+NVLink and combined on the device.  Metric: achieved HBM GB/s (algorithmic
+bytes: every input element read once, every output element written once,
+per op; ops run one after another on one stream).
 
     python bench.py [--gpus N --steps K --warmup W]       # B200 device table
     python bench.py --impl reference ...                   # CPU reference lane
     python bench.py --suite                                # per-op lines, all configs
-    python bench.py --workload cfg5 [--gpus N]             # config 5 sharded, strong scaling
+    python bench.py --workload cfg2 [--gpus N]             # configuration 2 sweep, weak scaling
 
-Multi-GPU (torchrun, one process per GPU): every rank runs the same
-per-GPU workload on its own seeded data (weak scaling, no collective on the
-data path); the timed region is bracketed by barriers and the max over
-ranks is reported.
+Multi-GPU (torchrun, one process per GPU): the timed region is bracketed by
+barriers and the max over ranks is reported.
 """
 
 import argparse
@@ -769,12 +771,143 @@ def run_suite(args):
 # ---------------------------------------------------------------------------
 # Configuration 5 sharded over the GPUs (strong scaling)
 # ---------------------------------------------------------------------------
+class Cfg5Shard:
+    """This rank's dim-3 slices [b, e) of configuration 5's src0 (the
+    dims-1/2-swapped view of contiguous [128, 8192, 32, 8]), the replicated
+    src1 [128, 1, 8192, 1], the two repeat-broadcast outputs and the
+    whole-tensor answers, all in device memory."""
+
+    def __init__(self, pkg, ctx, torch, device, world, rank):
+        from emel_rs_b200 import distributed as D
+        from emel_rs_b200 import workloads as W
+
+        self.pkg, self.ctx, self.torch, self.world, self.rank = pkg, ctx, torch, world, rank
+        self.lib = pkg.lib()
+        self.b, self.e = D.shard_bounds(W.CFG5_NE[3], world, rank)
+        parts, s1 = [], None
+        for j in range(self.b, self.e):
+            s0, s1 = W.cfg5(ne3=1, shard=j)
+            parts.append(s0)
+        if s1 is None:  # more ranks than slices: this rank holds nothing
+            _, s1 = W.cfg5(ne3=1, shard=0)
+        self.host0 = np.concatenate(parts) if parts else np.empty(0, np.float32)
+        self.host1 = s1
+        self.src0 = torch.from_numpy(self.host0).to(device)
+        self.src1 = torch.from_numpy(s1).to(device)
+        self.ne, self.nb = W.cfg5_src0_view(ne3=self.e - self.b)
+        self.mul_out = torch.empty_like(self.src0)
+        self.add_out = torch.empty_like(self.src0)
+        # exchange payload: the shard's f64 sum, then its argmax partial
+        self.partial = torch.zeros(32, dtype=torch.uint8, device=device)
+        self.gathered = torch.zeros(max(1, world) * 32, dtype=torch.uint8, device=device)
+        self.sum_out = torch.zeros(1, dtype=torch.float32, device=device)
+        self.idx_out = torch.zeros(1, dtype=torch.int64, device=device)
+        self.v0 = self.view(self.src0, self.ne, self.nb)
+        self.v1 = self.view(self.src1, [128, 1, 8192, 1])
+        self.vm = self.view(self.mul_out, self.ne)
+        self.va = self.view(self.add_out, self.ne)
+        self.vsum = self.view(self.sum_out, [1, 1, 1, 1])
+        self.vidx = self.view(self.idx_out, [1, 1, 1, 1], code=27)
+        self.plane = self.ne[0] * self.ne[1] * self.ne[2]
+        self.exchange = None
+        n = 128 * 32 * 8192 * 8
+        # algorithmic bytes of one step over the whole tensor (every rank's
+        # shard): repeat mul and repeat add read src0 and src1 and write dst;
+        # sum and argmax read src0
+        self.op_bytes = {"repeat_mul": 2 * n * 4 + 128 * 8192 * 4, "repeat_add": 2 * n * 4 + 128 * 8192 * 4,
+                         "sum": n * 4, "argmax": n * 4}
+        self.step_bytes = sum(self.op_bytes.values())
+        self.elements = n
+
+    def view(self, t, vne, vnb=None, code=0):
+        v = self.pkg.CView()
+        v.data = t.data_ptr()
+        v.storage_bytes = t.numel() * t.element_size()
+        vnb = vnb or self.pkg.contiguous_nb(vne, code)
+        for d in range(4):
+            v.ne[d], v.nb[d] = vne[d], vnb[d]
+        v.dtype = code
+        return v
+
+    def connect(self, dist):
+        from emel_rs_b200 import distributed as D
+        if self.world > 1:
+            self.exchange = D.PeerExchange(self.pkg, self.ctx, dist, self.world, self.rank)
+
+    def _ok(self, st, what):
+        if st != 0:
+            raise RuntimeError(f"{what}: status {st}: {self.ctx.last_error}")
+
+    def step(self, sh):
+        """One step on stream `sh`.  One GPU: OpSum, OpArgmax (exact i64
+        index), repeat mul, repeat add.  N GPUs: the shard's f64 sum and
+        argmax partial, published to every rank over NVLink before the two
+        repeat broadcasts stream, then one wait that gathers every rank's
+        partials and combines them on the device."""
+        lib, h, B = self.lib, self.ctx.handle, ctypes.byref
+        if self.exchange is None:
+            self._ok(lib.emel_cuda_sum(h, sh, B(self.v0), B(self.vsum)), "sum")
+            self._ok(lib.emel_cuda_argmax(h, sh, B(self.v0), B(self.vidx)), "argmax")
+        else:
+            p = self.partial.data_ptr()
+            self._ok(lib.emel_cuda_sum_f64(h, sh, B(self.v0), ctypes.c_void_p(p)), "sum_f64")
+            self._ok(lib.emel_cuda_argmax_partial_compute(h, sh, B(self.v0), self.b * self.plane,
+                                                          ctypes.c_void_p(p + 8)), "argmax partial")
+            self.exchange.publish(sh, p)
+        self._ok(lib.emel_cuda_binary_repeat(h, sh, 2, B(self.v0), B(self.v1), B(self.vm)), "repeat mul")
+        self._ok(lib.emel_cuda_binary_repeat(h, sh, 0, B(self.v0), B(self.v1), B(self.va)), "repeat add")
+        if self.exchange is not None:
+            self._ok(lib.emel_cuda_exchange_wait_sum_argmax(h, sh, self.exchange.handle,
+                                                            ctypes.c_void_p(self.gathered.data_ptr()),
+                                                            B(self.vsum), B(self.vidx)), "exchange wait")
+
+    def answers(self):
+        return float(self.sum_out.cpu()[0]), int(self.idx_out.cpu()[0])
+
+    def calibration(self, stream, reps):
+        """Per-op graphs: each op `reps` times back to back between two timed
+        events, alternating between two copies of the shard so no launch
+        finds its input in L2.  Returns (op, shard bytes, reps, graph, e0, e1)."""
+        torch, pkg, lib, h, B = self.torch, self.pkg, self.lib, self.ctx.handle, ctypes.byref
+        self.src0b = self.src0.clone()
+        v0b = self.view(self.src0b, self.ne, self.nb)
+        self._idx_scratch = torch.zeros(1, dtype=torch.int64, device=self.src0.device)
+        sidx = self.view(self._idx_scratch, [1, 1, 1, 1], code=27)
+        srcs, outs_m, outs_a = (self.v0, v0b), (self.vm, self.va), (self.va, self.vm)
+        shard_bytes = {k: v * (self.e - self.b) // 8 for k, v in self.op_bytes.items()}
+        ops = {
+            "repeat_mul": lambda k: lib.emel_cuda_binary_repeat(h, stream.handle, 2, B(srcs[k % 2]), B(self.v1),
+                                                                B(outs_m[k % 2])),
+            "repeat_add": lambda k: lib.emel_cuda_binary_repeat(h, stream.handle, 0, B(srcs[k % 2]), B(self.v1),
+                                                                B(outs_a[k % 2])),
+            "sum": lambda k: lib.emel_cuda_sum(h, stream.handle, B(srcs[k % 2]), B(self.vsum)),
+            "argmax": lambda k: lib.emel_cuda_argmax(h, stream.handle, B(srcs[k % 2]), B(sidx)),
+        }
+        out = []
+        for name, fn in ops.items():
+            e0, e1 = pkg.CudaEvent(self.ctx), pkg.CudaEvent(self.ctx)
+            g = pkg.Graph(self.ctx, stream)
+            with g:
+                e0.record_timed(stream.handle)
+                for k in range(reps):
+                    self._ok(fn(k), name)
+                e1.record_timed(stream.handle)
+            out.append((name, shard_bytes[name], reps, g, e0, e1))
+        return out
+
+    def close(self):
+        if self.exchange is not None:
+            self.exchange.close()
+            self.exchange = None
+
+
 def run_cfg5(args, world, rank, local):
-    """The 1.07 GB permuted tensor of configuration 5 split along dim 3
-    across the ranks (total work fixed: strong scaling).  One step = repeat
-    mul and repeat add with the replicated src1, then the whole-tensor sum
-    and argmax as per-shard partials all-gathered over NCCL (the only
-    communication) and combined in rank order on every rank."""
+    """Configuration 5, the default workload: the 1.07 GB permuted tensor
+    split along dim 3 across the ranks (total work fixed: strong scaling).
+    One step = whole-tensor sum and argmax, repeat mul and repeat add with
+    the replicated src1, captured as one CUDA graph; with N GPUs the per-shard
+    partials cross NVLink through the library's peer exchange and are
+    combined on the device."""
     import torch
     import torch.distributed as dist
     from datetime import timedelta
@@ -784,71 +917,19 @@ def run_cfg5(args, world, rank, local):
     if world > 1:
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
     pkg = load_package()
-    from emel_rs_b200 import distributed as D
-    from emel_rs_b200 import workloads as W
-
-    lib = pkg.lib()
     ctx = pkg.Context(local)
     stream = pkg.Stream(ctx)
     sh = stream.handle
-    b, e = D.shard_bounds(W.CFG5_NE[3], world, rank)
-    parts = []
-    s1 = None
-    for j in range(b, e):
-        s0, s1 = W.cfg5(ne3=1, shard=j)
-        parts.append(torch.from_numpy(s0))
-    src0 = torch.cat(parts).to(device) if parts else torch.empty(0, device=device)
-    src1 = torch.from_numpy(s1).to(device)
-    ne, nb = W.cfg5_src0_view(ne3=e - b)
-    mul_out = torch.empty_like(src0)
-    add_out = torch.empty_like(src0)
-    # one 32-byte partial per rank: the f64 sum, then the argmax partial
-    partial = torch.zeros(32, dtype=torch.uint8, device=device)
-    acc = partial[0:8].view(torch.float64)
-    part = partial[8:32]
-    gathered = torch.empty(world * 32, dtype=torch.uint8, device=device)
+    shard = Cfg5Shard(pkg, ctx, torch, device, world, rank)
+    shard.connect(dist)
     torch.cuda.synchronize()
-
-    def view(t, vne, vnb=None):
-        v = pkg.CView()
-        v.data = t.data_ptr()
-        v.storage_bytes = t.numel() * t.element_size()
-        vnb = vnb or pkg.contiguous_nb(vne)
-        for d in range(4):
-            v.ne[d], v.nb[d] = vne[d], vnb[d]
-        v.dtype = 0
-        return v
-
-    v0, v1 = view(src0, ne, nb), view(src1, [128, 1, 8192, 1])
-    vm, va = view(mul_out, ne), view(add_out, ne)
-    B = ctypes.byref
-    plane = ne[0] * ne[1] * ne[2]
-    exchange = D.PeerExchange(pkg, ctx, dist, world, rank) if world > 1 else None
-
-    def call(st):
-        if st != 0:
-            raise RuntimeError(ctx.last_error)
-
-    def step():
-        # partials first: their exchange over NVLink (peer stores) lands while
-        # the two repeat broadcasts stream; the wait at the end gathers them
-        call(lib.emel_cuda_sum_f64(ctx.handle, sh, B(v0), ctypes.c_void_p(acc.data_ptr())))
-        call(lib.emel_cuda_argmax_partial_compute(ctx.handle, sh, B(v0), b * plane, ctypes.c_void_p(part.data_ptr())))
-        if exchange:
-            exchange.publish(sh, partial.data_ptr())
-        call(lib.emel_cuda_binary_repeat(ctx.handle, sh, 2, B(v0), B(v1), B(vm)))
-        call(lib.emel_cuda_binary_repeat(ctx.handle, sh, 0, B(v0), B(v1), B(va)))
-        if exchange:
-            exchange.wait(sh, gathered.data_ptr())
 
     for _ in range(args.warmup):
-        step()
+        shard.step(sh)
     stream.synchronize()
-    torch.cuda.synchronize()
-    # the step (six kernels) replayed as one CUDA graph
     graph = pkg.Graph(ctx, stream)
     with graph:
-        step()
+        shard.step(sh)
     for _ in range(3):
         graph.launch()
     stream.synchronize()
@@ -856,50 +937,309 @@ def run_cfg5(args, world, rank, local):
     if world > 1:
         dist.barrier()
     t0, t1 = pkg.CudaEvent(ctx), pkg.CudaEvent(ctx)
-    stream.synchronize()
+    launches_before = ctx.launches
     with ClockSampler(local) as clocks:
         t0.record(sh)
         for _ in range(args.steps):
             graph.launch()
         t1.record(sh)
         stream.synchronize()
-        torch.cuda.synchronize()
+    gpu_launches = ctx.launches - launches_before
     ms = t0.elapsed_ms(t1) / args.steps
+    ms_t = torch.tensor([ms], dtype=torch.float64, device=device)
     if world > 1:
-        t = torch.tensor([ms], dtype=torch.float64, device=device)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        ms = float(t.item())
-    # combined answers (rank order) from the last step
-    raw = (gathered if world > 1 else partial).cpu().numpy().tobytes()
-    total32, index = D.combine_gathered(pkg, raw, world)
-    n = 128 * 32 * 8192 * 8
-    step_bytes = 2 * (2 * n * 4 + 128 * 8192 * 4) + 2 * n * 4
+        dist.all_reduce(ms_t, op=dist.ReduceOp.MAX)
+    ms = float(ms_t.item())
+    total32, index = shard.answers()
+
+    # per-op kernel time on this rank's shard, right after the timed region
+    reps = 8
+    per_op = {}
+    for name, nbytes, r, g, e0, e1 in shard.calibration(stream, reps):
+        d = []
+        for _ in range(3):
+            g.launch()
+            stream.synchronize()
+            d.append(e0.elapsed_ms(e1) / r)
+        g.close()
+        per_op[name] = (nbytes, statistics.median(d))
+    e2e = None if args.no_e2e else run_cfg5_e2e(args, pkg, ctx, torch, shard, stream, world)
+    graph.close()
+    cfg2_ops = None
+    if world == 1 and not args.no_cfg2:
+        cfg2_ops = cfg2_per_op(pkg, ctx, torch, device, stream)
+
     if rank == 0:
-        value = step_bytes / (ms / 1e3) / 1e9
-        print(json.dumps({
+        peak, peak_kind = peaks()
+        dom_name, (dom_bytes, dom_ms) = max(per_op.items(), key=lambda kv: kv[1][1])
+        kernel_ms = sum(t for _, t in per_op.values())
+        achieved = dom_bytes / (dom_ms / 1e3) / 1e9
+        traffic = profile_traffic("ew_rows_vec_cfg5_repeat_ncu.md")
+        if traffic is not None:
+            traffic = traffic * (shard.e - shard.b) // 8  # the profile covers the whole 8-slice tensor
+        value = shard.step_bytes / (ms / 1e3) / 1e9
+        line = {
             "metric": METRIC, "value": round(value, 2), "unit": UNIT, "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded per dim-3 slice)",
-            "config": {"workload": "cfg5 sharded: src0 [128,32,8192,8] (dims 1/2 swapped view) split along dim 3; "
-                                   "repeat mul + repeat add with replicated src1 [128,1,8192,1], whole sum and "
-                                   "argmax as per-shard partials exchanged by peer stores over NVLink (library "
-                                   "kernels, no collective library; one CUDA graph per step)",
-                       "bytes_per_step": step_bytes, "l2": "inputs 1.07 GB / N per GPU, larger than L2 up to N=8",
-                       "parallelism": f"dim-3 shards over {world} GPU(s)"},
-            "result": {"sum": float(total32), "argmax": int(index)},
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded per dim-3 slice, N(0,1))",
+            "config": {"workload": "cfg5: src0 f32 ne=[128,32,8192,8] stored as a view with dims 1 and 2 swapped "
+                                   "(1.07 GB), split along dim 3 across the GPUs; src1 ne=[128,1,8192,1] "
+                                   "replicated; one step = whole-tensor sum + argmax (exact i64 index), repeat "
+                                   "mul, repeat add, one CUDA graph, ops serial on one stream; with N>1 the "
+                                   "per-shard partials cross NVLink by peer stores (library kernels) and are "
+                                   "combined on the device",
+                       "bytes_per_step": shard.step_bytes, "elements": shard.elements,
+                       "l2": "inputs larger than L2: the shard (1.07 GB / N) plus its two outputs exceed the "
+                             "126 MB L2 at every N up to 8",
+                       "parallelism": f"dim-3 shards over {world} GPU(s)",
+                       "slices_per_gpu": shard.e - shard.b},
+            "result": {"sum": total32, "argmax": index},
+            "roofline": {"bound": "hbm", "kernel": f"ew_rows_vec ({dom_name})" if dom_name.startswith("repeat")
+                         else dom_name, "achieved": round(achieved, 1), "peak": peak,
+                         "peak_source": f"{peak_kind} hbm_gbs (burst copy)", "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "traffic": traffic,
+                         "algorithmic_bytes_per_launch": dom_bytes, "launch_ms": round(dom_ms, 5),
+                         "share_of_step": round(dom_ms / kernel_ms, 4)},
+            "per_op_gbs": {k: round(b / (t / 1e3) / 1e9, 1) for k, (b, t) in per_op.items()},
+            "per_op_us": {k: round(t * 1e3, 2) for k, (_, t) in per_op.items()},
+            "e2e": e2e,
+            "gpu_launches": gpu_launches,
             "clocks": clocks.summary(),
-        }), flush=True)
-    graph.close()
+        }
+        if cfg2_ops is not None:
+            line["cfg2_per_op_gbs"] = cfg2_ops
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline_cfg5(args)
+        print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()  # every rank's last wait is done: the peer buffers may go
-        exchange.close()
+        shard.close()
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_cfg5_e2e(args, pkg, ctx, torch, shard, stream, world):
+    """The same step through the C ABI with host buffers: every step copies
+    this rank's src0 shard and src1 from pinned host memory, runs the step,
+    and reads both outputs and the two whole-tensor answers back into pinned
+    host memory.  Copies in and out run on their own streams so one step's
+    upload overlaps the previous step's download (PCIe is full duplex);
+    the step's kernels wait for its upload and for the previous download
+    of the outputs they overwrite."""
+    lib, h = pkg.lib(), ctx.handle
+    up, down = pkg.Stream(ctx), pkg.Stream(ctx)
+    sh = stream.handle
+    hs0 = torch.from_numpy(shard.host0).pin_memory()
+    hs1 = torch.from_numpy(shard.host1).pin_memory()
+    hm = torch.empty(shard.mul_out.shape, dtype=torch.float32, pin_memory=True)
+    ha = torch.empty(shard.add_out.shape, dtype=torch.float32, pin_memory=True)
+    hsum = torch.empty(1, dtype=torch.float32, pin_memory=True)
+    hidx = torch.empty(1, dtype=torch.int64, pin_memory=True)
+    ins = [(shard.src0, hs0), (shard.src1, hs1)]
+    outs = [(hm, shard.mul_out), (ha, shard.add_out), (hsum, shard.sum_out), (hidx, shard.idx_out)]
+    h2d = sum(t.numel() * t.element_size() for _, t in ins)
+    d2h = sum(t.numel() * t.element_size() for t, _ in outs)
+    uploaded, computed, downloaded = pkg.CudaEvent(ctx), pkg.CudaEvent(ctx), pkg.CudaEvent(ctx)
+    first = [True]
+
+    def one():
+        if not first[0]:
+            up.wait(computed)  # the previous step has read src0
+        for d, hh in ins:
+            st = lib.emel_cuda_memcpy_h2d(h, up.handle, d.data_ptr(), hh.data_ptr(), hh.numel() * hh.element_size())
+            if st != 0:
+                raise RuntimeError(ctx.last_error)
+        uploaded.record(up.handle)
+        stream.wait(uploaded)
+        if not first[0]:
+            stream.wait(downloaded)  # the previous step's outputs are home
+        shard.step(sh)
+        computed.record(sh)
+        down.wait(computed)
+        for hh, d in outs:
+            st = lib.emel_cuda_memcpy_d2h(h, down.handle, hh.data_ptr(), d.data_ptr(), hh.numel() * hh.element_size())
+            if st != 0:
+                raise RuntimeError(ctx.last_error)
+        downloaded.record(down.handle)
+        first[0] = False
+
+    steps = max(3, min(args.steps, 10))
+    for _ in range(2):
+        one()
+    up.synchronize()
+    down.synchronize()
+    stream.synchronize()
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+    t0, t1 = pkg.CudaEvent(ctx), pkg.CudaEvent(ctx)
+    t0.record(sh)
+    up.wait(t0)
+    for _ in range(steps):
+        one()
+    stream.wait(downloaded)
+    t1.record(sh)
+    stream.synchronize()
+    ms = t0.elapsed_ms(t1)
+    if world > 1:
+        import torch.distributed as dist
+        m = torch.tensor([ms], dtype=torch.float64, device=shard.src0.device)
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        ms = float(m.item())
+    got = (float(hsum[0]), int(hidx[0]))
+    up.close()
+    down.close()
+    value = steps * shard.step_bytes / (ms / 1e3) / 1e9
+    return {"value": round(value, 2), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "steps": steps, "result": {"sum": got[0], "argmax": got[1]},
+            "path": "per step: emel_cuda_memcpy_h2d of the src0 shard and src1 (pinned host) on an upload stream, "
+                    "the step's entry points, emel_cuda_memcpy_d2h of both outputs, the sum and the argmax on a "
+                    "download stream (per-rank bytes; upload of step s+1 overlaps download of step s)"}
+
+
+def cfg2_per_op(pkg, ctx, torch, device, stream):
+    """Configuration 2's 16 unary ops, one GB/s figure each (every op over
+    eight distinct buffer pairs of its dtype, back to back, between two
+    events)."""
+    step = Cfg2Step(pkg, ctx, torch, device, seed=2)
+    torch.cuda.synchronize()
+    out = {}
+    for name, nbytes, reps, g, e0, e1 in step.calibration_graphs(stream):
+        d = []
+        for _ in range(3):
+            g.launch()
+            stream.synchronize()
+            d.append(e0.elapsed_ms(e1) / reps)
+        g.close()
+        out[name] = round(nbytes / (statistics.median(d) / 1e3) / 1e9, 1)
+    return out
 
 
 # ---------------------------------------------------------------------------
 # CPU lanes (the oracle: C restatement of the reference loops)
 # ---------------------------------------------------------------------------
+class Cfg5Sample:
+    """A bounded CPU sample of configuration 5: dim-2 rows [0, rows) of
+    dim-3 slice 0 of src0 (the same permuted view), the matching rows of
+    src1, and dense outputs; each part [r0, r1) of the rows is one
+    independent unit of the four ops (repeat mul, repeat add, f64 sum,
+    argmax with its ordinal base)."""
+
+    def __init__(self, rows):
+        sys.path.insert(0, str(ROOT / "oracle"))
+        import oracle
+        load_package()  # the seeded input generator lives in the package
+        from emel_rs_b200 import workloads as W
+        self.oracle = oracle
+        self.lib = oracle.load()
+        self.rows = rows
+        s0, s1 = W.cfg5(ne3=1, shard=0)
+        self.s0 = np.ascontiguousarray(s0)
+        self.s1 = np.ascontiguousarray(s1)
+        self.mul = np.empty((rows, 32, 128), np.float32)
+        self.add = np.empty((rows, 32, 128), np.float32)
+
+    def bytes_of(self, rows):
+        n = rows * 32 * 128
+        return 2 * (2 * n * 4 + rows * 128 * 4) + 2 * n * 4
+
+    def run(self, r0, r1):
+        """The four ops on rows [r0, r1); returns (f64 sum, (value, index, has))."""
+        o, L, B = self.oracle, self.lib, ctypes.byref
+        s = r1 - r0
+        nb0 = [4, 4 * 128 * 8192, 512, 4 * 128 * 8192 * 32]
+        base0 = self.s0.ctypes.data + r0 * 512
+        span0 = self.s0.nbytes - r0 * 512
+        v0 = o.make_view(base0, span0, [128, 32, s, 1], nb0, 0)
+        v1 = o.make_view(self.s1.ctypes.data + r0 * 512, (8192 - r0) * 512, [128, 1, s, 1], [4, 512, 512, 512 * s], 0)
+        out_nb = [4, 512, 512 * 32, 512 * 32 * s]
+        vm = o.make_view(self.mul.ctypes.data + r0 * 32 * 512, s * 32 * 512, [128, 32, s, 1], out_nb, 0)
+        va = o.make_view(self.add.ctypes.data + r0 * 32 * 512, s * 32 * 512, [128, 32, s, 1], out_nb, 0)
+        assert L.oracle_binary_repeat(2, B(v0), B(v1), B(vm)) == 0
+        assert L.oracle_binary_repeat(0, B(v0), B(v1), B(va)) == 0
+        acc = ctypes.c_double()
+        assert L.oracle_sum_f64(B(v0), B(acc)) == 0
+        idx, val = ctypes.c_int64(), ctypes.c_float()
+        assert L.oracle_argmax_index(B(v0), B(idx), B(val)) == 0
+        return acc.value, (val.value, idx.value + r0 * 32 * 128)
+
+
+def cpu_baseline_cfg5(args):
+    """Single-thread oracle (the reference's kernels are single-threaded) on
+    a time-bounded sample of configuration 5: repeated passes of the four
+    ops over the first 512 dim-2 rows of dim-3 slice 0."""
+    rows = 512
+    sample = Cfg5Sample(rows)
+    done, passes, t0 = 0, 0, time.perf_counter()
+    while True:
+        sample.run(0, rows)
+        done += sample.bytes_of(rows)
+        passes += 1
+        if time.perf_counter() - t0 >= args.cpu_seconds:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": round(done / dt / 1e9, 3), "unit": UNIT, "cores": 1, "kind": "port",
+            "sample": f"{passes} pass(es) of repeat mul + repeat add + sum + argmax over dim-2 rows [0, {rows}) of "
+                      f"dim-3 slice 0 (1/{8 * 8192 // rows} of the cfg5 tensor) in {dt:.1f} s, single thread, "
+                      f"C restatement of the emel-kernels loops (reference Rust not buildable offline)",
+            "cpu_model": cpu_model()}
+
+
+def run_reference_cfg5(args, world, rank):
+    """CPU reference lane for configuration 5: the oracle (the C restatement
+    of the emel-kernels loops; the reference's Rust is not buildable offline)
+    on every host thread.  Each step is a bounded sample: the four ops over
+    the first `rows` dim-2 rows of slice 0, the rows split across threads
+    (ctypes releases the GIL), partial sums added and argmax partials folded
+    in row order -- the same metric, unit and direction as the B200 arm."""
+    if rank != 0:
+        return
+    from concurrent.futures import ThreadPoolExecutor
+    threads = host_threads()
+    pool = ThreadPoolExecutor(max_workers=threads)
+    probe = Cfg5Sample(8192)
+
+    def step(rows):
+        chunk = max(1, -(-rows // threads))
+        futs = [pool.submit(probe.run, r0, min(rows, r0 + chunk)) for r0 in range(0, rows, chunk)]
+        total, best = 0.0, None
+        for f in futs:
+            s, (v, i) = f.result()
+            total += s
+            if best is None or v > best[0]:
+                best = (v, i)
+        return probe.bytes_of(rows)
+
+    rows = max(threads, 256)
+    t = time.perf_counter()
+    step(rows)
+    per_row = (time.perf_counter() - t) / rows
+    # size each step so warmup + steps stay within the time budget
+    rows = int(min(8192, max(threads, args.ref_seconds / max(1e-9, per_row * (args.steps + args.warmup)))))
+    for _ in range(args.warmup):
+        step(rows)
+    t = time.perf_counter()
+    done = 0
+    for _ in range(args.steps):
+        done += step(rows)
+    dt = time.perf_counter() - t
+    value = done / dt / 1e9
+    frac = rows / (8 * 8192)
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dt * 1e3 / args.steps, 3),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded per dim-3 slice, N(0,1))",
+        "config": {"workload": "cfg5 (same ops, tensors and view as the B200 arm): whole-tensor sum + argmax, "
+                               "repeat mul, repeat add on the dims-1/2-swapped view of [128,32,8192,8]",
+                   "sample_rows_per_step": rows, "sample_fraction_per_step": round(frac, 6)},
+        "cpu_baseline": {"value": round(value, 3), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"dim-2 rows [0, {rows}) of dim-3 slice 0 per step ({frac:.5f} of the tensor), "
+                                   f"{threads} threads", "cpu_model": cpu_model()},
+        "e2e": {"value": round(value, 3), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
 def cpu_workload():
     sys.path.insert(0, str(ROOT / "oracle"))
     import oracle
@@ -1021,15 +1361,19 @@ def main():
     ap.add_argument("--only", default="", help="comma list of ops to run, e.g. gelu_f32,relu_f16 (profiling; with --suite: suite op names)")
     ap.add_argument("--branches", type=int, default=4, help="parallel graph branches for the 16 independent ops")
     ap.add_argument("--suite", action="store_true", help="per-op lines for every configuration (1 GPU)")
-    ap.add_argument("--workload", choices=["cfg2", "cfg5"], default="cfg2",
-                    help="cfg2: the default 16-op unary sweep (weak scaling); cfg5: the sharded 4-D "
-                         "broadcast + whole-tensor reductions (strong scaling)")
+    ap.add_argument("--workload", choices=["cfg2", "cfg5"], default="cfg5",
+                    help="cfg5 (default): the 4-D broadcast + whole-tensor reductions sharded along dim 3 "
+                         "(strong scaling); cfg2: the 16-op unary sweep on independent per-GPU batches")
+    ap.add_argument("--no-cfg2", action="store_true", help="cfg5 at N=1: skip the extra cfg2 per-op figures")
     args = ap.parse_args()
     world, rank, local = dist_env()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
-        run_reference(args, world, rank)
+        if args.workload == "cfg5":
+            run_reference_cfg5(args, world, rank)
+        else:
+            run_reference(args, world, rank)
         return
     if args.suite:
         run_suite(args)

@@ -218,6 +218,7 @@ SIGNATURES = {
     "emel_cuda_exchange_connect": (_I, [_CTX, _V, _V]),
     "emel_cuda_exchange_publish": (_I, [_CTX, _V, _V, _V]),
     "emel_cuda_exchange_wait": (_I, [_CTX, _V, _V, _V]),
+    "emel_cuda_exchange_wait_sum_argmax": (_I, [_CTX, _V, _V, _V, _P, _P]),
     "emel_cuda_exchange_destroy": (_I, [_CTX, _V]),
 }
 

@@ -648,13 +648,12 @@ __global__ void __launch_bounds__(kTableThreads, 1) table_stream(typename K::Ele
 // dependent of the build (scheduled early, synchronised in-kernel).
 template <typename K, typename Build, typename... BuildArgs>
 cudaError_t launch_table_pair(const LaunchEnv& env, const EwPlan& p, int slot, Build build, BuildArgs... args) {
-    static int configured_device_mask = 0;  // bit per device with the attribute set
-    const int bit = env.device < 31 ? (1 << env.device) : 0;
-    if (!(configured_device_mask & bit)) {
+    static DeviceFlags configured;  // devices with the attribute set
+    if (!configured.done(env.device)) {
         const cudaError_t err =
             cudaFuncSetAttribute(table_stream<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTableBytes);
         if (err != cudaSuccess) return err;
-        configured_device_mask |= bit;
+        configured.mark(env.device);
     }
     uint16_t* table = reinterpret_cast<uint16_t*>(static_cast<char*>(env.tables) + (uint64_t)slot * kTableBytes);
     build<<<65536 / 256, 256, 0, env.stream>>>(table, args...);

@@ -19,6 +19,7 @@
 // (emel_cuda_stream_synchronize then returns EMEL_CUDA_TIMEOUT) and returns.
 #include <cstdint>
 
+#include "common.cuh"
 #include "launch.hpp"
 
 namespace emel {
@@ -58,31 +59,71 @@ __global__ void __launch_bounds__(kExchangeMaxRanks) exchange_publish(ExchangeAr
     store_release_sys(reinterpret_cast<uint32_t*>(a.peers[r]) + a.rank, epoch);
 }
 
-__global__ void __launch_bounds__(kExchangeMaxRanks) exchange_wait(ExchangeArgs a, void* gathered) {
+// COMBINE: the payload is a shard's f64 sum then its argmax partial (32
+// bytes); after the gather, thread 0 adds the sums in rank order and rounds
+// once to f32 (reductions.rs:671-681 accumulates the whole tensor in f64),
+// and picks the argmax with the reference's rules (reductions.rs:715-730:
+// a later shard wins only with a strictly greater value; no comparable value,
+// or a NaN at element 0 of the whole tensor, leaves index 0).
+template <bool COMBINE>
+__global__ void __launch_bounds__(kExchangeMaxRanks) exchange_wait(ExchangeArgs a, void* gathered, CombineOut c) {
+    __shared__ uint32_t failed;
+    if (threadIdx.x == 0) failed = 0u;
+    if constexpr (COMBINE) __syncthreads();
     const int r = threadIdx.x;
-    if (r >= a.world) return;
-    const uint32_t epoch = *a.epoch;  // set by this rank's publish, earlier on the stream
-    char* own = a.peers[a.rank];
-    const uint32_t* flag = reinterpret_cast<const uint32_t*>(own) + r;
-    const uint64_t t0 = now_ns();
-    bool ok = false;
-    for (uint32_t i = 0; i < (1u << 28); ++i) {
-        if ((int32_t)(load_acquire_sys(flag) - epoch) >= 0) {
-            ok = true;
-            break;
+    if (r < a.world) {
+        const uint32_t epoch = *a.epoch;  // set by this rank's publish, earlier on the stream
+        char* own = a.peers[a.rank];
+        const uint32_t* flag = reinterpret_cast<const uint32_t*>(own) + r;
+        const uint64_t t0 = now_ns();
+        bool ok = false;
+        for (uint32_t i = 0; i < (1u << 28); ++i) {
+            if ((int32_t)(load_acquire_sys(flag) - epoch) >= 0) {
+                ok = true;
+                break;
+            }
+            if ((i & 255u) == 255u) {
+                if (now_ns() - t0 > a.timeout_ns) break;
+                __nanosleep(200);
+            }
         }
-        if ((i & 255u) == 255u) {
-            if (now_ns() - t0 > a.timeout_ns) break;
-            __nanosleep(200);
+        if (!ok) {
+            atomicExch(a.fault, 1u);
+            atomicOr(&failed, 1u);
+        } else {
+            const uint4* src = reinterpret_cast<const uint4*>(slot(own, epoch, r, a.slot_bytes));
+            uint4* dst = reinterpret_cast<uint4*>(static_cast<char*>(gathered) + (uint64_t)r * a.bytes);
+            for (uint32_t i = 0; i < a.bytes / 16; ++i) dst[i] = src[i];
         }
     }
-    if (!ok) {
-        atomicExch(a.fault, 1u);
-        return;
+    if constexpr (COMBINE) {
+        __syncthreads();  // the gathered payloads of every rank are written
+        if (threadIdx.x != 0 || failed) return;
+        const char* g = static_cast<const char*>(gathered);
+        double total = 0.0;
+        bool has = false;
+        float best = 0.0f;
+        int64_t idx = 0;
+        for (int k = 0; k < a.world; ++k) {
+            const char* q = g + (uint64_t)k * a.bytes;
+            total += *reinterpret_cast<const double*>(q);
+            const float v = *reinterpret_cast<const float*>(q + 8);
+            const uint32_t h = *reinterpret_cast<const uint32_t*>(q + 12);
+            const int64_t i = *reinterpret_cast<const int64_t*>(q + 16);
+            if (!h) continue;
+            if (!has || v > best || (v == best && i < idx)) {
+                has = true;
+                best = v;
+                idx = i;
+            }
+        }
+        const uint32_t first_nan = *reinterpret_cast<const uint32_t*>(g + 24);
+        if (first_nan || !has) idx = 0;
+        *static_cast<float*>(c.sum) = __double2float_rn(total);
+        if (c.index_dtype == (int)DType::I64) *static_cast<int64_t*>(c.index) = idx;
+        else if (c.index_dtype == (int)DType::I32) *static_cast<int32_t*>(c.index) = (int32_t)idx;
+        else *static_cast<float*>(c.index) = (float)idx;
     }
-    const uint4* src = reinterpret_cast<const uint4*>(slot(own, epoch, r, a.slot_bytes));
-    uint4* dst = reinterpret_cast<uint4*>(static_cast<char*>(gathered) + (uint64_t)r * a.bytes);
-    for (uint32_t i = 0; i < a.bytes / 16; ++i) dst[i] = src[i];
 }
 
 }  // namespace
@@ -97,7 +138,13 @@ cudaError_t launch_exchange_publish(cudaStream_t stream, const ExchangeArgs& arg
 }
 
 cudaError_t launch_exchange_wait(cudaStream_t stream, const ExchangeArgs& args, void* gathered) {
-    exchange_wait<<<1, kExchangeMaxRanks, 0, stream>>>(args, gathered);
+    exchange_wait<false><<<1, kExchangeMaxRanks, 0, stream>>>(args, gathered, CombineOut{});
+    return cudaGetLastError();
+}
+
+cudaError_t launch_exchange_wait_combine(cudaStream_t stream, const ExchangeArgs& args, void* gathered,
+                                         const CombineOut& out) {
+    exchange_wait<true><<<1, kExchangeMaxRanks, 0, stream>>>(args, gathered, out);
     return cudaGetLastError();
 }
 

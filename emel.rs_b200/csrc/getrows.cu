@@ -303,15 +303,18 @@ __global__ void __launch_bounds__(kGatherThreads) gather_quant(GatherPlan p) {
 
 // Resident CTAs per SM of `kernel` (registers decide it): the gather grid
 // is one full wave, so no CTA waits behind the rows of another.
+// Cached per device and per kernel instantiation.
 template <typename K>
-int resident_ctas(K kernel) {
-    static int cached = 0;
-    if (cached == 0) {
-        int n = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, kGatherThreads, 0) != cudaSuccess || n < 1) n = 1;
-        cached = n;
+int resident_ctas(const LaunchEnv& env, K kernel) {
+    static DeviceKeyedValue cached;
+    uint32_t n = 0;
+    if (!cached.get(env.device, 0u, &n)) {
+        int m = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&m, kernel, kGatherThreads, 0) != cudaSuccess || m < 1) m = 1;
+        n = (uint32_t)m;
+        cached.put(env.device, 0u, n);
     }
-    return cached;
+    return (int)n;
 }
 
 template <typename K>
@@ -322,7 +325,7 @@ cudaError_t launch_pair(const LaunchEnv& env, const GatherPlan& p, K kernel) {
     ++*env.launches;
     cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return err;
-    const uint64_t cap = (uint64_t)env.sm_count * resident_ctas(kernel);
+    const uint64_t cap = (uint64_t)env.sm_count * resident_ctas(env, kernel);
     err = launch_dependent(kernel, dim3((unsigned)(p.dst_rows < cap ? p.dst_rows : cap)), dim3(kGatherThreads), 0,
                            env.stream, p);
     ++*env.launches;

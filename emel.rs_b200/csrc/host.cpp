@@ -731,6 +731,29 @@ emel_cuda_status emel_cuda_exchange_wait(emel_cuda_context* ctx, void* stream, e
     return device_status(ctx, err);
 }
 
+static bool scalar_shape(const emel_tensor_view* v);
+static bool index_view(const emel_tensor_view* v, Checked* c);
+
+emel_cuda_status emel_cuda_exchange_wait_sum_argmax(emel_cuda_context* ctx, void* stream, emel_cuda_exchange* ex,
+                                                    void* gathered, const emel_tensor_view* sum_dst,
+                                                    const emel_tensor_view* argmax_dst) {
+    if (sum_dst == nullptr || argmax_dst == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    Checked cs, ci;
+    // the destinations of OpSum and OpArgmax (reductions.rs:452-458, 520-530)
+    if (!validate_as(sum_dst, EMEL_DTYPE_F32, false, &cs) || !index_view(argmax_dst, &ci)) return EMEL_CUDA_INVALID_VIEW;
+    if (!scalar_shape(sum_dst) || !scalar_shape(argmax_dst)) return EMEL_CUDA_SHAPE_MISMATCH;
+    if (ctx == nullptr || ex == nullptr || !ex->connected || !aligned16_ptr(gathered) ||
+        ex->bytes != 8 + sizeof(emel_cuda_argmax_partial))
+        return EMEL_CUDA_INVALID_ARGUMENT;
+    cudaError_t err = select_device(ctx);
+    if (err == cudaSuccess) {
+        const emel::CombineOut out{sum_dst->data, argmax_dst->data, (int)argmax_dst->dtype};
+        err = emel::launch_exchange_wait_combine((cudaStream_t)stream, exchange_args(ctx, ex, nullptr), gathered, out);
+    }
+    if (err == cudaSuccess) ++ctx->launches;
+    return device_status(ctx, err);
+}
+
 emel_cuda_status emel_cuda_exchange_destroy(emel_cuda_context* ctx, emel_cuda_exchange* ex) {
     if (ctx == nullptr || ex == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
     cudaError_t err = select_device(ctx);

@@ -2,9 +2,47 @@
 // CUDA error of its launch(es); none allocates memory.
 #pragma once
 
+#include <atomic>
+#include <cstdint>
+
 #include "plan.hpp"
 
 namespace emel {
+
+// Per-device, thread-safe records of one-time launch set-up (a kernel's
+// shared-memory limit raised, its occupancy found).  Devices 0..63 each have
+// their own slot; a device beyond that redoes the set-up on every call.
+constexpr int kSetupDevices = 64;
+
+// One bit per device: the set-up it guards has been done on that device.
+struct DeviceFlags {
+    std::atomic<uint64_t> bits{0};
+    bool done(int dev) const {
+        return dev >= 0 && dev < kSetupDevices && ((bits.load(std::memory_order_acquire) >> dev) & 1ull);
+    }
+    void mark(int dev) {
+        if (dev >= 0 && dev < kSetupDevices) bits.fetch_or(1ull << dev, std::memory_order_acq_rel);
+    }
+};
+
+// One cached value per device, valid for one key (e.g. the dynamic
+// shared-memory size an occupancy figure was computed for).  A slot packs
+// (key + 1) << 32 | value, so 0 means empty; two threads that race store the
+// same value for the same key.
+struct DeviceKeyedValue {
+    std::atomic<uint64_t> slot[kSetupDevices] = {};
+    bool get(int dev, uint32_t key, uint32_t* value) const {
+        if (dev < 0 || dev >= kSetupDevices) return false;
+        const uint64_t s = slot[dev].load(std::memory_order_acquire);
+        if ((s >> 32) != (uint64_t)key + 1) return false;
+        *value = (uint32_t)s;
+        return true;
+    }
+    void put(int dev, uint32_t key, uint32_t value) {
+        if (dev >= 0 && dev < kSetupDevices)
+            slot[dev].store((((uint64_t)key + 1) << 32) | value, std::memory_order_release);
+    }
+};
 
 struct UnaryParams;
 
@@ -187,5 +225,15 @@ struct ExchangeArgs {
 uint64_t exchange_buffer_bytes(uint32_t slot_bytes);
 cudaError_t launch_exchange_publish(cudaStream_t stream, const ExchangeArgs& args);
 cudaError_t launch_exchange_wait(cudaStream_t stream, const ExchangeArgs& args, void* gathered);
+
+// Destinations of the combined whole-tensor answers: the f32 sum and the
+// argmax index in dtype index_dtype (F32, I32 or I64).
+struct CombineOut {
+    void* sum;
+    void* index;
+    int index_dtype;
+};
+cudaError_t launch_exchange_wait_combine(cudaStream_t stream, const ExchangeArgs& args, void* gathered,
+                                         const CombineOut& out);
 
 }  // namespace emel

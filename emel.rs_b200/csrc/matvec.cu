@@ -438,13 +438,12 @@ cudaError_t launch_packed(const LaunchEnv& env, const MvArgmaxPlan& p, const uin
     const uint64_t cap = (uint64_t)env.sm_count * 3;
     const size_t table = (size_t)kQ8Warps * 32 * kQ8TermStride * 4;
     const size_t smem = (size_t)(p.k / 32) * (9 * 4 + 4 + 4) + table;
-    static int configured_device_mask = 0;
-    const int bit = env.device < 31 ? (1 << env.device) : 0;
-    if (!(configured_device_mask & bit)) {
+    static DeviceFlags configured;
+    if (!configured.done(env.device)) {
         const cudaError_t e = cudaFuncSetAttribute(mv_argmax_packed<CODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    (int)(1024 * (9 * 4 + 4 + 4) + table));
         if (e != cudaSuccess) return e;
-        configured_device_mask |= bit;
+        configured.mark(env.device);
     }
     return launch_dependent(mv_argmax_packed<CODE>, dim3((unsigned)(groups < cap ? groups : cap)), dim3(kQ8Threads),
                             smem, env.stream, p, lhs);
@@ -862,13 +861,12 @@ cudaError_t launch_mul_mat_argmax(const LaunchEnv& env, const MvArgmaxPlan& p) {
                   CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
     }
     if (tma) {
-        static int configured_device_mask = 0;
-        const int bit = env.device < 31 ? (1 << env.device) : 0;
+        static DeviceFlags configured;
         const int smem = kMvStages * kMvStageBytes + 1024;  // + alignment slack
-        if (!(configured_device_mask & bit)) {
+        if (!configured.done(env.device)) {
             err = cudaFuncSetAttribute(mv_argmax_tma, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
             if (err != cudaSuccess) return err;
-            configured_device_mask |= bit;
+            configured.mark(env.device);
         }
         const uint64_t cap = (uint64_t)env.sm_count;  // one CTA per SM: its stages fill shared memory
         err = launch_dependent(mv_argmax_tma, dim3((unsigned)(tiles < cap ? tiles : cap)), dim3(kMvRows),
@@ -887,25 +885,25 @@ cudaError_t launch_k(const LaunchEnv& env, const MvArgmaxPlan& p, const uint8_t*
     const uint64_t groups = (p.rows + kKWarps * 32 - 1) / (kKWarps * 32);
     const size_t table = (size_t)kKWarps * 2 * 32 * KWindow<CODE>::SWM * 4 + 16;  // staging windows + alignment
     const size_t smem = (size_t)(p.k / 256) * (64 * 4 + 4 + 16 * 4) + table;
-    static int configured_device_mask = 0;
-    const int bit = env.device < 31 ? (1 << env.device) : 0;
-    if (!(configured_device_mask & bit)) {
+    static DeviceFlags configured;
+    if (!configured.done(env.device)) {
         const cudaError_t e = cudaFuncSetAttribute(mv_argmax_k<CODE>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                                    (int)(128 * (64 * 4 + 4 + 16 * 4) + table));
         if (e != cudaSuccess) return e;
-        configured_device_mask |= bit;
+        configured.mark(env.device);
     }
-    // one wave of resident CTAs (registers or shared memory decide how many)
-    static size_t cached_smem = 0;
-    static int cached_ctas = 1;
-    if (smem != cached_smem) {
+    // one wave of resident CTAs (registers or shared memory decide how many),
+    // cached per device for the last shared-memory size seen there
+    static DeviceKeyedValue resident;
+    uint32_t ctas = 0;
+    if (!resident.get(env.device, (uint32_t)smem, &ctas)) {
         int n = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, mv_argmax_k<CODE>, kKThreads, smem) != cudaSuccess || n < 1)
             n = 1;
-        cached_smem = smem;
-        cached_ctas = n;
+        ctas = (uint32_t)n;
+        resident.put(env.device, (uint32_t)smem, ctas);
     }
-    const uint64_t cap = (uint64_t)env.sm_count * cached_ctas;
+    const uint64_t cap = (uint64_t)env.sm_count * ctas;
     const cudaError_t err = launch_dependent(mv_argmax_k<CODE>, dim3((unsigned)(groups < cap ? groups : cap)),
                                              dim3(kKThreads), smem, env.stream, p, lhs);
     ++*env.launches;

@@ -529,13 +529,12 @@ bool fits_u32(uint64_t v) { return v > 0 && v <= 0xffffffffull; }
 // rings (up to kRingStagesMax) while shared memory lasts.
 template <int OP, int T, int R = 0, int MODE = 0>
 cudaError_t launch_ring_kernel(const LaunchEnv& env, RingArgs a, uint64_t rows, bool* launched) {
-    static int configured_device_mask = 0;  // bit per device with the attribute set
-    const int bit = env.device < 31 ? (1 << env.device) : 0;
-    if (!(configured_device_mask & bit)) {
+    static DeviceFlags configured;  // devices with the attribute set
+    if (!configured.done(env.device)) {
         const cudaError_t err =
             cudaFuncSetAttribute(row_ring<OP, T, R, MODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kRingSmemPerSm);
         if (err != cudaSuccess) return err;
-        configured_device_mask |= bit;
+        configured.mark(env.device);
     }
     *launched = false;
     const uint32_t two = a.weight_bytes + 2 * a.stage_bytes;

@@ -653,6 +653,21 @@ EMEL_CUDA_API emel_cuda_status emel_cuda_exchange_publish(emel_cuda_context* ctx
                                                           const void* payload);
 EMEL_CUDA_API emel_cuda_status emel_cuda_exchange_wait(emel_cuda_context* ctx, void* stream, emel_cuda_exchange* ex,
                                                        void* gathered);
+/* The wait above for the sharded whole-tensor reductions, with the combine
+ * done on the device in the same kernel: the payload of every rank is its
+ * emel_cuda_sum_f64 result followed by its emel_cuda_argmax_partial
+ * (bytes_per_rank == 32).  After the gather, the f64 sums are added in rank
+ * order and rounded once to f32 into sum_dst (OpSum, reductions.rs:671-681,
+ * one f64 accumulator over the whole tensor), and the argmax index is
+ * written to argmax_dst (OpArgmax, reductions.rs:715-730: a later shard wins
+ * only with a strictly greater value; a NaN at element 0 of the whole
+ * tensor, or no comparable value, gives index 0).  sum_dst is an F32 view and
+ * argmax_dst an F32 / I32 / I64 view, both of ne [1,1,1,1]; views are
+ * checked like emel_cuda_sum's and emel_cuda_argmax's destinations. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_exchange_wait_sum_argmax(emel_cuda_context* ctx, void* stream,
+                                                                  emel_cuda_exchange* ex, void* gathered,
+                                                                  const emel_tensor_view* sum_dst,
+                                                                  const emel_tensor_view* argmax_dst);
 EMEL_CUDA_API emel_cuda_status emel_cuda_exchange_destroy(emel_cuda_context* ctx, emel_cuda_exchange* ex);
 
 #ifdef __cplusplus

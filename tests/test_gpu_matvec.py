@@ -260,16 +260,21 @@ def q4k_rows(rng, k, rows, planted=None):
     return blob.reshape(-1)
 
 
-def run_q4k_both(emel, kern, olib, blob, rhs, k, rows, code=12):
+def run_q4k_both(emel, kern, olib, blob, rhs, k, rows, code=12, offset=0):
+    """Device and oracle answers for K-quant rows; the device copy of the
+    blob starts `offset` bytes into its buffer (4: a 4-byte aligned base that
+    is not 16-byte aligned, so every row takes the word-staging path)."""
     ctx = kern.ctx
     suffix, bb = {10: ("q2_k", 84), 11: ("q3_k", 110), 12: ("q4_k", 144), 14: ("q6_k", 210)}[code]
     rb = k // 256 * bb
-    bl, br = emel.DeviceBuffer(ctx, blob.nbytes + 16), emel.DeviceBuffer(ctx, rhs.nbytes)
+    store = np.zeros(blob.size + offset, np.uint8)
+    store[offset:] = blob
+    bl, br = emel.DeviceBuffer(ctx, store.nbytes + 16), emel.DeviceBuffer(ctx, rhs.nbytes)
     bd, bi = emel.DeviceBuffer(ctx, 16), emel.DeviceBuffer(ctx, 16)
-    bl.upload(blob)
+    bl.upload(store)
     br.upload(rhs)
     v = emel.CView()
-    v.data, v.storage_bytes, v.dtype = bl.ptr, blob.nbytes, code
+    v.data, v.storage_bytes, v.dtype = bl.ptr + offset, blob.nbytes, code
     for dim, (n, s) in enumerate(zip([k, rows, 1, 1], [1, rb, rb * rows, rb * rows])):
         v.ne[dim], v.nb[dim] = n, s
     fn = getattr(emel.lib(), f"emel_cuda_mul_mat_argmax_{suffix}")
@@ -387,5 +392,44 @@ def test_q2_k_q3_k_parity(emel, kern, oracle_lib, code, k, rows):
     blob = q23k_rows(rng, code, k, rows, planted)
     rhs = rng.standard_normal(k).astype(np.float32)
     st, sync, ost, gv, gi, ov, oi = run_q4k_both(emel, kern, oracle_lib, blob, rhs, k, rows, code)
+    assert st == 0 and sync == 0 and ost == 0
+    assert gi == oi and np.array([gv]).view(np.uint32)[0] == np.array([ov]).view(np.uint32)[0]
+
+
+# ---- K-quant staging paths and the grid-stride group loop ----------------------
+
+KQ_ROWS = {10: lambda rng, k, rows, pl: q23k_rows(rng, 10, k, rows, pl),
+           11: lambda rng, k, rows, pl: q23k_rows(rng, 11, k, rows, pl),
+           12: q4k_rows, 14: q6k_rows}
+
+
+@pytest.mark.parametrize("code", [10, 11, 12, 14])
+@pytest.mark.parametrize("k,rows", [(256, 33), (4096, 700), (32768, 40)])
+def test_k_quant_unaligned_base_parity(emel, kern, oracle_lib, code, k, rows):
+    """A 4-byte aligned, not 16-byte aligned lhs: Q4_K (144-byte blocks) and
+    Q6_K rows are otherwise always 16-byte aligned and would only take the
+    16-byte chunk staging; here every format stages aligned words."""
+    rng = np.random.default_rng(code * 31 + k + rows)
+    planted = int(rng.integers(0, rows))
+    blob = KQ_ROWS[code](rng, k, rows, planted)
+    rhs = rng.standard_normal(k).astype(np.float32)
+    st, sync, ost, gv, gi, ov, oi = run_q4k_both(emel, kern, oracle_lib, blob, rhs, k, rows, code, offset=4)
+    assert st == 0 and sync == 0 and ost == 0
+    assert gi == oi and np.array([gv]).view(np.uint32)[0] == np.array([ov]).view(np.uint32)[0]
+
+
+@pytest.mark.parametrize("code", [10, 12])
+@pytest.mark.parametrize("offset", [0, 4])
+def test_k_quant_rows_beyond_one_wave(emel, kern, oracle_lib, code, offset):
+    """500,000 rows: more than one resident wave can hold (148 SMs x at most
+    2048 threads x one row per lane), so warps loop to a second group of 32
+    rows and reuse both staging buffers.  The planted maximum sits in the
+    last group."""
+    k, rows = 256, 500_000
+    rng = np.random.default_rng(4242 + code + offset)
+    planted = rows - 17
+    blob = KQ_ROWS[code](rng, k, rows, planted)
+    rhs = np.abs(rng.standard_normal(k)).astype(np.float32)
+    st, sync, ost, gv, gi, ov, oi = run_q4k_both(emel, kern, oracle_lib, blob, rhs, k, rows, code, offset=offset)
     assert st == 0 and sync == 0 and ost == 0
     assert gi == oi and np.array([gv]).view(np.uint32)[0] == np.array([ov]).view(np.uint32)[0]

@@ -25,6 +25,9 @@ pytestmark = pytest.mark.gpu
 SMALL = {
     "uneven_split_tie_across_shards": dict(ne=[32, 4, 8, 5], plant=[(3, 40.0), (-7, 40.0)], nan0=False),
     "nan_at_element_zero": dict(ne=[32, 4, 8, 4], plant=[(100, 9.0)], nan0=True),
+    # one slice per rank at 8 GPUs; the tie's later copy sits in the last slice
+    "eight_slices_tie_first_and_last": dict(ne=[32, 4, 8, 8], plant=[(5, 50.0), (-3, 50.0), (6000, 49.0)],
+                                            nan0=False),
 }
 
 
@@ -64,7 +67,7 @@ def worker(rank, world, port, case_name, q):
     try:
         sys.path.insert(0, str(ROOT))
         sys.path.insert(0, str(ROOT / "oracle"))
-        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
         from datetime import timedelta
 
         import torch
@@ -230,7 +233,7 @@ def exchange_worker(rank, world, port, mode, q):
     must expire, report EMEL_CUDA_TIMEOUT and leave the context usable."""
     try:
         sys.path.insert(0, str(ROOT))
-        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
         from datetime import timedelta
 
         import torch
@@ -327,3 +330,147 @@ def test_peer_exchange_wait_expires_without_a_publisher():
     assert by_rank[0][1] and by_rank[0][2] and by_rank[1][1] and by_rank[1][2]
     assert by_rank[0][3] == 17, by_rank[0]  # EMEL_CUDA_TIMEOUT
     assert by_rank[0][4] is True, by_rank[0]
+
+
+# ---- device-side combine (emel_cuda_exchange_wait_sum_argmax) ----------------
+def shard_of(pkg, torch, dev, W, D, case_name, world, rank):
+    """(device tensor, view, first ordinal) of this rank's dim-3 slices."""
+    if case_name == "cfg5":
+        b, e = D.shard_bounds(W.CFG5_NE[3], world, rank)
+        s0, _ = cfg5_slices(W, b, e)
+        ne, nb = W.cfg5_src0_view(ne3=e - b)
+        t = torch.from_numpy(s0).to(dev)
+    else:
+        case = SMALL[case_name]
+        full = case["ne"]
+        x = small_tensor(case)
+        b, e = D.shard_bounds(full[3], world, rank)
+        plane = full[0] * full[1] * full[2]
+        t = torch.from_numpy(np.ascontiguousarray(x[b * plane:e * plane])).to(dev)
+        ne = [full[0], full[1], full[2], e - b]
+        nb = pkg.contiguous_nb(ne)
+    v = pkg.CView()
+    v.data, v.storage_bytes, v.dtype = t.data_ptr(), t.numel() * 4, 0
+    for d in range(4):
+        v.ne[d], v.nb[d] = ne[d], nb[d]
+    return t, v, b * ne[0] * ne[1] * ne[2]
+
+
+def combine_worker(rank, world, port, case_name, q):
+    """Per step: the shard's f64 sum and argmax partial, published over
+    NVLink, then one wait that gathers and combines on the device into an
+    F32 sum and an I64 index.  Two eager steps, then three replays of the
+    step captured as a graph; every step's answers are reported."""
+    try:
+        sys.path.insert(0, str(ROOT))
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        from datetime import timedelta
+
+        import torch
+        import torch.distributed as dist
+
+        from __graft_entry__ import load_package
+
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=120),
+                                device_id=dev)
+        pkg = load_package()
+        from emel_rs_b200 import distributed as D
+        from emel_rs_b200 import workloads as W
+
+        lib = pkg.lib()
+        ctx = pkg.Context(rank)
+        stream = pkg.Stream(ctx)
+        sh = stream.handle
+        t, v, base = shard_of(pkg, torch, dev, W, D, case_name, world, rank)
+        payload = torch.zeros(32, dtype=torch.uint8, device=dev)
+        gathered = torch.zeros(world * 32, dtype=torch.uint8, device=dev)
+        sum_out = torch.full((1,), 7.0, dtype=torch.float32, device=dev)
+        idx_out = torch.full((1,), -1, dtype=torch.int64, device=dev)
+        vs, vi = pkg.CView(), pkg.CView()
+        for cv, tt, code in ((vs, sum_out, 0), (vi, idx_out, 27)):
+            cv.data, cv.storage_bytes, cv.dtype = tt.data_ptr(), tt.numel() * tt.element_size(), code
+            for d, (n, b) in enumerate(zip([1, 1, 1, 1], pkg.contiguous_nb([1, 1, 1, 1], code))):
+                cv.ne[d], cv.nb[d] = n, b
+        torch.cuda.synchronize()
+        ex = D.PeerExchange(pkg, ctx, dist, world, rank, timeout_ms=10000)
+        B = ctypes.byref
+
+        def step():
+            p = payload.data_ptr()
+            assert lib.emel_cuda_sum_f64(ctx.handle, sh, B(v), ctypes.c_void_p(p)) == 0, ctx.last_error
+            assert lib.emel_cuda_argmax_partial_compute(ctx.handle, sh, B(v), base, ctypes.c_void_p(p + 8)) == 0
+            ex.publish(sh, p)
+            st = lib.emel_cuda_exchange_wait_sum_argmax(ctx.handle, sh, ex.handle, ctypes.c_void_p(gathered.data_ptr()),
+                                                        B(vs), B(vi))
+            assert st == 0, ctx.last_error
+
+        answers = []
+        for _ in range(2):
+            step()
+            assert lib.emel_cuda_stream_synchronize(ctx.handle, sh) == 0
+            answers.append((float(sum_out.cpu()[0]), int(idx_out.cpu()[0])))
+            sum_out.fill_(7.0)
+            idx_out.fill_(-1)
+            torch.cuda.synchronize()
+        graph = pkg.Graph(ctx, stream)
+        with graph:
+            step()
+        for _ in range(3):
+            graph.launch()
+            assert lib.emel_cuda_stream_synchronize(ctx.handle, sh) == 0
+            answers.append((float(sum_out.cpu()[0]), int(idx_out.cpu()[0])))
+            sum_out.fill_(7.0)
+            idx_out.fill_(-1)
+            torch.cuda.synchronize()
+        graph.close()
+        dist.barrier()
+        ex.close()
+        dist.barrier()
+        dist.destroy_process_group()
+        q.put((rank, answers, None, None, None))
+    except Exception as exc:  # report to the parent instead of hanging it
+        q.put((rank, "error", repr(exc), None, None))
+
+
+def check_combined(results, want_sum, want_idx):
+    for rank, answers, _, _, _ in results:
+        assert len(answers) == 5, rank
+        for total32, gidx in answers:
+            if np.isnan(want_sum):
+                assert np.isnan(total32), (rank, total32)
+            else:
+                assert abs(total32 - want_sum) <= 1e-5 * max(1.0, abs(want_sum)), (rank, total32, want_sum)
+            assert gidx == want_idx, (rank, gidx, want_idx)
+
+
+@pytest.mark.parametrize("case_name", list(SMALL))
+def test_device_combine_matches_whole_tensor(case_name):
+    """The combined whole-tensor sum (f64 partials added in rank order, one
+    rounding) and argmax (strict >, first index; a NaN at element 0 pins 0)
+    against the oracle's OpSum / OpArgmax on the whole tensor.  Cases with
+    eight slices run on up to 8 GPUs, the others on 2."""
+    gpus = gpu_count()
+    if gpus < 2:
+        pytest.skip("needs 2 GPUs")
+    case = SMALL[case_name]
+    world = min(gpus, 8) if case["ne"][3] >= 8 else 2
+    results = run_ranks(world, case_name, target=combine_worker)
+    want_sum, want_idx = whole_tensor_answers(small_tensor(case), case["ne"])
+    check_combined(results, want_sum, want_idx)
+
+
+def test_device_combine_cfg5_over_all_gpus():
+    gpus = gpu_count()
+    if gpus < 2:
+        pytest.skip("needs 2 GPUs")
+    results = run_ranks(min(gpus, 8), "cfg5", target=combine_worker)
+    sys.path.insert(0, str(ROOT))
+    from __graft_entry__ import load_package
+    load_package()
+    from emel_rs_b200 import workloads as W
+    x, _ = cfg5_slices(W, 0, W.CFG5_NE[3])
+    ne, nb = W.cfg5_src0_view()
+    want_sum, want_idx = whole_tensor_answers(x, ne, nb)
+    check_combined(results, want_sum, want_idx)

@@ -2,10 +2,12 @@
 allocate device memory (a host application that owns all of it, or code
 that must not let cudaMalloc/cudaFree synchronise the device).  It takes no
 context and keeps its scratch in a static device array, so this test checks
-that two calls in a row -- which reuse that array -- each return what the
-context-based emel_cuda_sum returns for the same input, within the 1e-5
-relative tolerance the sum tests use.  The file name sorts last so a run
-that stops at the first failure has already run every other test."""
+that two calls in a row -- which reuse that array -- each return exactly the
+bits the context-based emel_cuda_sum returns for the same input (both launch
+the same kernel on the same grid), and that both are within the 1e-5
+relative tolerance of the oracle's OpSum (reductions.rs:671-681).  The file
+name sorts last so a run that stops at the first failure has already run
+every other test."""
 
 import ctypes
 
@@ -17,7 +19,7 @@ import gpu_helpers as gh
 pytestmark = pytest.mark.gpu
 
 
-def test_noalloc_sum_matches_context_sum_on_consecutive_calls(emel):
+def test_noalloc_sum_matches_context_sum_on_consecutive_calls(emel, oracle_lib):
     lib = emel.lib()
     ctx = emel.Context(0)  # the test allocates its buffers; the entry point does not
     rng = np.random.default_rng(2024)
@@ -32,10 +34,17 @@ def test_noalloc_sum_matches_context_sum_on_consecutive_calls(emel):
         assert lib.emel_cuda_sum(ctx.handle, None, ctypes.byref(src), ctypes.byref(want_v)) == 0, ctx.last_error
         assert lib.emel_cuda_sum_noalloc(None, ctypes.byref(src), ctypes.byref(got_v)) == 0
         ctx.synchronize()
-        want = float(want_buf.download()[0])
-        got = float(got_buf.download()[0])
-        assert abs(got - want) <= 1e-5 * max(abs(want), 1e-3), (ne, got, want)
-        for p in (px, want_buf, got_buf):
+        want = want_buf.download()
+        got = got_buf.download()
+        # same kernel, same grid, same fold order: identical bits
+        gh.assert_bits_equal(got, want, f"noalloc vs context sum {ne}")
+        # and the oracle's f64 accumulation rounded once to f32
+        ref = np.zeros(1, np.float32)
+        ov = gh.Pair(emel, ctx, ref, [1, 1, 1, 1], upload=False)
+        assert oracle_lib.oracle_sum(ctypes.byref(px.oview()), ctypes.byref(ov.oview())) == 0
+        r = float(ov.host[0])
+        assert abs(float(got[0]) - r) <= 1e-5 * max(abs(r), 1e-3), (ne, float(got[0]), r)
+        for p in (px, want_buf, got_buf, ov):
             p.free()
 
 
