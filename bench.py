@@ -452,7 +452,7 @@ def run_suite(args):
     only = set(args.only.split(",")) if args.only else None
 
     def measure(cfg, name, nbytes, elems, make_launch, sets, extra=None):
-        if only and name not in only:
+        if only and name not in only and cfg not in only:
             return
         torch.cuda.synchronize()  # inputs were uploaded on torch's stream
         launches = [make_launch(k) for k in range(sets)]
@@ -565,7 +565,7 @@ def run_suite(args):
                 lambda k: (lambda: chk(lib.emel_cuda_sum_rows(ctx.handle, sh, B(vx), B(vr)))), 1)
         del xs, ys, ys2
     # cfg4a: masked, scaled softmax
-    if wants("soft_max_ext_scale_mask",):
+    if wants("soft_max_ext_scale_mask", "cfg4"):
         scores, mask = W.cfg4a()
         kv, q, h = W.CFG4A_NE
         spec = W.cfg4_spec()
@@ -578,7 +578,7 @@ def run_suite(args):
                                                                     float(W.CFG4A_SCALE)))), 1)
         del ts, to
     # cfg4b: vocab softmax and per-row argmax
-    if wants("soft_max_vocab", "argmax_rows_vocab"):
+    if wants("soft_max_vocab", "argmax_rows_vocab", "cfg4"):
         logits, _ = W.cfg4b()
         v, rws = W.CFG4B_NE
         S = sets_for(spec.ops[1].bytes)
@@ -861,6 +861,15 @@ class Cfg5Shard:
                                                             ctypes.c_void_p(self.gathered.data_ptr()),
                                                             B(self.vsum), B(self.vidx)), "exchange wait")
 
+    def align(self, sh):
+        """One untimed exchange round (publish + wait) on stream `sh`: every
+        rank's stream leaves it within the exchange latency of the others, so
+        a timed region that starts right after begins together on every GPU
+        instead of when each host returns from its barrier."""
+        if self.exchange is not None:
+            self.exchange.publish(sh, self.partial.data_ptr())
+            self.exchange.wait(sh, self.gathered.data_ptr())
+
     def answers(self):
         return float(self.sum_out.cpu()[0]), int(self.idx_out.cpu()[0])
 
@@ -937,6 +946,7 @@ def run_cfg5(args, world, rank, local):
     if world > 1:
         dist.barrier()
     t0, t1 = pkg.CudaEvent(ctx), pkg.CudaEvent(ctx)
+    shard.align(sh)
     launches_before = ctx.launches
     with ClockSampler(local) as clocks:
         t0.record(sh)
@@ -1073,6 +1083,7 @@ def run_cfg5_e2e(args, pkg, ctx, torch, shard, stream, world):
         import torch.distributed as dist
         dist.barrier()
     t0, t1 = pkg.CudaEvent(ctx), pkg.CudaEvent(ctx)
+    shard.align(sh)
     t0.record(sh)
     up.wait(t0)
     for _ in range(steps):

@@ -260,9 +260,9 @@ __global__ void __launch_bounds__(fa_threads(DPT, TILE), 1) fa_decode(FlashAttnP
             if (t < T) {
                 // flash_attn.rs:364-375
                 if (s > mb)
-                    rs = lm_exp(__fsub_rn(mb, s));
+                    rs = lm_exp_cr(__fsub_rn(mb, s));
                 else
-                    vs = lm_exp(__fsub_rn(s, mb));
+                    vs = lm_exp_cr(__fsub_rn(s, mb));
                 tiles[(it & 1) * TILE + sj] = make_float4(rs, vs, fa_round16(rs), fa_round16(vs));
             }
             // tokens whose binary16 rescale factor is not 1 (a rescale by 1 leaves

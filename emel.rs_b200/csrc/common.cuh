@@ -11,9 +11,10 @@
 //     a canonical NaN.  `x86_nan2`/`x86_nan1` rebuild the SSE bits.
 //   * sign/abs: PTX neg/abs leave NaN payloads unspecified, so they are
 //     done on the integer bits.
-// Transcendentals are evaluated in binary64 and rounded once to binary32,
-// which stays within 1 ulp of glibc's expf/expm1f/logf/sinf/cosf and within
-// 2 ulp of its tanhf over the inputs the parity tests sweep.
+// exp / expm1 / tanh run on the binary32 core of fastmath.cuh (within 1 / 1
+// / 2 ulp of the correctly rounded value over every binary32 input; the
+// tolerance for transcendental unary ops is 2 ulp); log, log1p, sin and cos
+// are evaluated in binary64 and rounded once.
 #pragma once
 
 #include <cuda_fp16.h>
@@ -104,21 +105,23 @@ struct UnaryParams {
     float b;
 };
 
-// One libm call of the reference evaluated as binary64 and rounded once.
-// exp / expm1 / tanh use the table-driven binary64 core (fastmath.cuh);
-// log, log1p, sin and cos call CUDA's binary64 functions.
-__device__ __forceinline__ float lm_exp(float x) { return x86_nan1(fast_expf(x), x); }
-__device__ __forceinline__ float lm_expm1(float x) { return x86_nan1(fast_expm1f(x), x); }
-__device__ __forceinline__ float lm_tanh(float x) { return x86_nan1(fast_tanhf(x), x); }
-// exp(z) for the fast soft_max passes (z <= 0, or NaN): branch-free.  The
-// argument is clamped into the core's range, the core is evaluated, and
-// z < -104 (a binary32 result of +0) is selected afterwards; a NaN z passes
-// both comparisons and gives NaN.
-__device__ __forceinline__ float softmax_exp(float z) {
-    const float zc = z < -104.0f ? -104.0f : z;
-    const float r = (float)exp_core((double)zc);
-    return z < -104.0f ? 0.0f : r;
-}
+// The reference's libm calls (f32::exp, exp_m1, tanh) on binary32 results:
+// the binary32 core of fastmath.cuh (exp and expm1 within 1 ulp of the
+// correctly rounded value over every binary32 input, tanh within 2), with
+// the x86 NaN rules.  The _cr forms evaluate in binary64 and round once
+// (correctly rounded but for rare double-rounding ties): the standalone tanh
+// op (glibc's tanhf is itself up to 2 ulp from the correctly rounded value,
+// so a 2-ulp tanh could sit 4 ulp from it) and the paths whose parity is
+// pinned bit for bit on the reference's golden vectors (single-query
+// attention's binary16 recurrence, RoPE frequencies, silu_back).
+__device__ __forceinline__ float lm_exp(float x) { return x86_nan1(exp32(x), x); }
+__device__ __forceinline__ float lm_expm1(float x) { return x86_nan1(expm1_32(x), x); }
+__device__ __forceinline__ float lm_tanh(float x) { return x86_nan1(tanh32(x), x); }
+__device__ __forceinline__ float lm_exp_cr(float x) { return x86_nan1(fast_expf(x), x); }
+__device__ __forceinline__ float lm_tanh_cr(float x) { return x86_nan1(fast_tanhf(x), x); }
+// exp(z) for the fast soft_max passes (z <= 0, or NaN): binary32 core,
+// which gives +0 below -104 and NaN for NaN.
+__device__ __forceinline__ float softmax_exp(float z) { return exp32(z); }
 
 // e / d rounded once for 0 <= e <= 1 and a finite d >= 1, given
 // inv = RN(1 / d): q0 = RN(e * inv) is within one ulp of e / d, the FMA
@@ -157,20 +160,35 @@ __device__ __forceinline__ float clamp_rs(float v, float lo, float hi) {
     return v;
 }
 
-// Arithmetic policy for the formulas.  Exact = the reference's x86 NaN
-// semantics on every operation; Fast = plain IEEE operations.  The two agree
-// bit for bit on every non-NaN result (NaN payloads are the only difference,
-// and a selection on a NaN intermediate does not depend on its payload), so
-// the heavy formulas run Fast and recompute Exact only when the result is NaN.
-template <bool EXACT>
+// Arithmetic policies for the formulas.
+//   kFast   plain IEEE binary32 operations and the binary32 exponential core;
+//   kExact  the same values with the reference's x86 NaN semantics on every
+//           operation.  The two agree bit for bit on every non-NaN result
+//           (a selection on a NaN intermediate does not depend on its
+//           payload), so the heavy formulas run kFast and recompute kExact
+//           only when the result is NaN;
+//   kHalf   for results rounded to binary16 (binary16 storage, and GELU,
+//           whose formula rounds its output through binary16): CUDA's
+//           exponential and division intrinsics (__expf, __fdividef: a few
+//           binary32 ulp) where binary16's half-ulp of 2^-12 relative
+//           absorbs them.  expm1 stays on the binary32 core (a small
+//           negative argument would lose relative accuracy to exp - 1), and
+//           tanh is 1 - 2 / (exp(2|y|) + 1): its error is absolute and tiny
+//           near +-1, where GELU's 1 + tanh cancels.
+enum ArithMode : int { kFast = 0, kExact = 1, kHalf = 2 };
+
+template <int MODE>
 struct Arith {
+    static constexpr bool EXACT = MODE == kExact;
     static __device__ __forceinline__ float add(float a, float b) { return EXACT ? f_add(a, b) : __fadd_rn(a, b); }
     static __device__ __forceinline__ float sub(float a, float b) { return EXACT ? f_sub(a, b) : __fsub_rn(a, b); }
     static __device__ __forceinline__ float mul(float a, float b) { return EXACT ? f_mul(a, b) : __fmul_rn(a, b); }
     static __device__ __forceinline__ float div(float a, float b) { return EXACT ? f_div(a, b) : __fdiv_rn(a, b); }
-    static __device__ __forceinline__ float exp(float x) { return EXACT ? lm_exp(x) : fast_expf(x); }
-    static __device__ __forceinline__ float expm1(float x) { return EXACT ? lm_expm1(x) : fast_expm1f(x); }
-    static __device__ __forceinline__ float tanh(float x) { return EXACT ? lm_tanh(x) : fast_tanhf(x); }
+    static __device__ __forceinline__ float exp(float x) { return EXACT ? lm_exp(x) : exp32(x); }
+    static __device__ __forceinline__ float expm1(float x) { return EXACT ? lm_expm1(x) : expm1_32(x); }
+    static __device__ __forceinline__ float tanh(float x) { return EXACT ? lm_tanh(x) : tanh32(x); }
+    // the standalone tanh op (unary.rs OpUnary Tanh): correctly rounded
+    static __device__ __forceinline__ float tanh_op(float x) { return EXACT ? lm_tanh_cr(x) : fast_tanhf(x); }
     static __device__ __forceinline__ float log1p(float x) { return EXACT ? lm_log1p(x) : (float)::log1p((double)x); }
     // fp16_to_f32(fp32_to_fp16(v)) (unary.rs:533,539)
     static __device__ __forceinline__ float round_f16(float v) {
@@ -185,24 +203,49 @@ struct Arith {
     }
 };
 
+template <>
+struct Arith<kHalf> {
+    static constexpr bool EXACT = false;
+    static __device__ __forceinline__ float add(float a, float b) { return __fadd_rn(a, b); }
+    static __device__ __forceinline__ float sub(float a, float b) { return __fsub_rn(a, b); }
+    static __device__ __forceinline__ float mul(float a, float b) { return __fmul_rn(a, b); }
+    static __device__ __forceinline__ float div(float a, float b) { return __fdividef(a, b); }
+    static __device__ __forceinline__ float exp(float x) { return __expf(x); }
+    static __device__ __forceinline__ float expm1(float x) { return expm1_32(x); }
+    static __device__ __forceinline__ float tanh(float x) {
+        const float ay = fabsf(x);
+        const float t = __fsub_rn(1.0f, __fdividef(2.0f, __fadd_rn(__expf(__fmul_rn(2.0f, ay)), 1.0f)));
+        const float r = ay >= 10.0f ? 1.0f : t;
+        return x == 0.0f ? x : (x < 0.0f ? -r : r);
+    }
+    static __device__ __forceinline__ float tanh_op(float x) { return tanh32(x); }
+    static __device__ __forceinline__ float log1p(float x) { return (float)::log1p((double)x); }
+    static __device__ __forceinline__ float round_f16(float v) { return __half2float(__float2half_rn(v)); }
+    static __device__ __forceinline__ float fma(float a, float b, float c) { return __fmaf_rn(a, b, c); }
+    static __device__ __forceinline__ float clamp(float v, float lo, float hi) {
+        return v < lo ? lo : (v > hi ? hi : v);
+    }
+};
+
 // GELU's tanh approximation of an already binary16-rounded input q
 // (unary.rs:533-539, between the two binary16 round trips).
-template <bool EXACT>
+template <int MODE>
 __device__ __forceinline__ float gelu_tanh_core(float q) {
-    using A = Arith<EXACT>;
+    using A = Arith<MODE>;
     const float cube = A::mul(A::mul(A::mul(0.044715f, q), q), q);
     const float inner = A::mul(0.7978846f, A::add(q, cube));
     return A::mul(A::mul(0.5f, q), A::add(1.0f, A::tanh(inner)));
 }
 
-template <int OP, bool EXACT, bool IN_F16 = false>
+template <int OP, int MODE, bool IN_F16 = false>
 __device__ __forceinline__ float unary_formula(float v, UnaryParams p) {
-    using A = Arith<EXACT>;
+    using A = Arith<MODE>;
+    constexpr bool EXACT = MODE == kExact;
     if constexpr (OP == kAbs) return f_abs(v);
     if constexpr (OP == kSgn) return is_nan(v) ? bitsf(0x7fc00000u) : bitsf((fbits(v) & 0x80000000u) | 0x3f800000u);
     if constexpr (OP == kNeg) return f_neg(v);
     if constexpr (OP == kStep) return v > 0.0f ? 1.0f : 0.0f;
-    if constexpr (OP == kTanh) return A::tanh(v);
+    if constexpr (OP == kTanh) return A::tanh_op(v);
     if constexpr (OP == kElu) return v >= 0.0f ? v : A::expm1(v);
     if constexpr (OP == kRelu) return v > 0.0f ? v : 0.0f;
     if constexpr (OP == kSigmoid) return A::div(1.0f, A::add(1.0f, A::exp(f_neg(v))));
@@ -212,7 +255,7 @@ __device__ __forceinline__ float unary_formula(float v, UnaryParams p) {
         // an f16 input is already binary16, and an f16 store rounds the
         // output the same way: the fast path skips both round trips
         const float q = (IN_F16 && !EXACT) ? v : A::round_f16(v);
-        const float approx = gelu_tanh_core<EXACT>(q);
+        const float approx = gelu_tanh_core<MODE>(q);
         return (IN_F16 && !EXACT) ? approx : A::round_f16(approx);
     }
     if constexpr (OP == kGeluGeneric) {
@@ -271,18 +314,21 @@ constexpr bool kHeavyFormula = OP == kTanh || OP == kElu || OP == kSigmoid || OP
 // the hot loop small.
 template <int OP, bool IN_F16>
 __device__ __noinline__ float unary_exact_slow(float v, UnaryParams p) {
-    return unary_formula<OP, true, IN_F16>(v, p);
+    return unary_formula<OP, kExact, IN_F16>(v, p);
 }
 
 // IN_F16: the value came from, and the result goes to, binary16 storage.
+// Results that end in binary16 (binary16 storage; GELU, which rounds its
+// output through binary16 itself) take the kHalf policy.
 template <int OP, bool IN_F16 = false>
 __device__ __forceinline__ float unary_apply(float v, UnaryParams p) {
     if constexpr (kHeavyFormula<OP>) {
-        const float r = unary_formula<OP, false, IN_F16>(v, p);
+        constexpr int M = (IN_F16 || OP == kGelu) ? kHalf : kFast;
+        const float r = unary_formula<OP, M, IN_F16>(v, p);
         if (!is_nan(r)) return r;
         return unary_exact_slow<OP, IN_F16>(v, p);
     } else {
-        return unary_formula<OP, true, IN_F16>(v, p);
+        return unary_formula<OP, kExact, IN_F16>(v, p);
     }
 }
 
@@ -292,36 +338,36 @@ __device__ __forceinline__ float unary_apply(float v, UnaryParams p) {
 // to maxss / minss with the constant as the second operand, which returns
 // that constant for a NaN input and for a tie: relu(-0.0) = +0.0.
 // ---------------------------------------------------------------------------
-template <bool EXACT>
+template <int MODE>
 __device__ __forceinline__ float glu_silu(float v) {
-    using A = Arith<EXACT>;
+    using A = Arith<MODE>;
     return A::div(v, A::add(1.0f, A::exp(f_neg(v))));
 }
 
-template <int SUB, bool EXACT>
+template <int SUB, int MODE>
 __device__ __forceinline__ float glu_formula(float value, float g) {
-    using A = Arith<EXACT>;
+    using A = Arith<MODE>;
     if constexpr (SUB == kReGlu) return A::mul(value, g > 0.0f ? g : 0.0f);
-    if constexpr (SUB == kGeGlu) return A::mul(value, unary_formula<kGeluQuick, EXACT>(g, UnaryParams{}));
-    if constexpr (SUB == kSwiGlu) return A::mul(value, glu_silu<EXACT>(g));
+    if constexpr (SUB == kGeGlu) return A::mul(value, unary_formula<kGeluQuick, MODE>(g, UnaryParams{}));
+    if constexpr (SUB == kSwiGlu) return A::mul(value, glu_silu<MODE>(g));
     if constexpr (SUB == kSwiGluOai) {
         const float gate = g < 7.0f ? g : 7.0f;
         const float v = value < 7.0f ? value : 7.0f;
-        return A::mul(A::div(glu_silu<EXACT>(A::mul(1.702f, gate)), 1.702f), A::add(v, 1.0f));
+        return A::mul(A::div(glu_silu<MODE>(A::mul(1.702f, gate)), 1.702f), A::add(v, 1.0f));
     }
-    if constexpr (SUB == kGeGluErf) return A::mul(value, unary_formula<kGeluErf, EXACT>(g, UnaryParams{}));
+    if constexpr (SUB == kGeGluErf) return A::mul(value, unary_formula<kGeluErf, MODE>(g, UnaryParams{}));
     // kGeGluQuick: value * (1 / (1 + exp(-1.702 * g)))
     return A::mul(value, A::div(1.0f, A::add(1.0f, A::exp(A::mul(-1.702f, g)))));
 }
 
 template <int SUB>
 __device__ __noinline__ float glu_exact_slow(float value, float g) {
-    return glu_formula<SUB, true>(value, g);
+    return glu_formula<SUB, kExact>(value, g);
 }
 
 template <int SUB>
 __device__ __forceinline__ float glu_apply(float value, float g) {
-    const float r = glu_formula<SUB, false>(value, g);
+    const float r = glu_formula<SUB, kFast>(value, g);
     if (!is_nan(r)) return r;
     return glu_exact_slow<SUB>(value, g);
 }

@@ -50,7 +50,7 @@ struct SiluBackFn {
     static constexpr int kUnroll = 2;
     static constexpr int kMinBlocks = 4;
     __device__ __forceinline__ float operator()(float x, float grad) const {
-        const float sigmoid = f_div(1.0f, f_add(1.0f, lm_exp(f_neg(x))));
+        const float sigmoid = f_div(1.0f, f_add(1.0f, lm_exp_cr(f_neg(x))));
         const float derivative = f_mul(sigmoid, f_add(1.0f, f_mul(x, f_sub(1.0f, sigmoid))));
         return f_mul(grad, derivative);
     }
@@ -493,205 +493,9 @@ cudaError_t launch_ew(const LaunchEnv& env, const EwPlan& p, const F& f) {
     return cudaGetLastError();
 }
 
-// ---------------------------------------------------------------------------
-// binary16 unary ops through a domain table.
-//
-// A binary16 operand has 65536 possible values, fewer than the elements of
-// a large tensor, so a launch first evaluates the op's exact formula (the
-// same unary_apply<OP, true> and reference conversions the direct kernels
-// use) once per possible input, into a 128 KB table, and then streams the
-// tensor through a shared-memory lookup.  Both kernels run on every call;
-// nothing is kept between calls.  The results are those of the direct path
-// bit for bit, and the stream does no per-element arithmetic, so it runs at
-// HBM speed for every op instead of being bound by the binary64 libm cores.
-// ---------------------------------------------------------------------------
-template <int OP>
-constexpr bool kTableOp = (kHeavyFormula<OP> || OP == kSqrt || OP == kLog || OP == kSin || OP == kCos) && OP < 128;
-
-constexpr uint64_t kTableMinCount = 1ull << 20;  // below this the table costs more than it saves
-constexpr int kTableThreads = 1024;  // one stream CTA fills an SM; every build CTA is resident before it is scheduled
-constexpr uint32_t kTableBytes = 65536u * 2u;
-
-// griddepcontrol: the table build lets the stream kernel be scheduled as
-// soon as every build CTA has started; the stream kernel reads its first
-// inputs (written before the build began), then waits for the build grid to
-// finish before it touches the table or writes anything.
-__device__ __forceinline__ void allow_dependent_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
-__device__ __forceinline__ void wait_for_prerequisite_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
-
-template <int OP>
-__global__ void __launch_bounds__(256) f16_table_build(uint16_t* __restrict__ table, UnaryParams p) {
-    allow_dependent_launch();
-    const uint32_t h = blockIdx.x * 256u + threadIdx.x;
-    table[h] = f32_to_f16_bits(unary_apply<OP, true>(f16_bits_to_f32((uint16_t)h), p));
-}
-
-// binary32 GELU (unary.rs:533-539) rounds its input to binary16 before the
-// formula and its result to binary16 after it, so for |x| < 10 the output is
-// a function of the binary16 input alone: entry h holds the rounded result of
-// the formula for q = binary16 value h (no +-10 clamp: a binary32 input
-// below 10 may round up to 10 in binary16 and still takes the formula).
-__global__ void __launch_bounds__(256) gelu_f32_table_build(uint16_t* __restrict__ table) {
-    allow_dependent_launch();
-    const uint32_t h = blockIdx.x * 256u + threadIdx.x;
-    const float q = f16_bits_to_f32((uint16_t)h);
-    float r = gelu_tanh_core<false>(q);
-    if (is_nan(r)) r = gelu_tanh_core<true>(q);
-    table[h] = f32_to_f16_bits(r);
-}
-
-__device__ __forceinline__ uint32_t lookup2(const uint16_t* tab, uint32_t w) {
-    return (uint32_t)tab[w & 0xffffu] | ((uint32_t)tab[w >> 16] << 16);
-}
-
-// binary16 in, binary16 out: eight lanes per 16-byte vector.
-struct HalfTable {
-    static constexpr int kLanes = 8;
-    using Elem = uint16_t;
-    static __device__ __forceinline__ uint4 apply(const uint16_t* tab, uint4 v) {
-        return make_uint4(lookup2(tab, v.x), lookup2(tab, v.y), lookup2(tab, v.z), lookup2(tab, v.w));
-    }
-    static __device__ __forceinline__ uint16_t apply1(const uint16_t* tab, uint16_t v) { return tab[v]; }
-};
-
-// binary32 GELU: four lanes per vector, +-10 clamps outside the table.
-struct GeluF32Table {
-    static constexpr int kLanes = 4;
-    using Elem = float;
-    static __device__ __forceinline__ float one(const uint16_t* tab, float v) {
-        if (v <= -10.0f) return 0.0f;
-        if (v >= 10.0f) return v;
-        return f16_bits_to_f32(tab[f32_to_f16_bits(v)]);
-    }
-    static __device__ __forceinline__ uint4 apply(const uint16_t* tab, uint4 v) {
-        return make_uint4(fbits(one(tab, bitsf(v.x))), fbits(one(tab, bitsf(v.y))), fbits(one(tab, bitsf(v.z))),
-                          fbits(one(tab, bitsf(v.w))));
-    }
-    static __device__ __forceinline__ float apply1(const uint16_t* tab, float v) { return one(tab, v); }
-};
-
-__device__ __forceinline__ uint4 ld_u4(const void* p) {
-    uint4 v;
-    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
-                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
-                 : "l"(p));
-    return v;
-}
-
-__device__ __forceinline__ void st_u4(void* p, uint4 v) {
-    asm volatile("st.global.L1::no_allocate.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
-                 "r"(v.w)
-                 : "memory");
-}
-
-// One CTA per SM (its registers leave room for two build CTAs, so it can
-// be resident while the build finishes).  Each thread loads its first U
-// vectors before the table exists, then waits for the build grid, pulls the
-// 128 KB table into shared memory with one bulk copy, and streams
-// grid-strided 16-byte vectors through it, U per iteration.
-template <typename K>
-__global__ void __launch_bounds__(kTableThreads, 1) table_stream(typename K::Elem* __restrict__ dst,
-                                                                 const typename K::Elem* __restrict__ src, uint64_t n,
-                                                                 const uint16_t* __restrict__ table, uint32_t* fault) {
-    extern __shared__ __align__(128) uint16_t tab[];
-    __shared__ __align__(8) uint64_t bar;
-    constexpr int L = K::kLanes;
-    constexpr int U = 8;  // 8 vectors per thread in flight: 128 KB of loads per SM
-    const uint64_t nvec = n / L;
-    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-    const uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    uint4 cur[U];
-#pragma unroll
-    for (int k = 0; k < U; ++k) {
-        const uint64_t i = gid + k * stride;
-        cur[k] = i < nvec ? ld_u4(src + i * L) : make_uint4(0, 0, 0, 0);
-    }
-    if (threadIdx.x == 0) {
-        mbar_init(&bar, 1);
-        mbar_init_fence();
-    }
-    wait_for_prerequisite_grid();  // the table is complete and visible
-    allow_dependent_launch();
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        mbar_expect_tx(&bar, kTableBytes);
-        bulk_load(tab, table, kTableBytes, &bar);
-    }
-    const bool ok = mbar_wait(&bar, 0);
-    if (!__syncthreads_and(ok)) {
-        if (threadIdx.x == 0) {
-            atomicExch(fault, 1u);
-            mbar_wait(&bar, 0);
-        }
-        return;
-    }
-    uint64_t base = gid;
-    for (;;) {
-#pragma unroll
-        for (int k = 0; k < U; ++k) {
-            const uint64_t i = base + k * stride;
-            if (i < nvec) st_u4(dst + i * L, K::apply(tab, cur[k]));
-        }
-        base += U * stride;
-        if (base >= nvec) break;
-#pragma unroll
-        for (int k = 0; k < U; ++k) {
-            const uint64_t i = base + k * stride;
-            cur[k] = i < nvec ? ld_u4(src + i * L) : make_uint4(0, 0, 0, 0);
-        }
-    }
-    const uint64_t t = nvec * L + gid;
-    if (t < n) dst[t] = K::apply1(tab, src[t]);
-}
-
-// Launches build then stream; the stream kernel is a programmatic
-// dependent of the build (scheduled early, synchronised in-kernel).
-template <typename K, typename Build, typename... BuildArgs>
-cudaError_t launch_table_pair(const LaunchEnv& env, const EwPlan& p, int slot, Build build, BuildArgs... args) {
-    static DeviceFlags configured;  // devices with the attribute set
-    if (!configured.done(env.device)) {
-        const cudaError_t err =
-            cudaFuncSetAttribute(table_stream<K>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTableBytes);
-        if (err != cudaSuccess) return err;
-        configured.mark(env.device);
-    }
-    uint16_t* table = reinterpret_cast<uint16_t*>(static_cast<char*>(env.tables) + (uint64_t)slot * kTableBytes);
-    build<<<65536 / 256, 256, 0, env.stream>>>(table, args...);
-    ++*env.launches;
-    cudaError_t err = cudaGetLastError();
-    if (err != cudaSuccess) return err;
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3((unsigned)env.sm_count);
-    cfg.blockDim = dim3(kTableThreads);
-    cfg.dynamicSmemBytes = kTableBytes;
-    cfg.stream = env.stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    uint32_t* fault = reinterpret_cast<uint32_t*>(static_cast<char*>(env.workspace) + kFaultWordOffset);
-    using E = typename K::Elem;
-    err = cudaLaunchKernelEx(&cfg, table_stream<K>, reinterpret_cast<E*>(p.dst.ptr),
-                             reinterpret_cast<const E*>(p.src0.ptr), p.count, (const uint16_t*)table, fault);
-    ++*env.launches;
-    return err != cudaSuccess ? err : cudaGetLastError();
-}
-
 template <int OP>
 cudaError_t unary_typed(const LaunchEnv& env, const EwPlan& p, float pa, float pb) {
-    if (p.dtype == DType::F16) {
-        if constexpr (kTableOp<OP>) {
-            if (p.kind == EwKind::Flat && p.vec && p.count >= kTableMinCount && env.tables != nullptr)
-                return launch_table_pair<HalfTable>(env, p, f16_table_slot(OP), f16_table_build<OP>,
-                                                    UnaryParams{pa, pb});
-        }
-        return launch_ew<uint16_t>(env, p, UnaryFn<OP, true>{UnaryParams{pa, pb}});
-    }
-    if constexpr (OP == kGelu) {
-        if (p.kind == EwKind::Flat && p.vec && p.count >= kTableMinCount && env.tables != nullptr)
-            return launch_table_pair<GeluF32Table>(env, p, kGeluF32TableSlot, gelu_f32_table_build);
-    }
+    if (p.dtype == DType::F16) return launch_ew<uint16_t>(env, p, UnaryFn<OP, true>{UnaryParams{pa, pb}});
     return launch_ew<float>(env, p, UnaryFn<OP, false>{UnaryParams{pa, pb}});
 }
 

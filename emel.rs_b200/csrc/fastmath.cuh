@@ -169,4 +169,135 @@ EMEL_HD float fast_tanhf(float y) {
     return y == 0.0f ? y : r;
 }
 
+
+// ===========================================================================
+// Binary32 exponential family: the default for the activation, soft_max and
+// GLU kernels.  The reference's tolerance for transcendental unary ops is
+// 2 ulp, so the correctly rounded binary64 evaluation above is more than the
+// path needs; this one runs entirely in binary32 FMAs.
+//
+// Method (Cody-Waite reduction, W. J. Cody and W. Waite, "Software Manual
+// for the Elementary Functions", 1980, with a Taylor polynomial):
+//     k = nearest(x / ln2)                       (1.5 * 2^23 shift)
+//     r = x - k * Ln2Hi     exact: Ln2Hi is ln2 rounded to binary32, so
+//                           k * Ln2Hi is a multiple of 2^-24 and the
+//                           difference (|r| < 0.35) fits 24 bits; the FMA
+//                           forms it without intermediate rounding
+//     c = -k * Ln2Lo        (Ln2Lo = ln2 - Ln2Hi, |c| < 3e-7)
+//     e^(r + c) - 1 = r + t,  t = r^2 (1/2! + r/3! + ... + r^5/7!) + c (1 + r)
+//     exp(x) = 2^k (1 + r + t)
+// Taylor truncation at degree 7 is below 2^-27 relative for |r| <= 0.35;
+// the constants are generated by gen_exp_table.py (1/ln2, the ln2 split and
+// 1/k!, each rounded once to binary32).  The power of two is applied as
+// 2^k1 * 2^k2 (k1 kept in the normal range) so results near overflow and
+// in the subnormal range need no special case.
+//
+// expm1(x) = (2^k - 1) + 2^k r + 2^k t: the first two terms are formed with
+// one rounding (2^k r is exact and 2^k - 1 is exact for |k| <= 24), so there
+// is no cancellation; with k = 0 it is r + t.
+// tanh(|y|) = e / (e + 2) with e = expm1(2|y|) > 0 below 0.625 (no
+// cancellation; the quotient's sensitivity to e stays below one), and
+// 1 - 2 / (exp(2|y|) + 1) above, where the subtracted term is small and its
+// relative error becomes a far smaller absolute one: near +-1 the result is
+// the correctly rounded value unless it lies next to a rounding boundary.
+// Over every binary32 input, against binary64 libm rounded once: exp and
+// expm1 within 1 ulp, tanh within 2 (tests/cpp/fastmath_check.cpp).
+// ===========================================================================
+
+EMEL_HD float fma32(float a, float b, float c) {
+#if defined(__CUDA_ARCH__)
+    return __fmaf_rn(a, b, c);
+#else
+    return std::fma(a, b, c);
+#endif
+}
+
+EMEL_HD uint32_t f32_to_bits(float f) {
+#if defined(__CUDA_ARCH__)
+    return __float_as_uint(f);
+#else
+    uint32_t u;
+    std::memcpy(&u, &f, 4);
+    return u;
+#endif
+}
+
+EMEL_HD float bits_to_f32(uint32_t u) {
+#if defined(__CUDA_ARCH__)
+    return __uint_as_float(u);
+#else
+    float f;
+    std::memcpy(&f, &u, 4);
+    return f;
+#endif
+}
+
+// 2^e for -126 <= e <= 127.
+EMEL_HD float pow2i(int e) { return bits_to_f32((uint32_t)(e + 127) << 23); }
+
+// k, r and t with e^(x - k ln2) - 1 = r + t for |x| <= 104: r is the exact
+// reduced argument, t = r^2 (1/2! + ... + r^5/7!) + c (1 + r) carries the
+// rest (|t| < 0.07).
+EMEL_HD void f32_exp_split(float x, int& k, float& r, float& t) {
+    constexpr float kShift = 0x1.8p23f;
+    const float tk = fma32(x, kF32InvLn2, kShift);
+    k = (int)(f32_to_bits(tk) - f32_to_bits(kShift));
+    const float kd = tk - kShift;  // exact
+    r = fma32(-kd, kF32Ln2Hi, x);
+    const float c = -kd * kF32Ln2Lo;
+    float q = fma32(r, kF32InvFact7, kF32InvFact6);
+    q = fma32(q, r, kF32InvFact5);
+    q = fma32(q, r, kF32InvFact4);
+    q = fma32(q, r, kF32InvFact3);
+    q = fma32(q, r, kF32InvFact2);
+    t = fma32(c, r, fma32(r * r, q, c));
+}
+
+// exp(x) within one ulp.  Saturates like the binary32 result (inf above 89,
+// +0 below -104); NaN propagates (every comparison is false).
+EMEL_HD float exp32(float x) {
+    const float xc = x > 89.0f ? 89.0f : (x < -104.0f ? -104.0f : x);
+    int k;
+    float r, t;
+    f32_exp_split(xc, k, r, t);
+    const int k1 = k > 127 ? 127 : (k < -100 ? -100 : k);
+    const float s1 = pow2i(k1), s2 = pow2i(k - k1);
+    const float y = fma32(s1, r + t, s1) * s2;
+    return x > 89.0f ? INFINITY : (x < -104.0f ? 0.0f : y);
+}
+
+// expm1(x) within one ulp; saturates to -1 below -18 and to inf above 89;
+// keeps -0.
+EMEL_HD float expm1_32(float x) {
+    const float xc = x > 89.0f ? 89.0f : (x < -18.0f ? -18.0f : x);
+    int k;
+    float r, t;
+    f32_exp_split(xc, k, r, t);
+    const int k1 = k > 127 ? 127 : k;  // k >= -26 here
+    const int k2 = k - k1;             // 0, or 1 right below the overflow threshold
+    const float s1 = pow2i(k1);
+    // (2^k1 - 2^-k2) + 2^k1 r is formed with one rounding (2^k1 r is exact),
+    // then the small tail 2^k1 t is added
+    const float y = fma32(s1, t, fma32(s1, r, s1 - pow2i(-k2))) * pow2i(k2);
+    if (x == 0.0f) return x;
+    return x > 89.0f ? INFINITY : (x < -18.0f ? -1.0f : y);
+}
+
+// tanh(y) within two ulp; +-1 once |y| >= 10 (binary32 tanh rounds to +-1
+// above 9.02).
+EMEL_HD float tanh32(float y) {
+    const float ay = std::fabs(y);
+    const float ac = ay >= 10.0f ? 10.0f : ay;
+    float t;
+    if (ac < 0.625f) {
+        const float e = expm1_32(2.0f * ac);
+        t = e / (e + 2.0f);
+    } else {
+        t = 1.0f - 2.0f / (exp32(2.0f * ac) + 1.0f);
+    }
+    const float s = y < 0.0f ? -1.0f : 1.0f;
+    const float r = ay >= 10.0f ? s : (y < 0.0f ? -t : t);
+    return y == 0.0f ? y : r;
+}
+
 }  // namespace emel

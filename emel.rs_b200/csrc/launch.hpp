@@ -89,13 +89,6 @@ cudaError_t launch_soft_max_split(const LaunchEnv& env, const RowPlan& plan, boo
 // kernel sets when one of its bounded waits expires.
 constexpr uint64_t kFaultWordOffset = 64;
 
-// binary16 domain tables (elementwise.cu): one slot of 65536 halves per
-// unary op code (0..21 and 64..68), and one for binary32 GELU.
-constexpr int kF16TableSlots = 28;
-constexpr int kGeluF32TableSlot = 27;
-constexpr uint64_t kF16TableSlotBytes = 65536ull * 2ull;
-constexpr int f16_table_slot(int op) { return op < 64 ? op : 22 + (op - 64); }
-
 // Bytes of workspace the whole-tensor reductions need.
 uint64_t reduction_workspace_bytes(int sm_count);
 

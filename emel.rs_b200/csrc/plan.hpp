@@ -88,7 +88,6 @@ struct LaunchEnv {
     uint64_t* launches;
     void* workspace;         // device scratch owned by the context
     uint64_t workspace_bytes;
-    void* tables;            // binary16 domain tables, one 128 KB slot per unary op
 };
 
 }  // namespace emel

@@ -85,7 +85,7 @@ __global__ void __launch_bounds__(kRopeThreads) rope_kernel(RopePlan p) {
                     const uint32_t j = e / nk, k = e - j * nk;
                     const float position =
                         __int2float_rn(*reinterpret_cast<const int32_t*>(p.positions + (p0 + j) * p.pos_stride));
-                    const float frequency = lm_exp(f_div(f_mul(p.neg_log_period, (float)(k0 + k)), (float)half));
+                    const float frequency = lm_exp_cr(f_div(f_mul(p.neg_log_period, (float)(k0 + k)), (float)half));
                     angle = f_mul(f_mul(position, frequency), p.freq_scale);
                 } else {
                     angle = f_mul(table[e], p.freq_scale);

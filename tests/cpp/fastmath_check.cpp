@@ -1,8 +1,14 @@
-// Host build of the device exponential core (emel.rs_b200/csrc/fastmath.cuh):
-// sweeps binary32 inputs with a stride (every sign and exponent: saturation,
-// infinities and NaNs included) and counts results that differ from binary64
-// libm rounded once to binary32.  Prints "n diffs_exp diffs_expm1
-// diffs_tanh max_ulp".
+// Host build of the device exponential cores (emel.rs_b200/csrc/fastmath.cuh).
+//   (default) / "edges": the binary64 core; sweeps binary32 inputs with a
+//     stride (every sign and exponent: saturation, infinities and NaNs
+//     included) and counts results that differ from binary64 libm rounded
+//     once to binary32.  Prints "n diffs_exp diffs_expm1 diffs_tanh max_ulp".
+//   "b32 <stride>": the binary32 core over the same strided sweep; prints
+//     "n max_ulp_exp max_ulp_expm1 max_ulp_tanh nan_mismatches" against
+//     binary64 libm rounded once.
+//   "gelu": the reference's GELU (binary16 round trips, unary.rs:533-539)
+//     with the binary32 tanh against the same formula with glibc's tanhf,
+//     for every binary16 input; prints "inputs max_binary16_steps".
 #include <climits>
 #include <cstdio>
 #include <cstdlib>
@@ -47,7 +53,72 @@ static void check_window(float lo, float hi) {  // every binary32 in [lo, hi], l
 // "edges": every binary32 in windows around the saturation thresholds (exp
 // 89 / -104, expm1 -18, tanh +-10) and around zero; otherwise a stride over
 // all 2^32 bit patterns.
+static void b32_sweep(unsigned stride) {
+    long long n32 = 0, worst32[3] = {0, 0, 0}, nan_bad = 0;
+    for (unsigned long long u = 0; u <= 0xffffffffull; u += stride) {
+        const unsigned b = (unsigned)u;
+        float x;
+        std::memcpy(&x, &b, 4);
+        ++n32;
+        const float got[3] = {emel::exp32(x), emel::expm1_32(x), emel::tanh32(x)};
+        const float want[3] = {(float)std::exp((double)x), (float)std::expm1((double)x), (float)std::tanh((double)x)};
+        for (int k = 0; k < 3; ++k) {
+            if (std::isnan(want[k]) || std::isnan(got[k])) {
+                if (!(std::isnan(want[k]) && std::isnan(got[k]))) ++nan_bad;
+                continue;
+            }
+            const long long d = llabs(ord(got[k]) - ord(want[k]));
+            if (d > worst32[k]) worst32[k] = d;
+        }
+    }
+    std::printf("%lld %lld %lld %lld %lld\n", n32, worst32[0], worst32[1], worst32[2], nan_bad);
+}
+
+static float round_half(float v) { return (float)(_Float16)v; }
+
+static int half_ord(float v) {
+    const _Float16 h = (_Float16)v;
+    short s;
+    std::memcpy(&s, &h, 2);
+    return s < 0 ? -(s & 0x7fff) : s;
+}
+
+template <typename T>
+static float gelu_ref(float v, T tanh_fn) {
+    if (v <= -10.0f) return 0.0f;
+    if (v >= 10.0f) return v;
+    const float q = round_half(v);
+    const float cube = 0.044715f * q * q * q;
+    const float inner = 0.7978846f * (q + cube);
+    return round_half((0.5f * q) * (1.0f + tanh_fn(inner)));
+}
+
+static void gelu_steps() {
+    int worst = 0, inputs = 0;
+    for (int h = 0; h < 65536; ++h) {
+        const unsigned short hb = (unsigned short)h;
+        _Float16 hv;
+        std::memcpy(&hv, &hb, 2);
+        const float v = (float)hv;
+        if (std::isnan(v)) continue;
+        ++inputs;
+        const float want = gelu_ref(v, [](float x) { return tanhf(x); });
+        const float got = gelu_ref(v, [](float x) { return emel::tanh32(x); });
+        const int d = std::abs(half_ord(got) - half_ord(want));
+        if (d > worst) worst = d;
+    }
+    std::printf("%d %d\n", inputs, worst);
+}
+
 int main(int argc, char** argv) {
+    if (argc > 1 && std::string(argv[1]) == "b32") {
+        b32_sweep(argc > 2 ? (unsigned)std::strtoul(argv[2], nullptr, 10) : 61u);
+        return 0;
+    }
+    if (argc > 1 && std::string(argv[1]) == "gelu") {
+        gelu_steps();
+        return 0;
+    }
     if (argc > 1 && std::string(argv[1]) == "edges") {
         const float w[][2] = {{88.0f, 90.0f}, {-105.0f, -103.0f}, {-19.0f, -17.0f}, {9.0f, 11.0f},
                               {-11.0f, -9.0f}, {-1e-38f, 1e-38f}, {-20.0f, -19.0f}};

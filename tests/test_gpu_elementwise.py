@@ -1,8 +1,10 @@
 """Elementwise parity on the GPU: binary (equal-count ordinal contract), row
 broadcast, repeat broadcast and the unary family, against the oracle on the
 same seeded inputs.  Bit-exact for add/sub/mul/div, copies and every
-non-transcendental formula; within 2 ulp (f32) / 1 ulp (f16) where the
-reference calls libm."""
+non-transcendental formula; where the reference calls libm, within 2 ulp of
+the glibc oracle for binary32 results (the tolerance for transcendental
+unary ops) and within one binary16 step for binary16 results and GELU (whose
+formula rounds its output through binary16)."""
 
 import numpy as np
 import pytest
@@ -12,6 +14,10 @@ import gpu_helpers as gh
 pytestmark = pytest.mark.gpu
 
 LIBM = {4, 5, 7, 8, 9, 10, 13, 14, 15, 16, 66, 67, 68}  # formulas that call exp/tanh/log/sin/cos
+# binary32 results evaluated in binary64 and rounded once: the standalone
+# tanh, log, sin, cos (bit-exact against the correctly rounded oracle up to
+# rare double-rounding ties)
+CR_OPS = {4, 66, 67, 68}
 
 
 @pytest.fixture(scope="module")
@@ -227,12 +233,6 @@ def check_unary(op, got, want, want_cr, what):
     if op not in LIBM:
         gh.assert_bits_equal(got, want, what)
         return
-    # the device evaluates libm calls in binary64 and rounds once: bit-exact
-    # against the correctly-rounded-libm oracle up to rare double-rounding ties
-    d_cr = ulps(got, want_cr)
-    assert int(d_cr.max(initial=0)) <= 1 and int(np.count_nonzero(d_cr)) <= max(2, d_cr.size // 1_000_000), (
-        f"{what}: vs CR oracle {int(np.count_nonzero(d_cr))} elements differ, max {int(d_cr.max())} ulp")
-    # against the host glibc libm
     d = ulps(got, want)
     if got.dtype == np.float16:
         assert int(d.max(initial=0)) <= 1, f"{what}: {int(d.max())} binary16 ulp from glibc oracle"
@@ -244,11 +244,22 @@ def check_unary(op, got, want, want_cr, what):
         gh.assert_bits_equal(got[~small], want[~small], what + " (|x| >= 10 passthrough)")
     elif op in CANCELLING:
         fin = np.isfinite(want)
+        assert np.array_equal(np.isfinite(got), fin), f"{what}: non-finite positions"
         err = np.abs(got[fin].astype(np.float64) - want[fin].astype(np.float64))
         assert float(err.max(initial=0)) <= 1e-6 * max(1.0, float(np.abs(want[fin]).max(initial=0))), (
             f"{what}: absolute error {float(err.max())}")
     else:
         assert int(d.max(initial=0)) <= 2, f"{what}: {int(d.max())} ulp from glibc oracle"
+        d_cr = ulps(got, want_cr)
+        if op in CR_OPS:
+            # binary64 evaluation rounded once: the correctly rounded oracle up
+            # to rare double-rounding ties
+            assert int(d_cr.max(initial=0)) <= 1 and int(np.count_nonzero(d_cr)) <= max(2, d_cr.size // 1_000_000), (
+                f"{what}: vs CR oracle {int(np.count_nonzero(d_cr))} elements differ, max {int(d_cr.max())} ulp")
+        else:
+            # the binary32 exponential core (within 1 ulp of the correctly
+            # rounded exp / expm1 over every binary32 input)
+            assert int(d_cr.max(initial=0)) <= 2, f"{what}: {int(d_cr.max())} ulp from the CR oracle"
 
 
 @pytest.mark.parametrize("op", UNARY_ALL)
@@ -280,24 +291,23 @@ def test_cfg2_unary_sweep_full_size(emel, kern, olib, dtype):
 def test_f16_every_input_large_tensor_matches_small(emel, kern, olib, op):
     """Every binary16 bit pattern (NaN payloads, infinities, subnormals, both
     zeros), once in a small tensor and 16 times plus a 5-element tail in a
-    tensor of more than 2^20 elements.  Large dense binary16 tensors of the
-    transcendental ops take the per-launch domain-table path, small ones the
-    direct kernels: both must give the same bits, and match the oracle."""
+    tensor of more than 2^20 elements (grid-stride loops, vector tails): both
+    must give the same bits, and match the oracle."""
     every = np.arange(65536, dtype=np.uint16).view(np.float16)
     small, want, want_cr = run_unary(emel, kern, olib, op, every)
     check_unary(op, small, want, want_cr, f"f16 every input op={op}")
     big = np.concatenate([np.tile(every, 16), every[1000:1005]])
     got_big, _, _ = run_unary_device_only(emel, kern, op, big)
     gh.assert_bits_equal(got_big, np.concatenate([np.tile(small, 16), small[1000:1005]]),
-                         f"f16 op={op}: large (table) vs small (direct)")
+                         f"f16 op={op}: large vs small tensor")
 
 
 def test_gelu_f32_large_tensor_matches_small(emel, kern, olib):
-    """binary32 GELU on more than 2^20 dense elements uses the binary16 domain
-    table (the formula sees only binary16-rounded inputs); smaller tensors
-    use the direct kernel.  Both must agree bit for bit, including inputs
-    next to +-10 that round to +-10 in binary16, NaN payloads and
-    infinities, and match the oracle."""
+    """binary32 GELU (the formula sees only binary16-rounded inputs and rounds
+    its result through binary16) on more than 2^20 dense elements and on the
+    same values split in four smaller tensors: both agree bit for bit,
+    including inputs next to +-10 that round to +-10 in binary16, NaN
+    payloads and infinities, and match the oracle."""
     rng = np.random.default_rng(8)
     near = np.array([9.99609375, 9.996094, 9.9960937, 9.999999, 10.0, -9.99609375, -9.996094, -9.999999, -10.0,
                      np.nextafter(np.float32(10), np.float32(0)), np.nextafter(np.float32(-10), np.float32(0)),
@@ -307,7 +317,7 @@ def test_gelu_f32_large_tensor_matches_small(emel, kern, olib):
                         (rng.standard_normal(1 << 16) * 1e-3).astype(np.float32)])
     got_big, _, _ = run_unary_device_only(emel, kern, 8, x)
     parts = [run_unary_device_only(emel, kern, 8, c)[0] for c in np.array_split(x, 4)]
-    gh.assert_bits_equal(got_big, np.concatenate(parts), "gelu f32: large (table) vs small (direct)")
+    gh.assert_bits_equal(got_big, np.concatenate(parts), "gelu f32: one large tensor vs four smaller ones")
     small = np.concatenate([near, nans, x[:200000]])
     got, want, want_cr = run_unary(emel, kern, olib, 8, small)
     check_unary(8, got, want, want_cr, "gelu f32 edge values")

