@@ -16,7 +16,13 @@ namespace emel {
 namespace {
 
 constexpr int kThreads = 256;
-constexpr int kCtasPerSm = 8;  // 2048 threads per SM, four 16-byte loads each in flight
+// Four resident CTAs per SM (guaranteed by the launch bounds' register cap)
+// with eight 16-byte loads in flight per thread: 128 KB of reads in flight
+// per SM from one full wave.  A grid larger than what is resident would run
+// a partial second wave; fewer threads with more loads each also shorten
+// the ramp and tail that dominate a shard of one dim-3 slice (134 MB).
+constexpr int kCtasPerSm = 4;
+constexpr int kVecsInFlight = 8;
 
 struct ArgPart {
     float v;
@@ -130,30 +136,32 @@ __device__ __forceinline__ float4 vec_load(const VecWalk& w, uint64_t v) {
 
 template <int MODE>
 __device__ __forceinline__ double partial_sum(const RowPlan& p) {
-    double acc = 0.0;
+    double acc = 0.0, acc2 = 0.0;  // two chains: x, y and z, w of every vector
     const uint64_t gthreads = (uint64_t)gridDim.x * blockDim.x;
     const uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if constexpr (MODE != 0) {
+        constexpr int U = kVecsInFlight;
         const VecWalk w = vec_walk<MODE>(p);
-        uint64_t i = gid;
-        for (; i + 3 * gthreads < w.nvec; i += 4 * gthreads) {
-            float4 q[4];
+        const uint32_t G = (uint32_t)gthreads;
+        uint32_t i = (uint32_t)gid;
+        for (; (uint64_t)i + (U - 1) * (uint64_t)G < w.nvec; i += U * G) {
+            float4 q[U];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) q[k] = vec_load<MODE>(w, i + k * gthreads);
+            for (int k = 0; k < U; ++k) q[k] = vec_load<MODE>(w, i + k * G);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
+            for (int k = 0; k < U; ++k) {
                 acc += (double)q[k].x;
+                acc2 += (double)q[k].z;
                 acc += (double)q[k].y;
-                acc += (double)q[k].z;
-                acc += (double)q[k].w;
+                acc2 += (double)q[k].w;
             }
         }
-        for (; i < w.nvec; i += gthreads) {
+        for (; (uint64_t)i < w.nvec; i += G) {
             const float4 a = vec_load<MODE>(w, i);
             acc += (double)a.x;
+            acc2 += (double)a.z;
             acc += (double)a.y;
-            acc += (double)a.z;
-            acc += (double)a.w;
+            acc2 += (double)a.w;
         }
         if constexpr (MODE == 1) {
             const uint64_t n = p.rows * p.ne[0];
@@ -169,7 +177,21 @@ __device__ __forceinline__ double partial_sum(const RowPlan& p) {
             for (uint64_t c = lane; c < p.ne[0]; c += 32) acc += (double)row[(int64_t)c * p.src.st[0]];
         }
     }
-    return acc;
+    return acc + acc2;
+}
+
+// One argmax chain of the vector walk: the running maximum of one lane of
+// the vectors (component c of vector v is element 4v + c) and the vector
+// index where it was taken; idx == kNoVec while no comparable (non-NaN)
+// value has been seen.  Within a chain vectors arrive in increasing order,
+// so the strict > keeps the first occurrence.
+constexpr uint32_t kNoVec = 0xffffffffu;
+
+__device__ __forceinline__ void chain_take(float& best, uint32_t& idx, float v, uint32_t vec) {
+    if ((idx == kNoVec && !is_nan(v)) || v > best) {
+        best = v;
+        idx = vec;
+    }
 }
 
 template <int MODE>
@@ -178,28 +200,39 @@ __device__ __forceinline__ ArgPart partial_arg(const RowPlan& p) {
     const uint64_t gthreads = (uint64_t)gridDim.x * blockDim.x;
     const uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if constexpr (MODE != 0) {
-        // vector v holds logical elements 4v .. 4v+3 in both walks
+        // vector v holds logical elements 4v .. 4v+3 in both walks; four
+        // independent chains, one per vector lane, folded at the end with
+        // the first-index rule
+        constexpr int U = kVecsInFlight;
         const VecWalk w = vec_walk<MODE>(p);
-        uint64_t i = gid;
-        for (; i + 3 * gthreads < w.nvec; i += 4 * gthreads) {
-            float4 q[4];
+        const uint32_t G = (uint32_t)gthreads;
+        float bv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+        uint32_t bi[4] = {kNoVec, kNoVec, kNoVec, kNoVec};
+        uint32_t i = (uint32_t)gid;
+        for (; (uint64_t)i + (U - 1) * (uint64_t)G < w.nvec; i += U * G) {
+            float4 q[U];
 #pragma unroll
-            for (int k = 0; k < 4; ++k) q[k] = vec_load<MODE>(w, i + k * gthreads);
+            for (int k = 0; k < U; ++k) q[k] = vec_load<MODE>(w, i + k * G);
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const int64_t e = (int64_t)(4 * (i + k * gthreads));
-                arg_take(b, q[k].x, e);
-                arg_take(b, q[k].y, e + 1);
-                arg_take(b, q[k].z, e + 2);
-                arg_take(b, q[k].w, e + 3);
+            for (int k = 0; k < U; ++k) {
+                const uint32_t v = i + k * G;
+                chain_take(bv[0], bi[0], q[k].x, v);
+                chain_take(bv[1], bi[1], q[k].y, v);
+                chain_take(bv[2], bi[2], q[k].z, v);
+                chain_take(bv[3], bi[3], q[k].w, v);
             }
         }
-        for (; i < w.nvec; i += gthreads) {
+        for (; (uint64_t)i < w.nvec; i += G) {
             const float4 a = vec_load<MODE>(w, i);
-            arg_take(b, a.x, (int64_t)(4 * i));
-            arg_take(b, a.y, (int64_t)(4 * i + 1));
-            arg_take(b, a.z, (int64_t)(4 * i + 2));
-            arg_take(b, a.w, (int64_t)(4 * i + 3));
+            chain_take(bv[0], bi[0], a.x, i);
+            chain_take(bv[1], bi[1], a.y, i);
+            chain_take(bv[2], bi[2], a.z, i);
+            chain_take(bv[3], bi[3], a.w, i);
+        }
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+            ArgPart q{bv[c], bi[c] != kNoVec ? 1u : 0u, 4 * (int64_t)bi[c] + c};
+            b = better(b, q);
         }
         if constexpr (MODE == 1) {
             const uint64_t n = p.rows * p.ne[0];
@@ -230,7 +263,7 @@ __device__ __forceinline__ bool last_cta(unsigned* ticket) {
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kThreads) sum_all(RowPlan p, double* partials, unsigned* ticket, int mode, void* out) {
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) sum_all(RowPlan p, double* partials, unsigned* ticket, int mode, void* out) {
     pdl_enter();
     __shared__ double sh[kThreads / 32];
     double acc = block_sum(partial_sum<MODE>(p), sh);
@@ -250,7 +283,7 @@ __global__ void __launch_bounds__(kThreads) sum_all(RowPlan p, double* partials,
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kThreads) argmax_all(RowPlan p, ArgPart* partials, unsigned* ticket, int out_kind,
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) argmax_all(RowPlan p, ArgPart* partials, unsigned* ticket, int out_kind,
                                                        int dst_dtype, int64_t index_base, void* out) {
     pdl_enter();
     __shared__ ArgPart sh[kThreads / 32];
@@ -302,7 +335,8 @@ uint64_t reduction_workspace_bytes(int sm_count) {
 }
 
 static uint32_t reduce_grid(const LaunchEnv& env, uint64_t n) {
-    const uint64_t want = (n + (uint64_t)kThreads * 8 - 1) / ((uint64_t)kThreads * 8);
+    constexpr uint64_t per_cta = (uint64_t)kThreads * kVecsInFlight * 4;  // one full batch per thread
+    const uint64_t want = (n + per_cta - 1) / per_cta;
     const uint64_t cap = (uint64_t)env.sm_count * kCtasPerSm;
     const uint64_t g = want < cap ? want : cap;
     return (uint32_t)(g == 0 ? 1 : g);
@@ -311,9 +345,10 @@ static uint32_t reduce_grid(const LaunchEnv& env, uint64_t n) {
 // 1: one dense run; 2: contiguous 16-byte aligned rows whose vector count
 // fits 32-bit addressing; 0: element by element.
 static int walk_mode(const RowPlan& p) {
-    if (p.flat) return 1;
     const uint64_t nvec = p.rows * p.ne[0] / 4;
-    if (p.vec && nvec < (1ull << 32) && p.ne[1] < (1ull << 32) && p.ne[2] < (1ull << 32)) return 2;
+    if (nvec >= (1ull << 32)) return 0;  // the vector walks index vectors in 32 bits
+    if (p.flat) return 1;
+    if (p.vec && p.ne[1] < (1ull << 32) && p.ne[2] < (1ull << 32)) return 2;
     return 0;
 }
 
@@ -369,7 +404,7 @@ emel_cuda_status check_scalar_sum(const emel_tensor_view* src, const emel_tensor
 
 namespace {
 
-constexpr int kNoAllocMaxPartials = 2048;  // one per CTA: 8 CTAs per SM up to 256 SMs
+constexpr int kNoAllocMaxPartials = 2048;  // one per CTA: 4 CTAs per SM up to 512 SMs
 constexpr int kNoAllocMaxDevices = 64;
 constexpr size_t kNoAllocHeader = 256;     // ticket, padded to the partials' alignment
 

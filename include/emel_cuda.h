@@ -291,7 +291,7 @@ EMEL_CUDA_API emel_cuda_status emel_cuda_sum(emel_cuda_context* ctx, void* strea
  * Its scratch is one fixed static device array -- a ticket plus 2048
  * per-block partial sums, 16.25 KiB -- that every GPU which loads this
  * library keeps until the process exits.  A device that would need more
- * than 2048 blocks (more than 256 SMs) gets EMEL_CUDA_OUT_OF_MEMORY and
+ * than 2048 blocks (more than 512 SMs) gets EMEL_CUDA_OUT_OF_MEMORY and
  * nothing is launched.  The first call on each device looks up the array's
  * device address (cudaGetSymbolAddress with that device current); make that
  * first call before any stream capture on the device.  All calls share the
