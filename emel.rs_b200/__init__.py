@@ -52,6 +52,9 @@ class Status(enum.IntEnum):
     UNSUPPORTED_SOURCE_STRIDE = 10
     INVALID_MODE = 11
     INVALID_REQUEST = 12
+    MODEL_INVALID = 13
+    CAPACITY = 14
+    PARSE_FAILED = 15
     DEVICE_ERROR = 16
     TIMEOUT = 17
     INVALID_ARGUMENT = 18
@@ -114,6 +117,30 @@ class CGenericRequest(ctypes.Structure):
                 ("src0", ctypes.POINTER(CView)), ("src1", ctypes.POINTER(CView)),
                 ("src2", ctypes.POINTER(CView)), ("dst", ctypes.POINTER(CView)),
                 ("params", ctypes.c_uint8 * 64), ("params_len", ctypes.c_uint32), ("reserved", ctypes.c_uint32)]
+
+
+class CExecuteRequest(ctypes.Structure):
+    """emel_cuda_execute_request: the data fields of emel-graph's processor
+    ExecuteRequest (processor/sm.rs:170-199), handles as integers."""
+    _fields_ = [("step_plan", ctypes.c_uint64), ("output_out", ctypes.c_uint64), ("lifecycle", ctypes.c_uint64),
+                ("tensor_machine", ctypes.c_uint64), ("step_index", ctypes.c_int32), ("step_size", ctypes.c_int32),
+                ("kv_tokens", ctypes.c_int32), ("expected_outputs", ctypes.c_int32), ("memory_sm", ctypes.c_uint64),
+                ("memory_view", ctypes.c_uint64), ("compute_ctx", ctypes.c_uint64)]
+
+
+class CGgufRequirements(ctypes.Structure):
+    """emel_gguf_requirements: emel-gguf's Requirements (loader/mod.rs:15-27)."""
+    _fields_ = [("tensor_count", ctypes.c_uint32), ("kv_count", ctypes.c_uint32), ("max_key_bytes", ctypes.c_uint32),
+                ("max_value_bytes", ctypes.c_uint32), ("tensor_data_bytes", ctypes.c_uint64)]
+
+
+class CGgufTensorInfo(ctypes.Structure):
+    """emel_gguf_tensor_info: emel-gguf's TensorInfo (loader/mod.rs:58-84)."""
+    _fields_ = [("name_offset", ctypes.c_uint32), ("name_length", ctypes.c_uint32), ("tensor_type", ctypes.c_uint32),
+                ("dimension_count", ctypes.c_uint32), ("dimensions", ctypes.c_uint64 * 4),
+                ("data_offset", ctypes.c_uint64), ("file_offset", ctypes.c_uint64),
+                ("data_section_offset", ctypes.c_uint64), ("alignment", ctypes.c_uint32),
+                ("reserved", ctypes.c_uint32), ("data_size", ctypes.c_uint64)]
 
 
 class CRopeParams(ctypes.Structure):
@@ -220,6 +247,19 @@ SIGNATURES = {
     "emel_cuda_exchange_wait": (_I, [_CTX, _V, _V, _V]),
     "emel_cuda_exchange_wait_sum_argmax": (_I, [_CTX, _V, _V, _V, _P, _P]),
     "emel_cuda_exchange_destroy": (_I, [_CTX, _V]),
+    "emel_cuda_step_create": (_I, [_CTX, _V, ctypes.POINTER(CGenericRequest), ctypes.c_uint32, ctypes.c_uint32,
+                                   ctypes.POINTER(_V)]),
+    "emel_cuda_step_destroy": (_I, [_CTX, _V]),
+    "emel_cuda_step_runs": (ctypes.c_uint64, [_V]),
+    "emel_cuda_run_kernel": (_I, [ctypes.POINTER(CExecuteRequest), ctypes.POINTER(ctypes.c_int32)]),
+    "emel_cuda_layout_view": (_I, [ctypes.POINTER(ctypes.c_uint64), ctypes.c_uint32, ctypes.c_uint32, _V,
+                                   ctypes.c_uint64, _P]),
+    "emel_gguf_probe": (_I, [_V, ctypes.c_uint64, ctypes.POINTER(CGgufRequirements)]),
+    "emel_gguf_parse": (_I, [_V, ctypes.c_uint64, ctypes.POINTER(CGgufRequirements), ctypes.POINTER(CGgufTensorInfo),
+                             ctypes.c_uint32]),
+    "emel_gguf_tensor_view": (_I, [ctypes.POINTER(CGgufTensorInfo), _V, ctypes.c_uint64, _P]),
+    "emel_gguf_upload": (_I, [_CTX, _V, _V, ctypes.c_uint64, ctypes.POINTER(CGgufTensorInfo), _V, ctypes.c_uint64,
+                              _P]),
 }
 
 _lib = None
@@ -1034,3 +1074,124 @@ def argmax_combine(partials):
     val = ctypes.c_float()
     _check(lib().emel_cuda_argmax_combine(arr, len(partials), ctypes.byref(idx), ctypes.byref(val)), "argmax_combine")
     return idx.value, val.value
+
+
+# ---------------------------------------------------------------------------
+# Graph seam: a device kernel step run through the RunKernelFn callback
+# (emel-graph processor/kernel_step/sm.rs:125-126)
+# ---------------------------------------------------------------------------
+
+STEP_CAPTURE = 1
+STEP_ASYNC = 2
+
+
+class ElementType(enum.IntEnum):
+    """emel-tensor's ElementType (crates/emel-tensor/src/lib.rs:8-20)."""
+    F32 = 0
+    F16 = 1
+    BF16 = 2
+    QUANTIZED = 3
+
+
+def layout_view(dimensions, element_type, data_ptr: int, storage_bytes: int) -> "CView":
+    """The dense device view of a TensorLayout (row-major dimensions,
+    element type) stored at `data_ptr`, through emel_cuda_layout_view."""
+    dims = (ctypes.c_uint64 * max(1, len(dimensions)))(*[int(d) for d in dimensions])
+    out = CView()
+    _check(lib().emel_cuda_layout_view(dims, len(dimensions), int(element_type), ctypes.c_void_p(data_ptr),
+                                       storage_bytes, ctypes.byref(out)), "layout_view")
+    return out
+
+
+class KernelStep:
+    """A processor step on the device: the generic events, in order, as one
+    emel_cuda_step; run() calls emel_cuda_run_kernel with an ExecuteRequest
+    naming the step and the context, as the processor's RunKernelFn would."""
+
+    def __init__(self, ctx: Context, stream, events, capture: bool = False, asynchronous: bool = False):
+        self.ctx = ctx
+        reqs = (CGenericRequest * len(events))()
+        keep = []
+        for k, ev in enumerate(events):
+            r = ev.request()
+            keep.append(ev)
+            ctypes.memmove(ctypes.addressof(reqs[k]), ctypes.addressof(r), ctypes.sizeof(r))
+        flags = (STEP_CAPTURE if capture else 0) | (STEP_ASYNC if asynchronous else 0)
+        h = ctypes.c_void_p()
+        self.stream = stream
+        _check(ctx._lib.emel_cuda_step_create(ctx.handle, stream, reqs, len(events), flags, ctypes.byref(h)),
+               "step create")  # the step copied the requests and their views
+        self.handle = h
+
+    def request(self, step_index: int = 0) -> CExecuteRequest:
+        r = CExecuteRequest()
+        r.step_plan = self.handle.value or 0
+        r.compute_ctx = self.ctx.handle.value or 0
+        r.step_index = step_index
+        r.step_size = 1
+        return r
+
+    def run(self, step_index: int = 0):
+        """(ok, status) of one RunKernelFn call."""
+        err = ctypes.c_int32(-1)
+        ok = self.ctx._lib.emel_cuda_run_kernel(ctypes.byref(self.request(step_index)), ctypes.byref(err))
+        return bool(ok), Status(err.value)
+
+    @property
+    def runs(self) -> int:
+        return int(self.ctx._lib.emel_cuda_step_runs(self.handle))
+
+    def close(self):
+        if self.handle:
+            self.ctx._lib.emel_cuda_step_destroy(self.ctx.handle, self.handle)
+            self.handle = None
+
+
+# ---------------------------------------------------------------------------
+# GGUF tensor tables into device buffers (emel-gguf loader/mod.rs:137-232)
+# ---------------------------------------------------------------------------
+
+class GgufError(RuntimeError):
+    def __init__(self, status, what):
+        super().__init__(f"{what}: {Status(status).name}")
+        self.status = Status(status)
+
+
+class GgufImage:
+    """A GGUF image in host memory, probed then parsed (the reference's
+    probe -> bind -> parse: the record storage is allocated here from the
+    probed requirements).  tensors: list of (name, CGgufTensorInfo)."""
+
+    def __init__(self, image: bytes):
+        self.image = bytes(image)
+        self._buf = ctypes.create_string_buffer(self.image, len(self.image)) if self.image else None
+        ptr = ctypes.cast(self._buf, ctypes.c_void_p) if self._buf is not None else None
+        self.requirements = CGgufRequirements()
+        st = lib().emel_gguf_probe(ptr, len(self.image), ctypes.byref(self.requirements))
+        if st != 0:
+            raise GgufError(st, "gguf probe")
+        n = self.requirements.tensor_count
+        self._records = (CGgufTensorInfo * max(1, n))()
+        st = lib().emel_gguf_parse(ptr, len(self.image), ctypes.byref(self.requirements), self._records, n)
+        if st != 0:
+            raise GgufError(st, "gguf parse")
+        self.tensors = []
+        for k in range(n):
+            t = self._records[k]
+            self.tensors.append((self.image[t.name_offset:t.name_offset + t.name_length].decode("utf-8", "replace"), t))
+
+    def record(self, name: str) -> CGgufTensorInfo:
+        for n, t in self.tensors:
+            if n == name:
+                return t
+        raise KeyError(name)
+
+    def upload(self, ctx: Context, name: str, stream=None):
+        """(DeviceBuffer, CView) holding the tensor's serialized bytes."""
+        t = self.record(name)
+        buf = DeviceBuffer(ctx, max(16, t.data_size))
+        view = CView()
+        _check(ctx._lib.emel_gguf_upload(ctx.handle, stream, ctypes.cast(self._buf, ctypes.c_void_p), len(self.image),
+                                         ctypes.byref(t), ctypes.c_void_p(buf.ptr), max(16, t.data_size),
+                                         ctypes.byref(view)), f"gguf upload {name}")
+        return buf, view

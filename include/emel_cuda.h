@@ -73,7 +73,10 @@ typedef enum emel_cuda_status {
     EMEL_CUDA_INDEX_OUT_OF_BOUNDS = 9, /* GetRowsError::IndexOutOfBounds (get_rows.rs:522-535) */
     EMEL_CUDA_UNSUPPORTED_SOURCE_STRIDE = 10, /* GetRowsError::UnsupportedSourceStride */
     EMEL_CUDA_INVALID_MODE = 11,      /* RopeError::InvalidMode (rope.rs:104-117) */
-    EMEL_CUDA_INVALID_REQUEST = 12,   /* FlashAttnError::InvalidRequest (flash_attn.rs:35-44) */
+    EMEL_CUDA_INVALID_REQUEST = 12,   /* FlashAttnError::InvalidRequest (flash_attn.rs:35-44); gguf Error::InvalidRequest */
+    EMEL_CUDA_MODEL_INVALID = 13,     /* emel-gguf Error::ModelInvalid (loader/mod.rs:103-118) */
+    EMEL_CUDA_CAPACITY = 14,          /* emel-gguf Error::Capacity */
+    EMEL_CUDA_PARSE_FAILED = 15,      /* emel-gguf Error::ParseFailed */
     EMEL_CUDA_DEVICE_ERROR = 16,      /* a CUDA runtime call failed */
     EMEL_CUDA_TIMEOUT = 17,           /* a bounded device wait expired */
     EMEL_CUDA_INVALID_ARGUMENT = 18,  /* null context / output pointer */
@@ -621,6 +624,124 @@ typedef struct emel_cuda_generic_request {
 } emel_cuda_generic_request;
 EMEL_CUDA_API emel_cuda_status emel_cuda_generic(emel_cuda_context* ctx, void* stream,
                                                  const emel_cuda_generic_request* request);
+
+/* ---- graph seam: a device kernel step ---------------------------------- */
+/* emel-graph's processor runs a step through RunKernelFn = fn(&ExecuteRequest,
+ * &mut i32) -> bool (crates/emel-graph/src/processor/kernel_step/sm.rs:125-126).
+ * The data fields of its ExecuteRequest (processor/sm.rs:170-199), in the same
+ * order; handles are integers as in the reference: step_plan is an
+ * emel_cuda_step and compute_ctx the emel_cuda_context it was built on. */
+typedef struct emel_cuda_execute_request {
+    uint64_t step_plan;
+    uint64_t output_out;
+    uint64_t lifecycle;
+    uint64_t tensor_machine;
+    int32_t step_index;
+    int32_t step_size;
+    int32_t kv_tokens;
+    int32_t expected_outputs;
+    uint64_t memory_sm;
+    uint64_t memory_view;
+    uint64_t compute_ctx;
+} emel_cuda_execute_request;
+
+typedef struct emel_cuda_step emel_cuda_step;
+#define EMEL_CUDA_STEP_MAX_REQUESTS 4096u
+/* flags: CAPTURE records the requests into one CUDA graph on the first run
+ * and replays it on every later run (the views and op_params are fixed at
+ * creation, as a processor step's bound tensors are); ASYNC returns from
+ * emel_cuda_run_kernel without synchronising the stream (device-side
+ * failures then surface at the caller's next emel_cuda_stream_synchronize). */
+#define EMEL_CUDA_STEP_CAPTURE 1u
+#define EMEL_CUDA_STEP_ASYNC 2u
+/* A step plan: `count` generic requests (emel_cuda_generic's envelope) and
+ * the views they point to, copied, to run in order on `stream`.  Requests
+ * are validated when they run, one by one, exactly as emel_cuda_generic
+ * validates them.  Invalid arguments (null pointers, count 0 or above
+ * EMEL_CUDA_STEP_MAX_REQUESTS, unknown flags, CAPTURE on the legacy stream,
+ * params_len > 64) are EMEL_CUDA_INVALID_ARGUMENT. */
+EMEL_CUDA_API emel_cuda_status emel_cuda_step_create(emel_cuda_context* ctx, void* stream,
+                                                     const emel_cuda_generic_request* requests, uint32_t count,
+                                                     uint32_t flags, emel_cuda_step** out);
+EMEL_CUDA_API emel_cuda_status emel_cuda_step_destroy(emel_cuda_context* ctx, emel_cuda_step* step);
+/* Completed runs of a step (a run counts when every request succeeded). */
+EMEL_CUDA_API uint64_t emel_cuda_step_runs(const emel_cuda_step* step);
+/* The RunKernelFn callback (kernel_step/sm.rs:126): runs the step named by
+ * request->step_plan on request->compute_ctx, synchronises its stream unless
+ * the step is ASYNC, writes the emel_cuda_status to *error_out and returns
+ * nonzero on success.  The first failing request stops the step; its status
+ * is the one reported (nothing after it runs). */
+EMEL_CUDA_API int emel_cuda_run_kernel(const emel_cuda_execute_request* request, int32_t* error_out);
+
+/* emel-tensor's TensorLayout (crates/emel-tensor/src/lib.rs:24-50):
+ * dimensions in row-major order and an ElementType.  Builds the dense view of
+ * such a tensor stored at device address `data`: ne[0] is the innermost
+ * (last) dimension, byte strides dense, unused dimensions 1.  Quantized
+ * elements have no fixed size (the model format names the block type: build
+ * those views from the GGUF tensor type) and are EMEL_CUDA_INVALID_ARGUMENT,
+ * as are rank > 4 and a storage smaller than the dense span. */
+#define EMEL_ELEMENT_F32 0u
+#define EMEL_ELEMENT_F16 1u
+#define EMEL_ELEMENT_BF16 2u
+#define EMEL_ELEMENT_QUANTIZED 3u
+EMEL_CUDA_API emel_cuda_status emel_cuda_layout_view(const uint64_t* dimensions, uint32_t rank, uint32_t element_type,
+                                                     void* data, uint64_t storage_bytes, emel_tensor_view* out);
+
+/* ---- GGUF tensor tables into device buffers ----------------------------- */
+/* emel-gguf's loader (crates/emel-gguf/src/loader/mod.rs:137-232; scanner
+ * loader/detail.rs:294-530), restated for the tensor records.  probe
+ * validates a GGUF v3 image held in host memory (magic, version, every
+ * metadata entry's type and bounds, general.alignment a u32 power of two,
+ * unique non-empty keys and tensor names, at most 4 dimensions, known tensor
+ * types, whole column groups, each tensor's offset the padded running total,
+ * the data section inside the image) and returns the Requirements
+ * (loader/mod.rs:15-27); parse fills one record per tensor (TensorInfo,
+ * loader/mod.rs:58-84) into caller storage of at least tensor_count records.
+ * Errors, with the reference's classes: EMEL_CUDA_PARSE_FAILED (truncated or
+ * inconsistent offsets), EMEL_CUDA_MODEL_INVALID (unsupported or invalid
+ * constructs), EMEL_CUDA_CAPACITY (counts, sizes or caller capacity),
+ * EMEL_CUDA_INVALID_REQUEST (null image or requirements, or a parse whose
+ * counts differ from the probe's).  Metadata values are validated and
+ * skipped (the tensor table is what feeds the device). */
+typedef struct emel_gguf_requirements {
+    uint32_t tensor_count;
+    uint32_t kv_count;
+    uint32_t max_key_bytes;
+    uint32_t max_value_bytes;
+    uint64_t tensor_data_bytes;
+} emel_gguf_requirements;
+typedef struct emel_gguf_tensor_info {
+    uint32_t name_offset;     /* byte offset of the name in the image */
+    uint32_t name_length;
+    uint32_t tensor_type;     /* GGML wire code (SerializedType) */
+    uint32_t dimension_count;
+    uint64_t dimensions[4];   /* ne order, unused entries 1 */
+    uint64_t data_offset;     /* relative to the tensor-data section */
+    uint64_t file_offset;     /* absolute in the image */
+    uint64_t data_section_offset;
+    uint32_t alignment;
+    uint32_t reserved;
+    uint64_t data_size;       /* unpadded payload bytes */
+} emel_gguf_tensor_info;
+EMEL_CUDA_API emel_cuda_status emel_gguf_probe(const uint8_t* image, uint64_t image_bytes,
+                                               emel_gguf_requirements* out);
+EMEL_CUDA_API emel_cuda_status emel_gguf_parse(const uint8_t* image, uint64_t image_bytes,
+                                               const emel_gguf_requirements* probed, emel_gguf_tensor_info* tensors,
+                                               uint32_t tensor_capacity);
+/* The device view of a parsed tensor stored at `data`: F32, F16 and BF16 as
+ * dense views; Q4_0, Q4_1, Q5_0, Q8_0, Q2_K, Q3_K, Q4_K and Q6_K as the block
+ * views the row gather and the vocabulary argmax consume (ne[0] values per
+ * row, nb[0] == 1, nb[1] the row's bytes).  Other GGUF types have no device
+ * kernel: EMEL_CUDA_UNSUPPORTED_OPERATION.  storage_bytes below data_size is
+ * EMEL_CUDA_INVALID_ARGUMENT. */
+EMEL_CUDA_API emel_cuda_status emel_gguf_tensor_view(const emel_gguf_tensor_info* tensor, void* data,
+                                                     uint64_t storage_bytes, emel_tensor_view* out);
+/* Copies one parsed tensor's serialized bytes from the host image into
+ * device memory `device_dst` (stream-ordered, like emel_cuda_memcpy_h2d)
+ * and writes its view (emel_gguf_tensor_view). */
+EMEL_CUDA_API emel_cuda_status emel_gguf_upload(emel_cuda_context* ctx, void* stream, const uint8_t* image,
+                                                uint64_t image_bytes, const emel_gguf_tensor_info* tensor,
+                                                void* device_dst, uint64_t device_bytes, emel_tensor_view* view_out);
 
 /* ---- peer exchange over NVLink (multi-GPU partials) -------------------- */
 /* One process per GPU shards a tensor; each rank's small partial (the f64

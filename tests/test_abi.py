@@ -23,7 +23,7 @@ ACCEPTED = 18  # EMEL_CUDA_INVALID_ARGUMENT from the null context after validati
 
 def declared_symbols():
     text = HEADER.read_text()
-    return sorted(set(re.findall(r"\b(emel_cuda_[a-z0-9_]+)\s*\(", text)))
+    return sorted(set(re.findall(r"\b(emel_(?:cuda|gguf)_[a-z0-9_]+)\s*\(", text)))
 
 
 def test_library_exports_every_declared_symbol(emel):
