@@ -494,6 +494,7 @@ def run_suite(args):
                  "cfg3": ["rms_norm", "rms_norm_mul_fused", "rms_norm_then_mul_two_ops", "norm", "sum_rows"],
                  "cfg5": ["repeat_mul_permuted", "repeat_add_permuted", "sum_whole_permuted",
                           "argmax_whole_permuted", "cont_permuted"],
+                 "cfg5_shard": ["repeat_mul_slice", "repeat_add_slice", "sum_slice", "argmax_slice"],
                  "glu": list(W.GLU_OPS), "get_rows": [f"get_rows_{f}" for f in W.EMB_FORMATS],
                  "rope": ["rope_neox", "rope_norm"],
                  "matvec": ["mul_mat_argmax_vocab", "mul_mat_argmax_q8_0_vocab", "mul_mat_argmax_q2_k_vocab",
@@ -619,6 +620,29 @@ def run_suite(args):
         measure("cfg5", "cont_permuted", 2 * spec.ops[2].bytes, spec.ops[2].elements,
                 lambda k: (lambda: chk(lib.emel_cuda_cont(ctx.handle, sh, B(v0), B(vd5)))), 1)
         del t0, t1, td
+    # configuration 5 on one dim-3 slice: what each GPU holds at N=8 (134 MB
+    # of src0); two shard copies alternate so no launch finds its input in L2
+    if wants("cfg5_shard",):
+        spec = W.cfg5_spec(ne3=1)
+        ne1s, nb1s = W.cfg5_src0_view(ne3=1)
+        sh0 = [torch.from_numpy(W.cfg5(ne3=1, shard=j)[0]).to(dev) for j in range(2)]
+        t1 = torch.from_numpy(W.cfg5(ne3=1, shard=0)[1]).to(dev)
+        outs = [torch.empty_like(sh0[0]) for _ in range(2)]
+        v0s = [view(t, ne1s, nb1s) for t in sh0]
+        vds = [view(t, ne1s) for t in outs]
+        v1 = view(t1, [128, 1, 8192, 1])
+        one = [1, 1, 1, 1]
+        tsum, targ = torch.empty(1, device=dev), torch.empty(1, dtype=torch.int64, device=dev)
+        vsum, varg = view(tsum, one), view(targ, one, code=27)
+        for op, opname in ((2, "mul"), (0, "add")):
+            measure("cfg5_shard", f"repeat_{opname}_slice", spec.ops[0].bytes, spec.ops[0].elements,
+                    lambda k, op=op: (lambda: chk(lib.emel_cuda_binary_repeat(ctx.handle, sh, op, B(v0s[k]), B(v1),
+                                                                               B(vds[k])))), 2)
+        measure("cfg5_shard", "sum_slice", spec.ops[2].bytes, spec.ops[2].elements,
+                lambda k: (lambda: chk(lib.emel_cuda_sum(ctx.handle, sh, B(v0s[k]), B(vsum)))), 2)
+        measure("cfg5_shard", "argmax_slice", spec.ops[3].bytes, spec.ops[3].elements,
+                lambda k: (lambda: chk(lib.emel_cuda_argmax(ctx.handle, sh, B(v0s[k]), B(varg)))), 2)
+        del sh0, t1, outs
     # gated linear units (glu.rs) on configuration 2's feed-forward shape
     if wants("glu",):
         spec = W.glu_spec()

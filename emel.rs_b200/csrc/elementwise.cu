@@ -27,28 +27,42 @@ namespace {
 
 constexpr int kThreads = 256;
 
+// Formula functors.  operator() is the full per-element evaluation (a fast
+// pass and, for a NaN result, the exact recompute with the x86 NaN rules);
+// fast() is the fast pass alone, for vector paths that check a whole vector
+// for NaN results and redo only such vectors lane by lane (kHeavy: the
+// formula has a separate fast pass).
 template <int OP, bool IN_F16>
 struct UnaryFn {
     UnaryParams p;
     static constexpr bool kBinary = false;
+    static constexpr bool kHeavy = kHeavyFormula<OP>;
     static constexpr int kUnroll = kHeavyFormula<OP> ? 2 : 4;  // arithmetic-bound ops need fewer loads in flight
     static constexpr int kMinBlocks = 4;  // 64 registers: a tighter cap spills the vectors in flight
     __device__ __forceinline__ float operator()(float a, float) const { return unary_apply<OP, IN_F16>(a, p); }
+    __device__ __forceinline__ float fast(float a, float) const {
+        if constexpr (kHeavy) return unary_formula<OP, (IN_F16 || OP == kGelu) ? kHalf : kFast, IN_F16>(a, p);
+        else return unary_apply<OP, IN_F16>(a, p);
+    }
 };
 
 template <int OP>
 struct BinaryFn {
     static constexpr bool kBinary = true;
+    static constexpr bool kHeavy = false;
     static constexpr int kUnroll = 4;
     static constexpr int kMinBlocks = 3;  // two operands of four vectors each: 85 registers
     __device__ __forceinline__ float operator()(float a, float b) const { return binary_apply<OP>(a, b); }
+    __device__ __forceinline__ float fast(float a, float b) const { return binary_apply<OP>(a, b); }
 };
 
 // activation.rs:467-481, silu_back as a two-input formula: grad * silu'(x).
 struct SiluBackFn {
     static constexpr bool kBinary = true;
+    static constexpr bool kHeavy = false;
     static constexpr int kUnroll = 2;
     static constexpr int kMinBlocks = 4;
+    __device__ __forceinline__ float fast(float x, float grad) const { return (*this)(x, grad); }
     __device__ __forceinline__ float operator()(float x, float grad) const {
         const float sigmoid = f_div(1.0f, f_add(1.0f, lm_exp_cr(f_neg(x))));
         const float derivative = f_mul(sigmoid, f_add(1.0f, f_mul(x, f_sub(1.0f, sigmoid))));
@@ -60,9 +74,14 @@ struct SiluBackFn {
 template <int SUB>
 struct GluFn {
     static constexpr bool kBinary = true;
+    static constexpr bool kHeavy = SUB != kReGlu;
     static constexpr int kUnroll = SUB == kReGlu ? 4 : 2;
     static constexpr int kMinBlocks = 3;
     __device__ __forceinline__ float operator()(float value, float g) const { return glu_apply<SUB>(value, g); }
+    __device__ __forceinline__ float fast(float value, float g) const {
+        if constexpr (kHeavy) return glu_formula<SUB, kFast>(value, g);
+        else return glu_apply<SUB>(value, g);
+    }
 };
 
 // Per-lane path (binary16 vectors with a NaN in or out take it rarely; f32
@@ -79,6 +98,19 @@ template <typename T, typename F>
 __device__ __forceinline__ Vec16<T> apply_vec_scalar(const F& f, const Vec16<T>& a, const Vec16<T>& b) {
     if constexpr (sizeof(T) == 2) return apply_vec_lanes<T>(f, a, b);
     Vec16<T> r;
+    if constexpr (F::kHeavy) {
+        // fast pass on every lane; a vector with a NaN result is redone lane
+        // by lane with the exact recompute (one out-of-line call site)
+        bool nan_out = false;
+#pragma unroll
+        for (int k = 0; k < Vec16<T>::N; ++k) {
+            const float v = f.fast(vget(a, k), F::kBinary ? vget(b, k) : 0.0f);
+            nan_out |= is_nan(v);
+            vset(r, k, v);
+        }
+        if (nan_out) return apply_vec_lanes<T>(f, a, b);
+        return r;
+    }
 #pragma unroll
     for (int k = 0; k < Vec16<T>::N; ++k) vset(r, k, f(vget(a, k), F::kBinary ? vget(b, k) : 0.0f));
     return r;
@@ -110,8 +142,8 @@ __device__ __forceinline__ Vec16<T> apply_vec(const F& f, const Vec16<T>& a, con
                 const float2 xa = __half22float2(*reinterpret_cast<const __half2*>(&wa[k]));
                 float2 xb = make_float2(0.0f, 0.0f);
                 if constexpr (F::kBinary) xb = __half22float2(*reinterpret_cast<const __half2*>(&wb[k]));
-                const float r0 = f(xa.x, xb.x);
-                const float r1 = f(xa.y, xb.y);
+                const float r0 = f.fast(xa.x, xb.x);
+                const float r1 = f.fast(xa.y, xb.y);
                 nan_out |= is_nan(r0) | is_nan(r1);
                 const __half2 h = __floats2half2_rn(r0, r1);
                 wr[k] = *reinterpret_cast<const unsigned*>(&h);
