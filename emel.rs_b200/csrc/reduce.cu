@@ -182,16 +182,16 @@ __device__ __forceinline__ double partial_sum(const RowPlan& p) {
 
 // One argmax chain of the vector walk: the running maximum of one lane of
 // the vectors (component c of vector v is element 4v + c) and the vector
-// index where it was taken; idx == kNoVec while no comparable (non-NaN)
-// value has been seen.  Within a chain vectors arrive in increasing order,
-// so the strict > keeps the first occurrence.
-constexpr uint32_t kNoVec = 0xffffffffu;
-
+// index where it was taken.  best starts as NaN; fmaxf ignores a NaN
+// operand, so nb = fmaxf(best, v) differs from best exactly when v is
+// strictly greater (the strict > of reductions.rs:721) or v is the chain's
+// first non-NaN value; a tie keeps the earlier index (vectors arrive in
+// increasing order within a chain).  A chain whose best is still NaN saw
+// no comparable value.  Three instructions per element.
 __device__ __forceinline__ void chain_take(float& best, uint32_t& idx, float v, uint32_t vec) {
-    if ((idx == kNoVec && !is_nan(v)) || v > best) {
-        best = v;
-        idx = vec;
-    }
+    const float nb = fmaxf(best, v);
+    if (nb != best) idx = vec;  // unordered compare: true while best is NaN
+    best = nb;
 }
 
 template <int MODE>
@@ -206,8 +206,9 @@ __device__ __forceinline__ ArgPart partial_arg(const RowPlan& p) {
         constexpr int U = kVecsInFlight;
         const VecWalk w = vec_walk<MODE>(p);
         const uint32_t G = (uint32_t)gthreads;
-        float bv[4] = {0.0f, 0.0f, 0.0f, 0.0f};
-        uint32_t bi[4] = {kNoVec, kNoVec, kNoVec, kNoVec};
+        const float nan = __int_as_float(0x7fc00000);
+        float bv[4] = {nan, nan, nan, nan};
+        uint32_t bi[4] = {0, 0, 0, 0};
         uint32_t i = (uint32_t)gid;
         for (; (uint64_t)i + (U - 1) * (uint64_t)G < w.nvec; i += U * G) {
             float4 q[U];
@@ -231,7 +232,7 @@ __device__ __forceinline__ ArgPart partial_arg(const RowPlan& p) {
         }
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-            ArgPart q{bv[c], bi[c] != kNoVec ? 1u : 0u, 4 * (int64_t)bi[c] + c};
+            ArgPart q{bv[c], is_nan(bv[c]) ? 0u : 1u, 4 * (int64_t)bi[c] + c};
             b = better(b, q);
         }
         if constexpr (MODE == 1) {

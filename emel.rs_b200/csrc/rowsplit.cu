@@ -383,8 +383,13 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kStagedT
     __syncthreads();
     if (threadIdx.x == 0)
         for (uint32_t j = 0; j < pieces && j < (uint32_t)kArgRingPieces; ++j) issue(j);
-    ArgBest init{0.0f, 0, 0};
-    ArgBest bl[4] = {init, init, init, init};
+    // four chains, one per vector lane: best starts as NaN and nb =
+    // fmaxf(best, v) differs from it exactly for a strictly greater value or
+    // the chain's first non-NaN one (NaN never wins; ties keep the earlier
+    // column, which arrives first in a chain)
+    const float nan = __int_as_float(0x7fc00000);
+    float bv[4] = {nan, nan, nan, nan};
+    uint32_t bc[4] = {0, 0, 0, 0};  // vector index within the chunk
     uint32_t j = 0;
     for (; j < pieces; ++j) {
         const uint32_t slot = j % kArgRingPieces, parity = (j / kArgRingPieces) & 1u;
@@ -394,11 +399,13 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kStagedT
         const uint32_t v0 = j * kPieceVecs, v1 = v0 + kPieceVecs < nv ? v0 + kPieceVecs : nv;
         for (uint32_t v = v0 + threadIdx.x; v < v1; v += kStagedThreadsArg) {
             const float4 q = ring[slot][v - v0];
-            const int64_t c = (int64_t)(ch.col0 + 4ull * v);
-            arg_take(bl[0], q.x, c);
-            arg_take(bl[1], q.y, c + 1);
-            arg_take(bl[2], q.z, c + 2);
-            arg_take(bl[3], q.w, c + 3);
+            const float q4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int l = 0; l < 4; ++l) {
+                const float nb = fmaxf(bv[l], q4[l]);
+                if (nb != bv[l]) bc[l] = v;
+                bv[l] = nb;
+            }
         }
         __syncthreads();  // every thread is done with this slot
         if (threadIdx.x == 0 && j + kArgRingPieces < pieces) issue(j + kArgRingPieces);
@@ -410,6 +417,10 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kStagedT
         for (uint32_t k = j; k < pieces && k < j + kArgRingPieces; ++k)
             mbar_wait(&bars[k % kArgRingPieces], (k / kArgRingPieces) & 1u);
     }
+    ArgBest bl[4];
+#pragma unroll
+    for (int l = 0; l < 4; ++l)
+        bl[l] = ArgBest{bv[l], (int64_t)(ch.col0 + 4ull * bc[l] + l), is_nan(bv[l]) ? 0u : 1u};
     ArgBest b = arg_better(arg_better(bl[0], bl[1]), arg_better(bl[2], bl[3]));
     b = group_argmax<kStagedThreadsArg>(b, &s);
     if (threadIdx.x == 0) {

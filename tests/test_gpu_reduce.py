@@ -113,6 +113,33 @@ def test_argmax_ties_nan_and_f32_encoding(emel, kern):
     assert gotf == np.float32(1000.0)
 
 
+@pytest.mark.parametrize("n", [4096, 1 << 22])
+def test_argmax_lane_chain_edges(emel, kern, n):
+    """The vector walk's per-lane chains: all NaN and all -inf give 0; a
+    lone late comparable value wins; -0 and +0 tie to the first; NaN runs
+    in front of the maximum are skipped."""
+    cases = []
+    x = np.full(n, np.nan, np.float32)
+    cases.append((x.copy(), 0))
+    x[n - 7] = -3.0
+    cases.append((x.copy(), n - 7))
+    cases.append((np.full(n, -np.inf, np.float32), 0))
+    z = np.zeros(n, np.float32)
+    z[0] = -0.0
+    cases.append((z, 0))
+    y = np.full(n, -1.0, np.float32)
+    y[: n // 2] = np.nan
+    y[0] = 2.0
+    y[n // 2 + 5] = 2.0  # later equal value loses to element 0
+    cases.append((y, 0))
+    y2 = y.copy()
+    y2[0] = -9.0
+    cases.append((y2, n // 2 + 5))
+    for arr, expect in cases:
+        got, want = device_argmax(emel, kern, arr, [n, 1, 1, 1])
+        assert int(got) == want == expect, (n, int(got), want, expect)
+
+
 def test_argmax_strided(emel, kern):
     rng = np.random.default_rng(8)
     x = rng.standard_normal(64 * 50 * 3).astype(np.float32)

@@ -366,8 +366,16 @@ def test_split_argmax_rows_ties_across_chunks_and_nans(emel, kern, oracle_lib):
     the earlier column; a NaN at column 0 pins 0; NaNs elsewhere are skipped;
     an all-NaN row gives 0."""
     rng = np.random.default_rng(46)
-    v, rows = 151936, 6
+    v, rows = 151936, 10
     x = rng.standard_normal(v * rows).astype(np.float32).reshape(rows, v)
+    x[6, :] = np.nan
+    x[6, 140000] = -5.0      # the row's only comparable value, late in the last chunk
+    x[7, :] = 0.0
+    x[7, 0] = -0.0           # -0 and +0 tie: the first column
+    x[8, :] = -np.inf
+    x[8, 3] = -1e30
+    x[9, :40000] = np.nan    # NaNs ahead of every lane chain's first value
+    x[9, 40001] = 7.0
     x[0, 150000] = 50.0
     x[0, 19000] = 50.0       # same maximum, earlier chunk
     x[1, 0] = np.nan
@@ -380,6 +388,7 @@ def test_split_argmax_rows_ties_across_chunks_and_nans(emel, kern, oracle_lib):
         got, want = run_row_op(emel, kern, oracle_lib, "argmax_rows", x.ravel(), [v, rows, 1, 1], out_dtype=dt)
         assert np.array_equal(got, want), (np.dtype(dt).name, got, want)
     assert got.astype(np.int64).tolist()[:2] == [19000, 0]
+    assert got.astype(np.int64).tolist()[6:] == [140000, 0, 3, 40001]
 
 
 @pytest.mark.parametrize("width", [40001, 151936])
