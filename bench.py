@@ -582,6 +582,7 @@ def run_suite(args):
     if wants("soft_max_vocab", "argmax_rows_vocab", "cfg4"):
         logits, _ = W.cfg4b()
         v, rws = W.CFG4B_NE
+        spec = W.cfg4_spec()
         S = sets_for(spec.ops[1].bytes)
         tl = [torch.from_numpy(logits).to(dev) for _ in range(S)]
         tlo = [torch.empty_like(tl[0]) for _ in range(S)]

@@ -62,7 +62,6 @@ struct SiluBackFn {
     static constexpr bool kHeavy = false;
     static constexpr int kUnroll = 2;
     static constexpr int kMinBlocks = 4;
-    __device__ __forceinline__ float fast(float x, float grad) const { return (*this)(x, grad); }
     __device__ __forceinline__ float operator()(float x, float grad) const {
         const float sigmoid = f_div(1.0f, f_add(1.0f, lm_exp_cr(f_neg(x))));
         const float derivative = f_mul(sigmoid, f_add(1.0f, f_mul(x, f_sub(1.0f, sigmoid))));
@@ -96,11 +95,12 @@ __device__ __noinline__ Vec16<T> apply_vec_lanes(const F& f, const Vec16<T>& a, 
 
 template <typename T, typename F>
 __device__ __forceinline__ Vec16<T> apply_vec_scalar(const F& f, const Vec16<T>& a, const Vec16<T>& b) {
-    if constexpr (sizeof(T) == 2) return apply_vec_lanes<T>(f, a, b);
-    Vec16<T> r;
-    if constexpr (F::kHeavy) {
+    if constexpr (sizeof(T) == 2) {
+        return apply_vec_lanes<T>(f, a, b);
+    } else if constexpr (F::kHeavy) {
         // fast pass on every lane; a vector with a NaN result is redone lane
         // by lane with the exact recompute (one out-of-line call site)
+        Vec16<T> r;
         bool nan_out = false;
 #pragma unroll
         for (int k = 0; k < Vec16<T>::N; ++k) {
@@ -110,10 +110,12 @@ __device__ __forceinline__ Vec16<T> apply_vec_scalar(const F& f, const Vec16<T>&
         }
         if (nan_out) return apply_vec_lanes<T>(f, a, b);
         return r;
-    }
+    } else {
+        Vec16<T> r;
 #pragma unroll
-    for (int k = 0; k < Vec16<T>::N; ++k) vset(r, k, f(vget(a, k), F::kBinary ? vget(b, k) : 0.0f));
-    return r;
+        for (int k = 0; k < Vec16<T>::N; ++k) vset(r, k, f(vget(a, k), F::kBinary ? vget(b, k) : 0.0f));
+        return r;
+    }
 }
 
 // True when any of the eight binary16 lanes of `v` is a NaN.
@@ -525,9 +527,183 @@ cudaError_t launch_ew(const LaunchEnv& env, const EwPlan& p, const F& f) {
     return cudaGetLastError();
 }
 
+// ---------------------------------------------------------------------------
+// binary16 unary ops through context-resident domain tables.
+//
+// A binary16 operand has 65,536 possible values, far fewer than the
+// elements of a large tensor.  When a context is created, one kernel
+// evaluates every table op's formula -- the same unary_apply<OP, true> and
+// reference conversions the direct kernels use -- for every binary16 input
+// into a 128 KB table per op, and the tables stay with the context.  A large
+// dense binary16 tensor then streams through a shared-memory copy of its
+// op's table: no per-element arithmetic, identical bits to the direct path.
+// ---------------------------------------------------------------------------
+template <int OP>
+constexpr bool kTableOp = (kHeavyFormula<OP> || OP == kSqrt || OP == kLog || OP == kSin || OP == kCos) && OP < 128;
+
+constexpr int kTableOpCodes[kDomainTableSlots] = {kTanh, kElu, kSigmoid, kGelu, kGeluQuick, kSilu, kHardswish,
+                                                  kHardsigmoid, kExp, kExpm1, kSoftplus, kGeluErf, kSqrt, kLog,
+                                                  kSin, kCos};
+
+constexpr int table_slot(int op) {
+    for (int k = 0; k < kDomainTableSlots; ++k)
+        if (kTableOpCodes[k] == op) return k;
+    return -1;
+}
+
+// the build kernel's case labels follow kTableOpCodes
+static_assert(table_slot(kTanh) == 0, "slot order");
+static_assert(table_slot(kElu) == 1, "slot order");
+static_assert(table_slot(kSigmoid) == 2, "slot order");
+static_assert(table_slot(kGelu) == 3, "slot order");
+static_assert(table_slot(kGeluQuick) == 4, "slot order");
+static_assert(table_slot(kSilu) == 5, "slot order");
+static_assert(table_slot(kHardswish) == 6, "slot order");
+static_assert(table_slot(kHardsigmoid) == 7, "slot order");
+static_assert(table_slot(kExp) == 8, "slot order");
+static_assert(table_slot(kExpm1) == 9, "slot order");
+static_assert(table_slot(kSoftplus) == 10, "slot order");
+static_assert(table_slot(kGeluErf) == 11, "slot order");
+static_assert(table_slot(kSqrt) == 12, "slot order");
+static_assert(table_slot(kLog) == 13, "slot order");
+static_assert(table_slot(kSin) == 14, "slot order");
+static_assert(table_slot(kCos) == 15, "slot order");
+
+constexpr uint64_t kTableMinCount = 1ull << 20;  // below this the 128 KB table copy costs more than it saves
+constexpr int kTableThreads = 1024;              // one stream CTA per SM
+constexpr uint32_t kTableBytes = 65536u * 2u;
+
+template <int OP>
+__device__ __forceinline__ void fill_entry(uint16_t* t, uint32_t h) {
+    t[h] = f32_to_f16_bits(unary_apply<OP, true>(f16_bits_to_f32((uint16_t)h), UnaryParams{}));
+}
+
+__global__ void __launch_bounds__(256) domain_tables_build(uint16_t* __restrict__ tables) {
+    const uint32_t h = blockIdx.x * 256u + threadIdx.x;
+    uint16_t* t = tables + (uint64_t)blockIdx.y * 65536u;
+    switch (blockIdx.y) {
+    case 0: fill_entry<kTanh>(t, h); break;
+    case 1: fill_entry<kElu>(t, h); break;
+    case 2: fill_entry<kSigmoid>(t, h); break;
+    case 3: fill_entry<kGelu>(t, h); break;
+    case 4: fill_entry<kGeluQuick>(t, h); break;
+    case 5: fill_entry<kSilu>(t, h); break;
+    case 6: fill_entry<kHardswish>(t, h); break;
+    case 7: fill_entry<kHardsigmoid>(t, h); break;
+    case 8: fill_entry<kExp>(t, h); break;
+    case 9: fill_entry<kExpm1>(t, h); break;
+    case 10: fill_entry<kSoftplus>(t, h); break;
+    case 11: fill_entry<kGeluErf>(t, h); break;
+    case 12: fill_entry<kSqrt>(t, h); break;
+    case 13: fill_entry<kLog>(t, h); break;
+    case 14: fill_entry<kSin>(t, h); break;
+    case 15: fill_entry<kCos>(t, h); break;
+    default: break;
+    }
+}
+
+__device__ __forceinline__ uint32_t lookup2(const uint16_t* tab, uint32_t w) {
+    return (uint32_t)tab[w & 0xffffu] | ((uint32_t)tab[w >> 16] << 16);
+}
+
+__device__ __forceinline__ uint4 ld_u4(const void* p) {
+    uint4 v;
+    asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p));
+    return v;
+}
+
+__device__ __forceinline__ void st_u4(void* p, uint4 v) {
+    asm volatile("st.global.L1::no_allocate.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w)
+                 : "memory");
+}
+
+// One CTA of 1024 threads per SM.  After the previous kernel of the stream
+// has completed (it may have produced the input), thread 0 has the TMA
+// engine copy the op's 128 KB table into shared memory while every thread
+// issues its first 8 vector loads (128 KB per SM in flight); then
+// grid-strided 16-byte vectors stream through the table, 8 per iteration.
+__global__ void __launch_bounds__(kTableThreads, 1) table_stream(uint16_t* __restrict__ dst,
+                                                                 const uint16_t* __restrict__ src, uint64_t n,
+                                                                 const uint16_t* __restrict__ table, uint32_t* fault) {
+    extern __shared__ __align__(128) uint16_t tab[];
+    __shared__ __align__(8) uint64_t bar;
+    pdl_enter();
+    constexpr int L = 8;  // halves per 16-byte vector
+    constexpr int U = 8;
+    const uint64_t nvec = n / L;
+    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
+    const uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (threadIdx.x == 0) {
+        mbar_init(&bar, 1);
+        mbar_init_fence();
+        mbar_expect_tx(&bar, kTableBytes);
+        bulk_load(tab, table, kTableBytes, &bar);
+    }
+    uint4 cur[U];
+#pragma unroll
+    for (int k = 0; k < U; ++k) {
+        const uint64_t i = gid + k * stride;
+        cur[k] = i < nvec ? ld_u4(src + i * L) : make_uint4(0, 0, 0, 0);
+    }
+    __syncthreads();  // the barrier is initialised before any thread waits on it
+    const bool ok = mbar_wait(&bar, 0);
+    if (!__syncthreads_and(ok)) {
+        if (threadIdx.x == 0) {
+            atomicExch(fault, 1u);
+            mbar_wait(&bar, 0);
+        }
+        return;
+    }
+    uint64_t base = gid;
+    for (;;) {
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const uint64_t i = base + k * stride;
+            if (i < nvec)
+                st_u4(dst + i * L, make_uint4(lookup2(tab, cur[k].x), lookup2(tab, cur[k].y), lookup2(tab, cur[k].z),
+                                              lookup2(tab, cur[k].w)));
+        }
+        base += U * stride;
+        if (base >= nvec) break;
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const uint64_t i = base + k * stride;
+            cur[k] = i < nvec ? ld_u4(src + i * L) : make_uint4(0, 0, 0, 0);
+        }
+    }
+    const uint64_t t = nvec * L + gid;
+    if (t < n) dst[t] = tab[src[t]];
+}
+
+cudaError_t launch_table_stream(const LaunchEnv& env, const EwPlan& p, int slot) {
+    static DeviceFlags configured;  // devices with the attribute set
+    if (!configured.done(env.device)) {
+        const cudaError_t err =
+            cudaFuncSetAttribute(table_stream, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kTableBytes);
+        if (err != cudaSuccess) return err;
+        configured.mark(env.device);
+    }
+    const uint16_t* table = static_cast<const uint16_t*>(env.tables) + (uint64_t)slot * 65536u;
+    uint32_t* fault = reinterpret_cast<uint32_t*>(static_cast<char*>(env.workspace) + kFaultWordOffset);
+    const cudaError_t err = launch_dependent(table_stream, dim3((unsigned)env.sm_count), dim3(kTableThreads),
+                                             (size_t)kTableBytes, env.stream, reinterpret_cast<uint16_t*>(p.dst.ptr),
+                                             reinterpret_cast<const uint16_t*>(p.src0.ptr), p.count, table, fault);
+    ++*env.launches;
+    return err != cudaSuccess ? err : cudaGetLastError();
+}
+
 template <int OP>
 cudaError_t unary_typed(const LaunchEnv& env, const EwPlan& p, float pa, float pb) {
-    if (p.dtype == DType::F16) return launch_ew<uint16_t>(env, p, UnaryFn<OP, true>{UnaryParams{pa, pb}});
+    if (p.dtype == DType::F16) {
+        if constexpr (kTableOp<OP>) {
+            if (p.kind == EwKind::Flat && p.vec && p.count >= kTableMinCount && env.tables != nullptr)
+                return launch_table_stream(env, p, table_slot(OP));
+        }
+        return launch_ew<uint16_t>(env, p, UnaryFn<OP, true>{UnaryParams{pa, pb}});
+    }
     return launch_ew<float>(env, p, UnaryFn<OP, false>{UnaryParams{pa, pb}});
 }
 
@@ -539,6 +715,11 @@ cudaError_t binary_typed(const LaunchEnv& env, const EwPlan& p) {
 }
 
 }  // namespace
+
+cudaError_t build_domain_tables(void* tables, cudaStream_t stream) {
+    domain_tables_build<<<dim3(65536 / 256, kDomainTableSlots), 256, 0, stream>>>(static_cast<uint16_t*>(tables));
+    return cudaGetLastError();
+}
 
 cudaError_t launch_unary(const LaunchEnv& env, const EwPlan& p, int op, float pa, float pb) {
     switch (op) {

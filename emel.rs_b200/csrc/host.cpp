@@ -22,6 +22,7 @@ struct emel_cuda_context {
     int sm_count;
     void* workspace;
     uint64_t workspace_bytes;
+    void* tables;  // binary16 domain tables, built at creation
     uint64_t launches;
     uint64_t fa_prepared_tokens;  // FlashAttnWorkspace::prepared_tokens (flash_attn.rs:117-118)
     uint64_t fa_reuse_count;      // FlashAttnWorkspace::reuse_count
@@ -327,6 +328,7 @@ emel::LaunchEnv env_of(emel_cuda_context* ctx, void* stream) {
     e.launches = &ctx->launches;
     e.workspace = ctx->workspace;
     e.workspace_bytes = ctx->workspace_bytes;
+    e.tables = ctx->tables;
     return e;
 }
 
@@ -387,10 +389,14 @@ emel_cuda_status emel_cuda_context_create(int device, emel_cuda_context** out) {
         err = cudaMalloc(&ctx->workspace, ctx->workspace_bytes);
     }
     if (err == cudaSuccess) err = cudaMemset(ctx->workspace, 0, ctx->workspace_bytes);
+    // the binary16 domain tables: every table op evaluated once per binary16 input
+    if (err == cudaSuccess) err = cudaMalloc(&ctx->tables, emel::kDomainTableBytes);
+    if (err == cudaSuccess) err = emel::build_domain_tables(ctx->tables, nullptr);
     if (err == cudaSuccess) err = cudaDeviceSynchronize();
     if (err != cudaSuccess) {
         emel_cuda_status st = device_status(ctx, err);
         if (ctx->workspace) cudaFree(ctx->workspace);
+        if (ctx->tables) cudaFree(ctx->tables);
         delete ctx;
         return st;
     }
@@ -402,6 +408,7 @@ emel_cuda_status emel_cuda_context_destroy(emel_cuda_context* ctx) {
     if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
     cudaError_t err = select_device(ctx);
     if (err == cudaSuccess && ctx->workspace) err = cudaFree(ctx->workspace);
+    if (err == cudaSuccess && ctx->tables) err = cudaFree(ctx->tables);
     delete ctx;
     return err == cudaSuccess ? EMEL_CUDA_OK : EMEL_CUDA_DEVICE_ERROR;
 }

@@ -89,6 +89,13 @@ cudaError_t launch_soft_max_split(const LaunchEnv& env, const RowPlan& plan, boo
 // kernel sets when one of its bounded waits expires.
 constexpr uint64_t kFaultWordOffset = 64;
 
+// binary16 domain tables of a context (elementwise.cu): one table of 65,536
+// halves for each of the 16 unary ops that stream large binary16 tensors
+// through a lookup; built once by build_domain_tables.
+constexpr int kDomainTableSlots = 16;
+constexpr uint64_t kDomainTableBytes = (uint64_t)kDomainTableSlots * 65536ull * 2ull;
+cudaError_t build_domain_tables(void* tables, cudaStream_t stream);
+
 // Bytes of workspace the whole-tensor reductions need.
 uint64_t reduction_workspace_bytes(int sm_count);
 

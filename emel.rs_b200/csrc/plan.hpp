@@ -88,6 +88,7 @@ struct LaunchEnv {
     uint64_t* launches;
     void* workspace;         // device scratch owned by the context
     uint64_t workspace_bytes;
+    const void* tables;      // the context's binary16 domain tables (kDomainTableSlots x 128 KB)
 };
 
 }  // namespace emel

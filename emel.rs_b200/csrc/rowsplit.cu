@@ -19,7 +19,6 @@
 #include "launch.hpp"
 #include "pdl.cuh"
 #include "rowreduce.cuh"
-#include "tma.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -338,270 +337,6 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitTh
     cluster.sync();  // peers' shared memory stays alive until every CTA has read it
 }
 
-constexpr int kStagedThreadsArg = 256;
-constexpr uint32_t kStagePieceBytesArg = 12288;  // 3 vectors per thread; the 36 KB ring stays under 48 KB of static shared memory
-
-// --- argmax through a bulk-copy ring ---------------------------------------------
-// The chunk streams through a ring of kArgRingPieces 12 KB pieces in shared
-// memory, refilled by the TMA engine as soon as every thread has read a
-// piece, so the copy engine keeps the ring in flight regardless of
-// registers (36 KB per CTA); four (value, column) chains per thread, one per
-// vector lane.
-constexpr int kArgRingPieces = 3;
-
-__global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kStagedThreadsArg, kSplitCtasPerSm)
-    argmax_rows_staged(RowPlan p, int dst_dtype, uint64_t chunk, uint32_t* fault) {
-    pdl_enter();
-    __shared__ __align__(128) float4 ring[kArgRingPieces][kStagePieceBytesArg / 16];
-    __shared__ __align__(8) uint64_t bars[kArgRingPieces];
-    __shared__ GroupScratch<kStagedThreadsArg> s;
-    __shared__ float pv;
-    __shared__ int64_t pi;
-    __shared__ uint32_t ph;
-    __shared__ uint32_t failed;
-    cg::cluster_group cluster = cg::this_cluster();
-    const unsigned rank = cluster.block_rank();
-    const uint64_t r = blockIdx.x / kSplitCluster;
-    const Chunk ch = my_chunk(p.ne[0], chunk, rank);
-    const float* row = reinterpret_cast<const float*>(p.src.ptr) + split_row_base(p.src, r, p.ne[1], p.ne[2]);
-    const uint32_t nv = (uint32_t)((ch.col1 - ch.col0) / 4);  // whole vectors: ne0 % 4 == 0
-    const uint32_t bytes = nv * 16u;
-    constexpr uint32_t kPieceVecs = kStagePieceBytesArg / 16;
-    const uint32_t pieces = (nv + kPieceVecs - 1) / kPieceVecs;
-    const char* src = reinterpret_cast<const char*>(row + ch.col0);
-    auto issue = [&](uint32_t j) {
-        const uint32_t b0 = j * kStagePieceBytesArg;
-        const uint32_t len = bytes - b0 < kStagePieceBytesArg ? bytes - b0 : kStagePieceBytesArg;
-        mbar_expect_tx(&bars[j % kArgRingPieces], len);
-        bulk_load(&ring[j % kArgRingPieces][0], src + b0, len, &bars[j % kArgRingPieces]);
-    };
-    if (threadIdx.x == 0) {
-        failed = 0u;
-        for (int k = 0; k < kArgRingPieces; ++k) mbar_init(&bars[k], 1);
-        mbar_init_fence();
-    }
-    __syncthreads();
-    if (threadIdx.x == 0)
-        for (uint32_t j = 0; j < pieces && j < (uint32_t)kArgRingPieces; ++j) issue(j);
-    // four chains, one per vector lane: best starts as NaN and nb =
-    // fmaxf(best, v) differs from it exactly for a strictly greater value or
-    // the chain's first non-NaN one (NaN never wins; ties keep the earlier
-    // column, which arrives first in a chain)
-    const float nan = __int_as_float(0x7fc00000);
-    float bv[4] = {nan, nan, nan, nan};
-    uint32_t bc[4] = {0, 0, 0, 0};  // vector index within the chunk
-    uint32_t j = 0;
-    for (; j < pieces; ++j) {
-        const uint32_t slot = j % kArgRingPieces, parity = (j / kArgRingPieces) & 1u;
-        if (!mbar_wait(&bars[slot], parity)) atomicOr(&failed, 1u);
-        __syncthreads();
-        if (failed) break;  // uniform: every thread read the flag after the barrier
-        const uint32_t v0 = j * kPieceVecs, v1 = v0 + kPieceVecs < nv ? v0 + kPieceVecs : nv;
-        for (uint32_t v = v0 + threadIdx.x; v < v1; v += kStagedThreadsArg) {
-            const float4 q = ring[slot][v - v0];
-            const float q4[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-            for (int l = 0; l < 4; ++l) {
-                const float nb = fmaxf(bv[l], q4[l]);
-                if (nb != bv[l]) bc[l] = v;
-                bv[l] = nb;
-            }
-        }
-        __syncthreads();  // every thread is done with this slot
-        if (threadIdx.x == 0 && j + kArgRingPieces < pieces) issue(j + kArgRingPieces);
-    }
-    if (failed && threadIdx.x == 0) {
-        atomicExch(fault, 1u);  // the context reports EMEL_CUDA_TIMEOUT
-        // pieces j .. j + 2 were issued and not consumed: bounded waits let
-        // them land before the CTA's shared memory goes away
-        for (uint32_t k = j; k < pieces && k < j + kArgRingPieces; ++k)
-            mbar_wait(&bars[k % kArgRingPieces], (k / kArgRingPieces) & 1u);
-    }
-    ArgBest bl[4];
-#pragma unroll
-    for (int l = 0; l < 4; ++l)
-        bl[l] = ArgBest{bv[l], (int64_t)(ch.col0 + 4ull * bc[l] + l), is_nan(bv[l]) ? 0u : 1u};
-    ArgBest b = arg_better(arg_better(bl[0], bl[1]), arg_better(bl[2], bl[3]));
-    b = group_argmax<kStagedThreadsArg>(b, &s);
-    if (threadIdx.x == 0) {
-        pv = b.v;
-        pi = b.i;
-        ph = b.has;
-    }
-    cluster.sync();
-    if (rank == 0 && threadIdx.x == 0) {
-        ArgBest best{0.0f, 0, 0};
-        for (int k = 0; k < kSplitCluster; ++k)
-            best = arg_better(best, ArgBest{*cluster.map_shared_rank(&pv, k), *cluster.map_shared_rank(&pi, k),
-                                            *cluster.map_shared_rank(&ph, k)});
-        const int64_t idx = (is_nan(row[0]) || !best.has) ? 0 : best.i;
-        const int64_t off = split_row_base(p.dst, r, p.ne[1], p.ne[2]);
-        if (dst_dtype == (int)DType::I64) reinterpret_cast<int64_t*>(p.dst.ptr)[off] = idx;
-        else if (dst_dtype == (int)DType::I32) reinterpret_cast<int32_t*>(p.dst.ptr)[off] = (int32_t)idx;
-        else reinterpret_cast<float*>(p.dst.ptr)[off] = (float)idx;
-    }
-    cluster.sync();  // peers' shared memory stays alive until rank 0 has read it
-}
-
-// --- soft_max with the chunk staged in shared memory ---------------------------
-// One HBM read and one HBM write per element: each CTA of the row's cluster
-// has the TMA engine copy its chunk into shared memory in 16 KB pieces (one
-// mbarrier each, waits bounded by the global timer), takes the maximum piece
-// by piece as the copies land, and after the cluster's maximum is known
-// turns the staged values into e = exp(v - max) in place with the f64 sum;
-// after the sums are exchanged it writes e / sum.  A row whose maximum is
-// not finite (a NaN, or +-inf) takes the exact pass from global memory.
-// The chunk must fit in shared memory (3 CTAs per SM for the 74 KB chunks
-// of a 151,936-column vocabulary row): rows run in waves of clusters.
-constexpr int kStagedThreads = 256;
-constexpr uint32_t kStagePieceBytes = 16384;
-constexpr int kStageMaxPieces = 13;  // 208 KB
-constexpr uint32_t kStageMaxBytes = kStageMaxPieces * kStagePieceBytes;
-
-__global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kStagedThreads)
-    softmax_rows_staged(RowPlan p, bool apply_scale, float scale, uint64_t chunk, uint32_t* fault) {
-    pdl_enter();
-    extern __shared__ __align__(128) float4 stage[];
-    __shared__ __align__(8) uint64_t bars[kStageMaxPieces];
-    __shared__ GroupScratch<kStagedThreads> s;
-    __shared__ float part_max;
-    __shared__ double part_sum;
-    cg::cluster_group cluster = cg::this_cluster();
-    const unsigned rank = cluster.block_rank();
-    const uint64_t r = blockIdx.x / kSplitCluster;
-    const Chunk ch = my_chunk(p.ne[0], chunk, rank);
-    SoftmaxRow w;
-    w.x = reinterpret_cast<const float*>(p.src.ptr) + split_row_base(p.src, r, p.ne[1], p.ne[2]);
-    w.y = reinterpret_cast<float*>(p.dst.ptr) + split_row_base(p.dst, r, p.ne[1], p.ne[2]);
-    w.xs = p.src.st[0];
-    w.ys = p.dst.st[0];
-    w.has_mask = false;
-    w.mbase = 0;
-    const uint32_t nv = (uint32_t)((ch.col1 - ch.col0) / 4);  // whole vectors: ne0 % 4 == 0
-    const uint32_t bytes = nv * 16u;
-    const uint32_t pieces = (bytes + kStagePieceBytes - 1) / kStagePieceBytes;
-    constexpr uint32_t kPieceVecs = kStagePieceBytes / 16;
-    if (threadIdx.x == 0) {
-        for (uint32_t j = 0; j < pieces; ++j) mbar_init(&bars[j], 1);
-        mbar_init_fence();
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const char* src = reinterpret_cast<const char*>(w.x + ch.col0);
-        for (uint32_t j = 0; j < pieces; ++j) {
-            const uint32_t b0 = j * kStagePieceBytes;
-            const uint32_t len = bytes - b0 < kStagePieceBytes ? bytes - b0 : kStagePieceBytes;
-            mbar_expect_tx(&bars[j], len);
-            bulk_load(reinterpret_cast<char*>(stage) + b0, src + b0, len, &bars[j]);
-        }
-    }
-    auto scale4 = [&](float4 q) {
-        return apply_scale ? make_float4(__fmul_rn(q.x, scale), __fmul_rn(q.y, scale), __fmul_rn(q.z, scale),
-                                         __fmul_rn(q.w, scale))
-                           : q;
-    };
-    // pass 1: NaN-propagating maximum of the staged values, piece by piece
-    float m = -INFINITY;
-    bool landed = true;
-    for (uint32_t j = 0; j < pieces; ++j) {
-        landed = mbar_wait(&bars[j], 0) && landed;
-        const uint32_t v1 = (j + 1) * kPieceVecs < nv ? (j + 1) * kPieceVecs : nv;
-        for (uint32_t v = j * kPieceVecs + threadIdx.x; v < v1; v += kStagedThreads) {
-            const float4 q = scale4(stage[v]);
-            m = max_nan(max_nan(m, q.x), max_nan(q.y, max_nan(q.z, q.w)));
-        }
-    }
-    if (!landed) atomicExch(fault, 1u);  // the context reports EMEL_CUDA_TIMEOUT; the cluster still syncs below
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, o));
-    if ((threadIdx.x & 31) == 0) s.f[threadIdx.x / 32] = m;
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        float cm = s.f[0];
-        for (int k = 1; k < kStagedThreads / 32; ++k) cm = max_nan(cm, s.f[k]);
-        part_max = cm;
-    }
-    cluster.sync();
-    float gm = *cluster.map_shared_rank(&part_max, 0);
-    for (int k = 1; k < kSplitCluster; ++k) gm = max_nan(gm, *cluster.map_shared_rank(&part_max, k));
-
-    double acc = 0.0;
-    float zmin = 0.0f;
-    const bool fast = isfinite(gm);
-    if (fast) {
-        // pass 2: e = exp(v - max) in place, f64 sum
-        for (uint32_t v = threadIdx.x; v < nv; v += kStagedThreads) {
-            const float4 q = scale4(stage[v]);
-            const float4 z = make_float4(__fsub_rn(q.x, gm), __fsub_rn(q.y, gm), __fsub_rn(q.z, gm), __fsub_rn(q.w, gm));
-            zmin = fminf(zmin, fminf(fminf(z.x, z.y), fminf(z.z, z.w)));
-            const float4 e = make_float4(softmax_exp(z.x), softmax_exp(z.y), softmax_exp(z.z), softmax_exp(z.w));
-            stage[v] = e;
-            acc += (double)e.x;
-            acc += (double)e.y;
-            acc += (double)e.z;
-            acc += (double)e.w;
-        }
-    } else {
-        // exact pass from global memory: the reference's NaN rules (a NaN at
-        // element 0 pins the maximum)
-        const float v0 = value_at<true>(p, w, 0, apply_scale, scale);
-        float em = bitsf(0x7fc00000u);
-        __syncthreads();
-        for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kStagedThreads)
-            em = max_nn(em, value_at<true>(p, w, c, apply_scale, scale));
-        em = group_max<kStagedThreads>(em, &s);
-        if (threadIdx.x == 0) part_max = em;
-        cluster.sync();
-        gm = bitsf(0x7fc00000u);
-        for (int k = 0; k < kSplitCluster; ++k) gm = max_nn(gm, *cluster.map_shared_rank(&part_max, k));
-        if (is_nan(v0)) gm = v0;
-        for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kStagedThreads) {
-            const float e = lm_exp(f_sub(value_at<true>(p, w, c, apply_scale, scale), gm));
-            w.y[(int64_t)c * w.ys] = e;
-            acc += (double)e;
-        }
-    }
-    acc = group_sum<kStagedThreads>(acc, &s);
-    if (threadIdx.x == 0) part_sum = acc;
-    cluster.sync();
-    double total = 0.0;
-    for (int k = 0; k < kSplitCluster; ++k) total += *cluster.map_shared_rank(&part_sum, k);
-    const float denom = __double2float_rn(total);
-    // pass 3: e / sum, one HBM write per element
-    if (fast && isfinite(denom)) {
-        const float inv = __frcp_rn(denom);
-        float4* y4 = reinterpret_cast<float4*>(w.y + ch.col0);
-        if (zmin >= kSoftmaxPlainDivFloor) {
-            for (uint32_t v = threadIdx.x; v < nv; v += kStagedThreads) {
-                const float4 e = stage[v];
-                __stcs(y4 + v, make_float4(markstein_div(e.x, denom, inv), markstein_div(e.y, denom, inv),
-                                           markstein_div(e.z, denom, inv), markstein_div(e.w, denom, inv)));
-            }
-        } else {
-            for (uint32_t v = threadIdx.x; v < nv; v += kStagedThreads) {
-                const float4 e = stage[v];
-                __stcs(y4 + v, make_float4(softmax_div(e.x, denom, inv), softmax_div(e.y, denom, inv),
-                                           softmax_div(e.z, denom, inv), softmax_div(e.w, denom, inv)));
-            }
-        }
-    } else if (fast) {
-        float4* y4 = reinterpret_cast<float4*>(w.y + ch.col0);
-        for (uint32_t v = threadIdx.x; v < nv; v += kStagedThreads) {
-            const float4 e = stage[v];
-            __stcs(y4 + v, make_float4(f_div(e.x, denom), f_div(e.y, denom), f_div(e.z, denom), f_div(e.w, denom)));
-        }
-    } else {
-        for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kStagedThreads) {
-            float* o = w.y + (int64_t)c * w.ys;
-            *o = f_div(*o, denom);
-        }
-    }
-    if (!landed && threadIdx.x == 0) {
-        for (uint32_t j = 0; j < pieces; ++j) mbar_wait(&bars[j], 0);  // copies in flight end before the CTA does
-    }
-    cluster.sync();  // peers' shared memory stays alive until every CTA has read it
-}
-
 uint64_t split_chunk(uint64_t ne0) {
     uint64_t c = (ne0 + kSplitCluster - 1) / kSplitCluster;
     return (c + 3) / 4 * 4;  // keeps every chunk's first column 16-byte aligned
@@ -616,15 +351,8 @@ bool split_rows_wanted(const LaunchEnv& env, const RowPlan& p) {
 }
 
 cudaError_t launch_argmax_rows_split(const LaunchEnv& env, const RowPlan& p, int dst_dtype) {
-    cudaError_t err;
-    if (p.vec) {
-        uint32_t* fault = reinterpret_cast<uint32_t*>(static_cast<char*>(env.workspace) + kFaultWordOffset);
-        err = launch_dependent(argmax_rows_staged, dim3((unsigned)(p.rows * kSplitCluster)), dim3(kStagedThreadsArg),
-                               0, env.stream, p, dst_dtype, split_chunk(p.ne[0]), fault);
-    } else {
-        err = launch_dependent(argmax_rows_split, dim3((unsigned)(p.rows * kSplitCluster)), dim3(kSplitThreads), 0,
-                               env.stream, p, dst_dtype, split_chunk(p.ne[0]));
-    }
+    const cudaError_t err = launch_dependent(argmax_rows_split, dim3((unsigned)(p.rows * kSplitCluster)),
+                                             dim3(kSplitThreads), 0, env.stream, p, dst_dtype, split_chunk(p.ne[0]));
     ++*env.launches;
     return err != cudaSuccess ? err : cudaGetLastError();
 }
@@ -637,23 +365,9 @@ cudaError_t launch_sum_rows_split(const LaunchEnv& env, const RowPlan& p) {
 }
 
 cudaError_t launch_soft_max_split(const LaunchEnv& env, const RowPlan& p, bool apply_scale, float scale) {
-    const uint64_t chunk = split_chunk(p.ne[0]);
-    cudaError_t err;
-    if (p.vec && !p.has_aux && chunk * 4 <= kStageMaxBytes) {
-        static DeviceFlags configured;
-        if (!configured.done(env.device)) {
-            err = cudaFuncSetAttribute(softmax_rows_staged, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       (int)kStageMaxBytes);
-            if (err != cudaSuccess) return err;
-            configured.mark(env.device);
-        }
-        uint32_t* fault = reinterpret_cast<uint32_t*>(static_cast<char*>(env.workspace) + kFaultWordOffset);
-        err = launch_dependent(softmax_rows_staged, dim3((unsigned)(p.rows * kSplitCluster)), dim3(kStagedThreads),
-                               (size_t)(chunk * 4), env.stream, p, apply_scale, scale, chunk, fault);
-    } else {
-        err = launch_dependent(softmax_rows_split, dim3((unsigned)(p.rows * kSplitCluster)), dim3(kSplitThreads), 0,
-                               env.stream, p, apply_scale, scale, chunk);
-    }
+    const cudaError_t err = launch_dependent(softmax_rows_split, dim3((unsigned)(p.rows * kSplitCluster)),
+                                             dim3(kSplitThreads), 0, env.stream, p, apply_scale, scale,
+                                             split_chunk(p.ne[0]));
     ++*env.launches;
     return err != cudaSuccess ? err : cudaGetLastError();
 }

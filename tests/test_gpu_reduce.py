@@ -115,12 +115,14 @@ def test_argmax_ties_nan_and_f32_encoding(emel, kern):
 
 @pytest.mark.parametrize("n", [4096, 1 << 22])
 def test_argmax_lane_chain_edges(emel, kern, n):
-    """The vector walk's per-lane chains: all NaN and all -inf give 0; a
-    lone late comparable value wins; -0 and +0 tie to the first; NaN runs
-    in front of the maximum are skipped."""
+    """The vector walk's per-lane chains: all NaN (and so a NaN at element 0,
+    which pins the answer) and all -inf give 0; behind a -inf at element 0,
+    a lone late comparable value among NaNs wins; -0 and +0 tie to the
+    first; NaN runs in front of the maximum are skipped."""
     cases = []
     x = np.full(n, np.nan, np.float32)
     cases.append((x.copy(), 0))
+    x[0] = -np.inf
     x[n - 7] = -3.0
     cases.append((x.copy(), n - 7))
     cases.append((np.full(n, -np.inf, np.float32), 0))
@@ -128,7 +130,7 @@ def test_argmax_lane_chain_edges(emel, kern, n):
     z[0] = -0.0
     cases.append((z, 0))
     y = np.full(n, -1.0, np.float32)
-    y[: n // 2] = np.nan
+    y[1: n // 2] = np.nan
     y[0] = 2.0
     y[n // 2 + 5] = 2.0  # later equal value loses to element 0
     cases.append((y, 0))

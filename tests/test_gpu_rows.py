@@ -369,12 +369,14 @@ def test_split_argmax_rows_ties_across_chunks_and_nans(emel, kern, oracle_lib):
     v, rows = 151936, 10
     x = rng.standard_normal(v * rows).astype(np.float32).reshape(rows, v)
     x[6, :] = np.nan
-    x[6, 140000] = -5.0      # the row's only comparable value, late in the last chunk
+    x[6, 0] = -np.inf        # comparable, so no NaN pin at column 0
+    x[6, 140000] = -5.0      # the only other comparable value, late in the last chunk
     x[7, :] = 0.0
     x[7, 0] = -0.0           # -0 and +0 tie: the first column
     x[8, :] = -np.inf
     x[8, 3] = -1e30
-    x[9, :40000] = np.nan    # NaNs ahead of every lane chain's first value
+    x[9, 1:40000] = np.nan   # NaNs ahead of every lane chain's first value
+    x[9, 0] = -50.0
     x[9, 40001] = 7.0
     x[0, 150000] = 50.0
     x[0, 19000] = 50.0       # same maximum, earlier chunk
