@@ -253,9 +253,9 @@ EMEL_HD void f32_exp_split(float x, int& k, float& r, float& t) {
     t = fma32(c, r, fma32(r * r, q, c));
 }
 
-// exp(x) within one ulp.  Saturates like the binary32 result (inf above 89,
-// +0 below -104); NaN propagates (every comparison is false).
-EMEL_HD float exp32(float x) {
+// exp(x) within one ulp, any x.  Saturates like the binary32 result (inf
+// above 89, +0 below -104); NaN propagates (every comparison is false).
+EMEL_HD float exp32_general(float x) {
     const float xc = x > 89.0f ? 89.0f : (x < -104.0f ? -104.0f : x);
     int k;
     float r, t;
@@ -264,6 +264,19 @@ EMEL_HD float exp32(float x) {
     const float s1 = pow2i(k1), s2 = pow2i(k - k1);
     const float y = fma32(s1, r + t, s1) * s2;
     return x > 89.0f ? INFINITY : (x < -104.0f ? 0.0f : y);
+}
+
+// exp(x): where the result is a normal binary32 number (-86 <= x <= 88.72)
+// 2^k is one exponent-field value -- 2^(k-1) scaled by 2 keeps k = 128 in
+// range -- and no saturation is needed; everything else (subnormal results,
+// overflow, NaN) takes the general routine.  The same bits either way.
+EMEL_HD float exp32(float x) {
+    if (!(x >= -86.0f && x <= 88.72f)) return exp32_general(x);
+    int k;
+    float r, t;
+    f32_exp_split(x, k, r, t);
+    const float sh = bits_to_f32((uint32_t)(k + 126) << 23);  // 2^(k-1), -125 <= k - 1 <= 127
+    return fma32(sh, r + t, sh) * 2.0f;
 }
 
 // expm1(x) within one ulp; saturates to -1 below -18 and to inf above 89;
