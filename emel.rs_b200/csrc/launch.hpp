@@ -90,9 +90,9 @@ cudaError_t launch_soft_max_split(const LaunchEnv& env, const RowPlan& plan, boo
 constexpr uint64_t kFaultWordOffset = 64;
 
 // binary16 domain tables of a context (elementwise.cu): one table of 65,536
-// halves for each of the 16 unary ops that stream large binary16 tensors
+// halves for each of the 8 unary ops that stream large binary16 tensors
 // through a lookup; built once by build_domain_tables.
-constexpr int kDomainTableSlots = 16;
+constexpr int kDomainTableSlots = 8;
 constexpr uint64_t kDomainTableBytes = (uint64_t)kDomainTableSlots * 65536ull * 2ull;
 cudaError_t build_domain_tables(void* tables, cudaStream_t stream);
 
