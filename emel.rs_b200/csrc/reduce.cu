@@ -330,9 +330,14 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) argmax_all(RowPlan p, Ar
 
 }  // namespace
 
+uint64_t split_rows_workspace_offset(int sm_count) {
+    // after the header (tickets, fault words) and one 16-byte partial per CTA
+    return (256 + (uint64_t)sm_count * kCtasPerSm * 16 + 255) / 256 * 256;
+}
+
 uint64_t reduction_workspace_bytes(int sm_count) {
-    // ticket (256 B slot) + one partial (16 B) per CTA
-    return 256 + (uint64_t)sm_count * kCtasPerSm * 16;
+    // + the few-long-rows kernels' per-row chunk partials and row tickets
+    return split_rows_workspace_offset(sm_count) + (uint64_t)sm_count * (kSplitRowChunks * 16 + 4) + 256;
 }
 
 static uint32_t reduce_grid(const LaunchEnv& env, uint64_t n) {

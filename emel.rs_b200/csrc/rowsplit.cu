@@ -143,6 +143,68 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitTh
     cluster.sync();  // peers' shared memory stays alive until rank 0 has read it
 }
 
+// argmax_rows without a cluster: the row's kSplitCluster CTAs are
+// independent; each writes its chunk's (value, column) partial to the
+// context workspace and takes a ticket on its row, and the CTA that takes
+// the last ticket folds the row's partials in chunk order (earliest column
+// on ties, NaN at column 0 pins 0) and re-arms the ticket.  No cluster
+// scheduling and no cluster barrier; four (value, vector) chains per thread
+// with fmaxf from a NaN start (three instructions per element).
+struct ChunkPartial {
+    float v;
+    uint32_t has;
+    int64_t i;
+};
+
+__global__ void __launch_bounds__(kSplitThreads, kSplitCtasPerSm)
+    argmax_rows_flat(RowPlan p, int dst_dtype, uint64_t chunk, ChunkPartial* partials, unsigned* tickets) {
+    pdl_enter();
+    __shared__ GroupScratch<kSplitThreads> s;
+    __shared__ bool is_last;
+    const unsigned rank = blockIdx.x % kSplitCluster;
+    const uint64_t r = blockIdx.x / kSplitCluster;
+    const Chunk ch = my_chunk(p.ne[0], chunk, rank);
+    const float* row = reinterpret_cast<const float*>(p.src.ptr) + split_row_base(p.src, r, p.ne[1], p.ne[2]);
+    const float nan = __int_as_float(0x7fc00000);
+    float bv[4] = {nan, nan, nan, nan};
+    uint64_t bc[4] = {0, 0, 0, 0};
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+    batched<8>(ch.col0 / 4, ch.col1 / 4, [&](uint64_t v) { return __ldcs(r4 + v); },
+               [&](uint64_t v, float4 q) {
+                   const float q4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                   for (int l = 0; l < 4; ++l) {
+                       const float nb = fmaxf(bv[l], q4[l]);
+                       if (nb != bv[l]) bc[l] = v;
+                       bv[l] = nb;
+                   }
+               });
+    ArgBest bl[4];
+#pragma unroll
+    for (int l = 0; l < 4; ++l) bl[l] = ArgBest{bv[l], (int64_t)(4 * bc[l] + l), is_nan(bv[l]) ? 0u : 1u};
+    ArgBest b = arg_better(arg_better(bl[0], bl[1]), arg_better(bl[2], bl[3]));
+    b = group_argmax<kSplitThreads>(b, &s);
+    if (threadIdx.x == 0) {
+        partials[r * kSplitCluster + rank] = ChunkPartial{b.v, b.has, b.i};
+        __threadfence();
+        is_last = atomicAdd(&tickets[r], 1u) == kSplitCluster - 1;
+    }
+    __syncthreads();
+    if (!is_last || threadIdx.x != 0) return;
+    __threadfence();
+    ArgBest best{0.0f, 0, 0};
+    for (int k = 0; k < kSplitCluster; ++k) {
+        const ChunkPartial* q = partials + r * kSplitCluster + k;
+        best = arg_better(best, ArgBest{__ldcg(&q->v), __ldcg(&q->i), __ldcg(&q->has)});
+    }
+    const int64_t idx = (is_nan(row[0]) || !best.has) ? 0 : best.i;
+    const int64_t off = split_row_base(p.dst, r, p.ne[1], p.ne[2]);
+    if (dst_dtype == (int)DType::I64) reinterpret_cast<int64_t*>(p.dst.ptr)[off] = idx;
+    else if (dst_dtype == (int)DType::I32) reinterpret_cast<int32_t*>(p.dst.ptr)[off] = (int32_t)idx;
+    else reinterpret_cast<float*>(p.dst.ptr)[off] = (float)idx;
+    tickets[r] = 0u;
+}
+
 __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitThreads, kSplitCtasPerSm)
     sum_rows_split(RowPlan p, uint64_t chunk) {
     pdl_enter();
@@ -351,8 +413,18 @@ bool split_rows_wanted(const LaunchEnv& env, const RowPlan& p) {
 }
 
 cudaError_t launch_argmax_rows_split(const LaunchEnv& env, const RowPlan& p, int dst_dtype) {
-    const cudaError_t err = launch_dependent(argmax_rows_split, dim3((unsigned)(p.rows * kSplitCluster)),
-                                             dim3(kSplitThreads), 0, env.stream, p, dst_dtype, split_chunk(p.ne[0]));
+    cudaError_t err;
+    if (p.vec) {
+        static_assert(kSplitCluster == kSplitRowChunks, "workspace slots per row");
+        char* base = static_cast<char*>(env.workspace) + split_rows_workspace_offset(env.sm_count);
+        auto* partials = reinterpret_cast<ChunkPartial*>(base);
+        auto* tickets = reinterpret_cast<unsigned*>(base + (uint64_t)env.sm_count * kSplitRowChunks * 16);
+        err = launch_dependent(argmax_rows_flat, dim3((unsigned)(p.rows * kSplitCluster)), dim3(kSplitThreads), 0,
+                               env.stream, p, dst_dtype, split_chunk(p.ne[0]), partials, tickets);
+    } else {
+        err = launch_dependent(argmax_rows_split, dim3((unsigned)(p.rows * kSplitCluster)), dim3(kSplitThreads), 0,
+                               env.stream, p, dst_dtype, split_chunk(p.ne[0]));
+    }
     ++*env.launches;
     return err != cudaSuccess ? err : cudaGetLastError();
 }
