@@ -4,7 +4,8 @@
 // of each output element.  Four shapes of the same loop body:
 //   ew_flat    dense operands with identical extents: a grid-stride stream
 //              of 16-byte vectors (4 x f32 / 8 x f16), two in flight per
-//              thread, loads marked no-allocate in L1;
+//              thread, loads marked no-allocate in L1, one resident wave of
+//              CTAs;
 //   ew_rows    every operand has unit stride in dim0: "row workers" of G
 //              threads (a warp for short rows, a whole CTA for long ones)
 //              walk rows of the iteration space, 16-byte vectors within a
@@ -16,6 +17,8 @@
 //   ew_ordinal equal element counts with different extents: every operand
 //              decodes the ordinal with its own extents (binary.rs:411-424).
 // Grids are sized in multiples of the SM count (148 on B200).
+#include <type_traits>
+
 #include "common.cuh"
 #include "launch.hpp"
 #include "pdl.cuh"
@@ -37,12 +40,33 @@ struct UnaryFn {
     UnaryParams p;
     static constexpr bool kBinary = false;
     static constexpr bool kHeavy = kHeavyFormula<OP>;
-    static constexpr int kUnroll = kHeavyFormula<OP> ? 2 : 4;  // arithmetic-bound ops need fewer loads in flight
-    static constexpr int kMinBlocks = 4;  // 64 registers: a tighter cap spills the vectors in flight
+    // two vectors in flight per thread; with 32-bit indexing most ops fit 32
+    // registers without spilling (eight CTAs, 2048 threads per SM), the
+    // longer formulas 51
+    static constexpr int kUnroll = 2;
+    static constexpr int kMinBlocks = (OP == kTanh || OP == kExpm1 || OP == kSoftplus || OP == kGeluErf) ? 5 : 8;
     __device__ __forceinline__ float operator()(float a, float) const { return unary_apply<OP, IN_F16>(a, p); }
     __device__ __forceinline__ float fast(float a, float) const {
         if constexpr (kHeavy) return unary_formula<OP, (IN_F16 || OP == kGelu) ? kHalf : kFast, IN_F16>(a, p);
         else return unary_apply<OP, IN_F16>(a, p);
+    }
+    // binary16 ops computed on two packed lanes, bit for bit the reference's
+    // f16 -> f32 -> op -> f16 for NaN-free inputs: sign-bit operations, the
+    // signed 16-bit compare (positive binary16 values are exactly the lanes
+    // > 0 as int16), and x * x, exact in binary32 and rounded once either way
+    static constexpr bool kPacked = IN_F16 && (OP == kAbs || OP == kNeg || OP == kRelu || OP == kStep || OP == kSqr);
+    static constexpr bool kPackedMayNan = false;
+    __device__ __forceinline__ uint32_t packed(uint32_t w, uint32_t) const {
+        if constexpr (OP == kAbs) return w & 0x7fff7fffu;
+        if constexpr (OP == kNeg) return w ^ 0x80008000u;
+        if constexpr (OP == kRelu) return w & __vcmpgts2(w, 0u);
+        if constexpr (OP == kStep) return __vcmpgts2(w, 0u) & 0x3c003c00u;
+        if constexpr (OP == kSqr) {
+            const __half2 h = *reinterpret_cast<const __half2*>(&w);
+            const __half2 r = __hmul2(h, h);
+            return *reinterpret_cast<const uint32_t*>(&r);
+        }
+        return w;
     }
 };
 
@@ -50,10 +74,19 @@ template <int OP>
 struct BinaryFn {
     static constexpr bool kBinary = true;
     static constexpr bool kHeavy = false;
-    static constexpr int kUnroll = 4;
-    static constexpr int kMinBlocks = 3;  // two operands of four vectors each: 85 registers
+    static constexpr int kUnroll = 2;
+    static constexpr int kMinBlocks = 6;  // two operands of two vectors each: 40 registers
     __device__ __forceinline__ float operator()(float a, float b) const { return binary_apply<OP>(a, b); }
     __device__ __forceinline__ float fast(float a, float b) const { return binary_apply<OP>(a, b); }
+    // binary16 multiply on packed lanes: the product of two binary16 values
+    // is exact in binary32, so one binary16 rounding either way; 0 * inf
+    // gives a NaN whose encoding the lane path supplies
+    static constexpr bool kPacked = OP == kMul;
+    static constexpr bool kPackedMayNan = true;
+    __device__ __forceinline__ uint32_t packed(uint32_t wa, uint32_t wb) const {
+        const __half2 r = __hmul2(*reinterpret_cast<const __half2*>(&wa), *reinterpret_cast<const __half2*>(&wb));
+        return *reinterpret_cast<const uint32_t*>(&r);
+    }
 };
 
 // activation.rs:467-481, silu_back as a two-input formula: grad * silu'(x).
@@ -126,6 +159,12 @@ __device__ __forceinline__ bool any_nan_h8(const Vec16<uint16_t>& v) {
     return m != 0;
 }
 
+// Functors with a packed binary16 form (kPacked).
+template <typename F, typename = void>
+struct PackedOp : std::false_type {};
+template <typename F>
+struct PackedOp<F, std::void_t<decltype(F::kPacked)>> : std::bool_constant<F::kPacked> {};
+
 template <typename T, typename F>
 __device__ __forceinline__ Vec16<T> apply_vec(const F& f, const Vec16<T>& a, const Vec16<T>& b) {
     if constexpr (sizeof(T) == 2) {
@@ -135,6 +174,13 @@ __device__ __forceinline__ Vec16<T> apply_vec(const F& f, const Vec16<T>& a, con
         if (!any_nan_h8(a) && !(F::kBinary && any_nan_h8(b))) {
             const uint4 ua = *reinterpret_cast<const uint4*>(&a);
             const uint4 ub = *reinterpret_cast<const uint4*>(&b);
+            if constexpr (PackedOp<F>::value) {
+                Vec16<T> r;
+                *reinterpret_cast<uint4*>(&r) = make_uint4(f.packed(ua.x, ub.x), f.packed(ua.y, ub.y),
+                                                           f.packed(ua.z, ub.z), f.packed(ua.w, ub.w));
+                if (!F::kPackedMayNan || !any_nan_h8(r)) return r;
+                return apply_vec_lanes<T>(f, a, b);
+            }
             const unsigned wa[4] = {ua.x, ua.y, ua.z, ua.w};
             const unsigned wb[4] = {ub.x, ub.y, ub.z, ub.w};
             unsigned wr[4];
@@ -160,34 +206,47 @@ __device__ __forceinline__ Vec16<T> apply_vec(const F& f, const Vec16<T>& a, con
     return apply_vec_scalar<T>(f, a, b);
 }
 
-template <typename T, typename F>
+// I: the index type -- 32-bit when the vector count and the grid stride
+// leave headroom below 2^31 (every realistic tensor), which keeps the loop's
+// registers low enough for eight CTAs per SM on the cheap ops.
+template <typename T, typename F, typename I>
 __global__ void __launch_bounds__(kThreads, F::kMinBlocks) ew_flat(T* __restrict__ dst, const T* __restrict__ a,
                                                     const T* __restrict__ b, uint64_t n, F f) {
     pdl_enter();
     constexpr int N = Vec16<T>::N;
     constexpr int U = F::kUnroll;  // vectors in flight per thread
-    const uint64_t nvec = n / N;
-    const uint64_t stride = (uint64_t)gridDim.x * blockDim.x;
-    const uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
-    uint64_t i = gid;
+    const I nvec = (I)(n / N);
+    const I stride = (I)gridDim.x * blockDim.x;
+    const I gid = (I)blockIdx.x * blockDim.x + threadIdx.x;
+    I i = gid;
     for (; i + (U - 1) * stride < nvec; i += U * stride) {
         Vec16<T> a0[U], b0[U];
 #pragma unroll
         for (int k = 0; k < U; ++k) {
-            a0[k] = ld_stream(a + (i + k * stride) * N);
-            if constexpr (F::kBinary) b0[k] = ld_stream(b + (i + k * stride) * N);
+            a0[k] = ld_stream(a + (uint64_t)(i + k * stride) * N);
+            if constexpr (F::kBinary) b0[k] = ld_stream(b + (uint64_t)(i + k * stride) * N);
             else b0[k] = Vec16<T>{};
         }
 #pragma unroll
-        for (int k = 0; k < U; ++k) st_stream(dst + (i + k * stride) * N, apply_vec<T>(f, a0[k], b0[k]));
+        for (int k = 0; k < U; ++k) st_stream(dst + (uint64_t)(i + k * stride) * N, apply_vec<T>(f, a0[k], b0[k]));
     }
-    for (; i < nvec; i += stride) {
-        const Vec16<T> a0 = ld_stream(a + i * N);
-        Vec16<T> b0{};
-        if constexpr (F::kBinary) b0 = ld_stream(b + i * N);
-        st_stream(dst + i * N, apply_vec<T>(f, a0, b0));
+    if (i < nvec) {
+        // this thread's last (fewer than U) vectors, their loads issued together
+        Vec16<T> a0[U], b0[U];
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            a0[k] = Vec16<T>{};
+            b0[k] = Vec16<T>{};
+            if (i + k * stride < nvec) {
+                a0[k] = ld_stream(a + (uint64_t)(i + k * stride) * N);
+                if constexpr (F::kBinary) b0[k] = ld_stream(b + (uint64_t)(i + k * stride) * N);
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k)
+            if (i + k * stride < nvec) st_stream(dst + (uint64_t)(i + k * stride) * N, apply_vec<T>(f, a0[k], b0[k]));
     }
-    const uint64_t t = nvec * N + gid;
+    const uint64_t t = (uint64_t)nvec * N + gid;
     if (t < n) {
         const float x = Elem<T>::load(a + t);
         const float y = F::kBinary ? Elem<T>::load(b + t) : 0.0f;
@@ -461,11 +520,26 @@ __global__ void __launch_bounds__(kThreads) repeat_copy(EwPlan p, RepeatArgs r) 
     }
 }
 
-uint32_t grid_for(const LaunchEnv& env, uint64_t work_items, int per_thread) {
+// resident: CTAs of the kernel that fit on one SM (8 x 256 threads = 2048,
+// the SM's thread limit, unless registers allow fewer); the grid never
+// exceeds one resident wave, so no CTA waits for another to finish.
+uint32_t grid_for(const LaunchEnv& env, uint64_t work_items, int per_thread, uint32_t resident = 8) {
     const uint64_t want = (work_items + (uint64_t)kThreads * per_thread - 1) / ((uint64_t)kThreads * per_thread);
-    const uint64_t cap = (uint64_t)env.sm_count * 8;  // 8 x 256 threads = 2048 resident threads per SM
+    const uint64_t cap = (uint64_t)env.sm_count * (resident < 8 ? resident : 8);
     uint64_t g = want < cap ? want : cap;
     return (uint32_t)(g == 0 ? 1 : g);
+}
+
+// CTAs of `kernel` resident per SM at kThreads threads, cached per device
+// (one cache per kernel instantiation).
+template <typename K>
+uint32_t resident_ctas(DeviceKeyedValue& cache, const LaunchEnv& env, K kernel) {
+    uint32_t n = 0;
+    if (cache.get(env.device, 0u, &n)) return n;
+    int r = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&r, kernel, kThreads, 0) != cudaSuccess || r < 1) r = 1;
+    cache.put(env.device, 0u, (uint32_t)r);
+    return (uint32_t)r;
 }
 
 template <typename T, typename F>
@@ -473,10 +547,21 @@ cudaError_t launch_ew(const LaunchEnv& env, const EwPlan& p, const F& f) {
     switch (p.kind) {
     case EwKind::Flat: {
         const uint64_t nvec = p.count / Vec16<T>::N;
-        const cudaError_t err = launch_dependent(
-            ew_flat<T, F>, dim3(grid_for(env, nvec, F::kUnroll)), dim3(kThreads), 0, env.stream,
-            reinterpret_cast<T*>(p.dst.ptr), reinterpret_cast<const T*>(p.src0.ptr),
-            reinterpret_cast<const T*>(p.src1.ptr), p.count, f);
+        static DeviceKeyedValue resident32, resident64;
+        cudaError_t err;
+        if (nvec < (1ull << 31) - (uint64_t)(F::kUnroll + 1) * env.sm_count * 8 * kThreads) {
+            auto* kernel = ew_flat<T, F, uint32_t>;
+            err = launch_dependent(kernel, dim3(grid_for(env, nvec, F::kUnroll, resident_ctas(resident32, env, kernel))),
+                                   dim3(kThreads), 0, env.stream, reinterpret_cast<T*>(p.dst.ptr),
+                                   reinterpret_cast<const T*>(p.src0.ptr), reinterpret_cast<const T*>(p.src1.ptr),
+                                   p.count, f);
+        } else {
+            auto* kernel = ew_flat<T, F, uint64_t>;
+            err = launch_dependent(kernel, dim3(grid_for(env, nvec, F::kUnroll, resident_ctas(resident64, env, kernel))),
+                                   dim3(kThreads), 0, env.stream, reinterpret_cast<T*>(p.dst.ptr),
+                                   reinterpret_cast<const T*>(p.src0.ptr), reinterpret_cast<const T*>(p.src1.ptr),
+                                   p.count, f);
+        }
         if (err != cudaSuccess) return err;
         break;
     }
@@ -484,17 +569,21 @@ cudaError_t launch_ew(const LaunchEnv& env, const EwPlan& p, const F& f) {
         if constexpr (F::kBinary) {
             if (dense_row_broadcast(p)) {
                 const uint32_t n = (uint32_t)(p.count / Vec16<T>::N);
+                static DeviceKeyedValue resident;
+                auto* kernel = ew_row_broadcast<T, F>;
                 const cudaError_t err = launch_dependent(
-                    ew_row_broadcast<T, F>, dim3(grid_for(env, n, 4)), dim3(kThreads), 0, env.stream, p, f,
-                    make_fastdiv((uint32_t)(p.ne[0] / Vec16<T>::N)), n);
+                    kernel, dim3(grid_for(env, n, 4, resident_ctas(resident, env, kernel))), dim3(kThreads), 0,
+                    env.stream, p, f, make_fastdiv((uint32_t)(p.ne[0] / Vec16<T>::N)), n);
                 if (err != cudaSuccess) return err;
                 break;
             }
         }
         RowsWalk w;
         if (rows_walk(p, &w)) {
-            const cudaError_t err =
-                launch_dependent(ew_rows_vec<T, F>, dim3(grid_for(env, w.nvec, 4)), dim3(kThreads), 0, env.stream, p, f, w);
+            static DeviceKeyedValue resident;
+            auto* kernel = ew_rows_vec<T, F>;
+            const cudaError_t err = launch_dependent(kernel, dim3(grid_for(env, w.nvec, 4, resident_ctas(resident, env, kernel))),
+                                                     dim3(kThreads), 0, env.stream, p, f, w);
             if (err != cudaSuccess) return err;
             break;
         }
