@@ -81,14 +81,36 @@ __device__ __forceinline__ bool last_cta(unsigned* ticket) {
     return is_last;
 }
 
+__device__ __forceinline__ MvPart mv_shfl(MvPart a, int o) {
+    MvPart b;
+    b.v = __shfl_xor_sync(0xffffffffu, a.v, o);
+    b.i = __shfl_xor_sync(0xffffffffu, a.i, o);
+    b.has = __shfl_xor_sync(0xffffffffu, a.has, o);
+    b.pin = __shfl_xor_sync(0xffffffffu, a.pin, o);
+    return b;
+}
+
+// Stores the CTA's partial; the last CTA folds all partials (mv_better is a
+// maximum under a total order -- only the partial holding row 0 can pin --
+// so every thread folds a strided share and the shares combine in any order).
 __device__ void finish(const MvArgmaxPlan& p, MvPart best) {
+    __shared__ MvPart fold[32];
     MvPart* parts = reinterpret_cast<MvPart*>(p.partials);
     if (threadIdx.x == 0) parts[blockIdx.x] = best;
     if (!last_cta(p.ticket)) return;
+    __threadfence();
+    MvPart t{0.0f, 0, 0u, 0u};
+    for (unsigned c = threadIdx.x; c < gridDim.x; c += blockDim.x) {
+        const int4 w = __ldcg(reinterpret_cast<const int4*>(parts + c));
+        t = mv_better(t, MvPart{__int_as_float(w.x), w.y, (uint32_t)w.z, (uint32_t)w.w});
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) t = mv_better(t, mv_shfl(t, o));
+    if ((threadIdx.x & 31) == 0) fold[threadIdx.x >> 5] = t;
+    __syncthreads();
     if (threadIdx.x == 0) {
-        __threadfence();
-        MvPart total = parts[0];
-        for (unsigned c = 1; c < gridDim.x; ++c) total = mv_better(total, parts[c]);
+        MvPart total = fold[0];
+        for (unsigned w = 1; w < blockDim.x / 32; ++w) total = mv_better(total, fold[w]);
         *p.dst_value = total.v;
         *p.dst_index = total.i;
         *p.ticket = 0u;
@@ -483,11 +505,24 @@ __device__ __forceinline__ int32_t q8k_nearest(float v) {
 }
 
 // Q4_K term: eight lane terms d * float(acc[j]) and the minimum term.
+// ALIGNED16: w is 16-byte aligned (the window is read as nine 16-byte words).
+template <bool ALIGNED16 = false>
 __device__ __forceinline__ void q4k_block_terms(const uint32_t* w, const uint32_t* r4, const int* bs, float rdb,
                                                 float* o) {
     uint32_t W[36];
+    if constexpr (ALIGNED16) {
 #pragma unroll
-    for (int i = 0; i < 36; ++i) W[i] = w[i];  // shared-memory window
+        for (int i = 0; i < 9; ++i) {
+            const uint4 q = reinterpret_cast<const uint4*>(w)[i];
+            W[4 * i] = q.x;
+            W[4 * i + 1] = q.y;
+            W[4 * i + 2] = q.z;
+            W[4 * i + 3] = q.w;
+        }
+    } else {
+#pragma unroll
+        for (int i = 0; i < 36; ++i) W[i] = w[i];  // shared-memory window
+    }
     // scales / minimums (dot_q4_k's unpacking)
     const uint32_t s0 = W[1], s1 = W[2], s2 = W[3];
     uint32_t sc[8], mn[8];
@@ -635,21 +670,15 @@ __device__ __forceinline__ void q3k_block_terms(const uint8_t* blk_ptr, const ui
     o[8] = 0.0f;
 }
 
+// The rhs quantized to Q8_K blocks (quantize_row_q8_k, the reference's
+// rhs step of dot_q*_k) into shared memory: rq [blocks][64] quant words in
+// the order the format's decode reads them, rd [blocks] scales, rb
+// [blocks][16] sums of each 16-value group.  One warp per block.
 template <int CODE>
-__global__ void __launch_bounds__(kKThreads, CODE == kDtypeQ6_K || CODE == kDtypeQ3_K ? 6 : 8)
-    mv_argmax_k(MvArgmaxPlan p, const uint8_t* lhs) {
-    extern __shared__ __align__(16) uint32_t k_smem[];
-    __shared__ MvPart warp_best[kKWarps];
-    const uint32_t blocks = (uint32_t)(p.k / 256);
-    uint32_t* rq = k_smem;                                           // [blocks][8 groups][8 lanes] quant words
-    float* rd = reinterpret_cast<float*>(rq + blocks * 64);          // [blocks] scales
-    int* rb = reinterpret_cast<int*>(rd + blocks);                   // [blocks][16] group sums
+__device__ __forceinline__ void quantize_rhs_q8k(const MvArgmaxPlan& p, uint32_t blocks, uint32_t* rq, float* rd,
+                                                 int* rb, int nwarps) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    using KW = KWindow<CODE>;
-    // [2][32 rows][SWM] staging windows, 16-byte aligned
-    uint32_t* stage = k_smem + ((blocks * 81u + 3u) & ~3u) + warp * 2 * 32 * KW::SWM;
-    pdl_enter();
-    for (uint32_t b = warp; b < blocks; b += kKWarps) {
+    for (uint32_t b = warp; b < blocks; b += (uint32_t)nwarps) {
         // lane l holds positions 8l .. 8l + 7
         float x[8];
         float absolute = 0.0f, maximum = 0.0f;
@@ -707,6 +736,23 @@ __global__ void __launch_bounds__(kKThreads, CODE == kDtypeQ6_K || CODE == kDtyp
         if ((lane & 1) == 0) rb[b * 16 + (lane >> 1)] = (int)(int16_t)gsum;
         if (lane == 0) rd[b] = d;
     }
+}
+
+template <int CODE>
+__global__ void __launch_bounds__(kKThreads, CODE == kDtypeQ6_K || CODE == kDtypeQ3_K ? 6 : 8)
+    mv_argmax_k(MvArgmaxPlan p, const uint8_t* lhs) {
+    extern __shared__ __align__(16) uint32_t k_smem[];
+    __shared__ MvPart warp_best[kKWarps];
+    const uint32_t blocks = (uint32_t)(p.k / 256);
+    uint32_t* rq = k_smem;                                           // [blocks][8 groups][8 lanes] quant words
+    float* rd = reinterpret_cast<float*>(rq + blocks * 64);          // [blocks] scales
+    int* rb = reinterpret_cast<int*>(rd + blocks);                   // [blocks][16] group sums
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    using KW = KWindow<CODE>;
+    // [2][32 rows][SWM] staging windows, 16-byte aligned
+    uint32_t* stage = k_smem + ((blocks * 81u + 3u) & ~3u) + warp * 2 * 32 * KW::SWM;
+    pdl_enter();
+    quantize_rhs_q8k<CODE>(p, blocks, rq, rd, rb, kKWarps);
     __syncthreads();
     constexpr uint64_t BB = KW::BB;
     const uint64_t row_bytes = (uint64_t)blocks * BB;
@@ -820,6 +866,142 @@ __global__ void __launch_bounds__(kKThreads, CODE == kDtypeQ6_K || CODE == kDtyp
     finish(p, warp_best[0]);
 }
 
+// Balanced K-quant rows (the vocabulary case).  One lane per row (the
+// kernel above) makes a warp's unit 32 rows: 151,936 rows are 4,748 units,
+// 2.005 per resident warp, so the last round runs a few warps alone and the
+// kernel takes three unit-times for two units of work.  Here a warp's unit
+// is two rows, 16 lanes per row: the unit's rows (contiguous, 16-byte
+// multiples) come in with one bulk copy into the warp's double-buffered
+// stage, lane j of a row forms the terms of blocks j, j + 16, ... into a
+// shared term tile, and the row's reference fold -- lane sums j = 0..7 and
+// the minimum chain, each over the blocks in order, then total + ls[0] + ...
+// + ls[7] -- runs as nine independent chains on nine lanes.  Units: 75,968,
+// 32 per warp; the rounding of the last round costs 3 % instead of 33 %.
+constexpr int kK2Warps = 4;
+constexpr int kK2Threads = kK2Warps * 32;
+
+// shared memory of one warp: two stages of two rows and the [2][blocks][9]
+// term tile, rounded to 128 bytes (every stage starts 16-byte aligned)
+__host__ __device__ __forceinline__ uint32_t k2_warp_words(uint32_t stage_bytes, uint32_t blocks) {
+    return ((2 * stage_bytes) / 4 + 18 * blocks + 31u) & ~31u;
+}
+__host__ __device__ __forceinline__ uint32_t k2_pre_words(uint32_t blocks) { return (blocks * 81u + 31u) & ~31u; }
+
+template <int CODE>
+__global__ void __launch_bounds__(kK2Threads, CODE == kDtypeQ6_K || CODE == kDtypeQ3_K ? 6 : 8)
+    mv_argmax_k2(MvArgmaxPlan p, const uint8_t* lhs, uint32_t stage_bytes) {
+    extern __shared__ __align__(128) uint32_t k2_smem[];
+    __shared__ __align__(8) uint64_t bars[kK2Warps][2];
+    __shared__ MvPart warp_best[kK2Warps];
+    const uint32_t blocks = (uint32_t)(p.k / 256);
+    constexpr uint32_t BB = KWindow<CODE>::BB;
+    const uint32_t row_bytes = blocks * BB;
+    uint32_t* rq = k2_smem;
+    float* rd = reinterpret_cast<float*>(rq + blocks * 64);
+    int* rb = reinterpret_cast<int*>(rd + blocks);
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const uint32_t pre_words = k2_pre_words(blocks);                          // 128-byte aligned
+    const uint32_t warp_words = k2_warp_words(stage_bytes, blocks);         // two stages + term tile
+    unsigned char* stage0 = reinterpret_cast<unsigned char*>(k2_smem + pre_words + warp * warp_words);
+    float* terms = reinterpret_cast<float*>(stage0 + 2 * stage_bytes);     // [2 rows][blocks][9]
+    if (lane == 0) {
+        mbar_init(&bars[warp][0], 1);
+        mbar_init(&bars[warp][1], 1);
+        mbar_init_fence();
+    }
+    pdl_enter();
+    quantize_rhs_q8k<CODE>(p, blocks, rq, rd, rb, kK2Warps);
+    __syncthreads();
+
+    const uint64_t units = (p.rows + 1) / 2;
+    const uint64_t W = (uint64_t)gridDim.x * kK2Warps;
+    const uint64_t gw = (uint64_t)blockIdx.x * kK2Warps + warp;
+    const auto issue = [&](uint64_t u, uint32_t s) {
+        if (lane == 0) {
+            const uint32_t nr = p.rows - 2 * u < 2 ? 1u : 2u;
+            mbar_expect_tx(&bars[warp][s], nr * row_bytes);
+            bulk_load(stage0 + s * stage_bytes, lhs + 2 * u * (uint64_t)row_bytes, nr * row_bytes, &bars[warp][s]);
+        }
+    };
+    const uint32_t rr = (uint32_t)lane >> 4, j = (uint32_t)lane & 15u;
+    MvPart best{0.0f, 0, 0u, 0u};
+    if (gw < units) issue(gw, 0);
+    uint32_t it = 0;
+    for (uint64_t u = gw; u < units; u += W, ++it) {
+        const uint32_t s = it & 1u;
+        const bool next = u + W < units;
+        if (next) issue(u + W, s ^ 1u);
+        if (!mbar_wait(&bars[warp][s], (it >> 1) & 1u)) {
+            // a copy that never landed: flag it, let the other stage's copy
+            // finish (bounded) before the shared memory is released, and stop
+            if (lane == 0) atomicExch(p.fault, 1u);
+            if (next) mbar_wait(&bars[warp][s ^ 1u], ((it + 1) >> 1) & 1u);
+            break;
+        }
+        const uint64_t row = 2 * u + rr;
+        const unsigned char* rowp = stage0 + s * stage_bytes + rr * row_bytes;
+        if (row < p.rows) {
+            for (uint32_t b = j; b < blocks; b += 16) {
+                float o[kKTerms];
+                if constexpr (CODE == kDtypeQ2_K)
+                    q2k_block_terms(reinterpret_cast<const uint32_t*>(rowp + b * BB), rq + b * 64, rb + b * 16, rd[b], o);
+                else if constexpr (CODE == kDtypeQ3_K)
+                    q3k_block_terms(rowp + b * BB, rq + b * 64, rd[b], o);
+                else if constexpr (CODE == kDtypeQ4_K)  // 144-byte blocks of 16-byte multiple rows: aligned
+                    q4k_block_terms<true>(reinterpret_cast<const uint32_t*>(rowp + b * BB), rq + b * 64, rb + b * 16,
+                                          rd[b], o);
+                else
+                    q6k_block_terms(rowp + b * BB, rq + b * 64, rd[b], o);
+                float* t = terms + (rr * blocks + b) * 9;
+                if constexpr (CODE == kDtypeQ2_K) {
+                    t[8] = o[8];
+                } else {
+#pragma unroll
+                    for (int q = 0; q < kKTerms; ++q) t[q] = o[q];
+                }
+            }
+        }
+        __syncwarp();
+        // chain j of the row: j < 8 the lane sum ls[j], j == 8 the running
+        // total (Q4_K subtracts the minimum terms, Q2_K adds its one term)
+        float chain = 0.0f;
+        if (row < p.rows && j < 9) {
+            const float* t = terms + rr * blocks * 9 + j;
+            if (j < 8) {
+                if constexpr (CODE != kDtypeQ2_K)
+                    for (uint32_t b = 0; b < blocks; ++b) chain = __fadd_rn(chain, t[b * 9]);
+            } else {
+                if constexpr (CODE == kDtypeQ2_K)
+                    for (uint32_t b = 0; b < blocks; ++b) chain = __fadd_rn(chain, t[b * 9]);
+                else if constexpr (CODE == kDtypeQ4_K)
+                    for (uint32_t b = 0; b < blocks; ++b) chain = __fsub_rn(chain, t[b * 9]);
+            }
+        }
+        float total = __shfl_sync(0xffffffffu, chain, (int)(rr * 16 + 8));
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            const float lsq = __shfl_sync(0xffffffffu, chain, (int)(rr * 16 + q));
+            if constexpr (CODE != kDtypeQ2_K) total = __fadd_rn(total, lsq);
+        }
+        if (j == 0 && row < p.rows) {
+            const bool nan = is_nan(total);
+            best = mv_better(best, MvPart{total, (int32_t)row, nan ? 0u : 1u, (nan && row == 0) ? 1u : 0u});
+        }
+        __syncwarp();  // the stage and the term tile are consumed before they are refilled
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) best = mv_better(best, mv_shfl(best, o));
+    if (lane == 0) warp_best[warp] = best;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        MvPart b = warp_best[0];
+        for (int w = 1; w < kK2Warps; ++w) b = mv_better(b, warp_best[w]);
+        warp_best[0] = b;
+    }
+    __syncthreads();
+    finish(p, warp_best[0]);
+}
+
 }  // namespace
 
 namespace {
@@ -880,8 +1062,46 @@ cudaError_t launch_mul_mat_argmax(const LaunchEnv& env, const MvArgmaxPlan& p) {
     return err != cudaSuccess ? err : cudaGetLastError();
 }
 
+// The balanced kernel when the rows are 16-byte multiples on a 16-byte
+// aligned base (one bulk copy per two rows) and four warps' stages fit
+// twice per SM; false to fall back to the one-lane-per-row kernel.
+template <int CODE>
+bool launch_k2(const LaunchEnv& env, const MvArgmaxPlan& p, const uint8_t* lhs, cudaError_t* err) {
+    const uint32_t blocks = (uint32_t)(p.k / 256);
+    const uint64_t row_bytes = (uint64_t)blocks * KWindow<CODE>::BB;
+    if (((reinterpret_cast<uintptr_t>(lhs) | (uintptr_t)row_bytes) & 15u) != 0 || p.rows > 0x7fffffffull) return false;
+    const uint32_t stage_bytes = (uint32_t)(2 * row_bytes);
+    const size_t smem = ((size_t)k2_pre_words(blocks) + (size_t)kK2Warps * k2_warp_words(stage_bytes, blocks)) * 4;
+    if (smem > 110 * 1024) return false;
+    static DeviceFlags configured;
+    if (!configured.done(env.device)) {
+        *err = cudaFuncSetAttribute(mv_argmax_k2<CODE>, cudaFuncAttributeMaxDynamicSharedMemorySize, 110 * 1024);
+        if (*err != cudaSuccess) return true;
+        configured.mark(env.device);
+    }
+    static DeviceKeyedValue resident;
+    uint32_t ctas = 0;
+    if (!resident.get(env.device, (uint32_t)smem, &ctas)) {
+        int n = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, mv_argmax_k2<CODE>, kK2Threads, smem) != cudaSuccess || n < 1)
+            n = 1;
+        ctas = (uint32_t)n;
+        resident.put(env.device, (uint32_t)smem, ctas);
+    }
+    const uint64_t units = (p.rows + 1) / 2;
+    const uint64_t want = (units + kK2Warps - 1) / kK2Warps;
+    const uint64_t cap = (uint64_t)env.sm_count * ctas;
+    *err = launch_dependent(mv_argmax_k2<CODE>, dim3((unsigned)(want < cap ? want : cap)), dim3(kK2Threads), smem,
+                            env.stream, p, lhs, stage_bytes);
+    ++*env.launches;
+    if (*err == cudaSuccess) *err = cudaGetLastError();
+    return true;
+}
+
 template <int CODE>
 cudaError_t launch_k(const LaunchEnv& env, const MvArgmaxPlan& p, const uint8_t* lhs) {
+    cudaError_t k2_err = cudaSuccess;
+    if (launch_k2<CODE>(env, p, lhs, &k2_err)) return k2_err;
     const uint64_t groups = (p.rows + kKWarps * 32 - 1) / (kKWarps * 32);
     const size_t table = (size_t)kKWarps * 2 * 32 * KWindow<CODE>::SWM * 4 + 16;  // staging windows + alignment
     const size_t smem = (size_t)(p.k / 256) * (64 * 4 + 4 + 16 * 4) + table;

@@ -433,3 +433,20 @@ def test_k_quant_rows_beyond_one_wave(emel, kern, oracle_lib, code, offset):
     st, sync, ost, gv, gi, ov, oi = run_q4k_both(emel, kern, oracle_lib, blob, rhs, k, rows, code, offset=offset)
     assert st == 0 and sync == 0 and ost == 0
     assert gi == oi and np.array([gv]).view(np.uint32)[0] == np.array([ov]).view(np.uint32)[0]
+
+
+@pytest.mark.parametrize("code", [10, 11, 12, 14])
+@pytest.mark.parametrize("rows,planted", [(151936, 151935), (20001, 0), (20001, 10000)])
+def test_k_quant_balanced_vocabulary_rows(emel, kern, oracle_lib, code, rows, planted):
+    """k = 4096 on a 16-byte aligned base takes the two-rows-per-warp kernel
+    (one bulk copy per two rows, sixteen lanes per row, the reference's fold
+    as nine chains): the vocabulary's 151,936 rows with the maximum in the
+    last row, an odd row count whose last unit holds one row, and maxima
+    at row 0 and mid-tensor, bit-exact against the oracle."""
+    k = 4096
+    rng = np.random.default_rng(777 + code + rows + planted)
+    blob = KQ_ROWS[code](rng, k, rows, planted)
+    rhs = rng.standard_normal(k).astype(np.float32)
+    st, sync, ost, gv, gi, ov, oi = run_q4k_both(emel, kern, oracle_lib, blob, rhs, k, rows, code, offset=0)
+    assert st == 0 and sync == 0 and ost == 0
+    assert gi == oi and np.array([gv]).view(np.uint32)[0] == np.array([ov]).view(np.uint32)[0]
