@@ -674,9 +674,12 @@ __device__ __forceinline__ void q3k_block_terms(const uint8_t* blk_ptr, const ui
 // rhs step of dot_q*_k) into shared memory: rq [blocks][64] quant words in
 // the order the format's decode reads them, rd [blocks] scales, rb
 // [blocks][16] sums of each 16-value group.  One warp per block.
+// qs / bsz: words of rq and ints of rb per block (64 and 16 packed; a
+// padded stride puts different blocks in different banks when lanes read
+// different blocks at once).
 template <int CODE>
 __device__ __forceinline__ void quantize_rhs_q8k(const MvArgmaxPlan& p, uint32_t blocks, uint32_t* rq, float* rd,
-                                                 int* rb, int nwarps) {
+                                                 int* rb, int nwarps, uint32_t qs = 64, uint32_t bsz = 16) {
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (uint32_t b = warp; b < blocks; b += (uint32_t)nwarps) {
         // lane l holds positions 8l .. 8l + 7
@@ -721,11 +724,11 @@ __device__ __forceinline__ void quantize_rhs_q8k(const MvArgmaxPlan& p, uint32_t
         if constexpr (CODE == kDtypeQ4_K) {
             // position 8 * lane + i = 32 g + 8 t + i: group g = lane / 4, t = lane % 4
             const int g = lane >> 2, t = lane & 3;
-            int8_t* words = reinterpret_cast<int8_t*>(rq + b * 64 + g * 8);
+            int8_t* words = reinterpret_cast<int8_t*>(rq + b * qs + g * 8);
 #pragma unroll
             for (int i = 0; i < 8; ++i) words[i * 4 + t] = q[i];
         } else {
-            int8_t* bytes = reinterpret_cast<int8_t*>(rq + b * 64);  // natural order
+            int8_t* bytes = reinterpret_cast<int8_t*>(rq + b * qs);  // natural order
 #pragma unroll
             for (int i = 0; i < 8; ++i) bytes[lane * 8 + i] = q[i];
         }
@@ -733,7 +736,7 @@ __device__ __forceinline__ void quantize_rhs_q8k(const MvArgmaxPlan& p, uint32_t
 #pragma unroll
         for (int i = 0; i < 8; ++i) gsum += q[i];
         gsum += __shfl_xor_sync(0xffffffffu, gsum, 1);  // lanes 2h, 2h + 1 hold group h of 16
-        if ((lane & 1) == 0) rb[b * 16 + (lane >> 1)] = (int)(int16_t)gsum;
+        if ((lane & 1) == 0) rb[b * bsz + (lane >> 1)] = (int)(int16_t)gsum;
         if (lane == 0) rd[b] = d;
     }
 }
@@ -885,7 +888,12 @@ constexpr int kK2Threads = kK2Warps * 32;
 __host__ __device__ __forceinline__ uint32_t k2_warp_words(uint32_t stage_bytes, uint32_t blocks) {
     return ((2 * stage_bytes) / 4 + 18 * blocks + 31u) & ~31u;
 }
-__host__ __device__ __forceinline__ uint32_t k2_pre_words(uint32_t blocks) { return (blocks * 81u + 31u) & ~31u; }
+// rq rows of 65 words and rb rows of 17 ints: sixteen lanes decoding
+// sixteen different blocks read sixteen different banks
+constexpr uint32_t kK2Qs = 65, kK2Bs = 17;
+__host__ __device__ __forceinline__ uint32_t k2_pre_words(uint32_t blocks) {
+    return (blocks * (kK2Qs + 1 + kK2Bs) + 31u) & ~31u;
+}
 
 template <int CODE>
 __global__ void __launch_bounds__(kK2Threads, CODE == kDtypeQ6_K || CODE == kDtypeQ3_K ? 6 : 8)
@@ -897,7 +905,7 @@ __global__ void __launch_bounds__(kK2Threads, CODE == kDtypeQ6_K || CODE == kDty
     constexpr uint32_t BB = KWindow<CODE>::BB;
     const uint32_t row_bytes = blocks * BB;
     uint32_t* rq = k2_smem;
-    float* rd = reinterpret_cast<float*>(rq + blocks * 64);
+    float* rd = reinterpret_cast<float*>(rq + blocks * kK2Qs);
     int* rb = reinterpret_cast<int*>(rd + blocks);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const uint32_t pre_words = k2_pre_words(blocks);                          // 128-byte aligned
@@ -910,7 +918,7 @@ __global__ void __launch_bounds__(kK2Threads, CODE == kDtypeQ6_K || CODE == kDty
         mbar_init_fence();
     }
     pdl_enter();
-    quantize_rhs_q8k<CODE>(p, blocks, rq, rd, rb, kK2Warps);
+    quantize_rhs_q8k<CODE>(p, blocks, rq, rd, rb, kK2Warps, kK2Qs, kK2Bs);
     __syncthreads();
 
     const uint64_t units = (p.rows + 1) / 2;
@@ -944,14 +952,15 @@ __global__ void __launch_bounds__(kK2Threads, CODE == kDtypeQ6_K || CODE == kDty
             for (uint32_t b = j; b < blocks; b += 16) {
                 float o[kKTerms];
                 if constexpr (CODE == kDtypeQ2_K)
-                    q2k_block_terms(reinterpret_cast<const uint32_t*>(rowp + b * BB), rq + b * 64, rb + b * 16, rd[b], o);
+                    q2k_block_terms(reinterpret_cast<const uint32_t*>(rowp + b * BB), rq + b * kK2Qs, rb + b * kK2Bs,
+                                    rd[b], o);
                 else if constexpr (CODE == kDtypeQ3_K)
-                    q3k_block_terms(rowp + b * BB, rq + b * 64, rd[b], o);
+                    q3k_block_terms(rowp + b * BB, rq + b * kK2Qs, rd[b], o);
                 else if constexpr (CODE == kDtypeQ4_K)  // 144-byte blocks of 16-byte multiple rows: aligned
-                    q4k_block_terms<true>(reinterpret_cast<const uint32_t*>(rowp + b * BB), rq + b * 64, rb + b * 16,
-                                          rd[b], o);
+                    q4k_block_terms<true>(reinterpret_cast<const uint32_t*>(rowp + b * BB), rq + b * kK2Qs,
+                                          rb + b * kK2Bs, rd[b], o);
                 else
-                    q6k_block_terms(rowp + b * BB, rq + b * 64, rd[b], o);
+                    q6k_block_terms(rowp + b * BB, rq + b * kK2Qs, rd[b], o);
                 float* t = terms + (rr * blocks + b) * 9;
                 if constexpr (CODE == kDtypeQ2_K) {
                     t[8] = o[8];

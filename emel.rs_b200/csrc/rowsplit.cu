@@ -143,11 +143,67 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitTh
     cluster.sync();  // peers' shared memory stays alive until rank 0 has read it
 }
 
+// argmax_rows without a cluster: the row's kSplitCluster CTAs are
+// independent; each writes its chunk's (value, column) partial to the
+// context workspace and takes a ticket on its row, and the CTA that takes
+// the last ticket folds the row's partials in chunk order (earliest column
+// on ties, NaN at column 0 pins 0) and re-arms the ticket.  No cluster
+// scheduling and no cluster barrier; four (value, vector) chains per thread
+// with fmaxf from a NaN start (three instructions per element).
 struct ChunkPartial {
     float v;
     uint32_t has;
     int64_t i;
 };
+
+__global__ void __launch_bounds__(kSplitThreads, kSplitCtasPerSm)
+    argmax_rows_flat(RowPlan p, int dst_dtype, uint64_t chunk, ChunkPartial* partials, unsigned* tickets) {
+    pdl_enter();
+    __shared__ GroupScratch<kSplitThreads> s;
+    __shared__ bool is_last;
+    const unsigned rank = blockIdx.x % kSplitCluster;
+    const uint64_t r = blockIdx.x / kSplitCluster;
+    const Chunk ch = my_chunk(p.ne[0], chunk, rank);
+    const float* row = reinterpret_cast<const float*>(p.src.ptr) + split_row_base(p.src, r, p.ne[1], p.ne[2]);
+    const float nan = __int_as_float(0x7fc00000);
+    float bv[4] = {nan, nan, nan, nan};
+    uint64_t bc[4] = {0, 0, 0, 0};
+    const float4* r4 = reinterpret_cast<const float4*>(row);
+    batched<8>(ch.col0 / 4, ch.col1 / 4, [&](uint64_t v) { return __ldcs(r4 + v); },
+               [&](uint64_t v, float4 q) {
+                   const float q4[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+                   for (int l = 0; l < 4; ++l) {
+                       const float nb = fmaxf(bv[l], q4[l]);
+                       if (nb != bv[l]) bc[l] = v;
+                       bv[l] = nb;
+                   }
+               });
+    ArgBest bl[4];
+#pragma unroll
+    for (int l = 0; l < 4; ++l) bl[l] = ArgBest{bv[l], (int64_t)(4 * bc[l] + l), is_nan(bv[l]) ? 0u : 1u};
+    ArgBest b = arg_better(arg_better(bl[0], bl[1]), arg_better(bl[2], bl[3]));
+    b = group_argmax<kSplitThreads>(b, &s);
+    if (threadIdx.x == 0) {
+        partials[r * kSplitCluster + rank] = ChunkPartial{b.v, b.has, b.i};
+        __threadfence();
+        is_last = atomicAdd(&tickets[r], 1u) == kSplitCluster - 1;
+    }
+    __syncthreads();
+    if (!is_last || threadIdx.x != 0) return;
+    __threadfence();
+    ArgBest best{0.0f, 0, 0};
+    for (int k = 0; k < kSplitCluster; ++k) {
+        const ChunkPartial* q = partials + r * kSplitCluster + k;
+        best = arg_better(best, ArgBest{__ldcg(&q->v), __ldcg(&q->i), __ldcg(&q->has)});
+    }
+    const int64_t idx = (is_nan(row[0]) || !best.has) ? 0 : best.i;
+    const int64_t off = split_row_base(p.dst, r, p.ne[1], p.ne[2]);
+    if (dst_dtype == (int)DType::I64) reinterpret_cast<int64_t*>(p.dst.ptr)[off] = idx;
+    else if (dst_dtype == (int)DType::I32) reinterpret_cast<int32_t*>(p.dst.ptr)[off] = (int32_t)idx;
+    else reinterpret_cast<float*>(p.dst.ptr)[off] = (float)idx;
+    tickets[r] = 0u;
+}
 
 __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitThreads, kSplitCtasPerSm)
     sum_rows_split(RowPlan p, uint64_t chunk) {
@@ -343,298 +399,6 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitTh
     cluster.sync();  // peers' shared memory stays alive until every CTA has read it
 }
 
-// ---------------------------------------------------------------------------
-// Dense rows as one balanced wave (argmax_rows, soft_max).  The grid is
-// kSegCtasPerSm CTAs per SM, all resident; CTA c owns the contiguous vectors
-// [c V / G, (c + 1) V / G) of the tensor's V = rows * ne0 / 4 vectors.  A row
-// is ne0 / 4 >= 4096 vectors and a CTA's share at most rows * ne0 / (4 G) <=
-// ne0 / 16 (rows <= SMs), so a share lies in one row or straddles two: one
-// or two (CTA, row) segments, each leaving one partial in the context
-// workspace (slots 2c and 2c + 1).  Per row a counter adds up the vectors of
-// the finished segments; the CTA whose segment completes the row folds the
-// row's partials (CTAs c_first(r) .. c_last(r)) and re-arms the counter.
-// Every SM streams the same number of bytes and no CTA waits for another.
-// ---------------------------------------------------------------------------
-constexpr int kSegCtasPerSm = 4;  // with four loads in flight per thread (64 KB per SM): 64 registers, no spills
-
-struct SegGrid {
-    uint64_t nvec;  // V
-    uint32_t ctas;  // G
-    uint32_t vpr;   // vectors per row
-};
-
-struct RowInfo {  // per row, in the workspace: soft_max's maximum and denominator
-    float max;
-    float den;
-    uint32_t exact;  // 1: the row had a NaN or an infinity and was computed whole with the x86 NaN rules
-    uint32_t pad;
-};
-
-__device__ __forceinline__ uint64_t seg_first(const SegGrid& g, uint64_t c) { return c * g.nvec / g.ctas; }
-// the CTA whose share holds vector v: the largest c with seg_first(c) <= v
-__device__ __forceinline__ uint64_t seg_owner(const SegGrid& g, uint64_t v) { return ((v + 1) * g.ctas - 1) / g.nvec; }
-// partial slot of CTA c's segment in row r
-__device__ __forceinline__ uint64_t seg_slot(const SegGrid& g, uint64_t c, uint64_t r) {
-    return 2 * c + (seg_first(g, c) / g.vpr == r ? 0 : 1);
-}
-
-// Calls seg(r, v0, v1, slot) for each of this CTA's segments.
-template <typename Seg>
-__device__ __forceinline__ void for_segments(const SegGrid& g, Seg seg) {
-    const uint64_t c = blockIdx.x;
-    const uint64_t end = seg_first(g, c + 1);
-    uint64_t v0 = seg_first(g, c);
-    unsigned k = 0;
-    while (v0 < end) {
-        const uint64_t r = v0 / g.vpr;
-        const uint64_t v1 = end < (r + 1) * g.vpr ? end : (r + 1) * g.vpr;
-        seg(r, v0, v1, 2 * c + k);
-        v0 = v1;
-        ++k;
-    }
-}
-
-// batched over a segment of n vectors with 32-bit indices (fewer registers
-// than the 64-bit walk): U loads issued before any is used, the last batch
-// included.
-template <int U, typename Load, typename Use>
-__device__ __forceinline__ void seg_batched(uint32_t n, Load load, Use use) {
-    uint32_t v = threadIdx.x;
-    for (; v + (U - 1) * kSplitThreads < n; v += U * kSplitThreads) {
-        float4 q[U];
-#pragma unroll
-        for (int k = 0; k < U; ++k) q[k] = load(v + k * kSplitThreads);
-#pragma unroll
-        for (int k = 0; k < U; ++k) use(v + k * kSplitThreads, q[k]);
-    }
-    if (v < n) {
-        float4 q[U];
-#pragma unroll
-        for (int k = 0; k < U; ++k)
-            if (v + k * kSplitThreads < n) q[k] = load(v + k * kSplitThreads);
-#pragma unroll
-        for (int k = 0; k < U; ++k)
-            if (v + k * kSplitThreads < n) use(v + k * kSplitThreads, q[k]);
-    }
-}
-
-// After thread 0 stored the segment's partial: adds the segment's vectors to
-// the row's counter; true (in every thread) when this segment completed the
-// row.  The partial store is ordered before the counter update, and the
-// folding CTA's reads after it.
-__device__ __forceinline__ bool seg_arrive(unsigned* counter, uint32_t nv, uint32_t vpr, bool* flag) {
-    if (threadIdx.x == 0) {
-        __threadfence();
-        *flag = atomicAdd(counter, nv) + nv == vpr;
-    }
-    __syncthreads();
-    const bool last = *flag;
-    if (last) __threadfence();
-    return last;
-}
-
-__device__ __forceinline__ float group_max_nan(float m, GroupScratch<kSplitThreads>* s) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, o));
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0) s->f[threadIdx.x / 32] = m;
-    __syncthreads();
-    m = s->f[0];
-#pragma unroll
-    for (int w = 1; w < kSplitThreads / 32; ++w) m = max_nan(m, s->f[w]);
-    return m;
-}
-
-__global__ void __launch_bounds__(kSplitThreads, kSegCtasPerSm)
-    argmax_rows_seg(RowPlan p, int dst_dtype, SegGrid g, ChunkPartial* partials, unsigned* counters) {
-    pdl_enter();
-    __shared__ GroupScratch<kSplitThreads> s;
-    __shared__ bool last_flag;
-    const float4* x4 = reinterpret_cast<const float4*>(p.src.ptr);
-    for_segments(g, [&](uint64_t r, uint64_t v0, uint64_t v1, uint64_t slot) {
-        // four (value, vector) chains per thread, fmaxf from a NaN start: the
-        // first occurrence of each lane's maximum (three instructions per element)
-        const uint64_t rbase = r * g.vpr;
-        const float nan = __int_as_float(0x7fc00000);
-        float bv[4] = {nan, nan, nan, nan};
-        uint32_t bc[4] = {0, 0, 0, 0};
-        const float4* xs = x4 + v0;
-        seg_batched<4>((uint32_t)(v1 - v0), [&](uint32_t v) { return __ldcs(xs + v); },
-                       [&](uint32_t v, float4 q) {
-                           const float q4[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-                           for (int l = 0; l < 4; ++l) {
-                               const float nb = fmaxf(bv[l], q4[l]);
-                               if (nb != bv[l]) bc[l] = v;
-                               bv[l] = nb;
-                           }
-                       });
-        const uint64_t off = v0 - rbase;  // the segment's first vector within the row
-        ArgBest bl[4];
-#pragma unroll
-        for (int l = 0; l < 4; ++l) bl[l] = ArgBest{bv[l], (int64_t)(4 * (off + bc[l]) + l), is_nan(bv[l]) ? 0u : 1u};
-        ArgBest b = arg_better(arg_better(bl[0], bl[1]), arg_better(bl[2], bl[3]));
-        b = group_argmax<kSplitThreads>(b, &s);
-        if (threadIdx.x == 0) partials[slot] = ChunkPartial{b.v, b.has, b.i};
-        if (!seg_arrive(&counters[r], (uint32_t)(v1 - v0), g.vpr, &last_flag)) return;
-        // fold: a maximum under a total order (has, value, then the smaller column)
-        const uint64_t cf = seg_owner(g, rbase), cl = seg_owner(g, rbase + g.vpr - 1);
-        ArgBest best{0.0f, 0, 0};
-        for (uint64_t cc = cf + threadIdx.x; cc <= cl; cc += kSplitThreads) {
-            const ChunkPartial* q = partials + seg_slot(g, cc, r);
-            best = arg_better(best, ArgBest{__ldcg(&q->v), __ldcg(&q->i), __ldcg(&q->has)});
-        }
-        best = group_argmax<kSplitThreads>(best, &s);
-        if (threadIdx.x == 0) {
-            const float* row = reinterpret_cast<const float*>(p.src.ptr) + rbase * 4;
-            const int64_t idx = (is_nan(row[0]) || !best.has) ? 0 : best.i;
-            const int64_t off = split_row_base(p.dst, r, p.ne[1], p.ne[2]);
-            if (dst_dtype == (int)DType::I64) reinterpret_cast<int64_t*>(p.dst.ptr)[off] = idx;
-            else if (dst_dtype == (int)DType::I32) reinterpret_cast<int32_t*>(p.dst.ptr)[off] = (int32_t)idx;
-            else reinterpret_cast<float*>(p.dst.ptr)[off] = (float)idx;
-            counters[r] = 0u;
-        }
-        __syncthreads();
-    });
-}
-
-// soft_max over dense rows in three launches: the row maximum (one HBM
-// read), e = exp(v - max) into dst with the f64 sum (the source again,
-// from L2), e / sum in place.  A row whose maximum is not finite (a NaN,
-// or an infinity) is computed whole, with the x86 NaN rules, by the CTA
-// that found its maximum, and the later launches skip it.
-__device__ __forceinline__ float4 seg_scale4(float4 q, bool apply_scale, float scale) {
-    return apply_scale ? make_float4(__fmul_rn(q.x, scale), __fmul_rn(q.y, scale), __fmul_rn(q.z, scale),
-                                     __fmul_rn(q.w, scale))
-                       : q;
-}
-
-__device__ void softmax_row_exact(const RowPlan& p, uint64_t r, bool apply_scale, float scale,
-                                  GroupScratch<kSplitThreads>* s) {
-    SoftmaxRow w;
-    w.x = reinterpret_cast<const float*>(p.src.ptr) + r * p.ne[0];
-    w.y = reinterpret_cast<float*>(p.dst.ptr) + r * p.ne[0];
-    w.xs = 1;
-    w.ys = 1;
-    w.mbase = 0;
-    w.has_mask = false;
-    const uint64_t n = p.ne[0];
-    // the reference's maximum: element 0, then strictly greater values (a
-    // NaN is never greater, so only a NaN at element 0 is selected)
-    float em = bitsf(0x7fc00000u);
-    for (uint64_t c = threadIdx.x; c < n; c += kSplitThreads) em = max_nn(em, value_at<true>(p, w, c, apply_scale, scale));
-    float gm = group_max<kSplitThreads>(em, s);
-    const float v0 = value_at<true>(p, w, 0, apply_scale, scale);
-    if (is_nan(v0)) gm = v0;
-    double acc = 0.0;
-    for (uint64_t c = threadIdx.x; c < n; c += kSplitThreads) {
-        const float e = lm_exp(f_sub(value_at<true>(p, w, c, apply_scale, scale), gm));
-        w.y[c] = e;
-        acc += (double)e;
-    }
-    const float denom = __double2float_rn(group_sum<kSplitThreads>(acc, s));
-    for (uint64_t c = threadIdx.x; c < n; c += kSplitThreads) w.y[c] = f_div(w.y[c], denom);
-}
-
-__global__ void __launch_bounds__(kSplitThreads, kSegCtasPerSm)
-    softmax_seg_max(RowPlan p, bool apply_scale, float scale, SegGrid g, ChunkPartial* partials, unsigned* counters,
-                    RowInfo* info) {
-    pdl_enter();
-    __shared__ GroupScratch<kSplitThreads> s;
-    __shared__ bool last_flag;
-    const float4* x4 = reinterpret_cast<const float4*>(p.src.ptr);
-    for_segments(g, [&](uint64_t r, uint64_t v0, uint64_t v1, uint64_t slot) {
-        // NaN-propagating maximum: a NaN anywhere, or a maximum of +-inf,
-        // leaves the row's maximum non-finite
-        float m = -INFINITY;
-        const float4* xs = x4 + v0;
-        seg_batched<4>((uint32_t)(v1 - v0), [&](uint32_t v) { return __ldcg(xs + v); },
-                       [&](uint32_t, float4 raw) {
-                           const float4 q = seg_scale4(raw, apply_scale, scale);
-                           m = max_nan(max_nan(m, q.x), max_nan(q.y, max_nan(q.z, q.w)));
-                       });
-        m = group_max_nan(m, &s);
-        if (threadIdx.x == 0) partials[slot].v = m;
-        if (!seg_arrive(&counters[r], (uint32_t)(v1 - v0), g.vpr, &last_flag)) return;
-        const uint64_t rbase = r * g.vpr;
-        const uint64_t cf = seg_owner(g, rbase), cl = seg_owner(g, rbase + g.vpr - 1);
-        float gm = -INFINITY;
-        for (uint64_t cc = cf + threadIdx.x; cc <= cl; cc += kSplitThreads)
-            gm = max_nan(gm, __ldcg(&partials[seg_slot(g, cc, r)].v));
-        gm = group_max_nan(gm, &s);
-        const bool exact = !isfinite(gm);
-        if (exact) softmax_row_exact(p, r, apply_scale, scale, &s);
-        if (threadIdx.x == 0) {
-            info[r].max = gm;
-            info[r].exact = exact ? 1u : 0u;
-            counters[r] = 0u;
-        }
-        __syncthreads();
-    });
-}
-
-__global__ void __launch_bounds__(kSplitThreads, kSegCtasPerSm)
-    softmax_seg_exp(RowPlan p, bool apply_scale, float scale, SegGrid g, ChunkPartial* partials, unsigned* counters,
-                    RowInfo* info) {
-    pdl_enter();
-    __shared__ GroupScratch<kSplitThreads> s;
-    __shared__ bool last_flag;
-    const float4* x4 = reinterpret_cast<const float4*>(p.src.ptr);
-    float4* y4 = reinterpret_cast<float4*>(p.dst.ptr);
-    for_segments(g, [&](uint64_t r, uint64_t v0, uint64_t v1, uint64_t slot) {
-        if (__ldcg(&info[r].exact)) return;
-        const float gm = __ldcg(&info[r].max);
-        double acc = 0.0;
-        const float4* xs = x4 + v0;
-        float4* ys = y4 + v0;
-        seg_batched<4>((uint32_t)(v1 - v0), [&](uint32_t v) { return __ldcg(xs + v); },
-                       [&](uint32_t v, float4 raw) {
-                           const float4 q = seg_scale4(raw, apply_scale, scale);
-                           const float4 e =
-                               make_float4(softmax_exp(__fsub_rn(q.x, gm)), softmax_exp(__fsub_rn(q.y, gm)),
-                                           softmax_exp(__fsub_rn(q.z, gm)), softmax_exp(__fsub_rn(q.w, gm)));
-                           ys[v] = e;
-                           acc += (double)e.x;
-                           acc += (double)e.y;
-                           acc += (double)e.z;
-                           acc += (double)e.w;
-                       });
-        acc = group_sum<kSplitThreads>(acc, &s);
-        if (threadIdx.x == 0) reinterpret_cast<double*>(partials)[2 * slot] = acc;
-        if (!seg_arrive(&counters[r], (uint32_t)(v1 - v0), g.vpr, &last_flag)) return;
-        // fold: each thread adds its share of the partials in CTA order, then
-        // the fixed tree of group_sum (deterministic for a fixed grid)
-        const uint64_t rbase = r * g.vpr;
-        const uint64_t cf = seg_owner(g, rbase), cl = seg_owner(g, rbase + g.vpr - 1);
-        double total = 0.0;
-        for (uint64_t cc = cf + threadIdx.x; cc <= cl; cc += kSplitThreads)
-            total += __ldcg(reinterpret_cast<const double*>(partials) + 2 * seg_slot(g, cc, r));
-        total = group_sum<kSplitThreads>(total, &s);
-        if (threadIdx.x == 0) {
-            info[r].den = __double2float_rn(total);
-            counters[r] = 0u;
-        }
-        __syncthreads();
-    });
-}
-
-__global__ void __launch_bounds__(kSplitThreads, kSegCtasPerSm)
-    softmax_seg_div(RowPlan p, SegGrid g, const RowInfo* info) {
-    pdl_enter();
-    float4* y4 = reinterpret_cast<float4*>(p.dst.ptr);
-    for_segments(g, [&](uint64_t r, uint64_t v0, uint64_t v1, uint64_t) {
-        if (__ldcg(&info[r].exact)) return;
-        const float denom = __ldcg(&info[r].den);
-        const float inv = __frcp_rn(denom);
-        float4* ys = y4 + v0;
-        seg_batched<4>((uint32_t)(v1 - v0), [&](uint32_t v) { return __ldcg(ys + v); },
-                       [&](uint32_t v, float4 e) {
-                           __stcs(ys + v, make_float4(softmax_div(e.x, denom, inv), softmax_div(e.y, denom, inv),
-                                                      softmax_div(e.z, denom, inv), softmax_div(e.w, denom, inv)));
-                       });
-    });
-}
-
 uint64_t split_chunk(uint64_t ne0) {
     uint64_t c = (ne0 + kSplitCluster - 1) / kSplitCluster;
     return (c + 3) / 4 * 4;  // keeps every chunk's first column 16-byte aligned
@@ -648,54 +412,15 @@ bool split_rows_wanted(const LaunchEnv& env, const RowPlan& p) {
            !p.dst_ordinal;
 }
 
-namespace {
-
-// The segmented kernels' workspace: 2 G (= kSplitRowChunks per SM) 16-byte
-// partials, one counter per row, one RowInfo per row.
-struct SegSpace {
-    ChunkPartial* partials;
-    unsigned* counters;
-    RowInfo* info;
-};
-
-SegSpace seg_space(const LaunchEnv& env) {
-    static_assert(2 * kSegCtasPerSm == kSplitRowChunks, "two partial slots per CTA");
-    char* base = static_cast<char*>(env.workspace) + split_rows_workspace_offset(env.sm_count);
-    SegSpace w;
-    w.partials = reinterpret_cast<ChunkPartial*>(base);
-    w.counters = reinterpret_cast<unsigned*>(base + (uint64_t)env.sm_count * kSplitRowChunks * 16);
-    w.info = reinterpret_cast<RowInfo*>(base + split_rows_info_offset(env.sm_count));
-    return w;
-}
-
-SegGrid seg_grid(const LaunchEnv& env, const RowPlan& p) {
-    return SegGrid{p.rows * p.ne[0] / 4, (uint32_t)env.sm_count * kSegCtasPerSm, (uint32_t)(p.ne[0] / 4)};
-}
-
-// one dense, 16-byte aligned run of rows * ne0 floats (ne0 % 4 == 0)
-bool dense_run(const RowOperand& o, const uint64_t ne[4]) {
-    if ((reinterpret_cast<uintptr_t>(o.ptr) & 15u) != 0 || ne[0] % 4 != 0 || o.st[0] != 1) return false;
-    uint64_t want = ne[0];
-    for (int d = 1; d < 4; ++d) {
-        if (ne[d] > 1 && (uint64_t)o.st[d] != want) return false;
-        want *= ne[d];
-    }
-    return true;
-}
-
-bool seg_wanted(const RowPlan& p) {
-    return dense_run(p.src, p.ne) && p.ne[0] / 4 <= 0xffffffffull;
-}
-
-}  // namespace
-
 cudaError_t launch_argmax_rows_split(const LaunchEnv& env, const RowPlan& p, int dst_dtype) {
     cudaError_t err;
-    if (seg_wanted(p)) {
-        const SegSpace w = seg_space(env);
-        const SegGrid g = seg_grid(env, p);
-        err = launch_dependent(argmax_rows_seg, dim3(g.ctas), dim3(kSplitThreads), 0, env.stream, p, dst_dtype, g,
-                               w.partials, w.counters);
+    if (p.vec) {
+        static_assert(kSplitCluster == kSplitRowChunks, "workspace slots per row");
+        char* base = static_cast<char*>(env.workspace) + split_rows_workspace_offset(env.sm_count);
+        auto* partials = reinterpret_cast<ChunkPartial*>(base);
+        auto* tickets = reinterpret_cast<unsigned*>(base + (uint64_t)env.sm_count * kSplitRowChunks * 16);
+        err = launch_dependent(argmax_rows_flat, dim3((unsigned)(p.rows * kSplitCluster)), dim3(kSplitThreads), 0,
+                               env.stream, p, dst_dtype, split_chunk(p.ne[0]), partials, tickets);
     } else {
         err = launch_dependent(argmax_rows_split, dim3((unsigned)(p.rows * kSplitCluster)), dim3(kSplitThreads), 0,
                                env.stream, p, dst_dtype, split_chunk(p.ne[0]));
@@ -712,24 +437,10 @@ cudaError_t launch_sum_rows_split(const LaunchEnv& env, const RowPlan& p) {
 }
 
 cudaError_t launch_soft_max_split(const LaunchEnv& env, const RowPlan& p, bool apply_scale, float scale) {
-    cudaError_t err;
-    if (seg_wanted(p) && dense_run(p.dst, p.ne) && !(apply_scale && p.has_aux)) {
-        const SegSpace w = seg_space(env);
-        const SegGrid g = seg_grid(env, p);
-        err = launch_dependent(softmax_seg_max, dim3(g.ctas), dim3(kSplitThreads), 0, env.stream, p, apply_scale, scale,
-                               g, w.partials, w.counters, w.info);
-        if (err == cudaSuccess)
-            err = launch_dependent(softmax_seg_exp, dim3(g.ctas), dim3(kSplitThreads), 0, env.stream, p, apply_scale,
-                                   scale, g, w.partials, w.counters, w.info);
-        if (err == cudaSuccess)
-            err = launch_dependent(softmax_seg_div, dim3(g.ctas), dim3(kSplitThreads), 0, env.stream, p, g,
-                                   static_cast<const RowInfo*>(w.info));
-        *env.launches += 3;
-    } else {
-        err = launch_dependent(softmax_rows_split, dim3((unsigned)(p.rows * kSplitCluster)), dim3(kSplitThreads), 0,
-                               env.stream, p, apply_scale, scale, split_chunk(p.ne[0]));
-        ++*env.launches;
-    }
+    const cudaError_t err = launch_dependent(softmax_rows_split, dim3((unsigned)(p.rows * kSplitCluster)),
+                                             dim3(kSplitThreads), 0, env.stream, p, apply_scale, scale,
+                                             split_chunk(p.ne[0]));
+    ++*env.launches;
     return err != cudaSuccess ? err : cudaGetLastError();
 }
 

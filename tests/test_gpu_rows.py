@@ -420,12 +420,12 @@ def test_split_softmax_special_rows_and_mask(emel, kern, oracle_lib):
 
 
 @pytest.mark.parametrize("width,rows", [(16388, 5), (151936, 1), (40000, 148), (65540, 3)])
-def test_segmented_rows_soft_max_scale_and_argmax(emel, kern, oracle_lib, width, rows):
-    """Dense few-long-rows tensors take the one-wave segmented kernels: every
-    CTA's share lies in one row or straddles two, and the share boundaries
-    fall at arbitrary columns (16388 columns = 4097 vectors per row; one
-    row; as many rows as SMs).  soft_max_ext with a scale and no mask takes
-    the same path; argmax ties across shares pick the earliest column."""
+def test_split_rows_soft_max_scale_and_argmax(emel, kern, oracle_lib, width, rows):
+    """Few long rows at widths whose chunk boundaries fall at arbitrary
+    columns (16388 columns = 4097 vectors per row), one row, and as many
+    rows as SMs: soft_max_ext with a scale and no mask (one row with an
+    infinite maximum, redone with the x86 NaN rules) and argmax ties across
+    chunks (the earlier column wins)."""
     rng = np.random.default_rng(width + rows)
     x = (rng.standard_normal(width * rows) * 3).astype(np.float32).reshape(rows, width)
     x[:, width // 3] = 50.0     # tie with the last column: the earlier one wins
@@ -434,7 +434,7 @@ def test_segmented_rows_soft_max_scale_and_argmax(emel, kern, oracle_lib, width,
         x[2, 0] = np.inf        # an infinite maximum: the row is redone exactly
     got, want = run_row_op(emel, kern, oracle_lib, "soft_max_ext", x.ravel(), [width, rows, 1, 1], scale=0.37)
     nan = np.isnan(want)
-    assert np.array_equal(np.isnan(got), nan), "segmented soft_max_ext: NaN positions"
-    close(got[~nan], want[~nan], 1e-30, f"segmented soft_max_ext {width}x{rows}")
+    assert np.array_equal(np.isnan(got), nan), "split soft_max_ext: NaN positions"
+    close(got[~nan], want[~nan], 1e-30, f"split soft_max_ext {width}x{rows}")
     got, want = run_row_op(emel, kern, oracle_lib, "argmax_rows", x.ravel(), [width, rows, 1, 1], out_dtype=np.int32)
-    assert np.array_equal(got, want), f"segmented argmax_rows {width}x{rows}"
+    assert np.array_equal(got, want), f"split argmax_rows {width}x{rows}"
