@@ -434,6 +434,15 @@ struct alignas(16) Vec16 {
     T v[N];
 };
 
+// binary16 lanes held as four 32-bit words (lane 2i in the low half of word
+// i): the vector stays in four registers from the load to the store instead
+// of being split into eight 16-bit values and packed again.
+template <>
+struct alignas(16) Vec16<uint16_t> {
+    static constexpr int N = 8;
+    uint32_t w[4];
+};
+
 template <typename T>
 __device__ __forceinline__ Vec16<T> ld_stream(const T* p) {
     Vec16<T> r;
@@ -461,9 +470,14 @@ __device__ __forceinline__ void st_stream(T* p, const Vec16<T>& v) {
 }
 
 __device__ __forceinline__ float vget(const Vec16<float>& v, int i) { return v.v[i]; }
-__device__ __forceinline__ float vget(const Vec16<uint16_t>& v, int i) { return f16_bits_to_f32(v.v[i]); }
+__device__ __forceinline__ float vget(const Vec16<uint16_t>& v, int i) {
+    return f16_bits_to_f32((uint16_t)(v.w[i >> 1] >> (16 * (i & 1))));
+}
 __device__ __forceinline__ void vset(Vec16<float>& v, int i, float x) { v.v[i] = x; }
-__device__ __forceinline__ void vset(Vec16<uint16_t>& v, int i, float x) { v.v[i] = f32_to_f16_bits(x); }
+__device__ __forceinline__ void vset(Vec16<uint16_t>& v, int i, float x) {
+    const int sh = 16 * (i & 1);
+    v.w[i >> 1] = (v.w[i >> 1] & ~(0xffffu << sh)) | ((uint32_t)f32_to_f16_bits(x) << sh);
+}
 
 // 32-bit unsigned division by a run-time constant (round-up multiply-shift,
 // Granlund-Montgomery), used to decode logical ordinals into coordinates.
