@@ -97,13 +97,11 @@ constexpr uint64_t kDomainTableBytes = (uint64_t)kDomainTableSlots * 65536ull * 
 cudaError_t build_domain_tables(void* tables, cudaStream_t stream);
 
 // Bytes of context workspace: the whole-tensor reductions' partials and, at
-// split_rows_workspace_offset, the few-long-rows kernels' area: kSplitRowChunks
-// 16-byte partials per SM, one counter per row (up to sm_count rows) and, at
-// split_rows_info_offset within the area, one 16-byte record per row.
+// split_rows_workspace_offset, one 16-byte partial per chunk of each of up to
+// sm_count long rows plus one ticket per row (the few-long-rows kernels).
 constexpr int kSplitRowChunks = 8;
 uint64_t reduction_workspace_bytes(int sm_count);
 uint64_t split_rows_workspace_offset(int sm_count);
-uint64_t split_rows_info_offset(int sm_count);
 
 // Row gather (getrows.cu).
 enum GatherKind : int { kGatherF32 = 0, kGatherF16 = 1, kGatherBF16 = 2, kGatherQ4_0 = 3, kGatherQ8_0 = 4, kGatherQ4_K = 5,

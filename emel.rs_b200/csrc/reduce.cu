@@ -335,14 +335,9 @@ uint64_t split_rows_workspace_offset(int sm_count) {
     return (256 + (uint64_t)sm_count * kCtasPerSm * 16 + 255) / 256 * 256;
 }
 
-uint64_t split_rows_info_offset(int sm_count) {
-    // after the chunk partials and the row counters, 16-byte aligned
-    return ((uint64_t)sm_count * (kSplitRowChunks * 16 + 4) + 15) / 16 * 16;
-}
-
 uint64_t reduction_workspace_bytes(int sm_count) {
-    // + the few-long-rows kernels' partials, row counters and 16-byte row records
-    return split_rows_workspace_offset(sm_count) + split_rows_info_offset(sm_count) + (uint64_t)sm_count * 16 + 256;
+    // + the few-long-rows kernels' per-row chunk partials and row tickets
+    return split_rows_workspace_offset(sm_count) + (uint64_t)sm_count * (kSplitRowChunks * 16 + 4) + 256;
 }
 
 static uint32_t reduce_grid(const LaunchEnv& env, uint64_t n) {

@@ -19,7 +19,6 @@
 #include "launch.hpp"
 #include "pdl.cuh"
 #include "rowreduce.cuh"
-#include "tma.cuh"
 
 namespace cg = cooperative_groups;
 
@@ -400,360 +399,6 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitTh
     cluster.sync();  // peers' shared memory stays alive until every CTA has read it
 }
 
-// ---------------------------------------------------------------------------
-// argmax over few long dense rows, streamed through a shared-memory ring.
-// kRaCtasPerSm CTAs of kRaThreads per SM, all resident; CTA c owns the
-// contiguous vectors [c V / G, (c + 1) V / G) of the tensor's V vectors -- a
-// share of at most half a row (rows <= SMs), so one row or the end of one
-// and the start of the next: one or two segments.  Thread 0 keeps
-// kRaStages bulk copies of up to 16 KB in flight (a chunk never crosses a
-// segment boundary), so the reads in flight per SM do not depend on
-// registers; every thread folds its vectors of each landed chunk into four
-// lane chains (fmaxf from a NaN start, the column moved when the maximum
-// changes).  At a segment's end the CTA's (value, column) partial goes to
-// the context workspace (slot 2c or 2c + 1), and a per-row counter of
-// vectors names the CTA that completes the row; it folds the row's partials
-// (the CTAs whose shares meet the row) -- a maximum under the total order
-// (value, then the smaller column), NaN at column 0 pinning 0 -- and re-arms
-// the counter.
-// ---------------------------------------------------------------------------
-constexpr int kRaThreads = 512;
-constexpr int kRaCtasPerSm = 2;
-constexpr int kRaStages = 4;
-constexpr uint32_t kRaChunk = 1024;  // vectors per stage (16 KB): two per thread
-
-struct RaGrid {
-    uint64_t nvec;  // V
-    uint32_t ctas;  // G
-    uint32_t vpr;   // vectors per row
-};
-
-__device__ __forceinline__ uint64_t ra_first(const RaGrid& g, uint64_t c) { return c * g.nvec / g.ctas; }
-// the CTA whose share holds vector v: the largest c with ra_first(c) <= v
-__device__ __forceinline__ uint64_t ra_owner(const RaGrid& g, uint64_t v) { return ((v + 1) * g.ctas - 1) / g.nvec; }
-
-// Streams this CTA's share through the ring: chunk(r, base, q4, cnt) for
-// each landed chunk of cnt vectors (q4 in shared memory; base = the
-// chunk's first vector within row r), then seg_end(r, k, nv, failed) at the
-// end of segment k (nv vectors; failed: a copy never landed, the fault word
-// is set and the segment's data must not be used).  Thread 0 issues the
-// copies; the caller initialised nothing.
-template <typename Chunk, typename SegEnd>
-__device__ __forceinline__ void ring_stream(const RaGrid& g, const float4* x4, float4* ring, uint64_t* full,
-                                            uint32_t* fault, Chunk on_chunk, SegEnd seg_end) {
-    const uint64_t c = blockIdx.x;
-    const uint64_t lo = ra_first(g, c), hi = ra_first(g, c + 1);
-    const uint64_t r0 = lo / g.vpr;
-    const uint64_t split = hi < (r0 + 1) * g.vpr ? hi : (r0 + 1) * g.vpr;  // end of the first segment
-    const uint32_t n0 = (uint32_t)((split - lo + kRaChunk - 1) / kRaChunk);
-    const uint32_t n = n0 + (uint32_t)((hi - split + kRaChunk - 1) / kRaChunk);
-    const auto chunk = [&](uint32_t j, uint64_t& a, uint64_t& b) {
-        if (j < n0) {
-            a = lo + (uint64_t)j * kRaChunk;
-            b = split < a + kRaChunk ? split : a + kRaChunk;
-        } else {
-            a = split + (uint64_t)(j - n0) * kRaChunk;
-            b = hi < a + kRaChunk ? hi : a + kRaChunk;
-        }
-    };
-    const auto issue = [&](uint32_t j) {
-        uint64_t a, b;
-        chunk(j, a, b);
-        const uint32_t st = j % kRaStages;
-        mbar_expect_tx(&full[st], (uint32_t)(b - a) * 16u);
-        bulk_load(ring + st * kRaChunk, x4 + a, (uint32_t)(b - a) * 16u, &full[st]);
-    };
-    if (threadIdx.x == 0) {
-        for (int st = 0; st < kRaStages; ++st) mbar_init(&full[st], 1);
-        mbar_init_fence();
-    }
-    __syncthreads();
-    pdl_enter();
-    uint32_t issued = 0;
-    if (threadIdx.x == 0)
-        for (; issued < n && issued < (uint32_t)kRaStages; ++issued) issue(issued);
-    bool failed = false;
-    for (uint32_t j = 0; j < n; ++j) {
-        const uint32_t st = j % kRaStages;
-        uint64_t a, b;
-        chunk(j, a, b);
-        const uint64_t r = j < n0 ? r0 : r0 + 1;
-        if (!failed) {
-            const bool ok = mbar_wait(&full[st], (j / kRaStages) & 1u);
-            if (!__syncthreads_and(ok)) {
-                // a copy that never landed: flag it and let every copy in
-                // flight finish (bounded) before the shared memory is released;
-                // the segments still end, so the row counters stay consistent
-                failed = true;
-                if (threadIdx.x == 0) {
-                    atomicExch(fault, 1u);
-                    for (uint32_t jj = j; jj < issued; ++jj) mbar_wait(&full[jj % kRaStages], (jj / kRaStages) & 1u);
-                }
-            }
-        }
-        if (!failed) on_chunk(r, (uint32_t)(a - r * g.vpr), ring + st * kRaChunk, (uint32_t)(b - a));
-        __syncthreads();  // stage st is consumed before it is refilled
-        if (!failed && threadIdx.x == 0 && issued < n) issue(issued++);
-        if (j == n0 - 1) seg_end(r, 0u, (uint32_t)(split - lo), failed);
-        else if (j == n - 1) seg_end(r, 1u, (uint32_t)(hi - split), failed);
-    }
-}
-
-// After thread 0 stored a segment's partial: adds the segment's vectors to
-// the row's counter; true in every thread when this segment completed the
-// row (the partial store ordered before the counter update, the folding
-// CTA's reads after it).
-__device__ __forceinline__ bool ring_arrive(unsigned* counter, uint32_t nv, uint32_t vpr, bool* flag) {
-    if (threadIdx.x == 0) {
-        __threadfence();
-        *flag = atomicAdd(counter, nv) + nv == vpr;
-    }
-    __syncthreads();
-    const bool last = *flag;
-    if (last) __threadfence();
-    return last;
-}
-
-// partial slot of CTA cc's segment in row r
-__device__ __forceinline__ uint64_t ra_slot(const RaGrid& g, uint64_t cc, uint64_t r) {
-    return 2 * cc + (ra_first(g, cc) / g.vpr == r ? 0 : 1);
-}
-
-__global__ void __launch_bounds__(kRaThreads, kRaCtasPerSm)
-    argmax_rows_ring(RowPlan p, int dst_dtype, RaGrid g, ChunkPartial* partials, unsigned* counters, uint32_t* fault) {
-    extern __shared__ __align__(128) float4 ring[];  // [kRaStages][kRaChunk]
-    __shared__ __align__(8) uint64_t full[kRaStages];
-    __shared__ GroupScratch<kRaThreads> s;
-    __shared__ bool last_flag;
-    const float nan = __int_as_float(0x7fc00000);
-    float bv[4] = {nan, nan, nan, nan};
-    uint32_t bc[4] = {0, 0, 0, 0};
-    ring_stream(
-        g, reinterpret_cast<const float4*>(p.src.ptr), ring, full, fault,
-        [&](uint64_t, uint32_t base, const float4* q4, uint32_t cnt) {
-            for (uint32_t v = threadIdx.x; v < cnt; v += kRaThreads) {
-                const float4 q = q4[v];
-                const float ql[4] = {q.x, q.y, q.z, q.w};
-#pragma unroll
-                for (int l = 0; l < 4; ++l) {
-                    const float nb = fmaxf(bv[l], ql[l]);
-                    if (nb != bv[l]) bc[l] = base + v;
-                    bv[l] = nb;
-                }
-            }
-        },
-        [&](uint64_t r, uint32_t k, uint32_t nv, bool failed) {
-            ArgBest bl[4];
-#pragma unroll
-            for (int l = 0; l < 4; ++l)
-                bl[l] = ArgBest{bv[l], (int64_t)(4ull * bc[l] + l), (failed || is_nan(bv[l])) ? 0u : 1u};
-            ArgBest best = arg_better(arg_better(bl[0], bl[1]), arg_better(bl[2], bl[3]));
-            best = group_argmax<kRaThreads>(best, &s);
-            if (threadIdx.x == 0) partials[2 * blockIdx.x + k] = ChunkPartial{best.v, best.has, best.i};
-            if (ring_arrive(&counters[r], nv, g.vpr, &last_flag)) {
-                // the row's fold: a maximum under the total order (value, then
-                // the smaller column), so the partials combine in any order
-                const uint64_t rbase = r * g.vpr;
-                const uint64_t cf = ra_owner(g, rbase), cl = ra_owner(g, rbase + g.vpr - 1);
-                ArgBest rb{0.0f, 0, 0};
-                for (uint64_t cc = cf + threadIdx.x; cc <= cl; cc += kRaThreads) {
-                    const ChunkPartial* q = partials + ra_slot(g, cc, r);
-                    rb = arg_better(rb, ArgBest{__ldcg(&q->v), __ldcg(&q->i), __ldcg(&q->has)});
-                }
-                rb = group_argmax<kRaThreads>(rb, &s);
-                if (threadIdx.x == 0) {
-                    const float* row = reinterpret_cast<const float*>(p.src.ptr) + rbase * 4;
-                    const int64_t idx = (is_nan(row[0]) || !rb.has) ? 0 : rb.i;
-                    const int64_t off = split_row_base(p.dst, r, p.ne[1], p.ne[2]);
-                    if (dst_dtype == (int)DType::I64) reinterpret_cast<int64_t*>(p.dst.ptr)[off] = idx;
-                    else if (dst_dtype == (int)DType::I32) reinterpret_cast<int32_t*>(p.dst.ptr)[off] = (int32_t)idx;
-                    else reinterpret_cast<float*>(p.dst.ptr)[off] = (float)idx;
-                    counters[r] = 0u;
-                }
-            }
-            __syncthreads();
-#pragma unroll
-            for (int l = 0; l < 4; ++l) {
-                bv[l] = nan;
-                bc[l] = 0;
-            }
-        });
-}
-
-// soft_max over few long dense rows in two launches.  Stats: the ring
-// pass keeps, per thread, a running maximum m and the f64 sum of
-// exp(v - m) over its values (rescaled by exp(m_old - m_new) when the
-// maximum grows); each segment combines its threads' (m, sum) pairs into a
-// partial, and the CTA completing a row combines the row's partials into
-// the maximum M and the denominator sum exp(v - M) (the rescaling factors
-// in binary64).  Apply: y = exp(v - M) / denominator over the whole tensor,
-// the source re-read from L2 -- one HBM read, one HBM write.  The
-// denominator differs from the reference's single f64 sum of the same
-// exponentials by the rounding of each term's rescaled exponential, a few
-// parts in 10^7, inside soft_max's 1e-5 bar.  A row whose maximum or sum is
-// not finite (a NaN, or an infinity) is computed whole, with the x86 NaN
-// rules, by the CTA that completed its stats; the apply pass skips it.
-struct RowInfo {
-    float max;
-    float den;
-    uint32_t exact;
-    uint32_t pad;
-};
-
-__device__ __forceinline__ float4 ra_scale4(float4 q, bool apply_scale, float scale) {
-    return apply_scale ? make_float4(__fmul_rn(q.x, scale), __fmul_rn(q.y, scale), __fmul_rn(q.z, scale),
-                                     __fmul_rn(q.w, scale))
-                       : q;
-}
-
-__device__ __forceinline__ float ra_group_max_nan(float m, GroupScratch<kRaThreads>* s) {
-#pragma unroll
-    for (int o = 16; o > 0; o >>= 1) m = max_nan(m, __shfl_xor_sync(0xffffffffu, m, o));
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0) s->f[threadIdx.x / 32] = m;
-    __syncthreads();
-    m = s->f[0];
-#pragma unroll
-    for (int w = 1; w < kRaThreads / 32; ++w) m = max_nan(m, s->f[w]);
-    return m;
-}
-
-// sum * exp(m - mx) in binary64 (0 for an empty sum)
-__device__ __forceinline__ double ra_rescale(double sum, float m, float mx) {
-    return sum == 0.0 ? 0.0 : sum * exp((double)m - (double)mx);
-}
-
-// The whole row with the reference's rules, by one CTA.
-__device__ void softmax_row_exact(const RowPlan& p, uint64_t r, bool apply_scale, float scale,
-                                  GroupScratch<kRaThreads>* s) {
-    SoftmaxRow w;
-    w.x = reinterpret_cast<const float*>(p.src.ptr) + r * p.ne[0];
-    w.y = reinterpret_cast<float*>(p.dst.ptr) + r * p.ne[0];
-    w.xs = 1;
-    w.ys = 1;
-    w.mbase = 0;
-    w.has_mask = false;
-    const uint64_t n = p.ne[0];
-    // element 0, then strictly greater values: a NaN is selected only at element 0
-    float em = bitsf(0x7fc00000u);
-    for (uint64_t c = threadIdx.x; c < n; c += kRaThreads) em = max_nn(em, value_at<true>(p, w, c, apply_scale, scale));
-    float gm = group_max<kRaThreads>(em, s);
-    const float v0 = value_at<true>(p, w, 0, apply_scale, scale);
-    if (is_nan(v0)) gm = v0;
-    double acc = 0.0;
-    for (uint64_t c = threadIdx.x; c < n; c += kRaThreads) {
-        const float e = lm_exp(f_sub(value_at<true>(p, w, c, apply_scale, scale), gm));
-        w.y[c] = e;
-        acc += (double)e;
-    }
-    const float denom = __double2float_rn(group_sum<kRaThreads>(acc, s));
-    for (uint64_t c = threadIdx.x; c < n; c += kRaThreads) w.y[c] = f_div(w.y[c], denom);
-}
-
-__global__ void __launch_bounds__(kRaThreads, kRaCtasPerSm)
-    softmax_rows_ring_stats(RowPlan p, bool apply_scale, float scale, RaGrid g, ChunkPartial* partials,
-                            unsigned* counters, RowInfo* info, uint32_t* fault) {
-    extern __shared__ __align__(128) float4 ring[];  // [kRaStages][kRaChunk]
-    __shared__ __align__(8) uint64_t full[kRaStages];
-    __shared__ GroupScratch<kRaThreads> s;
-    __shared__ bool last_flag;
-    float m = -INFINITY;  // this thread's running maximum
-    double sum = 0.0;     // sum of exp(v - m) over this thread's values
-    bool nan_seen = false;
-    ring_stream(
-        g, reinterpret_cast<const float4*>(p.src.ptr), ring, full, fault,
-        [&](uint64_t, uint32_t, const float4* q4, uint32_t cnt) {
-            for (uint32_t v = threadIdx.x; v < cnt; v += kRaThreads) {
-                const float4 q = ra_scale4(q4[v], apply_scale, scale);
-                const float mc = max_nan(max_nan(q.x, q.y), max_nan(q.z, q.w));
-                nan_seen |= is_nan(mc);
-                if (mc > m) {
-                    sum = ra_rescale(sum, m, mc);
-                    m = mc;
-                }
-                // v - m is NaN only for -inf - -inf (or a NaN, flagged above):
-                // the floor turns it into a zero term
-                sum += (double)softmax_exp(fmaxf(__fsub_rn(q.x, m), -200.0f));
-                sum += (double)softmax_exp(fmaxf(__fsub_rn(q.y, m), -200.0f));
-                sum += (double)softmax_exp(fmaxf(__fsub_rn(q.z, m), -200.0f));
-                sum += (double)softmax_exp(fmaxf(__fsub_rn(q.w, m), -200.0f));
-            }
-        },
-        [&](uint64_t r, uint32_t k, uint32_t nv, bool failed) {
-            // the segment's (maximum, sum at that maximum); has: 1, or 2 when
-            // a NaN was seen (the row goes to the exact pass), 0 after a fault
-            const float sm = ra_group_max_nan(m, &s);
-            const double ss = group_sum<kRaThreads>(ra_rescale(sum, m, sm), &s);
-            const bool seg_nan = __syncthreads_or(nan_seen);
-            if (threadIdx.x == 0) {
-                ChunkPartial q;
-                q.v = sm;
-                q.has = failed ? 0u : (seg_nan ? 2u : 1u);
-                q.i = __double_as_longlong(ss);
-                partials[2 * blockIdx.x + k] = q;
-            }
-            if (ring_arrive(&counters[r], nv, g.vpr, &last_flag)) {
-                const uint64_t rbase = r * g.vpr;
-                const uint64_t cf = ra_owner(g, rbase), cl = ra_owner(g, rbase + g.vpr - 1);
-                float rm = -INFINITY;
-                bool row_nan = false;
-                for (uint64_t cc = cf + threadIdx.x; cc <= cl; cc += kRaThreads) {
-                    rm = max_nan(rm, __ldcg(&partials[ra_slot(g, cc, r)].v));
-                    row_nan |= __ldcg(&partials[ra_slot(g, cc, r)].has) == 2u;
-                }
-                rm = ra_group_max_nan(rm, &s);
-                row_nan = __syncthreads_or(row_nan);
-                double rs = 0.0;  // each thread's share in CTA order, then the fixed tree
-                for (uint64_t cc = cf + threadIdx.x; cc <= cl; cc += kRaThreads) {
-                    const ChunkPartial* q = partials + ra_slot(g, cc, r);
-                    rs += ra_rescale(__longlong_as_double(__ldcg(&q->i)), __ldcg(&q->v), rm);
-                }
-                rs = group_sum<kRaThreads>(rs, &s);
-                const bool exact = row_nan || !isfinite(rm) || !isfinite(rs);
-                if (exact) softmax_row_exact(p, r, apply_scale, scale, &s);
-                if (threadIdx.x == 0) {
-                    info[r] = RowInfo{rm, __double2float_rn(rs), exact ? 1u : 0u, 0u};
-                    counters[r] = 0u;
-                }
-            }
-            __syncthreads();
-            m = -INFINITY;
-            sum = 0.0;
-            nan_seen = false;
-        });
-}
-
-constexpr int kRaApplyThreads = 256;
-
-__global__ void __launch_bounds__(kRaApplyThreads)
-    softmax_rows_ring_apply(RowPlan p, bool apply_scale, float scale, uint32_t nvec, FastDiv vpr,
-                            const RowInfo* info) {
-    pdl_enter();
-    const float4* x4 = reinterpret_cast<const float4*>(p.src.ptr);
-    float4* y4 = reinterpret_cast<float4*>(p.dst.ptr);
-    const uint32_t stride = gridDim.x * blockDim.x;
-    constexpr int U = 4;
-    for (uint32_t v0 = blockIdx.x * blockDim.x + threadIdx.x; v0 < nvec; v0 += U * stride) {
-        float4 q[U];
-#pragma unroll
-        for (int k = 0; k < U; ++k)
-            if (v0 + k * stride < nvec) q[k] = __ldcg(x4 + v0 + k * stride);
-#pragma unroll
-        for (int k = 0; k < U; ++k) {
-            const uint32_t v = v0 + k * stride;
-            if (v >= nvec) continue;
-            const RowInfo ri = info[fdiv(v, vpr)];
-            if (ri.exact) continue;
-            const float inv = __frcp_rn(ri.den);
-            const float4 z = ra_scale4(q[k], apply_scale, scale);
-            __stcs(y4 + v, make_float4(softmax_div(softmax_exp(__fsub_rn(z.x, ri.max)), ri.den, inv),
-                                       softmax_div(softmax_exp(__fsub_rn(z.y, ri.max)), ri.den, inv),
-                                       softmax_div(softmax_exp(__fsub_rn(z.z, ri.max)), ri.den, inv),
-                                       softmax_div(softmax_exp(__fsub_rn(z.w, ri.max)), ri.den, inv)));
-        }
-    }
-}
-
 uint64_t split_chunk(uint64_t ne0) {
     uint64_t c = (ne0 + kSplitCluster - 1) / kSplitCluster;
     return (c + 3) / 4 * 4;  // keeps every chunk's first column 16-byte aligned
@@ -767,40 +412,9 @@ bool split_rows_wanted(const LaunchEnv& env, const RowPlan& p) {
            !p.dst_ordinal;
 }
 
-namespace {
-
-// one dense, 16-byte aligned run of rows * ne0 floats (ne0 % 4 == 0)
-bool dense_run(const RowOperand& o, const uint64_t ne[4]) {
-    if ((reinterpret_cast<uintptr_t>(o.ptr) & 15u) != 0 || ne[0] % 4 != 0 || o.st[0] != 1) return false;
-    uint64_t want = ne[0];
-    for (int d = 1; d < 4; ++d) {
-        if (ne[d] > 1 && (uint64_t)o.st[d] != want) return false;
-        want *= ne[d];
-    }
-    return true;
-}
-
-}  // namespace
-
 cudaError_t launch_argmax_rows_split(const LaunchEnv& env, const RowPlan& p, int dst_dtype) {
     cudaError_t err;
-    if (dense_run(p.src, p.ne) && p.ne[0] / 4 <= 0xffffffffull) {
-        static_assert(2 * kRaCtasPerSm <= kSplitRowChunks, "two partial slots per CTA");
-        static DeviceFlags configured;
-        const size_t smem = (size_t)kRaStages * kRaChunk * 16;
-        if (!configured.done(env.device)) {
-            err = cudaFuncSetAttribute(argmax_rows_ring, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (err != cudaSuccess) return err;
-            configured.mark(env.device);
-        }
-        char* base = static_cast<char*>(env.workspace) + split_rows_workspace_offset(env.sm_count);
-        auto* partials = reinterpret_cast<ChunkPartial*>(base);
-        auto* counters = reinterpret_cast<unsigned*>(base + (uint64_t)env.sm_count * kSplitRowChunks * 16);
-        uint32_t* fault = reinterpret_cast<uint32_t*>(static_cast<char*>(env.workspace) + kFaultWordOffset);
-        const RaGrid g{p.rows * p.ne[0] / 4, (uint32_t)env.sm_count * kRaCtasPerSm, (uint32_t)(p.ne[0] / 4)};
-        err = launch_dependent(argmax_rows_ring, dim3(g.ctas), dim3(kRaThreads), smem, env.stream, p, dst_dtype, g,
-                               partials, counters, fault);
-    } else if (p.vec) {
+    if (p.vec) {
         static_assert(kSplitCluster == kSplitRowChunks, "workspace slots per row");
         char* base = static_cast<char*>(env.workspace) + split_rows_workspace_offset(env.sm_count);
         auto* partials = reinterpret_cast<ChunkPartial*>(base);
@@ -823,37 +437,10 @@ cudaError_t launch_sum_rows_split(const LaunchEnv& env, const RowPlan& p) {
 }
 
 cudaError_t launch_soft_max_split(const LaunchEnv& env, const RowPlan& p, bool apply_scale, float scale) {
-    cudaError_t err;
-    const uint64_t nvec = p.rows * p.ne[0] / 4;
-    if (dense_run(p.src, p.ne) && dense_run(p.dst, p.ne) && !(apply_scale && p.has_aux) && nvec < (1ull << 31)) {
-        static DeviceFlags configured;
-        const size_t smem = (size_t)kRaStages * kRaChunk * 16;
-        if (!configured.done(env.device)) {
-            err = cudaFuncSetAttribute(softmax_rows_ring_stats, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-            if (err != cudaSuccess) return err;
-            configured.mark(env.device);
-        }
-        char* base = static_cast<char*>(env.workspace) + split_rows_workspace_offset(env.sm_count);
-        auto* partials = reinterpret_cast<ChunkPartial*>(base);
-        auto* counters = reinterpret_cast<unsigned*>(base + (uint64_t)env.sm_count * kSplitRowChunks * 16);
-        auto* info = reinterpret_cast<RowInfo*>(base + split_rows_info_offset(env.sm_count));
-        uint32_t* fault = reinterpret_cast<uint32_t*>(static_cast<char*>(env.workspace) + kFaultWordOffset);
-        const RaGrid g{nvec, (uint32_t)env.sm_count * kRaCtasPerSm, (uint32_t)(p.ne[0] / 4)};
-        err = launch_dependent(softmax_rows_ring_stats, dim3(g.ctas), dim3(kRaThreads), smem, env.stream, p,
-                               apply_scale, scale, g, partials, counters, info, fault);
-        if (err == cudaSuccess) {
-            const uint64_t want = (nvec + kRaApplyThreads * 4 - 1) / (kRaApplyThreads * 4);
-            const uint64_t cap = (uint64_t)env.sm_count * 8;
-            err = launch_dependent(softmax_rows_ring_apply, dim3((unsigned)(want < cap ? want : cap)),
-                                   dim3(kRaApplyThreads), 0, env.stream, p, apply_scale, scale, (uint32_t)nvec,
-                                   make_fastdiv(g.vpr), static_cast<const RowInfo*>(info));
-        }
-        *env.launches += 2;
-    } else {
-        err = launch_dependent(softmax_rows_split, dim3((unsigned)(p.rows * kSplitCluster)), dim3(kSplitThreads), 0,
-                               env.stream, p, apply_scale, scale, split_chunk(p.ne[0]));
-        ++*env.launches;
-    }
+    const cudaError_t err = launch_dependent(softmax_rows_split, dim3((unsigned)(p.rows * kSplitCluster)),
+                                             dim3(kSplitThreads), 0, env.stream, p, apply_scale, scale,
+                                             split_chunk(p.ne[0]));
+    ++*env.launches;
     return err != cudaSuccess ? err : cudaGetLastError();
 }
 
