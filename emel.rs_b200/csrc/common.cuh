@@ -115,6 +115,7 @@ struct UnaryParams {
 // pinned bit for bit on the reference's golden vectors (single-query
 // attention's binary16 recurrence, RoPE frequencies, silu_back).
 __device__ __forceinline__ float lm_exp(float x) { return x86_nan1(exp32(x), x); }
+__device__ __forceinline__ float lm_exp_gate(float x) { return x86_nan1(exp32_gate(x), x); }
 __device__ __forceinline__ float lm_expm1(float x) { return x86_nan1(expm1_32(x), x); }
 __device__ __forceinline__ float lm_tanh(float x) { return x86_nan1(tanh32(x), x); }
 __device__ __forceinline__ float lm_exp_cr(float x) { return x86_nan1(fast_expf(x), x); }
@@ -137,6 +138,47 @@ __device__ __forceinline__ float softmax_exp(float z) {
     return __fmaf_rn(r, __fmul_rn(lo, kLn2), r);
 }
 
+// Packed binary32 pairs.  sm_100a executes add / mul / fma on two binary32
+// lanes in one instruction (__fadd2_rn, __fmul2_rn, __ffma2_rn), each lane
+// rounded exactly like the scalar operation, so the pair forms below give
+// the scalar forms' bits at half the instruction count.  x - y is written
+// x + (-y), which IEEE 754 defines it to be.
+__device__ __forceinline__ float2 lo2(float4 v) { return make_float2(v.x, v.y); }
+__device__ __forceinline__ float2 hi2(float4 v) { return make_float2(v.z, v.w); }
+__device__ __forceinline__ float4 cat2(float2 a, float2 b) { return make_float4(a.x, a.y, b.x, b.y); }
+__device__ __forceinline__ float2 splat2(float x) { return make_float2(x, x); }
+
+// Three-operand maximum / minimum (sm_100a): fmaxf / fminf of three values,
+// NaN operands skipped the same way.
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+    float d;
+    asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+__device__ __forceinline__ float fmin3(float a, float b, float c) {
+    float d;
+    asm("min.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+    return d;
+}
+
+// exp(z) for a pair of soft_max terms with -41 <= z <= 0 (the callers test
+// the range; NaN and anything below go to softmax_exp): Cody-Waite reduction
+// against base 2, hi = RN(z log2 e), lo = z - hi ln2 with ln2 split in two
+// binary32 constants (two FMAs, each rounding once at |lo| < 2^-17), then
+// exp(z) = 2^hi e^lo = ex2(hi) (1 + lo), the dropped lo^2 / 2 below 2^-35.
+// The error is the SFU's ex2 (a few units of 2^-24), the bar softmax_exp
+// is held to.
+__device__ __forceinline__ float2 softmax_exp2(float2 z) {
+    constexpr float kLog2e = 0x1.715476p0f, kLn2Hi = 0x1.62e43p-1f, kLn2Lo = -0x1.05c610p-29f;
+    const float2 hi = __fmul2_rn(z, splat2(kLog2e));
+    float2 lo = __ffma2_rn(hi, splat2(-kLn2Hi), z);
+    lo = __ffma2_rn(hi, splat2(-kLn2Lo), lo);
+    float2 r;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r.x) : "f"(hi.x));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r.y) : "f"(hi.y));
+    return __ffma2_rn(r, lo, r);
+}
+
 // e / d rounded once for 0 <= e <= 1 and a finite d >= 1, given
 // inv = RN(1 / d): q0 = RN(e * inv) is within one ulp of e / d, the FMA
 // residual e - d * q0 is exact, and RN(q0 + residual * inv) is the
@@ -146,6 +188,12 @@ __device__ __forceinline__ float softmax_exp(float z) {
 __device__ __forceinline__ float markstein_div(float e, float d, float inv) {
     const float q0 = __fmul_rn(e, inv);
     return __fmaf_rn(__fmaf_rn(-d, q0, e), inv, q0);
+}
+
+// markstein_div on a pair (same bits per lane), d2 = (d, d), inv2 = (inv, inv).
+__device__ __forceinline__ float2 markstein_div2(float2 e, float2 d2, float2 inv2) {
+    const float2 q0 = __fmul2_rn(e, inv2);
+    return __ffma2_rn(__ffma2_rn(make_float2(-d2.x, -d2.y), q0, e), inv2, q0);
 }
 
 // a / b inside the transcendental formulas (sigmoid, silu and the GLU
@@ -166,6 +214,18 @@ __device__ __forceinline__ float div_refined(float a, float b) {
     const float q = __fmaf_rn(r, y, q0);
     // a zero quotient keeps q0's sign (-0 / 2 = -0: the residual step would add +0)
     return r != r ? q0 : copysignf(q, q0);
+}
+
+// div_refined on a pair: the same operations lane for lane, the multiply and
+// the two FMAs packed.
+__device__ __forceinline__ float2 div_refined2(float2 a, float2 b) {
+    float2 y;
+    asm("rcp.approx.f32 %0, %1;" : "=f"(y.x) : "f"(b.x));
+    asm("rcp.approx.f32 %0, %1;" : "=f"(y.y) : "f"(b.y));
+    const float2 q0 = __fmul2_rn(a, y);
+    const float2 r = __ffma2_rn(make_float2(-b.x, -b.y), q0, a);
+    const float2 q = __ffma2_rn(r, y, q0);
+    return make_float2(r.x != r.x ? q0.x : copysignf(q.x, q0.x), r.y != r.y ? q0.y : copysignf(q.y, q0.y));
 }
 
 __device__ __forceinline__ float softmax_div(float e, float d, float inv) {
@@ -221,6 +281,8 @@ struct Arith {
     // division inside a transcendental formula (a few ulp allowed)
     static __device__ __forceinline__ float tdiv(float a, float b) { return EXACT ? f_div(a, b) : div_refined(a, b); }
     static __device__ __forceinline__ float exp(float x) { return EXACT ? lm_exp(x) : exp32(x); }
+    // exp inside a gate 1 + exp(x) (exp32_gate)
+    static __device__ __forceinline__ float exp_gate(float x) { return EXACT ? lm_exp_gate(x) : exp32_gate(x); }
     static __device__ __forceinline__ float expm1(float x) { return EXACT ? lm_expm1(x) : expm1_32(x); }
     static __device__ __forceinline__ float tanh(float x) { return EXACT ? lm_tanh(x) : tanh32(x); }
     // the standalone tanh op (unary.rs OpUnary Tanh): correctly rounded
@@ -248,6 +310,7 @@ struct Arith<kHalf> {
     static __device__ __forceinline__ float div(float a, float b) { return __fdividef(a, b); }
     static __device__ __forceinline__ float tdiv(float a, float b) { return __fdividef(a, b); }
     static __device__ __forceinline__ float exp(float x) { return __expf(x); }
+    static __device__ __forceinline__ float exp_gate(float x) { return __expf(x); }
     static __device__ __forceinline__ float expm1(float x) { return expm1_32(x); }
     static __device__ __forceinline__ float tanh(float x) {
         const float ay = fabsf(x);
@@ -285,7 +348,7 @@ __device__ __forceinline__ float unary_formula(float v, UnaryParams p) {
     if constexpr (OP == kTanh) return A::tanh_op(v);
     if constexpr (OP == kElu) return v >= 0.0f ? v : A::expm1(v);
     if constexpr (OP == kRelu) return v > 0.0f ? v : 0.0f;
-    if constexpr (OP == kSigmoid) return A::tdiv(1.0f, A::add(1.0f, A::exp(f_neg(v))));
+    if constexpr (OP == kSigmoid) return A::tdiv(1.0f, A::add(1.0f, A::exp_gate(f_neg(v))));
     if constexpr (OP == kGelu) {
         if (v <= -10.0f) return 0.0f;
         if (v >= 10.0f) return v;
@@ -306,7 +369,7 @@ __device__ __forceinline__ float unary_formula(float v, UnaryParams p) {
         const float inner = A::mul(A::mul(0.7978846f, v), A::add(1.0f, A::mul(A::mul(0.044715f, v), v)));
         return A::mul(A::mul(0.5f, v), A::add(1.0f, A::tanh(inner)));
     }
-    if constexpr (OP == kSilu) return A::tdiv(v, A::add(1.0f, A::exp(f_neg(v))));
+    if constexpr (OP == kSilu) return A::tdiv(v, A::add(1.0f, A::exp_gate(f_neg(v))));
     if constexpr (OP == kHardswish) return A::div(A::mul(v, A::clamp(A::add(v, 3.0f), 0.0f, 6.0f)), 6.0f);
     if constexpr (OP == kHardsigmoid) return A::div(A::clamp(A::add(v, 3.0f), 0.0f, 6.0f), 6.0f);
     if constexpr (OP == kExp) return A::exp(v);
@@ -338,6 +401,43 @@ __device__ __forceinline__ float unary_formula(float v, UnaryParams p) {
     if constexpr (OP == kLeakyRelu) return is_nan(v) ? v : (v < 0.0f ? f_mul(v, p.a) : v);
     if constexpr (OP == kAdd1) return f_add(v, p.a);
     if constexpr (OP == kCopy) return v;
+    return v;
+}
+
+// Pair forms of heavy formulas on binary32 storage: the fast pass of
+// unary_formula (kFast policy; GELU's kHalf) on two elements, lane for lane
+// the scalar formula's operations with the binary32 multiplies, adds and
+// FMAs packed two to an instruction (exp32x2, div_refined2), so each lane
+// has the scalar pass's bits.  CUDA's own intrinsics (__expf, __fdividef)
+// are still called per lane.
+template <int OP>
+constexpr bool kPairFormula = OP == kSilu || OP == kSigmoid || OP == kExp || OP == kGelu;
+
+template <int OP>
+__device__ __forceinline__ float2 unary_formula2(float2 v) {
+    if constexpr (OP == kExp) return exp32x2(v);
+    if constexpr (OP == kSilu || OP == kSigmoid) {
+        const float2 d = __fadd2_rn(splat2(1.0f), exp32x2<true>(make_float2(f_neg(v.x), f_neg(v.y))));
+        return div_refined2(OP == kSilu ? v : splat2(1.0f), d);
+    }
+    if constexpr (OP == kGelu) {
+        // unary_formula<kGelu, kHalf>: q = v through binary16, the tanh
+        // approximation, the result through binary16, +-10 clamps last
+        const float2 q = __half22float2(__floats2half2_rn(v.x, v.y));
+        const float2 cube = __fmul2_rn(__fmul2_rn(__fmul2_rn(splat2(0.044715f), q), q), q);
+        const float2 inner = __fmul2_rn(splat2(0.7978846f), __fadd2_rn(q, cube));
+        const float2 ay = make_float2(fabsf(inner.x), fabsf(inner.y));
+        const float2 d = __fadd2_rn(make_float2(__expf(__fmul_rn(2.0f, ay.x)), __expf(__fmul_rn(2.0f, ay.y))),
+                                    splat2(1.0f));
+        const float2 t = __fadd2_rn(splat2(1.0f), make_float2(-__fdividef(2.0f, d.x), -__fdividef(2.0f, d.y)));
+        const float rx = ay.x >= 10.0f ? 1.0f : t.x, ry = ay.y >= 10.0f ? 1.0f : t.y;
+        const float2 th = make_float2(inner.x == 0.0f ? inner.x : (inner.x < 0.0f ? -rx : rx),
+                                      inner.y == 0.0f ? inner.y : (inner.y < 0.0f ? -ry : ry));
+        const float2 g = __fmul2_rn(__fmul2_rn(splat2(0.5f), q), __fadd2_rn(splat2(1.0f), th));
+        const float2 o = __half22float2(__floats2half2_rn(g.x, g.y));
+        return make_float2(v.x <= -10.0f ? 0.0f : (v.x >= 10.0f ? v.x : o.x),
+                           v.y <= -10.0f ? 0.0f : (v.y >= 10.0f ? v.y : o.y));
+    }
     return v;
 }
 
@@ -378,7 +478,7 @@ __device__ __forceinline__ float unary_apply(float v, UnaryParams p) {
 template <int MODE>
 __device__ __forceinline__ float glu_silu(float v) {
     using A = Arith<MODE>;
-    return A::tdiv(v, A::add(1.0f, A::exp(f_neg(v))));
+    return A::tdiv(v, A::add(1.0f, A::exp_gate(f_neg(v))));
 }
 
 template <int SUB, int MODE>
@@ -394,7 +494,31 @@ __device__ __forceinline__ float glu_formula(float value, float g) {
     }
     if constexpr (SUB == kGeGluErf) return A::mul(value, unary_formula<kGeluErf, MODE>(g, UnaryParams{}));
     // kGeGluQuick: value * (1 / (1 + exp(-1.702 * g)))
-    return A::mul(value, A::tdiv(1.0f, A::add(1.0f, A::exp(A::mul(-1.702f, g)))));
+    return A::mul(value, A::tdiv(1.0f, A::add(1.0f, A::exp_gate(A::mul(-1.702f, g)))));
+}
+
+// Pair forms of the exp-based gates (kFast policy), lane for lane the
+// scalar glu_formula's operations with the binary32 ones packed.
+template <int SUB>
+constexpr bool kGluPairFormula = SUB == kSwiGlu || SUB == kSwiGluOai || SUB == kGeGluQuick;
+
+__device__ __forceinline__ float2 glu_silu2(float2 v) {
+    return div_refined2(v, __fadd2_rn(splat2(1.0f), exp32x2<true>(make_float2(f_neg(v.x), f_neg(v.y)))));
+}
+
+template <int SUB>
+__device__ __forceinline__ float2 glu_formula2(float2 value, float2 g) {
+    if constexpr (SUB == kSwiGlu) return __fmul2_rn(value, glu_silu2(g));
+    if constexpr (SUB == kSwiGluOai) {
+        const float2 gate = make_float2(g.x < 7.0f ? g.x : 7.0f, g.y < 7.0f ? g.y : 7.0f);
+        const float2 v = make_float2(value.x < 7.0f ? value.x : 7.0f, value.y < 7.0f ? value.y : 7.0f);
+        const float2 s = glu_silu2(__fmul2_rn(splat2(1.702f), gate));
+        return __fmul2_rn(make_float2(__fdiv_rn(s.x, 1.702f), __fdiv_rn(s.y, 1.702f)), __fadd2_rn(v, splat2(1.0f)));
+    }
+    if constexpr (SUB == kGeGluQuick)
+        return __fmul2_rn(value, div_refined2(splat2(1.0f), __fadd2_rn(splat2(1.0f),
+                                                                     exp32x2<true>(__fmul2_rn(splat2(-1.702f), g)))));
+    return value;
 }
 
 template <int SUB>

@@ -50,6 +50,9 @@ struct UnaryFn {
         if constexpr (kHeavy) return unary_formula<OP, (IN_F16 || OP == kGelu) ? kHalf : kFast, IN_F16>(a, p);
         else return unary_apply<OP, IN_F16>(a, p);
     }
+    // fast() on two binary32 elements at once (same bits per lane)
+    static constexpr bool kPair = !IN_F16 && kPairFormula<OP>;
+    __device__ __forceinline__ float2 fast2(float2 a, float2) const { return unary_formula2<OP>(a); }
     // binary16 ops computed on two packed lanes, bit for bit the reference's
     // f16 -> f32 -> op -> f16 for NaN-free inputs: sign-bit operations, the
     // signed 16-bit compare (positive binary16 values are exactly the lanes
@@ -114,6 +117,9 @@ struct GluFn {
         if constexpr (kHeavy) return glu_formula<SUB, kFast>(value, g);
         else return glu_apply<SUB>(value, g);
     }
+    // fast() on two (value, gate) pairs at once (same bits per lane)
+    static constexpr bool kPair = kGluPairFormula<SUB>;
+    __device__ __forceinline__ float2 fast2(float2 value, float2 g) const { return glu_formula2<SUB>(value, g); }
 };
 
 // Per-lane path (binary16 vectors with a NaN in or out take it rarely; f32
@@ -126,20 +132,39 @@ __device__ __noinline__ Vec16<T> apply_vec_lanes(const F& f, const Vec16<T>& a, 
     return r;
 }
 
+// Functors with a pair form of their fast pass (kPair, fast2).
+template <typename F, typename = void>
+struct PairOp : std::false_type {};
+template <typename F>
+struct PairOp<F, std::void_t<decltype(F::kPair)>> : std::bool_constant<F::kPair> {};
+
 template <typename T, typename F>
 __device__ __forceinline__ Vec16<T> apply_vec_scalar(const F& f, const Vec16<T>& a, const Vec16<T>& b) {
     if constexpr (sizeof(T) == 2) {
         return apply_vec_lanes<T>(f, a, b);
     } else if constexpr (F::kHeavy) {
-        // fast pass on every lane; a vector with a NaN result is redone lane
-        // by lane with the exact recompute (one out-of-line call site)
+        // fast pass on every lane (in pairs where the formula has a pair
+        // form); a vector with a NaN result is redone lane by lane with the
+        // exact recompute (one out-of-line call site)
         Vec16<T> r;
         bool nan_out = false;
+        if constexpr (PairOp<F>::value) {
 #pragma unroll
-        for (int k = 0; k < Vec16<T>::N; ++k) {
-            const float v = f.fast(vget(a, k), F::kBinary ? vget(b, k) : 0.0f);
-            nan_out |= is_nan(v);
-            vset(r, k, v);
+            for (int k = 0; k < Vec16<T>::N; k += 2) {
+                const float2 x = make_float2(vget(a, k), vget(a, k + 1));
+                const float2 y = F::kBinary ? make_float2(vget(b, k), vget(b, k + 1)) : make_float2(0.0f, 0.0f);
+                const float2 v = f.fast2(x, y);
+                nan_out |= is_nan(v.x) | is_nan(v.y);
+                vset(r, k, v.x);
+                vset(r, k + 1, v.y);
+            }
+        } else {
+#pragma unroll
+            for (int k = 0; k < Vec16<T>::N; ++k) {
+                const float v = f.fast(vget(a, k), F::kBinary ? vget(b, k) : 0.0f);
+                nan_out |= is_nan(v);
+                vset(r, k, v);
+            }
         }
         if (nan_out) return apply_vec_lanes<T>(f, a, b);
         return r;

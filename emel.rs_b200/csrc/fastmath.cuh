@@ -313,4 +313,43 @@ EMEL_HD float tanh32(float y) {
     return y == 0.0f ? y : r;
 }
 
+// exp(x) inside a gate 1 + exp(x) (sigmoid, silu and the GLU gates, whose
+// quotient is then taken).  From x > 15.9 on exp(x) >= 2^23, where the sum
+// 1 + exp(x) rounds and a one-ulp difference in exp(x) can become several
+// ulp of the quotient; there the correctly rounded binary64 evaluation is
+// used, so the gate is the correctly rounded formula's.  Below, exp32.
+constexpr float kExpGateCr = 15.9f;
+EMEL_HD float exp32_gate(float x) { return x > kExpGateCr ? fast_expf(x) : exp32(x); }
+
+#if defined(__CUDACC__)
+// exp32 (GATE: exp32_gate) on a pair of arguments.  When both lie in the
+// one-scale packed range the two lanes run exp32's operations packed two to
+// an instruction (__ffma2_rn / __fadd2_rn / __fmul2_rn round each lane
+// exactly like the scalar operation), so each lane gets the scalar bits at
+// about half the instructions; otherwise each lane calls the scalar form.
+template <bool GATE = false>
+__device__ __forceinline__ float2 exp32x2(float2 x) {
+    constexpr float kTop = GATE ? kExpGateCr : 88.72f;
+    if (!(x.x >= -86.0f && x.x <= kTop && x.y >= -86.0f && x.y <= kTop))
+        return GATE ? make_float2(exp32_gate(x.x), exp32_gate(x.y)) : make_float2(exp32(x.x), exp32(x.y));
+    constexpr float kShift = 0x1.8p23f;
+    auto sp = [](float v) { return make_float2(v, v); };
+    const float2 tk = __ffma2_rn(x, sp(kF32InvLn2), sp(kShift));
+    const float2 kd = __fadd2_rn(tk, sp(-kShift));  // exact
+    const float2 nkd = make_float2(-kd.x, -kd.y);
+    const float2 r = __ffma2_rn(nkd, sp(kF32Ln2Hi), x);
+    const float2 c = __fmul2_rn(nkd, sp(kF32Ln2Lo));
+    float2 q = __ffma2_rn(r, sp(kF32InvFact7), sp(kF32InvFact6));
+    q = __ffma2_rn(q, r, sp(kF32InvFact5));
+    q = __ffma2_rn(q, r, sp(kF32InvFact4));
+    q = __ffma2_rn(q, r, sp(kF32InvFact3));
+    q = __ffma2_rn(q, r, sp(kF32InvFact2));
+    const float2 t = __ffma2_rn(c, r, __ffma2_rn(__fmul2_rn(r, r), q, c));
+    // 2^(k - 1) with k = bits(tk) - bits(kShift), as in exp32
+    const uint32_t kb = f32_to_bits(kShift) - 126u;
+    const float2 sh = make_float2(bits_to_f32((f32_to_bits(tk.x) - kb) << 23), bits_to_f32((f32_to_bits(tk.y) - kb) << 23));
+    return __fmul2_rn(__ffma2_rn(sh, __fadd2_rn(r, t), sh), sp(2.0f));
+}
+#endif
+
 }  // namespace emel

@@ -203,7 +203,8 @@ __device__ __forceinline__ float4 sm_operand4(const RingArgs& a, const float* ro
                                               int64_t moff, uint32_t v) {
     float4 x = ld_f4(row + 4 * v);
     if constexpr (MODE == kSmPlain) return x;
-    x = make_float4(__fmul_rn(x.x, a.param), __fmul_rn(x.y, a.param), __fmul_rn(x.z, a.param), __fmul_rn(x.w, a.param));
+    const float2 s2 = make_float2(a.param, a.param);
+    x = cat2(__fmul2_rn(lo2(x), s2), __fmul2_rn(hi2(x), s2));
     if constexpr (MODE == kSmScale) return x;
     float4 mk;
     if constexpr (MODE == kSmMaskF16) {
@@ -216,15 +217,20 @@ __device__ __forceinline__ float4 sm_operand4(const RingArgs& a, const float* ro
     } else {
         mk = mask4(a, stage, moff, v);
     }
-    return make_float4(__fadd_rn(x.x, mk.x), __fadd_rn(x.y, mk.y), __fadd_rn(x.z, mk.z), __fadd_rn(x.w, mk.w));
+    return cat2(__fadd2_rn(lo2(x), lo2(mk)), __fadd2_rn(hi2(x), hi2(mk)));
 }
 
-// Maximum, exps and their f64 sum for the thread's R vectors (kept in sv);
-// zmin = the smallest v - max seen (for the division's range check).
-// GUARD: the row does not fill all R * T vector slots.
+// Maximum, exps and their sum for the thread's R vectors (kept in sv).  A
+// vector whose four v - max are all >= kSoftmaxPlainDivFloor takes the
+// packed exponential (softmax_exp2); any other vector (a masked -inf, a
+// tiny or NaN term) takes the scalar softmax_exp and sets its bit in
+// *slow, which routes its division through the range-checked softmax_div.
+// The thread's terms (at most 32, each <= 1) are summed in binary32 pairs,
+// then the thread sums meet in binary64.  GUARD: the row does not fill all
+// R * T vector slots.
 template <int T, int R, int MODE, bool GUARD>
 __device__ __forceinline__ double sm_exp_pass(const RingArgs& a, const float* row, const unsigned char* stage,
-                                              int64_t moff, uint32_t nvec, float4 (&sv)[R], float& zmin,
+                                              int64_t moff, uint32_t nvec, float4 (&sv)[R], uint32_t* slow,
                                               GroupScratch<T>* red) {
     float m = -INFINITY;
 #pragma unroll
@@ -232,49 +238,46 @@ __device__ __forceinline__ double sm_exp_pass(const RingArgs& a, const float* ro
         const uint32_t v = threadIdx.x + (uint32_t)(i * T);
         if (!GUARD || v < nvec) {
             sv[i] = sm_operand4<MODE>(a, row, stage, moff, v);
-            m = fmaxf(m, fmaxf(fmaxf(sv[i].x, sv[i].y), fmaxf(sv[i].z, sv[i].w)));
+            m = fmax3(fmax3(m, sv[i].x, sv[i].y), sv[i].z, sv[i].w);
         }
     }
     m = row_max_fast<T>(m, red);
-    double acc = 0.0;
-    float zl = 0.0f;
+    const float2 nm2 = make_float2(-m, -m);  // x + (-m) is IEEE x - m
+    float2 acc2 = make_float2(0.0f, 0.0f);
+    uint32_t bits = 0;
 #pragma unroll
     for (int i = 0; i < R; ++i) {
         const uint32_t v = threadIdx.x + (uint32_t)(i * T);
         if (!GUARD || v < nvec) {
-            const float4 z = make_float4(__fsub_rn(sv[i].x, m), __fsub_rn(sv[i].y, m), __fsub_rn(sv[i].z, m),
-                                         __fsub_rn(sv[i].w, m));
-            zl = fminf(zl, fminf(fminf(z.x, z.y), fminf(z.z, z.w)));
-            sv[i] = make_float4(softmax_exp(z.x), softmax_exp(z.y), softmax_exp(z.z), softmax_exp(z.w));
-            acc += (double)sv[i].x;
-            acc += (double)sv[i].y;
-            acc += (double)sv[i].z;
-            acc += (double)sv[i].w;
+            const float2 zl = __fadd2_rn(lo2(sv[i]), nm2), zh = __fadd2_rn(hi2(sv[i]), nm2);
+            if (fmin3(fminf(zl.x, zl.y), zh.x, zh.y) >= kSoftmaxPlainDivFloor) {
+                sv[i] = cat2(softmax_exp2(zl), softmax_exp2(zh));
+            } else {
+                sv[i] = make_float4(softmax_exp(zl.x), softmax_exp(zl.y), softmax_exp(zh.x), softmax_exp(zh.y));
+                bits |= 1u << i;
+            }
+            acc2 = __fadd2_rn(acc2, lo2(sv[i]));
+            acc2 = __fadd2_rn(acc2, hi2(sv[i]));
         }
     }
-    zmin = zl;
-    return row_sum_fast<T>(acc, red);
+    *slow = bits;
+    return row_sum_fast<T>((double)acc2.x + (double)acc2.y, red);
 }
 
-// e / denom for the thread's vectors: without range checks when the
-// thread's smallest v - max is at least kSoftmaxPlainDivFloor.
+// e / denom for the thread's vectors: the packed Markstein quotient for the
+// vectors whose terms are all >= e^kSoftmaxPlainDivFloor, the range-checked
+// scalar form for the vectors flagged in slow.
 template <int OP, int T, int R, bool GUARD>
 __device__ __forceinline__ void sm_div_pass(const RingArgs& a, float* drow, uint32_t nvec, const float4 (&sv)[R],
-                                            float denom, float inv, bool careful) {
-    if (!careful) {
+                                            float denom, float inv, uint32_t slow) {
+    const float2 d2 = make_float2(denom, denom), i2 = make_float2(inv, inv);
 #pragma unroll
-        for (int i = 0; i < R; ++i) {
-            const uint32_t v = threadIdx.x + (uint32_t)(i * T);
-            if (!GUARD || v < nvec)
-                store4<OP>(a, drow, v,
-                           make_float4(markstein_div(sv[i].x, denom, inv), markstein_div(sv[i].y, denom, inv),
-                                       markstein_div(sv[i].z, denom, inv), markstein_div(sv[i].w, denom, inv)));
-        }
-    } else {
-#pragma unroll
-        for (int i = 0; i < R; ++i) {
-            const uint32_t v = threadIdx.x + (uint32_t)(i * T);
-            if (!GUARD || v < nvec)
+    for (int i = 0; i < R; ++i) {
+        const uint32_t v = threadIdx.x + (uint32_t)(i * T);
+        if (!GUARD || v < nvec) {
+            if (!(slow >> i & 1u))
+                store4<OP>(a, drow, v, cat2(markstein_div2(lo2(sv[i]), d2, i2), markstein_div2(hi2(sv[i]), d2, i2)));
+            else
                 store4<OP>(a, drow, v,
                            make_float4(softmax_div(sv[i].x, denom, inv), softmax_div(sv[i].y, denom, inv),
                                        softmax_div(sv[i].z, denom, inv), softmax_div(sv[i].w, denom, inv)));
@@ -420,10 +423,10 @@ __global__ void __launch_bounds__(T, R >= 8 ? 2 : (R >= 4 ? 3 : 1024 / T)) row_r
                 // row whose sum comes back non-finite is redone exactly
                 // below from the untouched stage.
                 float4 sv[R];
-                float zmin;
+                uint32_t slow;
                 const bool guard = nvec != (uint32_t)(R * T);
-                const double acc = guard ? sm_exp_pass<T, R, MODE, true>(a, row, stage, moff, nvec, sv, zmin, &red)
-                                         : sm_exp_pass<T, R, MODE, false>(a, row, stage, moff, nvec, sv, zmin, &red);
+                const double acc = guard ? sm_exp_pass<T, R, MODE, true>(a, row, stage, moff, nvec, sv, &slow, &red)
+                                         : sm_exp_pass<T, R, MODE, false>(a, row, stage, moff, nvec, sv, &slow, &red);
                 if (isfinite(acc)) {
                     // every thread has finished reading the stage: refill it now
                     if (tid == 0 && k + (uint32_t)S < mine) {
@@ -432,9 +435,8 @@ __global__ void __launch_bounds__(T, R >= 8 ? 2 : (R >= 4 ? 3 : 1024 / T)) row_r
                     }
                     const float denom = __double2float_rn(acc);  // >= 1: the maximum contributes exp(0)
                     const float inv = __frcp_rn(denom);
-                    const bool careful = !(zmin >= kSoftmaxPlainDivFloor);
-                    if (guard) sm_div_pass<OP, T, R, true>(a, drow, nvec, sv, denom, inv, careful);
-                    else sm_div_pass<OP, T, R, false>(a, drow, nvec, sv, denom, inv, careful);
+                    if (guard) sm_div_pass<OP, T, R, true>(a, drow, nvec, sv, denom, inv, slow);
+                    else sm_div_pass<OP, T, R, false>(a, drow, nvec, sv, denom, inv, slow);
                     continue;
                 }
             }

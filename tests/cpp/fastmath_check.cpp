@@ -110,7 +110,48 @@ static void gelu_steps() {
     std::printf("%d %d\n", inputs, worst);
 }
 
+// "gate <stride>": sigmoid 1 / (1 + e) and silu x / (1 + e) with e the
+// device's gate exponential (exp32_gate(-x)) against the same formulas on
+// binary64 exp rounded once, every stride-th binary32 input plus every input
+// of the band -x in [15, 104] where 1 + e rounds; prints
+// "n max_ulp_sigmoid max_ulp_silu".
+static void gate_sweep(unsigned stride) {
+    long n = 0;
+    long long worst[2] = {0, 0};
+    auto one = [&](float x) {
+        if (std::isnan(x)) return;
+        ++n;
+        const float e = emel::exp32_gate(-x), ec = (float)std::exp(-(double)x);
+        const float got[2] = {1.0f / (1.0f + e), x / (1.0f + e)};
+        const float want[2] = {1.0f / (1.0f + ec), x / (1.0f + ec)};
+        for (int k = 0; k < 2; ++k) {
+            if (std::isnan(got[k]) || std::isnan(want[k])) {
+                if (std::isnan(got[k]) != std::isnan(want[k])) worst[k] = LLONG_MAX;
+                continue;
+            }
+            const long long d = std::llabs(ord(got[k]) - ord(want[k]));
+            if (d > worst[k]) worst[k] = d;
+        }
+    };
+    for (unsigned long long u = 0; u < (1ull << 32); u += stride) {
+        const unsigned b = (unsigned)u;
+        float x;
+        std::memcpy(&x, &b, 4);
+        one(x);
+    }
+    for (unsigned b = 0xc1700000u; b <= 0xc2d00000u; ++b) {  // -15 .. -104
+        float x;
+        std::memcpy(&x, &b, 4);
+        one(x);
+    }
+    std::printf("%ld %lld %lld\n", n, worst[0], worst[1]);
+}
+
 int main(int argc, char** argv) {
+    if (argc > 1 && std::string(argv[1]) == "gate") {
+        gate_sweep(argc > 2 ? (unsigned)std::strtoul(argv[2], nullptr, 10) : 61u);
+        return 0;
+    }
     if (argc > 1 && std::string(argv[1]) == "b32") {
         b32_sweep(argc > 2 ? (unsigned)std::strtoul(argv[2], nullptr, 10) : 61u);
         return 0;

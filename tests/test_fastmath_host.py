@@ -53,3 +53,15 @@ def test_gelu_on_the_binary32_tanh_within_one_binary16_step(tmp_path):
     exe = build_checker(tmp_path)
     inputs, worst = map(int, subprocess.run([str(exe), "gelu"], capture_output=True, text=True, check=True).stdout.split())
     assert inputs == 65536 - 2046 and worst <= 1, (inputs, worst)
+
+
+def test_gate_exponential_keeps_sigmoid_and_silu_within_two_ulp(tmp_path):
+    """sigmoid and silu on the gate exponential (exp32, and the correctly
+    rounded binary64 exp where 1 + exp(-x) rounds) against the same formulas
+    on binary64 exp rounded once: a strided sweep of all binary32 inputs plus
+    every input of the band x in [-104, -15]."""
+    exe = build_checker(tmp_path)
+    n, u_sig, u_silu = map(int, subprocess.run([str(exe), "gate", "131"], capture_output=True, text=True,
+                                               check=True).stdout.split())
+    assert n > 40_000_000
+    assert u_sig <= 2 and u_silu <= 2, (u_sig, u_silu)
