@@ -234,26 +234,53 @@ __device__ __forceinline__ Vec16<T> apply_vec(const F& f, const Vec16<T>& a, con
 // I: the index type -- 32-bit when the vector count and the grid stride
 // leave headroom below 2^31 (every realistic tensor), which keeps the loop's
 // registers low enough for eight CTAs per SM on the cheap ops.
+//
+// early: the inputs do not overlap anything the previous kernel on the
+// stream writes (the host's stream record), so each thread issues its first
+// batch of loads before waiting for that kernel (pdl_enter); stores always
+// come after the wait.  Under programmatic dependent launch the CTAs start
+// while the previous kernel drains, and these loads overlap its tail.
+template <typename T, typename F, typename I>
+__device__ __forceinline__ void flat_load(const T* __restrict__ a, const T* __restrict__ b, I at, I stride,
+                                          Vec16<T> (&a0)[F::kUnroll], Vec16<T> (&b0)[F::kUnroll]) {
+#pragma unroll
+    for (int k = 0; k < F::kUnroll; ++k) {
+        a0[k] = ld_stream(a + (uint64_t)(at + k * stride) * Vec16<T>::N);
+        if constexpr (F::kBinary) b0[k] = ld_stream(b + (uint64_t)(at + k * stride) * Vec16<T>::N);
+        else b0[k] = Vec16<T>{};
+    }
+}
+
+template <typename T, typename F, typename I>
+__device__ __forceinline__ void flat_store(T* __restrict__ dst, I at, I stride, const F& f,
+                                           const Vec16<T> (&a0)[F::kUnroll], const Vec16<T> (&b0)[F::kUnroll]) {
+#pragma unroll
+    for (int k = 0; k < F::kUnroll; ++k)
+        st_stream(dst + (uint64_t)(at + k * stride) * Vec16<T>::N, apply_vec<T>(f, a0[k], b0[k]));
+}
+
 template <typename T, typename F, typename I>
 __global__ void __launch_bounds__(kThreads, F::kMinBlocks) ew_flat(T* __restrict__ dst, const T* __restrict__ a,
-                                                    const T* __restrict__ b, uint64_t n, F f) {
-    pdl_enter();
+                                                    const T* __restrict__ b, uint64_t n, F f, int early) {
     constexpr int N = Vec16<T>::N;
     constexpr int U = F::kUnroll;  // vectors in flight per thread
     const I nvec = (I)(n / N);
     const I stride = (I)gridDim.x * blockDim.x;
     const I gid = (I)blockIdx.x * blockDim.x + threadIdx.x;
     I i = gid;
+    if (early && i + (U - 1) * stride < nvec) {
+        Vec16<T> a0[U], b0[U];
+        flat_load<T, F, I>(a, b, i, stride, a0, b0);
+        pdl_enter();
+        flat_store<T, F, I>(dst, i, stride, f, a0, b0);
+        i += U * stride;
+    } else {
+        pdl_enter();
+    }
     for (; i + (U - 1) * stride < nvec; i += U * stride) {
         Vec16<T> a0[U], b0[U];
-#pragma unroll
-        for (int k = 0; k < U; ++k) {
-            a0[k] = ld_stream(a + (uint64_t)(i + k * stride) * N);
-            if constexpr (F::kBinary) b0[k] = ld_stream(b + (uint64_t)(i + k * stride) * N);
-            else b0[k] = Vec16<T>{};
-        }
-#pragma unroll
-        for (int k = 0; k < U; ++k) st_stream(dst + (uint64_t)(i + k * stride) * N, apply_vec<T>(f, a0[k], b0[k]));
+        flat_load<T, F, I>(a, b, i, stride, a0, b0);
+        flat_store<T, F, I>(dst, i, stride, f, a0, b0);
     }
     if (i < nvec) {
         // this thread's last (fewer than U) vectors, their loads issued together
@@ -339,41 +366,64 @@ struct RowsWalk {
 };
 
 template <typename T, typename F>
-__global__ void __launch_bounds__(kThreads) ew_rows_vec(EwPlan p, F f, RowsWalk w) {
-    pdl_enter();
+__device__ __forceinline__ void rows_vec_load(const EwPlan& p, const RowsWalk& w, uint32_t i, uint32_t stride,
+                                              Vec16<T> (&a)[4], Vec16<T> (&b)[4], T* (&d)[4]) {
     constexpr int N = Vec16<T>::N;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+        const uint32_t v = i + k * stride;
+        d[k] = nullptr;
+        if (v >= w.nvec) continue;
+        const uint32_t row = fdiv(v, w.dv), c = (v - row * w.vpr) * N;
+        const uint32_t q = fdiv(row, w.d1), i1 = row - q * w.ne1;
+        const uint32_t i3 = fdiv(q, w.d2), i2 = q - i3 * w.ne2;
+        d[k] = at<T>(p.dst, (int64_t)i1 * p.dst.st[1] + (int64_t)i2 * p.dst.st[2] + (int64_t)i3 * p.dst.st[3]) + c;
+        a[k] = ld_stream(at<T>(p.src0, (int64_t)i1 * p.src0.st[1] + (int64_t)i2 * p.src0.st[2] +
+                                           (int64_t)i3 * p.src0.st[3]) + c);
+        if constexpr (F::kBinary) {
+            uint32_t j1 = i1, j2 = i2, j3 = i3;
+            if (p.src1_bcast) {
+                j1 = i1 - fdiv(i1, w.m1) * w.m1.d;
+                j2 = i2 - fdiv(i2, w.m2) * w.m2.d;
+                j3 = i3 - fdiv(i3, w.m3) * w.m3.d;
+            }
+            b[k] = ld_keep(at<T>(p.src1, (int64_t)j1 * p.src1.st[1] + (int64_t)j2 * p.src1.st[2] +
+                                             (int64_t)j3 * p.src1.st[3]) + c);
+        } else {
+            b[k] = Vec16<T>{};
+        }
+    }
+}
+
+template <typename T, typename F>
+__device__ __forceinline__ void rows_vec_store(const F& f, const Vec16<T> (&a)[4], const Vec16<T> (&b)[4],
+                                               T* const (&d)[4]) {
+#pragma unroll
+    for (int k = 0; k < 4; ++k)
+        if (d[k] != nullptr) st_stream(d[k], apply_vec<T>(f, a[k], b[k]));
+}
+
+// early: as ew_flat's (the first batch's loads before the wait).
+template <typename T, typename F>
+__global__ void __launch_bounds__(kThreads) ew_rows_vec(EwPlan p, F f, RowsWalk w, int early) {
     constexpr int U = 4;
     const uint32_t stride = gridDim.x * blockDim.x;
-    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < w.nvec; i += U * stride) {
+    uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (early && i < w.nvec) {
         Vec16<T> a[U], b[U];
         T* d[U];
-#pragma unroll
-        for (int k = 0; k < U; ++k) {
-            const uint32_t v = i + k * stride;
-            d[k] = nullptr;
-            if (v >= w.nvec) continue;
-            const uint32_t row = fdiv(v, w.dv), c = (v - row * w.vpr) * N;
-            const uint32_t q = fdiv(row, w.d1), i1 = row - q * w.ne1;
-            const uint32_t i3 = fdiv(q, w.d2), i2 = q - i3 * w.ne2;
-            d[k] = at<T>(p.dst, (int64_t)i1 * p.dst.st[1] + (int64_t)i2 * p.dst.st[2] + (int64_t)i3 * p.dst.st[3]) + c;
-            a[k] = ld_stream(at<T>(p.src0, (int64_t)i1 * p.src0.st[1] + (int64_t)i2 * p.src0.st[2] +
-                                               (int64_t)i3 * p.src0.st[3]) + c);
-            if constexpr (F::kBinary) {
-                uint32_t j1 = i1, j2 = i2, j3 = i3;
-                if (p.src1_bcast) {
-                    j1 = i1 - fdiv(i1, w.m1) * w.m1.d;
-                    j2 = i2 - fdiv(i2, w.m2) * w.m2.d;
-                    j3 = i3 - fdiv(i3, w.m3) * w.m3.d;
-                }
-                b[k] = ld_keep(at<T>(p.src1, (int64_t)j1 * p.src1.st[1] + (int64_t)j2 * p.src1.st[2] +
-                                                 (int64_t)j3 * p.src1.st[3]) + c);
-            } else {
-                b[k] = Vec16<T>{};
-            }
-        }
-#pragma unroll
-        for (int k = 0; k < U; ++k)
-            if (d[k] != nullptr) st_stream(d[k], apply_vec<T>(f, a[k], b[k]));
+        rows_vec_load<T, F>(p, w, i, stride, a, b, d);
+        pdl_enter();
+        rows_vec_store<T, F>(f, a, b, d);
+        i += U * stride;
+    } else {
+        pdl_enter();
+    }
+    for (; i < w.nvec; i += U * stride) {
+        Vec16<T> a[U], b[U];
+        T* d[U];
+        rows_vec_load<T, F>(p, w, i, stride, a, b, d);
+        rows_vec_store<T, F>(f, a, b, d);
     }
 }
 
@@ -382,15 +432,17 @@ __global__ void __launch_bounds__(kThreads) ew_rows_vec(EwPlan p, F f, RowsWalk 
 // is i, and src1's vector is i modulo the row's vector count -- one
 // magic-number division per vector instead of the row walk's four.
 template <typename T, typename F>
-__global__ void __launch_bounds__(kThreads) ew_row_broadcast(EwPlan p, F f, FastDiv dv, uint32_t nvec) {
-    pdl_enter();
+__global__ void __launch_bounds__(kThreads) ew_row_broadcast(EwPlan p, F f, FastDiv dv, uint32_t nvec, int early) {
     constexpr int N = Vec16<T>::N;
     constexpr int U = 4;
     const T* a = reinterpret_cast<const T*>(p.src0.ptr);
     const T* b = reinterpret_cast<const T*>(p.src1.ptr);
     T* d = reinterpret_cast<T*>(p.dst.ptr);
     const uint32_t stride = gridDim.x * blockDim.x;
-    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < nvec; i += U * stride) {
+    uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
+    bool first = early && i < nvec;  // this thread's first batch loads before the wait (as ew_flat's)
+    if (!first) pdl_enter();
+    for (; i < nvec; i += U * stride) {
         Vec16<T> av[U], bv[U];
 #pragma unroll
         for (int k = 0; k < U; ++k) {
@@ -398,6 +450,10 @@ __global__ void __launch_bounds__(kThreads) ew_row_broadcast(EwPlan p, F f, Fast
             if (v >= nvec) continue;
             av[k] = ld_stream(a + (size_t)v * N);
             bv[k] = ld_keep(b + (size_t)(v - fdiv(v, dv) * dv.d) * N);
+        }
+        if (first) {
+            pdl_enter();
+            first = false;
         }
 #pragma unroll
         for (int k = 0; k < U; ++k) {
@@ -567,11 +623,38 @@ uint32_t resident_ctas(DeviceKeyedValue& cache, const LaunchEnv& env, K kernel) 
     return (uint32_t)r;
 }
 
+// True when [p, p + bytes) lies outside what the previous launch on the
+// stream wrote (and that range is known).
+inline bool reads_clear(const LaunchEnv& env, const void* p, uint64_t bytes) {
+    if (!env.prev_known) return false;
+    const uintptr_t lo = reinterpret_cast<uintptr_t>(p), hi = lo + bytes;
+    return hi <= env.prev_lo || lo >= env.prev_hi;
+}
+
+// The bytes a strided view over extents ne can touch: from its base to the
+// last element of the last row (element strides are non-negative).
+struct Span {
+    uintptr_t lo, hi;
+};
+template <typename T>
+Span span_of(const Operand& o, const uint64_t* ne) {
+    uint64_t last = 0;
+    for (int d = 0; d < 4; ++d)
+        if (ne[d] > 0) last += (ne[d] - 1) * (uint64_t)(o.st[d] < 0 ? -o.st[d] : o.st[d]);
+    const uintptr_t lo = reinterpret_cast<uintptr_t>(o.ptr);
+    return Span{lo, lo + (last + 1) * sizeof(T)};
+}
+inline bool reads_clear(const LaunchEnv& env, const Span& s) {
+    return reads_clear(env, reinterpret_cast<const void*>(s.lo), s.hi - s.lo);
+}
+
 template <typename T, typename F>
 cudaError_t launch_ew(const LaunchEnv& env, const EwPlan& p, const F& f) {
     switch (p.kind) {
     case EwKind::Flat: {
         const uint64_t nvec = p.count / Vec16<T>::N;
+        const uint64_t bytes = p.count * sizeof(T);
+        const int early = reads_clear(env, p.src0.ptr, bytes) && (!F::kBinary || reads_clear(env, p.src1.ptr, bytes));
         static DeviceKeyedValue resident32, resident64;
         cudaError_t err;
         if (nvec < (1ull << 31) - (uint64_t)(F::kUnroll + 1) * env.sm_count * 8 * kThreads) {
@@ -579,15 +662,16 @@ cudaError_t launch_ew(const LaunchEnv& env, const EwPlan& p, const F& f) {
             err = launch_dependent(kernel, dim3(grid_for(env, nvec, F::kUnroll, resident_ctas(resident32, env, kernel))),
                                    dim3(kThreads), 0, env.stream, reinterpret_cast<T*>(p.dst.ptr),
                                    reinterpret_cast<const T*>(p.src0.ptr), reinterpret_cast<const T*>(p.src1.ptr),
-                                   p.count, f);
+                                   p.count, f, early);
         } else {
             auto* kernel = ew_flat<T, F, uint64_t>;
             err = launch_dependent(kernel, dim3(grid_for(env, nvec, F::kUnroll, resident_ctas(resident64, env, kernel))),
                                    dim3(kThreads), 0, env.stream, reinterpret_cast<T*>(p.dst.ptr),
                                    reinterpret_cast<const T*>(p.src0.ptr), reinterpret_cast<const T*>(p.src1.ptr),
-                                   p.count, f);
+                                   p.count, f, early);
         }
         if (err != cudaSuccess) return err;
+        stream_wrote(env.stream, p.dst.ptr, bytes);
         break;
     }
     case EwKind::Rows: {
@@ -596,10 +680,13 @@ cudaError_t launch_ew(const LaunchEnv& env, const EwPlan& p, const F& f) {
                 const uint32_t n = (uint32_t)(p.count / Vec16<T>::N);
                 static DeviceKeyedValue resident;
                 auto* kernel = ew_row_broadcast<T, F>;
+                const uint64_t bytes = p.count * sizeof(T);
+                const int early = reads_clear(env, p.src0.ptr, bytes) && reads_clear(env, p.src1.ptr, p.ne[0] * sizeof(T));
                 const cudaError_t err = launch_dependent(
                     kernel, dim3(grid_for(env, n, 4, resident_ctas(resident, env, kernel))), dim3(kThreads), 0,
-                    env.stream, p, f, make_fastdiv((uint32_t)(p.ne[0] / Vec16<T>::N)), n);
+                    env.stream, p, f, make_fastdiv((uint32_t)(p.ne[0] / Vec16<T>::N)), n, early);
                 if (err != cudaSuccess) return err;
+                stream_wrote(env.stream, p.dst.ptr, bytes);
                 break;
             }
         }
@@ -607,9 +694,12 @@ cudaError_t launch_ew(const LaunchEnv& env, const EwPlan& p, const F& f) {
         if (rows_walk(p, &w)) {
             static DeviceKeyedValue resident;
             auto* kernel = ew_rows_vec<T, F>;
+            const Span s0 = span_of<T>(p.src0, p.src0.ne), s1 = span_of<T>(p.src1, p.src1.ne), sd = span_of<T>(p.dst, p.dst.ne);
+            const int early = reads_clear(env, s0) && (!F::kBinary || reads_clear(env, s1));
             const cudaError_t err = launch_dependent(kernel, dim3(grid_for(env, w.nvec, 4, resident_ctas(resident, env, kernel))),
-                                                     dim3(kThreads), 0, env.stream, p, f, w);
+                                                     dim3(kThreads), 0, env.stream, p, f, w, early);
             if (err != cudaSuccess) return err;
+            stream_wrote(env.stream, reinterpret_cast<const void*>(sd.lo), sd.hi - sd.lo);
             break;
         }
         const uint64_t per_row = p.vec ? p.ne[0] / Vec16<T>::N : p.ne[0];

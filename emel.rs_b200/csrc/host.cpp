@@ -10,6 +10,7 @@
 #include <cmath>
 #include <cstdio>
 #include <cstring>
+#include <mutex>
 #include <new>
 
 #include <cuda_runtime.h>
@@ -320,8 +321,57 @@ emel_cuda_status device_status(emel_cuda_context* ctx, cudaError_t err) {
     return err == cudaErrorMemoryAllocation ? EMEL_CUDA_OUT_OF_MEMORY : EMEL_CUDA_DEVICE_ERROR;
 }
 
+}  // namespace
+
+// Per-stream record of the device bytes written by the library's last
+// launch, process-wide (two contexts may share a stream).  A stream not in
+// the table, or whose record was taken, is unknown: the next kernel reads
+// nothing before its predecessor has finished.
+namespace emel {
+namespace {
+struct StreamRecord {
+    cudaStream_t stream;
+    uintptr_t lo, hi;
+    bool used, known;
+};
+constexpr int kStreamRecords = 64;
+std::mutex g_stream_mu;
+StreamRecord g_streams[kStreamRecords];
+int g_stream_next = 0;
+
+StreamRecord* stream_slot(cudaStream_t stream) {
+    for (auto& r : g_streams)
+        if (r.used && r.stream == stream) return &r;
+    StreamRecord* r = &g_streams[g_stream_next];
+    g_stream_next = (g_stream_next + 1) % kStreamRecords;
+    *r = StreamRecord{stream, 0, 0, true, false};
+    return r;
+}
+}  // namespace
+
+void stream_take(cudaStream_t stream, uintptr_t* lo, uintptr_t* hi, bool* known) {
+    std::lock_guard<std::mutex> lock(g_stream_mu);
+    StreamRecord* r = stream_slot(stream);
+    *lo = r->lo;
+    *hi = r->hi;
+    *known = r->known;
+    r->known = false;
+}
+
+void stream_wrote(cudaStream_t stream, const void* p, uint64_t bytes) {
+    std::lock_guard<std::mutex> lock(g_stream_mu);
+    StreamRecord* r = stream_slot(stream);
+    r->lo = reinterpret_cast<uintptr_t>(p);
+    r->hi = r->lo + bytes;
+    r->known = true;
+}
+}  // namespace emel
+
+namespace {
+
 emel::LaunchEnv env_of(emel_cuda_context* ctx, void* stream) {
     emel::LaunchEnv e{};
+    emel::stream_take(static_cast<cudaStream_t>(stream), &e.prev_lo, &e.prev_hi, &e.prev_known);
     e.stream = static_cast<cudaStream_t>(stream);
     e.sm_count = ctx->sm_count;
     e.device = ctx->device;
@@ -561,6 +611,9 @@ emel_cuda_status emel_cuda_graph_begin(emel_cuda_context* ctx, void* stream) {
     cudaError_t err = select_device(ctx);
     if (err == cudaSuccess) err = cudaStreamBeginCapture((cudaStream_t)stream, cudaStreamCaptureModeThreadLocal);
     capture_launch_base = ctx->launches;
+    uintptr_t lo, hi;
+    bool known;
+    emel::stream_take((cudaStream_t)stream, &lo, &hi, &known);  // a captured graph starts with nothing known
     return device_status(ctx, err);
 }
 

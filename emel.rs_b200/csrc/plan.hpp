@@ -89,6 +89,18 @@ struct LaunchEnv {
     void* workspace;         // device scratch owned by the context
     uint64_t workspace_bytes;
     const void* tables;      // the context's binary16 domain tables (kDomainTableSlots x 128 KB)
+    // The device bytes [prev_lo, prev_hi) written by the library's previous
+    // launch on `stream`, when known (prev_known; stream_wrote).  A kernel
+    // whose inputs lie outside them may read before that launch finishes.
+    uintptr_t prev_lo, prev_hi;
+    bool prev_known;
 };
+
+// Per-stream record of the bytes the library's last launch wrote (host.cpp).
+// stream_take returns the stream's record and clears it (every entry point
+// that launches anything takes it first, so an unreported launch leaves the
+// record unknown); stream_wrote records a finished launch's output range.
+void stream_take(cudaStream_t stream, uintptr_t* lo, uintptr_t* hi, bool* known);
+void stream_wrote(cudaStream_t stream, const void* p, uint64_t bytes);
 
 }  // namespace emel

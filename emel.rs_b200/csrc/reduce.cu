@@ -459,6 +459,11 @@ extern "C" emel_cuda_status emel_cuda_sum_noalloc(void* stream, const emel_tenso
     double* partials = reinterpret_cast<double*>(static_cast<char*>(scratch) + kNoAllocHeader);
     // the array keeps the previous call's contents: the ticket must start at 0
     if (cudaMemsetAsync(ticket, 0, sizeof(unsigned), env.stream) != cudaSuccess) return EMEL_CUDA_DEVICE_ERROR;
+    {  // the stream's write record: this launch's output is not reported
+        uintptr_t lo, hi;
+        bool known;
+        stream_take(env.stream, &lo, &hi, &known);
+    }
     switch (walk_mode(p)) {
     case 1: sum_all<1><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, 0, dst->data); break;
     case 2: sum_all<2><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, 0, dst->data); break;

@@ -319,21 +319,29 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitTh
     double acc = 0.0;
     float zmin = 0.0f;  // smallest v - max among this thread's values
     if (isfinite(gm)) {
-        // pass 2: e = exp(v - max) into dst, f64 sum
+        // pass 2: e = exp(v - max) into dst, f64 sum.  Vectors whose four
+        // z = v - max are all >= kSoftmaxPlainDivFloor take the packed
+        // exponential (softmax_exp2), the rest softmax_exp lane by lane; a
+        // vector's four terms are added in binary32 (relative error <= 2^-23)
+        // before the f64 sum.
         if (vec) {
+            const float2 ngm = make_float2(-gm, -gm);  // z = q + (-max) is IEEE q - max
             batched<8>(ch.col0 / 4, ch.col1 / 4, [&](uint64_t v) { return __ldcg(x4 + v); },
                        [&](uint64_t v, float4 raw) {
                            const float4 q = scale4(raw);
-                           const float4 z = make_float4(__fsub_rn(q.x, gm), __fsub_rn(q.y, gm), __fsub_rn(q.z, gm),
-                                                        __fsub_rn(q.w, gm));
-                           zmin = fminf(zmin, fminf(fminf(z.x, z.y), fminf(z.z, z.w)));
-                           const float4 e = make_float4(softmax_exp(z.x), softmax_exp(z.y), softmax_exp(z.z),
-                                                        softmax_exp(z.w));
+                           const float2 zl = __fadd2_rn(lo2(q), ngm), zh = __fadd2_rn(hi2(q), ngm);
+                           const float zm = fmin3(fminf(zl.x, zl.y), zh.x, zh.y);
+                           float4 e;
+                           if (zm >= kSoftmaxPlainDivFloor) {
+                               e = cat2(softmax_exp2(zl), softmax_exp2(zh));
+                           } else {
+                               zmin = fminf(zmin, zm);
+                               e = make_float4(softmax_exp(zl.x), softmax_exp(zl.y), softmax_exp(zh.x),
+                                               softmax_exp(zh.y));
+                           }
                            y4[v] = e;
-                           acc += (double)e.x;
-                           acc += (double)e.y;
-                           acc += (double)e.z;
-                           acc += (double)e.w;
+                           const float2 pr = __fadd2_rn(lo2(e), hi2(e));
+                           acc += (double)__fadd_rn(pr.x, pr.y);
                        });
         } else {
             for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kSplitThreads) {
@@ -373,10 +381,10 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitTh
     if (isfinite(gm) && isfinite(denom)) {
         const float inv = __frcp_rn(denom);
         if (vec && zmin >= kSoftmaxPlainDivFloor) {
+            const float2 d2 = make_float2(denom, denom), i2 = make_float2(inv, inv);
             batched<8>(ch.col0 / 4, ch.col1 / 4, [&](uint64_t v) { return y4[v]; },
                        [&](uint64_t v, float4 e) {
-                           __stcs(y4 + v, make_float4(markstein_div(e.x, denom, inv), markstein_div(e.y, denom, inv),
-                                                      markstein_div(e.z, denom, inv), markstein_div(e.w, denom, inv)));
+                           __stcs(y4 + v, cat2(markstein_div2(lo2(e), d2, i2), markstein_div2(hi2(e), d2, i2)));
                        });
         } else if (vec) {
             batched<8>(ch.col0 / 4, ch.col1 / 4, [&](uint64_t v) { return y4[v]; },
