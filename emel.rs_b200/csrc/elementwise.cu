@@ -623,31 +623,6 @@ uint32_t resident_ctas(DeviceKeyedValue& cache, const LaunchEnv& env, K kernel) 
     return (uint32_t)r;
 }
 
-// True when [p, p + bytes) lies outside what the previous launch on the
-// stream wrote (and that range is known).
-inline bool reads_clear(const LaunchEnv& env, const void* p, uint64_t bytes) {
-    if (!env.prev_known) return false;
-    const uintptr_t lo = reinterpret_cast<uintptr_t>(p), hi = lo + bytes;
-    return hi <= env.prev_lo || lo >= env.prev_hi;
-}
-
-// The bytes a strided view over extents ne can touch: from its base to the
-// last element of the last row (element strides are non-negative).
-struct Span {
-    uintptr_t lo, hi;
-};
-template <typename T>
-Span span_of(const Operand& o, const uint64_t* ne) {
-    uint64_t last = 0;
-    for (int d = 0; d < 4; ++d)
-        if (ne[d] > 0) last += (ne[d] - 1) * (uint64_t)(o.st[d] < 0 ? -o.st[d] : o.st[d]);
-    const uintptr_t lo = reinterpret_cast<uintptr_t>(o.ptr);
-    return Span{lo, lo + (last + 1) * sizeof(T)};
-}
-inline bool reads_clear(const LaunchEnv& env, const Span& s) {
-    return reads_clear(env, reinterpret_cast<const void*>(s.lo), s.hi - s.lo);
-}
-
 template <typename T, typename F>
 cudaError_t launch_ew(const LaunchEnv& env, const EwPlan& p, const F& f) {
     switch (p.kind) {
@@ -694,12 +669,12 @@ cudaError_t launch_ew(const LaunchEnv& env, const EwPlan& p, const F& f) {
         if (rows_walk(p, &w)) {
             static DeviceKeyedValue resident;
             auto* kernel = ew_rows_vec<T, F>;
-            const Span s0 = span_of<T>(p.src0, p.src0.ne), s1 = span_of<T>(p.src1, p.src1.ne), sd = span_of<T>(p.dst, p.dst.ne);
+            const Span s0 = span_of(p.src0, sizeof(T)), s1 = span_of(p.src1, sizeof(T)), sd = span_of(p.dst, sizeof(T));
             const int early = reads_clear(env, s0) && (!F::kBinary || reads_clear(env, s1));
             const cudaError_t err = launch_dependent(kernel, dim3(grid_for(env, w.nvec, 4, resident_ctas(resident, env, kernel))),
                                                      dim3(kThreads), 0, env.stream, p, f, w, early);
             if (err != cudaSuccess) return err;
-            stream_wrote(env.stream, reinterpret_cast<const void*>(sd.lo), sd.hi - sd.lo);
+            stream_wrote(env.stream, sd);
             break;
         }
         const uint64_t per_row = p.vec ? p.ne[0] / Vec16<T>::N : p.ne[0];

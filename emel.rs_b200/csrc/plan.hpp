@@ -103,4 +103,32 @@ struct LaunchEnv {
 void stream_take(cudaStream_t stream, uintptr_t* lo, uintptr_t* hi, bool* known);
 void stream_wrote(cudaStream_t stream, const void* p, uint64_t bytes);
 
+// The bytes a view (Operand or RowOperand: ptr, element strides st, extents
+// ne) can touch: from its base to the last element of the last row.
+struct Span {
+    uintptr_t lo, hi;
+};
+template <typename O>
+inline Span span_of(const O& o, uint64_t elem_bytes) {
+    uint64_t last = 0;
+    for (int d = 0; d < 4; ++d)
+        if (o.ne[d] > 0) last += (o.ne[d] - 1) * (uint64_t)(o.st[d] < 0 ? -o.st[d] : o.st[d]);
+    const uintptr_t lo = reinterpret_cast<uintptr_t>(o.ptr);
+    return Span{lo, lo + (last + 1) * elem_bytes};
+}
+
+// True when the span lies outside what the previous launch on the stream
+// wrote (and that range is known).
+inline bool reads_clear(const LaunchEnv& env, const Span& s) {
+    if (!env.prev_known) return false;
+    return s.hi <= env.prev_lo || s.lo >= env.prev_hi;
+}
+inline bool reads_clear(const LaunchEnv& env, const void* p, uint64_t bytes) {
+    const uintptr_t lo = reinterpret_cast<uintptr_t>(p);
+    return reads_clear(env, Span{lo, lo + bytes});
+}
+inline void stream_wrote(cudaStream_t stream, const Span& s) {
+    stream_wrote(stream, reinterpret_cast<const void*>(s.lo), s.hi - s.lo);
+}
+
 }  // namespace emel

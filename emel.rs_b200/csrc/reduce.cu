@@ -134,8 +134,11 @@ __device__ __forceinline__ float4 vec_load(const VecWalk& w, uint64_t v) {
     }
 }
 
+// partial_sum / partial_arg wait for the previous kernel (pdl_enter) on
+// every path; with `early` (the input is clear of that kernel's writes) a
+// thread's first batch of loads goes out before the wait.
 template <int MODE>
-__device__ __forceinline__ double partial_sum(const RowPlan& p) {
+__device__ __forceinline__ double partial_sum(const RowPlan& p, bool early) {
     double acc = 0.0, acc2 = 0.0;  // two chains: x, y and z, w of every vector
     const uint64_t gthreads = (uint64_t)gridDim.x * blockDim.x;
     const uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -144,6 +147,22 @@ __device__ __forceinline__ double partial_sum(const RowPlan& p) {
         const VecWalk w = vec_walk<MODE>(p);
         const uint32_t G = (uint32_t)gthreads;
         uint32_t i = (uint32_t)gid;
+        if (early && (uint64_t)i + (U - 1) * (uint64_t)G < w.nvec) {
+            float4 q[U];
+#pragma unroll
+            for (int k = 0; k < U; ++k) q[k] = vec_load<MODE>(w, i + k * G);
+            pdl_enter();
+#pragma unroll
+            for (int k = 0; k < U; ++k) {
+                acc += (double)q[k].x;
+                acc2 += (double)q[k].z;
+                acc += (double)q[k].y;
+                acc2 += (double)q[k].w;
+            }
+            i += U * G;
+        } else {
+            pdl_enter();
+        }
         for (; (uint64_t)i + (U - 1) * (uint64_t)G < w.nvec; i += U * G) {
             float4 q[U];
 #pragma unroll
@@ -172,6 +191,7 @@ __device__ __forceinline__ double partial_sum(const RowPlan& p) {
         // warps walk rows; lanes walk columns
         const uint64_t warp = gid / 32, nwarps = gthreads / 32;
         const uint32_t lane = threadIdx.x & 31;
+        pdl_enter();
         for (uint64_t r = warp; r < p.rows; r += nwarps) {
             const float* row = row_ptr(p, r);
             for (uint64_t c = lane; c < p.ne[0]; c += 32) acc += (double)row[(int64_t)c * p.src.st[0]];
@@ -195,7 +215,7 @@ __device__ __forceinline__ void chain_take(float& best, uint32_t& idx, float v, 
 }
 
 template <int MODE>
-__device__ __forceinline__ ArgPart partial_arg(const RowPlan& p) {
+__device__ __forceinline__ ArgPart partial_arg(const RowPlan& p, bool early) {
     ArgPart b{0.0f, 0, 0};
     const uint64_t gthreads = (uint64_t)gridDim.x * blockDim.x;
     const uint64_t gid = (uint64_t)blockIdx.x * blockDim.x + threadIdx.x;
@@ -210,6 +230,23 @@ __device__ __forceinline__ ArgPart partial_arg(const RowPlan& p) {
         float bv[4] = {nan, nan, nan, nan};
         uint32_t bi[4] = {0, 0, 0, 0};
         uint32_t i = (uint32_t)gid;
+        if (early && (uint64_t)i + (U - 1) * (uint64_t)G < w.nvec) {
+            float4 q[U];
+#pragma unroll
+            for (int k = 0; k < U; ++k) q[k] = vec_load<MODE>(w, i + k * G);
+            pdl_enter();
+#pragma unroll
+            for (int k = 0; k < U; ++k) {
+                const uint32_t v = i + k * G;
+                chain_take(bv[0], bi[0], q[k].x, v);
+                chain_take(bv[1], bi[1], q[k].y, v);
+                chain_take(bv[2], bi[2], q[k].z, v);
+                chain_take(bv[3], bi[3], q[k].w, v);
+            }
+            i += U * G;
+        } else {
+            pdl_enter();
+        }
         for (; (uint64_t)i + (U - 1) * (uint64_t)G < w.nvec; i += U * G) {
             float4 q[U];
 #pragma unroll
@@ -243,6 +280,7 @@ __device__ __forceinline__ ArgPart partial_arg(const RowPlan& p) {
     } else {
         const uint64_t warp = gid / 32, nwarps = gthreads / 32;
         const uint32_t lane = threadIdx.x & 31;
+        pdl_enter();
         for (uint64_t r = warp; r < p.rows; r += nwarps) {
             const float* row = row_ptr(p, r);
             for (uint64_t c = lane; c < p.ne[0]; c += 32)
@@ -264,10 +302,10 @@ __device__ __forceinline__ bool last_cta(unsigned* ticket) {
 }
 
 template <int MODE>
-__global__ void __launch_bounds__(kThreads, kCtasPerSm) sum_all(RowPlan p, double* partials, unsigned* ticket, int mode, void* out) {
-    pdl_enter();
+__global__ void __launch_bounds__(kThreads, kCtasPerSm) sum_all(RowPlan p, double* partials, unsigned* ticket, int mode, void* out,
+                                                    int early) {
     __shared__ double sh[kThreads / 32];
-    double acc = block_sum(partial_sum<MODE>(p), sh);
+    double acc = block_sum(partial_sum<MODE>(p, early != 0), sh);
     if (threadIdx.x == 0) partials[blockIdx.x] = acc;
     if (!last_cta(ticket)) return;
     // fixed-order fold: thread t adds partials t, t+256, ... then a fixed tree
@@ -285,10 +323,9 @@ __global__ void __launch_bounds__(kThreads, kCtasPerSm) sum_all(RowPlan p, doubl
 
 template <int MODE>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm) argmax_all(RowPlan p, ArgPart* partials, unsigned* ticket, int out_kind,
-                                                       int dst_dtype, int64_t index_base, void* out) {
-    pdl_enter();
+                                                       int dst_dtype, int64_t index_base, void* out, int early) {
     __shared__ ArgPart sh[kThreads / 32];
-    ArgPart b = block_arg(partial_arg<MODE>(p), sh);
+    ArgPart b = block_arg(partial_arg<MODE>(p, early != 0), sh);
     if (threadIdx.x == 0) partials[blockIdx.x] = b;
     if (!last_cta(ticket)) return;
     ArgPart t{0.0f, 0, 0};
@@ -362,12 +399,14 @@ cudaError_t launch_sum(const LaunchEnv& env, const RowPlan& p, int mode, void* o
     unsigned* ticket = reinterpret_cast<unsigned*>(env.workspace);
     double* partials = reinterpret_cast<double*>(reinterpret_cast<char*>(env.workspace) + 256);
     const uint32_t grid = reduce_grid(env, p.rows * p.ne[0]);
+    const int early = reads_clear(env, span_of(p.src, 4));
     cudaError_t err;
     switch (walk_mode(p)) {
-    case 1: err = launch_dependent(sum_all<1>, dim3(grid), dim3(kThreads), 0, env.stream, p, partials, ticket, mode, out); break;
-    case 2: err = launch_dependent(sum_all<2>, dim3(grid), dim3(kThreads), 0, env.stream, p, partials, ticket, mode, out); break;
-    default: err = launch_dependent(sum_all<0>, dim3(grid), dim3(kThreads), 0, env.stream, p, partials, ticket, mode, out); break;
+    case 1: err = launch_dependent(sum_all<1>, dim3(grid), dim3(kThreads), 0, env.stream, p, partials, ticket, mode, out, early); break;
+    case 2: err = launch_dependent(sum_all<2>, dim3(grid), dim3(kThreads), 0, env.stream, p, partials, ticket, mode, out, early); break;
+    default: err = launch_dependent(sum_all<0>, dim3(grid), dim3(kThreads), 0, env.stream, p, partials, ticket, mode, out, early); break;
     }
+    if (err == cudaSuccess) stream_wrote(env.stream, out, mode == 2 ? 8 : 4);  // the workspace is the library's own
     ++*env.launches;
     return err != cudaSuccess ? err : cudaGetLastError();
 }
@@ -377,12 +416,14 @@ cudaError_t launch_argmax(const LaunchEnv& env, const RowPlan& p, int out_kind, 
     unsigned* ticket = reinterpret_cast<unsigned*>(env.workspace);
     ArgPart* partials = reinterpret_cast<ArgPart*>(reinterpret_cast<char*>(env.workspace) + 256);
     const uint32_t grid = reduce_grid(env, p.rows * p.ne[0]);
+    const int early = reads_clear(env, span_of(p.src, 4));
     cudaError_t err;
     switch (walk_mode(p)) {
-    case 1: err = launch_dependent(argmax_all<1>, dim3(grid), dim3(kThreads), 0, env.stream, p, partials, ticket, out_kind, dst_dtype, index_base, out); break;
-    case 2: err = launch_dependent(argmax_all<2>, dim3(grid), dim3(kThreads), 0, env.stream, p, partials, ticket, out_kind, dst_dtype, index_base, out); break;
-    default: err = launch_dependent(argmax_all<0>, dim3(grid), dim3(kThreads), 0, env.stream, p, partials, ticket, out_kind, dst_dtype, index_base, out); break;
+    case 1: err = launch_dependent(argmax_all<1>, dim3(grid), dim3(kThreads), 0, env.stream, p, partials, ticket, out_kind, dst_dtype, index_base, out, early); break;
+    case 2: err = launch_dependent(argmax_all<2>, dim3(grid), dim3(kThreads), 0, env.stream, p, partials, ticket, out_kind, dst_dtype, index_base, out, early); break;
+    default: err = launch_dependent(argmax_all<0>, dim3(grid), dim3(kThreads), 0, env.stream, p, partials, ticket, out_kind, dst_dtype, index_base, out, early); break;
     }
+    if (err == cudaSuccess) stream_wrote(env.stream, out, out_kind == 0 ? 8 : 24);  // the workspace is the library's own
     ++*env.launches;
     return err != cudaSuccess ? err : cudaGetLastError();
 }
@@ -465,9 +506,9 @@ extern "C" emel_cuda_status emel_cuda_sum_noalloc(void* stream, const emel_tenso
         stream_take(env.stream, &lo, &hi, &known);
     }
     switch (walk_mode(p)) {
-    case 1: sum_all<1><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, 0, dst->data); break;
-    case 2: sum_all<2><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, 0, dst->data); break;
-    default: sum_all<0><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, 0, dst->data); break;
+    case 1: sum_all<1><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, 0, dst->data, 0); break;
+    case 2: sum_all<2><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, 0, dst->data, 0); break;
+    default: sum_all<0><<<grid, kThreads, 0, env.stream>>>(p, partials, ticket, 0, dst->data, 0); break;
     }
     return cudaGetLastError() == cudaSuccess ? EMEL_CUDA_OK : EMEL_CUDA_DEVICE_ERROR;
 }

@@ -71,6 +71,7 @@ struct RingArgs {
     uint32_t weight_bytes;
     int stages;
     float param;  // eps (norms) or scale (soft_max)
+    int early;    // inputs clear of the previous kernel's writes: first copies before the wait
 };
 
 __device__ __forceinline__ void row_coords(uint32_t r, const RingArgs& a, uint32_t& i1, uint32_t& i2, uint32_t& i3) {
@@ -293,7 +294,7 @@ __global__ void __launch_bounds__(T, R >= 8 ? 2 : (R >= 4 ? 3 : 1024 / T)) row_r
     extern __shared__ __align__(128) unsigned char ring_smem[];
     __shared__ __align__(8) uint64_t full[kRingStagesMax];
     __shared__ GroupScratch<T> red;
-    pdl_enter();
+    if (!a.early) pdl_enter();
     const int tid = threadIdx.x;
     const int S = a.stages;
     const uint32_t mine = a.rows > blockIdx.x ? (a.rows - 1 - blockIdx.x) / gridDim.x + 1 : 0;
@@ -323,6 +324,7 @@ __global__ void __launch_bounds__(T, R >= 8 ? 2 : (R >= 4 ? 3 : 1024 / T)) row_r
     };
     if (tid == 0)
         for (uint32_t k = 0; k < mine && k < (uint32_t)S; ++k) issue(k, (int)k);
+    if (a.early) pdl_enter();  // every global store comes after this
 
     int s = 0;            // stage of row k: k % S
     uint32_t parity = 0;  // phase parity of row k: (k / S) & 1
@@ -632,6 +634,8 @@ bool launch_row_ring(const LaunchEnv& env, const RowPlan& p, int op, float param
     const uint32_t row_bytes = round_up(ne0 * 4, kStageAlign);
     a.mask_offset = row_bytes;
     a.stage_bytes = row_bytes + mask_bytes;
+    a.early = reads_clear(env, span_of(p.src, 4)) &&
+              (a.aux_mode == kAuxNone || reads_clear(env, span_of(p.aux, a.aux_f16 && op == 3 ? 2 : 4)));
     cudaError_t e;
     bool launched = false;
     switch (op) {
@@ -652,6 +656,7 @@ bool launch_row_ring(const LaunchEnv& env, const RowPlan& p, int op, float param
     default: e = launch_ring_kernel<kRingRmsGeneric, kRingThreads>(env, a, p.rows, &launched); break;
     }
     if (e == cudaSuccess && !launched) return false;
+    if (e == cudaSuccess) stream_wrote(env.stream, span_of(p.dst, 4));
     ++*env.launches;
     *err = e;
     return true;

@@ -78,6 +78,18 @@ def _run_chain(emel, ctx, lib, s, bufs, x, y):
     assert lib.emel_cuda_broadcast_row(ctx.handle, h, 1, B(rows(3, 4096)), B(row_vec(1, 4096)),
                                        B(rows(5, 4096))) == 0, ctx.last_error
 
+    # whole-tensor sum of b5, the previous launch's output (small[0]); argmax
+    # of x, independent (small[1], i64)
+    sv = _view(emel, bufs[7].ptr, 1)
+    assert lib.emel_cuda_sum(ctx.handle, h, B(_view(emel, bufs[5].ptr, N)), B(sv)) == 0, ctx.last_error
+    av = _view(emel, bufs[7].ptr + 8, 1, dtype_code=27, itemsize=8)
+    assert lib.emel_cuda_argmax(ctx.handle, h, B(_view(emel, bufs[0].ptr, N)), B(av)) == 0, ctx.last_error
+    # rms_norm rows of b6 (written three launches ago) into b8, then soft_max
+    # rows of b8 (the previous output) into b4
+    assert lib.emel_cuda_rms_norm(ctx.handle, h, B(rows(6, 4096)), B(rows(8, 4096)), ctypes.c_float(1e-6)) == 0, \
+        ctx.last_error
+    assert lib.emel_cuda_soft_max(ctx.handle, h, B(rows(8, 4096)), B(rows(4, 4096))) == 0, ctx.last_error
+
     b2 = np.empty(N, np.float32)
     b2[:N - 4] = -np.maximum(x, 0)[4:]
     b2[N - 4:] = -x[N - 4:]
@@ -88,7 +100,11 @@ def _run_chain(emel, ctx, lib, s, bufs, x, y):
     b6 = (b4.reshape(-1, 4096) + y[:4096]).reshape(-1)
     b2 = (x.reshape(-1, 4096) * b6[:4096]).reshape(-1)
     b5 = (b3.reshape(-1, 4096) - y[:4096]).reshape(-1)
-    return {2: b2, 3: b3, 4: b4, 5: b5, 6: b6}
+    r6 = b6.reshape(-1, 4096).astype(np.float64)
+    b8 = r6 / np.sqrt((r6 * r6).mean(axis=1, keepdims=True) + 1e-6)
+    e8 = np.exp(b8 - b8.max(axis=1, keepdims=True))
+    b4 = (e8 / e8.sum(axis=1, keepdims=True)).reshape(-1)
+    return {2: b2, 3: b3, 4: b4, 5: b5, 6: b6, 8: b8.reshape(-1), "argmax": int(np.argmax(x))}
 
 
 @pytest.mark.parametrize("graph", [False, True])
@@ -99,12 +115,12 @@ def test_chained_launches_respect_their_inputs(emel, graph):
     rng = np.random.default_rng(41)
     x = (rng.standard_normal(N) * 2).astype(np.float32)
     y = (rng.standard_normal(N) * 2).astype(np.float32)
-    bufs = [emel.DeviceBuffer(ctx, N * 4) for _ in range(7)]
+    bufs = [emel.DeviceBuffer(ctx, N * 4) for _ in range(9)]
     bufs[0].upload(x)
     bufs[1].upload(y)
     for r in range(3):
         # scramble the result buffers so a read that came too early shows
-        for i in range(2, 7):
+        for i in range(2, 9):
             bufs[i].upload(np.full(N, np.float32(1e30 + r)))
         if graph:
             g = emel.Graph(ctx, s)
@@ -116,14 +132,21 @@ def test_chained_launches_respect_their_inputs(emel, graph):
         else:
             want = _run_chain(emel, ctx, lib, s, bufs, x, y)
             s.synchronize()
-        got = {i: bufs[i].download(np.empty(N, np.float32)) for i in want}
+        got = {i: bufs[i].download(np.empty(N, np.float32)) for i in want if i != "argmax"}
+        small = bufs[7].download(np.empty(4, np.float32))
         # b3 holds exp results (within 2 ulp of the correctly rounded exp);
         # b5 = b3 - y per row is then checked bit for bit on the device's b3
         d = gh.ulp_diff_f32(got[3], want[3])
         assert int(d.max()) <= 2, f"buffer 3: {int(d.max())} ulp"
         want[5] = (got[3].reshape(-1, 4096) - y[:4096]).reshape(-1)
-        for i in (2, 4, 5, 6):
+        for i in (2, 5, 6):
             gh.assert_bits_equal(got[i], want[i], f"buffer {i} (graph={graph}, round {r})")
+        total = float(np.sum(got[5].astype(np.float64)))
+        assert abs(float(small[0]) - total) <= 1e-5 * abs(total), (float(small[0]), total)
+        assert int(small[2:4].view(np.int64)[0]) == want["argmax"]
+        for i in (8, 4):  # rms_norm rows, then soft_max of them
+            err = np.abs(got[i].astype(np.float64) - want[i]) / np.maximum(np.abs(want[i]), 1e-30)
+            assert float(err[np.abs(want[i]) > 1e-30].max()) <= 1e-5, (i, float(err.max()))
     for b in bufs:
         b.free()
     s.close()
