@@ -970,29 +970,33 @@ def run_cfg5(args, world, rank, local):
     for _ in range(3):
         graph.launch()
     stream.synchronize()
-    # The timed region: the K steps captured back to back in one graph and
-    # launched with one host call, so the device never waits on the host
-    # between steps (a host loop of K launches let the clock sampler's NVML
-    # calls, or any host hiccup, leave the GPU idle between short steps).
+    # The timed region: one graph holding an exchange round that aligns the
+    # ranks (N > 1), the start event, the K steps back to back and the end
+    # event, launched with one host call.  The device never waits on the
+    # host inside it, and every rank's start event fires right after the
+    # alignment, however late its host launched the graph (a host loop of K
+    # launches, or host time between the alignment and the start event,
+    # left GPUs idle and folded host skew into the max over ranks).
+    t0, t1 = pkg.CudaEvent(ctx), pkg.CudaEvent(ctx)
     steps_graph = pkg.Graph(ctx, stream)
     with steps_graph:
+        shard.align(sh)
+        t0.record_timed(sh)
         for _ in range(args.steps):
             shard.step(sh)
+        t1.record_timed(sh)
     steps_graph.launch()  # untimed: first replay of the new graph
     stream.synchronize()
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    t0, t1 = pkg.CudaEvent(ctx), pkg.CudaEvent(ctx)
-    shard.align(sh)
     launches_before = ctx.launches
     with ClockSampler(local) as clocks:
-        t0.record(sh)
         steps_graph.launch()
-        t1.record(sh)
         stream.synchronize()
     steps_graph.close()
-    gpu_launches = ctx.launches - launches_before
+    # the alignment's two exchange kernels sit before the start event
+    gpu_launches = ctx.launches - launches_before - (2 if shard.exchange is not None else 0)
     ms = t0.elapsed_ms(t1) / args.steps
     ms_t = torch.tensor([ms], dtype=torch.float64, device=device)
     if world > 1:

@@ -21,6 +21,7 @@
 
 #include "common.cuh"
 #include "launch.hpp"
+#include "pdl.cuh"
 
 namespace emel {
 
@@ -46,7 +47,12 @@ __device__ __forceinline__ char* slot(char* buffer, uint32_t epoch, int rank, ui
     return buffer + kExchangeHeaderBytes + ((uint64_t)(epoch & 1u) * kExchangeMaxRanks + (uint64_t)rank) * slot_bytes;
 }
 
+// Both kernels are launched as programmatic dependents (pdl.cuh): they wait
+// for the previous kernel of the stream (the payload's producer, or the
+// work the gathered values follow) before touching memory, while their own
+// launch overlaps its tail, and they let the next kernel be scheduled.
 __global__ void __launch_bounds__(kExchangeMaxRanks) exchange_publish(ExchangeArgs a) {
+    pdl_enter();
     __shared__ uint32_t epoch;
     if (threadIdx.x == 0) epoch = ++*a.epoch;
     __syncthreads();
@@ -67,6 +73,7 @@ __global__ void __launch_bounds__(kExchangeMaxRanks) exchange_publish(ExchangeAr
 // or a NaN at element 0 of the whole tensor, leaves index 0).
 template <bool COMBINE>
 __global__ void __launch_bounds__(kExchangeMaxRanks) exchange_wait(ExchangeArgs a, void* gathered, CombineOut c) {
+    pdl_enter();
     __shared__ uint32_t failed;
     if (threadIdx.x == 0) failed = 0u;
     if constexpr (COMBINE) __syncthreads();
@@ -133,19 +140,21 @@ uint64_t exchange_buffer_bytes(uint32_t slot_bytes) {
 }
 
 cudaError_t launch_exchange_publish(cudaStream_t stream, const ExchangeArgs& args) {
-    exchange_publish<<<1, kExchangeMaxRanks, 0, stream>>>(args);
-    return cudaGetLastError();
+    const cudaError_t err = launch_dependent(exchange_publish, dim3(1), dim3(kExchangeMaxRanks), 0, stream, args);
+    return err != cudaSuccess ? err : cudaGetLastError();
 }
 
 cudaError_t launch_exchange_wait(cudaStream_t stream, const ExchangeArgs& args, void* gathered) {
-    exchange_wait<false><<<1, kExchangeMaxRanks, 0, stream>>>(args, gathered, CombineOut{});
-    return cudaGetLastError();
+    const cudaError_t err =
+        launch_dependent(exchange_wait<false>, dim3(1), dim3(kExchangeMaxRanks), 0, stream, args, gathered, CombineOut{});
+    return err != cudaSuccess ? err : cudaGetLastError();
 }
 
 cudaError_t launch_exchange_wait_combine(cudaStream_t stream, const ExchangeArgs& args, void* gathered,
                                          const CombineOut& out) {
-    exchange_wait<true><<<1, kExchangeMaxRanks, 0, stream>>>(args, gathered, out);
-    return cudaGetLastError();
+    const cudaError_t err =
+        launch_dependent(exchange_wait<true>, dim3(1), dim3(kExchangeMaxRanks), 0, stream, args, gathered, out);
+    return err != cudaSuccess ? err : cudaGetLastError();
 }
 
 }  // namespace emel

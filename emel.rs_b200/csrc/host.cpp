@@ -369,6 +369,13 @@ void stream_wrote(cudaStream_t stream, const void* p, uint64_t bytes) {
 
 namespace {
 
+// Clears the stream's write record (a launch that reports no output range).
+void forget_stream(void* stream) {
+    uintptr_t lo, hi;
+    bool known;
+    emel::stream_take(static_cast<cudaStream_t>(stream), &lo, &hi, &known);
+}
+
 emel::LaunchEnv env_of(emel_cuda_context* ctx, void* stream) {
     emel::LaunchEnv e{};
     emel::stream_take(static_cast<cudaStream_t>(stream), &e.prev_lo, &e.prev_hi, &e.prev_known);
@@ -771,6 +778,7 @@ emel_cuda_status emel_cuda_exchange_publish(emel_cuda_context* ctx, void* stream
                                             const void* payload) {
     if (ctx == nullptr || ex == nullptr || !ex->connected || !aligned16_ptr(payload)) return EMEL_CUDA_INVALID_ARGUMENT;
     cudaError_t err = select_device(ctx);
+    forget_stream(stream);
     if (err == cudaSuccess) err = emel::launch_exchange_publish((cudaStream_t)stream, exchange_args(ctx, ex, payload));
     if (err == cudaSuccess) ++ctx->launches;
     return device_status(ctx, err);
@@ -780,6 +788,7 @@ emel_cuda_status emel_cuda_exchange_wait(emel_cuda_context* ctx, void* stream, e
                                          void* gathered) {
     if (ctx == nullptr || ex == nullptr || !ex->connected || !aligned16_ptr(gathered)) return EMEL_CUDA_INVALID_ARGUMENT;
     cudaError_t err = select_device(ctx);
+    forget_stream(stream);
     if (err == cudaSuccess)
         err = emel::launch_exchange_wait((cudaStream_t)stream, exchange_args(ctx, ex, nullptr), gathered);
     if (err == cudaSuccess) ++ctx->launches;
@@ -801,6 +810,7 @@ emel_cuda_status emel_cuda_exchange_wait_sum_argmax(emel_cuda_context* ctx, void
         ex->bytes != 8 + sizeof(emel_cuda_argmax_partial))
         return EMEL_CUDA_INVALID_ARGUMENT;
     cudaError_t err = select_device(ctx);
+    forget_stream(stream);
     if (err == cudaSuccess) {
         const emel::CombineOut out{sum_dst->data, argmax_dst->data, (int)argmax_dst->dtype};
         err = emel::launch_exchange_wait_combine((cudaStream_t)stream, exchange_args(ctx, ex, nullptr), gathered, out);
