@@ -1070,6 +1070,113 @@ def run_cfg5(args, world, rank, local):
         dist.destroy_process_group()
 
 
+def run_cfg5_breakdown(args, world, rank, local):
+    """Where one rank's configuration-5 step goes (`--breakdown`): the step,
+    the step without the exchange, the exchange alone, one kernel alone, each
+    captured as a CUDA graph and replayed K times (device time per replay),
+    and one replay with an event node between consecutive kernels (the
+    parts; the nodes stop the programmatic overlap, so they add up to more
+    than the step).  Every rank prints one JSON line."""
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=device)
+    pkg = load_package()
+    ctx = pkg.Context(local)
+    stream = pkg.Stream(ctx)
+    sh = stream.handle
+    shard = Cfg5Shard(pkg, ctx, torch, device, world, rank)
+    shard.connect(dist)
+    torch.cuda.synchronize()
+    lib, h, B = shard.lib, ctx.handle, ctypes.byref
+
+    def partials():
+        p = shard.partial.data_ptr()
+        shard._ok(lib.emel_cuda_sum_f64(h, sh, B(shard.v0), ctypes.c_void_p(p)), "sum_f64")
+        shard._ok(lib.emel_cuda_argmax_partial_compute(h, sh, B(shard.v0), shard.b * shard.plane,
+                                                       ctypes.c_void_p(p + 8)), "argmax partial")
+
+    def broadcasts():
+        mul_only()
+        shard._ok(lib.emel_cuda_binary_repeat(h, sh, 0, B(shard.v0), B(shard.v1), B(shard.va)), "repeat add")
+
+    def exchange():
+        if shard.exchange is not None:
+            shard.align(sh)
+
+    def no_exchange():
+        partials()
+        broadcasts()
+
+    evs = [pkg.CudaEvent(ctx) for _ in range(7)]
+
+    def parts():
+        p = shard.partial.data_ptr()
+        evs[0].record_timed(sh)
+        shard._ok(lib.emel_cuda_sum_f64(h, sh, B(shard.v0), ctypes.c_void_p(p)), "sum_f64")
+        evs[1].record_timed(sh)
+        shard._ok(lib.emel_cuda_argmax_partial_compute(h, sh, B(shard.v0), shard.b * shard.plane,
+                                                       ctypes.c_void_p(p + 8)), "argmax partial")
+        evs[2].record_timed(sh)
+        if shard.exchange is not None:
+            shard.exchange.publish(sh, p)
+        evs[3].record_timed(sh)
+        shard._ok(lib.emel_cuda_binary_repeat(h, sh, 2, B(shard.v0), B(shard.v1), B(shard.vm)), "repeat mul")
+        evs[4].record_timed(sh)
+        shard._ok(lib.emel_cuda_binary_repeat(h, sh, 0, B(shard.v0), B(shard.v1), B(shard.va)), "repeat add")
+        evs[5].record_timed(sh)
+        if shard.exchange is not None:
+            shard._ok(lib.emel_cuda_exchange_wait_sum_argmax(h, sh, shard.exchange.handle,
+                                                            ctypes.c_void_p(shard.gathered.data_ptr()),
+                                                            B(shard.vsum), B(shard.vidx)), "exchange wait")
+        evs[6].record_timed(sh)
+
+    res = {"rank": rank, "world": world, "replays": args.steps}
+    def mul_only():
+        shard._ok(lib.emel_cuda_binary_repeat(h, sh, 2, B(shard.v0), B(shard.v1), B(shard.vm)), "repeat mul")
+
+    variants = (("step", lambda: shard.step(sh)), ("no_exchange", no_exchange), ("exchange_only", exchange),
+                ("repeat_mul_only", mul_only), ("parts", parts))
+    for name, fn in variants:
+        for _ in range(3):
+            fn()
+        stream.synchronize()
+        g = pkg.Graph(ctx, stream)
+        with g:
+            fn()
+        t0, t1 = pkg.CudaEvent(ctx), pkg.CudaEvent(ctx)
+        for _ in range(3):
+            g.launch()
+        stream.synchronize()
+        if world > 1:
+            dist.barrier()
+        shard.align(sh)
+        t0.record(sh)
+        for _ in range(args.steps):
+            g.launch()
+        t1.record(sh)
+        stream.synchronize()
+        res[f"{name}_us"] = round(t0.elapsed_ms(t1) / args.steps * 1e3, 2)
+        if name == "parts":
+            g.launch()
+            stream.synchronize()
+            res["parts_us"] = dict(zip(("sum", "argmax", "publish", "repeat_mul", "repeat_add", "wait"),
+                                       (round(evs[i].elapsed_ms(evs[i + 1]) * 1e3, 2) for i in range(6))))
+        g.close()
+        if world > 1:
+            dist.barrier()
+    print(json.dumps(res), flush=True)
+    if world > 1:
+        dist.barrier()
+        shard.close()
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def run_cfg5_e2e(args, pkg, ctx, torch, shard, stream, world):
     """The same step through the C ABI with host buffers: every step copies
     this rank's src0 shard and src1 from pinned host memory, runs the step,
@@ -1418,6 +1525,8 @@ def main():
                     help="cfg5 (default): the 4-D broadcast + whole-tensor reductions sharded along dim 3 "
                          "(strong scaling); cfg2: the 16-op unary sweep on independent per-GPU batches")
     ap.add_argument("--no-cfg2", action="store_true", help="cfg5 at N=1: skip the extra cfg2 per-op figures")
+    ap.add_argument("--breakdown", action="store_true",
+                    help="cfg5: per-rank step breakdown (step, without exchange, exchange alone, parts), K replays")
     args = ap.parse_args()
     world, rank, local = dist_env()
     if args.warmup < 3:
@@ -1430,6 +1539,9 @@ def main():
         return
     if args.suite:
         run_suite(args)
+        return
+    if args.breakdown:
+        run_cfg5_breakdown(args, world, rank, local)
         return
     if args.workload == "cfg5":
         run_cfg5(args, world, rank, local)
