@@ -365,65 +365,45 @@ struct RowsWalk {
     uint32_t nvec;
 };
 
+// No early loads here: holding the first batch across the wait, or
+// prefetching it into L2 before the wait, both measured slower on this
+// kernel than waiting first (359 vs 363 us on cfg5's full repeat).
 template <typename T, typename F>
-__device__ __forceinline__ void rows_vec_load(const EwPlan& p, const RowsWalk& w, uint32_t i, uint32_t stride,
-                                              Vec16<T> (&a)[4], Vec16<T> (&b)[4], T* (&d)[4]) {
+__global__ void __launch_bounds__(kThreads) ew_rows_vec(EwPlan p, F f, RowsWalk w) {
     constexpr int N = Vec16<T>::N;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const uint32_t v = i + k * stride;
-        d[k] = nullptr;
-        if (v >= w.nvec) continue;
-        const uint32_t row = fdiv(v, w.dv), c = (v - row * w.vpr) * N;
-        const uint32_t q = fdiv(row, w.d1), i1 = row - q * w.ne1;
-        const uint32_t i3 = fdiv(q, w.d2), i2 = q - i3 * w.ne2;
-        d[k] = at<T>(p.dst, (int64_t)i1 * p.dst.st[1] + (int64_t)i2 * p.dst.st[2] + (int64_t)i3 * p.dst.st[3]) + c;
-        a[k] = ld_stream(at<T>(p.src0, (int64_t)i1 * p.src0.st[1] + (int64_t)i2 * p.src0.st[2] +
-                                           (int64_t)i3 * p.src0.st[3]) + c);
-        if constexpr (F::kBinary) {
-            uint32_t j1 = i1, j2 = i2, j3 = i3;
-            if (p.src1_bcast) {
-                j1 = i1 - fdiv(i1, w.m1) * w.m1.d;
-                j2 = i2 - fdiv(i2, w.m2) * w.m2.d;
-                j3 = i3 - fdiv(i3, w.m3) * w.m3.d;
-            }
-            b[k] = ld_keep(at<T>(p.src1, (int64_t)j1 * p.src1.st[1] + (int64_t)j2 * p.src1.st[2] +
-                                             (int64_t)j3 * p.src1.st[3]) + c);
-        } else {
-            b[k] = Vec16<T>{};
-        }
-    }
-}
-
-template <typename T, typename F>
-__device__ __forceinline__ void rows_vec_store(const F& f, const Vec16<T> (&a)[4], const Vec16<T> (&b)[4],
-                                               T* const (&d)[4]) {
-#pragma unroll
-    for (int k = 0; k < 4; ++k)
-        if (d[k] != nullptr) st_stream(d[k], apply_vec<T>(f, a[k], b[k]));
-}
-
-// early: as ew_flat's (the first batch's loads before the wait).
-template <typename T, typename F>
-__global__ void __launch_bounds__(kThreads) ew_rows_vec(EwPlan p, F f, RowsWalk w, int early) {
     constexpr int U = 4;
     const uint32_t stride = gridDim.x * blockDim.x;
-    uint32_t i = blockIdx.x * blockDim.x + threadIdx.x;
-    if (early && i < w.nvec) {
+    pdl_enter();
+    for (uint32_t i = blockIdx.x * blockDim.x + threadIdx.x; i < w.nvec; i += U * stride) {
         Vec16<T> a[U], b[U];
         T* d[U];
-        rows_vec_load<T, F>(p, w, i, stride, a, b, d);
-        pdl_enter();
-        rows_vec_store<T, F>(f, a, b, d);
-        i += U * stride;
-    } else {
-        pdl_enter();
-    }
-    for (; i < w.nvec; i += U * stride) {
-        Vec16<T> a[U], b[U];
-        T* d[U];
-        rows_vec_load<T, F>(p, w, i, stride, a, b, d);
-        rows_vec_store<T, F>(f, a, b, d);
+#pragma unroll
+        for (int k = 0; k < U; ++k) {
+            const uint32_t v = i + k * stride;
+            d[k] = nullptr;
+            if (v >= w.nvec) continue;
+            const uint32_t row = fdiv(v, w.dv), c = (v - row * w.vpr) * N;
+            const uint32_t q = fdiv(row, w.d1), i1 = row - q * w.ne1;
+            const uint32_t i3 = fdiv(q, w.d2), i2 = q - i3 * w.ne2;
+            d[k] = at<T>(p.dst, (int64_t)i1 * p.dst.st[1] + (int64_t)i2 * p.dst.st[2] + (int64_t)i3 * p.dst.st[3]) + c;
+            a[k] = ld_stream(at<T>(p.src0, (int64_t)i1 * p.src0.st[1] + (int64_t)i2 * p.src0.st[2] +
+                                               (int64_t)i3 * p.src0.st[3]) + c);
+            if constexpr (F::kBinary) {
+                uint32_t j1 = i1, j2 = i2, j3 = i3;
+                if (p.src1_bcast) {
+                    j1 = i1 - fdiv(i1, w.m1) * w.m1.d;
+                    j2 = i2 - fdiv(i2, w.m2) * w.m2.d;
+                    j3 = i3 - fdiv(i3, w.m3) * w.m3.d;
+                }
+                b[k] = ld_keep(at<T>(p.src1, (int64_t)j1 * p.src1.st[1] + (int64_t)j2 * p.src1.st[2] +
+                                                 (int64_t)j3 * p.src1.st[3]) + c);
+            } else {
+                b[k] = Vec16<T>{};
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < U; ++k)
+            if (d[k] != nullptr) st_stream(d[k], apply_vec<T>(f, a[k], b[k]));
     }
 }
 
@@ -669,10 +649,9 @@ cudaError_t launch_ew(const LaunchEnv& env, const EwPlan& p, const F& f) {
         if (rows_walk(p, &w)) {
             static DeviceKeyedValue resident;
             auto* kernel = ew_rows_vec<T, F>;
-            const Span s0 = span_of(p.src0, sizeof(T)), s1 = span_of(p.src1, sizeof(T)), sd = span_of(p.dst, sizeof(T));
-            const int early = reads_clear(env, s0) && (!F::kBinary || reads_clear(env, s1));
+            const Span sd = span_of(p.dst, sizeof(T));
             const cudaError_t err = launch_dependent(kernel, dim3(grid_for(env, w.nvec, 4, resident_ctas(resident, env, kernel))),
-                                                     dim3(kThreads), 0, env.stream, p, f, w, early);
+                                                     dim3(kThreads), 0, env.stream, p, f, w);
             if (err != cudaSuccess) return err;
             stream_wrote(env.stream, sd);
             break;
