@@ -861,6 +861,9 @@ class Cfg5Shard:
         from emel_rs_b200 import distributed as D
         if self.world > 1:
             self.exchange = D.PeerExchange(self.pkg, self.ctx, dist, self.world, self.rank)
+            # the publish runs on a side branch, beside the two broadcasts
+            self.side = self.pkg.Stream(self.ctx)
+            self.ev_fork, self.ev_join = self.pkg.CudaEvent(self.ctx), self.pkg.CudaEvent(self.ctx)
 
     def _ok(self, st, what):
         if st != 0:
@@ -869,7 +872,8 @@ class Cfg5Shard:
     def step(self, sh):
         """One step on stream `sh`.  One GPU: OpSum, OpArgmax (exact i64
         index), repeat mul, repeat add.  N GPUs: the shard's f64 sum and
-        argmax partial, published to every rank over NVLink before the two
+        argmax partial, published to every rank over NVLink on a side branch
+        (forked after the partials, joined before the wait) while the two
         repeat broadcasts stream, then one wait that gathers every rank's
         partials and combines them on the device."""
         lib, h, B = self.lib, self.ctx.handle, ctypes.byref
@@ -881,10 +885,14 @@ class Cfg5Shard:
             self._ok(lib.emel_cuda_sum_f64(h, sh, B(self.v0), ctypes.c_void_p(p)), "sum_f64")
             self._ok(lib.emel_cuda_argmax_partial_compute(h, sh, B(self.v0), self.b * self.plane,
                                                           ctypes.c_void_p(p + 8)), "argmax partial")
-            self.exchange.publish(sh, p)
+            self.ev_fork.record(sh)
+            self.side.wait(self.ev_fork)
+            self.exchange.publish(self.side.handle, p)
+            self.ev_join.record(self.side.handle)
         self._ok(lib.emel_cuda_binary_repeat(h, sh, 2, B(self.v0), B(self.v1), B(self.vm)), "repeat mul")
         self._ok(lib.emel_cuda_binary_repeat(h, sh, 0, B(self.v0), B(self.v1), B(self.va)), "repeat add")
         if self.exchange is not None:
+            self._ok(lib.emel_cuda_stream_wait_event(h, sh, self.ev_join.handle), "join")
             self._ok(lib.emel_cuda_exchange_wait_sum_argmax(h, sh, self.exchange.handle,
                                                             ctypes.c_void_p(self.gathered.data_ptr()),
                                                             B(self.vsum), B(self.vidx)), "exchange wait")
@@ -934,6 +942,7 @@ class Cfg5Shard:
 
     def close(self):
         if self.exchange is not None:
+            self.side.synchronize()
             self.exchange.close()
             self.exchange = None
 
