@@ -156,9 +156,31 @@ struct ChunkPartial {
     int64_t i;
 };
 
-__global__ void __launch_bounds__(kSplitThreads, kSplitCtasPerSm)
-    argmax_rows_flat(RowPlan p, int dst_dtype, uint64_t chunk, ChunkPartial* partials, unsigned* tickets) {
+// early_batch: with `early` (the row is clear of the previous kernel's
+// writes) the thread's first batch of U vectors of [v0, v1) is loaded before
+// the wait for that kernel (pdl_enter) and used after it; returns where the
+// batched walk continues.  Without it, waits first.
+template <int U, typename Load, typename Use>
+__device__ __forceinline__ uint64_t early_batch(bool early, uint64_t v0, uint64_t v1, Load load, Use use) {
+    if (!early) {
+        pdl_enter();
+        return v0;
+    }
+    const uint64_t v = v0 + threadIdx.x;
+    float4 q[U];
+#pragma unroll
+    for (int k = 0; k < U; ++k)
+        if (v + k * kSplitThreads < v1) q[k] = load(v + k * kSplitThreads);
     pdl_enter();
+#pragma unroll
+    for (int k = 0; k < U; ++k)
+        if (v + k * kSplitThreads < v1) use(v + k * kSplitThreads, q[k]);
+    return v0 + (uint64_t)U * kSplitThreads;
+}
+
+__global__ void __launch_bounds__(kSplitThreads, kSplitCtasPerSm)
+    argmax_rows_flat(RowPlan p, int dst_dtype, uint64_t chunk, ChunkPartial* partials, unsigned* tickets,
+                     int early) {
     __shared__ GroupScratch<kSplitThreads> s;
     __shared__ bool is_last;
     const unsigned rank = blockIdx.x % kSplitCluster;
@@ -169,16 +191,18 @@ __global__ void __launch_bounds__(kSplitThreads, kSplitCtasPerSm)
     float bv[4] = {nan, nan, nan, nan};
     uint64_t bc[4] = {0, 0, 0, 0};
     const float4* r4 = reinterpret_cast<const float4*>(row);
-    batched<8>(ch.col0 / 4, ch.col1 / 4, [&](uint64_t v) { return __ldcs(r4 + v); },
-               [&](uint64_t v, float4 q) {
-                   const float q4[4] = {q.x, q.y, q.z, q.w};
+    auto load = [&](uint64_t v) { return __ldcs(r4 + v); };
+    auto use = [&](uint64_t v, float4 q) {
+        const float q4[4] = {q.x, q.y, q.z, q.w};
 #pragma unroll
-                   for (int l = 0; l < 4; ++l) {
-                       const float nb = fmaxf(bv[l], q4[l]);
-                       if (nb != bv[l]) bc[l] = v;
-                       bv[l] = nb;
-                   }
-               });
+        for (int l = 0; l < 4; ++l) {
+            const float nb = fmaxf(bv[l], q4[l]);
+            if (nb != bv[l]) bc[l] = v;
+            bv[l] = nb;
+        }
+    };
+    const uint64_t vstart = early_batch<8>(early != 0, ch.col0 / 4, ch.col1 / 4, load, use);
+    batched<8>(vstart, ch.col1 / 4, load, use);
     ArgBest bl[4];
 #pragma unroll
     for (int l = 0; l < 4; ++l) bl[l] = ArgBest{bv[l], (int64_t)(4 * bc[l] + l), is_nan(bv[l]) ? 0u : 1u};
@@ -265,8 +289,7 @@ __device__ __forceinline__ float value_at(const RowPlan& p, const SoftmaxRow& w,
 }
 
 __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitThreads, kSplitCtasPerSm)
-    softmax_rows_split(RowPlan p, bool apply_scale, float scale, uint64_t chunk) {
-    pdl_enter();
+    softmax_rows_split(RowPlan p, bool apply_scale, float scale, uint64_t chunk, int early) {
     __shared__ GroupScratch<kSplitThreads> s;
     __shared__ float part_max;
     __shared__ double part_sum;
@@ -294,12 +317,15 @@ __global__ void __cluster_dims__(kSplitCluster, 1, 1) __launch_bounds__(kSplitTh
     // or a maximum of +-inf, leaves the row's maximum non-finite
     float m = -INFINITY;
     if (vec) {
-        batched<8>(ch.col0 / 4, ch.col1 / 4, [&](uint64_t v) { return __ldcg(x4 + v); },
-                   [&](uint64_t, float4 raw) {
-                       const float4 q = scale4(raw);
-                       m = max_nan(max_nan(m, q.x), max_nan(q.y, max_nan(q.z, q.w)));
-                   });
+        auto load = [&](uint64_t v) { return __ldcg(x4 + v); };
+        auto use = [&](uint64_t, float4 raw) {
+            const float4 q = scale4(raw);
+            m = max_nan(max_nan(m, q.x), max_nan(q.y, max_nan(q.z, q.w)));
+        };
+        const uint64_t vstart = early_batch<8>(early != 0, ch.col0 / 4, ch.col1 / 4, load, use);
+        batched<8>(vstart, ch.col1 / 4, load, use);
     } else {
+        pdl_enter();
         for (uint64_t c = ch.col0 + threadIdx.x; c < ch.col1; c += kSplitThreads)
             m = max_nan(m, value_at<false>(p, w, c, apply_scale, scale));
     }
@@ -427,8 +453,10 @@ cudaError_t launch_argmax_rows_split(const LaunchEnv& env, const RowPlan& p, int
         char* base = static_cast<char*>(env.workspace) + split_rows_workspace_offset(env.sm_count);
         auto* partials = reinterpret_cast<ChunkPartial*>(base);
         auto* tickets = reinterpret_cast<unsigned*>(base + (uint64_t)env.sm_count * kSplitRowChunks * 16);
+        const int early = reads_clear(env, span_of(p.src, 4));
         err = launch_dependent(argmax_rows_flat, dim3((unsigned)(p.rows * kSplitCluster)), dim3(kSplitThreads), 0,
-                               env.stream, p, dst_dtype, split_chunk(p.ne[0]), partials, tickets);
+                               env.stream, p, dst_dtype, split_chunk(p.ne[0]), partials, tickets, early);
+        if (err == cudaSuccess) stream_wrote(env.stream, span_of(p.dst, dst_dtype == (int)DType::I64 ? 8 : 4));
     } else {
         err = launch_dependent(argmax_rows_split, dim3((unsigned)(p.rows * kSplitCluster)), dim3(kSplitThreads), 0,
                                env.stream, p, dst_dtype, split_chunk(p.ne[0]));
@@ -445,9 +473,12 @@ cudaError_t launch_sum_rows_split(const LaunchEnv& env, const RowPlan& p) {
 }
 
 cudaError_t launch_soft_max_split(const LaunchEnv& env, const RowPlan& p, bool apply_scale, float scale) {
+    // early only for the vector pass without a mask (the kernel's `vec`)
+    const int early = p.vec && !(apply_scale && p.has_aux) && reads_clear(env, span_of(p.src, 4));
     const cudaError_t err = launch_dependent(softmax_rows_split, dim3((unsigned)(p.rows * kSplitCluster)),
                                              dim3(kSplitThreads), 0, env.stream, p, apply_scale, scale,
-                                             split_chunk(p.ne[0]));
+                                             split_chunk(p.ne[0]), early);
+    if (err == cudaSuccess) stream_wrote(env.stream, span_of(p.dst, 4));
     ++*env.launches;
     return err != cudaSuccess ? err : cudaGetLastError();
 }
