@@ -765,17 +765,29 @@ __device__ __forceinline__ void st_u4(void* p, uint4 v) {
                  : "memory");
 }
 
-// One CTA of 1024 threads per SM.  After the previous kernel of the stream
-// has completed (it may have produced the input), thread 0 has the TMA
-// engine copy the op's 128 KB table into shared memory while every thread
-// issues its first 8 vector loads (128 KB per SM in flight); then
+template <int U>
+__device__ __forceinline__ void table_first_loads(uint4 (&cur)[U], const uint16_t* __restrict__ src, uint64_t gid,
+                                                  uint64_t stride, uint64_t nvec) {
+#pragma unroll
+    for (int k = 0; k < U; ++k) {
+        const uint64_t i = gid + k * stride;
+        cur[k] = i < nvec ? ld_u4(src + i * 8) : make_uint4(0, 0, 0, 0);
+    }
+}
+
+// One CTA of 1024 threads per SM.  Thread 0 has the TMA engine copy the
+// op's 128 KB table into shared memory -- the tables are written once at
+// context creation, before any operator, so the copy starts before the wait
+// for the previous kernel -- while every thread issues its first 8 vector
+// loads (128 KB per SM in flight): before that wait too when `early` (the
+// input is clear of the previous kernel's writes), after it otherwise; then
 // grid-strided 16-byte vectors stream through the table, 8 per iteration.
 __global__ void __launch_bounds__(kTableThreads, 1) table_stream(uint16_t* __restrict__ dst,
                                                                  const uint16_t* __restrict__ src, uint64_t n,
-                                                                 const uint16_t* __restrict__ table, uint32_t* fault) {
+                                                                 const uint16_t* __restrict__ table, uint32_t* fault,
+                                                                 int early) {
     extern __shared__ __align__(128) uint16_t tab[];
     __shared__ __align__(8) uint64_t bar;
-    pdl_enter();
     constexpr int L = 8;  // halves per 16-byte vector
     constexpr int U = 8;
     const uint64_t nvec = n / L;
@@ -788,10 +800,12 @@ __global__ void __launch_bounds__(kTableThreads, 1) table_stream(uint16_t* __res
         bulk_load(tab, table, kTableBytes, &bar);
     }
     uint4 cur[U];
-#pragma unroll
-    for (int k = 0; k < U; ++k) {
-        const uint64_t i = gid + k * stride;
-        cur[k] = i < nvec ? ld_u4(src + i * L) : make_uint4(0, 0, 0, 0);
+    if (early) {
+        table_first_loads<U>(cur, src, gid, stride, nvec);
+        pdl_enter();
+    } else {
+        pdl_enter();
+        table_first_loads<U>(cur, src, gid, stride, nvec);
     }
     __syncthreads();  // the barrier is initialised before any thread waits on it
     const bool ok = mbar_wait(&bar, 0);
@@ -833,9 +847,11 @@ cudaError_t launch_table_stream(const LaunchEnv& env, const EwPlan& p, int slot)
     }
     const uint16_t* table = static_cast<const uint16_t*>(env.tables) + (uint64_t)slot * 65536u;
     uint32_t* fault = reinterpret_cast<uint32_t*>(static_cast<char*>(env.workspace) + kFaultWordOffset);
+    const int early = reads_clear(env, p.src0.ptr, p.count * 2);
     const cudaError_t err = launch_dependent(table_stream, dim3((unsigned)env.sm_count), dim3(kTableThreads),
                                              (size_t)kTableBytes, env.stream, reinterpret_cast<uint16_t*>(p.dst.ptr),
-                                             reinterpret_cast<const uint16_t*>(p.src0.ptr), p.count, table, fault);
+                                             reinterpret_cast<const uint16_t*>(p.src0.ptr), p.count, table, fault, early);
+    if (err == cudaSuccess) stream_wrote(env.stream, p.dst.ptr, p.count * 2);
     ++*env.launches;
     return err != cudaSuccess ? err : cudaGetLastError();
 }
