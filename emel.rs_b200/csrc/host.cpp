@@ -494,6 +494,7 @@ emel_cuda_status emel_cuda_memcpy_h2d(emel_cuda_context* ctx, void* stream, void
                                       uint64_t bytes) {
     if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
     cudaError_t err = select_device(ctx);
+    forget_stream(stream);  // the stream's last work is now a copy
     if (err == cudaSuccess) err = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, (cudaStream_t)stream);
     return device_status(ctx, err);
 }
@@ -502,6 +503,7 @@ emel_cuda_status emel_cuda_memcpy_d2h(emel_cuda_context* ctx, void* stream, void
                                       uint64_t bytes) {
     if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
     cudaError_t err = select_device(ctx);
+    forget_stream(stream);
     if (err == cudaSuccess) err = cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToHost, (cudaStream_t)stream);
     return device_status(ctx, err);
 }
@@ -509,6 +511,7 @@ emel_cuda_status emel_cuda_memcpy_d2h(emel_cuda_context* ctx, void* stream, void
 emel_cuda_status emel_cuda_memset(emel_cuda_context* ctx, void* stream, void* dst, int value, uint64_t bytes) {
     if (ctx == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
     cudaError_t err = select_device(ctx);
+    forget_stream(stream);
     if (err == cudaSuccess) err = cudaMemsetAsync(dst, value, bytes, (cudaStream_t)stream);
     return device_status(ctx, err);
 }
@@ -568,11 +571,13 @@ emel_cuda_status emel_cuda_event_create(emel_cuda_context* ctx, void** out) {
 
 emel_cuda_status emel_cuda_event_record(emel_cuda_context* ctx, void* event, void* stream) {
     if (ctx == nullptr || event == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    forget_stream(stream);
     return device_status(ctx, cudaEventRecord((cudaEvent_t)event, (cudaStream_t)stream));
 }
 
 emel_cuda_status emel_cuda_event_record_timed(emel_cuda_context* ctx, void* event, void* stream) {
     if (ctx == nullptr || event == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    forget_stream(stream);
     cudaStreamCaptureStatus cap = cudaStreamCaptureStatusNone;
     cudaError_t err = cudaStreamIsCapturing((cudaStream_t)stream, &cap);
     if (err == cudaSuccess) {
@@ -596,6 +601,7 @@ emel_cuda_status emel_cuda_event_destroy(emel_cuda_context* ctx, void* event) {
 
 emel_cuda_status emel_cuda_stream_wait_event(emel_cuda_context* ctx, void* stream, void* event) {
     if (ctx == nullptr || event == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
+    forget_stream(stream);  // what the event covers is not in this stream's record
     return device_status(ctx, cudaStreamWaitEvent((cudaStream_t)stream, (cudaEvent_t)event, 0));
 }
 
@@ -629,6 +635,9 @@ emel_cuda_status emel_cuda_graph_end(emel_cuda_context* ctx, void* stream, emel_
     *out = nullptr;
     cudaGraph_t g = nullptr;
     cudaError_t err = cudaStreamEndCapture((cudaStream_t)stream, &g);
+    // the captured launches did not run: the stream's real last kernel is
+    // whatever ran before the capture, which the record no longer knows
+    forget_stream(stream);
     // captured kernels did not run: the replay accounts for them
     const uint64_t captured = ctx->launches - capture_launch_base;
     ctx->launches = capture_launch_base;
@@ -652,6 +661,7 @@ emel_cuda_status emel_cuda_graph_end(emel_cuda_context* ctx, void* stream, emel_
 emel_cuda_status emel_cuda_graph_launch(emel_cuda_context* ctx, emel_cuda_graph* graph, void* stream) {
     if (ctx == nullptr || graph == nullptr) return EMEL_CUDA_INVALID_ARGUMENT;
     cudaError_t err = select_device(ctx);
+    forget_stream(stream);  // the graph's writes are not in the record
     if (err == cudaSuccess) err = cudaGraphLaunch(graph->exec, (cudaStream_t)stream);
     if (err == cudaSuccess) ctx->launches += graph->kernels;
     return device_status(ctx, err);

@@ -150,3 +150,32 @@ def test_chained_launches_respect_their_inputs(emel, graph):
     for b in bufs:
         b.free()
     s.close()
+
+
+def test_eager_launch_after_a_capture_waits_for_the_kernel_before_it(emel):
+    """Launches captured into a graph do not run on the stream, so the kernel
+    an eager launch follows is the one before the capture: c = -x runs
+    eagerly, b = relu(x) is only captured, then y = c * c must see all of c."""
+    ctx = emel.Context(0)
+    lib = emel.lib()
+    s = emel.Stream(ctx)
+    rng = np.random.default_rng(43)
+    x = (rng.standard_normal(N) * 2).astype(np.float32)
+    bufs = [emel.DeviceBuffer(ctx, N * 4) for _ in range(4)]
+    bufs[0].upload(x)
+    B = ctypes.byref
+    v = [_view(emel, b.ptr, N) for b in bufs]
+    for r in range(3):
+        for i in (1, 2, 3):
+            bufs[i].upload(np.full(N, np.float32(7e20 + r)))
+        assert lib.emel_cuda_unary(ctx.handle, s.handle, NEG, B(v[0]), B(v[1])) == 0, ctx.last_error
+        g = emel.Graph(ctx, s)
+        with g:
+            assert lib.emel_cuda_unary(ctx.handle, s.handle, RELU, B(v[0]), B(v[2])) == 0, ctx.last_error
+        assert lib.emel_cuda_unary(ctx.handle, s.handle, SQR, B(v[1]), B(v[3])) == 0, ctx.last_error
+        s.synchronize()
+        gh.assert_bits_equal(bufs[3].download(np.empty(N, np.float32)), (-x) * (-x), f"round {r}")
+        g.close()
+    for b in bufs:
+        b.free()
+    s.close()
