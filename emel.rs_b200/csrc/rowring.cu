@@ -164,19 +164,30 @@ __device__ __forceinline__ float4 scaled4_fast(const RingArgs& a, const float* r
 // Reductions for the register-resident soft_max rows.  They skip the
 // leading barrier of group_max / group_sum: each uses its own scratch array
 // and, between two uses of the same array, every thread passes the other
-// reduction's barrier and the next row's stage wait, so no reader of the
-// previous value is left.  fmaxf skips NaN; the sign of a zero maximum does
-// not change any exp(v - max).
+// reduction's barrier, so no reader of the previous value is left.  fmaxf
+// skips NaN; the sign of a zero maximum does not change any exp(v - max).
+// The maximum's barrier also carries every thread's stage-wait outcome
+// (ok): *all_ok is the same AND of them in every thread, so the row needs
+// no barrier of its own after the stage wait.
 template <int T>
-__device__ __forceinline__ float row_max_fast(float v, GroupScratch<T>* s) {
+__device__ __forceinline__ float row_max_fast(float v, GroupScratch<T>* s, bool ok, bool* all_ok) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
     const int lane = threadIdx.x & 31, warp = threadIdx.x / 32;
-    if (lane == 0) s->f[warp] = v;
+    const uint32_t warp_ok = __all_sync(0xffffffffu, ok) ? 1u : 0u;
+    if (lane == 0) {
+        s->f[warp] = v;
+        s->h[warp] = warp_ok;
+    }
     __syncthreads();
     v = s->f[0];
+    uint32_t all = s->h[0];
 #pragma unroll
-    for (int w = 1; w < T / 32; ++w) v = fmaxf(v, s->f[w]);
+    for (int w = 1; w < T / 32; ++w) {
+        v = fmaxf(v, s->f[w]);
+        all &= s->h[w];
+    }
+    *all_ok = all != 0;
     return v;
 }
 
@@ -229,10 +240,12 @@ __device__ __forceinline__ float4 sm_operand4(const RingArgs& a, const float* ro
 // The thread's terms (at most 32, each <= 1) are summed in binary32 pairs,
 // then the thread sums meet in binary64.  GUARD: the row does not fill all
 // R * T vector slots.
+// ok: this thread's stage wait succeeded; *all_ok comes back false in
+// every thread (and nothing past the maximum runs) if any thread's did not.
 template <int T, int R, int MODE, bool GUARD>
 __device__ __forceinline__ double sm_exp_pass(const RingArgs& a, const float* row, const unsigned char* stage,
                                               int64_t moff, uint32_t nvec, float4 (&sv)[R], uint32_t* slow,
-                                              GroupScratch<T>* red) {
+                                              GroupScratch<T>* red, bool ok, bool* all_ok) {
     float m = -INFINITY;
 #pragma unroll
     for (int i = 0; i < R; ++i) {
@@ -242,7 +255,8 @@ __device__ __forceinline__ double sm_exp_pass(const RingArgs& a, const float* ro
             m = fmax3(fmax3(m, sv[i].x, sv[i].y), sv[i].z, sv[i].w);
         }
     }
-    m = row_max_fast<T>(m, red);
+    m = row_max_fast<T>(m, red, ok, all_ok);
+    if (!*all_ok) return 0.0;
     const float2 nm2 = make_float2(-m, -m);  // x + (-m) is IEEE x - m
     float2 acc2 = make_float2(0.0f, 0.0f);
     uint32_t bits = 0;
@@ -330,13 +344,23 @@ __global__ void __launch_bounds__(T, R >= 8 ? 2 : (R >= 4 ? 3 : 1024 / T)) row_r
     uint32_t parity = 0;  // phase parity of row k: (k / S) & 1
     for (uint32_t k = 0; k < mine; ++k, s = s + 1 == S ? 0 : s + 1, parity ^= (s == 0)) {
         const bool ok = mbar_wait(&full[s], parity);
-        if (!__syncthreads_and(ok)) {
+        // an expired wait: every thread returns together, thread 0 records
+        // the fault and waits (bounded) for the copies still in flight
+        auto fail = [&]() {
             if (tid == 0) {
                 atomicExch(a.fault, 1u);
                 for (uint32_t j = k; j < mine && j < k + (uint32_t)S; ++j)
                     mbar_wait(&full[j % (uint32_t)S], (j / (uint32_t)S) & 1u);
             }
-            return;
+        };
+        // the register-resident soft_max folds the outcome into its maximum's
+        // barrier (row_max_fast); every other pass agrees on it here
+        constexpr bool kFoldedWait = OP == kRingSoftMax && R > 0;
+        if constexpr (!kFoldedWait) {
+            if (!__syncthreads_and(ok)) {
+                fail();
+                return;
+            }
         }
         unsigned char* stage = stage0 + (size_t)s * a.stage_bytes;
         float* row = reinterpret_cast<float*>(stage);
@@ -427,8 +451,15 @@ __global__ void __launch_bounds__(T, R >= 8 ? 2 : (R >= 4 ? 3 : 1024 / T)) row_r
                 float4 sv[R];
                 uint32_t slow;
                 const bool guard = nvec != (uint32_t)(R * T);
-                const double acc = guard ? sm_exp_pass<T, R, MODE, true>(a, row, stage, moff, nvec, sv, &slow, &red)
-                                         : sm_exp_pass<T, R, MODE, false>(a, row, stage, moff, nvec, sv, &slow, &red);
+                bool all_ok;
+                const double acc = guard ? sm_exp_pass<T, R, MODE, true>(a, row, stage, moff, nvec, sv, &slow, &red, ok,
+                                                                        &all_ok)
+                                         : sm_exp_pass<T, R, MODE, false>(a, row, stage, moff, nvec, sv, &slow, &red,
+                                                                         ok, &all_ok);
+                if (!all_ok) {
+                    fail();
+                    return;
+                }
                 if (isfinite(acc)) {
                     // every thread has finished reading the stage: refill it now
                     if (tid == 0 && k + (uint32_t)S < mine) {
