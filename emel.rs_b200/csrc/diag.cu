@@ -88,6 +88,34 @@ __global__ void __launch_bounds__(kDiagThreads) diag_rows(DiagPlan p) {
 // prefix is read: max, e = exp(v - max) stored in dst, binary64 sum, e / sum.
 // Otherwise the row is redone with the reference's selection and NaN rules
 // over all columns (the scan's maximum starts from column 0).
+// The fast path's two block reductions, without group_max / group_sum's
+// leading barrier: the maximum uses the scratch's f array and the sum its d
+// array, and between one row's read of an array and the next row's write to
+// it every thread passes the other reduction's barrier, so one barrier per
+// reduction and none at the end of a row.  (The exact path's group_max /
+// group_sum keep their leading barriers.)
+__device__ __forceinline__ float diag_max_fast(float v, GroupScratch<kDiagThreads>* s) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    if ((threadIdx.x & 31) == 0) s->f[threadIdx.x / 32] = v;
+    __syncthreads();
+    v = s->f[0];
+#pragma unroll
+    for (int w = 1; w < kDiagThreads / 32; ++w) v = fmaxf(v, s->f[w]);
+    return v;
+}
+
+__device__ __forceinline__ double diag_sum_fast(double v, GroupScratch<kDiagThreads>* s) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    if ((threadIdx.x & 31) == 0) s->d[threadIdx.x / 32] = v;
+    __syncthreads();
+    v = 0.0;
+#pragma unroll
+    for (int w = 0; w < kDiagThreads / 32; ++w) v += s->d[w];
+    return v;
+}
+
 template <bool VEC>
 __global__ void __launch_bounds__(kDiagThreads) softmax_causal_rows(DiagPlan p) {
     __shared__ GroupScratch<kDiagThreads> red;
@@ -119,7 +147,7 @@ __global__ void __launch_bounds__(kDiagThreads) softmax_causal_rows(DiagPlan p) 
                 m = fmaxf(m, v);
             }
         }
-        m = group_max<kDiagThreads>(odd ? INFINITY : m, &red);
+        m = diag_max_fast(odd ? INFINITY : m, &red);  // the kept values hold no NaN here, or odd is set
         if (isfinite(m)) {
             double acc = 0.0;
             if constexpr (VEC) {
@@ -141,7 +169,7 @@ __global__ void __launch_bounds__(kDiagThreads) softmax_causal_rows(DiagPlan p) 
                     acc += (double)e;
                 }
             }
-            acc = group_sum<kDiagThreads>(acc, &red);
+            acc = diag_sum_fast(acc, &red);
             const float denom = __double2float_rn(acc);  // >= 1: the maximum contributes exp(0)
             const float inv = __frcp_rn(denom);
             if constexpr (VEC) {
@@ -176,7 +204,7 @@ __global__ void __launch_bounds__(kDiagThreads) softmax_causal_rows(DiagPlan p) 
             const float denom = __double2float_rn(acc);
             for (uint64_t c = threadIdx.x; c < side; c += kDiagThreads) y[c] = f_div(y[c], denom);
         }
-        __syncthreads();  // the reduction scratch is reused by the next row
+        if (!isfinite(m)) __syncthreads();  // after the exact path, before the next row's fast maximum
     }
 }
 
